@@ -1,0 +1,187 @@
+/*
+ * whisper4j_cuda.h — C ABI of libwhisper4j_cuda.so, the B200 (sm_100a) Whisper
+ * text-decoder token loop.
+ *
+ * The library replaces the reference's decoder hot path
+ * (com.sparrowlogic.whisper4j.nn.WhisperDecoder and the nn/tensor code under it)
+ * behind plain C types, so a Java host binds it with java.lang.foreign downcalls
+ * and any C/C++/Python host with its own FFI.  All entry points return an int
+ * status (W4J_OK = 0, negative on error); w4j_last_error() gives the message of
+ * the calling thread's last failure.  A context is bound to one CUDA device;
+ * calls on one context are serialised internally, separate contexts run
+ * concurrently.
+ *
+ * Reference interfaces each entry point replaces are cited as file:line within
+ * sparrowlogic/whisper4j (W4J = src/main/java/com/sparrowlogic/whisper4j).
+ */
+#ifndef WHISPER4J_CUDA_H
+#define WHISPER4J_CUDA_H
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+#define W4J_OK 0
+#define W4J_ERR_ARG -1       /* IllegalArgumentException in the reference */
+#define W4J_ERR_STATE -2     /* IllegalStateException (e.g. weights missing, closed) */
+#define W4J_ERR_CUDA -3      /* CUDA runtime or kernel failure */
+#define W4J_ERR_OOM -4       /* device allocation failed */
+#define W4J_ERR_CANCELLED -5 /* w4j_cancel() observed between steps */
+
+/* GGML tensor types (W4J/model/GgmlLoader.java:30-36). */
+#define W4J_GGML_F32 0
+#define W4J_GGML_F16 1
+#define W4J_GGML_Q8_0 8
+
+/* W4J/model/ModelDimensions.java:6-17, same field order. */
+typedef struct w4j_dims {
+    int32_t n_mels, n_audio_ctx, n_audio_state, n_audio_head, n_audio_layer;
+    int32_t n_vocab, n_text_ctx, n_text_state, n_text_head, n_text_layer;
+} w4j_dims;
+
+typedef struct w4j_ctx w4j_ctx;
+
+/* Last error message of the calling thread ("" if none). */
+const char *w4j_last_error(void);
+
+/* Library version string. */
+const char *w4j_version(void);
+
+/*
+ * Create a decoder context on `device` (replaces `new WhisperDecoder(weights, dims)`,
+ * W4J/nn/WhisperDecoder.java:36-56, called at W4J/WhisperModel.java:160).
+ * max_streams: independent audio chunks decoded together by one call;
+ * max_beam: largest beam size used (1 for greedy only).  Device memory for the
+ * KV caches is sized from these and n_text_ctx / n_audio_ctx.
+ */
+int w4j_ctx_create(const w4j_dims *dims, int device, int max_streams, int max_beam, w4j_ctx **out);
+int w4j_ctx_destroy(w4j_ctx *ctx);
+
+/*
+ * Upload one decoder tensor straight from the GGML file's bytes (the hook next
+ * to GgmlLoader.dequantize, W4J/model/GgmlLoader.java:185-202).  `ne` is the
+ * GGML shape (fastest dimension first), `data` the raw payload: F32, F16 or
+ * Q8_0 (34-byte blocks).  Encoder tensors are accepted and ignored (return 1).
+ * Unknown decoder tensor names, wrong shapes and unsupported types are errors.
+ */
+int w4j_upload_tensor(w4j_ctx *ctx, const char *name, int ggml_type, const int64_t *ne, int n_dims,
+                      const void *data, size_t nbytes);
+
+/* Check that every decoder tensor is present (WeightStore.get, W4J/model/WeightStore.java:28-34). */
+int w4j_finalize(w4j_ctx *ctx);
+
+/*
+ * Set the encoder output xa (n_audio_ctx x n_audio_state f32, row-major, host
+ * memory) of stream `slot` and project the cross-attention K/V of every layer
+ * into the device cache (the first-call branch of MultiHeadAttention.forward,
+ * W4J/nn/MultiHeadAttention.java:65-75).  The _device variant takes a device
+ * pointer on the context's device.
+ */
+int w4j_set_encoder_output(w4j_ctx *ctx, int slot, const float *xa, int n_audio_ctx);
+int w4j_set_encoder_output_device(w4j_ctx *ctx, int slot, const float *xa_device, int n_audio_ctx);
+
+/*
+ * WhisperDecoder.forward(tokens, xa, kvCache) (W4J/nn/WhisperDecoder.java:59-104)
+ * for stream `slot`.  use_cache=1 appends the tokens to the slot's self-attention
+ * cache (the kvCache map); use_cache=0 runs with an empty private cache and leaves
+ * the slot's cache unchanged (kvCache == null, as detectLanguage does at
+ * W4J/WhisperModel.java:548).  out_logits receives n_tokens x n_vocab f32.
+ */
+int w4j_forward(w4j_ctx *ctx, int slot, const int32_t *tokens, int n_tokens, int use_cache, float *out_logits);
+
+/* Empty the self-attention cache of a stream (a fresh kvCache map). */
+int w4j_reset_cache(w4j_ctx *ctx, int slot);
+
+/*
+ * Decode result per stream (WhisperDecoder.DecodeResult, W4J/nn/WhisperDecoder.java:672-673):
+ * out_tokens[s * max_tokens .. + out_lens[s]) are the generated ids; sum/avg
+ * log-probabilities, compression ratio and no-speech probability per stream.
+ */
+typedef struct w4j_result {
+    int32_t *tokens;         /* n_streams * max_tokens */
+    int32_t *lens;           /* n_streams */
+    double *sum_logprob;     /* n_streams */
+    float *avg_logprob;      /* n_streams */
+    float *compression;      /* n_streams (zlib ratio, WhisperDecoder.java:628-647) */
+    float *no_speech_prob;   /* n_streams */
+} w4j_result;
+
+/*
+ * Greedy (temperature 0) or sampled decode of n_streams independent streams
+ * (slots[i] names the stream whose encoder output was set), each starting from
+ * its own prompt of n_prompt tokens (prompts: n_streams x n_prompt).  Mirrors
+ * WhisperDecoder.decode (W4J/nn/WhisperDecoder.java:161-204) including the
+ * logit processors (:450-564) and no-speech probability (:442-448).  ts_begin
+ * <= 0 disables timestamp rules.  seed drives temperature sampling.
+ */
+int w4j_decode(w4j_ctx *ctx, const int32_t *slots, int n_streams, const int32_t *prompts, int n_prompt,
+               int32_t eot, int max_tokens, const int32_t *suppress, int n_suppress, int32_t no_speech,
+               float temperature, int32_t ts_begin, uint64_t seed, w4j_result *out);
+
+/* Beam search (WhisperDecoder.decodeBeam, W4J/nn/WhisperDecoder.java:214-394). */
+int w4j_decode_beam(w4j_ctx *ctx, const int32_t *slots, int n_streams, const int32_t *prompts, int n_prompt,
+                    int32_t eot, int max_tokens, const int32_t *suppress, int n_suppress, int32_t no_speech,
+                    int32_t ts_begin, int beam, w4j_result *out);
+
+/*
+ * Temperature-fallback policy (WhisperDecoder.decodeWithFallback,
+ * W4J/nn/WhisperDecoder.java:119-149): beam search (beam > 1) or greedy at
+ * t = 0, then sampling at 0.2 .. 1.0 while needsFallback (:435-440) holds.
+ * out_temperature receives the temperature of the returned result per stream.
+ */
+int w4j_decode_with_fallback(w4j_ctx *ctx, const int32_t *slots, int n_streams, const int32_t *prompts,
+                             int n_prompt, int32_t eot, int max_tokens, const int32_t *suppress, int n_suppress,
+                             int32_t no_speech, int32_t ts_begin, int beam, uint64_t seed, w4j_result *out,
+                             float *out_temperature);
+
+/* Ask a running decode on this context to stop at its next step boundary
+ * (TranscriptionHandle cancellation, W4J/WhisperModel.java:620-633). */
+int w4j_cancel(w4j_ctx *ctx);
+
+/* Host-side helpers of the policy (no device work). */
+float w4j_compression_ratio(const int32_t *tokens, int n);                            /* :628-647 */
+int w4j_needs_fallback(float compression_ratio, float avg_logprob, float no_speech);  /* :435-440 */
+
+/*
+ * Timing of the last decode call on this context: device milliseconds of the
+ * step loop (prefill excluded) and number of steps, plus kernels launched.
+ */
+int w4j_last_timing(w4j_ctx *ctx, double *loop_ms, int *steps, long long *kernel_launches);
+
+/* ---------------------------------------------------------------------------
+ * Op-level entry points on device buffers (plain pointers on the context's
+ * device, stream 0 of the calling thread unless `stream` is given).  They run
+ * single kernels of the step for tests and for hosts that drive their own loop.
+ * ------------------------------------------------------------------------- */
+
+/*
+ * y = LN?(x) . W^T + b for M rows (Linear.forward, W4J/nn/Linear.java:23-26,
+ * optionally preceded by LayerNorm.forward, W4J/nn/LayerNorm.java:28-30).
+ * W is a GGML F16 or Q8_0 payload already on the device: F16 (N x K halves), or
+ * Q8_0 repacked by w4j_q8_0_repack.  ln_g/ln_b may be NULL (no LayerNorm).
+ * epilogue: 0 = store, 1 = GELU (Tensor.geluInPlace), 2 = residual y += ...
+ */
+int w4j_op_linear(w4j_ctx *ctx, const float *x, int M, int K, const void *W, int w_type, int N,
+                  const float *bias, const float *ln_g, const float *ln_b, int epilogue, float *y, void *stream);
+
+/* Split a GGML Q8_0 payload (N*K/32 blocks of 34 bytes, device) into the
+ * device layout: int8 quants (N x K) then f16 scales (N x K/32). dst holds N*K + N*K/16 bytes. */
+int w4j_q8_0_repack(const void *src_device, int N, int K, void *dst_device, void *stream);
+
+/*
+ * logits = LN(x) . E^T over the vocabulary followed by argmax and log-softmax
+ * of the chosen id, for M rows (WhisperDecoder.java:102-103 then argmax :566-574
+ * and logSoftmax :614-626).  x: M x d f32, E: V x d f16, ln: d f32 each;
+ * outputs token ids (M) and log-probabilities (M, double).  Scratch memory for
+ * the per-block partial results is taken from the context.
+ */
+int w4j_op_logits_argmax(w4j_ctx *ctx, const float *x, int M, const void *E, int V, const float *ln_g,
+                         const float *ln_b, int32_t *out_token, double *out_logprob, void *stream);
+
+#ifdef __cplusplus
+}
+#endif
+#endif /* WHISPER4J_CUDA_H */

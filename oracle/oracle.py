@@ -1,0 +1,248 @@
+"""ctypes front end of the CPU oracle (oracle/w4j_oracle.c).
+
+TEST INFRASTRUCTURE ONLY.  Imported by tests/, __graft_entry__.smoke() and
+bench.py's CPU-baseline / reference arm as the checker; the product library and
+its Python wrapper never import this module.
+"""
+from __future__ import annotations
+
+import ctypes
+import os
+import subprocess
+import threading
+
+import numpy as np
+
+_HERE = os.path.dirname(os.path.abspath(__file__))
+_LIB_PATH = os.path.join(_HERE, "_build", "libw4j_oracle.so")
+_lib = None
+_lock = threading.Lock()
+
+
+def build(force: bool = False) -> str:
+    """Compile the oracle with its Makefile (strict IEEE f32 flags)."""
+    src = os.path.join(_HERE, "w4j_oracle.c")
+    if force or not os.path.exists(_LIB_PATH) or os.path.getmtime(_LIB_PATH) < os.path.getmtime(src):
+        subprocess.run(["make", "-s", "-C", _HERE], check=True)
+    return _LIB_PATH
+
+
+class _Dims(ctypes.Structure):
+    _fields_ = [(n, ctypes.c_int) for n in
+                ("n_vocab", "n_audio_ctx", "n_text_ctx", "n_text_state", "n_text_head", "n_text_layer")]
+
+
+def lib():
+    global _lib
+    with _lock:
+        if _lib is None:
+            build()
+            L = ctypes.CDLL(_LIB_PATH)
+            P, I, F, D = ctypes.c_void_p, ctypes.c_int, ctypes.c_float, ctypes.c_double
+            L.orc_last_error.restype = ctypes.c_char_p
+            L.orc_model_new.restype = P
+            L.orc_model_new.argtypes = [ctypes.POINTER(_Dims)]
+            L.orc_model_free.argtypes = [P]
+            L.orc_set_tensor.argtypes = [P, ctypes.c_char_p, P, ctypes.c_long]
+            L.orc_model_check.argtypes = [P]
+            L.orc_gelu_table.restype = ctypes.POINTER(ctypes.c_float)
+            L.orc_gelu_table.argtypes = [P]
+            L.orc_cache_new.restype = P
+            L.orc_cache_new.argtypes = [P, I]
+            L.orc_cache_free.argtypes = [P]
+            L.orc_cache_len.argtypes = [P]
+            L.orc_forward.argtypes = [P, P, I, P, I, P, P]
+            L.orc_decode.argtypes = [P, P, I, P, I, I, I, P, I, I, F, I, ctypes.c_uint64, P, P, P, P, P, I]
+            L.orc_decode_beam.argtypes = [P, P, I, P, I, I, I, P, I, I, I, I, P, P, P, P, P, I]
+            L.orc_apply_repetition_penalty.argtypes = [P, P, I, I]
+            L.orc_apply_timestamp_rules.argtypes = [P, P, I, I, I, I, I]
+            L.orc_dot.restype = F
+            L.orc_dot.argtypes = [P, P, I]
+            L.orc_matmul.argtypes = [P, P, I, I, I, P]
+            L.orc_matmul_transb.argtypes = [P, P, I, I, I, F, P]
+            L.orc_softmax_rows.argtypes = [P, I, I]
+            L.orc_layer_norm.argtypes = [P, I, I, P, P, F, P]
+            L.orc_gelu.argtypes = [P, P, ctypes.c_long]
+            L.orc_f16_to_f32.restype = F
+            L.orc_f16_to_f32.argtypes = [ctypes.c_uint16]
+            L.orc_f32_to_f16.restype = ctypes.c_uint16
+            L.orc_f32_to_f16.argtypes = [F]
+            _lib = L
+    return _lib
+
+
+def _p(a: np.ndarray):
+    return a.ctypes.data_as(ctypes.c_void_p)
+
+
+def _f32(a):
+    return np.ascontiguousarray(a, dtype=np.float32)
+
+
+def _i32(a):
+    return np.ascontiguousarray(a, dtype=np.int32)
+
+
+class OracleError(RuntimeError):
+    pass
+
+
+def _check(rc):
+    if rc < 0:
+        raise OracleError(lib().orc_last_error().decode())
+
+
+# ---- tensor KATs ------------------------------------------------------------
+
+def dot(a, b) -> float:
+    a, b = _f32(a), _f32(b)
+    return float(lib().orc_dot(_p(a), _p(b), a.size))
+
+
+def matmul(a, b):
+    a, b = _f32(a), _f32(b)
+    M, K = a.shape
+    N = b.shape[1]
+    out = np.zeros((M, N), np.float32)
+    lib().orc_matmul(_p(a), _p(b), M, K, N, _p(out))
+    return out
+
+
+def matmul_transb(a, b, alpha=1.0):
+    a, b = _f32(a), _f32(b)
+    M, K = a.shape
+    N = b.shape[0]
+    out = np.zeros((M, N), np.float32)
+    lib().orc_matmul_transb(_p(a), _p(b), M, K, N, alpha, _p(out))
+    return out
+
+
+def softmax(x):
+    x = _f32(x).copy()
+    rows = x.size // x.shape[-1]
+    lib().orc_softmax_rows(_p(x), rows, x.shape[-1])
+    return x
+
+
+def layer_norm(x, g, b, eps=1e-5):
+    x, g, b = _f32(x), _f32(g), _f32(b)
+    y = np.zeros_like(x)
+    lib().orc_layer_norm(_p(x), x.size // x.shape[-1], x.shape[-1], _p(g), _p(b), eps, _p(y))
+    return y
+
+
+def f32_to_f16_bits(v: float) -> int:
+    return int(lib().orc_f32_to_f16(v))
+
+
+# ---- model ------------------------------------------------------------------
+
+class OracleModel:
+    """The oracle's decoder, loaded from a parsed GGML model (whisper4j_b200.ggml.GgmlModel)."""
+
+    def __init__(self, gmodel, n_audio_ctx: int | None = None):
+        from whisper4j_b200 import ggml  # dequantisation helper with the reference's semantics
+
+        dm = gmodel.dims
+        self.dims = dm
+        self.n_audio_ctx = n_audio_ctx or dm.n_audio_ctx
+        d = _Dims(dm.n_vocab, self.n_audio_ctx, dm.n_text_ctx, dm.n_text_state, dm.n_text_head, dm.n_text_layer)
+        self._m = lib().orc_model_new(ctypes.byref(d))
+        if not self._m:
+            raise OracleError(lib().orc_last_error().decode())
+        for name, t in gmodel.tensors.items():
+            if not name.startswith("decoder."):
+                continue
+            arr = _f32(ggml.dequantize(t)).reshape(-1)
+            _check(lib().orc_set_tensor(self._m, name.encode(), _p(arr), arr.size))
+        _check(lib().orc_model_check(self._m))
+
+    def close(self):
+        if self._m:
+            lib().orc_model_free(self._m)
+            self._m = None
+
+    def __del__(self):
+        try:
+            self.close()
+        except Exception:
+            pass
+
+    def gelu_table(self) -> np.ndarray:
+        ptr = lib().orc_gelu_table(self._m)
+        return np.ctypeslib.as_array(ptr, shape=(65536,)).copy()
+
+    def gelu(self, x):
+        x = _f32(x).copy()
+        lib().orc_gelu(self._m, _p(x), x.size)
+        return x
+
+    def new_cache(self):
+        return OracleCache(self)
+
+    def forward(self, tokens, xa, cache=None) -> np.ndarray:
+        """WhisperDecoder.forward: logits (n, n_vocab) as float32."""
+        tok = _i32(tokens)
+        xa = _f32(xa)
+        V = self.dims.n_vocab
+        out = np.zeros((tok.size, V), np.float32)
+        _check(lib().orc_forward(self._m, _p(tok), tok.size, _p(xa), xa.shape[0],
+                                 cache._c if cache is not None else None, _p(out)))
+        return out
+
+    def decode(self, xa, prompt, eot, max_tokens, suppress=(), no_speech=-1, temperature=0.0, ts_begin=-1,
+               seed=0, max_steps=0):
+        xa, pr, sp = _f32(xa), _i32(prompt), _i32(list(suppress) or [0])
+        toks = np.zeros(max(max_tokens, 1), np.int32)
+        n = ctypes.c_int()
+        s = ctypes.c_double()
+        a = ctypes.c_float()
+        ns = ctypes.c_float()
+        _check(lib().orc_decode(self._m, _p(xa), xa.shape[0], _p(pr), pr.size, eot, max_tokens, _p(sp),
+                                len(suppress), no_speech, temperature, ts_begin, seed, _p(toks), ctypes.byref(n),
+                                ctypes.byref(s), ctypes.byref(a), ctypes.byref(ns), max_steps))
+        return dict(tokens=toks[:n.value].tolist(), sum_logprob=s.value, avg_logprob=a.value,
+                    no_speech_prob=ns.value)
+
+    def decode_beam(self, xa, prompt, eot, max_tokens, suppress=(), no_speech=-1, ts_begin=-1, beam=5,
+                    max_steps=0):
+        xa, pr, sp = _f32(xa), _i32(prompt), _i32(list(suppress) or [0])
+        toks = np.zeros(max(max_tokens, 1) + 1, np.int32)
+        n = ctypes.c_int()
+        s = ctypes.c_double()
+        a = ctypes.c_float()
+        ns = ctypes.c_float()
+        _check(lib().orc_decode_beam(self._m, _p(xa), xa.shape[0], _p(pr), pr.size, eot, max_tokens, _p(sp),
+                                     len(suppress), no_speech, ts_begin, beam, _p(toks), ctypes.byref(n),
+                                     ctypes.byref(s), ctypes.byref(a), ctypes.byref(ns), max_steps))
+        return dict(tokens=toks[:n.value].tolist(), sum_logprob=s.value, avg_logprob=a.value,
+                    no_speech_prob=ns.value)
+
+
+class OracleCache:
+    def __init__(self, model: OracleModel):
+        self._model = model
+        self._c = lib().orc_cache_new(model._m, model.n_audio_ctx)
+
+    def __len__(self):
+        return lib().orc_cache_len(self._c)
+
+    def __del__(self):
+        try:
+            lib().orc_cache_free(self._c)
+        except Exception:
+            pass
+
+
+def apply_repetition_penalty(logits, generated):
+    lg = _f32(logits).copy()
+    g = _i32(list(generated) or [0])
+    lib().orc_apply_repetition_penalty(_p(lg), _p(g), len(generated), lg.size)
+    return lg
+
+
+def apply_timestamp_rules(logits, generated, ts_begin, eot, is_first):
+    lg = _f32(logits).copy()
+    g = _i32(list(generated) or [0])
+    lib().orc_apply_timestamp_rules(_p(lg), _p(g), len(generated), ts_begin, eot, lg.size, int(is_first))
+    return lg

@@ -1,0 +1,71 @@
+/*
+ * w4j_oracle.h — CPU restatement of whisper4j's decoder token loop.
+ *
+ * TEST INFRASTRUCTURE ONLY: the checker for the CUDA path, never part of the
+ * product library.  See w4j_oracle.c for the reference file:line each function
+ * restates.
+ */
+#ifndef W4J_ORACLE_H
+#define W4J_ORACLE_H
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+typedef struct {
+    int n_vocab, n_audio_ctx, n_text_ctx, n_text_state, n_text_head, n_text_layer;
+} orc_dims;
+
+typedef struct orc_model orc_model;
+typedef struct orc_cache orc_cache;
+
+const char *orc_last_error(void);
+
+orc_model *orc_model_new(const orc_dims *d);
+void orc_model_free(orc_model *m);
+/* name: canonical GGML tensor name; data: f32 values in the file's row-major
+ * order (GGML `ne` reversed).  Returns 0 when stored, 1 when the tensor is not
+ * on the decoder path (ignored), -1 on error. */
+int orc_set_tensor(orc_model *m, const char *name, const float *data, long n);
+int orc_model_check(const orc_model *m);
+const float *orc_gelu_table(const orc_model *m);
+
+orc_cache *orc_cache_new(const orc_model *m, int n_audio_ctx);
+void orc_cache_free(orc_cache *c);
+int orc_cache_len(const orc_cache *c);
+
+/* WhisperDecoder.forward(tokens, xa, kvCache): logits (n, n_vocab). cache may be NULL. */
+int orc_forward(const orc_model *m, const int *tokens, int n, const float *xa, int n_audio_ctx, orc_cache *cache,
+                float *logits);
+
+/* WhisperDecoder.decode(...) — max_steps > 0 stops after that many steps (bounded samples). */
+int orc_decode(const orc_model *m, const float *xa, int n_audio_ctx, const int *prompt, int n_prompt, int eot,
+               int max_tokens, const int *suppress, int n_suppress, int no_speech, float temperature, int ts_begin,
+               uint64_t seed, int *out_tokens, int *out_len, double *out_sum_logprob, float *out_avg_logprob,
+               float *out_no_speech_prob, int max_steps);
+
+/* WhisperDecoder.decodeBeam(...) */
+int orc_decode_beam(const orc_model *m, const float *xa, int n_audio_ctx, const int *prompt, int n_prompt, int eot,
+                    int max_tokens, const int *suppress, int n_suppress, int no_speech, int ts_begin, int beam,
+                    int *out_tokens, int *out_len, double *out_sum_logprob, float *out_avg_logprob,
+                    float *out_no_speech_prob, int max_steps);
+
+/* processors exposed for unit tests */
+void orc_apply_repetition_penalty(float *logits, const int *gen, int count, int n);
+void orc_apply_timestamp_rules(float *logits, const int *gen, int count, int ts_begin, int eot, int n, int is_first);
+
+/* tensor KATs (TensorTest.java / SimdOpsTest.java) */
+float orc_dot(const float *a, const float *b, int n);
+void orc_matmul(const float *a, const float *b, int M, int K, int N, float *out);
+void orc_matmul_transb(const float *a, const float *b, int M, int K, int N, float alpha, float *out);
+void orc_softmax_rows(float *x, int rows, int n);
+void orc_layer_norm(const float *x, int rows, int n, const float *g, const float *b, float eps, float *y);
+void orc_gelu(const orc_model *m, float *x, long n);
+float orc_f16_to_f32(uint16_t h);
+uint16_t orc_f32_to_f16(float f);
+
+#ifdef __cplusplus
+}
+#endif
+#endif

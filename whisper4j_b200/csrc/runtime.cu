@@ -1,0 +1,1266 @@
+// runtime.cu — host runtime and C ABI of libwhisper4j_cuda.so.
+//
+// The decoder context replaces the reference's WhisperDecoder object
+// (nn/WhisperDecoder.java:36-56) and its per-call kvCache maps: weights live on one GPU in
+// their GGML storage type, the KV caches are preallocated device arrays, and a decode call
+// runs the whole token loop on the device.  The prompt steps are launched directly; every
+// later step is one CUDA-graph replay (kernels chained with programmatic dependent launch),
+// and only token ids, log-prob sums and the no-speech probability come back to the host.
+#include <zlib.h>
+
+#include <algorithm>
+#include <atomic>
+#include <cmath>
+#include <cstdarg>
+#include <cstdio>
+#include <cstring>
+#include <map>
+#include <mutex>
+#include <set>
+#include <string>
+#include <vector>
+
+#include "../../include/whisper4j_cuda.h"
+#include "w4j_internal.cuh"
+
+using namespace w4j;
+
+// ---------------------------------------------------------------------------
+// errors
+// ---------------------------------------------------------------------------
+static thread_local std::string g_err;
+
+static int set_err(int code, const char *fmt, ...) {
+    char buf[1024];
+    va_list ap;
+    va_start(ap, fmt);
+    vsnprintf(buf, sizeof buf, fmt, ap);
+    va_end(ap);
+    g_err = buf;
+    return code;
+}
+
+#define CUDA_TRY(expr)                                                                             \
+    do {                                                                                           \
+        cudaError_t e_ = (expr);                                                                   \
+        if (e_ != cudaSuccess)                                                                     \
+            return set_err(e_ == cudaErrorMemoryAllocation ? W4J_ERR_OOM : W4J_ERR_CUDA, "%s: %s (%s:%d)", \
+                           #expr, cudaGetErrorString(e_), __FILE__, __LINE__);                     \
+    } while (0)
+
+#define TRY(expr)            \
+    do {                     \
+        int r_ = (expr);     \
+        if (r_ < 0) return r_; \
+    } while (0)
+
+// ---------------------------------------------------------------------------
+// context
+// ---------------------------------------------------------------------------
+struct LayerDev {
+    DMat qkv, o, xq, xk, xv, xo, m0, m2;
+    float *bqkv = nullptr, *bo = nullptr, *bxq = nullptr, *bxk = nullptr, *bxv = nullptr, *bxo = nullptr;
+    float *bm0 = nullptr, *bm2 = nullptr;
+    float *ln1g = nullptr, *ln1b = nullptr, *ln2g = nullptr, *ln2b = nullptr, *ln3g = nullptr, *ln3b = nullptr;
+    int qkv_type = 0;
+};
+
+struct GraphKey {
+    int mode, S, B, eot, ts_begin, n_sup, max_tokens, ns, n_prompt;
+    float temperature;
+    unsigned long long seed;
+    bool operator<(const GraphKey &o) const { return memcmp(this, &o, sizeof *this) < 0; }
+};
+
+struct w4j_ctx {
+    int device = 0;
+    cudaStream_t stream = nullptr;
+    std::mutex mu;
+    int V = 0, C = 0, A = 0, d = 0, H = 0, L = 0;
+    w4j_dims dims{};
+    int max_streams = 0, max_beam = 0, n_slots = 0, M_max = 0;
+    int sm_count = 148;
+    std::vector<LayerDev> layers;
+    DMat E;
+    float *pos_emb = nullptr, *lng = nullptr, *lnb = nullptr, *gelu_lut = nullptr;
+    std::set<std::string> uploaded;
+    std::vector<void *> allocs;
+    // caches
+    __half *ck = nullptr, *cv = nullptr, *sk = nullptr, *sv = nullptr;
+    std::vector<int> cache_len;
+    std::vector<char> has_xa;
+    // activations / scratch
+    float *x = nullptr, *q = nullptr, *attn = nullptr, *h = nullptr, *xa_stage = nullptr;
+    float *attn_part = nullptr;
+    unsigned *attn_ctr = nullptr;
+    int attn_split_max = 1;
+    int n_parts = 0;
+    float *logit_part = nullptr, *ns_part = nullptr, *ns_value = nullptr;
+    float *masked = nullptr;  // M_max x V (sampling)
+    float *raw = nullptr;     // n_text_ctx x V (forward)
+    // decode state
+    DecodeState st;
+    int *d_int_area = nullptr;     // per-call small int arrays (see layout in prepare_call)
+    int *h_int_area = nullptr;     // pinned mirror
+    size_t int_area_n = 0;
+    int *d_done_snapshot = nullptr;
+    int *h_done = nullptr;
+    // graphs
+    std::map<GraphKey, cudaGraphExec_t> graphs;
+    std::atomic<int> cancel{0};
+    double last_ms = 0;
+    int last_steps = 0;
+    long long last_launches = 0;
+    cudaEvent_t ev0 = nullptr, ev1 = nullptr;
+};
+
+template <typename T>
+static int dalloc(w4j_ctx *c, T **p, size_t n) {
+    void *v = nullptr;
+    if (n == 0) n = 1;
+    CUDA_TRY(cudaMalloc(&v, n * sizeof(T)));
+    CUDA_TRY(cudaMemset(v, 0, n * sizeof(T)));
+    c->allocs.push_back(v);
+    *p = reinterpret_cast<T *>(v);
+    return 0;
+}
+
+static void free_all(w4j_ctx *c) {
+    for (auto &kv : c->graphs) cudaGraphExecDestroy(kv.second);
+    c->graphs.clear();
+    for (void *p : c->allocs) cudaFree(p);
+    c->allocs.clear();
+    if (c->h_int_area) cudaFreeHost(c->h_int_area);
+    if (c->h_done) cudaFreeHost(c->h_done);
+    if (c->ev0) cudaEventDestroy(c->ev0);
+    if (c->ev1) cudaEventDestroy(c->ev1);
+    if (c->stream) cudaStreamDestroy(c->stream);
+}
+
+// Tensor.java:493-501: GELU table over every f16 bit pattern (tanh form, evaluated as the
+// reference does: float arithmetic with the tanh in double).
+static void build_gelu_lut(std::vector<float> &t) {
+    t.resize(65536);
+    const float s = (float)std::sqrt(2.0 / M_PI);
+    for (int i = 0; i < 65536; ++i) {
+        __half_raw hr;
+        hr.x = (unsigned short)i;
+        const float x = __half2float(__half(hr));
+        t[i] = 0.5f * x * (1.0f + (float)std::tanh((double)(s * (x + 0.044715f * x * x * x))));
+    }
+}
+
+static int choose_split(int groups_x_heads, int len, int sms) {
+    int want = (2 * sms + groups_x_heads - 1) / std::max(1, groups_x_heads);
+    const int cap = std::max(1, (len + 63) / 64);
+    return std::max(1, std::min(want, cap));
+}
+
+extern "C" const char *w4j_last_error(void) { return g_err.c_str(); }
+extern "C" const char *w4j_version(void) { return "whisper4j-b200 0.1 (sm_100a)"; }
+
+extern "C" int w4j_ctx_create(const w4j_dims *dims, int device, int max_streams, int max_beam, w4j_ctx **out) {
+    if (!dims || !out) return set_err(W4J_ERR_ARG, "w4j_ctx_create: null argument");
+    *out = nullptr;
+    const int d = dims->n_text_state, H = dims->n_text_head;
+    if (d <= 0 || H <= 0 || d != H * kHeadDim)
+        return set_err(W4J_ERR_ARG, "n_text_state must equal n_text_head * 64 (got %d, %d)", d, H);
+    if (d % 64 != 0 || d > 4096) return set_err(W4J_ERR_ARG, "n_text_state %d unsupported", d);
+    if (dims->n_vocab <= 0 || dims->n_text_ctx <= 0 || dims->n_audio_ctx <= 0 || dims->n_text_layer <= 0)
+        return set_err(W4J_ERR_ARG, "invalid model dimensions");
+    if (max_streams < 1 || max_beam < 1 || max_beam > 8)
+        return set_err(W4J_ERR_ARG, "max_streams >= 1 and 1 <= max_beam <= 8 required");
+    int ndev = 0;
+    if (cudaGetDeviceCount(&ndev) != cudaSuccess || ndev == 0)
+        return set_err(W4J_ERR_CUDA, "no CUDA device available");
+    if (device < 0 || device >= ndev) return set_err(W4J_ERR_ARG, "device %d out of range", device);
+    CUDA_TRY(cudaSetDevice(device));
+    cudaDeviceProp prop;
+    CUDA_TRY(cudaGetDeviceProperties(&prop, device));
+    if (prop.major != 10) return set_err(W4J_ERR_STATE, "libwhisper4j_cuda is built for sm_100a (B200); device is sm_%d%d",
+                                         prop.major, prop.minor);
+    w4j_ctx *c = new w4j_ctx();
+    c->device = device;
+    c->dims = *dims;
+    c->V = dims->n_vocab;
+    c->C = dims->n_text_ctx;
+    c->A = dims->n_audio_ctx;
+    c->d = d;
+    c->H = H;
+    c->L = dims->n_text_layer;
+    c->max_streams = max_streams;
+    c->max_beam = max_beam;
+    c->n_slots = max_streams * max_beam + 1;  // + one private slot for forward without a cache
+    c->M_max = max_streams * max_beam;
+    c->sm_count = prop.multiProcessorCount;
+    c->layers.resize(c->L);
+    c->cache_len.assign(max_streams, 0);
+    c->has_xa.assign(max_streams, 0);
+    int rc = 0;
+    auto fail = [&](int r) {
+        free_all(c);
+        delete c;
+        return r;
+    };
+    if (cudaStreamCreateWithFlags(&c->stream, cudaStreamNonBlocking) != cudaSuccess) return fail(set_err(W4J_ERR_CUDA, "stream"));
+    cudaEventCreate(&c->ev0);
+    cudaEventCreate(&c->ev1);
+    if ((rc = (int)gemv_prepare()) != 0) return fail(set_err(W4J_ERR_CUDA, "kernel attributes: %s", cudaGetErrorString((cudaError_t)rc)));
+    const size_t V = c->V, C = c->C, A = c->A, L = c->L;
+    const size_t M = c->M_max;
+    // caches
+    const size_t cross = (size_t)max_streams * L * A * d;
+    const size_t self = (size_t)c->n_slots * L * C * d;
+    if ((rc = dalloc(c, &c->ck, cross)) || (rc = dalloc(c, &c->cv, cross)) || (rc = dalloc(c, &c->sk, self)) ||
+        (rc = dalloc(c, &c->sv, self)))
+        return fail(rc);
+    // activations
+    if ((rc = dalloc(c, &c->x, M * d)) || (rc = dalloc(c, &c->q, M * d)) || (rc = dalloc(c, &c->attn, M * d)) ||
+        (rc = dalloc(c, &c->h, M * 4 * d)) || (rc = dalloc(c, &c->xa_stage, A * d)))
+        return fail(rc);
+    c->attn_split_max = std::max((int)((C + 63) / 64), (int)((A + 63) / 64));
+    if ((rc = dalloc(c, &c->attn_part, M * H * c->attn_split_max * (2 + kHeadDim))) ||
+        (rc = dalloc(c, &c->attn_ctr, M * H)))
+        return fail(rc);
+    c->n_parts = logits_parts_for(c->V, c->sm_count);
+    if ((rc = dalloc(c, &c->logit_part, M * c->n_parts * kPartStride)) || (rc = dalloc(c, &c->ns_part, M * c->n_parts * 2)) ||
+        (rc = dalloc(c, &c->ns_value, M)) || (rc = dalloc(c, &c->masked, M * V)) || (rc = dalloc(c, &c->raw, C * V)))
+        return fail(rc);
+    // GELU table
+    {
+        std::vector<float> lut;
+        build_gelu_lut(lut);
+        if ((rc = dalloc(c, &c->gelu_lut, 65536))) return fail(rc);
+        if (cudaMemcpy(c->gelu_lut, lut.data(), 65536 * 4, cudaMemcpyHostToDevice) != cudaSuccess)
+            return fail(set_err(W4J_ERR_CUDA, "gelu table upload"));
+    }
+    // decode state
+    DecodeState &st = c->st;
+    st.n_ctx = (int)C;
+    st.V = (int)V;
+    st.hs = (int)C + 1;
+    st.dyn_stride = 2 * ((int)C + 1) + 8;
+    if ((rc = dalloc(c, &st.tok_in, M)) || (rc = dalloc(c, &st.seq_slot, M)) || (rc = dalloc(c, &st.seq_pos, M)) ||
+        (rc = dalloc(c, &st.active, M)) || (rc = dalloc(c, &st.table[0], M * C)) || (rc = dalloc(c, &st.table[1], M * C)) ||
+        (rc = dalloc(c, &st.hist[0], M * st.hs)) || (rc = dalloc(c, &st.hist[1], M * st.hs)) ||
+        (rc = dalloc(c, &st.hist_len[0], M)) || (rc = dalloc(c, &st.hist_len[1], M)) || (rc = dalloc(c, &st.lp[0], M)) ||
+        (rc = dalloc(c, &st.lp[1], M)) || (rc = dalloc(c, &st.dyn_list, M * st.dyn_stride)) ||
+        (rc = dalloc(c, &st.dyn_count, M)) || (rc = dalloc(c, &st.ranges, M * kMaxRanges)) ||
+        (rc = dalloc(c, &st.n_ranges, M)) || (rc = dalloc(c, &st.done, (size_t)max_streams)) ||
+        (rc = dalloc(c, &st.beam_par, (size_t)max_streams)) || (rc = dalloc(c, &st.nsp, (size_t)max_streams)) ||
+        (rc = dalloc(c, &st.fin_n, (size_t)max_streams)) || (rc = dalloc(c, &st.fin_tok, M * st.hs)) ||
+        (rc = dalloc(c, &st.fin_len, M)) || (rc = dalloc(c, &st.fin_lp, M)) ||
+        (rc = dalloc(c, &st.out_tok, (size_t)max_streams * st.hs)) || (rc = dalloc(c, &st.out_len, (size_t)max_streams)) ||
+        (rc = dalloc(c, &st.out_sum, (size_t)max_streams)) || (rc = dalloc(c, &st.err, 1)))
+        return fail(rc);
+    // per-call int arrays: prompt tokens [C][S], prompt positions [C][S], stream base [S],
+    // cross stream [S], suppress list [V], forward tokens [C], forward positions [C], misc [16]
+    c->int_area_n = 2 * C * (size_t)max_streams + 2 * (size_t)max_streams + V + 2 * C + 16;
+    if ((rc = dalloc(c, &c->d_int_area, c->int_area_n)) || (rc = dalloc(c, &c->d_done_snapshot, (size_t)max_streams)))
+        return fail(rc);
+    if (cudaMallocHost(&c->h_int_area, c->int_area_n * sizeof(int)) != cudaSuccess ||
+        cudaMallocHost(&c->h_done, (size_t)max_streams * sizeof(int)) != cudaSuccess)
+        return fail(set_err(W4J_ERR_OOM, "pinned host buffers"));
+    // fused self-attention bias (key bias defaults to zero)
+    for (int l = 0; l < c->L; ++l) {
+        LayerDev &ly = c->layers[l];
+        if ((rc = dalloc(c, &ly.bqkv, 3 * (size_t)d))) return fail(rc);
+    }
+    *out = c;
+    return W4J_OK;
+}
+
+extern "C" int w4j_ctx_destroy(w4j_ctx *c) {
+    if (!c) return W4J_OK;
+    {
+        std::lock_guard<std::mutex> g(c->mu);
+        cudaSetDevice(c->device);
+        cudaStreamSynchronize(c->stream);
+        free_all(c);
+    }
+    delete c;
+    return W4J_OK;
+}
+
+// ---------------------------------------------------------------------------
+// weight upload (raw GGML payloads)
+// ---------------------------------------------------------------------------
+static float half_bits_to_float(uint16_t b) {
+    __half_raw hr;
+    hr.x = b;
+    return __half2float(__half(hr));
+}
+
+// Host dequantisation of small tensors (biases, LayerNorm, positional table).
+static int host_f32(const void *data, size_t nbytes, int type, size_t n, std::vector<float> &out) {
+    out.resize(n);
+    if (type == W4J_GGML_F32) {
+        if (nbytes != n * 4) return set_err(W4J_ERR_ARG, "payload size %zu != %zu", nbytes, n * 4);
+        memcpy(out.data(), data, n * 4);
+    } else if (type == W4J_GGML_F16) {
+        if (nbytes != n * 2) return set_err(W4J_ERR_ARG, "payload size %zu != %zu", nbytes, n * 2);
+        const uint16_t *p = reinterpret_cast<const uint16_t *>(data);
+        for (size_t i = 0; i < n; ++i) out[i] = half_bits_to_float(p[i]);
+    } else if (type == W4J_GGML_Q8_0) {
+        if (n % 32 || nbytes != n / 32 * 34) return set_err(W4J_ERR_ARG, "Q8_0 payload size mismatch");
+        const uint8_t *p = reinterpret_cast<const uint8_t *>(data);
+        for (size_t b = 0; b < n / 32; ++b) {
+            const float sc = half_bits_to_float((uint16_t)(p[b * 34] | (p[b * 34 + 1] << 8)));
+            for (int i = 0; i < 32; ++i) out[b * 32 + i] = (float)(int8_t)p[b * 34 + 2 + i] * sc;
+        }
+    } else {
+        return set_err(W4J_ERR_ARG, "unsupported GGML type %d", type);
+    }
+    return 0;
+}
+
+static int upload_vec(w4j_ctx *c, float **dst, size_t n, const void *data, size_t nbytes, int type, size_t offset = 0) {
+    std::vector<float> v;
+    TRY(host_f32(data, nbytes, type, n, v));
+    if (!*dst) TRY(dalloc(c, dst, n));
+    CUDA_TRY(cudaMemcpy(*dst + offset, v.data(), n * 4, cudaMemcpyHostToDevice));
+    return 0;
+}
+
+// Matrix (N x K) into DMat `m` rows [row0, row0 + N) of a buffer holding `rows_total` rows.
+static int upload_mat(w4j_ctx *c, DMat &m, int rows_total, int row0, int N, int K, const void *data, size_t nbytes,
+                      int type, int *type_slot = nullptr) {
+    const int want = type == W4J_GGML_Q8_0 ? WT_Q8 : WT_F16;
+    if (type != W4J_GGML_F16 && type != W4J_GGML_F32 && type != W4J_GGML_Q8_0)
+        return set_err(W4J_ERR_ARG, "unsupported GGML type %d for a matrix (F32, F16, Q8_0 accepted)", type);
+    if (type == W4J_GGML_Q8_0 && K % 32) return set_err(W4J_ERR_ARG, "Q8_0 rows must be a multiple of 32");
+    const size_t n = (size_t)N * K;
+    const size_t expect = type == W4J_GGML_F32 ? n * 4 : type == W4J_GGML_F16 ? n * 2 : n / 32 * 34;
+    if (nbytes != expect) return set_err(W4J_ERR_ARG, "payload size %zu, expected %zu", nbytes, expect);
+    if (m.type == 0) {
+        m.type = want;
+        m.N = rows_total;
+        m.K = K;
+        if (want == WT_F16) {
+            __half *p = nullptr;
+            TRY(dalloc(c, &p, (size_t)rows_total * K));
+            m.h = p;
+        } else {
+            int8_t *q = nullptr;
+            __half *s = nullptr;
+            TRY(dalloc(c, &q, (size_t)rows_total * K));
+            TRY(dalloc(c, &s, (size_t)rows_total * (K / 32)));
+            m.q = q;
+            m.s = s;
+        }
+    } else if (m.type != want) {
+        return set_err(W4J_ERR_ARG, "attn.query/key/value of one layer must share a storage type (F16/F32 vs Q8_0)");
+    }
+    if (type_slot) *type_slot = want;
+    void *stage = nullptr;
+    CUDA_TRY(cudaMalloc(&stage, nbytes));
+    cudaError_t e = cudaMemcpy(stage, data, nbytes, cudaMemcpyHostToDevice);
+    if (e == cudaSuccess) {
+        if (type == W4J_GGML_F16) {
+            e = cudaMemcpy(const_cast<__half *>(m.h) + (size_t)row0 * K, stage, nbytes, cudaMemcpyDeviceToDevice);
+        } else if (type == W4J_GGML_F32) {
+            e = launch_f32_to_f16(reinterpret_cast<const float *>(stage), const_cast<__half *>(m.h) + (size_t)row0 * K, n, 0);
+        } else {
+            e = launch_q8_repack(stage, N, K, const_cast<int8_t *>(m.q) + (size_t)row0 * K,
+                                 const_cast<__half *>(m.s) + (size_t)row0 * (K / 32), 0);
+        }
+    }
+    if (e == cudaSuccess) e = cudaDeviceSynchronize();
+    cudaFree(stage);
+    if (e != cudaSuccess) return set_err(W4J_ERR_CUDA, "matrix upload: %s", cudaGetErrorString(e));
+    return 0;
+}
+
+extern "C" int w4j_upload_tensor(w4j_ctx *c, const char *name, int type, const int64_t *ne, int n_dims,
+                                 const void *data, size_t nbytes) {
+    if (!c || !name || !ne || !data) return set_err(W4J_ERR_ARG, "w4j_upload_tensor: null argument");
+    std::lock_guard<std::mutex> g(c->mu);
+    CUDA_TRY(cudaSetDevice(c->device));
+    const std::string nm(name);
+    if (nm.rfind("decoder.", 0) != 0) return 1;  // encoder tensors are not on this path
+    if (n_dims < 1 || n_dims > 4) return set_err(W4J_ERR_ARG, "%s: n_dims %d", name, n_dims);
+    int64_t nel = 1;
+    for (int i = 0; i < n_dims; ++i) {
+        if (ne[i] <= 0) return set_err(W4J_ERR_ARG, "%s: bad shape", name);
+        nel *= ne[i];
+    }
+    const int d = c->d;
+    auto shape_is = [&](int64_t in, int64_t out) { return ne[0] == in && nel == in * out; };
+    std::string s = nm.substr(8);
+    if (s == "token_embedding.weight") {
+        if (!shape_is(d, c->V)) return set_err(W4J_ERR_ARG, "%s: expected (%d, %d)", name, c->V, d);
+        TRY(upload_mat(c, c->E, c->V, 0, c->V, d, data, nbytes, type));
+    } else if (s == "positional_embedding") {
+        if (!shape_is(d, c->C)) return set_err(W4J_ERR_ARG, "%s: expected (%d, %d)", name, c->C, d);
+        TRY(upload_vec(c, &c->pos_emb, (size_t)c->C * d, data, nbytes, type));
+    } else if (s == "ln.weight" || s == "ln.bias") {
+        if (nel != d) return set_err(W4J_ERR_ARG, "%s: expected %d elements", name, d);
+        TRY(upload_vec(c, s == "ln.weight" ? &c->lng : &c->lnb, d, data, nbytes, type));
+    } else {
+        int li = -1, off = 0;
+        if (sscanf(s.c_str(), "blocks.%d.%n", &li, &off) != 1 || li < 0 || li >= c->L)
+            return set_err(W4J_ERR_ARG, "unknown decoder tensor %s", name);
+        LayerDev &ly = c->layers[li];
+        const std::string t = s.substr(off);
+        struct MatRole { const char *nm; DMat *m; int rows_total, row0, N, K; };
+        const MatRole mats[] = {
+            {"attn.query.weight", &ly.qkv, 3 * d, 0, d, d},         {"attn.key.weight", &ly.qkv, 3 * d, d, d, d},
+            {"attn.value.weight", &ly.qkv, 3 * d, 2 * d, d, d},     {"attn.out.weight", &ly.o, d, 0, d, d},
+            {"cross_attn.query.weight", &ly.xq, d, 0, d, d},        {"cross_attn.key.weight", &ly.xk, d, 0, d, d},
+            {"cross_attn.value.weight", &ly.xv, d, 0, d, d},        {"cross_attn.out.weight", &ly.xo, d, 0, d, d},
+            {"mlp.0.weight", &ly.m0, 4 * d, 0, 4 * d, d},           {"mlp.2.weight", &ly.m2, d, 0, d, 4 * d},
+        };
+        for (const MatRole &r : mats) {
+            if (t != r.nm) continue;
+            if (!shape_is(r.K, r.N)) return set_err(W4J_ERR_ARG, "%s: expected (%d, %d)", name, r.N, r.K);
+            TRY(upload_mat(c, *r.m, r.rows_total, r.row0, r.N, r.K, data, nbytes, type));
+            c->uploaded.insert(nm);
+            return W4J_OK;
+        }
+        struct VecRole { const char *nm; float **dst; int n; size_t off; };
+        const VecRole vecs[] = {
+            {"attn.query.bias", &ly.bqkv, d, 0},          {"attn.key.bias", &ly.bqkv, d, (size_t)d},
+            {"attn.value.bias", &ly.bqkv, d, 2 * (size_t)d}, {"attn.out.bias", &ly.bo, d, 0},
+            {"cross_attn.query.bias", &ly.bxq, d, 0},     {"cross_attn.key.bias", &ly.bxk, d, 0},
+            {"cross_attn.value.bias", &ly.bxv, d, 0},     {"cross_attn.out.bias", &ly.bxo, d, 0},
+            {"mlp.0.bias", &ly.bm0, 4 * d, 0},            {"mlp.2.bias", &ly.bm2, d, 0},
+            {"attn_ln.weight", &ly.ln1g, d, 0},           {"attn_ln.bias", &ly.ln1b, d, 0},
+            {"cross_attn_ln.weight", &ly.ln2g, d, 0},     {"cross_attn_ln.bias", &ly.ln2b, d, 0},
+            {"mlp_ln.weight", &ly.ln3g, d, 0},            {"mlp_ln.bias", &ly.ln3b, d, 0},
+        };
+        bool found = false;
+        for (const VecRole &r : vecs) {
+            if (t != r.nm) continue;
+            if (nel != r.n) return set_err(W4J_ERR_ARG, "%s: expected %d elements", name, r.n);
+            TRY(upload_vec(c, r.dst, r.n, data, nbytes, type, r.off));
+            found = true;
+            break;
+        }
+        if (!found) return set_err(W4J_ERR_ARG, "unknown decoder tensor %s", name);
+    }
+    c->uploaded.insert(nm);
+    return W4J_OK;
+}
+
+static std::vector<std::string> required_names(int L) {
+    std::vector<std::string> r = {"decoder.token_embedding.weight", "decoder.positional_embedding",
+                                  "decoder.ln.weight", "decoder.ln.bias"};
+    const char *per[] = {"attn.query.weight", "attn.query.bias", "attn.key.weight", "attn.value.weight",
+                         "attn.value.bias", "attn.out.weight", "attn.out.bias", "attn_ln.weight", "attn_ln.bias",
+                         "cross_attn.query.weight", "cross_attn.query.bias", "cross_attn.key.weight",
+                         "cross_attn.value.weight", "cross_attn.value.bias", "cross_attn.out.weight",
+                         "cross_attn.out.bias", "cross_attn_ln.weight", "cross_attn_ln.bias", "mlp.0.weight",
+                         "mlp.0.bias", "mlp.2.weight", "mlp.2.bias", "mlp_ln.weight", "mlp_ln.bias"};
+    for (int l = 0; l < L; ++l)
+        for (const char *p : per) r.push_back("decoder.blocks." + std::to_string(l) + "." + p);
+    return r;
+}
+
+static int check_ready(w4j_ctx *c) {
+    for (const std::string &n : required_names(c->L))
+        if (!c->uploaded.count(n)) return set_err(W4J_ERR_STATE, "weight not found: %s", n.c_str());
+    return 0;
+}
+
+extern "C" int w4j_finalize(w4j_ctx *c) {
+    if (!c) return set_err(W4J_ERR_ARG, "null context");
+    std::lock_guard<std::mutex> g(c->mu);
+    return check_ready(c);
+}
+
+// ---------------------------------------------------------------------------
+// cross K/V prefill
+// ---------------------------------------------------------------------------
+static int prefill(w4j_ctx *c, int slot, const float *xa_dev) {
+    for (int l = 0; l < c->L; ++l) {
+        LayerDev &ly = c->layers[l];
+        const size_t off = ((size_t)slot * c->L + l) * (size_t)c->H * c->A * kHeadDim;
+        CUDA_TRY(launch_cross_kv(xa_dev, c->A, c->d, ly.xk, ly.xv, ly.bxk, ly.bxv, c->ck + off, c->cv + off, c->H,
+                                 c->stream));
+    }
+    CUDA_TRY(cudaStreamSynchronize(c->stream));
+    c->has_xa[slot] = 1;
+    c->cache_len[slot] = 0;
+    return 0;
+}
+
+extern "C" int w4j_set_encoder_output(w4j_ctx *c, int slot, const float *xa, int n_audio_ctx) {
+    if (!c || !xa) return set_err(W4J_ERR_ARG, "w4j_set_encoder_output: null argument");
+    std::lock_guard<std::mutex> g(c->mu);
+    CUDA_TRY(cudaSetDevice(c->device));
+    TRY(check_ready(c));
+    if (slot < 0 || slot >= c->max_streams) return set_err(W4J_ERR_ARG, "slot %d out of range", slot);
+    if (n_audio_ctx != c->A) return set_err(W4J_ERR_ARG, "encoder output has %d frames, model expects %d", n_audio_ctx, c->A);
+    CUDA_TRY(cudaMemcpyAsync(c->xa_stage, xa, (size_t)c->A * c->d * 4, cudaMemcpyHostToDevice, c->stream));
+    return prefill(c, slot, c->xa_stage);
+}
+
+extern "C" int w4j_set_encoder_output_device(w4j_ctx *c, int slot, const float *xa, int n_audio_ctx) {
+    if (!c || !xa) return set_err(W4J_ERR_ARG, "w4j_set_encoder_output_device: null argument");
+    std::lock_guard<std::mutex> g(c->mu);
+    CUDA_TRY(cudaSetDevice(c->device));
+    TRY(check_ready(c));
+    if (slot < 0 || slot >= c->max_streams) return set_err(W4J_ERR_ARG, "slot %d out of range", slot);
+    if (n_audio_ctx != c->A) return set_err(W4J_ERR_ARG, "encoder output has %d frames, model expects %d", n_audio_ctx, c->A);
+    return prefill(c, slot, xa);
+}
+
+// ---------------------------------------------------------------------------
+// one decoder pass over M rows (all layers)
+// ---------------------------------------------------------------------------
+struct PassArgs {
+    int M;                 // rows (sequences)
+    const int *tok, *pos;  // [M]
+    const int *seq_slot;   // [M] self-cache slots
+    const int *table;      // [M][C] or null
+    const int *active;     // [M] or null
+    // cross attention grouping
+    int groups, nq;
+    const int *cross_stream;  // [groups]
+    const int *group_active;  // [groups] or null
+};
+
+static int run_layers(w4j_ctx *c, const PassArgs &pa, long long &launches) {
+    const bool pdl = true;
+    const int d = c->d;
+    const int self_split = choose_split(pa.M * c->H, c->C, c->sm_count);
+    const int cross_split = choose_split(pa.groups * c->H, c->A, c->sm_count);
+    for (int l = 0; l < c->L; ++l) {
+        LayerDev &ly = c->layers[l];
+        GemvArgs g;
+        g.W = ly.qkv;
+        g.bias = ly.bqkv;
+        g.M = pa.M;
+        g.in_mode = l == 0 ? IN_EMBED_LN : IN_LN;
+        g.act = c->x;
+        g.ln_g = ly.ln1g;
+        g.ln_b = ly.ln1b;
+        g.E = c->E;
+        g.pos_emb = c->pos_emb;
+        g.tok = pa.tok;
+        g.pos = pa.pos;
+        g.x_out = c->x;
+        g.out_mode = OUT_QKV;
+        g.y = c->q;
+        g.kcache = c->sk;
+        g.vcache = c->sv;
+        g.seq_slot = pa.seq_slot;
+        g.layer = l;
+        g.n_layer = c->L;
+        g.n_head = c->H;
+        g.n_ctx = c->C;
+        g.active = pa.active;
+        CUDA_TRY(launch_gemv(g, c->stream, pdl));
+
+        AttnArgs sa;
+        sa.q = c->q;
+        sa.d = d;
+        sa.n_head = c->H;
+        sa.n_layer = c->L;
+        sa.layer = l;
+        sa.cross = 0;
+        sa.kc = c->sk;
+        sa.vc = c->sv;
+        sa.n_ctx = c->C;
+        sa.seq_slot = pa.seq_slot;
+        sa.table = pa.table;
+        sa.pos = pa.pos;
+        sa.nq = 1;
+        sa.groups = pa.M;
+        sa.nsplit = self_split;
+        sa.part = c->attn_part;
+        sa.counters = c->attn_ctr;
+        sa.out = c->attn;
+        sa.active = pa.active;
+        CUDA_TRY(launch_attn(sa, c->stream, pdl));
+
+        GemvArgs go;
+        go.W = ly.o;
+        go.bias = ly.bo;
+        go.M = pa.M;
+        go.in_mode = IN_ACT;
+        go.act = c->attn;
+        go.out_mode = OUT_RESIDUAL;
+        go.y = c->x;
+        go.active = pa.active;
+        CUDA_TRY(launch_gemv(go, c->stream, pdl));
+
+        GemvArgs gq;
+        gq.W = ly.xq;
+        gq.bias = ly.bxq;
+        gq.M = pa.M;
+        gq.in_mode = IN_LN;
+        gq.act = c->x;
+        gq.ln_g = ly.ln2g;
+        gq.ln_b = ly.ln2b;
+        gq.out_mode = OUT_STORE;
+        gq.y = c->q;
+        CUDA_TRY(launch_gemv(gq, c->stream, pdl));
+
+        AttnArgs ca;
+        ca.q = c->q;
+        ca.d = d;
+        ca.n_head = c->H;
+        ca.n_layer = c->L;
+        ca.layer = l;
+        ca.cross = 1;
+        ca.kc = c->ck;
+        ca.vc = c->cv;
+        ca.n_audio = c->A;
+        ca.stream_of_group = pa.cross_stream;
+        ca.nq = pa.nq;
+        ca.groups = pa.groups;
+        ca.nsplit = cross_split;
+        ca.part = c->attn_part;
+        ca.counters = c->attn_ctr;
+        ca.out = c->attn;
+        ca.active = pa.group_active;
+        CUDA_TRY(launch_attn(ca, c->stream, pdl));
+
+        GemvArgs gxo;
+        gxo.W = ly.xo;
+        gxo.bias = ly.bxo;
+        gxo.M = pa.M;
+        gxo.in_mode = IN_ACT;
+        gxo.act = c->attn;
+        gxo.out_mode = OUT_RESIDUAL;
+        gxo.y = c->x;
+        gxo.active = pa.active;
+        CUDA_TRY(launch_gemv(gxo, c->stream, pdl));
+
+        GemvArgs g1;
+        g1.W = ly.m0;
+        g1.bias = ly.bm0;
+        g1.M = pa.M;
+        g1.in_mode = IN_LN;
+        g1.act = c->x;
+        g1.ln_g = ly.ln3g;
+        g1.ln_b = ly.ln3b;
+        g1.out_mode = OUT_GELU;
+        g1.y = c->h;
+        g1.gelu_lut = c->gelu_lut;
+        CUDA_TRY(launch_gemv(g1, c->stream, pdl));
+
+        GemvArgs g2;
+        g2.W = ly.m2;
+        g2.bias = ly.bm2;
+        g2.M = pa.M;
+        g2.in_mode = IN_ACT;
+        g2.act = c->h;
+        g2.out_mode = OUT_RESIDUAL;
+        g2.y = c->x;
+        g2.active = pa.active;
+        CUDA_TRY(launch_gemv(g2, c->stream, pdl));
+        launches += 8;
+    }
+    return 0;
+}
+
+static LogitsArgs logits_args(w4j_ctx *c, int M, const int *active) {
+    LogitsArgs la;
+    la.E = c->E;
+    la.x = c->x;
+    la.ln_g = c->lng;
+    la.ln_b = c->lnb;
+    la.M = M;
+    la.V = c->V;
+    la.d = c->d;
+    la.part = c->logit_part;
+    la.active = active;
+    return la;
+}
+
+// ---------------------------------------------------------------------------
+// forward (WhisperDecoder.forward)
+// ---------------------------------------------------------------------------
+extern "C" int w4j_forward(w4j_ctx *c, int slot, const int32_t *tokens, int n, int use_cache, float *out_logits) {
+    if (!c || !tokens || !out_logits) return set_err(W4J_ERR_ARG, "w4j_forward: null argument");
+    std::lock_guard<std::mutex> g(c->mu);
+    CUDA_TRY(cudaSetDevice(c->device));
+    TRY(check_ready(c));
+    if (slot < 0 || slot >= c->max_streams) return set_err(W4J_ERR_ARG, "slot %d out of range", slot);
+    if (!c->has_xa[slot]) return set_err(W4J_ERR_STATE, "no encoder output set for slot %d", slot);
+    if (n <= 0) return set_err(W4J_ERR_ARG, "empty token list");
+    for (int i = 0; i < n; ++i)
+        if (tokens[i] < 0 || tokens[i] >= c->V) return set_err(W4J_ERR_ARG, "token id %d out of range", tokens[i]);
+    const int start = use_cache ? c->cache_len[slot] : 0;
+    if (start + n > c->C)
+        return set_err(W4J_ERR_ARG, "sequence of %d tokens exceeds n_text_ctx %d", start + n, c->C);
+    const int phys = use_cache ? slot * c->max_beam : c->n_slots - 1;
+    // int area layout for forward: tok[C], pos[C], slot[1], stream[1]
+    int *hi = c->h_int_area;
+    int *di = c->d_int_area;
+    for (int i = 0; i < n; ++i) {
+        hi[i] = tokens[i];
+        hi[c->C + i] = start + i;
+    }
+    hi[2 * c->C] = phys;
+    hi[2 * c->C + 1] = slot;
+    CUDA_TRY(cudaMemcpyAsync(di, hi, (2 * (size_t)c->C + 2) * 4, cudaMemcpyHostToDevice, c->stream));
+    long long launches = 0;
+    for (int t = 0; t < n; ++t) {
+        PassArgs pa{};
+        pa.M = 1;
+        pa.tok = di + t;
+        pa.pos = di + c->C + t;
+        pa.seq_slot = di + 2 * c->C;
+        pa.groups = 1;
+        pa.nq = 1;
+        pa.cross_stream = di + 2 * c->C + 1;
+        TRY(run_layers(c, pa, launches));
+        LogitsArgs la = logits_args(c, 1, nullptr);
+        la.raw_out = c->raw + (size_t)t * c->V;
+        CUDA_TRY(launch_logits(la, c->n_parts, c->stream, true));
+    }
+    CUDA_TRY(cudaMemcpyAsync(out_logits, c->raw, (size_t)n * c->V * 4, cudaMemcpyDeviceToHost, c->stream));
+    CUDA_TRY(cudaStreamSynchronize(c->stream));
+    if (use_cache) c->cache_len[slot] = start + n;
+    return W4J_OK;
+}
+
+extern "C" int w4j_reset_cache(w4j_ctx *c, int slot) {
+    if (!c) return set_err(W4J_ERR_ARG, "null context");
+    std::lock_guard<std::mutex> g(c->mu);
+    if (slot < 0 || slot >= c->max_streams) return set_err(W4J_ERR_ARG, "slot %d out of range", slot);
+    c->cache_len[slot] = 0;
+    return W4J_OK;
+}
+
+// ---------------------------------------------------------------------------
+// decode loops
+// ---------------------------------------------------------------------------
+enum { MODE_GREEDY = 0, MODE_SAMPLE = 1, MODE_BEAM = 2 };
+
+struct CallArgs {
+    const int32_t *slots;
+    int S;
+    const int32_t *prompts;
+    int n_prompt;
+    int eot, max_tokens;
+    const int32_t *suppress;
+    int n_sup;
+    int ns;
+    float temperature;
+    int ts_begin;
+    unsigned long long seed;
+    int beam;
+};
+
+// Device int area layout for a decode call (offsets in ints).
+struct CallLayout {
+    size_t ptok, ppos, base, cross, sup, total;
+};
+
+static CallLayout call_layout(w4j_ctx *c, int S, int n_prompt, int n_sup) {
+    CallLayout L;
+    L.ptok = 0;
+    L.ppos = L.ptok + (size_t)n_prompt * S;
+    L.base = L.ppos + (size_t)n_prompt * S;
+    L.cross = L.base + S;
+    L.sup = L.cross + S;
+    L.total = L.sup + std::max(1, n_sup);
+    (void)c;
+    return L;
+}
+
+static int validate_call(w4j_ctx *c, const CallArgs &a) {
+    if (!a.slots || !a.prompts) return set_err(W4J_ERR_ARG, "null argument");
+    if (a.S < 1 || a.S > c->max_streams) return set_err(W4J_ERR_ARG, "n_streams %d out of [1, %d]", a.S, c->max_streams);
+    if (a.beam < 1 || a.beam > c->max_beam)
+        return set_err(W4J_ERR_ARG, "beam %d out of [1, %d] (context max_beam)", a.beam, c->max_beam);
+    if (a.n_prompt < 1 || a.n_prompt > c->C) return set_err(W4J_ERR_ARG, "prompt length %d", a.n_prompt);
+    if (a.eot < 0 || a.eot >= c->V) return set_err(W4J_ERR_ARG, "eot token %d out of range", a.eot);
+    if (a.max_tokens < 0) return set_err(W4J_ERR_ARG, "max_tokens must be >= 0");
+    if (a.beam > 1 && a.max_tokens < 1) return set_err(W4J_ERR_ARG, "beam search needs max_tokens >= 1");
+    if (a.n_prompt + std::max(a.max_tokens, 1) - 1 > c->C)
+        return set_err(W4J_ERR_ARG, "prompt (%d) + max_tokens (%d) exceeds the %d-position self-attention cache",
+                       a.n_prompt, a.max_tokens, c->C);
+    if (a.n_sup < 0 || (a.n_sup > 0 && !a.suppress)) return set_err(W4J_ERR_ARG, "suppress list");
+    if (a.n_sup > c->V) return set_err(W4J_ERR_ARG, "suppress list longer than the vocabulary");
+    if (a.temperature < 0.f || !(a.temperature == a.temperature)) return set_err(W4J_ERR_ARG, "temperature");
+    std::set<int> seen;
+    for (int s = 0; s < a.S; ++s) {
+        const int sl = a.slots[s];
+        if (sl < 0 || sl >= c->max_streams) return set_err(W4J_ERR_ARG, "slot %d out of range", sl);
+        if (!seen.insert(sl).second) return set_err(W4J_ERR_ARG, "slot %d listed twice", sl);
+        if (!c->has_xa[sl]) return set_err(W4J_ERR_STATE, "no encoder output set for slot %d", sl);
+    }
+    for (int i = 0; i < a.S * a.n_prompt; ++i)
+        if (a.prompts[i] < 0 || a.prompts[i] >= c->V) return set_err(W4J_ERR_ARG, "prompt token %d out of range", a.prompts[i]);
+    return 0;
+}
+
+// Upload per-call inputs and reset the decode state.
+static int prepare_call(w4j_ctx *c, const CallArgs &a, const CallLayout &Ly) {
+    if (Ly.total > c->int_area_n) return set_err(W4J_ERR_ARG, "call too large for the context");
+    int *hi = c->h_int_area;
+    for (int s = 0; s < a.S; ++s)
+        for (int i = 0; i < a.n_prompt; ++i) {
+            hi[Ly.ptok + (size_t)i * a.S + s] = a.prompts[(size_t)s * a.n_prompt + i];
+            hi[Ly.ppos + (size_t)i * a.S + s] = i;
+        }
+    for (int s = 0; s < a.S; ++s) {
+        hi[Ly.base + s] = a.slots[s] * c->max_beam;
+        hi[Ly.cross + s] = a.slots[s];
+    }
+    for (int i = 0; i < a.n_sup; ++i) hi[Ly.sup + i] = a.suppress[i];
+    CUDA_TRY(cudaMemcpyAsync(c->d_int_area, hi, Ly.total * 4, cudaMemcpyHostToDevice, c->stream));
+    // per-sequence state
+    const int B = a.beam, M = a.S * B;
+    std::vector<int> slot(M), pos(M, a.n_prompt - 1), ones(M, 1);
+    for (int s = 0; s < a.S; ++s)
+        for (int b = 0; b < B; ++b) slot[s * B + b] = a.slots[s] * c->max_beam + b;
+    DecodeState &st = c->st;
+    CUDA_TRY(cudaMemcpyAsync(st.seq_slot, slot.data(), M * 4, cudaMemcpyHostToDevice, c->stream));
+    CUDA_TRY(cudaMemcpyAsync(st.seq_pos, pos.data(), M * 4, cudaMemcpyHostToDevice, c->stream));
+    CUDA_TRY(cudaMemcpyAsync(st.active, ones.data(), M * 4, cudaMemcpyHostToDevice, c->stream));
+    CUDA_TRY(cudaMemsetAsync(st.hist_len[0], 0, M * 4, c->stream));
+    CUDA_TRY(cudaMemsetAsync(st.hist_len[1], 0, M * 4, c->stream));
+    CUDA_TRY(cudaMemsetAsync(st.lp[0], 0, M * 8, c->stream));
+    CUDA_TRY(cudaMemsetAsync(st.lp[1], 0, M * 8, c->stream));
+    CUDA_TRY(cudaMemsetAsync(st.dyn_count, 0, M * 4, c->stream));
+    CUDA_TRY(cudaMemsetAsync(st.n_ranges, 0, M * 4, c->stream));
+    CUDA_TRY(cudaMemsetAsync(st.done, 0, a.S * 4, c->stream));
+    CUDA_TRY(cudaMemsetAsync(st.beam_par, 0, a.S * 4, c->stream));
+    CUDA_TRY(cudaMemsetAsync(st.fin_n, 0, a.S * 4, c->stream));
+    CUDA_TRY(cudaMemsetAsync(st.nsp, 0, a.S * 4, c->stream));
+    CUDA_TRY(cudaMemsetAsync(st.err, 0, 4, c->stream));
+    st.n_streams = a.S;
+    st.beam = B;
+    st.max_tokens = a.max_tokens;
+    st.n_prompt = a.n_prompt;
+    st.eot = a.eot;
+    st.ts_begin = a.ts_begin;
+    st.ns_token = (a.ns >= 0 && a.ns < c->V) ? a.ns : -1;
+    st.n_suppress = a.n_sup;
+    st.temperature = a.temperature;
+    st.seed = a.seed;
+    st.n_parts = c->n_parts;
+    st.suppress = c->d_int_area + Ly.sup;
+    st.stream_base = c->d_int_area + Ly.base;
+    return 0;
+}
+
+static MaskArgs mask_args(w4j_ctx *c) {
+    MaskArgs mk;
+    mk.static_list = c->st.suppress;
+    mk.n_static = c->st.n_suppress;
+    mk.dyn_list = c->st.dyn_list;
+    mk.dyn_count = c->st.dyn_count;
+    mk.dyn_stride = c->st.dyn_stride;
+    mk.ranges = c->st.ranges;
+    mk.n_ranges = c->st.n_ranges;
+    return mk;
+}
+
+// The prompt: one pass per prompt token over all streams (beam 0 slots), then the first decision.
+static int run_prompt(w4j_ctx *c, const CallArgs &a, const CallLayout &Ly, int mode, long long &launches) {
+    DecodeState &st = c->st;
+    const int S = a.S;
+    const int *di = c->d_int_area;
+    for (int i = 0; i < a.n_prompt; ++i) {
+        PassArgs pa{};
+        pa.M = S;
+        pa.tok = di + Ly.ptok + (size_t)i * S;
+        pa.pos = di + Ly.ppos + (size_t)i * S;
+        pa.seq_slot = st.stream_base;
+        pa.groups = S;
+        pa.nq = 1;
+        pa.cross_stream = di + Ly.cross;
+        TRY(run_layers(c, pa, launches));
+        const bool last = i == a.n_prompt - 1;
+        const bool ns_here = i == 0 && st.ns_token >= 0;
+        if (!last && !ns_here) continue;
+        if (last) {
+            CUDA_TRY(launch_init_masks(st, mode == MODE_BEAM, c->stream));
+            ++launches;
+        }
+        LogitsArgs la = logits_args(c, S, nullptr);
+        if (last) {
+            la.use_mask = 1;
+            la.mask = mask_args(c);
+            la.topk = mode == MODE_BEAM ? a.beam : 0;
+            if (mode == MODE_SAMPLE) la.masked_out = c->masked;
+        }
+        if (ns_here) {
+            la.ns_token = st.ns_token;
+            la.ns_part = c->ns_part;
+            la.ns_value = c->ns_value;
+        }
+        CUDA_TRY(launch_logits(la, c->n_parts, c->stream, !last));
+        ++launches;
+        if (ns_here) {
+            CUDA_TRY(launch_nsp(st, c->ns_part, c->n_parts, c->ns_value, c->stream, true));
+            ++launches;
+        }
+        if (last) {
+            const int sel = mode == MODE_BEAM ? SEL_BEAM_INIT : mode == MODE_SAMPLE ? SEL_SAMPLE : SEL_GREEDY;
+            CUDA_TRY(launch_select(st, sel, 0, c->logit_part, c->n_parts, c->masked, 0, c->stream, true));
+            ++launches;
+        }
+    }
+    return 0;
+}
+
+// One decode step after the prompt (captured into a graph).
+static int enqueue_step(w4j_ctx *c, const CallArgs &a, const CallLayout &Ly, int mode, int parity, long long &launches) {
+    DecodeState &st = c->st;
+    const int S = a.S, B = a.beam, M = S * B;
+    PassArgs pa{};
+    pa.M = M;
+    pa.tok = st.tok_in;
+    pa.pos = st.seq_pos;
+    pa.seq_slot = st.seq_slot;
+    pa.table = mode == MODE_BEAM ? st.table[parity] : nullptr;
+    pa.active = st.active;
+    pa.groups = S;
+    pa.nq = B;
+    pa.cross_stream = c->d_int_area + Ly.cross;
+    pa.group_active = B == 1 ? st.active : nullptr;
+    TRY(run_layers(c, pa, launches));
+    LogitsArgs la = logits_args(c, M, st.active);
+    la.use_mask = 1;
+    la.mask = mask_args(c);
+    la.topk = mode == MODE_BEAM ? B + 1 : 0;
+    if (mode == MODE_SAMPLE) la.masked_out = c->masked;
+    CUDA_TRY(launch_logits(la, c->n_parts, c->stream, true));
+    const int sel = mode == MODE_BEAM ? SEL_BEAM : mode == MODE_SAMPLE ? SEL_SAMPLE : SEL_GREEDY;
+    CUDA_TRY(launch_select(st, sel, parity, c->logit_part, c->n_parts, c->masked, 0, c->stream, true));
+    launches += 2;
+    return 0;
+}
+
+static int get_step_graph(w4j_ctx *c, const CallArgs &a, const CallLayout &Ly, int mode, int parity,
+                          cudaGraphExec_t *out, long long &per_step) {
+    GraphKey k;
+    memset(&k, 0, sizeof k);
+    k.mode = mode * 2 + parity;
+    k.S = a.S;
+    k.B = a.beam;
+    k.eot = a.eot;
+    k.ts_begin = a.ts_begin;
+    k.n_sup = a.n_sup;
+    k.max_tokens = a.max_tokens;
+    k.ns = c->st.ns_token;
+    k.n_prompt = a.n_prompt;
+    k.temperature = a.temperature;
+    k.seed = a.seed;
+    long long launches = 0;
+    auto it = c->graphs.find(k);
+    if (it != c->graphs.end()) {
+        *out = it->second;
+        per_step = (long long)c->L * 8 + 2;
+        return 0;
+    }
+    if (c->graphs.size() >= 16) {
+        for (auto &kv : c->graphs) cudaGraphExecDestroy(kv.second);
+        c->graphs.clear();
+    }
+    cudaGraph_t graph = nullptr;
+    CUDA_TRY(cudaStreamBeginCapture(c->stream, cudaStreamCaptureModeThreadLocal));
+    int rc = enqueue_step(c, a, Ly, mode, parity, launches);
+    cudaError_t e = cudaStreamEndCapture(c->stream, &graph);
+    if (rc < 0) {
+        if (graph) cudaGraphDestroy(graph);
+        return rc;
+    }
+    if (e != cudaSuccess) return set_err(W4J_ERR_CUDA, "graph capture: %s", cudaGetErrorString(e));
+    cudaGraphExec_t exec = nullptr;
+    e = cudaGraphInstantiate(&exec, graph, 0);
+    cudaGraphDestroy(graph);
+    if (e != cudaSuccess) return set_err(W4J_ERR_CUDA, "graph instantiate: %s", cudaGetErrorString(e));
+    c->graphs[k] = exec;
+    *out = exec;
+    per_step = launches;
+    return 0;
+}
+
+static int read_results(w4j_ctx *c, const CallArgs &a, w4j_result *r) {
+    DecodeState &st = c->st;
+    const int S = a.S;
+    std::vector<int> toks((size_t)S * std::max(a.max_tokens, 1)), lens(S), errw(1);
+    std::vector<double> sums(S);
+    std::vector<float> nsp(S);
+    if (a.max_tokens > 0)
+        CUDA_TRY(cudaMemcpyAsync(toks.data(), st.out_tok, (size_t)S * a.max_tokens * 4, cudaMemcpyDeviceToHost, c->stream));
+    CUDA_TRY(cudaMemcpyAsync(lens.data(), st.out_len, S * 4, cudaMemcpyDeviceToHost, c->stream));
+    CUDA_TRY(cudaMemcpyAsync(sums.data(), st.out_sum, S * 8, cudaMemcpyDeviceToHost, c->stream));
+    CUDA_TRY(cudaMemcpyAsync(nsp.data(), st.nsp, S * 4, cudaMemcpyDeviceToHost, c->stream));
+    CUDA_TRY(cudaMemcpyAsync(errw.data(), st.err, 4, cudaMemcpyDeviceToHost, c->stream));
+    CUDA_TRY(cudaStreamSynchronize(c->stream));
+    if (errw[0]) return set_err(W4J_ERR_STATE, "device bookkeeping overflow (mask list)");
+    for (int s = 0; s < S; ++s) {
+        const int n = std::min(lens[s], a.max_tokens);
+        if (r->tokens)
+            for (int i = 0; i < n; ++i) r->tokens[(size_t)s * a.max_tokens + i] = toks[(size_t)s * a.max_tokens + i];
+        if (r->lens) r->lens[s] = n;
+        if (r->sum_logprob) r->sum_logprob[s] = sums[s];
+        if (r->avg_logprob) r->avg_logprob[s] = n > 0 ? (float)(sums[s] / n) : 0.f;
+        if (r->no_speech_prob) r->no_speech_prob[s] = nsp[s];
+        if (r->compression) r->compression[s] = w4j_compression_ratio(toks.data() + (size_t)s * a.max_tokens, n);
+    }
+    return 0;
+}
+
+static int decode_impl(w4j_ctx *c, const CallArgs &a, w4j_result *r) {
+    CUDA_TRY(cudaSetDevice(c->device));
+    TRY(check_ready(c));
+    TRY(validate_call(c, a));
+    const int mode = a.beam > 1 ? MODE_BEAM : a.temperature > 0.f ? MODE_SAMPLE : MODE_GREEDY;
+    c->cancel.store(0);
+    c->last_ms = 0;
+    c->last_steps = 0;
+    c->last_launches = 0;
+    if (a.max_tokens == 0) {  // the reference's loop body never runs: empty result
+        for (int s = 0; s < a.S; ++s) {
+            if (r->lens) r->lens[s] = 0;
+            if (r->sum_logprob) r->sum_logprob[s] = 0;
+            if (r->avg_logprob) r->avg_logprob[s] = 0;
+            if (r->compression) r->compression[s] = 0;
+            if (r->no_speech_prob) r->no_speech_prob[s] = 0;
+        }
+        return W4J_OK;
+    }
+    const CallLayout Ly = call_layout(c, a.S, a.n_prompt, a.n_sup);
+    TRY(prepare_call(c, a, Ly));
+    long long launches = 0;
+    TRY(run_prompt(c, a, Ly, mode, launches));
+    // steps 1 .. max_tokens-1 (both loops produce max_tokens decisions in total)
+    CUDA_TRY(cudaEventRecord(c->ev0, c->stream));
+    int steps = 0;
+    bool cancelled = false;
+    bool snapshot_pending = false;
+    for (int step = 1; step < a.max_tokens; ++step) {
+        if (c->cancel.load()) {
+            cancelled = true;
+            break;
+        }
+        const int parity = mode == MODE_BEAM ? (step - 1) & 1 : 0;
+        cudaGraphExec_t g = nullptr;
+        long long per = 0;
+        TRY(get_step_graph(c, a, Ly, mode, parity, &g, per));
+        CUDA_TRY(cudaGraphLaunch(g, c->stream));
+        launches += per;
+        ++steps;
+        // every 16 steps look at a done-flag snapshot taken 16 steps earlier (no stall)
+        if ((step & 15) == 0) {
+            if (snapshot_pending && cudaEventQuery(c->ev1) == cudaSuccess) {
+                bool all = true;
+                for (int s = 0; s < a.S; ++s) all &= c->h_done[s] != 0;
+                if (all) break;
+            }
+            CUDA_TRY(cudaMemcpyAsync(c->h_done, c->st.done, a.S * 4, cudaMemcpyDeviceToHost, c->stream));
+            CUDA_TRY(cudaEventRecord(c->ev1, c->stream));
+            snapshot_pending = true;
+        }
+    }
+    CUDA_TRY(cudaStreamSynchronize(c->stream));  // ev1 must not be re-recorded while pending
+    cudaEvent_t stop;
+    CUDA_TRY(cudaEventCreate(&stop));
+    CUDA_TRY(cudaEventRecord(stop, c->stream));
+    CUDA_TRY(cudaEventSynchronize(stop));
+    float ms = 0.f;
+    cudaEventElapsedTime(&ms, c->ev0, stop);
+    cudaEventDestroy(stop);
+    CUDA_TRY(launch_finalize(c->st, mode == MODE_BEAM, 0, c->stream));
+    ++launches;
+    TRY(read_results(c, a, r));
+    c->last_ms = ms;
+    c->last_steps = steps;
+    c->last_launches = launches;
+    if (cancelled) return set_err(W4J_ERR_CANCELLED, "decode cancelled");
+    return W4J_OK;
+}
+
+extern "C" int w4j_decode(w4j_ctx *c, const int32_t *slots, int S, const int32_t *prompts, int n_prompt, int32_t eot,
+                          int max_tokens, const int32_t *suppress, int n_sup, int32_t ns, float temperature,
+                          int32_t ts_begin, uint64_t seed, w4j_result *out) {
+    if (!c || !out) return set_err(W4J_ERR_ARG, "w4j_decode: null argument");
+    std::lock_guard<std::mutex> g(c->mu);
+    CallArgs a{slots, S, prompts, n_prompt, eot, max_tokens, suppress, n_sup, ns, temperature, ts_begin, seed, 1};
+    return decode_impl(c, a, out);
+}
+
+extern "C" int w4j_decode_beam(w4j_ctx *c, const int32_t *slots, int S, const int32_t *prompts, int n_prompt,
+                               int32_t eot, int max_tokens, const int32_t *suppress, int n_sup, int32_t ns,
+                               int32_t ts_begin, int beam, w4j_result *out) {
+    if (!c || !out) return set_err(W4J_ERR_ARG, "w4j_decode_beam: null argument");
+    if (beam < 1) return set_err(W4J_ERR_ARG, "beam size must be >= 1");
+    std::lock_guard<std::mutex> g(c->mu);
+    CallArgs a{slots, S, prompts, n_prompt, eot, max_tokens, suppress, n_sup, ns, 0.f, ts_begin, 0, beam};
+    return decode_impl(c, a, out);
+}
+
+// WhisperDecoder.java:435-440
+extern "C" int w4j_needs_fallback(float cr, float avg, float nsp) {
+    if (cr > 2.4f) return !(nsp > 0.6f && avg < -1.0f);
+    return avg < -1.0f && !(nsp > 0.6f);
+}
+
+// WhisperDecoder.java:628-647: tokens as little-endian 16-bit pairs, zlib (Deflater default level)
+extern "C" float w4j_compression_ratio(const int32_t *tokens, int n) {
+    if (!tokens || n <= 0) return 0.f;
+    std::vector<unsigned char> bytes((size_t)n * 2);
+    for (int i = 0; i < n; ++i) {
+        bytes[2 * i] = (unsigned char)(tokens[i] & 0xff);
+        bytes[2 * i + 1] = (unsigned char)((tokens[i] >> 8) & 0xff);
+    }
+    uLongf cap = compressBound((uLong)bytes.size());
+    std::vector<unsigned char> outb(cap);
+    if (compress2(outb.data(), &cap, bytes.data(), (uLong)bytes.size(), Z_DEFAULT_COMPRESSION) != Z_OK) return 0.f;
+    return (float)bytes.size() / (float)std::max<uLongf>(1, cap);
+}
+
+extern "C" int w4j_decode_with_fallback(w4j_ctx *c, const int32_t *slots, int S, const int32_t *prompts, int n_prompt,
+                                        int32_t eot, int max_tokens, const int32_t *suppress, int n_sup, int32_t ns,
+                                        int32_t ts_begin, int beam, uint64_t seed, w4j_result *out, float *out_temp) {
+    if (!c || !out || !slots || !prompts) return set_err(W4J_ERR_ARG, "w4j_decode_with_fallback: null argument");
+    if (S < 1) return set_err(W4J_ERR_ARG, "n_streams must be >= 1");
+    const float temps[] = {0.0f, 0.2f, 0.4f, 0.6f, 0.8f, 1.0f};
+    const int mt = std::max(max_tokens, 1);
+    std::vector<int> pending(S), best_set(S, 0), finished(S, 0);
+    for (int s = 0; s < S; ++s) pending[s] = s;
+    std::vector<int32_t> btok((size_t)S * mt), blen(S);
+    std::vector<double> bsum(S);
+    std::vector<float> bavg(S), bcr(S), bnsp(S), btemp(S);
+    for (float temp : temps) {
+        const int P = (int)pending.size();
+        if (P == 0) break;
+        std::vector<int32_t> sl(P), pr((size_t)P * n_prompt), tok((size_t)P * mt), len(P);
+        std::vector<double> sum(P);
+        std::vector<float> avg(P), cr(P), nsp(P);
+        for (int i = 0; i < P; ++i) {
+            sl[i] = slots[pending[i]];
+            memcpy(&pr[(size_t)i * n_prompt], prompts + (size_t)pending[i] * n_prompt, n_prompt * 4);
+        }
+        w4j_result r{tok.data(), len.data(), sum.data(), avg.data(), cr.data(), nsp.data()};
+        int rc = (beam > 1 && temp == 0.0f)
+                     ? w4j_decode_beam(c, sl.data(), P, pr.data(), n_prompt, eot, max_tokens, suppress, n_sup, ns,
+                                       ts_begin, beam, &r)
+                     : w4j_decode(c, sl.data(), P, pr.data(), n_prompt, eot, max_tokens, suppress, n_sup, ns, temp,
+                                  ts_begin, seed, &r);
+        if (rc < 0) return rc;
+        std::vector<int> next;
+        for (int i = 0; i < P; ++i) {
+            const int s = pending[i];
+            auto take = [&]() {
+                best_set[s] = 1;
+                memcpy(&btok[(size_t)s * mt], &tok[(size_t)i * mt], mt * 4);
+                blen[s] = len[i];
+                bsum[s] = sum[i];
+                bavg[s] = avg[i];
+                bcr[s] = cr[i];
+                bnsp[s] = nsp[i];
+                btemp[s] = temp;
+            };
+            if (!w4j_needs_fallback(cr[i], avg[i], nsp[i])) {
+                take();
+                continue;
+            }
+            if (!best_set[s] || avg[i] > bavg[s]) take();
+            if (temp == 0.0f && cr[i] <= 2.4f) continue;
+            if (temp > 0.0f && avg[i] < bavg[s] - 1.0f) continue;
+            next.push_back(s);
+        }
+        pending.swap(next);
+    }
+    for (int s = 0; s < S; ++s) {
+        if (out->tokens) memcpy(out->tokens + (size_t)s * max_tokens, &btok[(size_t)s * mt], std::max(0, blen[s]) * 4);
+        if (out->lens) out->lens[s] = blen[s];
+        if (out->sum_logprob) out->sum_logprob[s] = bsum[s];
+        if (out->avg_logprob) out->avg_logprob[s] = bavg[s];
+        if (out->compression) out->compression[s] = bcr[s];
+        if (out->no_speech_prob) out->no_speech_prob[s] = bnsp[s];
+        if (out_temp) out_temp[s] = btemp[s];
+    }
+    return W4J_OK;
+}
+
+extern "C" int w4j_cancel(w4j_ctx *c) {
+    if (!c) return set_err(W4J_ERR_ARG, "null context");
+    c->cancel.store(1);
+    return W4J_OK;
+}
+
+extern "C" int w4j_last_timing(w4j_ctx *c, double *ms, int *steps, long long *launches) {
+    if (!c) return set_err(W4J_ERR_ARG, "null context");
+    if (ms) *ms = c->last_ms;
+    if (steps) *steps = c->last_steps;
+    if (launches) *launches = c->last_launches;
+    return W4J_OK;
+}
+
+// ---------------------------------------------------------------------------
+// op-level entry points
+// ---------------------------------------------------------------------------
+extern "C" int w4j_op_linear(w4j_ctx *c, const float *x, int M, int K, const void *W, int w_type, int N,
+                             const float *bias, const float *ln_g, const float *ln_b, int epilogue, float *y,
+                             void *stream) {
+    if (!c || !x || !W || !y) return set_err(W4J_ERR_ARG, "w4j_op_linear: null argument");
+    if (M < 1 || K < 8 || N < 1 || K % 8) return set_err(W4J_ERR_ARG, "w4j_op_linear: bad shape");
+    if (w_type == W4J_GGML_Q8_0 && K % 32) return set_err(W4J_ERR_ARG, "Q8_0 needs K % 32 == 0");
+    if ((ln_g == nullptr) != (ln_b == nullptr)) return set_err(W4J_ERR_ARG, "LayerNorm needs both gamma and beta");
+    if (epilogue < 0 || epilogue > 2) return set_err(W4J_ERR_ARG, "epilogue must be 0, 1 or 2");
+    if ((size_t)std::min(M, 16) * K * 4 > 160 * 1024) return set_err(W4J_ERR_ARG, "K too large");
+    CUDA_TRY(cudaSetDevice(c->device));
+    GemvArgs g;
+    g.W.N = N;
+    g.W.K = K;
+    if (w_type == W4J_GGML_F16) {
+        g.W.type = WT_F16;
+        g.W.h = reinterpret_cast<const __half *>(W);
+    } else if (w_type == W4J_GGML_Q8_0) {
+        g.W.type = WT_Q8;
+        g.W.q = reinterpret_cast<const int8_t *>(W);
+        g.W.s = reinterpret_cast<const __half *>(g.W.q + (size_t)N * K);
+    } else {
+        return set_err(W4J_ERR_ARG, "w_type must be F16 (1) or Q8_0 (8)");
+    }
+    g.bias = bias;
+    g.M = M;
+    g.in_mode = ln_g ? IN_LN : IN_ACT;
+    g.act = x;
+    g.ln_g = ln_g;
+    g.ln_b = ln_b;
+    g.out_mode = epilogue == 0 ? OUT_STORE : epilogue == 1 ? OUT_GELU : OUT_RESIDUAL;
+    g.y = y;
+    g.gelu_lut = c->gelu_lut;
+    cudaStream_t s = stream ? reinterpret_cast<cudaStream_t>(stream) : 0;
+    CUDA_TRY(launch_gemv(g, s, false));
+    return W4J_OK;
+}
+
+extern "C" int w4j_q8_0_repack(const void *src, int N, int K, void *dst, void *stream) {
+    if (!src || !dst || N < 1 || K < 32 || K % 32) return set_err(W4J_ERR_ARG, "w4j_q8_0_repack: bad argument");
+    int8_t *q = reinterpret_cast<int8_t *>(dst);
+    __half *sc = reinterpret_cast<__half *>(q + (size_t)N * K);
+    CUDA_TRY(launch_q8_repack(src, N, K, q, sc, reinterpret_cast<cudaStream_t>(stream)));
+    return W4J_OK;
+}
+
+extern "C" int w4j_op_logits_argmax(w4j_ctx *c, const float *x, int M, const void *E, int V, const float *ln_g,
+                                    const float *ln_b, int32_t *out_token, double *out_logprob, void *stream) {
+    if (!c || !x || !E || !ln_g || !ln_b || !out_token || !out_logprob)
+        return set_err(W4J_ERR_ARG, "w4j_op_logits_argmax: null argument");
+    if (M < 1 || M > c->M_max) return set_err(W4J_ERR_ARG, "M %d out of [1, %d]", M, c->M_max);
+    if (V < 1 || V > c->V) return set_err(W4J_ERR_ARG, "V %d out of [1, %d]", V, c->V);
+    CUDA_TRY(cudaSetDevice(c->device));
+    std::lock_guard<std::mutex> g(c->mu);
+    LogitsArgs la;
+    la.E.type = WT_F16;
+    la.E.N = V;
+    la.E.K = c->d;
+    la.E.h = reinterpret_cast<const __half *>(E);
+    la.x = x;
+    la.ln_g = ln_g;
+    la.ln_b = ln_b;
+    la.M = M;
+    la.V = V;
+    la.d = c->d;
+    la.part = c->logit_part;
+    const int P = logits_parts_for(V, c->sm_count);
+    cudaStream_t s = stream ? reinterpret_cast<cudaStream_t>(stream) : 0;
+    CUDA_TRY(launch_logits(la, P, s, false));
+    CUDA_TRY(launch_argmax_merge(c->logit_part, P, M, out_token, out_logprob, s));
+    return W4J_OK;
+}

@@ -1,0 +1,216 @@
+// w4j_internal.cuh — shared device structures and helpers of libwhisper4j_cuda.
+//
+// Device data layout (all in HBM of the context's GPU):
+//   matrices      f16 [N][K] row-major (GGML native, the (out, in) layout of nn.Linear) or
+//                 Q8_0 split into int8 quants [N][K] followed by f16 scales [N][K/32]
+//   cross K / V   f16 [stream][layer][head][n_audio_ctx][64]   (head-major, one contiguous
+//                 n_audio_ctx x 128 B run per head)
+//   self  K / V   f16 [seq slot][layer][head][n_text_ctx][64]
+//   activations   f32 [M][d] residual stream x, q, attention output, [M][4d] MLP hidden
+#pragma once
+#include <cuda_fp16.h>
+#include <cuda_runtime.h>
+#include <stdint.h>
+
+namespace w4j {
+
+constexpr int kHeadDim = 64;
+constexpr int kMaxTopK = 16;                        // beam + 1 <= 16
+constexpr int kPartStride = 4 + 2 * kMaxTopK;       // floats per logits partial
+constexpr int kMaxRanges = 4;                       // masked id ranges per sequence
+constexpr int kGemvThreads = 256;
+constexpr int kAttnThreads = 128;
+constexpr int kAttnKeyTile = 128;
+
+enum WType : int { WT_F16 = 1, WT_Q8 = 8 };
+
+struct DMat {
+    int type = 0;   // WT_F16 / WT_Q8
+    int N = 0, K = 0;
+    const __half *h = nullptr;   // WT_F16: [N][K]
+    const int8_t *q = nullptr;   // WT_Q8: [N][K]
+    const __half *s = nullptr;   // WT_Q8: [N][K/32]
+};
+
+// ---------------------------------------------------------------------------
+// GEMV over M <= a few dozen rows: y[m][n] = sum_k act[m][k] * W[n][k] (+ epilogue)
+// ---------------------------------------------------------------------------
+enum InMode : int { IN_ACT = 0, IN_LN = 1, IN_EMBED_LN = 2 };
+enum OutMode : int { OUT_STORE = 0, OUT_GELU = 1, OUT_RESIDUAL = 2, OUT_QKV = 3 };
+
+struct GemvArgs {
+    DMat W;
+    const float *bias = nullptr;       // [N] or null
+    int M = 0;
+    int in_mode = IN_ACT;
+    const float *act = nullptr;        // [M][K] input (IN_ACT) or residual stream x (IN_LN)
+    const float *ln_g = nullptr, *ln_b = nullptr;
+    // IN_EMBED_LN: x[m] = E[tok[m]] + P[pos[m]] computed in the prologue; block 0 stores x
+    DMat E;
+    const float *pos_emb = nullptr;    // [n_text_ctx][d]
+    const int *tok = nullptr;          // [M]
+    const int *pos = nullptr;          // [M] positions (also the self-cache row written by OUT_QKV)
+    float *x_out = nullptr;            // [M][d]
+    // outputs
+    int out_mode = OUT_STORE;
+    float *y = nullptr;                // [M][N] (OUT_STORE/GELU/RESIDUAL) or q [M][d] (OUT_QKV)
+    const float *gelu_lut = nullptr;   // 65536 f32 entries indexed by f16 bits
+    // OUT_QKV: rows [d, 2d) -> K cache, [2d, 3d) -> V cache of layer `layer`
+    __half *kcache = nullptr, *vcache = nullptr;
+    const int *seq_slot = nullptr;     // [M] physical self-cache slot
+    int layer = 0, n_layer = 0, n_head = 0, n_ctx = 0;
+    const int *active = nullptr;       // [M] nonzero: row is live (null = all live)
+};
+
+// ---------------------------------------------------------------------------
+// single-query attention (self: rows gathered through the beam table; cross:
+// contiguous per stream), split over keys with a deterministic combine
+// ---------------------------------------------------------------------------
+struct AttnArgs {
+    const float *q = nullptr;          // [groups*nq][d] f32 queries
+    int d = 0, n_head = 0, n_layer = 0, layer = 0;
+    int cross = 0;                     // 0 self, 1 cross
+    const __half *kc = nullptr, *vc = nullptr;
+    int n_ctx = 0;                     // self rows per slot
+    int n_audio = 0;                   // cross rows per stream
+    const int *seq_slot = nullptr;     // self: [groups] own slot
+    const int *table = nullptr;        // self: [groups][n_ctx] slot per position (null: own slot)
+    const int *pos = nullptr;          // self: [groups] position of the newest row (kv len = pos+1)
+    const int *stream_of_group = nullptr;  // cross: [groups] stream index into the cross cache
+    int nq = 1;                        // queries per group (cross: beams of one stream)
+    int groups = 0;
+    int nsplit = 1;
+    float *part = nullptr;             // [groups*nq][n_head][nsplit][2 + 64]
+    unsigned *counters = nullptr;      // [groups][n_head], zero between uses
+    float *out = nullptr;              // [groups*nq][d]
+    const int *active = nullptr;       // [groups]
+};
+
+// ---------------------------------------------------------------------------
+// vocabulary logits with the logit processors and per-block partial results
+// ---------------------------------------------------------------------------
+struct MaskArgs {
+    const int *static_list = nullptr;  // suppress tokens, shared
+    int n_static = 0;
+    const int *dyn_list = nullptr;     // [M][dyn_stride] per-sequence masked ids
+    const int *dyn_count = nullptr;    // [M]
+    int dyn_stride = 0;
+    const int2 *ranges = nullptr;      // [M][kMaxRanges] masked [lo, hi)
+    const int *n_ranges = nullptr;     // [M]
+};
+
+struct LogitsArgs {
+    DMat E;                            // [V][d]
+    const float *x = nullptr;          // [M][d] residual stream
+    const float *ln_g = nullptr, *ln_b = nullptr;
+    int M = 0, V = 0, d = 0;
+    MaskArgs mask;
+    int use_mask = 0;
+    int topk = 0;                      // candidates kept per block (beam + 1), 0 = greedy
+    float *part = nullptr;             // [M][gridDim.x][kPartStride]
+    float *raw_out = nullptr;          // [M][V] pre-mask logits (forward) or null
+    float *masked_out = nullptr;       // [M][V] post-mask logits (sampling) or null
+    int ns_token = -1;                 // >= 0: also reduce unmasked stats and keep this id's logit
+    float *ns_part = nullptr;          // [M][gridDim.x][2] unmasked (max, sum)
+    float *ns_value = nullptr;         // [M]
+    const int *active = nullptr;       // [M]
+};
+
+// ---------------------------------------------------------------------------
+// decode state (device) and per-step selection
+// ---------------------------------------------------------------------------
+struct DecodeState {
+    int n_streams = 0, beam = 1, max_tokens = 0, n_prompt = 0, n_ctx = 0, V = 0, n_parts = 0;
+    int eot = 0, ts_begin = -1, ns_token = -1, n_suppress = 0;
+    float temperature = 0.f;
+    unsigned long long seed = 0;
+    int hs = 0;                        // stride of token histories (n_text_ctx + 1)
+    // per sequence (M = n_streams * beam), double-buffered by step parity where noted
+    int *tok_in = nullptr;             // [M] token fed at the next step
+    int *seq_slot = nullptr;           // [M]
+    int *seq_pos = nullptr;            // [M]
+    int *active = nullptr;             // [M]
+    int *table[2] = {nullptr, nullptr};    // [M][n_ctx]
+    int *hist[2] = {nullptr, nullptr};     // [M][hs]
+    int *hist_len[2] = {nullptr, nullptr}; // [M]
+    double *lp[2] = {nullptr, nullptr};    // [M] beam score / greedy sum of log-probs
+    int *dyn_list = nullptr;           // [M][dyn_stride]
+    int *dyn_count = nullptr;          // [M]
+    int dyn_stride = 0;
+    int2 *ranges = nullptr;            // [M][kMaxRanges]
+    int *n_ranges = nullptr;           // [M]
+    const int *suppress = nullptr;     // [n_suppress]
+    // per stream
+    int *done = nullptr;               // [S]
+    const int *stream_base = nullptr;  // [S] first physical self-cache slot of the stream
+    int *beam_par = nullptr;           // [S] parity of the buffers holding the live beams
+    float *nsp = nullptr;              // [S] no-speech probability
+    int *fin_n = nullptr;              // [S]
+    int *fin_tok = nullptr;            // [S][beam][hs]
+    int *fin_len = nullptr;            // [S][beam]
+    double *fin_lp = nullptr;          // [S][beam]
+    // outputs (finalize)
+    int *out_tok = nullptr;            // [S][max_tokens]
+    int *out_len = nullptr;            // [S]
+    double *out_sum = nullptr;         // [S]
+    int *err = nullptr;                // device error word (bounds failures), 0 = ok
+};
+
+// ---------------------------------------------------------------------------
+// PTX helpers
+// ---------------------------------------------------------------------------
+__device__ __forceinline__ void pdl_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
+__device__ __forceinline__ void pdl_trigger() { asm volatile("griddepcontrol.launch_dependents;" ::: "memory"); }
+
+// Bulk prefetch of a contiguous global range into L2 (no shared-memory destination).
+__device__ __forceinline__ void prefetch_l2(const void *p, unsigned bytes) {
+    asm volatile("cp.async.bulk.prefetch.L2.global [%0], %1;" ::"l"(p), "r"(bytes) : "memory");
+}
+
+__device__ __forceinline__ uint4 ld_nc_v4(const void *p) {
+    uint4 r;
+    asm volatile("ld.global.nc.L1::no_allocate.v4.u32 {%0,%1,%2,%3}, [%4];"
+                 : "=r"(r.x), "=r"(r.y), "=r"(r.z), "=r"(r.w)
+                 : "l"(p));
+    return r;
+}
+
+__device__ __forceinline__ float warp_sum(float v) {
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
+    return v;
+}
+__device__ __forceinline__ float warp_max(float v) {
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) v = fmaxf(v, __shfl_xor_sync(0xffffffffu, v, o));
+    return v;
+}
+
+// ---------------------------------------------------------------------------
+// host launchers (defined in the kernel .cu files)
+// ---------------------------------------------------------------------------
+cudaError_t launch_gemv(const GemvArgs &a, cudaStream_t s, bool pdl);
+cudaError_t launch_attn(const AttnArgs &a, cudaStream_t s, bool pdl);
+cudaError_t launch_logits(const LogitsArgs &a, int n_parts, cudaStream_t s, bool pdl);
+int logits_parts_for(int V, int sm_count);
+size_t logits_smem_bytes(int M, int V, int d, int n_parts);
+
+// select / bookkeeping kernels
+enum SelectMode : int { SEL_GREEDY = 0, SEL_SAMPLE = 1, SEL_BEAM_INIT = 2, SEL_BEAM = 3 };
+cudaError_t launch_select(const DecodeState &st, int mode, int parity, const float *part, int n_parts,
+                          float *masked_logits, int step, cudaStream_t s, bool pdl);
+cudaError_t launch_nsp(const DecodeState &st, const float *ns_part, int n_parts, const float *ns_value,
+                       cudaStream_t s, bool pdl);
+cudaError_t launch_init_masks(const DecodeState &st, int beam_mode, cudaStream_t s);
+cudaError_t launch_finalize(const DecodeState &st, int beam_mode, int parity, cudaStream_t s);
+cudaError_t launch_argmax_merge(const float *part, int n_parts, int M, int32_t *tok, double *lp, cudaStream_t s);
+
+// prefill: out_k/out_v (f16 head-major) = xa . Wk^T, xa . Wv^T + bv
+cudaError_t launch_cross_kv(const float *xa, int A, int d, const DMat &wk, const DMat &wv, const float *bk,
+                            const float *bv, __half *kout, __half *vout, int n_head, cudaStream_t s);
+
+cudaError_t launch_q8_repack(const void *src, int N, int K, int8_t *q, __half *scales, cudaStream_t s);
+cudaError_t gemv_prepare();
+cudaError_t launch_f32_to_f16(const float *src, __half *dst, size_t n, cudaStream_t s);
+
+}  // namespace w4j
