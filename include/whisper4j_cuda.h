@@ -146,8 +146,10 @@ float w4j_compression_ratio(const int32_t *tokens, int n);                      
 int w4j_needs_fallback(float compression_ratio, float avg_logprob, float no_speech);  /* :435-440 */
 
 /*
- * Timing of the last decode call on this context: device milliseconds of the
- * step loop (prefill excluded) and number of steps, plus kernels launched.
+ * Timing of the last decode call on this context: device milliseconds from the
+ * first prompt kernel to the end of the result gather (the cross K/V projection
+ * of w4j_set_encoder_output excluded), the number of graph-replayed steps after
+ * the prompt, and the number of kernels launched.
  */
 int w4j_last_timing(w4j_ctx *ctx, double *loop_ms, int *steps, long long *kernel_launches);
 

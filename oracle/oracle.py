@@ -40,6 +40,7 @@ def lib():
             L = ctypes.CDLL(_LIB_PATH)
             P, I, F, D = ctypes.c_void_p, ctypes.c_int, ctypes.c_float, ctypes.c_double
             L.orc_last_error.restype = ctypes.c_char_p
+            L.orc_last_loop_seconds.restype = ctypes.c_double
             L.orc_model_new.restype = P
             L.orc_model_new.argtypes = [ctypes.POINTER(_Dims)]
             L.orc_model_free.argtypes = [P]
@@ -202,7 +203,7 @@ class OracleModel:
                                 len(suppress), no_speech, temperature, ts_begin, seed, _p(toks), ctypes.byref(n),
                                 ctypes.byref(s), ctypes.byref(a), ctypes.byref(ns), max_steps))
         return dict(tokens=toks[:n.value].tolist(), sum_logprob=s.value, avg_logprob=a.value,
-                    no_speech_prob=ns.value)
+                    no_speech_prob=ns.value, loop_seconds=lib().orc_last_loop_seconds())
 
     def decode_beam(self, xa, prompt, eot, max_tokens, suppress=(), no_speech=-1, ts_begin=-1, beam=5,
                     max_steps=0):
@@ -216,7 +217,7 @@ class OracleModel:
                                      len(suppress), no_speech, ts_begin, beam, _p(toks), ctypes.byref(n),
                                      ctypes.byref(s), ctypes.byref(a), ctypes.byref(ns), max_steps))
         return dict(tokens=toks[:n.value].tolist(), sum_logprob=s.value, avg_logprob=a.value,
-                    no_speech_prob=ns.value)
+                    no_speech_prob=ns.value, loop_seconds=lib().orc_last_loop_seconds())
 
 
 class OracleCache:

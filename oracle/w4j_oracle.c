@@ -44,6 +44,16 @@
 /* ------------------------------------------------------------------------ */
 
 static _Thread_local char g_err[512];
+static _Thread_local double g_loop_seconds; /* wall time of the token loop after the first step */
+
+#include <time.h>
+static double now_seconds(void) {
+    struct timespec ts;
+    clock_gettime(CLOCK_MONOTONIC, &ts);
+    return (double)ts.tv_sec + 1e-9 * (double)ts.tv_nsec;
+}
+
+double orc_last_loop_seconds(void) { return g_loop_seconds; }
 
 static int fail(const char *msg, const char *detail) {
     snprintf(g_err, sizeof g_err, "%s%s%s", msg, detail ? ": " : "", detail ? detail : "");
@@ -747,7 +757,10 @@ int orc_decode(const orc_model *m, const float *xa, int n_audio_ctx, const int *
     uint64_t rng = seed;
     int steps = max_tokens;
     if (max_steps > 0 && max_steps < steps) steps = max_steps;
+    double t_loop = 0;
+    g_loop_seconds = 0;
     for (int step = 0; step < steps; step++) {
+        if (step == 1) t_loop = now_seconds();
         if (orc_forward(m, cur, n_cur, xa, n_audio_ctx, cache, logits)) { rc = -1; break; }
         memcpy(last, logits + (size_t)(n_cur - 1) * V, (size_t)V * sizeof(float));
         if (step == 0) {
@@ -765,6 +778,7 @@ int orc_decode(const orc_model *m, const float *xa, int n_audio_ctx, const int *
         cur = &tok_buf;
         n_cur = 1;
     }
+    if (t_loop > 0) g_loop_seconds = now_seconds() - t_loop;
     if (rc == 0) {
         memcpy(out_tokens, generated, (size_t)gen_count * sizeof(int));
         *out_len = gen_count;
@@ -854,6 +868,8 @@ int orc_decode_beam(const orc_model *m, const float *xa, int n_audio_ctx, const 
 
     int steps = max_tokens;
     if (max_steps > 0 && max_steps < steps) steps = max_steps;
+    g_loop_seconds = 0;
+    const double t_loop = now_seconds();
     for (int step = 1; step < steps; step++) { /* :269-367 */
         int nc = 0;
         for (int b = 0; b < beam; b++) {
@@ -924,6 +940,7 @@ int orc_decode_beam(const orc_model *m, const float *xa, int n_audio_ctx, const 
         { double *t = blp; blp = nblp; nblp = t; }
     }
 
+    g_loop_seconds = now_seconds() - t_loop;
     if (fin_n < beam) { /* :370-377 */
         for (int b = 0; b < beam && fin_n < beam; b++) {
             fin_tok[fin_n] = (int *)malloc((size_t)blen[b] * sizeof(int) + 1);

@@ -21,6 +21,9 @@ typedef struct orc_model orc_model;
 typedef struct orc_cache orc_cache;
 
 const char *orc_last_error(void);
+/* Wall seconds of the last decode's token loop after its first step (prompt and cross K/V
+ * projection excluded), on the calling thread. */
+double orc_last_loop_seconds(void);
 
 orc_model *orc_model_new(const orc_dims *d);
 void orc_model_free(orc_model *m);

@@ -10,17 +10,21 @@
 // logit processors (WhisperDecoder.java:450-564) and the reductions that argmax / log-softmax /
 // top-k need (:566-574, :397-431, :614-626).
 //
-// Design (HBM-bound, M small): weights stay in their GGML (N, K) row layout; a warp owns R
-// rows and its lanes walk K in 16-byte chunks (8 f16 or 16 int8), loading each weight byte
-// exactly once with 128-bit non-allocating loads and dequantising in registers.  The M
-// activation rows sit in shared memory as f32 (LayerNorm applied on the way in), every
-// weight chunk is reused for all M rows, and the R x M partial sums are reduced across the
-// warp with a butterfly that ends with one finished sum per lane.  Under programmatic
-// dependent launch each block first asks L2 to prefetch its weight rows (bulk prefetch),
-// then waits for the previous kernel; the weight stream therefore overlaps the tail of the
-// kernel before it.
+// Design (HBM-bound, M small).  Weights stay in their GGML (N, K) row layout.  Each block
+// owns a contiguous range of rows, so its weight bytes are one contiguous run that a single
+// thread moves into shared memory with TMA bulk copies (cp.async.bulk + mbarrier).  Under
+// programmatic dependent launch those copies are issued *before* griddepcontrol.wait: the
+// weight stream of kernel i+1 overlaps kernel i, and after the wait only the activations
+// (a few KB from L2) stand between the previous kernel and this one's result.  A warp owns R
+// rows at a time and its lanes walk K in 16-byte chunks (8 f16 or 16 int8), dequantising in
+// registers; the M activation rows sit in shared memory as f32 (LayerNorm applied on the way
+// in), every weight chunk is reused for all M rows, and the R x M partial sums are reduced
+// across the warp with a butterfly that leaves one finished sum per lane.  The vocabulary
+// projection streams its rows through a ring of shared-memory stages, the first stages again
+// issued before the wait.
 #include <float.h>
 
+#include "logits_epilogue.cuh"
 #include "w4j_internal.cuh"
 
 namespace w4j {
@@ -65,6 +69,13 @@ __device__ __forceinline__ bool reduced_owner(int lane) {
     return (lane & ((32 / NV) - 1)) == 0;
 }
 
+// Accumulators are laid out acc[r * P2 + mm] with P2 the power of two >= MT, so the
+// butterfly reduction works on a power-of-two count; entries mm >= MT stay zero.
+template <int MT>
+struct P2 {
+    static constexpr int v = MT <= 1 ? 1 : MT <= 2 ? 2 : MT <= 4 ? 4 : MT <= 8 ? 8 : 16;
+};
+
 __device__ __forceinline__ float row_value(const DMat &m, int row, int k) {
     if (m.type == WT_F16) return __half2float(m.h[(size_t)row * m.K + k]);
     const float s = __half2float(m.s[(size_t)row * (m.K / 32) + k / 32]);
@@ -72,35 +83,70 @@ __device__ __forceinline__ float row_value(const DMat &m, int row, int k) {
 }
 
 // Fill act_s[mm][k] (mm < MT) for rows m0.. of the pass: plain copy, LayerNorm of x, or
-// token + positional embedding then LayerNorm.  8 warps, one row per warp at a time.
+// token + positional embedding then LayerNorm.  All threads cooperate on the loads with
+// eight independent 16-byte loads in flight each (one L2 round trip for a few KB), then
+// one warp per row normalises in shared memory.
 template <int MT>
-__device__ void load_activations(const GemvArgs &a, int m0, int K, float *act_s, int warp, int lane) {
-    for (int mm = warp; mm < MT; mm += kGemvThreads / 32) {
-        const int m = m0 + mm;
-        float *dst = act_s + (size_t)mm * K;
-        if (m >= a.M) {
-            for (int k = lane; k < K; k += 32) dst[k] = 0.f;
-            continue;
-        }
-        if (a.in_mode == IN_ACT) {
-            const float4 *src = reinterpret_cast<const float4 *>(a.act + (size_t)m * K);
-            for (int k4 = lane; k4 < K / 4; k4 += 32) reinterpret_cast<float4 *>(dst)[k4] = src[k4];
-            continue;
-        }
-        // residual stream row -> shared (embedding first when asked)
-        if (a.in_mode == IN_EMBED_LN) {
-            const int tok = a.tok[m];
-            const int p = a.pos[m];
-            for (int k = lane; k < K; k += 32) {
-                const float v = row_value(a.E, tok, k) + a.pos_emb[(size_t)p * K + k];
-                dst[k] = v;
-                if (blockIdx.x == 0 && a.x_out) a.x_out[(size_t)m * K + k] = v;
+__device__ void load_activations(const GemvArgs &a, int m0, int K, float *act_s, const float *ln_s, int warp,
+                                 int lane) {
+    const int K4 = K / 4;
+    const int total = MT * K4;
+    if (a.in_mode == IN_EMBED_LN) {
+        const bool f16 = a.E.type == WT_F16;
+        for (int i0 = threadIdx.x; i0 < total; i0 += kGemvThreads * 8) {
+            float4 e[8], p[8];
+#pragma unroll
+            for (int j = 0; j < 8; ++j) {
+                const int i = i0 + kGemvThreads * j;
+                const int mm = i / K4, k = (i - mm * K4) * 4;
+                const int m = m0 + mm;
+                e[j] = p[j] = make_float4(0.f, 0.f, 0.f, 0.f);
+                if (i < total && m < a.M) {
+                    const int tok = a.tok[m], pos = a.pos[m];
+                    p[j] = *reinterpret_cast<const float4 *>(a.pos_emb + (size_t)pos * K + k);
+                    if (f16) {
+                        const uint2 u = *reinterpret_cast<const uint2 *>(a.E.h + (size_t)tok * K + k);
+                        const float2 lo = __half22float2(*reinterpret_cast<const __half2 *>(&u.x));
+                        const float2 hi = __half22float2(*reinterpret_cast<const __half2 *>(&u.y));
+                        e[j] = make_float4(lo.x, lo.y, hi.x, hi.y);
+                    } else {
+                        const float sc = __half2float(a.E.s[(size_t)tok * (K / 32) + k / 32]);
+                        const char4 q = *reinterpret_cast<const char4 *>(a.E.q + (size_t)tok * K + k);
+                        e[j] = make_float4(q.x * sc, q.y * sc, q.z * sc, q.w * sc);
+                    }
+                }
             }
-        } else {
-            const float *src = a.act + (size_t)m * K;
-            for (int k = lane; k < K; k += 32) dst[k] = src[k];
+#pragma unroll
+            for (int j = 0; j < 8; ++j) {
+                const int i = i0 + kGemvThreads * j;
+                if (i >= total) continue;
+                const float4 v = make_float4(e[j].x + p[j].x, e[j].y + p[j].y, e[j].z + p[j].z, e[j].w + p[j].w);
+                reinterpret_cast<float4 *>(act_s)[i] = v;
+                const int mm = i / K4, m = m0 + mm;
+                if (blockIdx.x == 0 && a.x_out && m < a.M)
+                    reinterpret_cast<float4 *>(a.x_out)[(size_t)m * K4 + (i - mm * K4)] = v;
+            }
         }
-        __syncwarp();
+    } else {
+        for (int i0 = threadIdx.x; i0 < total; i0 += kGemvThreads * 8) {
+            float4 v[8];
+#pragma unroll
+            for (int j = 0; j < 8; ++j) {
+                const int i = i0 + kGemvThreads * j;
+                const int mm = i / K4, m = m0 + mm;
+                v[j] = (i < total && m < a.M) ? reinterpret_cast<const float4 *>(a.act)[(size_t)m * K4 + (i - mm * K4)]
+                                              : make_float4(0.f, 0.f, 0.f, 0.f);
+            }
+#pragma unroll
+            for (int j = 0; j < 8; ++j)
+                if (i0 + kGemvThreads * j < total) reinterpret_cast<float4 *>(act_s)[i0 + kGemvThreads * j] = v[j];
+        }
+    }
+    if (a.in_mode == IN_ACT) return;
+    __syncthreads();
+    for (int mm = warp; mm < MT; mm += kGemvThreads / 32) {
+        if (m0 + mm >= a.M) continue;
+        float *dst = act_s + (size_t)mm * K;
         // Tensor.layerNorm (Tensor.java:592-619): two-pass mean / variance, eps 1e-5,
         // invStd = 1 / sqrt(var / n + eps), y = (x - mean) * invStd * g + b.
         float s = 0.f;
@@ -114,19 +160,28 @@ __device__ void load_activations(const GemvArgs &a, int m0, int K, float *act_s,
         const float var = warp_sum(v2);
         const float inv_std = 1.0f / sqrtf(var / (float)K + 1e-5f);
         __syncwarp();
-        for (int k = lane; k < K; k += 32) dst[k] = (dst[k] - mean) * inv_std * a.ln_g[k] + a.ln_b[k];
+        for (int k = lane; k < K; k += 32) dst[k] = (dst[k] - mean) * inv_std * ln_s[k] + ln_s[K + k];
     }
 }
 
-// acc[r][mm] += W[row r, chunk c] . act[mm][chunk c]
-template <int MT, int R, int WT>
-struct Chunk {
-    static constexpr int CE = WT == WT_F16 ? 8 : 16;  // elements per 16-byte chunk
-};
+// gamma / beta of the LayerNorm into shared memory (constant: done before the grid wait)
+__device__ __forceinline__ void stage_ln(const float *g, const float *b, int K, float *ln_s) {
+    for (int i0 = threadIdx.x; i0 < 2 * K; i0 += kGemvThreads * 8) {
+        float v[8];
+#pragma unroll
+        for (int j = 0; j < 8; ++j) {
+            const int i = i0 + kGemvThreads * j;
+            v[j] = i < K ? g[i] : i < 2 * K ? b[i - K] : 0.f;
+        }
+#pragma unroll
+        for (int j = 0; j < 8; ++j)
+            if (i0 + kGemvThreads * j < 2 * K) ln_s[i0 + kGemvThreads * j] = v[j];
+    }
+}
 
 template <int MT, int R>
 __device__ __forceinline__ void fma_chunk_f16(const uint4 (&w)[R], const float *act_s, int K, int k0,
-                                              float (&acc)[R * MT]) {
+                                              float (&acc)[R * P2<MT>::v]) {
     float wf[R][8];
 #pragma unroll
     for (int r = 0; r < R; ++r) {
@@ -144,7 +199,7 @@ __device__ __forceinline__ void fma_chunk_f16(const uint4 (&w)[R], const float *
         const float4 a1 = *reinterpret_cast<const float4 *>(act_s + (size_t)mm * K + k0 + 4);
 #pragma unroll
         for (int r = 0; r < R; ++r) {
-            float t = acc[r * MT + mm];
+            float t = acc[r * P2<MT>::v + mm];
             t = fmaf(wf[r][0], a0.x, t);
             t = fmaf(wf[r][1], a0.y, t);
             t = fmaf(wf[r][2], a0.z, t);
@@ -153,14 +208,14 @@ __device__ __forceinline__ void fma_chunk_f16(const uint4 (&w)[R], const float *
             t = fmaf(wf[r][5], a1.y, t);
             t = fmaf(wf[r][6], a1.z, t);
             t = fmaf(wf[r][7], a1.w, t);
-            acc[r * MT + mm] = t;
+            acc[r * P2<MT>::v + mm] = t;
         }
     }
 }
 
 template <int MT, int R>
-__device__ __forceinline__ void fma_chunk_q8(const uint4 (&w)[R], const float (&sc)[R], const float *act_s,
-                                             int K, int k0, float (&acc)[R * MT]) {
+__device__ __forceinline__ void fma_chunk_q8(const uint4 (&w)[R], const float (&sc)[R], const float *act_s, int K,
+                                             int k0, float (&acc)[R * P2<MT>::v]) {
     float wf[R][16];
 #pragma unroll
     for (int r = 0; r < R; ++r) {
@@ -189,152 +244,136 @@ __device__ __forceinline__ void fma_chunk_q8(const uint4 (&w)[R], const float (&
             }
         }
 #pragma unroll
-        for (int r = 0; r < R; ++r) acc[r * MT + mm] = fmaf(part[r], sc[r], acc[r * MT + mm]);
+        for (int r = 0; r < R; ++r) acc[r * P2<MT>::v + mm] = fmaf(part[r], sc[r], acc[r * P2<MT>::v + mm]);
     }
 }
 
-// Dot products of rows [row0, row0+R) with the MT activation rows; result reduced over the warp.
+// Dot products of R rows staged in shared memory (row stride `row_bytes`; Q8 scales in
+// `sc_s` with K/32 per row, or read from global when sc_s is null) with the MT activation rows.
 template <int MT, int R, int WT>
-__device__ __forceinline__ void warp_rows(const DMat &W, int row0, const float *act_s, float (&acc)[R * MT],
-                                          int lane) {
+__device__ __forceinline__ void smem_rows(const unsigned char *w_s, int row_bytes, int nrows, const __half *sc_s,
+                                          const __half *sc_g, int K, const float *act_s,
+                                          float (&acc)[R * P2<MT>::v], int lane) {
     constexpr int CE = WT == WT_F16 ? 8 : 16;
-    const int K = W.K;
     const int nchunk = K / CE;
 #pragma unroll
-    for (int i = 0; i < R * MT; ++i) acc[i] = 0.f;
-    bool ok[R];
+    for (int i = 0; i < R * P2<MT>::v; ++i) acc[i] = 0.f;
+    for (int c = lane; c < nchunk; c += 32) {
+        uint4 w[R];
+        float sc[R];
 #pragma unroll
-    for (int r = 0; r < R; ++r) ok[r] = row0 + r < W.N;
-    constexpr int U = (R * 2 >= 8) ? 2 : 4;  // chunks per batch: keep ~8 loads in flight per lane
-    for (int c0 = lane; c0 < nchunk; c0 += 32 * U) {
-        uint4 w[U][R];
-        float sc[U][R];
-#pragma unroll
-        for (int u = 0; u < U; ++u) {
-            const int c = c0 + 32 * u;
-#pragma unroll
-            for (int r = 0; r < R; ++r) {
-                if (ok[r] && c < nchunk) {
-                    if (WT == WT_F16) {
-                        w[u][r] = ld_nc_v4(W.h + (size_t)(row0 + r) * K + (size_t)c * CE);
-                        sc[u][r] = 0.f;
-                    } else {
-                        w[u][r] = ld_nc_v4(W.q + (size_t)(row0 + r) * K + (size_t)c * CE);
-                        sc[u][r] = __half2float(W.s[(size_t)(row0 + r) * (K / 32) + (c * CE) / 32]);
-                    }
-                } else {
-                    w[u][r] = make_uint4(0, 0, 0, 0);
-                    sc[u][r] = 0.f;
-                }
-            }
-        }
-#pragma unroll
-        for (int u = 0; u < U; ++u) {
-            const int c = c0 + 32 * u;
-            if (c < nchunk) {
-                if (WT == WT_F16)
-                    fma_chunk_f16<MT, R>(w[u], act_s, K, c * CE, acc);
+        for (int r = 0; r < R; ++r) {
+            if (r < nrows) {
+                w[r] = *reinterpret_cast<const uint4 *>(w_s + (size_t)r * row_bytes + (size_t)c * 16);
+                if (WT == WT_Q8)
+                    sc[r] = __half2float(sc_s ? sc_s[(size_t)r * (K / 32) + (c * CE) / 32]
+                                              : sc_g[(size_t)r * (K / 32) + (c * CE) / 32]);
                 else
-                    fma_chunk_q8<MT, R>(w[u], sc[u], act_s, K, c * CE, acc);
+                    sc[r] = 0.f;
+            } else {
+                w[r] = make_uint4(0, 0, 0, 0);
+                sc[r] = 0.f;
             }
         }
+        if (WT == WT_F16)
+            fma_chunk_f16<MT, R>(w, act_s, K, c * CE, acc);
+        else
+            fma_chunk_q8<MT, R>(w, sc, act_s, K, c * CE, acc);
     }
 }
 
-__device__ __forceinline__ void prefetch_rows(const DMat &W, int row0, int rows) {
-    if (row0 >= W.N) return;
-    rows = min(rows, W.N - row0);
-    if (W.type == WT_F16) {
-        prefetch_l2(W.h + (size_t)row0 * W.K, (unsigned)((size_t)rows * W.K * 2));
-    } else {
-        prefetch_l2(W.q + (size_t)row0 * W.K, (unsigned)((size_t)rows * W.K));
-        const size_t sb = (size_t)rows * (W.K / 32) * 2;
-        if (sb % 16 == 0 && (((size_t)row0 * (W.K / 32) * 2) % 16) == 0)
-            prefetch_l2(W.s + (size_t)row0 * (W.K / 32), (unsigned)sb);
-    }
+__device__ __forceinline__ void drain(uint64_t *bar, unsigned parity) {
+    // a wait that timed out: give the copy in flight a second bounded chance to land
+    for (long long it = 0; it < (1ll << 22); ++it)
+        if (mbar_test(bar, parity)) return;
 }
 
 // ---------------------------------------------------------------------------
-// GEMV kernel
+// GEMV kernel: block = rows [r0, r0 + rows_per_block) of W, staged whole in shared memory
 // ---------------------------------------------------------------------------
+struct GemvLaunch {
+    int rows_per_block;
+    size_t w_bytes, s_bytes;  // staging capacity for weights / Q8 scales (16-byte multiples)
+};
+
 template <int MT, int R, int WT>
-__global__ void __launch_bounds__(kGemvThreads) k_gemv(GemvArgs a) {
-    extern __shared__ float4 smem_f4[];
-    float *act_s = reinterpret_cast<float *>(smem_f4);
-    pdl_trigger();
-    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+__global__ void __launch_bounds__(kGemvThreads) k_gemv(GemvArgs a, GemvLaunch L) {
+    extern __shared__ __align__(128) unsigned char smem[];
     const int N = a.W.N, K = a.W.K;
-    const int n_groups = (N + R - 1) / R;
-    const int total_warps = gridDim.x * (kGemvThreads / 32);
-    const int gw = blockIdx.x * (kGemvThreads / 32) + warp;
-    // weights do not depend on the previous kernel: start their trip to L2 now
-    if (lane == 0)
-        for (int g = gw; g < n_groups; g += total_warps) prefetch_rows(a.W, g * R, R);
+    const int r0 = blockIdx.x * L.rows_per_block;
+    const int nr = min(N, r0 + L.rows_per_block) - r0;
+    unsigned char *w_s = smem;
+    __half *sc_s = reinterpret_cast<__half *>(smem + L.w_bytes);
+    float *act_s = reinterpret_cast<float *>(smem + L.w_bytes + L.s_bytes);
+    float *ln_s = act_s + (size_t)MT * K;  // [gamma | beta]
+    uint64_t *bar = reinterpret_cast<uint64_t *>(ln_s + 2 * (size_t)K);
+    const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+    const int row_bytes = WT == WT_F16 ? K * 2 : K;
+    // --- independent of the previous kernel: the weight rows ---
+    if (tid == 0) {
+        mbar_init(bar, 1);
+        fence_mbar_init();
+        const unsigned bytes = (unsigned)((size_t)nr * row_bytes);
+        mbar_expect_tx(bar, bytes);
+        const unsigned char *src = WT == WT_F16 ? reinterpret_cast<const unsigned char *>(a.W.h + (size_t)r0 * K)
+                                                : reinterpret_cast<const unsigned char *>(a.W.q + (size_t)r0 * K);
+        for (unsigned off = 0; off < bytes; off += 65536u) bulk_g2s(w_s + off, src + off, min(65536u, bytes - off), bar);
+    }
+    if (WT == WT_Q8)
+        for (int i = tid; i < nr * (K / 32); i += kGemvThreads) sc_s[i] = a.W.s[(size_t)r0 * (K / 32) + i];
+    if (a.in_mode != IN_ACT) stage_ln(a.ln_g, a.ln_b, K, ln_s);
+    pdl_trigger();
     pdl_wait();
 
+    bool ok = true;
     for (int m0 = 0; m0 < a.M; m0 += MT) {
-        load_activations<MT>(a, m0, K, act_s, warp, lane);
+        load_activations<MT>(a, m0, K, act_s, ln_s, warp, lane);
         __syncthreads();
-        for (int g = gw; g < n_groups; g += total_warps) {
-            float acc[R * MT];
-            warp_rows<MT, R, WT>(a.W, g * R, act_s, acc, lane);
-            const float v = warp_reduce_multi<R * MT>(acc, lane);
-            if (!reduced_owner<R * MT>(lane)) continue;
-            const int idx = reduced_index<R * MT>(lane);
-            const int r = idx / MT, mm = idx % MT;
-            const int n = g * R + r, m = m0 + mm;
-            if (n >= N || m >= a.M) continue;
-            if (a.active && !a.active[m]) continue;
-            const float val = v + (a.bias ? a.bias[n] : 0.f);
-            switch (a.out_mode) {
-                case OUT_STORE:
-                    a.y[(size_t)m * N + n] = val;
-                    break;
-                case OUT_GELU:  // Tensor.geluInPlace: table lookup at the f16 rounding of x
-                    a.y[(size_t)m * N + n] = a.gelu_lut[__half_as_ushort(__float2half_rn(val))];
-                    break;
-                case OUT_RESIDUAL:
-                    a.y[(size_t)m * N + n] += val;
-                    break;
-                case OUT_QKV: {
-                    const int dm = N / 3;
-                    const int part = n / dm, c = n - part * dm;
-                    if (part == 0) {
-                        a.y[(size_t)m * dm + c] = val;
-                    } else {
-                        const int head = c / kHeadDim, dd = c % kHeadDim;
-                        const size_t row = (((size_t)a.seq_slot[m] * a.n_layer + a.layer) * a.n_head + head) *
-                                               (size_t)a.n_ctx + (size_t)a.pos[m];
-                        __half *dst = part == 1 ? a.kcache : a.vcache;
-                        dst[row * kHeadDim + dd] = __float2half_rn(val);
+        if (m0 == 0) ok = mbar_wait(bar, 0, a.err);
+        if (ok) {
+            constexpr int PM = P2<MT>::v;
+            for (int g = warp; g * R < nr; g += kGemvThreads / 32) {
+                float acc[R * PM];
+                smem_rows<MT, R, WT>(w_s + (size_t)g * R * row_bytes, row_bytes, min(R, nr - g * R),
+                                     sc_s + (size_t)g * R * (K / 32), nullptr, K, act_s, acc, lane);
+                const float v = warp_reduce_multi<R * PM>(acc, lane);
+                if (!reduced_owner<R * PM>(lane)) continue;
+                const int idx = reduced_index<R * PM>(lane);
+                const int r = idx / PM, mm = idx % PM;
+                const int n = r0 + g * R + r, m = m0 + mm;
+                if (mm >= MT || g * R + r >= nr || m >= a.M) continue;
+                if (a.active && !a.active[m]) continue;
+                const float val = v + (a.bias ? a.bias[n] : 0.f);
+                switch (a.out_mode) {
+                    case OUT_STORE:
+                        a.y[(size_t)m * N + n] = val;
+                        break;
+                    case OUT_GELU:  // Tensor.geluInPlace: table lookup at the f16 rounding of x
+                        a.y[(size_t)m * N + n] = a.gelu_lut[__half_as_ushort(__float2half_rn(val))];
+                        break;
+                    case OUT_RESIDUAL:
+                        a.y[(size_t)m * N + n] += val;
+                        break;
+                    case OUT_QKV: {
+                        const int dm = N / 3;
+                        const int part = n / dm, c = n - part * dm;
+                        if (part == 0) {
+                            a.y[(size_t)m * dm + c] = val;
+                        } else {
+                            const int head = c / kHeadDim, dd = c % kHeadDim;
+                            const size_t row = (((size_t)a.seq_slot[m] * a.n_layer + a.layer) * a.n_head + head) *
+                                                   (size_t)a.n_ctx + (size_t)a.pos[m];
+                            __half *dst = part == 1 ? a.kcache : a.vcache;
+                            dst[row * kHeadDim + dd] = __float2half_rn(val);
+                        }
+                        break;
                     }
-                    break;
                 }
             }
         }
         __syncthreads();
     }
-}
-
-template <int MT, int R, int WT>
-static cudaError_t launch_gemv_t(const GemvArgs &a, cudaStream_t s, bool pdl, int sm_count) {
-    const int n_groups = (a.W.N + R - 1) / R;
-    int blocks = (n_groups + 7) / 8;
-    blocks = blocks < 4 * sm_count ? blocks : 4 * sm_count;
-    if (blocks < 1) blocks = 1;
-    const size_t smem = (size_t)MT * a.W.K * sizeof(float);
-    auto kern = k_gemv<MT, R, WT>;
-    cudaLaunchConfig_t cfg = {};
-    cfg.gridDim = dim3(blocks);
-    cfg.blockDim = dim3(kGemvThreads);
-    cfg.dynamicSmemBytes = smem;
-    cfg.stream = s;
-    cudaLaunchAttribute attr[1];
-    attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
-    attr[0].val.programmaticStreamSerializationAllowed = 1;
-    cfg.attrs = attr;
-    cfg.numAttrs = pdl ? 1 : 0;
-    return cudaLaunchKernelEx(&cfg, kern, a);
+    if (!ok) drain(bar, 0);
 }
 
 static int g_sm_count = 0;
@@ -348,24 +387,74 @@ static int sm_count() {
     return g_sm_count;
 }
 
-// Rows of activations kept in shared memory per pass: bounded by 96 KB of f32.
-static int pick_mt(int M, int K) {
-    const int cap = 24576 / K;  // MT * K * 4 <= 96 KB
-    int mt = 1;
-    while (mt < M && mt * 2 <= cap && mt < 16) mt *= 2;
-    return mt;
+constexpr size_t kSmemBudget = 220 * 1024;  // of the 227 KB a block may use
+
+static size_t align16(size_t x) { return (x + 15) & ~(size_t)15; }
+
+// Activation rows per pass (exact, up to 8) and the weight staging of one block.
+static void plan_gemv(int M, int N, int K, int type, int sms, int &mt, GemvLaunch &L, int &blocks) {
+    const size_t row_bytes = type == WT_F16 ? (size_t)K * 2 : (size_t)K;
+    const size_t srow = type == WT_F16 ? 0 : (size_t)(K / 32) * 2;
+    int rpb = (N + sms - 1) / sms;
+    // keep the weight slice within ~160 KB so activations fit beside it
+    const size_t wcap = 160 * 1024;
+    if ((size_t)rpb * (row_bytes + srow) > wcap) rpb = (int)(wcap / (row_bytes + srow));
+    if (rpb < 1) rpb = 1;
+    blocks = (N + rpb - 1) / rpb;
+    L.rows_per_block = rpb;
+    L.w_bytes = align16((size_t)rpb * row_bytes);
+    L.s_bytes = align16((size_t)rpb * srow);
+    const size_t left = kSmemBudget - L.w_bytes - L.s_bytes - 64 - 2 * (size_t)K * 4;
+    int cap = (int)(left / ((size_t)K * 4));
+    mt = M < 8 ? M : 8;
+    if (mt > cap) mt = cap;
+    if (mt < 1) mt = 1;
+    if (M > mt) {
+        const int passes = (M + mt - 1) / mt;
+        mt = (M + passes - 1) / passes;
+    }
+}
+
+template <int MT, int R, int WT>
+static cudaError_t launch_gemv_t(const GemvArgs &a, const GemvLaunch &L, int blocks, cudaStream_t s, bool pdl) {
+    const size_t smem = L.w_bytes + L.s_bytes + ((size_t)MT + 2) * a.W.K * sizeof(float) + 16;
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = dim3(blocks);
+    cfg.blockDim = dim3(kGemvThreads);
+    cfg.dynamicSmemBytes = smem;
+    cfg.stream = s;
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[0].val.programmaticStreamSerializationAllowed = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = pdl ? 1 : 0;
+    return cudaLaunchKernelEx(&cfg, k_gemv<MT, R, WT>, a, L);
+}
+
+template <int MT, int WT>
+static cudaError_t launch_gemv_r(const GemvArgs &a, const GemvLaunch &L, int blocks, cudaStream_t s, bool pdl) {
+    // few rows per block: one row per warp keeps all warps busy; many rows: 4 rows share
+    // each activation read
+    if (L.rows_per_block <= 8) return launch_gemv_t<MT, 1, WT>(a, L, blocks, s, pdl);
+    if constexpr (MT <= 4) return launch_gemv_t<MT, 4, WT>(a, L, blocks, s, pdl);
+    else
+    return launch_gemv_t<MT, 2, WT>(a, L, blocks, s, pdl);
 }
 
 template <int WT>
 static cudaError_t dispatch_gemv(const GemvArgs &a, cudaStream_t s, bool pdl) {
-    const int mt = pick_mt(a.M, a.W.K);
-    const int sms = sm_count();
+    int mt, blocks;
+    GemvLaunch L;
+    plan_gemv(a.M, a.W.N, a.W.K, WT, sm_count(), mt, L, blocks);
     switch (mt) {
-        case 1: return launch_gemv_t<1, 4, WT>(a, s, pdl, sms);
-        case 2: return launch_gemv_t<2, 4, WT>(a, s, pdl, sms);
-        case 4: return launch_gemv_t<4, 4, WT>(a, s, pdl, sms);
-        case 8: return launch_gemv_t<8, 2, WT>(a, s, pdl, sms);
-        default: return launch_gemv_t<16, 2, WT>(a, s, pdl, sms);
+        case 1: return launch_gemv_r<1, WT>(a, L, blocks, s, pdl);
+        case 2: return launch_gemv_r<2, WT>(a, L, blocks, s, pdl);
+        case 3: return launch_gemv_r<3, WT>(a, L, blocks, s, pdl);
+        case 4: return launch_gemv_r<4, WT>(a, L, blocks, s, pdl);
+        case 5: return launch_gemv_r<5, WT>(a, L, blocks, s, pdl);
+        case 6: return launch_gemv_r<6, WT>(a, L, blocks, s, pdl);
+        case 7: return launch_gemv_r<7, WT>(a, L, blocks, s, pdl);
+        default: return launch_gemv_r<8, WT>(a, L, blocks, s, pdl);
     }
 }
 
@@ -384,182 +473,132 @@ __device__ __forceinline__ bool better(float v1, int i1, float v2, int i2) {
     return v1 > v2 || (v1 == v2 && i1 < i2);
 }
 
-// LayerNorm of the residual rows into act_s (shared by all blocks, recomputed per block).
-template <int MT>
-__device__ void load_ln_rows(const LogitsArgs &a, int m0, float *act_s, int warp, int lane) {
-    GemvArgs g;
-    g.M = a.M;
-    g.in_mode = IN_LN;
-    g.act = a.x;
-    g.ln_g = a.ln_g;
-    g.ln_b = a.ln_b;
-    load_activations<MT>(g, m0, a.d, act_s, warp, lane);
-}
+struct LogitsLaunch {
+    int stage_rows;      // rows per ring stage (8 * R)
+    int n_stages;
+    size_t stage_bytes;  // 16-byte multiple
+    int ch;              // max rows per block (+1)
+};
 
 template <int MT, int R, int WT>
-__global__ void __launch_bounds__(kGemvThreads) k_logits(LogitsArgs a) {
-    extern __shared__ float4 smem_f4[];
-    float *act_s = reinterpret_cast<float *>(smem_f4);
+__global__ void __launch_bounds__(kGemvThreads) k_logits(LogitsArgs a, LogitsLaunch L) {
+    extern __shared__ __align__(128) unsigned char smem[];
     const int P = gridDim.x;
     const int lo = (int)(((long long)blockIdx.x * a.V) / P);
     const int hi = (int)(((long long)(blockIdx.x + 1) * a.V) / P);
-    const int CH = (a.V + P - 1) / P + 1;
-    float *tile = act_s + (size_t)MT * a.d;  // [MT][CH]
-    pdl_trigger();
-    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-    // the vocabulary matrix is larger than L2 for big models: warm only the head of this block's rows
-    if (threadIdx.x == 0) {
-        const int row_bytes = a.E.type == WT_F16 ? a.d * 2 : a.d;
-        const int rows = min(hi - lo, max(4, (32 * 1024 / row_bytes) & ~3));
-        prefetch_rows(a.E, lo, rows);
+    const int nrows = hi - lo;
+    const int d = a.d;
+    const int row_bytes = WT == WT_F16 ? d * 2 : d;
+    const int SR = L.stage_rows, NS = L.n_stages;
+    unsigned char *ring = smem;
+    float *act_s = reinterpret_cast<float *>(smem + (size_t)NS * L.stage_bytes);
+    float *ln_s = act_s + (size_t)MT * d;  // [gamma | beta]
+    float *tile = ln_s + 2 * (size_t)d;     // [MT][ch]
+    uint64_t *bars = reinterpret_cast<uint64_t *>((reinterpret_cast<uintptr_t>(tile + (size_t)MT * L.ch) + 15) &
+                                                  ~(uintptr_t)15);
+    const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+    const int n_tiles = (nrows + SR - 1) / SR;
+    const int passes = (a.M + MT - 1) / MT;
+    const int total = n_tiles * passes;
+    const unsigned char *base = WT == WT_F16 ? reinterpret_cast<const unsigned char *>(a.E.h + (size_t)lo * d)
+                                             : reinterpret_cast<const unsigned char *>(a.E.q + (size_t)lo * d);
+    auto issue = [&](int gidx) {  // thread 0: stream tile (gidx % n_tiles) into stage gidx % NS
+        const int t = gidx % n_tiles;
+        const int rows = min(SR, nrows - t * SR);
+        const unsigned bytes = (unsigned)rows * row_bytes;
+        uint64_t *b = bars + (gidx % NS);
+        mbar_expect_tx(b, bytes);
+        bulk_g2s(ring + (size_t)(gidx % NS) * L.stage_bytes, base + (size_t)t * SR * row_bytes, bytes, b);
+    };
+    // --- independent of the previous kernel: the first stages of this block's rows ---
+    if (tid == 0) {
+        for (int i = 0; i < NS; ++i) mbar_init(bars + i, 1);
+        fence_mbar_init();
+        for (int g = 0; g < NS && g < total; ++g) issue(g);
     }
+    stage_ln(a.ln_g, a.ln_b, d, ln_s);
+    pdl_trigger();
     pdl_wait();
 
-    for (int m0 = 0; m0 < a.M; m0 += MT) {
-        load_ln_rows<MT>(a, m0, act_s, warp, lane);
+    bool ok = true;
+    for (int pass = 0; pass < passes; ++pass) {
+        const int m0 = pass * MT;
+        GemvArgs g;
+        g.M = a.M;
+        g.in_mode = IN_LN;
+        g.act = a.x;
+        g.ln_g = a.ln_g;
+        g.ln_b = a.ln_b;
+        load_activations<MT>(g, m0, d, act_s, ln_s, warp, lane);
         __syncthreads();
-        const int n_groups = (hi - lo + R - 1) / R;
-        for (int g = warp; g < n_groups; g += kGemvThreads / 32) {
-            float acc[R * MT];
-            const int row0 = lo + g * R;
-            DMat E = a.E;
-            E.N = hi;  // rows beyond this block's range are left to the next block
-            warp_rows<MT, R, WT>(E, row0, act_s, acc, lane);
-            const float v = warp_reduce_multi<R * MT>(acc, lane);
-            if (reduced_owner<R * MT>(lane)) {
-                const int idx = reduced_index<R * MT>(lane);
-                const int r = idx / MT, mm = idx % MT;
-                const int n = row0 + r;
-                if (n < hi) {
-                    tile[(size_t)mm * CH + (n - lo)] = v;
-                    const int m = m0 + mm;
-                    if (a.raw_out && m < a.M) a.raw_out[(size_t)m * a.V + n] = v;
-                }
-            }
-        }
-        __syncthreads();
-        // one warp per sequence: processors, then the reductions
-        for (int mm = warp; mm < MT; mm += kGemvThreads / 32) {
-            const int m = m0 + mm;
-            if (m >= a.M) continue;
-            if (a.active && !a.active[m]) continue;
-            float *row = tile + (size_t)mm * CH;
-            const int n = hi - lo;
-            if (a.ns_token >= 0) {  // unmasked statistics of this row (no-speech probability)
-                float mx = -INFINITY;
-                for (int i = lane; i < n; i += 32) mx = fmaxf(mx, row[i]);
-                mx = warp_max(mx);
-                float sm = 0.f;
-                for (int i = lane; i < n; i += 32) sm += (mx == -INFINITY) ? 0.f : __expf(row[i] - mx);
-                sm = warp_sum(sm);
-                if (lane == 0) {
-                    float *np = a.ns_part + ((size_t)m * P + blockIdx.x) * 2;
-                    np[0] = mx;
-                    np[1] = sm;
-                }
-                if (a.ns_token >= lo && a.ns_token < hi && lane == 0) a.ns_value[m] = row[a.ns_token - lo];
-                __syncwarp();
-            }
-            if (a.use_mask) {
-                const MaskArgs &mk = a.mask;
-                for (int r = 0; r < mk.n_ranges[m]; ++r) {
-                    const int2 rg = mk.ranges[(size_t)m * kMaxRanges + r];
-                    const int b0 = max(rg.x, lo), b1 = min(rg.y, hi);
-                    for (int i = b0 + lane; i < b1; i += 32) row[i - lo] = -INFINITY;
-                }
-                for (int i = lane; i < mk.n_static; i += 32) {
-                    const int t = mk.static_list[i];
-                    if (t >= lo && t < hi) row[t - lo] = -INFINITY;
-                }
-                const int nd = mk.dyn_count[m];
-                for (int i = lane; i < nd; i += 32) {
-                    const int t = mk.dyn_list[(size_t)m * mk.dyn_stride + i];
-                    if (t >= lo && t < hi) row[t - lo] = -INFINITY;
-                }
-                __syncwarp();
-            }
-            if (a.masked_out)
-                for (int i = lane; i < n; i += 32) a.masked_out[(size_t)m * a.V + lo + i] = row[i];
-            // max + first argmax
-            float bv = -INFINITY;
-            int bi = INT_MAX;
-            for (int i = lane; i < n; i += 32)
-                if (better(row[i], lo + i, bv, bi)) {
-                    bv = row[i];
-                    bi = lo + i;
-                }
-#pragma unroll
-            for (int o = 16; o > 0; o >>= 1) {
-                const float ov = __shfl_xor_sync(0xffffffffu, bv, o);
-                const int oi = __shfl_xor_sync(0xffffffffu, bi, o);
-                if (better(ov, oi, bv, bi)) {
-                    bv = ov;
-                    bi = oi;
-                }
-            }
-            float sm = 0.f;
-            if (bv != -INFINITY)
-                for (int i = lane; i < n; i += 32) sm += __expf(row[i] - bv);
-            sm = warp_sum(sm);
-            float *pp = a.part + ((size_t)m * P + blockIdx.x) * kPartStride;
-            if (lane == 0) {
-                pp[0] = bv;
-                pp[1] = sm;
-                pp[2] = __int_as_float(bi == INT_MAX ? lo : bi);
-            }
-            // top-k candidates of this block (value desc, index asc); unfilled: (-inf, 0)
-            for (int k = 0; k < a.topk; ++k) {
-                float kv = -INFINITY;
-                int ki = INT_MAX;
-                for (int i = lane; i < n; i += 32)
-                    if (row[i] != -INFINITY && better(row[i], lo + i, kv, ki)) {
-                        kv = row[i];
-                        ki = lo + i;
-                    }
-#pragma unroll
-                for (int o = 16; o > 0; o >>= 1) {
-                    const float ov = __shfl_xor_sync(0xffffffffu, kv, o);
-                    const int oi = __shfl_xor_sync(0xffffffffu, ki, o);
-                    if (better(ov, oi, kv, ki)) {
-                        kv = ov;
-                        ki = oi;
+        for (int t = 0; t < n_tiles; ++t) {
+            const int gidx = pass * n_tiles + t;
+            if (ok) ok = mbar_wait(bars + (gidx % NS), (unsigned)((gidx / NS) & 1), a.err);
+            const int rows = min(SR, nrows - t * SR);
+            const unsigned char *st = ring + (size_t)(gidx % NS) * L.stage_bytes;
+            constexpr int PM = P2<MT>::v;
+            if (ok && warp * R < rows) {
+                float acc[R * PM];
+                const int rloc = warp * R;
+                smem_rows<MT, R, WT>(st + (size_t)rloc * row_bytes, row_bytes, min(R, rows - rloc), nullptr,
+                                     WT == WT_Q8 ? a.E.s + (size_t)(lo + t * SR + rloc) * (d / 32) : nullptr, d,
+                                     act_s, acc, lane);
+                const float v = warp_reduce_multi<R * PM>(acc, lane);
+                if (reduced_owner<R * PM>(lane)) {
+                    const int idx = reduced_index<R * PM>(lane);
+                    const int r = idx / PM, mm = idx % PM;
+                    const int local = t * SR + rloc + r;
+                    if (mm < MT && rloc + r < rows) {
+                        tile[(size_t)mm * L.ch + local] = v;
+                        const int m = m0 + mm;
+                        if (a.raw_out && m < a.M) a.raw_out[(size_t)m * a.V + lo + local] = v;
                     }
                 }
-                if (lane == 0) {
-                    pp[4 + k] = kv;
-                    pp[4 + kMaxTopK + k] = __int_as_float(ki == INT_MAX ? 0 : ki);
-                }
-                if (ki != INT_MAX && ki - lo >= 0 && ki - lo < n && lane == ((ki - lo) & 31))
-                    row[ki - lo] = -INFINITY;
-                __syncwarp();
             }
+            __syncthreads();  // stage consumed by every warp
+            if (tid == 0 && ok && gidx + NS < total) issue(gidx + NS);
         }
+        logits_rows_epilogue(a, tile, L.ch, MT, m0, lo, hi, ok);
         __syncthreads();
     }
+    if (!ok)
+        for (int i = 0; i < NS; ++i) drain(bars + i, 0), drain(bars + i, 1);
 }
 
 int logits_parts_for(int V, int sms) {
-    int p = 2 * sms;
+    int p = sms;
     if (p > V) p = V;
     return p < 1 ? 1 : p;
 }
 
-static int pick_mt_logits(int M, int d) {
-    int mt = pick_mt(M, d);
-    return mt > 8 ? 8 : mt;
+static void plan_logits(int M, int V, int d, int type, int P, int &mt, int &R, LogitsLaunch &L) {
+    const int row_bytes = type == WT_F16 ? d * 2 : d;
+    mt = M < 8 ? M : 8;
+    if (M > mt) {
+        const int passes = (M + mt - 1) / mt;
+        mt = (M + passes - 1) / passes;
+    }
+    R = mt <= 4 ? 4 : 2;
+    if (mt <= 2 && d <= 512) R = 4;
+    L.stage_rows = 8 * R;
+    L.stage_bytes = align16((size_t)L.stage_rows * row_bytes);
+    L.ch = (V + P - 1) / P + 1;
+    const size_t fixed = ((size_t)mt + 2) * d * 4 + (size_t)mt * L.ch * 4 + 16 * 8 + 64;
+    int ns = (int)((kSmemBudget - fixed) / L.stage_bytes);
+    L.n_stages = ns < 2 ? 2 : ns > 8 ? 8 : ns;
 }
 
 size_t logits_smem_bytes(int M, int V, int d, int P) {
-    const int mt = pick_mt_logits(M, d);
-    const int CH = (V + P - 1) / P + 1;
-    return ((size_t)mt * d + (size_t)mt * CH) * sizeof(float);
+    int mt, R;
+    LogitsLaunch L;
+    plan_logits(M, V, d, WT_F16, P, mt, R, L);
+    return (size_t)L.n_stages * L.stage_bytes + ((size_t)mt + 2) * d * 4 + (size_t)mt * L.ch * 4 + 8 * L.n_stages + 16;
 }
 
 template <int MT, int R, int WT>
-static cudaError_t launch_logits_t(const LogitsArgs &a, int P, cudaStream_t s, bool pdl) {
-    const int CH = (a.V + P - 1) / P + 1;
-    const size_t smem = ((size_t)MT * a.d + (size_t)MT * CH) * sizeof(float);
-    auto kern = k_logits<MT, R, WT>;
+static cudaError_t launch_logits_t(const LogitsArgs &a, const LogitsLaunch &L, int P, cudaStream_t s, bool pdl) {
+    const size_t smem =
+        (size_t)L.n_stages * L.stage_bytes + ((size_t)MT + 2) * a.d * 4 + (size_t)MT * L.ch * 4 + 8 * (size_t)L.n_stages + 16;
     cudaLaunchConfig_t cfg = {};
     cfg.gridDim = dim3(P);
     cfg.blockDim = dim3(kGemvThreads);
@@ -570,35 +609,56 @@ static cudaError_t launch_logits_t(const LogitsArgs &a, int P, cudaStream_t s, b
     attr[0].val.programmaticStreamSerializationAllowed = 1;
     cfg.attrs = attr;
     cfg.numAttrs = pdl ? 1 : 0;
-    return cudaLaunchKernelEx(&cfg, kern, a);
+    return cudaLaunchKernelEx(&cfg, k_logits<MT, R, WT>, a, L);
 }
 
 template <int WT>
 static cudaError_t dispatch_logits(const LogitsArgs &a, int P, cudaStream_t s, bool pdl) {
-    switch (pick_mt_logits(a.M, a.d)) {
-        case 1: return launch_logits_t<1, 4, WT>(a, P, s, pdl);
-        case 2: return launch_logits_t<2, 4, WT>(a, P, s, pdl);
-        case 4: return launch_logits_t<4, 4, WT>(a, P, s, pdl);
-        default: return launch_logits_t<8, 2, WT>(a, P, s, pdl);
+    int mt, R;
+    LogitsLaunch L;
+    plan_logits(a.M, a.V, a.d, WT, P, mt, R, L);
+    if (R == 4) {
+        switch (mt) {
+            case 1: return launch_logits_t<1, 4, WT>(a, L, P, s, pdl);
+            case 2: return launch_logits_t<2, 4, WT>(a, L, P, s, pdl);
+            case 3: return launch_logits_t<3, 4, WT>(a, L, P, s, pdl);
+            default: return launch_logits_t<4, 4, WT>(a, L, P, s, pdl);
+        }
+    }
+    switch (mt) {
+        case 5: return launch_logits_t<5, 2, WT>(a, L, P, s, pdl);
+        case 6: return launch_logits_t<6, 2, WT>(a, L, P, s, pdl);
+        case 7: return launch_logits_t<7, 2, WT>(a, L, P, s, pdl);
+        default: return launch_logits_t<8, 2, WT>(a, L, P, s, pdl);
     }
 }
 
 // Raise the dynamic shared-memory limit of every instantiation once (outside any graph capture).
 template <int WT>
 static cudaError_t prepare_wt() {
-    const int lim = 160 * 1024;
     cudaError_t e = cudaSuccess;
-#define W4J_SET(kern) \
-    if (e == cudaSuccess) e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, lim)
-    W4J_SET((k_gemv<1, 4, WT>));
-    W4J_SET((k_gemv<2, 4, WT>));
-    W4J_SET((k_gemv<4, 4, WT>));
-    W4J_SET((k_gemv<8, 2, WT>));
-    W4J_SET((k_gemv<16, 2, WT>));
-    W4J_SET((k_logits<1, 4, WT>));
-    W4J_SET((k_logits<2, 4, WT>));
-    W4J_SET((k_logits<4, 4, WT>));
-    W4J_SET((k_logits<8, 2, WT>));
+#define W4J_SET(...) \
+    if (e == cudaSuccess) e = allow_dynamic_smem(__VA_ARGS__)
+#define W4J_SET_MT(MT)                  \
+    W4J_SET(k_gemv<MT, 1, WT>);         \
+    W4J_SET(k_gemv<MT, (MT <= 4 ? 4 : 2), WT>)
+    W4J_SET_MT(1);
+    W4J_SET_MT(2);
+    W4J_SET_MT(3);
+    W4J_SET_MT(4);
+    W4J_SET_MT(5);
+    W4J_SET_MT(6);
+    W4J_SET_MT(7);
+    W4J_SET_MT(8);
+    W4J_SET(k_logits<1, 4, WT>);
+    W4J_SET(k_logits<2, 4, WT>);
+    W4J_SET(k_logits<3, 4, WT>);
+    W4J_SET(k_logits<4, 4, WT>);
+    W4J_SET(k_logits<5, 2, WT>);
+    W4J_SET(k_logits<6, 2, WT>);
+    W4J_SET(k_logits<7, 2, WT>);
+    W4J_SET(k_logits<8, 2, WT>);
+#undef W4J_SET_MT
 #undef W4J_SET
     return e;
 }

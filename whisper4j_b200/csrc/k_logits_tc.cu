@@ -1,0 +1,377 @@
+// k_logits_tc.cu — vocabulary logits on the 5th-generation tensor cores (tcgen05 + TMEM + TMA).
+//
+// Replaces the logits GEMV of WhisperDecoder.forwardWithAttn (nn/WhisperDecoder.java:102-103,
+// Tensor.matmulTransB M=1 path, tensor/Tensor.java:316-340): logits[m][v] = LN(x[m]) . E[v]
+// for the M live sequences (M <= 32), followed by the logit processors and block reductions
+// of logits_rows_epilogue (shared with the SIMT kernel in k_gemv.cu).
+//
+// Each block owns whole 128-row tiles of the token embedding E (V x d, f16, GGML row layout).
+//   * TMA (cp.async.bulk.tensor.2d, 128-byte swizzle) streams [128 rows x 64 k] tiles through a
+//     ring of shared-memory stages; the first stages are issued before griddepcontrol.wait, so
+//     they load while the previous kernel finishes.
+//   * The activations are LayerNorm-ed once per block straight into the MMA's B operand:
+//     [NU x d] f16, K-major with the same 128-byte swizzle (NU = M padded to 16 or 32).
+//   * One thread issues tcgen05.mma.kind::f16 (M=128, N=NU, K=16) into a double-buffered f32
+//     accumulator in tensor memory; tcgen05.commit releases ring stages and hands finished
+//     tiles to four epilogue warps, which read TMEM with tcgen05.ld into a shared tile.
+// Every wait is bounded; a time-out raises the device error word and the block drains.
+#include <cuda.h>
+#include <cudaTypedefs.h>
+
+#include "logits_epilogue.cuh"
+#include "w4j_internal.cuh"
+
+namespace w4j {
+
+// ---------------------------------------------------------------------------
+// tcgen05 / TMA helpers
+// ---------------------------------------------------------------------------
+__device__ __forceinline__ void tma_load_2d(void *dst, const CUtensorMap *map, int x, int y, uint64_t *bar) {
+    asm volatile(
+        "cp.async.bulk.tensor.2d.shared::cluster.global.tile.mbarrier::complete_tx::bytes [%0], [%1, {%2, %3}], [%4];" ::
+            "r"(smem_u32(dst)),
+        "l"(map), "r"(x), "r"(y), "r"(smem_u32(bar))
+        : "memory");
+}
+__device__ __forceinline__ void tmem_alloc(uint32_t *slot, uint32_t ncols) {
+    asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(smem_u32(slot)), "r"(ncols)
+                 : "memory");
+}
+__device__ __forceinline__ void tmem_relinquish() {
+    asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;" ::: "memory");
+}
+__device__ __forceinline__ void tmem_dealloc(uint32_t taddr, uint32_t ncols) {
+    asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(taddr), "r"(ncols) : "memory");
+}
+__device__ __forceinline__ void tc_fence_before() { asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory"); }
+__device__ __forceinline__ void tc_fence_after() { asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory"); }
+__device__ __forceinline__ void fence_proxy_async() { asm volatile("fence.proxy.async.shared::cta;" ::: "memory"); }
+__device__ __forceinline__ void umma_f16(uint32_t d_tmem, uint64_t adesc, uint64_t bdesc, uint32_t idesc,
+                                         uint32_t accumulate) {
+    asm volatile(
+        "{\n .reg .pred p;\n setp.ne.b32 p, %4, 0;\n tcgen05.mma.cta_group::1.kind::f16 [%0], %1, %2, %3, p;\n}" ::"r"(
+            d_tmem),
+        "l"(adesc), "l"(bdesc), "r"(idesc), "r"(accumulate)
+        : "memory");
+}
+__device__ __forceinline__ void umma_commit(uint64_t *bar) {
+    asm volatile("tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(smem_u32(bar))
+                 : "memory");
+}
+__device__ __forceinline__ void mbar_arrive(uint64_t *bar) {
+    asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(smem_u32(bar)) : "memory");
+}
+__device__ __forceinline__ void tmem_ld16(uint32_t taddr, float (&v)[16]) {
+    uint32_t r[16];
+    asm volatile(
+        "tcgen05.ld.sync.aligned.32x32b.x16.b32 {%0,%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15}, [%16];"
+        : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]), "=r"(r[7]), "=r"(r[8]),
+          "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]), "=r"(r[13]), "=r"(r[14]), "=r"(r[15])
+        : "r"(taddr)
+        : "memory");
+    asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
+#pragma unroll
+    for (int i = 0; i < 16; ++i) v[i] = __uint_as_float(r[i]);
+}
+
+// Shared-memory matrix descriptor of a K-major operand with the 128-byte swizzle: rows of
+// 128 B (64 f16 along K), 8-row atoms 1024 B apart (stride byte offset), version 1 (sm_100).
+__device__ __forceinline__ uint64_t sw128_desc(uint32_t saddr) {
+    uint64_t d = 0;
+    d |= (uint64_t)((saddr >> 4) & 0x3FFFu);  // start address >> 4
+    d |= (uint64_t)1 << 16;                   // leading byte offset (implied for swizzled K-major)
+    d |= (uint64_t)(1024 >> 4) << 32;         // stride byte offset: next 8-row atom
+    d |= (uint64_t)1 << 46;                   // descriptor version
+    d |= (uint64_t)2 << 61;                   // SWIZZLE_128B
+    return d;
+}
+
+// Instruction descriptor, kind::f16: f32 accumulator, f16 A and B, both K-major, M x N.
+__host__ __device__ constexpr uint32_t idesc_f16(int M, int N) {
+    return (1u << 4) | ((uint32_t)(N >> 3) << 17) | ((uint32_t)(M >> 4) << 24);
+}
+
+struct LogitsTcLaunch {
+    int tiles_total;  // ceil(V / 128)
+    int ch;           // max rows of a block (tiles per block * 128)
+    int n_stages;
+    unsigned b_off, tile_off, ln_off, bar_off;  // shared-memory layout (bytes)
+};
+
+constexpr int kTileRows = 128, kKB = 64, kStageBytes = kTileRows * kKB * 2;
+
+template <int NU>
+__global__ void __launch_bounds__(256, 1) k_logits_tc(LogitsArgs a, const __grid_constant__ CUtensorMap tmap,
+                                                       LogitsTcLaunch L) {
+    extern __shared__ __align__(1024) unsigned char smem_raw[];
+    // the 128-byte swizzle pattern is anchored on 1024-byte boundaries: align the base
+    unsigned char *smem = smem_raw + ((1024u - (smem_u32(smem_raw) & 1023u)) & 1023u);
+    const int P = gridDim.x;
+    const int t0 = (int)(((long long)blockIdx.x * L.tiles_total) / P);
+    const int t1 = (int)(((long long)(blockIdx.x + 1) * L.tiles_total) / P);
+    const int n_tiles = t1 - t0;
+    const int lo = min(a.V, t0 * kTileRows), hi = min(a.V, t1 * kTileRows);
+    const int d = a.d, KB = d / kKB, NS = L.n_stages;
+    const int total = n_tiles * KB;
+    unsigned char *ring = smem;
+    unsigned char *bop = smem + L.b_off;  // [KB][NU rows][128 B]
+    float *tile = reinterpret_cast<float *>(smem + L.tile_off);
+    float *ln_s = reinterpret_cast<float *>(smem + L.ln_off);
+    uint64_t *full = reinterpret_cast<uint64_t *>(smem + L.bar_off);
+    uint64_t *empty = full + NS;
+    uint64_t *accf = empty + NS;  // [2]
+    uint64_t *acce = accf + 2;    // [2]
+    uint32_t *tslot = reinterpret_cast<uint32_t *>(acce + 2);
+    volatile int *fail = reinterpret_cast<volatile int *>(tslot + 1);
+    const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+    constexpr uint32_t kCols = NU * 2 <= 32 ? 32 : 64;
+
+    // ---- independent of the previous kernel: barriers, TMEM, first weight stages, LN params ----
+    if (tid == 0) {
+        for (int i = 0; i < NS; ++i) {
+            mbar_init(full + i, 1);
+            mbar_init(empty + i, 1);
+        }
+        mbar_init(accf + 0, 1);
+        mbar_init(accf + 1, 1);
+        mbar_init(acce + 0, 4);
+        mbar_init(acce + 1, 4);
+        *fail = 0;
+        fence_mbar_init();
+        for (int i = 0; i < NS && i < total; ++i) {
+            mbar_expect_tx(full + i, kStageBytes);
+            tma_load_2d(ring + (size_t)i * kStageBytes, &tmap, (i % KB) * kKB, (t0 + i / KB) * kTileRows, full + i);
+        }
+    }
+    if (warp == 1) {
+        tmem_alloc(tslot, kCols);
+        tmem_relinquish();
+    }
+    for (int i = tid; i < 2 * d; i += blockDim.x) ln_s[i] = i < d ? a.ln_g[i] : a.ln_b[i - d];
+    pdl_trigger();
+    pdl_wait();
+    __syncthreads();  // ln_s is read across warps below
+
+    // ---- B operand: LayerNorm(x[m]) as f16, K-major, 128-byte swizzle; rows >= M are zero ----
+    for (int m = warp; m < NU; m += 8) {
+        const bool live = m < a.M;
+        constexpr int kMaxChunks = 1280 / 8 / 32;  // 16-byte chunks per lane for d <= 1280
+        float v[kMaxChunks][8];
+        const int nch = d / 8;  // chunks of 8 along K
+        float s = 0.f;
+#pragma unroll
+        for (int j = 0; j < kMaxChunks; ++j) {
+            const int c = lane + 32 * j;
+            if (live && c < nch) {
+                const float4 x0 = *reinterpret_cast<const float4 *>(a.x + (size_t)m * d + c * 8);
+                const float4 x1 = *reinterpret_cast<const float4 *>(a.x + (size_t)m * d + c * 8 + 4);
+                v[j][0] = x0.x; v[j][1] = x0.y; v[j][2] = x0.z; v[j][3] = x0.w;
+                v[j][4] = x1.x; v[j][5] = x1.y; v[j][6] = x1.z; v[j][7] = x1.w;
+            } else {
+#pragma unroll
+                for (int e = 0; e < 8; ++e) v[j][e] = 0.f;
+            }
+#pragma unroll
+            for (int e = 0; e < 8; ++e) s += v[j][e];
+        }
+        const float mean = warp_sum(s) / (float)d;
+        float s2 = 0.f;
+#pragma unroll
+        for (int j = 0; j < kMaxChunks; ++j)
+            if (lane + 32 * j < nch)
+#pragma unroll
+                for (int e = 0; e < 8; ++e) s2 += (v[j][e] - mean) * (v[j][e] - mean);
+        const float inv_std = 1.0f / sqrtf(warp_sum(s2) / (float)d + 1e-5f);
+#pragma unroll
+        for (int j = 0; j < kMaxChunks; ++j) {
+            const int c = lane + 32 * j;
+            if (c >= nch) continue;
+            uint32_t hpk[4];
+#pragma unroll
+            for (int e = 0; e < 8; e += 2) {
+                const int k = c * 8 + e;
+                const float y0 = live ? (v[j][e] - mean) * inv_std * ln_s[k] + ln_s[d + k] : 0.f;
+                const float y1 = live ? (v[j][e + 1] - mean) * inv_std * ln_s[k + 1] + ln_s[d + k + 1] : 0.f;
+                const __half2 h = __floats2half2_rn(y0, y1);
+                hpk[e / 2] = *reinterpret_cast<const uint32_t *>(&h);
+            }
+            const int kb = c / 8, cc = c % 8;
+            unsigned char *dst = bop + (size_t)kb * NU * 128 + (size_t)m * 128 + ((cc ^ (m & 7)) * 16);
+            *reinterpret_cast<uint4 *>(dst) = make_uint4(hpk[0], hpk[1], hpk[2], hpk[3]);
+        }
+    }
+    fence_proxy_async();  // generic-proxy writes of B visible to the tensor core
+    tc_fence_before();
+    __syncthreads();
+    tc_fence_after();
+    const uint32_t taddr = *tslot;
+    const uint32_t idesc = idesc_f16(kTileRows, NU);
+
+    if (warp == 0 && lane == 0) {
+        // ---- producer: stream the remaining tiles as stages free up ----
+        for (int i = NS; i < total && !*fail; ++i) {
+            const int st = i % NS, use = i / NS;
+            if (!mbar_wait(empty + st, (unsigned)((use - 1) & 1), a.err)) {
+                *fail = 1;
+                break;
+            }
+            mbar_expect_tx(full + st, kStageBytes);
+            tma_load_2d(ring + (size_t)st * kStageBytes, &tmap, (i % KB) * kKB, (t0 + i / KB) * kTileRows, full + st);
+        }
+    } else if (warp == 1 && lane == 0) {
+        // ---- MMA issuer ----
+        const uint32_t ring_a = smem_u32(ring), b_a = smem_u32(bop);
+        for (int lt = 0; lt < n_tiles && !*fail; ++lt) {
+            const int b = lt & 1;
+            if (lt >= 2 && !mbar_wait(acce + b, (unsigned)(((lt - 2) >> 1) & 1), a.err)) {
+                *fail = 1;
+                break;
+            }
+            tc_fence_after();
+            for (int kb = 0; kb < KB; ++kb) {
+                const int i = lt * KB + kb, st = i % NS;
+                if (!mbar_wait(full + st, (unsigned)((i / NS) & 1), a.err)) {
+                    *fail = 1;
+                    break;
+                }
+                tc_fence_after();
+#pragma unroll
+                for (int j = 0; j < kKB / 16; ++j) {
+                    const uint64_t ad = sw128_desc(ring_a + (uint32_t)st * kStageBytes + j * 32);
+                    const uint64_t bd = sw128_desc(b_a + (uint32_t)kb * NU * 128 + j * 32);
+                    umma_f16(taddr + (uint32_t)(b * NU), ad, bd, idesc, (kb | j) != 0);
+                }
+                umma_commit(empty + st);  // the stage is free once these MMAs have read it
+            }
+            umma_commit(accf + b);  // tile lt's accumulator is complete
+        }
+    } else if (warp >= 4) {
+        // ---- epilogue: TMEM -> shared logits tile ----
+        const int q = warp - 4;  // TMEM lane quarter of this warp
+        for (int lt = 0; lt < n_tiles; ++lt) {
+            const int b = lt & 1;
+            if (*fail || !mbar_wait(accf + b, (unsigned)((lt >> 1) & 1), a.err)) {
+                *fail = 1;
+                break;
+            }
+            tc_fence_after();
+            const int row = lt * kTileRows + q * 32 + lane;
+#pragma unroll
+            for (int c0 = 0; c0 < NU; c0 += 16) {
+                float v[16];
+                tmem_ld16(taddr + ((uint32_t)(q * 32) << 16) + (uint32_t)(b * NU + c0), v);
+                if (row < hi - lo)
+#pragma unroll
+                    for (int e = 0; e < 16; ++e)
+                        if (c0 + e < a.M) tile[(size_t)(c0 + e) * L.ch + row] = v[e];
+            }
+            tc_fence_before();
+            __syncwarp();
+            if (lane == 0) mbar_arrive(acce + b);
+        }
+    }
+    __syncthreads();
+    const bool ok = !*fail;
+    if (ok && a.raw_out)
+        for (int i = tid; i < a.M * (hi - lo); i += blockDim.x) {
+            const int m = i / (hi - lo), r = i - m * (hi - lo);
+            a.raw_out[(size_t)m * a.V + lo + r] = tile[(size_t)m * L.ch + r];
+        }
+    logits_rows_epilogue(a, tile, L.ch, a.M, 0, lo, hi, ok);
+    __syncthreads();
+    if (!ok && tid == 0)  // let copies in flight land before the block's memory is reused
+        for (int i = 0; i < NS; ++i) {
+            for (long long it = 0; it < (1ll << 20) && !mbar_test(full + i, 0) && !mbar_test(full + i, 1); ++it) {
+            }
+        }
+    if (warp == 1) {
+        tc_fence_after();
+        tmem_dealloc(taddr, kCols);
+    }
+}
+
+// ---------------------------------------------------------------------------
+// host side
+// ---------------------------------------------------------------------------
+static PFN_cuTensorMapEncodeTiled_v12000 encode_fn() {
+    static PFN_cuTensorMapEncodeTiled_v12000 fn = nullptr;
+    if (!fn) {
+        void *p = nullptr;
+        cudaDriverEntryPointQueryResult q;
+        if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &p, cudaEnableDefault, &q) == cudaSuccess &&
+            q == cudaDriverEntryPointSuccess)
+            fn = reinterpret_cast<PFN_cuTensorMapEncodeTiled_v12000>(p);
+    }
+    return fn;
+}
+
+// Tensor map of a row-major f16 matrix [rows][cols] read in [128 rows x 64 cols] boxes with
+// the 128-byte swizzle the UMMA K-major operand expects.
+bool make_tmap_f16_rows(void *map_out, const void *base, int rows, int cols) {
+    auto fn = encode_fn();
+    if (!fn || cols % kKB != 0 || ((uintptr_t)base & 15)) return false;
+    CUtensorMap *m = reinterpret_cast<CUtensorMap *>(map_out);
+    const cuuint64_t dims[2] = {(cuuint64_t)cols, (cuuint64_t)rows};
+    const cuuint64_t strides[1] = {(cuuint64_t)cols * 2};
+    const cuuint32_t box[2] = {(cuuint32_t)kKB, (cuuint32_t)kTileRows};
+    const cuuint32_t estr[2] = {1, 1};
+    return fn(m, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 2, const_cast<void *>(base), dims, strides, box, estr,
+              CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+              CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
+}
+
+static bool plan_tc(int M, int V, int d, int P, int &nu, LogitsTcLaunch &L) {
+    if (M < 1 || M > 32 || d % kKB != 0 || d > 1280) return false;
+    nu = M <= 16 ? 16 : 32;
+    L.tiles_total = (V + kTileRows - 1) / kTileRows;
+    L.ch = ((L.tiles_total + P - 1) / P) * kTileRows;
+    const size_t bbytes = (size_t)nu * d * 2;
+    const size_t tbytes = (size_t)M * L.ch * 4;
+    const size_t lnbytes = (size_t)2 * d * 4;
+    const size_t fixed = bbytes + tbytes + lnbytes + 256;
+    const size_t budget = 220 * 1024;
+    if (fixed + 2 * kStageBytes > budget) return false;
+    int ns = (int)((budget - fixed) / kStageBytes);
+    L.n_stages = ns > 12 ? 12 : ns;
+    L.b_off = (unsigned)(L.n_stages * kStageBytes);  // 1024-byte aligned (stages are 16 KB)
+    L.tile_off = L.b_off + (unsigned)bbytes;        // bbytes is a multiple of 2 KB
+    L.ln_off = L.tile_off + (unsigned)((tbytes + 15) & ~(size_t)15);
+    L.bar_off = L.ln_off + (unsigned)lnbytes;
+    return true;
+}
+
+static size_t tc_smem(const LogitsTcLaunch &L) { return (size_t)L.bar_off + (2 * L.n_stages + 4) * 8 + 16 + 1024; }
+
+template <int NU>
+static cudaError_t launch_tc_t(const LogitsArgs &a, const CUtensorMap &map, const LogitsTcLaunch &L, int P,
+                               cudaStream_t s, bool pdl) {
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = dim3(P);
+    cfg.blockDim = dim3(256);
+    cfg.dynamicSmemBytes = tc_smem(L);
+    cfg.stream = s;
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[0].val.programmaticStreamSerializationAllowed = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = pdl ? 1 : 0;
+    return cudaLaunchKernelEx(&cfg, k_logits_tc<NU>, a, map, L);
+}
+
+cudaError_t logits_tc_prepare() {
+    cudaError_t e = allow_dynamic_smem(k_logits_tc<16>);
+    if (e == cudaSuccess) e = allow_dynamic_smem(k_logits_tc<32>);
+    return e;
+}
+
+// Returns cudaErrorNotSupported when the shape is outside the tensor-core kernel's range.
+cudaError_t launch_logits_tc(const LogitsArgs &a, const void *tmap, int P, cudaStream_t s, bool pdl) {
+    int nu;
+    LogitsTcLaunch L;
+    if (!tmap || a.E.type != WT_F16 || !plan_tc(a.M, a.V, a.d, P, nu, L)) return cudaErrorNotSupported;
+    const CUtensorMap &map = *reinterpret_cast<const CUtensorMap *>(tmap);
+    if (nu == 16) return launch_tc_t<16>(a, map, L, P, s, pdl);
+    return launch_tc_t<32>(a, map, L, P, s, pdl);
+}
+
+}  // namespace w4j

@@ -35,7 +35,7 @@ __device__ __forceinline__ bool dgreater(double a, double b) {
 }
 
 // ---------------------------------------------------------------------------
-// block-level merge of the logits partials of one sequence
+// warp-level merges of the logits partials of one sequence
 // ---------------------------------------------------------------------------
 struct Merged {
     float max;
@@ -43,101 +43,125 @@ struct Merged {
     double sum;  // sum_i exp(l_i - max)
 };
 
-__device__ Merged merge_partials(const float *part, int P) {
-    __shared__ float r_v[kSelThreads];
-    __shared__ int r_i[kSelThreads];
-    __shared__ double r_s[kSelThreads];
-    const int tid = threadIdx.x;
+__device__ __forceinline__ void warp_best(float &v, int &i) {
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) {
+        const float ov = __shfl_xor_sync(0xffffffffu, v, o);
+        const int oi = __shfl_xor_sync(0xffffffffu, i, o);
+        if (better_c(ov, oi, v, i)) {
+            v = ov;
+            i = oi;
+        }
+    }
+}
+
+// One warp: copy P block partials into shared memory with 8 independent 8-byte loads in
+// flight per lane (one L2 round trip instead of one per partial).  A partial record starts
+// [max, sum, argmax, pad, topv[0..k), topi[0..k)], which is what is copied: row c of `dst`
+// holds those F = 4 + 2k floats.
+__device__ void stage_partials(const float *part, int P, int k, float *dst) {
+    const int lane = threadIdx.x & 31;
+    const int F2 = 2 + k;  // float2 per record
+    const int n = P * F2;
+    for (int e0 = lane; e0 < n; e0 += 32 * 8) {
+        float2 v[8];
+#pragma unroll
+        for (int j = 0; j < 8; ++j) {
+            const int e = e0 + 32 * j;
+            if (e < n) {
+                const int c = e / F2, f = e - c * F2;
+                v[j] = reinterpret_cast<const float2 *>(part + (size_t)c * kPartStride)[f];
+            }
+        }
+#pragma unroll
+        for (int j = 0; j < 8; ++j)
+            if (e0 + 32 * j < n) reinterpret_cast<float2 *>(dst)[e0 + 32 * j] = v[j];
+    }
+    __syncwarp();
+}
+
+// One warp: (max, first argmax, sum of exp relative to the max) over P staged partials.
+__device__ Merged merge_partials(const float *stg, int P, int F) {
+    const int lane = threadIdx.x & 31;
     float bv = -INFINITY;
     int bi = INT_MAX;
-    for (int c = tid; c < P; c += kSelThreads) {
-        const float v = part[(size_t)c * kPartStride];
-        const int i = __float_as_int(part[(size_t)c * kPartStride + 2]);
+    for (int c = lane; c < P; c += 32) {
+        const float v = stg[c * F];
+        const int i = __float_as_int(stg[c * F + 2]);
         if (better_c(v, i, bv, bi)) {
             bv = v;
             bi = i;
         }
     }
-    r_v[tid] = bv;
-    r_i[tid] = bi;
-    __syncthreads();
-    for (int o = kSelThreads / 2; o > 0; o >>= 1) {
-        if (tid < o && better_c(r_v[tid + o], r_i[tid + o], r_v[tid], r_i[tid])) {
-            r_v[tid] = r_v[tid + o];
-            r_i[tid] = r_i[tid + o];
-        }
-        __syncthreads();
-    }
-    const float M = r_v[0];
-    const int arg = r_i[0];
+    warp_best(bv, bi);
     double s = 0.0;
-    if (M != -INFINITY)
-        for (int c = tid; c < P; c += kSelThreads) {
-            const float mc = part[(size_t)c * kPartStride];
-            if (mc != -INFINITY) s += (double)part[(size_t)c * kPartStride + 1] * exp((double)(mc - M));
+    if (bv != -INFINITY)
+        for (int c = lane; c < P; c += 32) {
+            const float mc = stg[c * F];
+            if (mc != -INFINITY) s += (double)stg[c * F + 1] * exp((double)(mc - bv));
         }
-    r_s[tid] = s;
-    __syncthreads();
-    for (int o = kSelThreads / 2; o > 0; o >>= 1) {
-        if (tid < o) r_s[tid] += r_s[tid + o];
-        __syncthreads();
-    }
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) s += __shfl_xor_sync(0xffffffffu, s, o);
     Merged out;
-    out.max = M;
+    out.max = bv;
     // reference argmax: index 0 when nothing beats a[0] = -inf
-    out.argmax = (M == -INFINITY || arg == INT_MAX) ? 0 : arg;
-    out.sum = r_s[0];
-    __syncthreads();
+    out.argmax = (bv == -INFINITY || bi == INT_MAX) ? 0 : bi;
+    out.sum = s;
     return out;
 }
 
-// Top-k over the per-block candidate lists (value desc, index asc); unfilled -> (-inf, 0).
-__device__ void merge_topk(const float *part, int P, int k, float *out_v, int *out_i) {
-    __shared__ float r_v[kSelThreads];
-    __shared__ int r_i[kSelThreads];
-    __shared__ int chosen[kMaxTopK];
-    const int tid = threadIdx.x;
+// One warp: top-k over the staged per-block candidate lists, each sorted (value desc,
+// index asc); a k-way merge where every lane advances the heads of the blocks it owns.
+// Unfilled entries come out as (-inf, 0), as topkIndices leaves them.
+__device__ void merge_topk(const float *stg, int P, int F, int kk, int k, float *out_v, int *out_i) {
+    const int lane = threadIdx.x & 31;
+    constexpr int kMaxOwned = 32;  // P <= 1024 blocks
+    unsigned char head[kMaxOwned];
+    const int J = (P + 31) / 32;
+    for (int j = 0; j < J && j < kMaxOwned; ++j) head[j] = 0;
     for (int r = 0; r < k; ++r) {
         float bv = -INFINITY;
-        int bi = INT_MAX;
-        for (int e = tid; e < P * k; e += kSelThreads) {
-            const int c = e / k, j = e % k;
-            const float v = part[(size_t)c * kPartStride + 4 + j];
-            const int i = __float_as_int(part[(size_t)c * kPartStride + 4 + kMaxTopK + j]);
-            if (v == -INFINITY) continue;
-            bool taken = false;
-            for (int q = 0; q < r; ++q) taken |= chosen[q] == i;
-            if (!taken && better_c(v, i, bv, bi)) {
+        int bi = INT_MAX, bj = -1;
+        for (int j = 0; j < J && j < kMaxOwned; ++j) {
+            const int c = lane + 32 * j;
+            if (c >= P || head[j] >= kk) continue;
+            const float v = stg[c * F + 4 + head[j]];
+            const int i = __float_as_int(stg[c * F + 4 + kk + head[j]]);
+            if (v != -INFINITY && better_c(v, i, bv, bi)) {
                 bv = v;
                 bi = i;
+                bj = j;
             }
         }
-        r_v[tid] = bv;
-        r_i[tid] = bi;
-        __syncthreads();
-        for (int o = kSelThreads / 2; o > 0; o >>= 1) {
-            if (tid < o && better_c(r_v[tid + o], r_i[tid + o], r_v[tid], r_i[tid])) {
-                r_v[tid] = r_v[tid + o];
-                r_i[tid] = r_i[tid + o];
-            }
-            __syncthreads();
+        const int mine = bi;
+        warp_best(bv, bi);
+        if (bi != INT_MAX && mine == bi && bj >= 0) head[bj]++;  // ids are unique across blocks
+        if (lane == 0) {
+            out_v[r] = bi == INT_MAX ? -INFINITY : bv;
+            out_i[r] = bi == INT_MAX ? 0 : bi;
         }
-        if (tid == 0) {
-            const bool none = r_i[0] == INT_MAX;
-            out_v[r] = none ? -INFINITY : r_v[0];
-            out_i[r] = none ? 0 : r_i[0];
-            chosen[r] = none ? -1 : r_i[0];
-        }
-        __syncthreads();
     }
+    __syncwarp();
 }
 
 // ---------------------------------------------------------------------------
 // masks of the next step (one warp)
 // ---------------------------------------------------------------------------
-__device__ void build_masks(const DecodeState &st, int m, const int *h, int n, bool first_ts, bool blank,
-                            bool rules) {
+__device__ void build_masks(const DecodeState &st, int m, const int *hg, int n, bool first_ts, bool blank,
+                            bool rules, int *hbuf) {
     const int lane = threadIdx.x & 31;
+    // the history is scanned many times below: bring it into shared memory first
+    for (int i0 = lane; i0 < n; i0 += 32 * 8) {
+        int v[8];
+#pragma unroll
+        for (int j = 0; j < 8; ++j)
+            if (i0 + 32 * j < n) v[j] = hg[i0 + 32 * j];
+#pragma unroll
+        for (int j = 0; j < 8; ++j)
+            if (i0 + 32 * j < n) hbuf[i0 + 32 * j] = v[j];
+    }
+    __syncwarp();
+    const int *h = hbuf;
     int *list = st.dyn_list + (size_t)m * st.dyn_stride;
     int2 *rg = st.ranges + (size_t)m * kMaxRanges;
     int cnt = 0, nr = 0;
@@ -311,17 +335,23 @@ __global__ void __launch_bounds__(kSelThreads) k_select_greedy(DecodeState st, i
                                                                float *masked, int step) {
     __shared__ int s_tok;
     __shared__ double s_lp;
+    extern __shared__ __align__(16) float sel_smem[];
+    float *stg = sel_smem;                                   // [P][3]
+    int *hbuf = reinterpret_cast<int *>(sel_smem + P * 4);   // [hs]
     pdl_trigger();
     pdl_wait();
     const int s = blockIdx.x;
     const int m = s;
     if (st.done[s]) return;
     if (mode == SEL_GREEDY) {
-        const Merged mg = merge_partials(part + (size_t)m * P * kPartStride, P);
-        if (threadIdx.x == 0) {
-            s_tok = mg.argmax;
-            // logSoftmax(last, best) with last[best] == max: (max - max) - log(sum)
-            s_lp = (double)(mg.max - mg.max) - log(mg.sum);
+        if (threadIdx.x < 32) {
+            stage_partials(part + (size_t)m * P * kPartStride, P, 0, stg);
+            const Merged mg = merge_partials(stg, P, 4);
+            if (threadIdx.x == 0) {
+                s_tok = mg.argmax;
+                // logSoftmax(last, best) with last[best] == max: (max - max) - log(sum)
+                s_lp = (double)(mg.max - mg.max) - log(mg.sum);
+            }
         }
     } else {
         int tok;
@@ -353,7 +383,7 @@ __global__ void __launch_bounds__(kSelThreads) k_select_greedy(DecodeState st, i
     __syncthreads();
     if (threadIdx.x < 32 && s_tok != st.eot)
         build_masks(st, m, st.hist[0] + (size_t)m * st.hs, min(len + 1, st.max_tokens), false, false,
-                    true);
+                    true, hbuf);
 }
 
 // ---------------------------------------------------------------------------
@@ -367,11 +397,21 @@ __global__ void __launch_bounds__(kSelThreads) k_select_beam_init(DecodeState st
     const int s = blockIdx.x;
     const int B = st.beam;
     const float *pp = part + (size_t)s * P * kPartStride;
-    const Merged mg = merge_partials(pp, P);
-    merge_topk(pp, P, B, tv, ti);
-    const float log_sum_f = (float)((double)mg.max + log(mg.sum));
+    extern __shared__ __align__(16) float sel_smem[];
+    const int F = 4 + 2 * B;
+    // per warp: staged partials, then a history buffer; a multiple of 4 floats keeps every
+    // warp's region 16-byte aligned for the vector copies into it
+    const int region = (P * F + st.hs + 3) & ~3;
+    __shared__ float s_lsf;
+    if (threadIdx.x < 32) {
+        stage_partials(pp, P, B, sel_smem);
+        const Merged mg = merge_partials(sel_smem, P, F);
+        merge_topk(sel_smem, P, F, B, B, tv, ti);
+        if (threadIdx.x == 0) s_lsf = (float)((double)mg.max + log(mg.sum));
+    }
     const int base = st.stream_base[s];  // prompt rows were written in the stream's first slot
     __syncthreads();
+    const float log_sum_f = s_lsf;
     for (int b = 0; b < B; ++b) {
         const int mb = s * B + b;
         for (int p = threadIdx.x; p < st.n_prompt; p += kSelThreads)
@@ -394,7 +434,8 @@ __global__ void __launch_bounds__(kSelThreads) k_select_beam_init(DecodeState st
     const int warp = threadIdx.x >> 5;
     for (int b = warp; b < B; b += kSelThreads / 32) {
         const int mb = s * B + b;
-        build_masks(st, mb, st.hist[0] + (size_t)mb * st.hs, 1, false, false, true);
+        build_masks(st, mb, st.hist[0] + (size_t)mb * st.hs, 1, false, false, true,
+                    reinterpret_cast<int *>(sel_smem + (size_t)b * region + P * F));
     }
 }
 
@@ -403,8 +444,6 @@ __global__ void __launch_bounds__(kSelThreads) k_select_beam(DecodeState st, int
     __shared__ double c_score[kMaxB * (kMaxB + 1)];
     __shared__ int c_beam[kMaxB * (kMaxB + 1)], c_tok[kMaxB * (kMaxB + 1)];
     __shared__ int n_c;
-    __shared__ float tv[kMaxTopK];
-    __shared__ int ti[kMaxTopK];
     __shared__ int new_src[kMaxB], new_tok[kMaxB];
     __shared__ double new_score[kMaxB];
     __shared__ int fin_src[kMaxB];
@@ -417,43 +456,67 @@ __global__ void __launch_bounds__(kSelThreads) k_select_beam(DecodeState st, int
     const int B = st.beam;
     const int po = parity, pn = parity ^ 1;
     const int stride = st.hs;
-    if (threadIdx.x == 0) n_c = 0;
-    __syncthreads();
-    for (int b = 0; b < B; ++b) {
+    __shared__ float b_tv[kMaxB][kMaxTopK];
+    __shared__ int b_ti[kMaxB][kMaxTopK];
+    __shared__ float b_lsf[kMaxB];
+    __shared__ int b_live[kMaxB];
+    extern __shared__ __align__(16) float sel_smem[];
+    const int F = 4 + 2 * (B + 1);
+    // per warp: staged partials, then a history buffer; a multiple of 4 floats keeps every
+    // warp's region 16-byte aligned for the vector copies into it
+    const int region = (P * F + stride + 3) & ~3;
+    const int warp = threadIdx.x >> 5;
+    for (int b = warp; b < B; b += kSelThreads / 32) {  // one warp per beam
         const int mb = s * B + b;
         const int len = st.hist_len[po][mb];
-        if (st.hist[po][(size_t)mb * stride + len - 1] == st.eot) continue;  // finished beam
-        const float *pp = part + (size_t)mb * P * kPartStride;
-        const Merged mg = merge_partials(pp, P);
-        merge_topk(pp, P, B + 1, tv, ti);
-        if (threadIdx.x == 0) {
-            const float log_sum_f = (float)((double)mg.max + log(mg.sum));
-            const double blp = st.lp[po][mb];
+        const bool live = st.hist[po][(size_t)mb * stride + len - 1] != st.eot;  // finished beams skip
+        if (threadIdx.x % 32 == 0) b_live[b] = live;
+        if (!live) continue;
+        float *stg = sel_smem + (size_t)b * region;
+        stage_partials(part + (size_t)mb * P * kPartStride, P, B + 1, stg);
+        const Merged mg = merge_partials(stg, P, F);
+        merge_topk(stg, P, F, B + 1, B + 1, b_tv[b], b_ti[b]);
+        if (threadIdx.x % 32 == 0) b_lsf[b] = (float)((double)mg.max + log(mg.sum));
+    }
+    __syncthreads();
+    if (threadIdx.x == 0) {
+        n_c = 0;
+        for (int b = 0; b < B; ++b) {  // candidates in the reference's insertion order
+            if (!b_live[b]) continue;
+            const double blp = st.lp[po][s * B + b];
             for (int k = 0; k < B + 1; ++k) {
-                c_score[n_c] = blp + (double)(float)(tv[k] - log_sum_f);
+                c_score[n_c] = blp + (double)(float)(b_tv[b][k] - b_lsf[b]);
                 c_beam[n_c] = b;
-                c_tok[n_c] = ti[k];
+                c_tok[n_c] = b_ti[b][k];
                 ++n_c;
             }
         }
-        __syncthreads();
     }
-    if (threadIdx.x == 0) {
-        // stable sort by score, descending (List.sort with Double.compare)
-        for (int i = 1; i < n_c; ++i) {
-            const double cs = c_score[i];
-            const int cb = c_beam[i], ct = c_tok[i];
-            int j = i - 1;
-            while (j >= 0 && dgreater(cs, c_score[j])) {
-                c_score[j + 1] = c_score[j];
-                c_beam[j + 1] = c_beam[j];
-                c_tok[j + 1] = c_tok[j];
-                --j;
-            }
-            c_score[j + 1] = cs;
-            c_beam[j + 1] = cb;
-            c_tok[j + 1] = ct;
+    __syncthreads();
+    // stable sort by score, descending (List.sort with Double.compare): every candidate
+    // computes its own rank in parallel and moves there
+    __shared__ double r_score[kMaxB * (kMaxB + 1)];
+    __shared__ int r_beam[kMaxB * (kMaxB + 1)], r_tok[kMaxB * (kMaxB + 1)];
+    if (threadIdx.x < n_c) {
+        const int t = threadIdx.x;
+        const double cs = c_score[t];
+        int rank = 0;
+        for (int u = 0; u < n_c; ++u) {
+            const double us = c_score[u];
+            if (dgreater(us, cs) || (u < t && !dgreater(cs, us))) ++rank;
         }
+        r_score[rank] = cs;
+        r_beam[rank] = c_beam[t];
+        r_tok[rank] = c_tok[t];
+    }
+    __syncthreads();
+    if (threadIdx.x < n_c) {
+        c_score[threadIdx.x] = r_score[threadIdx.x];
+        c_beam[threadIdx.x] = r_beam[threadIdx.x];
+        c_tok[threadIdx.x] = r_tok[threadIdx.x];
+    }
+    __syncthreads();
+    if (threadIdx.x == 0) {
         int saved = 0, nf = 0, fin = st.fin_n[s];
         for (int i = 0; i < n_c; ++i) {
             if (c_tok[i] == st.eot) {
@@ -498,24 +561,57 @@ __global__ void __launch_bounds__(kSelThreads) k_select_beam(DecodeState st, int
     }
     // rearrange: new beam b continues source beam new_src[b] (beams past `saved` copy beam 0)
     const int saved = saved_s;
-    for (int b = 0; b < B; ++b) {
+    __shared__ int c_len[kMaxB], c_pos[kMaxB], c_src[kMaxB];
+    if (threadIdx.x < B) {
+        const int b = threadIdx.x;
         const int bb = b < saved ? b : 0;
-        const int src = s * B + new_src[bb];
-        const int mb = s * B + b;
-        const int len = st.hist_len[po][src];
-        const int pos = st.seq_pos[src];  // row written this step by the source beam
-        int *hd = st.hist[pn] + (size_t)mb * stride;
-        const int *hs = st.hist[po] + (size_t)src * stride;
-        for (int i = threadIdx.x; i < len; i += kSelThreads) hd[i] = hs[i];
-        int *td = st.table[pn] + (size_t)mb * st.n_ctx;
-        const int *ts = st.table[po] + (size_t)src * st.n_ctx;
-        for (int i = threadIdx.x; i <= pos; i += kSelThreads) td[i] = ts[i];
-        if (threadIdx.x == 0) {
-            hd[len] = new_tok[bb];
-            st.hist_len[pn][mb] = len + 1;
-            st.lp[pn][mb] = new_score[bb];
-            if (pos + 1 < st.n_ctx) td[pos + 1] = st.seq_slot[mb];
+        c_src[b] = s * B + new_src[bb];
+        c_len[b] = st.hist_len[po][c_src[b]];
+        c_pos[b] = st.seq_pos[c_src[b]];  // row written this step by the source beam
+    }
+    __syncthreads();
+    // copy histories (len ints) and tables (pos + 1 ints) of all new beams, flattened over
+    // the block with 8 independent loads in flight per thread
+    {
+        const int per = stride + st.n_ctx;  // slot per beam: history part then table part
+        const int total = B * per;
+        for (int i0 = threadIdx.x; i0 < total; i0 += kSelThreads * 8) {
+            int v[8];
+#pragma unroll
+            for (int j = 0; j < 8; ++j) {
+                const int i = i0 + kSelThreads * j;
+                v[j] = 0;
+                if (i < total) {
+                    const int b = i / per, r = i - b * per;
+                    if (r < stride) {
+                        if (r < c_len[b]) v[j] = st.hist[po][(size_t)c_src[b] * stride + r];
+                    } else if (r - stride <= c_pos[b]) {
+                        v[j] = st.table[po][(size_t)c_src[b] * st.n_ctx + (r - stride)];
+                    }
+                }
+            }
+#pragma unroll
+            for (int j = 0; j < 8; ++j) {
+                const int i = i0 + kSelThreads * j;
+                if (i >= total) continue;
+                const int b = i / per, r = i - b * per;
+                const int mb = s * B + b;
+                if (r < stride) {
+                    if (r < c_len[b]) st.hist[pn][(size_t)mb * stride + r] = v[j];
+                } else if (r - stride <= c_pos[b]) {
+                    st.table[pn][(size_t)mb * st.n_ctx + (r - stride)] = v[j];
+                }
+            }
         }
+    }
+    if (threadIdx.x < B) {
+        const int b = threadIdx.x;
+        const int bb = b < saved ? b : 0;
+        const int mb = s * B + b;
+        st.hist[pn][(size_t)mb * stride + c_len[b]] = new_tok[bb];
+        st.hist_len[pn][mb] = c_len[b] + 1;
+        st.lp[pn][mb] = new_score[bb];
+        if (c_pos[b] + 1 < st.n_ctx) st.table[pn][(size_t)mb * st.n_ctx + c_pos[b] + 1] = st.seq_slot[mb];
     }
     __syncthreads();
     if (threadIdx.x == 0) {
@@ -529,10 +625,10 @@ __global__ void __launch_bounds__(kSelThreads) k_select_beam(DecodeState st, int
     }
     __syncthreads();
     // every beam advanced one position; positions were equal, so read them after the writes
-    const int warp = threadIdx.x >> 5;
     for (int b = warp; b < B; b += kSelThreads / 32) {
         const int mb = s * B + b;
-        build_masks(st, mb, st.hist[pn] + (size_t)mb * stride, st.hist_len[pn][mb], false, false, true);
+        build_masks(st, mb, st.hist[pn] + (size_t)mb * stride, st.hist_len[pn][mb], false, false, true,
+                    reinterpret_cast<int *>(sel_smem + (size_t)b * region + P * F));
     }
     if (threadIdx.x == 0) st.beam_par[s] = pn;  // parity holding the live beams (finalize reads it)
 }
@@ -571,7 +667,8 @@ __global__ void k_nsp(DecodeState st, const float *ns_part, int P, const float *
 __global__ void k_init_masks(DecodeState st, int beam_mode) {
     const int m = blockIdx.x;
     if (threadIdx.x >= 32) return;
-    build_masks(st, m, st.hist[0] + (size_t)m * st.hs, 0, !beam_mode, true, !beam_mode);
+    __shared__ int hbuf[1];  // the first decision has no history
+    build_masks(st, m, st.hist[0] + (size_t)m * st.hs, 0, !beam_mode, true, !beam_mode, hbuf);
 }
 
 __global__ void k_finalize(DecodeState st, int beam_mode) {
@@ -628,7 +725,10 @@ __global__ void k_finalize(DecodeState st, int beam_mode) {
 
 __global__ void k_argmax_merge(const float *part, int P, int32_t *tok, double *lp) {
     const int m = blockIdx.x;
-    const Merged mg = merge_partials(part + (size_t)m * P * kPartStride, P);
+    extern __shared__ __align__(16) float sel_smem[];
+    if (threadIdx.x >= 32) return;
+    stage_partials(part + (size_t)m * P * kPartStride, P, 0, sel_smem);
+    const Merged mg = merge_partials(sel_smem, P, 4);
     if (threadIdx.x == 0) {
         tok[m] = mg.argmax;
         lp[m] = (double)(mg.max - mg.max) - log(mg.sum);
@@ -648,10 +748,29 @@ static cudaLaunchConfig_t cfg_for(dim3 grid, dim3 block, cudaStream_t s, bool pd
     return cfg;
 }
 
+// Dynamic shared memory of the select kernels: per working warp, the staged partials of one
+// sequence (P x (3 + 2k) floats) followed by a token-history buffer (hs ints).
+static size_t select_smem(const DecodeState &st, int mode, int P) {
+    const int B = st.beam;
+    if (mode == SEL_GREEDY || mode == SEL_SAMPLE) return ((size_t)P * 4 + st.hs) * 4;
+    const int k = mode == SEL_BEAM_INIT ? B : B + 1;
+    return (size_t)B * (((size_t)P * (4 + 2 * k) + st.hs + 3) & ~(size_t)3) * 4;
+}
+
+cudaError_t select_prepare() {
+    cudaError_t e = allow_dynamic_smem(k_select_greedy);
+    if (e == cudaSuccess) e = allow_dynamic_smem(k_select_beam_init);
+    if (e == cudaSuccess) e = allow_dynamic_smem(k_select_beam);
+    if (e == cudaSuccess) e = allow_dynamic_smem(k_argmax_merge);
+    return e;
+}
+
 cudaError_t launch_select(const DecodeState &st, int mode, int parity, const float *part, int n_parts,
                           float *masked, int step, cudaStream_t s, bool pdl) {
     cudaLaunchAttribute attr[1];
     cudaLaunchConfig_t cfg = cfg_for(dim3(st.n_streams), dim3(kSelThreads), s, pdl, attr);
+    cfg.dynamicSmemBytes = select_smem(st, mode, n_parts);
+    if (cfg.dynamicSmemBytes > 227 * 1024) return cudaErrorInvalidValue;
     switch (mode) {
         case SEL_GREEDY:
         case SEL_SAMPLE:
@@ -683,7 +802,7 @@ cudaError_t launch_finalize(const DecodeState &st, int beam_mode, int parity, cu
 }
 
 cudaError_t launch_argmax_merge(const float *part, int n_parts, int M, int32_t *tok, double *lp, cudaStream_t s) {
-    k_argmax_merge<<<M, kSelThreads, 0, s>>>(part, n_parts, tok, lp);
+    k_argmax_merge<<<M, kSelThreads, (size_t)n_parts * 4 * 4, s>>>(part, n_parts, tok, lp);
     return cudaGetLastError();
 }
 

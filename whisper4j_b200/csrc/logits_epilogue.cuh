@@ -1,0 +1,120 @@
+// logits_epilogue.cuh — shared epilogue of the vocabulary-logits kernels (SIMT and tcgen05).
+#pragma once
+#include "w4j_internal.cuh"
+
+namespace w4j {
+
+__device__ __forceinline__ bool logit_better(float v1, int i1, float v2, int i2) {
+    return v1 > v2 || (v1 == v2 && i1 < i2);
+}
+
+// Logit processors and block reductions over the logits of rows [lo, hi) held in shared
+// memory (tile[mm][row - lo], stride ch) for sequences m0 .. m0+MT: unmasked statistics for
+// the no-speech probability, the masks (suppress list, n-gram and timestamp rules), then max,
+// first argmax, sum of exp and the block's top-k candidates.  One warp per sequence.
+__device__ __forceinline__ void logits_rows_epilogue(const LogitsArgs &a, float *tile, int ch, int MT, int m0, int lo, int hi,
+                                     bool ok) {
+    const int P = gridDim.x;
+    const int nrows = hi - lo;
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+for (int mm = warp; mm < MT; mm += blockDim.x / 32) {
+        const int m = m0 + mm;
+        if (m >= a.M || !ok) continue;
+        if (a.active && !a.active[m]) continue;
+        float *row = tile + (size_t)mm * ch;
+        const int n = nrows;
+        if (a.ns_token >= 0) {  // unmasked statistics of this row (no-speech probability)
+            float mx = -INFINITY;
+            for (int i = lane; i < n; i += 32) mx = fmaxf(mx, row[i]);
+            mx = warp_max(mx);
+            float sm = 0.f;
+            for (int i = lane; i < n; i += 32) sm += (mx == -INFINITY) ? 0.f : __expf(row[i] - mx);
+            sm = warp_sum(sm);
+            if (lane == 0) {
+                float *np = a.ns_part + ((size_t)m * P + blockIdx.x) * 2;
+                np[0] = mx;
+                np[1] = sm;
+            }
+            if (a.ns_token >= lo && a.ns_token < hi && lane == 0) a.ns_value[m] = row[a.ns_token - lo];
+            __syncwarp();
+        }
+        if (a.use_mask) {
+            const MaskArgs &mk = a.mask;
+            for (int r = 0; r < mk.n_ranges[m]; ++r) {
+                const int2 rg = mk.ranges[(size_t)m * kMaxRanges + r];
+                const int b0 = max(rg.x, lo), b1 = min(rg.y, hi);
+                for (int i = b0 + lane; i < b1; i += 32) row[i - lo] = -INFINITY;
+            }
+            // id lists: 8 independent loads in flight per lane
+            auto mask_list = [&](const int *list, int n_list) {
+                for (int i0 = lane; i0 < n_list; i0 += 32 * 8) {
+                    int tk[8];
+#pragma unroll
+                    for (int j = 0; j < 8; ++j) tk[j] = i0 + 32 * j < n_list ? list[i0 + 32 * j] : -1;
+#pragma unroll
+                    for (int j = 0; j < 8; ++j)
+                        if (tk[j] >= lo && tk[j] < hi) row[tk[j] - lo] = -INFINITY;
+                }
+            };
+            mask_list(mk.static_list, mk.n_static);
+            mask_list(mk.dyn_list + (size_t)m * mk.dyn_stride, mk.dyn_count[m]);
+            __syncwarp();
+        }
+        if (a.masked_out)
+            for (int i = lane; i < n; i += 32) a.masked_out[(size_t)m * a.V + lo + i] = row[i];
+        // max + first argmax
+        float bv = -INFINITY;
+        int bi = INT_MAX;
+        for (int i = lane; i < n; i += 32)
+            if (logit_better(row[i], lo + i, bv, bi)) {
+                bv = row[i];
+                bi = lo + i;
+            }
+#pragma unroll
+        for (int o = 16; o > 0; o >>= 1) {
+            const float ov = __shfl_xor_sync(0xffffffffu, bv, o);
+            const int oi = __shfl_xor_sync(0xffffffffu, bi, o);
+            if (logit_better(ov, oi, bv, bi)) {
+                bv = ov;
+                bi = oi;
+            }
+        }
+        float sm = 0.f;
+        if (bv != -INFINITY)
+            for (int i = lane; i < n; i += 32) sm += __expf(row[i] - bv);
+        sm = warp_sum(sm);
+        float *pp = a.part + ((size_t)m * P + blockIdx.x) * kPartStride;
+        if (lane == 0) {
+            pp[0] = bv;
+            pp[1] = sm;
+            pp[2] = __int_as_float(bi == INT_MAX ? lo : bi);
+        }
+        // top-k candidates of this block (value desc, index asc); unfilled: (-inf, 0)
+        for (int k = 0; k < a.topk; ++k) {
+            float kv = -INFINITY;
+            int ki = INT_MAX;
+            for (int i = lane; i < n; i += 32)
+                if (row[i] != -INFINITY && logit_better(row[i], lo + i, kv, ki)) {
+                    kv = row[i];
+                    ki = lo + i;
+                }
+#pragma unroll
+            for (int o = 16; o > 0; o >>= 1) {
+                const float ov = __shfl_xor_sync(0xffffffffu, kv, o);
+                const int oi = __shfl_xor_sync(0xffffffffu, ki, o);
+                if (logit_better(ov, oi, kv, ki)) {
+                    kv = ov;
+                    ki = oi;
+                }
+            }
+            if (lane == 0) {
+                pp[4 + k] = kv;
+                pp[4 + a.topk + k] = __int_as_float(ki == INT_MAX ? 0 : ki);
+            }
+            if (ki != INT_MAX && ki - lo >= 0 && ki - lo < n && lane == ((ki - lo) & 31)) row[ki - lo] = -INFINITY;
+            __syncwarp();
+        }
+    }
+}
+
+}  // namespace w4j

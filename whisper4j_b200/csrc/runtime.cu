@@ -13,6 +13,7 @@
 #include <cmath>
 #include <cstdarg>
 #include <cstdio>
+#include <cstdlib>
 #include <cstring>
 #include <map>
 #include <mutex>
@@ -112,6 +113,9 @@ struct w4j_ctx {
     int last_steps = 0;
     long long last_launches = 0;
     cudaEvent_t ev0 = nullptr, ev1 = nullptr;
+    alignas(64) unsigned char e_tmap[128] = {};  // TMA map of the f16 token embedding
+    bool e_tmap_ok = false;
+    bool tc_logits = true;
 };
 
 template <typename T>
@@ -150,9 +154,11 @@ static void build_gelu_lut(std::vector<float> &t) {
     }
 }
 
-static int choose_split(int groups_x_heads, int len, int sms) {
+// Key splits of an attention launch: enough blocks to cover the SMs twice, at least one
+// full 128-key tile per split, and no more partials than the combine can stage.
+static int choose_split(int groups_x_heads, int len, int sms, int nq) {
     int want = (2 * sms + groups_x_heads - 1) / std::max(1, groups_x_heads);
-    const int cap = std::max(1, (len + 63) / 64);
+    const int cap = std::min(std::max(1, (len + 63) / 64), attn_max_splits(nq));
     return std::max(1, std::min(want, cap));
 }
 
@@ -193,6 +199,7 @@ extern "C" int w4j_ctx_create(const w4j_dims *dims, int device, int max_streams,
     c->n_slots = max_streams * max_beam + 1;  // + one private slot for forward without a cache
     c->M_max = max_streams * max_beam;
     c->sm_count = prop.multiProcessorCount;
+    if (const char *ev = getenv("W4J_NO_TC_LOGITS")) c->tc_logits = ev[0] == '0';
     c->layers.resize(c->L);
     c->cache_len.assign(max_streams, 0);
     c->has_xa.assign(max_streams, 0);
@@ -205,7 +212,8 @@ extern "C" int w4j_ctx_create(const w4j_dims *dims, int device, int max_streams,
     if (cudaStreamCreateWithFlags(&c->stream, cudaStreamNonBlocking) != cudaSuccess) return fail(set_err(W4J_ERR_CUDA, "stream"));
     cudaEventCreate(&c->ev0);
     cudaEventCreate(&c->ev1);
-    if ((rc = (int)gemv_prepare()) != 0) return fail(set_err(W4J_ERR_CUDA, "kernel attributes: %s", cudaGetErrorString((cudaError_t)rc)));
+    if ((rc = (int)gemv_prepare()) != 0 || (rc = (int)select_prepare()) != 0 || (rc = (int)logits_tc_prepare()) != 0)
+        return fail(set_err(W4J_ERR_CUDA, "kernel attributes: %s", cudaGetErrorString((cudaError_t)rc)));
     const size_t V = c->V, C = c->C, A = c->A, L = c->L;
     const size_t M = c->M_max;
     // caches
@@ -390,6 +398,7 @@ extern "C" int w4j_upload_tensor(w4j_ctx *c, const char *name, int type, const i
     if (s == "token_embedding.weight") {
         if (!shape_is(d, c->V)) return set_err(W4J_ERR_ARG, "%s: expected (%d, %d)", name, c->V, d);
         TRY(upload_mat(c, c->E, c->V, 0, c->V, d, data, nbytes, type));
+        c->e_tmap_ok = c->tc_logits && c->E.type == WT_F16 && make_tmap_f16_rows(c->e_tmap, c->E.h, c->V, d);
     } else if (s == "positional_embedding") {
         if (!shape_is(d, c->C)) return set_err(W4J_ERR_ARG, "%s: expected (%d, %d)", name, c->C, d);
         TRY(upload_vec(c, &c->pos_emb, (size_t)c->C * d, data, nbytes, type));
@@ -518,13 +527,14 @@ struct PassArgs {
     int groups, nq;
     const int *cross_stream;  // [groups]
     const int *group_active;  // [groups] or null
+    int self_prefetch;        // older self-cache rows were written by an earlier graph launch
 };
 
 static int run_layers(w4j_ctx *c, const PassArgs &pa, long long &launches) {
     const bool pdl = true;
     const int d = c->d;
-    const int self_split = choose_split(pa.M * c->H, c->C, c->sm_count);
-    const int cross_split = choose_split(pa.groups * c->H, c->A, c->sm_count);
+    const int self_split = choose_split(pa.M * c->H, c->C, c->sm_count, 1);
+    const int cross_split = choose_split(pa.groups * c->H, c->A, c->sm_count, pa.nq);
     for (int l = 0; l < c->L; ++l) {
         LayerDev &ly = c->layers[l];
         GemvArgs g;
@@ -550,6 +560,7 @@ static int run_layers(w4j_ctx *c, const PassArgs &pa, long long &launches) {
         g.n_head = c->H;
         g.n_ctx = c->C;
         g.active = pa.active;
+        g.err = c->st.err;
         CUDA_TRY(launch_gemv(g, c->stream, pdl));
 
         AttnArgs sa;
@@ -572,6 +583,8 @@ static int run_layers(w4j_ctx *c, const PassArgs &pa, long long &launches) {
         sa.counters = c->attn_ctr;
         sa.out = c->attn;
         sa.active = pa.active;
+        sa.err = c->st.err;
+        sa.self_prefetch = pa.self_prefetch;
         CUDA_TRY(launch_attn(sa, c->stream, pdl));
 
         GemvArgs go;
@@ -583,6 +596,7 @@ static int run_layers(w4j_ctx *c, const PassArgs &pa, long long &launches) {
         go.out_mode = OUT_RESIDUAL;
         go.y = c->x;
         go.active = pa.active;
+        go.err = c->st.err;
         CUDA_TRY(launch_gemv(go, c->stream, pdl));
 
         GemvArgs gq;
@@ -595,6 +609,7 @@ static int run_layers(w4j_ctx *c, const PassArgs &pa, long long &launches) {
         gq.ln_b = ly.ln2b;
         gq.out_mode = OUT_STORE;
         gq.y = c->q;
+        gq.err = c->st.err;
         CUDA_TRY(launch_gemv(gq, c->stream, pdl));
 
         AttnArgs ca;
@@ -615,6 +630,7 @@ static int run_layers(w4j_ctx *c, const PassArgs &pa, long long &launches) {
         ca.counters = c->attn_ctr;
         ca.out = c->attn;
         ca.active = pa.group_active;
+        ca.err = c->st.err;
         CUDA_TRY(launch_attn(ca, c->stream, pdl));
 
         GemvArgs gxo;
@@ -626,6 +642,7 @@ static int run_layers(w4j_ctx *c, const PassArgs &pa, long long &launches) {
         gxo.out_mode = OUT_RESIDUAL;
         gxo.y = c->x;
         gxo.active = pa.active;
+        gxo.err = c->st.err;
         CUDA_TRY(launch_gemv(gxo, c->stream, pdl));
 
         GemvArgs g1;
@@ -639,6 +656,7 @@ static int run_layers(w4j_ctx *c, const PassArgs &pa, long long &launches) {
         g1.out_mode = OUT_GELU;
         g1.y = c->h;
         g1.gelu_lut = c->gelu_lut;
+        g1.err = c->st.err;
         CUDA_TRY(launch_gemv(g1, c->stream, pdl));
 
         GemvArgs g2;
@@ -650,6 +668,7 @@ static int run_layers(w4j_ctx *c, const PassArgs &pa, long long &launches) {
         g2.out_mode = OUT_RESIDUAL;
         g2.y = c->x;
         g2.active = pa.active;
+        g2.err = c->st.err;
         CUDA_TRY(launch_gemv(g2, c->stream, pdl));
         launches += 8;
     }
@@ -667,7 +686,17 @@ static LogitsArgs logits_args(w4j_ctx *c, int M, const int *active) {
     la.d = c->d;
     la.part = c->logit_part;
     la.active = active;
+    la.err = c->st.err;
     return la;
+}
+
+// The vocabulary pass: tcgen05 kernel when the embedding is f16 and M <= 32, else the SIMT one.
+static cudaError_t run_logits(w4j_ctx *c, const LogitsArgs &la, bool pdl) {
+    if (c->e_tmap_ok) {
+        const cudaError_t e = launch_logits_tc(la, c->e_tmap, c->n_parts, c->stream, pdl);
+        if (e != cudaErrorNotSupported) return e;
+    }
+    return launch_logits(la, c->n_parts, c->stream, pdl);
 }
 
 // ---------------------------------------------------------------------------
@@ -710,7 +739,7 @@ extern "C" int w4j_forward(w4j_ctx *c, int slot, const int32_t *tokens, int n, i
         TRY(run_layers(c, pa, launches));
         LogitsArgs la = logits_args(c, 1, nullptr);
         la.raw_out = c->raw + (size_t)t * c->V;
-        CUDA_TRY(launch_logits(la, c->n_parts, c->stream, true));
+        CUDA_TRY(run_logits(c, la, true));
     }
     CUDA_TRY(cudaMemcpyAsync(out_logits, c->raw, (size_t)n * c->V * 4, cudaMemcpyDeviceToHost, c->stream));
     CUDA_TRY(cudaStreamSynchronize(c->stream));
@@ -887,7 +916,7 @@ static int run_prompt(w4j_ctx *c, const CallArgs &a, const CallLayout &Ly, int m
             la.ns_part = c->ns_part;
             la.ns_value = c->ns_value;
         }
-        CUDA_TRY(launch_logits(la, c->n_parts, c->stream, !last));
+        CUDA_TRY(run_logits(c, la, !last));
         ++launches;
         if (ns_here) {
             CUDA_TRY(launch_nsp(st, c->ns_part, c->n_parts, c->ns_value, c->stream, true));
@@ -917,13 +946,14 @@ static int enqueue_step(w4j_ctx *c, const CallArgs &a, const CallLayout &Ly, int
     pa.nq = B;
     pa.cross_stream = c->d_int_area + Ly.cross;
     pa.group_active = B == 1 ? st.active : nullptr;
+    pa.self_prefetch = 1;  // each step is its own graph launch: older rows are complete
     TRY(run_layers(c, pa, launches));
     LogitsArgs la = logits_args(c, M, st.active);
     la.use_mask = 1;
     la.mask = mask_args(c);
     la.topk = mode == MODE_BEAM ? B + 1 : 0;
     if (mode == MODE_SAMPLE) la.masked_out = c->masked;
-    CUDA_TRY(launch_logits(la, c->n_parts, c->stream, true));
+    CUDA_TRY(run_logits(c, la, true));
     const int sel = mode == MODE_BEAM ? SEL_BEAM : mode == MODE_SAMPLE ? SEL_SAMPLE : SEL_GREEDY;
     CUDA_TRY(launch_select(st, sel, parity, c->logit_part, c->n_parts, c->masked, 0, c->stream, true));
     launches += 2;
@@ -988,6 +1018,7 @@ static int read_results(w4j_ctx *c, const CallArgs &a, w4j_result *r) {
     CUDA_TRY(cudaMemcpyAsync(nsp.data(), st.nsp, S * 4, cudaMemcpyDeviceToHost, c->stream));
     CUDA_TRY(cudaMemcpyAsync(errw.data(), st.err, 4, cudaMemcpyDeviceToHost, c->stream));
     CUDA_TRY(cudaStreamSynchronize(c->stream));
+    if (errw[0] == 2) return set_err(W4J_ERR_CUDA, "a bounded device wait ran out (copy never completed)");
     if (errw[0]) return set_err(W4J_ERR_STATE, "device bookkeeping overflow (mask list)");
     for (int s = 0; s < S; ++s) {
         const int n = std::min(lens[s], a.max_tokens);
@@ -1024,9 +1055,9 @@ static int decode_impl(w4j_ctx *c, const CallArgs &a, w4j_result *r) {
     const CallLayout Ly = call_layout(c, a.S, a.n_prompt, a.n_sup);
     TRY(prepare_call(c, a, Ly));
     long long launches = 0;
+    CUDA_TRY(cudaEventRecord(c->ev0, c->stream));
     TRY(run_prompt(c, a, Ly, mode, launches));
     // steps 1 .. max_tokens-1 (both loops produce max_tokens decisions in total)
-    CUDA_TRY(cudaEventRecord(c->ev0, c->stream));
     int steps = 0;
     bool cancelled = false;
     bool snapshot_pending = false;
@@ -1054,7 +1085,8 @@ static int decode_impl(w4j_ctx *c, const CallArgs &a, w4j_result *r) {
             snapshot_pending = true;
         }
     }
-    CUDA_TRY(cudaStreamSynchronize(c->stream));  // ev1 must not be re-recorded while pending
+    CUDA_TRY(launch_finalize(c->st, mode == MODE_BEAM, 0, c->stream));
+    ++launches;
     cudaEvent_t stop;
     CUDA_TRY(cudaEventCreate(&stop));
     CUDA_TRY(cudaEventRecord(stop, c->stream));
@@ -1062,8 +1094,6 @@ static int decode_impl(w4j_ctx *c, const CallArgs &a, w4j_result *r) {
     float ms = 0.f;
     cudaEventElapsedTime(&ms, c->ev0, stop);
     cudaEventDestroy(stop);
-    CUDA_TRY(launch_finalize(c->st, mode == MODE_BEAM, 0, c->stream));
-    ++launches;
     TRY(read_results(c, a, r));
     c->last_ms = ms;
     c->last_steps = steps;
@@ -1260,7 +1290,11 @@ extern "C" int w4j_op_logits_argmax(w4j_ctx *c, const float *x, int M, const voi
     la.part = c->logit_part;
     const int P = logits_parts_for(V, c->sm_count);
     cudaStream_t s = stream ? reinterpret_cast<cudaStream_t>(stream) : 0;
-    CUDA_TRY(launch_logits(la, P, s, false));
+    alignas(64) unsigned char map[128];
+    cudaError_t e = cudaErrorNotSupported;
+    if (c->tc_logits && make_tmap_f16_rows(map, E, V, c->d)) e = launch_logits_tc(la, map, P, s, false);
+    if (e == cudaErrorNotSupported) e = launch_logits(la, P, s, false);
+    CUDA_TRY(e);
     CUDA_TRY(launch_argmax_merge(c->logit_part, P, M, out_token, out_logprob, s));
     return W4J_OK;
 }

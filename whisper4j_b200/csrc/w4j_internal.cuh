@@ -60,6 +60,7 @@ struct GemvArgs {
     const int *seq_slot = nullptr;     // [M] physical self-cache slot
     int layer = 0, n_layer = 0, n_head = 0, n_ctx = 0;
     const int *active = nullptr;       // [M] nonzero: row is live (null = all live)
+    int *err = nullptr;                // device error word (bounded waits that ran out)
 };
 
 // ---------------------------------------------------------------------------
@@ -77,6 +78,7 @@ struct AttnArgs {
     const int *table = nullptr;        // self: [groups][n_ctx] slot per position (null: own slot)
     const int *pos = nullptr;          // self: [groups] position of the newest row (kv len = pos+1)
     const int *stream_of_group = nullptr;  // cross: [groups] stream index into the cross cache
+    int self_prefetch = 0;             // self rows before the newest may be staged before the wait
     int nq = 1;                        // queries per group (cross: beams of one stream)
     int groups = 0;
     int nsplit = 1;
@@ -84,6 +86,7 @@ struct AttnArgs {
     unsigned *counters = nullptr;      // [groups][n_head], zero between uses
     float *out = nullptr;              // [groups*nq][d]
     const int *active = nullptr;       // [groups]
+    int *err = nullptr;                // device error word
 };
 
 // ---------------------------------------------------------------------------
@@ -114,6 +117,7 @@ struct LogitsArgs {
     float *ns_part = nullptr;          // [M][gridDim.x][2] unmasked (max, sum)
     float *ns_value = nullptr;         // [M]
     const int *active = nullptr;       // [M]
+    int *err = nullptr;                // device error word
 };
 
 // ---------------------------------------------------------------------------
@@ -167,6 +171,42 @@ __device__ __forceinline__ void prefetch_l2(const void *p, unsigned bytes) {
     asm volatile("cp.async.bulk.prefetch.L2.global [%0], %1;" ::"l"(p), "r"(bytes) : "memory");
 }
 
+// ---- TMA bulk copies into shared memory, completed through an mbarrier ----
+__device__ __forceinline__ unsigned smem_u32(const void *p) { return (unsigned)__cvta_generic_to_shared(p); }
+__device__ __forceinline__ void mbar_init(uint64_t *b, unsigned count) {
+    asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;" ::"r"(smem_u32(b)), "r"(count) : "memory");
+}
+__device__ __forceinline__ void fence_mbar_init() { asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory"); }
+__device__ __forceinline__ void mbar_expect_tx(uint64_t *b, unsigned bytes) {
+    asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(smem_u32(b)), "r"(bytes) : "memory");
+}
+// 1-D bulk copy global -> shared (16-byte aligned addresses, size a multiple of 16)
+__device__ __forceinline__ void bulk_g2s(void *dst, const void *src, unsigned bytes, uint64_t *b) {
+    asm volatile("cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];" ::"r"(
+                     smem_u32(dst)),
+                 "l"(src), "r"(bytes), "r"(smem_u32(b))
+                 : "memory");
+}
+__device__ __forceinline__ bool mbar_test(uint64_t *b, unsigned parity) {
+    unsigned ok;
+    asm volatile(
+        "{\n .reg .pred p;\n mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n selp.u32 %0, 1, 0, p;\n}"
+        : "=r"(ok)
+        : "r"(smem_u32(b)), "r"(parity)
+        : "memory");
+    return ok != 0;
+}
+// Bounded wait for phase `parity` of an mbarrier; on time-out raises the error word and
+// returns false (callers skip their compute, then drain with a second bounded wait).
+__device__ __forceinline__ bool mbar_wait(uint64_t *b, unsigned parity, int *err) {
+    for (long long it = 0; it < (1ll << 22); ++it) {
+        if (mbar_test(b, parity)) return true;
+        if (it > 32) __nanosleep(128);
+    }
+    if (err) atomicExch(err, 2);
+    return false;
+}
+
 __device__ __forceinline__ uint4 ld_nc_v4(const void *p) {
     uint4 r;
     asm volatile("ld.global.nc.L1::no_allocate.v4.u32 {%0,%1,%2,%3}, [%4];"
@@ -186,11 +226,25 @@ __device__ __forceinline__ float warp_max(float v) {
     return v;
 }
 
+// Let `kern` use all the opt-in shared memory the device offers beside its static arrays.
+template <typename Kern>
+inline cudaError_t allow_dynamic_smem(Kern kern) {
+    int dev = 0, optin = 0;
+    cudaGetDevice(&dev);
+    cudaDeviceGetAttribute(&optin, cudaDevAttrMaxSharedMemoryPerBlockOptin, dev);
+    cudaFuncAttributes fa;
+    cudaError_t e = cudaFuncGetAttributes(&fa, reinterpret_cast<const void *>(kern));
+    if (e != cudaSuccess) return e;
+    return cudaFuncSetAttribute(reinterpret_cast<const void *>(kern), cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                optin - (int)fa.sharedSizeBytes);
+}
+
 // ---------------------------------------------------------------------------
 // host launchers (defined in the kernel .cu files)
 // ---------------------------------------------------------------------------
 cudaError_t launch_gemv(const GemvArgs &a, cudaStream_t s, bool pdl);
 cudaError_t launch_attn(const AttnArgs &a, cudaStream_t s, bool pdl);
+int attn_max_splits(int nq);  // splits whose partials fit the combine's shared-memory staging
 cudaError_t launch_logits(const LogitsArgs &a, int n_parts, cudaStream_t s, bool pdl);
 int logits_parts_for(int V, int sm_count);
 size_t logits_smem_bytes(int M, int V, int d, int n_parts);
@@ -211,6 +265,11 @@ cudaError_t launch_cross_kv(const float *xa, int A, int d, const DMat &wk, const
 
 cudaError_t launch_q8_repack(const void *src, int N, int K, int8_t *q, __half *scales, cudaStream_t s);
 cudaError_t gemv_prepare();
+cudaError_t logits_tc_prepare();
+// tcgen05 vocabulary logits (f16 embedding, M <= 32); cudaErrorNotSupported outside its range
+cudaError_t launch_logits_tc(const LogitsArgs &a, const void *tmap, int n_parts, cudaStream_t s, bool pdl);
+bool make_tmap_f16_rows(void *map_out, const void *base, int rows, int cols);  // 128-byte map
+cudaError_t select_prepare();
 cudaError_t launch_f32_to_f16(const float *src, __half *dst, size_t n, cudaStream_t s);
 
 }  // namespace w4j
