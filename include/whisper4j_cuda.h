@@ -183,6 +183,43 @@ int w4j_q8_0_repack(const void *src_device, int N, int K, void *dst_device, void
 int w4j_op_logits_argmax(w4j_ctx *ctx, const float *x, int M, const void *E, int V, const float *ln_g,
                          const float *ln_b, int32_t *out_token, double *out_logprob, void *stream);
 
+/*
+ * w4j_op_logits_argmax_noalloc — no counterpart in the reference.
+ *
+ * The computation of w4j_op_logits_argmax (same kernels, same results) for callers that
+ * cannot let the library allocate device memory: a host that has handed the whole device to
+ * its own arena or caching allocator (so a cudaMalloc would fail or fragment it), a process
+ * under a fixed device-memory budget, or code that only needs this one op and holds no
+ * decoder context (creating one allocates the weights, caches and scratch of a whole model).
+ * It takes no context and never calls cudaMalloc, cudaFree or an allocating library routine.
+ *
+ * Scratch: the per-block partial results live in a file-scope device array of the library
+ * (W4J_NOALLOC_MAX_ROWS x W4J_NOALLOC_MAX_PARTS records of 144 bytes = 360 KiB per device),
+ * found with cudaGetSymbolAddress on the first call for each device.  That first call also
+ * sets kernel attributes; make it before any stream capture begins on that device.
+ * Nothing in the partials has to start at zero (each call writes every record it reads).
+ * One device error word must be zero when a call starts: it is zero when the library loads,
+ * and each call clears it at the end.
+ *
+ * Limits: 1 <= M <= W4J_NOALLOC_MAX_ROWS; d a multiple of 64 in [64, 1280]; x, E, ln_g and
+ * ln_b 16-byte aligned; min(SM count, V) <= W4J_NOALLOC_MAX_PARTS.  Outside them the call
+ * returns W4J_ERR_ARG with the reason in w4j_last_error() and launches nothing.
+ *
+ * Concurrency: calls on one device share the scratch.  Two calls whose executions overlap on
+ * the device (different streams without an event between them, or different host threads)
+ * race and return wrong ids; order them on one stream, or with events.
+ *
+ * device: the GPU holding every pointer (made current on the calling thread).  x: M x d f32,
+ * E: V x d f16, ln_g/ln_b: d f32; out_token (M int32) and out_logprob (M double) on the device.
+ * If a bounded wait inside the kernels ran out, every out_token of that call is -1 and every
+ * out_logprob NaN.  Asynchronous on `stream` (NULL = legacy default stream).
+ */
+#define W4J_NOALLOC_MAX_ROWS 16
+#define W4J_NOALLOC_MAX_PARTS 160
+int w4j_op_logits_argmax_noalloc(int device, const float *x, int M, int d, const void *E, int V,
+                                 const float *ln_g, const float *ln_b, int32_t *out_token, double *out_logprob,
+                                 void *stream);
+
 #ifdef __cplusplus
 }
 #endif

@@ -74,6 +74,7 @@ SIGNATURES = {
     "w4j_op_linear": (_I, [_P, _P, _I, _I, _P, _I, _I, _P, _P, _P, _I, _P, _P]),
     "w4j_q8_0_repack": (_I, [_P, _I, _I, _P, _P]),
     "w4j_op_logits_argmax": (_I, [_P, _P, _I, _P, _I, _P, _P, _P, _P, _P]),
+    "w4j_op_logits_argmax_noalloc": (_I, [_I, _P, _I, _I, _P, _I, _P, _P, _P, _P, _P]),
 }
 
 _lib = None

@@ -735,6 +735,31 @@ __global__ void k_argmax_merge(const float *part, int P, int32_t *tok, double *l
     }
 }
 
+// One block, one warp per row: the same merge as k_argmax_merge, then the device error word.
+// If a bounded wait of the logits kernel ran out, every row reports token -1 and a NaN
+// log-probability, and the word is cleared so that the next call starts from zero.
+__global__ void k_argmax_merge_status(const float *part, int P, int M, int32_t *tok, double *lp, int *err) {
+    extern __shared__ __align__(16) float sel_smem[];
+    const int warp = threadIdx.x >> 5;
+    if (warp < M) {
+        float *stg = sel_smem + (size_t)warp * P * 4;
+        stage_partials(part + (size_t)warp * P * kPartStride, P, 0, stg);
+        const Merged mg = merge_partials(stg, P, 4);
+        if ((threadIdx.x & 31) == 0) {
+            tok[warp] = mg.argmax;
+            lp[warp] = (double)(mg.max - mg.max) - log(mg.sum);
+        }
+    }
+    __syncthreads();
+    if (threadIdx.x == 0 && *err != 0) {
+        for (int m = 0; m < M; ++m) {
+            tok[m] = -1;
+            lp[m] = __longlong_as_double(0x7ff8000000000000ll);
+        }
+        *err = 0;
+    }
+}
+
 // ---------------------------------------------------------------------------
 static cudaLaunchConfig_t cfg_for(dim3 grid, dim3 block, cudaStream_t s, bool pdl, cudaLaunchAttribute *attr) {
     cudaLaunchConfig_t cfg = {};
@@ -803,6 +828,14 @@ cudaError_t launch_finalize(const DecodeState &st, int beam_mode, int parity, cu
 
 cudaError_t launch_argmax_merge(const float *part, int n_parts, int M, int32_t *tok, double *lp, cudaStream_t s) {
     k_argmax_merge<<<M, kSelThreads, (size_t)n_parts * 4 * 4, s>>>(part, n_parts, tok, lp);
+    return cudaGetLastError();
+}
+
+// M <= 32 rows in one block; shared memory M * n_parts * 16 bytes (the caller bounds it).
+cudaError_t launch_argmax_merge_status(const float *part, int n_parts, int M, int32_t *tok, double *lp, int *err,
+                                       cudaStream_t s) {
+    if (M < 1 || M > 32) return cudaErrorInvalidValue;
+    k_argmax_merge_status<<<1, 32 * M, (size_t)M * n_parts * 4 * 4, s>>>(part, n_parts, M, tok, lp, err);
     return cudaGetLastError();
 }
 

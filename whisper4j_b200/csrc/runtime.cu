@@ -15,6 +15,7 @@
 #include <cstdio>
 #include <cstdlib>
 #include <cstring>
+#include <functional>
 #include <map>
 #include <mutex>
 #include <set>
@@ -1296,5 +1297,96 @@ extern "C" int w4j_op_logits_argmax(w4j_ctx *c, const float *x, int M, const voi
     if (e == cudaErrorNotSupported) e = launch_logits(la, P, s, false);
     CUDA_TRY(e);
     CUDA_TRY(launch_argmax_merge(c->logit_part, P, M, out_token, out_logprob, s));
+    return W4J_OK;
+}
+
+// ---------------------------------------------------------------------------
+// w4j_op_logits_argmax_noalloc: the same vocabulary pass with no context and no allocation.
+// The per-block partials and the device error word live in file-scope device arrays, one copy
+// per device, whose addresses are looked up once per device.
+// ---------------------------------------------------------------------------
+static __device__ __align__(256) float g_noalloc_part[W4J_NOALLOC_MAX_ROWS * W4J_NOALLOC_MAX_PARTS * kPartStride];
+static __device__ __align__(256) int g_noalloc_err;  // zero at load; cleared by every call's merge
+
+namespace {
+constexpr int kNoAllocMaxDevices = 64;
+struct NoAllocDevice {
+    std::once_flag once;
+    int rc = W4J_OK;
+    std::string msg;
+    float *part = nullptr;
+    int *err = nullptr;
+    int sms = 0;
+};
+NoAllocDevice g_noalloc_dev[kNoAllocMaxDevices];
+
+// Called once per device: kernel attributes, the SM count and the two symbol addresses.
+void noalloc_setup(int device, NoAllocDevice &nd) {
+    auto fail = [&](cudaError_t e, const char *what) {
+        nd.rc = W4J_ERR_CUDA;
+        nd.msg = std::string("w4j_op_logits_argmax_noalloc set-up on device ") + std::to_string(device) + ": " +
+                 what + ": " + cudaGetErrorString(e);
+    };
+    cudaError_t e;
+    if ((e = gemv_prepare()) != cudaSuccess) return fail(e, "kernel attributes");
+    if ((e = logits_tc_prepare()) != cudaSuccess) return fail(e, "kernel attributes");
+    if ((e = cudaDeviceGetAttribute(&nd.sms, cudaDevAttrMultiProcessorCount, device)) != cudaSuccess)
+        return fail(e, "cudaDeviceGetAttribute");
+    if ((e = cudaGetSymbolAddress(reinterpret_cast<void **>(&nd.part), g_noalloc_part)) != cudaSuccess)
+        return fail(e, "cudaGetSymbolAddress(partials)");
+    if ((e = cudaGetSymbolAddress(reinterpret_cast<void **>(&nd.err), g_noalloc_err)) != cudaSuccess)
+        return fail(e, "cudaGetSymbolAddress(error word)");
+}
+}  // namespace
+
+extern "C" int w4j_op_logits_argmax_noalloc(int device, const float *x, int M, int d, const void *E, int V,
+                                            const float *ln_g, const float *ln_b, int32_t *out_token,
+                                            double *out_logprob, void *stream) {
+    if (!x || !E || !ln_g || !ln_b || !out_token || !out_logprob)
+        return set_err(W4J_ERR_ARG, "w4j_op_logits_argmax_noalloc: null argument");
+    if (M < 1 || M > W4J_NOALLOC_MAX_ROWS)
+        return set_err(W4J_ERR_ARG,
+                       "w4j_op_logits_argmax_noalloc: M = %d rows is outside [1, %d], the size of its static "
+                       "scratch; use w4j_op_logits_argmax with a context for more rows",
+                       M, W4J_NOALLOC_MAX_ROWS);
+    if (d < 64 || d > 1280 || d % 64 != 0)
+        return set_err(W4J_ERR_ARG, "w4j_op_logits_argmax_noalloc: d = %d must be a multiple of 64 in [64, 1280]", d);
+    if (V < 1) return set_err(W4J_ERR_ARG, "w4j_op_logits_argmax_noalloc: V = %d must be positive", V);
+    const uintptr_t align = reinterpret_cast<uintptr_t>(x) | reinterpret_cast<uintptr_t>(E) |
+                            reinterpret_cast<uintptr_t>(ln_g) | reinterpret_cast<uintptr_t>(ln_b);
+    if (align & 15) return set_err(W4J_ERR_ARG, "w4j_op_logits_argmax_noalloc: x, E, ln_g and ln_b must be 16-byte aligned");
+    int ndev = 0;
+    if (cudaGetDeviceCount(&ndev) != cudaSuccess || ndev == 0)
+        return set_err(W4J_ERR_CUDA, "w4j_op_logits_argmax_noalloc: no CUDA device available");
+    if (device < 0 || device >= ndev || device >= kNoAllocMaxDevices)
+        return set_err(W4J_ERR_ARG, "w4j_op_logits_argmax_noalloc: device %d out of range", device);
+    CUDA_TRY(cudaSetDevice(device));
+    NoAllocDevice &nd = g_noalloc_dev[device];
+    std::call_once(nd.once, noalloc_setup, device, std::ref(nd));
+    if (nd.rc != W4J_OK) return set_err(nd.rc, "%s", nd.msg.c_str());
+    const int P = logits_parts_for(V, nd.sms);
+    if (P > W4J_NOALLOC_MAX_PARTS)
+        return set_err(W4J_ERR_ARG, "w4j_op_logits_argmax_noalloc: %d vocabulary blocks exceed the static scratch (%d)", P,
+                       W4J_NOALLOC_MAX_PARTS);
+    LogitsArgs la;
+    la.E.type = WT_F16;
+    la.E.N = V;
+    la.E.K = d;
+    la.E.h = reinterpret_cast<const __half *>(E);
+    la.x = x;
+    la.ln_g = ln_g;
+    la.ln_b = ln_b;
+    la.M = M;
+    la.V = V;
+    la.d = d;
+    la.part = nd.part;
+    la.err = nd.err;
+    cudaStream_t s = stream ? reinterpret_cast<cudaStream_t>(stream) : 0;
+    alignas(64) unsigned char map[128];
+    cudaError_t e = cudaErrorNotSupported;
+    if (make_tmap_f16_rows(map, E, V, d)) e = launch_logits_tc(la, map, P, s, false);
+    if (e == cudaErrorNotSupported) e = launch_logits(la, P, s, false);
+    CUDA_TRY(e);
+    CUDA_TRY(launch_argmax_merge_status(nd.part, P, M, out_token, out_logprob, nd.err, s));
     return W4J_OK;
 }

@@ -258,6 +258,9 @@ cudaError_t launch_nsp(const DecodeState &st, const float *ns_part, int n_parts,
 cudaError_t launch_init_masks(const DecodeState &st, int beam_mode, cudaStream_t s);
 cudaError_t launch_finalize(const DecodeState &st, int beam_mode, int parity, cudaStream_t s);
 cudaError_t launch_argmax_merge(const float *part, int n_parts, int M, int32_t *tok, double *lp, cudaStream_t s);
+// single-block merge that also reports and clears the device error word `err`
+cudaError_t launch_argmax_merge_status(const float *part, int n_parts, int M, int32_t *tok, double *lp, int *err,
+                                       cudaStream_t s);
 
 // prefill: out_k/out_v (f16 head-major) = xa . Wk^T, xa . Wv^T + bv
 cudaError_t launch_cross_kv(const float *xa, int A, int d, const DMat &wk, const DMat &wv, const float *bk,
