@@ -367,10 +367,14 @@ def main():
     ap.add_argument("--config", default=DEFAULT_CONFIG, choices=sorted(CONFIGS))
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--max-tokens", type=int, default=0,
+                    help="override the config's forced length (short profiling cases; reported in config)")
     args = ap.parse_args()
     if args.warmup < 3:
         args.warmup = 3
-    cfg = CONFIGS[args.config]
+    cfg = dict(CONFIGS[args.config])
+    if args.max_tokens > 0:
+        cfg["max_tokens"] = args.max_tokens
     dims = ggml.ARCHS[cfg["arch"]]
     world = int(os.environ.get("WORLD_SIZE", "1"))
     rank = int(os.environ.get("RANK", "0"))

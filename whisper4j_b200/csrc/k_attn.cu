@@ -21,6 +21,7 @@ namespace w4j {
 
 constexpr int kRowPad = 72;  // halves per shared K/V row (144 B: conflict-free 16-byte reads)
 constexpr int kMaxNq = 8;
+constexpr int kWarps = kAttnThreads / 32;
 
 __device__ __forceinline__ void cp_async16(void *smem, const void *gmem) {
     const unsigned s = (unsigned)__cvta_generic_to_shared(smem);
@@ -28,20 +29,21 @@ __device__ __forceinline__ void cp_async16(void *smem, const void *gmem) {
 }
 __device__ __forceinline__ void cp_async_wait_all() { asm volatile("cp.async.wait_all;" ::: "memory"); }
 
+// NQ queries per group (self-attention: 1; cross-attention: the beams of one stream).
+template <int NQ>
 __global__ void __launch_bounds__(kAttnThreads) k_attn(AttnArgs a) {
-    __shared__ __align__(16) __half skv[2 * kAttnKeyTile * kRowPad];  // K tile, V tile; combine staging
+    __shared__ __align__(16) __half skv[2 * kAttnKeyTile * kRowPad];  // K tile, V tile; reduction and combine staging
     __half *sk = skv, *sv = skv + kAttnKeyTile * kRowPad;
-    __shared__ __align__(16) float sq[kMaxNq][kHeadDim];
-    __shared__ float sp[kMaxNq][kAttnKeyTile];
-    __shared__ float s_m[kMaxNq], s_l[kMaxNq], s_alpha[kMaxNq];
+    __shared__ __align__(16) float sq[NQ][kHeadDim];
+    __shared__ float sp[NQ][kAttnKeyTile];
+    __shared__ float s_m[NQ], s_l[NQ], s_alpha[NQ];
     __shared__ int s_last;
 
     const int split = blockIdx.x, head = blockIdx.y, group = blockIdx.z;
     const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
-    const int nq = a.nq;
 
     // Positions, beam tables and liveness were written by the host or by an earlier graph
-    // launch, never by the kernel this one waits on, so they are read before the wait.
+    // launch, never by a kernel of this launch's chain, so they are read before the wait.
     const bool live = !a.active || a.active[group];
     const __half *kbase = nullptr, *vbase = nullptr;
     if (a.cross) {
@@ -52,7 +54,11 @@ __global__ void __launch_bounds__(kAttnThreads) k_attn(AttnArgs a) {
     }
     const int len = a.cross ? a.n_audio : a.pos[group] + 1;
     const int newest = a.cross ? -1 : len - 1;  // the row the previous kernel (QKV) writes
-    const int j0 = (int)(((long long)split * len) / a.nsplit), j1 = (int)(((long long)(split + 1) * len) / a.nsplit);
+    // splits in use: one key tile each while the context is short (the grid is sized for the
+    // longest context); blocks past them have nothing to do
+    const int ns = a.cross ? a.nsplit : min(a.nsplit, max(1, (len + kAttnKeyTile - 1) / kAttnKeyTile));
+    if (split >= ns) return;
+    const int j0 = (int)(((long long)split * len) / ns), j1 = (int)(((long long)(split + 1) * len) / ns);
     const float scale = 0.125f;  // (float)(1 / sqrt(64))
 
     // stage K and V rows [t0, t0 + nk) (128 B each = 8 x 16 B); which: 0 all, 1 all but the
@@ -87,81 +93,70 @@ __global__ void __launch_bounds__(kAttnThreads) k_attn(AttnArgs a) {
         cp_async_wait_all();
         return;
     }
-
-    {  // queries: all loads issued before any is used
-        constexpr int kQ = kMaxNq * kHeadDim / kAttnThreads;
-        float qv[kQ];
-#pragma unroll
-        for (int t = 0; t < kQ; ++t) {
-            const int i = tid + kAttnThreads * t;
-            qv[t] = i < nq * kHeadDim
-                        ? a.q[(size_t)(group * nq + i / kHeadDim) * a.d + head * kHeadDim + i % kHeadDim]
-                        : 0.f;
-        }
-#pragma unroll
-        for (int t = 0; t < kQ; ++t) {
-            const int i = tid + kAttnThreads * t;
-            if (i < nq * kHeadDim) sq[i / kHeadDim][i % kHeadDim] = qv[t];
-        }
+    // the newest self row (written by the previous kernel) streams in with the queries
+    if (pre && !a.cross) stage(j0, min(kAttnKeyTile, j1 - j0), 2);
+    if (tid < NQ * kHeadDim / 4) {  // queries: one 16-byte load per thread
+        const int i = tid / (kHeadDim / 4), c = tid % (kHeadDim / 4);
+        reinterpret_cast<float4 *>(sq[i])[c] =
+            reinterpret_cast<const float4 *>(a.q + (size_t)(group * NQ + i) * a.d + head * kHeadDim)[c];
     }
-    if (tid < kMaxNq) {
+    if (tid < NQ) {
         s_m[tid] = -INFINITY;
         s_l[tid] = 0.f;
     }
-    // output accumulators: warp w sums the keys j = w (mod 4) of every tile for dims
-    // 2*lane, 2*lane+1 of every query; the four warp shares are added at the end
-    float ow[kMaxNq][2];
+    // output accumulators: warp w sums the keys j = w (mod kWarps) of every tile for dims
+    // 2*lane, 2*lane+1 of every query; the warp shares are added at the end
+    float ow[NQ][2];
 #pragma unroll
-    for (int i = 0; i < kMaxNq; ++i) ow[i][0] = ow[i][1] = 0.f;
-    constexpr int kPairsPerThread = kMaxNq * kHeadDim / kAttnThreads;
+    for (int i = 0; i < NQ; ++i) ow[i][0] = ow[i][1] = 0.f;
     __syncthreads();
 
     for (int t0 = j0; t0 < j1; t0 += kAttnKeyTile) {
         const int nk = min(kAttnKeyTile, j1 - t0);
-        if (t0 == j0 && pre) {
-            if (!a.cross) stage(t0, nk, 2);  // the newest row, now written
-        } else {
-            stage(t0, nk, 0);
-        }
+        if (t0 != j0 || !pre) stage(t0, nk, 0);
         cp_async_wait_all();
         __syncthreads();
-        // scores: thread per key
-        if (tid < nk) {
-            float kf[kHeadDim];
+        {  // scores: two threads per key, 32 dims each
+            const int key = tid >> 1, hf = tid & 1;
+            float acc[NQ];
 #pragma unroll
-            for (int c = 0; c < 8; ++c) {
-                const uint4 u = *reinterpret_cast<const uint4 *>(&sk[tid * kRowPad + c * 8]);
-                const __half2 *h = reinterpret_cast<const __half2 *>(&u);
+            for (int i = 0; i < NQ; ++i) acc[i] = 0.f;
+            if (key < nk) {
 #pragma unroll
-                for (int j = 0; j < 4; ++j) {
-                    const float2 f = __half22float2(h[j]);
-                    kf[c * 8 + 2 * j] = f.x;
-                    kf[c * 8 + 2 * j + 1] = f.y;
-                }
-            }
-            float acc[kMaxNq];
+                for (int c = 0; c < 4; ++c) {
+                    const uint4 u = *reinterpret_cast<const uint4 *>(&sk[key * kRowPad + hf * 32 + c * 8]);
+                    const __half2 *h = reinterpret_cast<const __half2 *>(&u);
+                    float kf[8];
 #pragma unroll
-            for (int i = 0; i < kMaxNq; ++i) acc[i] = 0.f;
+                    for (int j = 0; j < 4; ++j) {
+                        const float2 f = __half22float2(h[j]);
+                        kf[2 * j] = f.x;
+                        kf[2 * j + 1] = f.y;
+                    }
 #pragma unroll
-            for (int dd = 0; dd < kHeadDim; dd += 4) {
-#pragma unroll
-                for (int i = 0; i < kMaxNq; ++i) {
-                    if (i < nq) {  // independent chains per query
-                        const float4 q4 = *reinterpret_cast<const float4 *>(&sq[i][dd]);
-                        acc[i] = fmaf(q4.x, kf[dd], acc[i]);
-                        acc[i] = fmaf(q4.y, kf[dd + 1], acc[i]);
-                        acc[i] = fmaf(q4.z, kf[dd + 2], acc[i]);
-                        acc[i] = fmaf(q4.w, kf[dd + 3], acc[i]);
+                    for (int i = 0; i < NQ; ++i) {
+                        const float4 q0 = *reinterpret_cast<const float4 *>(&sq[i][hf * 32 + c * 8]);
+                        const float4 q1 = *reinterpret_cast<const float4 *>(&sq[i][hf * 32 + c * 8 + 4]);
+                        acc[i] = fmaf(q0.x, kf[0], acc[i]);
+                        acc[i] = fmaf(q0.y, kf[1], acc[i]);
+                        acc[i] = fmaf(q0.z, kf[2], acc[i]);
+                        acc[i] = fmaf(q0.w, kf[3], acc[i]);
+                        acc[i] = fmaf(q1.x, kf[4], acc[i]);
+                        acc[i] = fmaf(q1.y, kf[5], acc[i]);
+                        acc[i] = fmaf(q1.z, kf[6], acc[i]);
+                        acc[i] = fmaf(q1.w, kf[7], acc[i]);
                     }
                 }
             }
 #pragma unroll
-            for (int i = 0; i < kMaxNq; ++i)
-                if (i < nq) sp[i][tid] = acc[i] * scale;
+            for (int i = 0; i < NQ; ++i) acc[i] += __shfl_xor_sync(0xffffffffu, acc[i], 1);
+            if (key < nk && hf == 0)
+#pragma unroll
+                for (int i = 0; i < NQ; ++i) sp[i][key] = acc[i] * scale;
         }
         __syncthreads();
-        // online softmax bookkeeping: warp w takes queries w, w+4
-        for (int i = warp; i < nq; i += kAttnThreads / 32) {
+        // online softmax bookkeeping: warp i takes query i
+        for (int i = warp; i < NQ; i += kWarps) {
             float mx = -INFINITY;
             for (int j = lane; j < nk; j += 32) mx = fmaxf(mx, sp[i][j]);
             mx = warp_max(mx);
@@ -184,63 +179,58 @@ __global__ void __launch_bounds__(kAttnThreads) k_attn(AttnArgs a) {
         __syncthreads();
         // o = o * alpha + p . V  (this warp's keys, two dims per lane)
 #pragma unroll
-        for (int i = 0; i < kMaxNq; ++i) {
-            const float al = i < nq ? s_alpha[i] : 0.f;
+        for (int i = 0; i < NQ; ++i) {
+            const float al = s_alpha[i];
             ow[i][0] *= al;
             ow[i][1] *= al;
         }
-        for (int j = warp; j < nk; j += kAttnThreads / 32) {
+        for (int j = warp; j < nk; j += kWarps) {
             const float2 v = __half22float2(*reinterpret_cast<const __half2 *>(&sv[j * kRowPad + 2 * lane]));
 #pragma unroll
-            for (int i = 0; i < kMaxNq; ++i) {
-                if (i < nq) {
-                    const float p = sp[i][j];
-                    ow[i][0] = fmaf(p, v.x, ow[i][0]);
-                    ow[i][1] = fmaf(p, v.y, ow[i][1]);
-                }
+            for (int i = 0; i < NQ; ++i) {
+                const float p = sp[i][j];
+                ow[i][0] = fmaf(p, v.x, ow[i][0]);
+                ow[i][1] = fmaf(p, v.y, ow[i][1]);
             }
         }
         __syncthreads();
     }
-    // add the four warp shares (through the K tile's shared memory, no longer needed)
-    float *red = reinterpret_cast<float *>(sk);  // [4][kMaxNq][64]
+    // add the warp shares (through the K/V tiles' shared memory, no longer needed)
+    float *red = reinterpret_cast<float *>(skv);  // [kWarps][NQ][64]
 #pragma unroll
-    for (int i = 0; i < kMaxNq; ++i) {
-        if (i < nq) {
-            red[((size_t)warp * kMaxNq + i) * kHeadDim + 2 * lane] = ow[i][0];
-            red[((size_t)warp * kMaxNq + i) * kHeadDim + 2 * lane + 1] = ow[i][1];
-        }
-    }
+    for (int i = 0; i < NQ; ++i)
+        *reinterpret_cast<float2 *>(&red[((size_t)warp * NQ + i) * kHeadDim + 2 * lane]) = make_float2(ow[i][0], ow[i][1]);
     __syncthreads();
-    float o[kPairsPerThread];
+    constexpr int kPer = (NQ * kHeadDim + kAttnThreads - 1) / kAttnThreads;  // (query, dim) pairs per thread
+    float o[kPer];
 #pragma unroll
-    for (int t = 0; t < kPairsPerThread; ++t) {
+    for (int t = 0; t < kPer; ++t) {
         const int pidx = tid + kAttnThreads * t;
-        const int i = pidx / kHeadDim, dd = pidx % kHeadDim;
         o[t] = 0.f;
-        if (i < nq)
+        if (pidx < NQ * kHeadDim)
 #pragma unroll
-            for (int w = 0; w < kAttnThreads / 32; ++w) o[t] += red[((size_t)w * kMaxNq + i) * kHeadDim + dd];
+            for (int w = 0; w < kWarps; ++w) o[t] += red[(size_t)w * NQ * kHeadDim + pidx];
     }
-    __syncthreads();  // `red` aliases the staging area used by the combine below
-
-    if (a.nsplit == 1) {
+    if (ns == 1) {
 #pragma unroll
-        for (int t = 0; t < kPairsPerThread; ++t) {
+        for (int t = 0; t < kPer; ++t) {
             const int pidx = tid + kAttnThreads * t;
             const int i = pidx / kHeadDim, dd = pidx % kHeadDim;
-            if (i < nq) a.out[(size_t)(group * nq + i) * a.d + head * kHeadDim + dd] = o[t] / s_l[i];
+            if (pidx < NQ * kHeadDim) a.out[(size_t)(group * NQ + i) * a.d + head * kHeadDim + dd] = o[t] / s_l[i];
         }
         return;
     }
-    // partial (m, l, o[64]) of this split
+    // partial record (m, l, o[64], pad) of this split
+    auto rec = [&](int i, int sp_) {
+        return a.part + ((((size_t)(group * NQ + i)) * a.n_head + head) * a.nsplit + sp_) * kAttnRec;
+    };
 #pragma unroll
-    for (int t = 0; t < kPairsPerThread; ++t) {
+    for (int t = 0; t < kPer; ++t) {
         const int pidx = tid + kAttnThreads * t;
         const int i = pidx / kHeadDim, dd = pidx % kHeadDim;
-        if (i < nq) {
-            float *pp = a.part + ((((size_t)(group * nq + i)) * a.n_head + head) * a.nsplit + split) * (2 + kHeadDim);
-            pp[2 + dd] = o[t];
+        if (pidx < NQ * kHeadDim) {
+            float *pp = rec(i, split);
+            pp[4 + dd] = o[t];
             if (dd == 0) {
                 pp[0] = s_m[i];
                 pp[1] = s_l[i];
@@ -252,48 +242,85 @@ __global__ void __launch_bounds__(kAttnThreads) k_attn(AttnArgs a) {
     if (tid == 0) {
         unsigned *ctr = a.counters + (size_t)group * a.n_head + head;
         const unsigned prev = atomicAdd(ctr, 1u);
-        s_last = prev == (unsigned)(a.nsplit - 1);
+        s_last = prev == (unsigned)(ns - 1);
         if (s_last) *ctr = 0u;  // ready for the next use of the counter
     }
     __syncthreads();
     if (!s_last) return;
     __threadfence();
-    // stage every split's partial of this (group, head) in shared memory with one round of
-    // independent L2 loads, then combine in split order
-    constexpr int per = 2 + kHeadDim;
-    float *stg = reinterpret_cast<float *>(skv);
-    const int span = a.nsplit * per;
-    for (int e = tid; e < nq * span; e += kAttnThreads) {
-        const int i = e / span, rest = e - i * span;
-        stg[e] = __ldcg(a.part + ((((size_t)(group * nq + i)) * a.n_head + head) * a.nsplit) * per + rest);
+    // every split's record of this (group, head): one round of independent 16-byte L2 loads
+    float *stg = reinterpret_cast<float *>(skv);  // [NQ][ns][kAttnRec]
+    constexpr int kR4 = kAttnRec / 4;
+    const int n4 = ns * kR4;
+    for (int e0 = tid; e0 < n4; e0 += kAttnThreads * 2) {
+        float4 v[NQ][2];
+#pragma unroll
+        for (int i = 0; i < NQ; ++i)
+#pragma unroll
+            for (int j = 0; j < 2; ++j) {
+                const int e = e0 + kAttnThreads * j;
+                if (e < n4) v[i][j] = __ldcg(reinterpret_cast<const float4 *>(rec(i, 0)) + e);
+            }
+#pragma unroll
+        for (int i = 0; i < NQ; ++i)
+#pragma unroll
+            for (int j = 0; j < 2; ++j) {
+                const int e = e0 + kAttnThreads * j;
+                if (e < n4) reinterpret_cast<float4 *>(stg + (size_t)i * ns * kAttnRec)[e] = v[i][j];
+            }
+    }
+    __syncthreads();
+    // per query: the split weights exp(m_s - M) (in split order) and the denominator, once
+    float *wts = stg + (size_t)NQ * ns * kAttnRec;  // [NQ][ns + 1]
+    for (int i = warp; i < NQ; i += kWarps) {
+        const float *base = stg + (size_t)i * ns * kAttnRec;
+        float M = -INFINITY;
+        for (int s2 = lane; s2 < ns; s2 += 32) M = fmaxf(M, base[s2 * kAttnRec]);
+        M = warp_max(M);
+        float den = 0.f;
+        for (int s2 = lane; s2 < ns; s2 += 32) {
+            const float ms = base[s2 * kAttnRec];
+            const float w = ms == -INFINITY ? 0.f : __expf(ms - M);
+            wts[i * (ns + 1) + s2] = w;
+            den = fmaf(w, base[s2 * kAttnRec + 1], den);
+        }
+        den = warp_sum(den);
+        if (lane == 0) wts[i * (ns + 1) + ns] = den;
     }
     __syncthreads();
 #pragma unroll
-    for (int t = 0; t < kPairsPerThread; ++t) {
+    for (int t = 0; t < kPer; ++t) {
         const int pidx = tid + kAttnThreads * t;
         const int i = pidx / kHeadDim, dd = pidx % kHeadDim;
-        if (i >= nq) continue;
-        const float *base = stg + (size_t)i * span;
-        float M = -INFINITY;
-        for (int s = 0; s < a.nsplit; ++s) M = fmaxf(M, base[s * per]);
-        float num = 0.f, den = 0.f;
-        for (int s = 0; s < a.nsplit; ++s) {
-            const float *pp = base + s * per;
-            const float ms = pp[0];
-            if (ms == -INFINITY) continue;
-            const float w = __expf(ms - M);
-            num = fmaf(w, pp[2 + dd], num);
-            den = fmaf(w, pp[1], den);
-        }
-        a.out[(size_t)(group * nq + i) * a.d + head * kHeadDim + dd] = num / den;
+        if (pidx >= NQ * kHeadDim) continue;
+        const float *base = stg + (size_t)i * ns * kAttnRec;
+        const float *w = wts + i * (ns + 1);
+        float num = 0.f;
+        for (int s2 = 0; s2 < ns; ++s2) num = fmaf(w[s2], base[s2 * kAttnRec + 4 + dd], num);
+        a.out[(size_t)(group * NQ + i) * a.d + head * kHeadDim + dd] = num / w[ns];
     }
 }
 
-int attn_max_splits(int nq) { return (2 * kAttnKeyTile * kRowPad * 2 / 4) / ((2 + kHeadDim) * nq); }
+cudaError_t attn_prepare() {
+    cudaError_t e = prefer_max_smem(k_attn<1>);
+    if (e == cudaSuccess) e = prefer_max_smem(k_attn<2>);
+    if (e == cudaSuccess) e = prefer_max_smem(k_attn<3>);
+    if (e == cudaSuccess) e = prefer_max_smem(k_attn<4>);
+    if (e == cudaSuccess) e = prefer_max_smem(k_attn<5>);
+    if (e == cudaSuccess) e = prefer_max_smem(k_attn<6>);
+    if (e == cudaSuccess) e = prefer_max_smem(k_attn<7>);
+    if (e == cudaSuccess) e = prefer_max_smem(k_attn<8>);
+    return e;
+}
+
+// Splits whose records (and the per-query weights) fit the combine's staging in the K/V tiles.
+int attn_max_splits(int nq) {
+    return (int)((2 * kAttnKeyTile * kRowPad * sizeof(__half) / sizeof(float)) / (nq * (kAttnRec + 1) + 1));
+}
 
 cudaError_t launch_attn(const AttnArgs &a, cudaStream_t s, bool pdl) {
     if (a.groups <= 0) return cudaSuccess;
-    if (a.nq < 1 || a.nq > kMaxNq) return cudaErrorInvalidValue;
+    if (a.nq < 1 || a.nq > kMaxNq || a.nsplit > attn_max_splits(a.nq)) return cudaErrorInvalidValue;
     cudaLaunchConfig_t cfg = {};
     cfg.gridDim = dim3(a.nsplit, a.n_head, a.groups);
     cfg.blockDim = dim3(kAttnThreads);
@@ -304,7 +331,16 @@ cudaError_t launch_attn(const AttnArgs &a, cudaStream_t s, bool pdl) {
     attr[0].val.programmaticStreamSerializationAllowed = 1;
     cfg.attrs = attr;
     cfg.numAttrs = pdl ? 1 : 0;
-    return cudaLaunchKernelEx(&cfg, k_attn, a);
+    switch (a.nq) {
+        case 1: return cudaLaunchKernelEx(&cfg, k_attn<1>, a);
+        case 2: return cudaLaunchKernelEx(&cfg, k_attn<2>, a);
+        case 3: return cudaLaunchKernelEx(&cfg, k_attn<3>, a);
+        case 4: return cudaLaunchKernelEx(&cfg, k_attn<4>, a);
+        case 5: return cudaLaunchKernelEx(&cfg, k_attn<5>, a);
+        case 6: return cudaLaunchKernelEx(&cfg, k_attn<6>, a);
+        case 7: return cudaLaunchKernelEx(&cfg, k_attn<7>, a);
+        default: return cudaLaunchKernelEx(&cfg, k_attn<8>, a);
+    }
 }
 
 }  // namespace w4j

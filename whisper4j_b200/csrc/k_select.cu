@@ -111,31 +111,44 @@ __device__ Merged merge_partials(const float *stg, int P, int F) {
 }
 
 // One warp: top-k over the staged per-block candidate lists, each sorted (value desc,
-// index asc); a k-way merge where every lane advances the heads of the blocks it owns.
-// Unfilled entries come out as (-inf, 0), as topkIndices leaves them.
+// index asc); a k-way merge where every lane keeps the current heads of the blocks it owns
+// in registers and only the lane whose head won reloads it.  Unfilled entries come out as
+// (-inf, 0), as topkIndices leaves them.  P <= 32 * kMaxOwned.
 __device__ void merge_topk(const float *stg, int P, int F, int kk, int k, float *out_v, int *out_i) {
     const int lane = threadIdx.x & 31;
-    constexpr int kMaxOwned = 32;  // P <= 1024 blocks
-    unsigned char head[kMaxOwned];
-    const int J = (P + 31) / 32;
-    for (int j = 0; j < J && j < kMaxOwned; ++j) head[j] = 0;
+    constexpr int kMaxOwned = 8;
+    int head[kMaxOwned];
+    float hv[kMaxOwned];
+    int hi[kMaxOwned];
+#pragma unroll
+    for (int j = 0; j < kMaxOwned; ++j) {
+        const int c = lane + 32 * j;
+        head[j] = 0;
+        hv[j] = c < P && kk > 0 ? stg[c * F + 4] : -INFINITY;
+        hi[j] = c < P && kk > 0 ? __float_as_int(stg[c * F + 4 + kk]) : INT_MAX;
+    }
     for (int r = 0; r < k; ++r) {
         float bv = -INFINITY;
         int bi = INT_MAX, bj = -1;
-        for (int j = 0; j < J && j < kMaxOwned; ++j) {
-            const int c = lane + 32 * j;
-            if (c >= P || head[j] >= kk) continue;
-            const float v = stg[c * F + 4 + head[j]];
-            const int i = __float_as_int(stg[c * F + 4 + kk + head[j]]);
-            if (v != -INFINITY && better_c(v, i, bv, bi)) {
-                bv = v;
-                bi = i;
+#pragma unroll
+        for (int j = 0; j < kMaxOwned; ++j)
+            if (hv[j] != -INFINITY && better_c(hv[j], hi[j], bv, bi)) {
+                bv = hv[j];
+                bi = hi[j];
                 bj = j;
             }
-        }
         const int mine = bi;
         warp_best(bv, bi);
-        if (bi != INT_MAX && mine == bi && bj >= 0) head[bj]++;  // ids are unique across blocks
+        if (bi != INT_MAX && mine == bi && bj >= 0) {  // ids are unique across blocks
+#pragma unroll
+            for (int j = 0; j < kMaxOwned; ++j)
+                if (j == bj) {
+                    const int c = lane + 32 * j;
+                    ++head[j];
+                    hv[j] = head[j] < kk ? stg[c * F + 4 + head[j]] : -INFINITY;
+                    hi[j] = head[j] < kk ? __float_as_int(stg[c * F + 4 + kk + head[j]]) : INT_MAX;
+                }
+        }
         if (lane == 0) {
             out_v[r] = bi == INT_MAX ? -INFINITY : bv;
             out_i[r] = bi == INT_MAX ? 0 : bi;
@@ -151,7 +164,7 @@ __device__ void build_masks(const DecodeState &st, int m, const int *hg, int n, 
                             bool rules, int *hbuf) {
     const int lane = threadIdx.x & 31;
     // the history is scanned many times below: bring it into shared memory first
-    for (int i0 = lane; i0 < n; i0 += 32 * 8) {
+    for (int i0 = lane; hg != hbuf && i0 < n; i0 += 32 * 8) {
         int v[8];
 #pragma unroll
         for (int j = 0; j < 8; ++j)
@@ -331,21 +344,83 @@ __device__ void sample_row(float *row, int V, float T, double u, int *out_tok, d
 // ---------------------------------------------------------------------------
 // greedy / sampling step (one block per stream, beam = 1)
 // ---------------------------------------------------------------------------
+// log2 of the float4 count of a staged partial record holding 4 + 2k floats, rounded up to
+// a power of two (so record and field split with shifts): k = 0 -> 0, k = 6 -> 2, k = 9 -> 3.
+__host__ __device__ inline int rec_l2(int k) {
+    const int f4 = (4 + 2 * k + 3) / 4;
+    int l2 = 0;
+    while ((1 << l2) < f4) ++l2;
+    return l2;
+}
+
+// One warp: the P partial records of one sequence into shared memory, record c at
+// dst + c * (4 << l2) floats (the first 4 << l2 <= kPartStride floats of the record, whose
+// used prefix is 4 + 2k); 24 independent 16-byte loads in flight per lane.
+__device__ void stage_partials_warp(const float *part, int P, int l2, float *dst) {
+    const int lane = threadIdx.x & 31;
+    const int n = P << l2;
+    const int mask = (1 << l2) - 1;
+    constexpr int kB = 24;
+    for (int e0 = lane; e0 < n; e0 += 32 * kB) {
+        float4 v[kB];
+#pragma unroll
+        for (int j = 0; j < kB; ++j) {
+            const int e = e0 + 32 * j;
+            if (e < n) v[j] = *reinterpret_cast<const float4 *>(part + (size_t)(e >> l2) * kPartStride + ((e & mask) << 2));
+        }
+#pragma unroll
+        for (int j = 0; j < kB; ++j) {
+            const int e = e0 + 32 * j;
+            if (e < n) reinterpret_cast<float4 *>(dst)[e] = v[j];
+        }
+    }
+    __syncwarp();
+}
+
+// All threads of the block: n ints from global memory into shared memory, 8 loads in flight.
+__device__ __forceinline__ void stage_ints(const int *src, int n, int *dst) {
+    for (int i0 = threadIdx.x; i0 < n; i0 += blockDim.x * 8) {
+        int v[8];
+#pragma unroll
+        for (int j = 0; j < 8; ++j) {
+            const int i = i0 + blockDim.x * j;
+            v[j] = i < n ? src[i] : 0;
+        }
+#pragma unroll
+        for (int j = 0; j < 8; ++j) {
+            const int i = i0 + blockDim.x * j;
+            if (i < n) dst[i] = v[j];
+        }
+    }
+}
+
 __global__ void __launch_bounds__(kSelThreads) k_select_greedy(DecodeState st, int mode, const float *part, int P,
                                                                float *masked, int step) {
-    __shared__ int s_tok;
-    __shared__ double s_lp;
+    __shared__ int s_tok, s_len, s_done, s_pos;
+    __shared__ double s_lp, s_lp0;
     extern __shared__ __align__(16) float sel_smem[];
-    float *stg = sel_smem;                                   // [P][3]
-    int *hbuf = reinterpret_cast<int *>(sel_smem + P * 4);   // [hs]
-    pdl_trigger();
-    pdl_wait();
+    float *stg = sel_smem;                                   // [P][4]
+    int *hbuf = reinterpret_cast<int *>(sel_smem + P * 4);   // [hs]: this sequence's history
     const int s = blockIdx.x;
     const int m = s;
-    if (st.done[s]) return;
+    // The sequence's state was written by an earlier graph launch (or, after the prompt, by
+    // kernels that completed before the logits kernel started), never by the logits kernel
+    // this one waits on: read it, and stage the history, before the wait.
+    if (threadIdx.x == 0) {
+        s_done = st.done[s];
+        s_len = st.hist_len[0][m];
+        s_lp0 = st.lp[0][m];
+        s_pos = st.seq_pos[m];
+    }
+    __syncthreads();
+    const int len = s_len;
+    if (!s_done) stage_ints(st.hist[0] + (size_t)m * st.hs, len, hbuf);
+    pdl_trigger();
+    pdl_wait();
+    if (s_done) return;
     if (mode == SEL_GREEDY) {
         if (threadIdx.x < 32) {
-            stage_partials(part + (size_t)m * P * kPartStride, P, 0, stg);
+            stage_partials_warp(part + (size_t)m * P * kPartStride, P, 0, stg);
             const Merged mg = merge_partials(stg, P, 4);
             if (threadIdx.x == 0) {
                 s_tok = mg.argmax;
@@ -357,33 +432,30 @@ __global__ void __launch_bounds__(kSelThreads) k_select_greedy(DecodeState st, i
         int tok;
         double lp;
         // the draw is keyed by (seed, stream, tokens so far): reproducible for a given seed
-        sample_row(masked + (size_t)m * st.V, st.V, st.temperature, uniform01(st.seed, s, st.hist_len[0][m]), &tok,
-                   &lp);
+        sample_row(masked + (size_t)m * st.V, st.V, st.temperature, uniform01(st.seed, s, len), &tok, &lp);
         if (threadIdx.x == 0) {
             s_tok = tok;
             s_lp = lp;
         }
     }
-    __shared__ int s_len;
-    if (threadIdx.x == 0) s_len = st.hist_len[0][m];
     __syncthreads();
-    const int len = s_len;
+    const int tok = s_tok;
     if (threadIdx.x == 0) {
-        st.lp[0][m] += s_lp;
-        if (s_tok == st.eot) {
+        st.lp[0][m] = s_lp0 + s_lp;
+        if (tok == st.eot) {
             st.done[s] = 1;
             st.active[m] = 0;
         } else if (len < st.max_tokens) {
-            st.hist[0][(size_t)m * st.hs + len] = s_tok;
+            st.hist[0][(size_t)m * st.hs + len] = tok;
             st.hist_len[0][m] = len + 1;
-            st.tok_in[m] = s_tok;
-            st.seq_pos[m] += 1;
+            st.tok_in[m] = tok;
+            st.seq_pos[m] = s_pos + 1;
+            hbuf[len] = tok;
         }
     }
     __syncthreads();
-    if (threadIdx.x < 32 && s_tok != st.eot)
-        build_masks(st, m, st.hist[0] + (size_t)m * st.hs, min(len + 1, st.max_tokens), false, false,
-                    true, hbuf);
+    if (threadIdx.x < 32 && tok != st.eot)
+        build_masks(st, m, hbuf, min(len + 1, st.max_tokens), false, false, true, hbuf);
 }
 
 // ---------------------------------------------------------------------------
@@ -439,64 +511,108 @@ __global__ void __launch_bounds__(kSelThreads) k_select_beam_init(DecodeState st
     }
 }
 
+constexpr int kMaxBeam = 8;  // contexts allow beam <= 8
+
 __global__ void __launch_bounds__(kSelThreads) k_select_beam(DecodeState st, int parity, const float *part, int P) {
-    constexpr int kMaxB = kMaxTopK - 1;
-    __shared__ double c_score[kMaxB * (kMaxB + 1)];
-    __shared__ int c_beam[kMaxB * (kMaxB + 1)], c_tok[kMaxB * (kMaxB + 1)];
-    __shared__ int n_c;
-    __shared__ int new_src[kMaxB], new_tok[kMaxB];
-    __shared__ double new_score[kMaxB];
-    __shared__ int fin_src[kMaxB];
-    __shared__ double fin_score[kMaxB];
-    __shared__ int n_fin_new, saved_s, finish;
-    pdl_trigger();
-    pdl_wait();
-    const int s = blockIdx.x;
-    if (st.done[s]) return;
-    const int B = st.beam;
-    const int po = parity, pn = parity ^ 1;
-    const int stride = st.hs;
-    __shared__ float b_tv[kMaxB][kMaxTopK];
-    __shared__ int b_ti[kMaxB][kMaxTopK];
-    __shared__ float b_lsf[kMaxB];
-    __shared__ int b_live[kMaxB];
+    constexpr int kMaxC = kMaxBeam * (kMaxBeam + 1);
+    __shared__ double c_score[kMaxC], r_score[kMaxC];
+    __shared__ int c_beam[kMaxC], c_tok[kMaxC], r_beam[kMaxC], r_tok[kMaxC];
+    __shared__ int new_src[kMaxBeam], new_tok[kMaxBeam], fin_src[kMaxBeam];
+    __shared__ double new_score[kMaxBeam], fin_score[kMaxBeam];
+    __shared__ float b_tv[kMaxBeam][kMaxBeam + 1];
+    __shared__ int b_ti[kMaxBeam][kMaxBeam + 1];
+    __shared__ float b_lsf[kMaxBeam];
+    __shared__ int b_live[kMaxBeam], b_len[kMaxBeam], b_pos[kMaxBeam], b_slot[kMaxBeam];
+    __shared__ double b_lp[kMaxBeam];
+    __shared__ int s_done, s_fin, s_nc, n_saved, n_fin_new;
     extern __shared__ __align__(16) float sel_smem[];
-    const int F = 4 + 2 * (B + 1);
-    // per warp: staged partials, then a history buffer; a multiple of 4 floats keeps every
-    // warp's region 16-byte aligned for the vector copies into it
-    const int region = (P * F + stride + 3) & ~3;
-    const int warp = threadIdx.x >> 5;
-    for (int b = warp; b < B; b += kSelThreads / 32) {  // one warp per beam
-        const int mb = s * B + b;
-        const int len = st.hist_len[po][mb];
-        const bool live = st.hist[po][(size_t)mb * stride + len - 1] != st.eot;  // finished beams skip
-        if (threadIdx.x % 32 == 0) b_live[b] = live;
-        if (!live) continue;
-        float *stg = sel_smem + (size_t)b * region;
-        stage_partials(part + (size_t)mb * P * kPartStride, P, B + 1, stg);
-        const Merged mg = merge_partials(stg, P, F);
-        merge_topk(stg, P, F, B + 1, B + 1, b_tv[b], b_ti[b]);
-        if (threadIdx.x % 32 == 0) b_lsf[b] = (float)((double)mg.max + log(mg.sum));
+    const int s = blockIdx.x;
+    const int B = st.beam, K1 = B + 1;
+    const int po = parity, pn = parity ^ 1;
+    const int stride = st.hs, C = st.n_ctx;
+    const int l2 = rec_l2(K1), Fp = 4 << l2;
+    // shared memory: per beam a region (staged partials, then the new history for the masks;
+    // a multiple of 4 floats keeps every region 16-byte aligned), then the old histories and
+    // beam tables of all beams
+    const int region = (P * Fp + stride + 3) & ~3;
+    int *h_old = reinterpret_cast<int *>(sel_smem + (size_t)B * region);  // [B][stride]
+    int *t_old = h_old + (size_t)B * stride;                               // [B][C]
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+
+    // The beams' state at parity po was written by an earlier graph launch (or by the initial
+    // expansion, which completed before the logits kernel started), never by the logits kernel
+    // this one waits on: read it, and stage histories and tables, before the wait.
+    if (threadIdx.x == 0) {
+        s_done = st.done[s];
+        s_fin = st.fin_n[s];
+        n_saved = 0;
+        n_fin_new = 0;
+    }
+    if (threadIdx.x < B) {
+        const int mb = s * B + threadIdx.x;
+        b_len[threadIdx.x] = st.hist_len[po][mb];
+        b_pos[threadIdx.x] = st.seq_pos[mb];
+        b_lp[threadIdx.x] = st.lp[po][mb];
+        b_slot[threadIdx.x] = st.seq_slot[mb];
     }
     __syncthreads();
-    if (threadIdx.x == 0) {
-        n_c = 0;
-        for (int b = 0; b < B; ++b) {  // candidates in the reference's insertion order
-            if (!b_live[b]) continue;
-            const double blp = st.lp[po][s * B + b];
-            for (int k = 0; k < B + 1; ++k) {
-                c_score[n_c] = blp + (double)(float)(b_tv[b][k] - b_lsf[b]);
-                c_beam[n_c] = b;
-                c_tok[n_c] = b_ti[b][k];
-                ++n_c;
+    if (!s_done) {
+        int n = 0;
+        for (int b = 0; b < B; ++b) n = max(n, max(b_len[b], min(b_pos[b] + 1, C)));
+        for (int r = threadIdx.x; r < n; r += kSelThreads) {  // every beam's entry r at once
+            int hv[kMaxBeam], tv[kMaxBeam];
+#pragma unroll
+            for (int b = 0; b < kMaxBeam; ++b) {
+                const int mb = s * B + b;
+                hv[b] = (b < B && r < b_len[b]) ? st.hist[po][(size_t)mb * stride + r] : 0;
+                tv[b] = (b < B && r <= b_pos[b] && r < C) ? st.table[po][(size_t)mb * C + r] : 0;
+            }
+#pragma unroll
+            for (int b = 0; b < kMaxBeam; ++b) {
+                if (b < B && r < b_len[b]) h_old[b * stride + r] = hv[b];
+                if (b < B && r <= b_pos[b] && r < C) t_old[b * C + r] = tv[b];
             }
         }
     }
+    pdl_trigger();
+    pdl_wait();
+    if (s_done) return;
+    __syncthreads();  // staged histories
+    // one warp per beam: its partials, their merge and top-(beam + 1); finished beams skip
+    if (warp < B) {
+        const int b = warp;
+        const bool live = h_old[b * stride + b_len[b] - 1] != st.eot;
+        if (lane == 0) b_live[b] = live;
+        if (live) {
+            float *stg = sel_smem + (size_t)b * region;
+            stage_partials_warp(part + (size_t)(s * B + b) * P * kPartStride, P, l2, stg);
+            const Merged mg = merge_partials(stg, P, Fp);
+            merge_topk(stg, P, Fp, K1, K1, b_tv[b], b_ti[b]);
+            if (lane == 0) b_lsf[b] = (float)((double)mg.max + log(mg.sum));
+        }
+    }
     __syncthreads();
+    // candidates in the reference's insertion order (live beams, then rank within the beam)
+    if (threadIdx.x < B * K1) {
+        const int t = threadIdx.x, b = t / K1, k = t - b * K1;
+        if (b_live[b]) {
+            int before = 0;
+            for (int u = 0; u < b; ++u) before += b_live[u];
+            const int idx = before * K1 + k;
+            c_score[idx] = b_lp[b] + (double)(float)(b_tv[b][k] - b_lsf[b]);
+            c_beam[idx] = b;
+            c_tok[idx] = b_ti[b][k];
+        }
+    }
+    if (threadIdx.x == 0) {
+        int nl = 0;
+        for (int b = 0; b < B; ++b) nl += b_live[b];
+        s_nc = nl * K1;
+    }
+    __syncthreads();
+    const int n_c = s_nc;
     // stable sort by score, descending (List.sort with Double.compare): every candidate
-    // computes its own rank in parallel and moves there
-    __shared__ double r_score[kMaxB * (kMaxB + 1)];
-    __shared__ int r_beam[kMaxB * (kMaxB + 1)], r_tok[kMaxB * (kMaxB + 1)];
+    // computes its own rank and moves there
     if (threadIdx.x < n_c) {
         const int t = threadIdx.x;
         const double cs = c_score[t];
@@ -510,48 +626,41 @@ __global__ void __launch_bounds__(kSelThreads) k_select_beam(DecodeState st, int
         r_tok[rank] = c_tok[t];
     }
     __syncthreads();
+    // the reference walks the sorted list: an eot candidate finishes a sequence (and the walk
+    // stops once fin_n reaches beam), any other continues as a new beam while fewer than beam
+    // are saved.  Candidate i is reached iff fin_n + (eot candidates before i) < beam.
     if (threadIdx.x < n_c) {
-        c_score[threadIdx.x] = r_score[threadIdx.x];
-        c_beam[threadIdx.x] = r_beam[threadIdx.x];
-        c_tok[threadIdx.x] = r_tok[threadIdx.x];
-    }
-    __syncthreads();
-    if (threadIdx.x == 0) {
-        int saved = 0, nf = 0, fin = st.fin_n[s];
-        for (int i = 0; i < n_c; ++i) {
-            if (c_tok[i] == st.eot) {
-                fin_src[nf] = c_beam[i];
-                fin_score[nf] = c_score[i];
-                ++nf;
-                ++fin;
-                if (fin >= B) break;
-                continue;
+        const int i = threadIdx.x;
+        int eb = 0;
+        for (int j = 0; j < i; ++j) eb += r_tok[j] == st.eot;
+        if (s_fin + eb < B) {
+            if (r_tok[i] == st.eot) {
+                fin_src[eb] = r_beam[i];
+                fin_score[eb] = r_score[i];
+                atomicAdd(&n_fin_new, 1);
+            } else if (i - eb < B) {
+                new_src[i - eb] = r_beam[i];
+                new_tok[i - eb] = r_tok[i];
+                new_score[i - eb] = r_score[i];
+                atomicAdd(&n_saved, 1);
             }
-            if (saved >= B) continue;
-            new_src[saved] = c_beam[i];
-            new_tok[saved] = c_tok[i];
-            new_score[saved] = c_score[i];
-            ++saved;
         }
-        n_fin_new = nf;
-        saved_s = saved;
-        finish = (n_c == 0 || saved == 0 || fin >= B) ? 1 : 0;
     }
     __syncthreads();
-    // finished sequences: copy the source beam's tokens (without the eot)
-    const int fin0 = st.fin_n[s];
-    for (int f = 0; f < n_fin_new; ++f) {
-        const int src = s * B + fin_src[f];
-        const int len = st.hist_len[po][src];
+    const int saved = n_saved, nf = n_fin_new, fin0 = s_fin;
+    const bool finish = n_c == 0 || saved == 0 || fin0 + nf >= B;
+    // finished sequences: the source beam's tokens (without the eot), from shared memory
+    for (int f = 0; f < nf; ++f) {
+        const int sb = fin_src[f];
+        const int len = b_len[sb];
         int *dst = st.fin_tok + ((size_t)s * B + fin0 + f) * stride;
-        for (int i = threadIdx.x; i < len; i += kSelThreads) dst[i] = st.hist[po][(size_t)src * stride + i];
+        for (int i = threadIdx.x; i < len; i += kSelThreads) dst[i] = h_old[sb * stride + i];
         if (threadIdx.x == 0) {
             st.fin_len[(size_t)s * B + fin0 + f] = len;
             st.fin_lp[(size_t)s * B + fin0 + f] = fin_score[f];
         }
     }
-    __syncthreads();
-    if (threadIdx.x == 0) st.fin_n[s] = fin0 + n_fin_new;
+    if (threadIdx.x == 0) st.fin_n[s] = fin0 + nf;
     if (finish) {
         if (threadIdx.x == 0) {
             st.done[s] = 1;
@@ -559,76 +668,42 @@ __global__ void __launch_bounds__(kSelThreads) k_select_beam(DecodeState st, int
         }
         return;
     }
-    // rearrange: new beam b continues source beam new_src[b] (beams past `saved` copy beam 0)
-    const int saved = saved_s;
-    __shared__ int c_len[kMaxB], c_pos[kMaxB], c_src[kMaxB];
-    if (threadIdx.x < B) {
-        const int b = threadIdx.x;
-        const int bb = b < saved ? b : 0;
-        c_src[b] = s * B + new_src[bb];
-        c_len[b] = st.hist_len[po][c_src[b]];
-        c_pos[b] = st.seq_pos[c_src[b]];  // row written this step by the source beam
-    }
-    __syncthreads();
-    // copy histories (len ints) and tables (pos + 1 ints) of all new beams, flattened over
-    // the block with 8 independent loads in flight per thread
-    {
-        const int per = stride + st.n_ctx;  // slot per beam: history part then table part
-        const int total = B * per;
-        for (int i0 = threadIdx.x; i0 < total; i0 += kSelThreads * 8) {
-            int v[8];
-#pragma unroll
-            for (int j = 0; j < 8; ++j) {
-                const int i = i0 + kSelThreads * j;
-                v[j] = 0;
-                if (i < total) {
-                    const int b = i / per, r = i - b * per;
-                    if (r < stride) {
-                        if (r < c_len[b]) v[j] = st.hist[po][(size_t)c_src[b] * stride + r];
-                    } else if (r - stride <= c_pos[b]) {
-                        v[j] = st.table[po][(size_t)c_src[b] * st.n_ctx + (r - stride)];
-                    }
-                }
-            }
-#pragma unroll
-            for (int j = 0; j < 8; ++j) {
-                const int i = i0 + kSelThreads * j;
-                if (i >= total) continue;
-                const int b = i / per, r = i - b * per;
-                const int mb = s * B + b;
-                if (r < stride) {
-                    if (r < c_len[b]) st.hist[pn][(size_t)mb * stride + r] = v[j];
-                } else if (r - stride <= c_pos[b]) {
-                    st.table[pn][(size_t)mb * st.n_ctx + (r - stride)] = v[j];
-                }
-            }
-        }
-    }
-    if (threadIdx.x < B) {
-        const int b = threadIdx.x;
-        const int bb = b < saved ? b : 0;
+    // rearrange: new beam b continues source beam new_src[b] (beams past `saved` copy beam 0);
+    // histories and tables at parity pn are written from the staged copies, and each new
+    // history also goes to its beam's region for the masks
+    for (int b = 0; b < B; ++b) {
+        const int sb = new_src[b < saved ? b : 0];
+        const int len = b_len[sb], pos = b_pos[sb];
         const int mb = s * B + b;
-        st.hist[pn][(size_t)mb * stride + c_len[b]] = new_tok[bb];
-        st.hist_len[pn][mb] = c_len[b] + 1;
+        int *hb = reinterpret_cast<int *>(sel_smem + (size_t)b * region + P * Fp);
+        for (int r = threadIdx.x; r < len; r += kSelThreads) {
+            const int v = h_old[sb * stride + r];
+            st.hist[pn][(size_t)mb * stride + r] = v;
+            hb[r] = v;
+        }
+        for (int r = threadIdx.x; r <= pos && r < C; r += kSelThreads)
+            st.table[pn][(size_t)mb * C + r] = t_old[sb * C + r];
+    }
+    if (threadIdx.x < B) {
+        const int b = threadIdx.x;
+        const int bb = b < saved ? b : 0;
+        const int sb = new_src[bb];
+        const int mb = s * B + b;
+        const int len = b_len[sb];
+        const int pos = b_pos[sb];  // row written this step by the source beam
+        st.hist[pn][(size_t)mb * stride + len] = new_tok[bb];
+        reinterpret_cast<int *>(sel_smem + (size_t)b * region + P * Fp)[len] = new_tok[bb];
+        st.hist_len[pn][mb] = len + 1;
         st.lp[pn][mb] = new_score[bb];
-        if (c_pos[b] + 1 < st.n_ctx) st.table[pn][(size_t)mb * st.n_ctx + c_pos[b] + 1] = st.seq_slot[mb];
+        if (pos + 1 < C) st.table[pn][(size_t)mb * C + pos + 1] = b_slot[b];
+        st.tok_in[mb] = new_tok[bb];
+        st.seq_pos[mb] = b_pos[0] + 1;  // beams of a stream advance in lockstep
     }
     __syncthreads();
-    if (threadIdx.x == 0) {
-        const int pos0 = st.seq_pos[s * B];  // beams of a stream advance in lockstep
-        for (int b = 0; b < B; ++b) {
-            const int bb = b < saved ? b : 0;
-            const int mb = s * B + b;
-            st.tok_in[mb] = new_tok[bb];
-            st.seq_pos[mb] = pos0 + 1;
-        }
-    }
-    __syncthreads();
-    // every beam advanced one position; positions were equal, so read them after the writes
-    for (int b = warp; b < B; b += kSelThreads / 32) {
-        const int mb = s * B + b;
-        build_masks(st, mb, st.hist[pn] + (size_t)mb * stride, st.hist_len[pn][mb], false, false, true,
-                    reinterpret_cast<int *>(sel_smem + (size_t)b * region + P * F));
+    if (warp < B) {
+        const int b = warp;
+        int *hb = reinterpret_cast<int *>(sel_smem + (size_t)b * region + P * Fp);
+        build_masks(st, s * B + b, hb, b_len[new_src[b < saved ? b : 0]] + 1, false, false, true, hb);
     }
     if (threadIdx.x == 0) st.beam_par[s] = pn;  // parity holding the live beams (finalize reads it)
 }
@@ -778,8 +853,9 @@ static cudaLaunchConfig_t cfg_for(dim3 grid, dim3 block, cudaStream_t s, bool pd
 static size_t select_smem(const DecodeState &st, int mode, int P) {
     const int B = st.beam;
     if (mode == SEL_GREEDY || mode == SEL_SAMPLE) return ((size_t)P * 4 + st.hs) * 4;
-    const int k = mode == SEL_BEAM_INIT ? B : B + 1;
-    return (size_t)B * (((size_t)P * (4 + 2 * k) + st.hs + 3) & ~(size_t)3) * 4;
+    if (mode == SEL_BEAM_INIT) return (size_t)B * (((size_t)P * (4 + 2 * B) + st.hs + 3) & ~(size_t)3) * 4;
+    const size_t fp = (size_t)4 << rec_l2(B + 1);
+    return ((size_t)B * (((size_t)P * fp + st.hs + 3) & ~(size_t)3) + (size_t)B * (st.hs + st.n_ctx)) * 4;
 }
 
 cudaError_t select_prepare() {
@@ -787,6 +863,10 @@ cudaError_t select_prepare() {
     if (e == cudaSuccess) e = allow_dynamic_smem(k_select_beam_init);
     if (e == cudaSuccess) e = allow_dynamic_smem(k_select_beam);
     if (e == cudaSuccess) e = allow_dynamic_smem(k_argmax_merge);
+    if (e == cudaSuccess) e = prefer_max_smem(k_argmax_merge_status);
+    if (e == cudaSuccess) e = prefer_max_smem(k_nsp);
+    if (e == cudaSuccess) e = prefer_max_smem(k_init_masks);
+    if (e == cudaSuccess) e = prefer_max_smem(k_finalize);
     return e;
 }
 
@@ -795,7 +875,7 @@ cudaError_t launch_select(const DecodeState &st, int mode, int parity, const flo
     cudaLaunchAttribute attr[1];
     cudaLaunchConfig_t cfg = cfg_for(dim3(st.n_streams), dim3(kSelThreads), s, pdl, attr);
     cfg.dynamicSmemBytes = select_smem(st, mode, n_parts);
-    if (cfg.dynamicSmemBytes > 227 * 1024) return cudaErrorInvalidValue;
+    if (cfg.dynamicSmemBytes > 227 * 1024 || n_parts > 256 || st.beam > kMaxBeam) return cudaErrorInvalidValue;
     switch (mode) {
         case SEL_GREEDY:
         case SEL_SAMPLE:

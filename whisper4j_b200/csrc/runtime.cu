@@ -157,10 +157,12 @@ static void build_gelu_lut(std::vector<float> &t) {
 
 // Key splits of an attention launch: enough blocks to cover the SMs twice, at least one
 // full 128-key tile per split, and no more partials than the combine can stage.
-static int choose_split(int groups_x_heads, int len, int sms, int nq) {
-    int want = (2 * sms + groups_x_heads - 1) / std::max(1, groups_x_heads);
-    const int cap = std::min(std::max(1, (len + 63) / 64), attn_max_splits(nq));
-    return std::max(1, std::min(want, cap));
+// Key splits of one attention launch: one 128-key tile per split block (every tile then
+// streams in before the block's wait), bounded by the combine's staging capacity.  Self-
+// attention blocks past ceil(len / 128) exit at once, so the grid can be sized for the
+// longest context.
+static int choose_split(int len, int nq) {
+    return std::max(1, std::min((len + kAttnKeyTile - 1) / kAttnKeyTile, attn_max_splits(nq)));
 }
 
 extern "C" const char *w4j_last_error(void) { return g_err.c_str(); }
@@ -213,7 +215,8 @@ extern "C" int w4j_ctx_create(const w4j_dims *dims, int device, int max_streams,
     if (cudaStreamCreateWithFlags(&c->stream, cudaStreamNonBlocking) != cudaSuccess) return fail(set_err(W4J_ERR_CUDA, "stream"));
     cudaEventCreate(&c->ev0);
     cudaEventCreate(&c->ev1);
-    if ((rc = (int)gemv_prepare()) != 0 || (rc = (int)select_prepare()) != 0 || (rc = (int)logits_tc_prepare()) != 0)
+    if ((rc = (int)gemv_prepare()) != 0 || (rc = (int)select_prepare()) != 0 || (rc = (int)logits_tc_prepare()) != 0 ||
+        (rc = (int)attn_prepare()) != 0)
         return fail(set_err(W4J_ERR_CUDA, "kernel attributes: %s", cudaGetErrorString((cudaError_t)rc)));
     const size_t V = c->V, C = c->C, A = c->A, L = c->L;
     const size_t M = c->M_max;
@@ -228,7 +231,7 @@ extern "C" int w4j_ctx_create(const w4j_dims *dims, int device, int max_streams,
         (rc = dalloc(c, &c->h, M * 4 * d)) || (rc = dalloc(c, &c->xa_stage, A * d)))
         return fail(rc);
     c->attn_split_max = std::max((int)((C + 63) / 64), (int)((A + 63) / 64));
-    if ((rc = dalloc(c, &c->attn_part, M * H * c->attn_split_max * (2 + kHeadDim))) ||
+    if ((rc = dalloc(c, &c->attn_part, M * H * c->attn_split_max * kAttnRec)) ||
         (rc = dalloc(c, &c->attn_ctr, M * H)))
         return fail(rc);
     c->n_parts = logits_parts_for(c->V, c->sm_count);
@@ -534,8 +537,8 @@ struct PassArgs {
 static int run_layers(w4j_ctx *c, const PassArgs &pa, long long &launches) {
     const bool pdl = true;
     const int d = c->d;
-    const int self_split = choose_split(pa.M * c->H, c->C, c->sm_count, 1);
-    const int cross_split = choose_split(pa.groups * c->H, c->A, c->sm_count, pa.nq);
+    const int self_split = choose_split(c->C, 1);
+    const int cross_split = choose_split(c->A, pa.nq);
     for (int l = 0; l < c->L; ++l) {
         LayerDev &ly = c->layers[l];
         GemvArgs g;

@@ -19,7 +19,8 @@ constexpr int kMaxTopK = 16;                        // beam + 1 <= 16
 constexpr int kPartStride = 4 + 2 * kMaxTopK;       // floats per logits partial
 constexpr int kMaxRanges = 4;                       // masked id ranges per sequence
 constexpr int kGemvThreads = 256;
-constexpr int kAttnThreads = 128;
+constexpr int kAttnThreads = 256;
+constexpr int kAttnRec = 68;                       // floats per attention split record: m, l, pad, o[64]
 constexpr int kAttnKeyTile = 128;
 
 enum WType : int { WT_F16 = 1, WT_Q8 = 8 };
@@ -82,7 +83,7 @@ struct AttnArgs {
     int nq = 1;                        // queries per group (cross: beams of one stream)
     int groups = 0;
     int nsplit = 1;
-    float *part = nullptr;             // [groups*nq][n_head][nsplit][2 + 64]
+    float *part = nullptr;             // [groups*nq][n_head][nsplit][kAttnRec]
     unsigned *counters = nullptr;      // [groups][n_head], zero between uses
     float *out = nullptr;              // [groups*nq][d]
     const int *active = nullptr;       // [groups]
@@ -226,6 +227,16 @@ __device__ __forceinline__ float warp_max(float v) {
     return v;
 }
 
+// Every kernel of the decode chain asks for the largest shared-memory carveout: an SM then
+// never has to drain and reconfigure its L1/shared split between two kernels of the chain,
+// so a dependent kernel's blocks can become resident (and prefetch) while its predecessor's
+// blocks still run.
+template <typename Kern>
+inline cudaError_t prefer_max_smem(Kern kern) {
+    return cudaFuncSetAttribute(reinterpret_cast<const void *>(kern), cudaFuncAttributePreferredSharedMemoryCarveout,
+                                (int)cudaSharedmemCarveoutMaxShared);
+}
+
 // Let `kern` use all the opt-in shared memory the device offers beside its static arrays.
 template <typename Kern>
 inline cudaError_t allow_dynamic_smem(Kern kern) {
@@ -235,8 +246,9 @@ inline cudaError_t allow_dynamic_smem(Kern kern) {
     cudaFuncAttributes fa;
     cudaError_t e = cudaFuncGetAttributes(&fa, reinterpret_cast<const void *>(kern));
     if (e != cudaSuccess) return e;
-    return cudaFuncSetAttribute(reinterpret_cast<const void *>(kern), cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                optin - (int)fa.sharedSizeBytes);
+    e = cudaFuncSetAttribute(reinterpret_cast<const void *>(kern), cudaFuncAttributeMaxDynamicSharedMemorySize,
+                             optin - (int)fa.sharedSizeBytes);
+    return e == cudaSuccess ? prefer_max_smem(kern) : e;
 }
 
 // ---------------------------------------------------------------------------
@@ -273,6 +285,7 @@ cudaError_t logits_tc_prepare();
 cudaError_t launch_logits_tc(const LogitsArgs &a, const void *tmap, int n_parts, cudaStream_t s, bool pdl);
 bool make_tmap_f16_rows(void *map_out, const void *base, int rows, int cols);  // 128-byte map
 cudaError_t select_prepare();
+cudaError_t attn_prepare();
 cudaError_t launch_f32_to_f16(const float *src, __half *dst, size_t n, cudaStream_t s);
 
 }  // namespace w4j
