@@ -88,7 +88,7 @@ __device__ __forceinline__ float row_value(const DMat &m, int row, int k) {
 // one warp per row normalises in shared memory.
 template <int MT>
 __device__ void load_activations(const GemvArgs &a, int m0, int K, float *act_s, const float *ln_s, int warp,
-                                 int lane) {
+                                 int lane, const int *tok_s = nullptr, const int *pos_s = nullptr) {
     const int K4 = K / 4;
     const int total = MT * K4;
     if (a.in_mode == IN_EMBED_LN) {
@@ -102,7 +102,7 @@ __device__ void load_activations(const GemvArgs &a, int m0, int K, float *act_s,
                 const int m = m0 + mm;
                 e[j] = p[j] = make_float4(0.f, 0.f, 0.f, 0.f);
                 if (i < total && m < a.M) {
-                    const int tok = a.tok[m], pos = a.pos[m];
+                    const int tok = tok_s ? tok_s[m] : a.tok[m], pos = pos_s ? pos_s[m] : a.pos[m];
                     p[j] = *reinterpret_cast<const float4 *>(a.pos_emb + (size_t)pos * K + k);
                     if (f16) {
                         const uint2 u = *reinterpret_cast<const uint2 *>(a.E.h + (size_t)tok * K + k);
@@ -128,14 +128,15 @@ __device__ void load_activations(const GemvArgs &a, int m0, int K, float *act_s,
             }
         }
     } else {
+        // rows m0.. are contiguous in `act`: one flat copy of the live rows (rows past M: zero)
+        const int live = (a.M - m0 < MT ? a.M - m0 : MT) * K4;
+        const float4 *src = reinterpret_cast<const float4 *>(a.act) + (size_t)m0 * K4;
         for (int i0 = threadIdx.x; i0 < total; i0 += kGemvThreads * 8) {
             float4 v[8];
 #pragma unroll
             for (int j = 0; j < 8; ++j) {
                 const int i = i0 + kGemvThreads * j;
-                const int mm = i / K4, m = m0 + mm;
-                v[j] = (i < total && m < a.M) ? reinterpret_cast<const float4 *>(a.act)[(size_t)m * K4 + (i - mm * K4)]
-                                              : make_float4(0.f, 0.f, 0.f, 0.f);
+                v[j] = i < live ? src[i] : make_float4(0.f, 0.f, 0.f, 0.f);
             }
 #pragma unroll
             for (int j = 0; j < 8; ++j)
@@ -253,12 +254,12 @@ __device__ __forceinline__ void fma_chunk_q8(const uint4 (&w)[R], const float (&
 template <int MT, int R, int WT>
 __device__ __forceinline__ void smem_rows(const unsigned char *w_s, int row_bytes, int nrows, const __half *sc_s,
                                           const __half *sc_g, int K, const float *act_s,
-                                          float (&acc)[R * P2<MT>::v], int lane) {
+                                          float (&acc)[R * P2<MT>::v], int lane, int c0, int cstep) {
     constexpr int CE = WT == WT_F16 ? 8 : 16;
     const int nchunk = K / CE;
 #pragma unroll
     for (int i = 0; i < R * P2<MT>::v; ++i) acc[i] = 0.f;
-    for (int c = lane; c < nchunk; c += 32) {
+    for (int c = c0; c < nchunk; c += cstep) {
         uint4 w[R];
         float sc[R];
 #pragma unroll
@@ -306,9 +307,15 @@ __global__ void __launch_bounds__(kGemvThreads) k_gemv(GemvArgs a, GemvLaunch L)
     __half *sc_s = reinterpret_cast<__half *>(smem + L.w_bytes);
     float *act_s = reinterpret_cast<float *>(smem + L.w_bytes + L.s_bytes);
     float *ln_s = act_s + (size_t)MT * K;  // [gamma | beta]
-    uint64_t *bar = reinterpret_cast<uint64_t *>(ln_s + 2 * (size_t)K);
+    uint64_t *bar = reinterpret_cast<uint64_t *>(ln_s + (a.in_mode != IN_ACT ? 2 * (size_t)K : 0));
+    // epilogue operands: bias of the block's rows, per-sequence liveness / cache slot / position /
+    // token, and (residual epilogue) the residual values of the pass
+    float *bias_s = reinterpret_cast<float *>(bar + 2);                        // [rows_per_block]
+    int *mi_s = reinterpret_cast<int *>(bias_s + L.rows_per_block);           // [4][M]
+    float *res_s = reinterpret_cast<float *>(mi_s + 4 * (size_t)a.M);         // [MT][rows_per_block]
     const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
     const int row_bytes = WT == WT_F16 ? K * 2 : K;
+    const int M = a.M;
     // --- independent of the previous kernel: the weight rows ---
     if (tid == 0) {
         mbar_init(bar, 1);
@@ -322,28 +329,51 @@ __global__ void __launch_bounds__(kGemvThreads) k_gemv(GemvArgs a, GemvLaunch L)
     if (WT == WT_Q8)
         for (int i = tid; i < nr * (K / 32); i += kGemvThreads) sc_s[i] = a.W.s[(size_t)r0 * (K / 32) + i];
     if (a.in_mode != IN_ACT) stage_ln(a.ln_g, a.ln_b, K, ln_s);
+    // Biases are weights; liveness, cache slots, positions and tokens were written by the host
+    // or by an earlier graph launch, never by a kernel of this launch's chain: read them now.
+    for (int i = tid; i < nr; i += kGemvThreads) bias_s[i] = a.bias ? a.bias[r0 + i] : 0.f;
+    for (int i = tid; i < M; i += kGemvThreads) {
+        mi_s[i] = a.active ? a.active[i] : 1;
+        if (a.out_mode == OUT_QKV) {
+            mi_s[M + i] = a.seq_slot[i];
+            mi_s[2 * M + i] = a.pos[i];
+        }
+        if (a.in_mode == IN_EMBED_LN) {
+            mi_s[2 * M + i] = a.pos[i];
+            mi_s[3 * M + i] = a.tok[i];
+        }
+    }
     pdl_trigger();
     pdl_wait();
 
     bool ok = true;
     for (int m0 = 0; m0 < a.M; m0 += MT) {
-        load_activations<MT>(a, m0, K, act_s, ln_s, warp, lane);
+        // residual values of the pass (rows r0 + tid): loaded into registers now, stored to
+        // shared memory after the activation loads were issued, so both are in flight together
+        float resv[MT];
+        const bool has_res = a.out_mode == OUT_RESIDUAL && tid < nr;
+        if (has_res)
+#pragma unroll
+            for (int mm = 0; mm < MT; ++mm) resv[mm] = m0 + mm < M ? a.y[(size_t)(m0 + mm) * N + r0 + tid] : 0.f;
+        if (m0 == 0) __syncthreads();  // mi_s
+        load_activations<MT>(a, m0, K, act_s, ln_s, warp, lane, mi_s + 3 * M, mi_s + 2 * M);
+        if (has_res)
+#pragma unroll
+            for (int mm = 0; mm < MT; ++mm) res_s[mm * L.rows_per_block + tid] = resv[mm];
+        if (a.out_mode == OUT_RESIDUAL)  // blocks of more than kGemvThreads rows (op-level calls)
+            for (int r = tid + kGemvThreads; r < nr; r += kGemvThreads)
+#pragma unroll
+                for (int mm = 0; mm < MT; ++mm)
+                    res_s[mm * L.rows_per_block + r] = m0 + mm < M ? a.y[(size_t)(m0 + mm) * N + r0 + r] : 0.f;
         __syncthreads();
-        if (m0 == 0) ok = mbar_wait(bar, 0, a.err);
+        if (m0 == 0) ok = __syncthreads_and(mbar_wait(bar, 0, a.err));  // block-uniform: a barrier follows
         if (ok) {
             constexpr int PM = P2<MT>::v;
-            for (int g = warp; g * R < nr; g += kGemvThreads / 32) {
-                float acc[R * PM];
-                smem_rows<MT, R, WT>(w_s + (size_t)g * R * row_bytes, row_bytes, min(R, nr - g * R),
-                                     sc_s + (size_t)g * R * (K / 32), nullptr, K, act_s, acc, lane);
-                const float v = warp_reduce_multi<R * PM>(acc, lane);
-                if (!reduced_owner<R * PM>(lane)) continue;
-                const int idx = reduced_index<R * PM>(lane);
-                const int r = idx / PM, mm = idx % PM;
-                const int n = r0 + g * R + r, m = m0 + mm;
-                if (mm >= MT || g * R + r >= nr || m >= a.M) continue;
-                if (a.active && !a.active[m]) continue;
-                const float val = v + (a.bias ? a.bias[n] : 0.f);
+            // output (row lr of the block, sequence m0 + mm) with its epilogue
+            auto emit = [&](float v, int lr, int mm) {
+                const int n = r0 + lr, m = m0 + mm;
+                if (mm >= MT || lr >= nr || m >= a.M || !mi_s[m]) return;
+                const float val = v + bias_s[lr];
                 switch (a.out_mode) {
                     case OUT_STORE:
                         a.y[(size_t)m * N + n] = val;
@@ -352,7 +382,7 @@ __global__ void __launch_bounds__(kGemvThreads) k_gemv(GemvArgs a, GemvLaunch L)
                         a.y[(size_t)m * N + n] = a.gelu_lut[__half_as_ushort(__float2half_rn(val))];
                         break;
                     case OUT_RESIDUAL:
-                        a.y[(size_t)m * N + n] += val;
+                        a.y[(size_t)m * N + n] = res_s[mm * L.rows_per_block + lr] + val;
                         break;
                     case OUT_QKV: {
                         const int dm = N / 3;
@@ -361,13 +391,46 @@ __global__ void __launch_bounds__(kGemvThreads) k_gemv(GemvArgs a, GemvLaunch L)
                             a.y[(size_t)m * dm + c] = val;
                         } else {
                             const int head = c / kHeadDim, dd = c % kHeadDim;
-                            const size_t row = (((size_t)a.seq_slot[m] * a.n_layer + a.layer) * a.n_head + head) *
-                                                   (size_t)a.n_ctx + (size_t)a.pos[m];
+                            const size_t row = (((size_t)mi_s[M + m] * a.n_layer + a.layer) * a.n_head + head) *
+                                                   (size_t)a.n_ctx + (size_t)mi_s[2 * M + m];
                             __half *dst = part == 1 ? a.kcache : a.vcache;
                             dst[row * kHeadDim + dd] = __float2half_rn(val);
                         }
                         break;
                     }
+                }
+            };
+            // G groups of R rows; with fewer groups than warps, KS warps share a group's K
+            // chunks and their sums meet in shared memory (added in warp order)
+            const int G = (nr + R - 1) / R;
+            const int KS = G >= 5 ? 1 : G >= 3 ? 2 : G == 2 ? 4 : 8;  // G * KS <= 8 warps
+            if (KS == 1) {
+                for (int g = warp; g < G; g += kGemvThreads / 32) {
+                    float acc[R * PM];
+                    smem_rows<MT, R, WT>(w_s + (size_t)g * R * row_bytes, row_bytes, min(R, nr - g * R),
+                                         sc_s + (size_t)g * R * (K / 32), nullptr, K, act_s, acc, lane, lane, 32);
+                    const float v = warp_reduce_multi<R * PM>(acc, lane);
+                    if (!reduced_owner<R * PM>(lane)) continue;
+                    const int idx = reduced_index<R * PM>(lane);
+                    emit(v, g * R + idx / PM, idx % PM);
+                }
+            } else {
+                __shared__ float red_s[kGemvThreads / 32][32];
+                const int g = warp / KS, kp = warp % KS;
+                if (g < G) {
+                    float acc[R * PM];
+                    smem_rows<MT, R, WT>(w_s + (size_t)g * R * row_bytes, row_bytes, min(R, nr - g * R),
+                                         sc_s + (size_t)g * R * (K / 32), nullptr, K, act_s, acc, lane,
+                                         lane + 32 * kp, 32 * KS);
+                    const float v = warp_reduce_multi<R * PM>(acc, lane);
+                    if (reduced_owner<R * PM>(lane)) red_s[warp][reduced_index<R * PM>(lane)] = v;
+                }
+                __syncthreads();
+                if (g < G && kp == 0 && reduced_owner<R * PM>(lane)) {
+                    const int idx = reduced_index<R * PM>(lane);
+                    float v = 0.f;
+                    for (int q = 0; q < KS; ++q) v += red_s[warp + q][idx];
+                    emit(v, g * R + idx / PM, idx % PM);
                 }
             }
         }
@@ -404,7 +467,9 @@ static void plan_gemv(int M, int N, int K, int type, int sms, int &mt, GemvLaunc
     L.rows_per_block = rpb;
     L.w_bytes = align16((size_t)rpb * row_bytes);
     L.s_bytes = align16((size_t)rpb * srow);
-    const size_t left = kSmemBudget - L.w_bytes - L.s_bytes - 64 - 2 * (size_t)K * 4;
+    // epilogue staging: bias, 4 ints per sequence, up to 8 residual rows
+    const size_t epi = ((size_t)rpb * 9 + 4 * (size_t)M) * 4;
+    const size_t left = kSmemBudget - L.w_bytes - L.s_bytes - 64 - 2 * (size_t)K * 4 - epi;
     int cap = (int)(left / ((size_t)K * 4));
     mt = M < 8 ? M : 8;
     if (mt > cap) mt = cap;
@@ -417,7 +482,8 @@ static void plan_gemv(int M, int N, int K, int type, int sms, int &mt, GemvLaunc
 
 template <int MT, int R, int WT>
 static cudaError_t launch_gemv_t(const GemvArgs &a, const GemvLaunch &L, int blocks, cudaStream_t s, bool pdl) {
-    const size_t smem = L.w_bytes + L.s_bytes + ((size_t)MT + 2) * a.W.K * sizeof(float) + 16;
+    const size_t smem = L.w_bytes + L.s_bytes + ((size_t)MT + (a.in_mode != IN_ACT ? 2 : 0)) * a.W.K * sizeof(float) + 16 +
+                        ((size_t)L.rows_per_block * (1 + MT) + 4 * (size_t)a.M) * 4;
     cudaLaunchConfig_t cfg = {};
     cfg.gridDim = dim3(blocks);
     cfg.blockDim = dim3(kGemvThreads);
@@ -542,7 +608,7 @@ __global__ void __launch_bounds__(kGemvThreads) k_logits(LogitsArgs a, LogitsLau
                 const int rloc = warp * R;
                 smem_rows<MT, R, WT>(st + (size_t)rloc * row_bytes, row_bytes, min(R, rows - rloc), nullptr,
                                      WT == WT_Q8 ? a.E.s + (size_t)(lo + t * SR + rloc) * (d / 32) : nullptr, d,
-                                     act_s, acc, lane);
+                                     act_s, acc, lane, lane, 32);
                 const float v = warp_reduce_multi<R * PM>(acc, lane);
                 if (reduced_owner<R * PM>(lane)) {
                     const int idx = reduced_index<R * PM>(lane);
@@ -671,7 +737,7 @@ cudaError_t gemv_prepare() {
 
 cudaError_t launch_logits(const LogitsArgs &a, int P, cudaStream_t s, bool pdl) {
     if (a.M <= 0) return cudaSuccess;
-    if (a.topk > kMaxTopK) return cudaErrorInvalidValue;
+    if (a.topk > kLaneTopK) return cudaErrorInvalidValue;
     if (a.E.type == WT_F16) return dispatch_logits<WT_F16>(a, P, s, pdl);
     if (a.E.type == WT_Q8) return dispatch_logits<WT_Q8>(a, P, s, pdl);
     return cudaErrorInvalidValue;

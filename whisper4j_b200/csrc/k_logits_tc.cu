@@ -148,13 +148,20 @@ __global__ void __launch_bounds__(256, 1) k_logits_tc(LogitsArgs a, const __grid
         tmem_relinquish();
     }
     for (int i = tid; i < 2 * d; i += blockDim.x) ln_s[i] = i < d ? a.ln_g[i] : a.ln_b[i - d];
+    // rows M..NU of the B operand are zero whatever the activations are
+    for (int i = tid; i < (NU - a.M) * (d / 8); i += blockDim.x) {
+        const int m = a.M + i / (d / 8), c = i % (d / 8);
+        const int kb = c / 8, cc = c % 8;
+        *reinterpret_cast<uint4 *>(bop + (size_t)kb * NU * 128 + (size_t)m * 128 + ((cc ^ (m & 7)) * 16)) =
+            make_uint4(0, 0, 0, 0);
+    }
     pdl_trigger();
     pdl_wait();
     __syncthreads();  // ln_s is read across warps below
 
-    // ---- B operand: LayerNorm(x[m]) as f16, K-major, 128-byte swizzle; rows >= M are zero ----
-    for (int m = warp; m < NU; m += 8) {
-        const bool live = m < a.M;
+    // ---- B operand: LayerNorm(x[m]) as f16, K-major, 128-byte swizzle (rows >= M were zeroed) ----
+    for (int m = warp; m < a.M; m += 8) {
+        const bool live = true;
         constexpr int kMaxChunks = 1280 / 8 / 32;  // 16-byte chunks per lane for d <= 1280
         float v[kMaxChunks][8];
         const int nch = d / 8;  // chunks of 8 along K
@@ -331,8 +338,10 @@ static bool plan_tc(int M, int V, int d, int P, int &nu, LogitsTcLaunch &L) {
     const size_t fixed = bbytes + tbytes + lnbytes + 256;
     const size_t budget = 220 * 1024;
     if (fixed + 2 * kStageBytes > budget) return false;
+    // 7 stages (112 KB) keep ~16 MB of the embedding in flight over the GPU, enough to cover
+    // DRAM latency, and leave room beside the block for the select kernel that follows
     int ns = (int)((budget - fixed) / kStageBytes);
-    L.n_stages = ns > 12 ? 12 : ns;
+    L.n_stages = ns > 7 ? 7 : ns;
     L.b_off = (unsigned)(L.n_stages * kStageBytes);  // 1024-byte aligned (stages are 16 KB)
     L.tile_off = L.b_off + (unsigned)bbytes;        // bbytes is a multiple of 2 KB
     L.ln_off = L.tile_off + (unsigned)((tbytes + 15) & ~(size_t)15);
@@ -368,6 +377,7 @@ cudaError_t logits_tc_prepare() {
 cudaError_t launch_logits_tc(const LogitsArgs &a, const void *tmap, int P, cudaStream_t s, bool pdl) {
     int nu;
     LogitsTcLaunch L;
+    if (a.topk > kLaneTopK) return cudaErrorInvalidValue;
     if (!tmap || a.E.type != WT_F16 || !plan_tc(a.M, a.V, a.d, P, nu, L)) return cudaErrorNotSupported;
     const CUtensorMap &map = *reinterpret_cast<const CUtensorMap *>(tmap);
     if (nu == 16) return launch_tc_t<16>(a, map, L, P, s, pdl);

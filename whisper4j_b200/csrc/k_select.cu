@@ -25,13 +25,12 @@ __device__ __forceinline__ bool better_c(float v1, int i1, float v2, int i2) {
     return v1 > v2 || (v1 == v2 && i1 < i2);
 }
 
-// Double.compare(a, b) > 0, as the reference's candidate sort uses (-0.0 < 0.0, NaN largest).
-__device__ __forceinline__ bool dgreater(double a, double b) {
-    if (a > b) return true;
-    if (a < b) return false;
-    const bool an = isnan(a), bn = isnan(b);
-    if (an || bn) return an && !bn;
-    return !signbit(a) && signbit(b);
+// A 64-bit key whose unsigned order is Double.compare's order (-0.0 < 0.0, every NaN equal
+// and above +inf), so a sort compares integers.
+__device__ __forceinline__ unsigned long long dkey(double x) {
+    if (isnan(x)) return ~0ull;
+    const unsigned long long b = (unsigned long long)__double_as_longlong(x);
+    return (b >> 63) ? ~b : (b | 0x8000000000000000ull);
 }
 
 // ---------------------------------------------------------------------------
@@ -98,7 +97,7 @@ __device__ Merged merge_partials(const float *stg, int P, int F) {
     if (bv != -INFINITY)
         for (int c = lane; c < P; c += 32) {
             const float mc = stg[c * F];
-            if (mc != -INFINITY) s += (double)stg[c * F + 1] * exp((double)(mc - bv));
+            if (mc != -INFINITY) s += (double)(stg[c * F + 1] * expf(mc - bv));
         }
 #pragma unroll
     for (int o = 16; o > 0; o >>= 1) s += __shfl_xor_sync(0xffffffffu, s, o);
@@ -613,15 +612,19 @@ __global__ void __launch_bounds__(kSelThreads) k_select_beam(DecodeState st, int
     const int n_c = s_nc;
     // stable sort by score, descending (List.sort with Double.compare): every candidate
     // computes its own rank and moves there
+    __shared__ unsigned long long c_key[kMaxC];
+    if (threadIdx.x < n_c) c_key[threadIdx.x] = dkey(c_score[threadIdx.x]);
+    __syncthreads();
     if (threadIdx.x < n_c) {
         const int t = threadIdx.x;
-        const double cs = c_score[t];
+        const unsigned long long ck = c_key[t];
         int rank = 0;
+#pragma unroll 8
         for (int u = 0; u < n_c; ++u) {
-            const double us = c_score[u];
-            if (dgreater(us, cs) || (u < t && !dgreater(cs, us))) ++rank;
+            const unsigned long long uk = c_key[u];
+            rank += (uk > ck) | ((uk == ck) & (u < t));
         }
-        r_score[rank] = cs;
+        r_score[rank] = c_score[t];
         r_beam[rank] = c_beam[t];
         r_tok[rank] = c_tok[t];
     }
@@ -632,6 +635,7 @@ __global__ void __launch_bounds__(kSelThreads) k_select_beam(DecodeState st, int
     if (threadIdx.x < n_c) {
         const int i = threadIdx.x;
         int eb = 0;
+#pragma unroll 8
         for (int j = 0; j < i; ++j) eb += r_tok[j] == st.eot;
         if (s_fin + eb < B) {
             if (r_tok[i] == st.eot) {

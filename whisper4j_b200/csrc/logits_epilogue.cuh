@@ -4,6 +4,8 @@
 
 namespace w4j {
 
+constexpr int kLaneTopK = 9;  // per-lane candidate list: beam + 1 <= 9 (beam <= 8)
+
 __device__ __forceinline__ bool logit_better(float v1, int i1, float v2, int i2) {
     return v1 > v2 || (v1 == v2 && i1 < i2);
 }
@@ -62,57 +64,92 @@ for (int mm = warp; mm < MT; mm += blockDim.x / 32) {
         }
         if (a.masked_out)
             for (int i = lane; i < n; i += 32) a.masked_out[(size_t)m * a.V + lo + i] = row[i];
-        // max + first argmax
-        float bv = -INFINITY;
+        // one pass: running max with its first index, sum of exp rescaled as the max grows,
+        // and (beam search) a sorted per-lane top-k list (value desc, index asc)
+        const int K = a.topk;
+        float bv = -INFINITY, sm = 0.f;
         int bi = INT_MAX;
-        for (int i = lane; i < n; i += 32)
-            if (logit_better(row[i], lo + i, bv, bi)) {
-                bv = row[i];
-                bi = lo + i;
+        float tv[kLaneTopK];
+        int ti[kLaneTopK];
+#pragma unroll
+        for (int j = 0; j < kLaneTopK; ++j) {
+            tv[j] = -INFINITY;
+            ti[j] = INT_MAX;
+        }
+        for (int i = lane; i < n; i += 32) {
+            const float v = row[i];
+            if (v == -INFINITY) continue;
+            const int id = lo + i;
+            if (logit_better(v, id, bv, bi)) {
+                sm = (bv == -INFINITY ? 0.f : sm * __expf(bv - v)) + 1.f;
+                bv = v;
+                bi = id;
+            } else {
+                sm += __expf(v - bv);
             }
+            if (K > 0) {  // insertion into the sorted list (the displaced tail moves down one slot)
+                float cv = v;
+                int ci = id;
+#pragma unroll
+                for (int j = 0; j < kLaneTopK; ++j) {
+                    if (j < K && logit_better(cv, ci, tv[j], ti[j])) {
+                        const float xv = tv[j];
+                        const int xi = ti[j];
+                        tv[j] = cv;
+                        ti[j] = ci;
+                        cv = xv;
+                        ci = xi;
+                    }
+                }
+            }
+        }
+        // warp: max / first argmax, then the sums relative to it
+        float wv = bv;
+        int wi = bi;
 #pragma unroll
         for (int o = 16; o > 0; o >>= 1) {
-            const float ov = __shfl_xor_sync(0xffffffffu, bv, o);
-            const int oi = __shfl_xor_sync(0xffffffffu, bi, o);
-            if (logit_better(ov, oi, bv, bi)) {
-                bv = ov;
-                bi = oi;
+            const float ov = __shfl_xor_sync(0xffffffffu, wv, o);
+            const int oi = __shfl_xor_sync(0xffffffffu, wi, o);
+            if (logit_better(ov, oi, wv, wi)) {
+                wv = ov;
+                wi = oi;
             }
         }
-        float sm = 0.f;
-        if (bv != -INFINITY)
-            for (int i = lane; i < n; i += 32) sm += __expf(row[i] - bv);
-        sm = warp_sum(sm);
+        float ws = (bv == -INFINITY) ? 0.f : sm * __expf(bv - wv);
+        ws = warp_sum(ws);
         float *pp = a.part + ((size_t)m * P + blockIdx.x) * kPartStride;
         if (lane == 0) {
-            pp[0] = bv;
-            pp[1] = sm;
-            pp[2] = __int_as_float(bi == INT_MAX ? lo : bi);
+            pp[0] = wv;
+            pp[1] = wv == -INFINITY ? 0.f : ws;
+            pp[2] = __int_as_float(wi == INT_MAX ? lo : wi);
         }
-        // top-k candidates of this block (value desc, index asc); unfilled: (-inf, 0)
-        for (int k = 0; k < a.topk; ++k) {
-            float kv = -INFINITY;
-            int ki = INT_MAX;
-            for (int i = lane; i < n; i += 32)
-                if (row[i] != -INFINITY && logit_better(row[i], lo + i, kv, ki)) {
-                    kv = row[i];
-                    ki = lo + i;
-                }
+        // top-k of the block: k rounds of a warp argmax over the lanes' list heads; the lane
+        // whose head won shifts its list.  Unfilled entries: (-inf, 0).
+        for (int k = 0; k < K; ++k) {
+            float hv = tv[0];
+            int hi2 = ti[0];
 #pragma unroll
             for (int o = 16; o > 0; o >>= 1) {
-                const float ov = __shfl_xor_sync(0xffffffffu, kv, o);
-                const int oi = __shfl_xor_sync(0xffffffffu, ki, o);
-                if (logit_better(ov, oi, kv, ki)) {
-                    kv = ov;
-                    ki = oi;
+                const float ov = __shfl_xor_sync(0xffffffffu, hv, o);
+                const int oi = __shfl_xor_sync(0xffffffffu, hi2, o);
+                if (logit_better(ov, oi, hv, hi2)) {
+                    hv = ov;
+                    hi2 = oi;
                 }
             }
             if (lane == 0) {
-                pp[4 + k] = kv;
-                pp[4 + a.topk + k] = __int_as_float(ki == INT_MAX ? 0 : ki);
+                pp[4 + k] = hi2 == INT_MAX ? -INFINITY : hv;
+                pp[4 + K + k] = __int_as_float(hi2 == INT_MAX ? 0 : hi2);
             }
-            if (ki != INT_MAX && ki - lo >= 0 && ki - lo < n && lane == ((ki - lo) & 31)) row[ki - lo] = -INFINITY;
-            __syncwarp();
+            if (hi2 != INT_MAX && ti[0] == hi2) {  // ids are unique: exactly one lane owns it
+#pragma unroll
+                for (int j = 0; j + 1 < kLaneTopK; ++j) {
+                    tv[j] = tv[j + 1];
+                    ti[j] = ti[j + 1];
+                }
+                tv[kLaneTopK - 1] = -INFINITY;
+                ti[kLaneTopK - 1] = INT_MAX;
+            }
         }
     }
 }
