@@ -70,6 +70,11 @@ def encoder_output(seed, n_audio_ctx, d):
     return x.astype(np.float32)
 
 
+# DRAM bytes per k_gemv launch (read + write, mean over the six projections of a layer) from the
+# ncu capture summarised in profiles/k_gemv_base.en-beam5.md; other workloads were not captured.
+GEMV_TRAFFIC = {"base.en-beam5": (2.265 + 2.218 + 1.666 + 0.614 + 0.609 + 0.615) / 6 * 1e6}
+
+
 def step_bytes(dims, wtype, streams, beam, max_tokens, n_prompt):
     """Algorithmic HBM bytes of one token step: weights + cross K/V per stream + self K/V per sequence."""
     d, L, V = dims.n_text_state, dims.n_text_layer, dims.n_vocab
@@ -266,10 +271,68 @@ def run_ours(args, cfg, dims, rank, world, local_rank):
         one_step()
         e2e_s += time.perf_counter() - t1
     e2e_steps = max(1, args.steps // 2)
-    # ---- dominant kernel: the vocabulary logits pass, replayed alone with CUDA events ----
+    # ---- kernels replayed alone with CUDA events (cold L2), on the stream they are launched on ----
     M = S * B
     d, V = dims.n_text_state, dims.n_vocab
-    roof = None
+    st = torch.cuda.current_stream()
+    vp = lambda t: ctypes.c_void_p(t.data_ptr())  # noqa: E731
+    peaks = {}
+    try:
+        with open(os.path.join(ROOT, "MEASURED_PEAKS.json")) as f:
+            peaks = json.load(f)
+    except Exception:
+        pass
+    peak = peaks.get("hbm_gbs")
+    src = "measured" if peak else "fallback"
+    peak = peak or 6650.0
+
+    def time_alone(launch, reps=20):
+        durs = []
+        for i in range(args.warmup + reps):
+            flush.fill_(1.0)
+            e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            e0.record(st)
+            launch()
+            e1.record(st)
+            e1.synchronize()
+            if i >= args.warmup:
+                durs.append(e0.elapsed_time(e1))
+        return statistics.median(durs)
+
+    # dominant kernel by time share (profiles/launches_*.md): k_gemv, the six projections of a
+    # decoder layer at this workload's M, K and N (LayerNorm prologue / GELU / residual epilogues)
+    from whisper4j_b200._lib import GGML_F16, GGML_Q8_0
+    proj = [(3 * d, d, 1, 0), (d, d, 0, 2), (d, d, 1, 0), (d, d, 0, 2), (4 * d, d, 1, 1), (d, 4 * d, 0, 2)]
+    gdur, galg = [], []
+    for N, K, ln, epi in proj:
+        W = (torch.randn(N, K, device=dev) * 0.02).half()
+        wt = GGML_F16
+        if cfg["wtype"] == "q8_0":
+            raw = torch.empty(N * K // 32 * 34, dtype=torch.uint8, device=dev)
+            raw.view(-1, 34)[:, 2:] = torch.randint(-127, 128, (N * K // 32, 32), device=dev).to(torch.int8).view(torch.uint8)
+            raw.view(-1, 34)[:, :2] = torch.full((N * K // 32, 1), 0.01, device=dev).half().view(torch.uint8)
+            W = torch.empty(N * K + N * K // 16, dtype=torch.uint8, device=dev)
+            check(lib().w4j_q8_0_repack(vp(raw), N, K, vp(W), ctypes.c_void_p(st.cuda_stream)))
+            wt = GGML_Q8_0
+        x = torch.randn(M, K, device=dev)
+        y = torch.zeros(M, N, device=dev)
+        bias = torch.zeros(N, device=dev)
+        g, bt = torch.ones(K, device=dev), torch.zeros(K, device=dev)
+        gdur.append(time_alone(lambda: check(lib().w4j_op_linear(
+            dec._ctx, vp(x), M, K, vp(W), wt, N, vp(bias), vp(g) if ln else None, vp(bt) if ln else None, epi, vp(y),
+            ctypes.c_void_p(st.cuda_stream)))))
+        wbytes_ = N * K * 2 if cfg["wtype"] == "f16" else N * K * 34 // 32
+        galg.append(wbytes_ + M * K * 4 + M * N * 4 * (2 if epi == 2 else 1))
+    g_ms, g_alg = sum(gdur) / len(gdur), sum(galg) / len(galg)
+    g_ach = g_alg / (g_ms * 1e-3) / 1e9
+    roof = {"bound": "hbm", "kernel": "k_gemv: the six projections of one decoder layer (QKV with LN, attn.out + "
+                                      "residual, cross q with LN, cross out + residual, mlp.0 with LN + GELU, "
+                                      "mlp.2 + residual), each replayed alone",
+            "achieved": g_ach, "peak": peak, "peak_source": src, "unit": "GB/s", "frac": g_ach / peak,
+            "traffic": GEMV_TRAFFIC.get(args.config) if not args.max_tokens else None,
+            "algorithmic_bytes_per_launch": g_alg, "launch_ms": g_ms,
+            "launch_ms_each": gdur, "timing": "cold L2, alone, CUDA events around one launch (includes launch latency)"}
+    roof_logits = None
     if cfg["wtype"] == "f16":
         E = torch.from_numpy(np.frombuffer(gm.tensors["decoder.token_embedding.weight"].data, np.float16).copy()
                              ).to(dev).view(V, d)
@@ -278,35 +341,14 @@ def run_ours(args, cfg, dims, rank, world, local_rank):
         bta = torch.zeros(d, device=dev)
         tok = torch.zeros(M, dtype=torch.int32, device=dev)
         lp = torch.zeros(M, dtype=torch.float64, device=dev)
-        st = torch.cuda.current_stream()
-        vp = lambda t: ctypes.c_void_p(t.data_ptr())  # noqa: E731
-        durs = []
-        for i in range(args.warmup + 20):
-            flush.fill_(1.0)
-            e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-            e0.record(st)
-            check(lib().w4j_op_logits_argmax(dec._ctx, vp(x), M, vp(E), V, vp(g), vp(bta), vp(tok), vp(lp),
-                                             ctypes.c_void_p(st.cuda_stream)))
-            e1.record(st)
-            e1.synchronize()
-            if i >= args.warmup:
-                durs.append(e0.elapsed_time(e1))
-        kern_ms = statistics.mean(durs)
-        peaks = {}
-        try:
-            with open(os.path.join(ROOT, "MEASURED_PEAKS.json")) as f:
-                peaks = json.load(f)
-        except Exception:
-            pass
-        peak = peaks.get("hbm_gbs")
-        src = "measured" if peak else "fallback"
-        peak = peak or 6650.0
+        kern_ms = time_alone(lambda: check(lib().w4j_op_logits_argmax(
+            dec._ctx, vp(x), M, vp(E), V, vp(g), vp(bta), vp(tok), vp(lp), ctypes.c_void_p(st.cuda_stream))))
         alg = V * d * 2.0 + M * d * 4.0
         achieved = alg / (kern_ms * 1e-3) / 1e9
-        roof = {"bound": "hbm", "kernel": "k_logits (vocabulary logits + processors + partial reductions) "
-                                          "followed by the argmax merge", "achieved": achieved, "peak": peak,
-                "peak_source": src, "unit": "GB/s", "frac": achieved / peak, "traffic": None,
-                "algorithmic_bytes_per_launch": alg, "launch_ms": kern_ms, "timing": "cold L2, alone"}
+        roof_logits = {"bound": "hbm", "kernel": "k_logits_tc (vocabulary logits + processors + partial reductions) "
+                                                 "followed by the argmax merge", "achieved": achieved, "peak": peak,
+                       "peak_source": src, "unit": "GB/s", "frac": achieved / peak, "traffic": None,
+                       "algorithmic_bytes_per_launch": alg, "launch_ms": kern_ms, "timing": "cold L2, alone"}
     # ---- gather over ranks ----
     vals = torch.tensor([dev_ms, wall, e2e_s, float(tokens)], dtype=torch.float64, device=dev)
     if world > 1:
@@ -323,7 +365,6 @@ def run_ours(args, cfg, dims, rank, world, local_rank):
     value = tokens_all / (dev_ms * 1e-3)
     per_token_step_ms = dev_ms / args.steps / T
     bstep, wbytes = step_bytes(dims, cfg["wtype"], S, B, T, len(prompt))
-    peak = roof["peak"] if roof else 6650.0
     out = {
         "metric": "decoder tokens/s", "value": value, "unit": "tokens/s", "n_gpus": world, "steps": args.steps,
         "warmup": args.warmup, "ms_per_step": dev_ms / args.steps, "higher_is_better": True, "scaling": "weak",
@@ -345,8 +386,9 @@ def run_ours(args, cfg, dims, rank, world, local_rank):
         "gpu_launches": launches,
         "clocks": clocks,
     }
-    if roof:
-        out["roofline"] = roof
+    out["roofline"] = roof
+    if roof_logits:
+        out["roofline_logits"] = roof_logits
     if world == 1 and not args.no_cpu_baseline:
         sample = int(os.environ.get("W4J_CPU_SAMPLE_STEPS", "0")) or max(4, min(64, int(40 / B) + 2))
         ctoks, csec, cthreads, _ = cpu_decode_sample(gm, dims, cfg, 1, sample)
