@@ -7,14 +7,16 @@
 // (kvLen = n_audio_ctx), and the cache append of appendHeadsCache (:140-164), which here is
 // an in-place row write done by the QKV kernel's epilogue.
 //
-// Flash-decoding: block (split, head, group) streams keys [j0, j1) of one head through
-// shared memory in tiles of 128 rows with an online softmax, for every query of the group
-// (cross-attention: all beams of one stream share its encoder K/V, so those bytes are read
-// once per stream, not once per beam).  Per-split partial (max, sum, o[64]) go to scratch;
-// the last split block of a (group, head) to finish combines them in split order, so the
-// result is deterministic.  Self-attention rows are gathered through the beam table
-// (position -> physical slot), which replaces the reference's per-beam cache copies
-// (WhisperDecoder.java:343-361).
+// Flash-decoding: block (split, head, group) stages keys [j0, j1) of one head in shared memory
+// (every tile before griddepcontrol.wait where the rows are already final) and runs an online
+// softmax over them for every query of the group (cross-attention: all beams of one stream
+// share its encoder K/V, so those bytes are read once per stream, not once per beam).  The
+// split blocks of one (group, head) form a thread-block cluster: each leaves its partial
+// (max, sum, o[64] per query) in its own shared memory and, after a cluster barrier, combines
+// a slice of the output from all partials through distributed shared memory, in split order,
+// so the result is deterministic and no partial goes through global memory.  Self-attention
+// rows are gathered through the beam table (position -> physical slot), which replaces the
+// reference's per-beam cache copies (WhisperDecoder.java:343-361).
 #include "w4j_internal.cuh"
 
 namespace w4j {
@@ -22,22 +24,34 @@ namespace w4j {
 constexpr int kRowPad = 72;  // halves per shared K/V row (144 B: conflict-free 16-byte reads)
 constexpr int kMaxNq = 8;
 constexpr int kWarps = kAttnThreads / 32;
+constexpr int kMaxSplits = 8;  // portable cluster size
+constexpr int kTileHalves = 2 * kAttnKeyTile * kRowPad;  // one K tile + one V tile
 
 __device__ __forceinline__ void cp_async16(void *smem, const void *gmem) {
     const unsigned s = (unsigned)__cvta_generic_to_shared(smem);
     asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" ::"r"(s), "l"(gmem) : "memory");
 }
 __device__ __forceinline__ void cp_async_wait_all() { asm volatile("cp.async.wait_all;" ::: "memory"); }
+__device__ __forceinline__ void cluster_sync() {
+    asm volatile("barrier.cluster.arrive.release.aligned;\n\tbarrier.cluster.wait.acquire.aligned;" ::: "memory");
+}
+__device__ __forceinline__ float ld_cluster_f32(const float *local, unsigned rank) {
+    unsigned remote;
+    asm volatile("mapa.shared::cluster.u32 %0, %1, %2;" : "=r"(remote) : "r"(smem_u32(local)), "r"(rank));
+    float v;
+    asm volatile("ld.shared::cluster.f32 %0, [%1];" : "=f"(v) : "r"(remote) : "memory");
+    return v;
+}
 
+// Dynamic shared memory: `tiles` K/V tile pairs of the block's key range.
 // NQ queries per group (self-attention: 1; cross-attention: the beams of one stream).
 template <int NQ>
 __global__ void __launch_bounds__(kAttnThreads) k_attn(AttnArgs a) {
-    __shared__ __align__(16) __half skv[2 * kAttnKeyTile * kRowPad];  // K tile, V tile; reduction and combine staging
-    __half *sk = skv, *sv = skv + kAttnKeyTile * kRowPad;
+    extern __shared__ __align__(16) __half skv[];  // [tiles][K tile | V tile]; then reused for the reduction
     __shared__ __align__(16) float sq[NQ][kHeadDim];
     __shared__ float sp[NQ][kAttnKeyTile];
     __shared__ float s_m[NQ], s_l[NQ], s_alpha[NQ];
-    __shared__ int s_last;
+    __shared__ __align__(16) float s_part[NQ][kHeadDim];  // this split's unnormalised output (cluster mode)
 
     const int split = blockIdx.x, head = blockIdx.y, group = blockIdx.z;
     const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
@@ -45,6 +59,7 @@ __global__ void __launch_bounds__(kAttnThreads) k_attn(AttnArgs a) {
     // Positions, beam tables and liveness were written by the host or by an earlier graph
     // launch, never by a kernel of this launch's chain, so they are read before the wait.
     const bool live = !a.active || a.active[group];
+    if (!live) return;  // uniform over the cluster (one group)
     const __half *kbase = nullptr, *vbase = nullptr;
     if (a.cross) {
         const int stream = a.stream_of_group[group];
@@ -55,15 +70,17 @@ __global__ void __launch_bounds__(kAttnThreads) k_attn(AttnArgs a) {
     const int len = a.cross ? a.n_audio : a.pos[group] + 1;
     const int newest = a.cross ? -1 : len - 1;  // the row the previous kernel (QKV) writes
     // splits in use: one key tile each while the context is short (the grid is sized for the
-    // longest context); blocks past them have nothing to do
+    // longest context); with a single one, the other blocks have nothing to do
     const int ns = a.cross ? a.nsplit : min(a.nsplit, max(1, (len + kAttnKeyTile - 1) / kAttnKeyTile));
-    if (split >= ns) return;
-    const int j0 = (int)(((long long)split * len) / ns), j1 = (int)(((long long)(split + 1) * len) / ns);
+    if (ns == 1 && split > 0) return;  // uniform over the cluster: no cluster barrier is reached
+    const int j0 = split < ns ? (int)(((long long)split * len) / ns) : len;
+    const int j1 = split < ns ? (int)(((long long)(split + 1) * len) / ns) : len;
     const float scale = 0.125f;  // (float)(1 / sqrt(64))
 
-    // stage K and V rows [t0, t0 + nk) (128 B each = 8 x 16 B); which: 0 all, 1 all but the
-    // newest self row, 2 only the newest
-    auto stage = [&](int t0, int nk, int which) {
+    // stage K and V rows [t0, t0 + nk) into tile pair `ti` (128 B each = 8 x 16 B); which: 0 all,
+    // 1 all but the newest self row, 2 only the newest
+    auto stage = [&](int ti, int t0, int nk, int which) {
+        __half *tk = skv + (size_t)ti * kTileHalves, *tv = tk + kAttnKeyTile * kRowPad;
         for (int c = tid; c < nk * 8; c += kAttnThreads) {
             const int r = c >> 3, part = c & 7;
             const int p = t0 + r;
@@ -78,23 +95,21 @@ __global__ void __launch_bounds__(kAttnThreads) k_attn(AttnArgs a) {
                 krow = a.kc + off;
                 vrow = a.vc + off;
             }
-            cp_async16(&sk[r * kRowPad + part * 8], krow + part * 8);
-            cp_async16(&sv[r * kRowPad + part * 8], vrow + part * 8);
+            cp_async16(&tk[r * kRowPad + part * 8], krow + part * 8);
+            cp_async16(&tv[r * kRowPad + part * 8], vrow + part * 8);
         }
     };
     // Encoder K/V never change during a decode, and self rows older than the newest were
-    // written by an earlier graph launch (a.self_prefetch): stage the first tile now, so it
-    // streams in while the previous kernel finishes.
-    const bool pre = live && j1 > j0 && (a.cross || a.self_prefetch);
-    if (pre) stage(j0, min(kAttnKeyTile, j1 - j0), a.cross ? 0 : 1);
+    // written by an earlier graph launch (a.self_prefetch): stage them now, so they stream in
+    // while the previous kernel finishes.
+    const int nt = (j1 - j0 + kAttnKeyTile - 1) / kAttnKeyTile;
+    const bool pre = a.cross || a.self_prefetch;
+    if (pre)
+        for (int ti = 0; ti < nt; ++ti) stage(ti, j0 + ti * kAttnKeyTile, min(kAttnKeyTile, j1 - j0 - ti * kAttnKeyTile), a.cross ? 0 : 1);
     pdl_trigger();
     pdl_wait();
-    if (!live) {
-        cp_async_wait_all();
-        return;
-    }
-    // the newest self row (written by the previous kernel) streams in with the queries
-    if (pre && !a.cross) stage(j0, min(kAttnKeyTile, j1 - j0), 2);
+    for (int ti = 0; ti < nt; ++ti)  // the newest self row (written by the previous kernel), or everything
+        stage(ti, j0 + ti * kAttnKeyTile, min(kAttnKeyTile, j1 - j0 - ti * kAttnKeyTile), pre ? 2 : 0);
     if (tid < NQ * kHeadDim / 4) {  // queries: one 16-byte load per thread
         const int i = tid / (kHeadDim / 4), c = tid % (kHeadDim / 4);
         reinterpret_cast<float4 *>(sq[i])[c] =
@@ -109,13 +124,12 @@ __global__ void __launch_bounds__(kAttnThreads) k_attn(AttnArgs a) {
     float ow[NQ][2];
 #pragma unroll
     for (int i = 0; i < NQ; ++i) ow[i][0] = ow[i][1] = 0.f;
+    cp_async_wait_all();
     __syncthreads();
 
-    for (int t0 = j0; t0 < j1; t0 += kAttnKeyTile) {
-        const int nk = min(kAttnKeyTile, j1 - t0);
-        if (t0 != j0 || !pre) stage(t0, nk, 0);
-        cp_async_wait_all();
-        __syncthreads();
+    for (int ti = 0; ti < nt; ++ti) {
+        const int nk = min(kAttnKeyTile, j1 - j0 - ti * kAttnKeyTile);
+        const __half *sk = skv + (size_t)ti * kTileHalves, *sv = sk + kAttnKeyTile * kRowPad;
         {  // scores: two threads per key, 32 dims each
             const int key = tid >> 1, hf = tid & 1;
             float acc[NQ];
@@ -220,117 +234,95 @@ __global__ void __launch_bounds__(kAttnThreads) k_attn(AttnArgs a) {
         }
         return;
     }
-    // partial record (m, l, o[64], pad) of this split
-    auto rec = [&](int i, int sp_) {
-        return a.part + ((((size_t)(group * NQ + i)) * a.n_head + head) * a.nsplit + sp_) * kAttnRec;
-    };
+    // cluster combine: this split's (max, sum, o) stay in shared memory; after the barrier,
+    // block r produces the outputs (query, dim) with index = r (mod cluster size) from the
+    // partials of all splits, read through distributed shared memory in split order
 #pragma unroll
     for (int t = 0; t < kPer; ++t) {
         const int pidx = tid + kAttnThreads * t;
+        if (pidx < NQ * kHeadDim) s_part[pidx / kHeadDim][pidx % kHeadDim] = o[t];
+    }
+    cluster_sync();
+    const int cs = a.nsplit;  // cluster size = blocks along x
+    for (int pidx = split + cs * tid; pidx < NQ * kHeadDim; pidx += cs * kAttnThreads) {
         const int i = pidx / kHeadDim, dd = pidx % kHeadDim;
-        if (pidx < NQ * kHeadDim) {
-            float *pp = rec(i, split);
-            pp[4 + dd] = o[t];
-            if (dd == 0) {
-                pp[0] = s_m[i];
-                pp[1] = s_l[i];
+        float ms[kMaxSplits], ls[kMaxSplits], os[kMaxSplits];
+#pragma unroll
+        for (int r = 0; r < kMaxSplits; ++r)
+            if (r < ns) {
+                ms[r] = ld_cluster_f32(&s_m[i], (unsigned)r);
+                ls[r] = ld_cluster_f32(&s_l[i], (unsigned)r);
+                os[r] = ld_cluster_f32(&s_part[i][dd], (unsigned)r);
             }
-        }
-    }
-    __threadfence();
-    __syncthreads();
-    if (tid == 0) {
-        unsigned *ctr = a.counters + (size_t)group * a.n_head + head;
-        const unsigned prev = atomicAdd(ctr, 1u);
-        s_last = prev == (unsigned)(ns - 1);
-        if (s_last) *ctr = 0u;  // ready for the next use of the counter
-    }
-    __syncthreads();
-    if (!s_last) return;
-    __threadfence();
-    // every split's record of this (group, head): one round of independent 16-byte L2 loads
-    float *stg = reinterpret_cast<float *>(skv);  // [NQ][ns][kAttnRec]
-    constexpr int kR4 = kAttnRec / 4;
-    const int n4 = ns * kR4;
-    for (int e0 = tid; e0 < n4; e0 += kAttnThreads * 2) {
-        float4 v[NQ][2];
-#pragma unroll
-        for (int i = 0; i < NQ; ++i)
-#pragma unroll
-            for (int j = 0; j < 2; ++j) {
-                const int e = e0 + kAttnThreads * j;
-                if (e < n4) v[i][j] = __ldcg(reinterpret_cast<const float4 *>(rec(i, 0)) + e);
-            }
-#pragma unroll
-        for (int i = 0; i < NQ; ++i)
-#pragma unroll
-            for (int j = 0; j < 2; ++j) {
-                const int e = e0 + kAttnThreads * j;
-                if (e < n4) reinterpret_cast<float4 *>(stg + (size_t)i * ns * kAttnRec)[e] = v[i][j];
-            }
-    }
-    __syncthreads();
-    // per query: the split weights exp(m_s - M) (in split order) and the denominator, once
-    float *wts = stg + (size_t)NQ * ns * kAttnRec;  // [NQ][ns + 1]
-    for (int i = warp; i < NQ; i += kWarps) {
-        const float *base = stg + (size_t)i * ns * kAttnRec;
         float M = -INFINITY;
-        for (int s2 = lane; s2 < ns; s2 += 32) M = fmaxf(M, base[s2 * kAttnRec]);
-        M = warp_max(M);
-        float den = 0.f;
-        for (int s2 = lane; s2 < ns; s2 += 32) {
-            const float ms = base[s2 * kAttnRec];
-            const float w = ms == -INFINITY ? 0.f : __expf(ms - M);
-            wts[i * (ns + 1) + s2] = w;
-            den = fmaf(w, base[s2 * kAttnRec + 1], den);
-        }
-        den = warp_sum(den);
-        if (lane == 0) wts[i * (ns + 1) + ns] = den;
-    }
-    __syncthreads();
 #pragma unroll
-    for (int t = 0; t < kPer; ++t) {
-        const int pidx = tid + kAttnThreads * t;
-        const int i = pidx / kHeadDim, dd = pidx % kHeadDim;
-        if (pidx >= NQ * kHeadDim) continue;
-        const float *base = stg + (size_t)i * ns * kAttnRec;
-        const float *w = wts + i * (ns + 1);
-        float num = 0.f;
-        for (int s2 = 0; s2 < ns; ++s2) num = fmaf(w[s2], base[s2 * kAttnRec + 4 + dd], num);
-        a.out[(size_t)(group * NQ + i) * a.d + head * kHeadDim + dd] = num / w[ns];
+        for (int r = 0; r < kMaxSplits; ++r)
+            if (r < ns) M = fmaxf(M, ms[r]);
+        float num = 0.f, den = 0.f;
+#pragma unroll
+        for (int r = 0; r < kMaxSplits; ++r)
+            if (r < ns && ms[r] != -INFINITY) {
+                const float w = __expf(ms[r] - M);
+                num = fmaf(w, os[r], num);
+                den = fmaf(w, ls[r], den);
+            }
+        a.out[(size_t)(group * NQ + i) * a.d + head * kHeadDim + dd] = num / den;
     }
+    cluster_sync();  // no block leaves while its partial may still be read
+}
+
+// Key splits of one launch: up to kMaxSplits (one cluster); tiles each block stages.
+int attn_max_splits(int) { return kMaxSplits; }
+static int attn_tiles(const AttnArgs &a) {
+    const int len_max = a.cross ? a.n_audio : a.n_ctx;
+    const int per = (len_max + a.nsplit - 1) / a.nsplit;
+    return (per + kAttnKeyTile - 1) / kAttnKeyTile;
+}
+
+template <int NQ>
+static cudaError_t prep_nq() {
+    return allow_dynamic_smem(k_attn<NQ>);
 }
 
 cudaError_t attn_prepare() {
-    cudaError_t e = prefer_max_smem(k_attn<1>);
-    if (e == cudaSuccess) e = prefer_max_smem(k_attn<2>);
-    if (e == cudaSuccess) e = prefer_max_smem(k_attn<3>);
-    if (e == cudaSuccess) e = prefer_max_smem(k_attn<4>);
-    if (e == cudaSuccess) e = prefer_max_smem(k_attn<5>);
-    if (e == cudaSuccess) e = prefer_max_smem(k_attn<6>);
-    if (e == cudaSuccess) e = prefer_max_smem(k_attn<7>);
-    if (e == cudaSuccess) e = prefer_max_smem(k_attn<8>);
+    cudaError_t e = prep_nq<1>();
+    if (e == cudaSuccess) e = prep_nq<2>();
+    if (e == cudaSuccess) e = prep_nq<3>();
+    if (e == cudaSuccess) e = prep_nq<4>();
+    if (e == cudaSuccess) e = prep_nq<5>();
+    if (e == cudaSuccess) e = prep_nq<6>();
+    if (e == cudaSuccess) e = prep_nq<7>();
+    if (e == cudaSuccess) e = prep_nq<8>();
     return e;
-}
-
-// Splits whose records (and the per-query weights) fit the combine's staging in the K/V tiles.
-int attn_max_splits(int nq) {
-    return (int)((2 * kAttnKeyTile * kRowPad * sizeof(__half) / sizeof(float)) / (nq * (kAttnRec + 1) + 1));
 }
 
 cudaError_t launch_attn(const AttnArgs &a, cudaStream_t s, bool pdl) {
     if (a.groups <= 0) return cudaSuccess;
-    if (a.nq < 1 || a.nq > kMaxNq || a.nsplit > attn_max_splits(a.nq)) return cudaErrorInvalidValue;
+    if (a.nq < 1 || a.nq > kMaxNq || a.nsplit < 1 || a.nsplit > kMaxSplits) return cudaErrorInvalidValue;
+    const int tiles = attn_tiles(a);
     cudaLaunchConfig_t cfg = {};
     cfg.gridDim = dim3(a.nsplit, a.n_head, a.groups);
     cfg.blockDim = dim3(kAttnThreads);
-    cfg.dynamicSmemBytes = 0;
+    cfg.dynamicSmemBytes = (size_t)tiles * kTileHalves * sizeof(__half);
+    if (cfg.dynamicSmemBytes < (size_t)kWarps * kMaxNq * kHeadDim * sizeof(float))
+        cfg.dynamicSmemBytes = (size_t)kWarps * kMaxNq * kHeadDim * sizeof(float);  // the reduction reuses it
     cfg.stream = s;
-    cudaLaunchAttribute attr[1];
-    attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
-    attr[0].val.programmaticStreamSerializationAllowed = 1;
+    cudaLaunchAttribute attr[2];
+    int na = 0;
+    if (pdl) {
+        attr[na].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+        attr[na].val.programmaticStreamSerializationAllowed = 1;
+        ++na;
+    }
+    if (a.nsplit > 1) {  // the split blocks of one (head, group) combine through a cluster
+        attr[na].id = cudaLaunchAttributeClusterDimension;
+        attr[na].val.clusterDim.x = a.nsplit;
+        attr[na].val.clusterDim.y = 1;
+        attr[na].val.clusterDim.z = 1;
+        ++na;
+    }
     cfg.attrs = attr;
-    cfg.numAttrs = pdl ? 1 : 0;
+    cfg.numAttrs = na;
     switch (a.nq) {
         case 1: return cudaLaunchKernelEx(&cfg, k_attn<1>, a);
         case 2: return cudaLaunchKernelEx(&cfg, k_attn<2>, a);

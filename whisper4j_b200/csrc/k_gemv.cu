@@ -91,6 +91,72 @@ __device__ void load_activations(const GemvArgs &a, int m0, int K, float *act_s,
                                  int lane, const int *tok_s = nullptr, const int *pos_s = nullptr) {
     const int K4 = K / 4;
     const int total = MT * K4;
+    // LayerNorm inputs with K a multiple of 128 up to 1280 (every Whisper width): one warp per
+    // row loads the row straight into registers (all loads in flight), reduces mean and
+    // variance there, and writes the normalised row once
+    constexpr int kLnF4 = 10;  // float4 per lane
+    const bool embed_f16 = a.in_mode == IN_EMBED_LN && a.E.type == WT_F16;
+    if ((a.in_mode == IN_LN || embed_f16) && K % 128 == 0 && K <= 128 * kLnF4) {
+        const int nf4 = K / 128;
+        for (int mm = warp; mm < MT; mm += kGemvThreads / 32) {
+            float4 *dst = reinterpret_cast<float4 *>(act_s + (size_t)mm * K);
+            const int m = m0 + mm;
+            if (m >= a.M) {
+                for (int c = lane; c < K4; c += 32) dst[c] = make_float4(0.f, 0.f, 0.f, 0.f);
+                continue;
+            }
+            float4 v[kLnF4];
+            if (a.in_mode == IN_LN) {
+                const float4 *src = reinterpret_cast<const float4 *>(a.act + (size_t)m * K);
+#pragma unroll
+                for (int j = 0; j < kLnF4; ++j) v[j] = j < nf4 ? src[lane + 32 * j] : make_float4(0.f, 0.f, 0.f, 0.f);
+            } else {  // x = E[tok] + P[pos] (WhisperDecoder.java:66-80), kept in x_out by block 0
+                const int tok = tok_s ? tok_s[m] : a.tok[m], pos = pos_s ? pos_s[m] : a.pos[m];
+                const uint2 *e = reinterpret_cast<const uint2 *>(a.E.h + (size_t)tok * K);
+                const float4 *pe = reinterpret_cast<const float4 *>(a.pos_emb + (size_t)pos * K);
+                uint2 eu[kLnF4];
+#pragma unroll
+                for (int j = 0; j < kLnF4; ++j) {
+                    eu[j] = j < nf4 ? e[lane + 32 * j] : make_uint2(0u, 0u);
+                    v[j] = j < nf4 ? pe[lane + 32 * j] : make_float4(0.f, 0.f, 0.f, 0.f);
+                }
+#pragma unroll
+                for (int j = 0; j < kLnF4; ++j) {
+                    const float2 lo = __half22float2(*reinterpret_cast<const __half2 *>(&eu[j].x));
+                    const float2 hi = __half22float2(*reinterpret_cast<const __half2 *>(&eu[j].y));
+                    v[j] = make_float4(lo.x + v[j].x, lo.y + v[j].y, hi.x + v[j].z, hi.y + v[j].w);
+                    if (j < nf4 && blockIdx.x == 0 && a.x_out)
+                        reinterpret_cast<float4 *>(a.x_out)[(size_t)m * K4 + lane + 32 * j] = v[j];
+                }
+            }
+            // Tensor.layerNorm (Tensor.java:592-619): two-pass mean / variance, eps 1e-5,
+            // invStd = 1 / sqrt(var / n + eps), y = (x - mean) * invStd * g + b.
+            float s = 0.f;
+#pragma unroll
+            for (int j = 0; j < kLnF4; ++j)
+                if (j < nf4) s += (v[j].x + v[j].y) + (v[j].z + v[j].w);
+            const float mean = warp_sum(s) / (float)K;
+            float v2 = 0.f;
+#pragma unroll
+            for (int j = 0; j < kLnF4; ++j)
+                if (j < nf4) {
+                    const float dx = v[j].x - mean, dy = v[j].y - mean, dz = v[j].z - mean, dw = v[j].w - mean;
+                    v2 += (dx * dx + dy * dy) + (dz * dz + dw * dw);
+                }
+            const float inv_std = 1.0f / sqrtf(warp_sum(v2) / (float)K + 1e-5f);
+            const float4 *g4 = reinterpret_cast<const float4 *>(ln_s);
+            const float4 *b4 = reinterpret_cast<const float4 *>(ln_s + K);
+#pragma unroll
+            for (int j = 0; j < kLnF4; ++j)
+                if (j < nf4) {
+                    const int c = lane + 32 * j;
+                    const float4 g = g4[c], b = b4[c];
+                    dst[c] = make_float4((v[j].x - mean) * inv_std * g.x + b.x, (v[j].y - mean) * inv_std * g.y + b.y,
+                                         (v[j].z - mean) * inv_std * g.z + b.z, (v[j].w - mean) * inv_std * g.w + b.w);
+                }
+        }
+        return;
+    }
     if (a.in_mode == IN_EMBED_LN) {
         const bool f16 = a.E.type == WT_F16;
         for (int i0 = threadIdx.x; i0 < total; i0 += kGemvThreads * 8) {
@@ -131,15 +197,16 @@ __device__ void load_activations(const GemvArgs &a, int m0, int K, float *act_s,
         // rows m0.. are contiguous in `act`: one flat copy of the live rows (rows past M: zero)
         const int live = (a.M - m0 < MT ? a.M - m0 : MT) * K4;
         const float4 *src = reinterpret_cast<const float4 *>(a.act) + (size_t)m0 * K4;
-        for (int i0 = threadIdx.x; i0 < total; i0 += kGemvThreads * 8) {
-            float4 v[8];
+        constexpr int kB = 16;  // 16 x 16 B in flight per thread: 64 KB per block per round trip
+        for (int i0 = threadIdx.x; i0 < total; i0 += kGemvThreads * kB) {
+            float4 v[kB];
 #pragma unroll
-            for (int j = 0; j < 8; ++j) {
+            for (int j = 0; j < kB; ++j) {
                 const int i = i0 + kGemvThreads * j;
                 v[j] = i < live ? src[i] : make_float4(0.f, 0.f, 0.f, 0.f);
             }
 #pragma unroll
-            for (int j = 0; j < 8; ++j)
+            for (int j = 0; j < kB; ++j)
                 if (i0 + kGemvThreads * j < total) reinterpret_cast<float4 *>(act_s)[i0 + kGemvThreads * j] = v[j];
         }
     }
@@ -502,6 +569,9 @@ static cudaError_t launch_gemv_r(const GemvArgs &a, const GemvLaunch &L, int blo
     // few rows per block: one row per warp keeps all warps busy; many rows: 4 rows share
     // each activation read
     if (L.rows_per_block <= 8) return launch_gemv_t<MT, 1, WT>(a, L, blocks, s, pdl);
+    if constexpr (MT <= 2) {  // > 32 rows: 8 rows per warp keeps every row group within one round
+        if (L.rows_per_block > 32) return launch_gemv_t<MT, 8, WT>(a, L, blocks, s, pdl);
+    }
     if constexpr (MT <= 4) return launch_gemv_t<MT, 4, WT>(a, L, blocks, s, pdl);
     else
     return launch_gemv_t<MT, 2, WT>(a, L, blocks, s, pdl);
@@ -708,6 +778,8 @@ static cudaError_t prepare_wt() {
 #define W4J_SET_MT(MT)                  \
     W4J_SET(k_gemv<MT, 1, WT>);         \
     W4J_SET(k_gemv<MT, (MT <= 4 ? 4 : 2), WT>)
+    W4J_SET(k_gemv<1, 8, WT>);
+    W4J_SET(k_gemv<2, 8, WT>);
     W4J_SET_MT(1);
     W4J_SET_MT(2);
     W4J_SET_MT(3);

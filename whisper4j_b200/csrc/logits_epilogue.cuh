@@ -4,7 +4,8 @@
 
 namespace w4j {
 
-constexpr int kLaneTopK = 9;  // per-lane candidate list: beam + 1 <= 9 (beam <= 8)
+constexpr int kLaneTopK = 9;   // candidates per block: beam + 1 <= 9 (beam <= 8)
+constexpr int kRowRegs = 16;   // row elements per lane held in registers (blocks of <= 512 rows)
 
 __device__ __forceinline__ bool logit_better(float v1, int i1, float v2, int i2) {
     return v1 > v2 || (v1 == v2 && i1 < i2);
@@ -64,92 +65,125 @@ for (int mm = warp; mm < MT; mm += blockDim.x / 32) {
         }
         if (a.masked_out)
             for (int i = lane; i < n; i += 32) a.masked_out[(size_t)m * a.V + lo + i] = row[i];
-        // one pass: running max with its first index, sum of exp rescaled as the max grows,
-        // and (beam search) a sorted per-lane top-k list (value desc, index asc)
         const int K = a.topk;
-        float bv = -INFINITY, sm = 0.f;
-        int bi = INT_MAX;
-        float tv[kLaneTopK];
-        int ti[kLaneTopK];
-#pragma unroll
-        for (int j = 0; j < kLaneTopK; ++j) {
-            tv[j] = -INFINITY;
-            ti[j] = INT_MAX;
-        }
-        for (int i = lane; i < n; i += 32) {
-            const float v = row[i];
-            if (v == -INFINITY) continue;
-            const int id = lo + i;
-            if (logit_better(v, id, bv, bi)) {
-                sm = (bv == -INFINITY ? 0.f : sm * __expf(bv - v)) + 1.f;
-                bv = v;
-                bi = id;
-            } else {
-                sm += __expf(v - bv);
-            }
-            if (K > 0) {  // insertion into the sorted list (the displaced tail moves down one slot)
-                float cv = v;
-                int ci = id;
-#pragma unroll
-                for (int j = 0; j < kLaneTopK; ++j) {
-                    if (j < K && logit_better(cv, ci, tv[j], ti[j])) {
-                        const float xv = tv[j];
-                        const int xi = ti[j];
-                        tv[j] = cv;
-                        ti[j] = ci;
-                        cv = xv;
-                        ci = xi;
-                    }
-                }
-            }
-        }
-        // warp: max / first argmax, then the sums relative to it
-        float wv = bv;
-        int wi = bi;
-#pragma unroll
-        for (int o = 16; o > 0; o >>= 1) {
-            const float ov = __shfl_xor_sync(0xffffffffu, wv, o);
-            const int oi = __shfl_xor_sync(0xffffffffu, wi, o);
-            if (logit_better(ov, oi, wv, wi)) {
-                wv = ov;
-                wi = oi;
-            }
-        }
-        float ws = (bv == -INFINITY) ? 0.f : sm * __expf(bv - wv);
-        ws = warp_sum(ws);
         float *pp = a.part + ((size_t)m * P + blockIdx.x) * kPartStride;
-        if (lane == 0) {
-            pp[0] = wv;
-            pp[1] = wv == -INFINITY ? 0.f : ws;
-            pp[2] = __int_as_float(wi == INT_MAX ? lo : wi);
-        }
-        // top-k of the block: k rounds of a warp argmax over the lanes' list heads; the lane
-        // whose head won shifts its list.  Unfilled entries: (-inf, 0).
-        for (int k = 0; k < K; ++k) {
-            float hv = tv[0];
-            int hi2 = ti[0];
+        if (n <= 32 * kRowRegs) {
+            // the row in registers (lane + 32 j: ids ascending in j), then every reduction there
+            float v[kRowRegs];
+#pragma unroll
+            for (int j = 0; j < kRowRegs; ++j) v[j] = lane + 32 * j < n ? row[lane + 32 * j] : -INFINITY;
+            float bv = -INFINITY;
+            int bj = -1;
+#pragma unroll
+            for (int j = 0; j < kRowRegs; ++j)
+                if (v[j] > bv) {  // strict: the first index of the lane's maximum
+                    bv = v[j];
+                    bj = j;
+                }
+            float wv = bv;
+            int wi = bj < 0 ? INT_MAX : lo + lane + 32 * bj;
 #pragma unroll
             for (int o = 16; o > 0; o >>= 1) {
-                const float ov = __shfl_xor_sync(0xffffffffu, hv, o);
-                const int oi = __shfl_xor_sync(0xffffffffu, hi2, o);
-                if (logit_better(ov, oi, hv, hi2)) {
-                    hv = ov;
-                    hi2 = oi;
+                const float ov = __shfl_xor_sync(0xffffffffu, wv, o);
+                const int oi = __shfl_xor_sync(0xffffffffu, wi, o);
+                if (logit_better(ov, oi, wv, wi)) {
+                    wv = ov;
+                    wi = oi;
+                }
+            }
+            float sm = 0.f;
+            if (wv != -INFINITY)
+#pragma unroll
+                for (int j = 0; j < kRowRegs; ++j) sm += __expf(v[j] - wv);  // exp(-inf) = 0
+            sm = warp_sum(sm);
+            if (lane == 0) {
+                pp[0] = wv;
+                pp[1] = sm;
+                pp[2] = __int_as_float(wi == INT_MAX ? lo : wi);
+            }
+            // top-k of the block (value desc, index asc): k rounds of lane-best then warp-best;
+            // the winning lane drops its element.  Unfilled entries: (-inf, 0).
+            for (int k = 0; k < K; ++k) {
+                float cv = -INFINITY;
+                int cj = -1;
+#pragma unroll
+                for (int j = 0; j < kRowRegs; ++j)
+                    if (v[j] > cv) {
+                        cv = v[j];
+                        cj = j;
+                    }
+                const int ci = cj < 0 ? INT_MAX : lo + lane + 32 * cj;
+                float hv = cv;
+                int hi2 = ci;
+#pragma unroll
+                for (int o = 16; o > 0; o >>= 1) {
+                    const float ov = __shfl_xor_sync(0xffffffffu, hv, o);
+                    const int oi = __shfl_xor_sync(0xffffffffu, hi2, o);
+                    if (logit_better(ov, oi, hv, hi2)) {
+                        hv = ov;
+                        hi2 = oi;
+                    }
+                }
+                if (lane == 0) {
+                    pp[4 + k] = hi2 == INT_MAX ? -INFINITY : hv;
+                    pp[4 + K + k] = __int_as_float(hi2 == INT_MAX ? 0 : hi2);
+                }
+                if (hi2 != INT_MAX && ci == hi2)  // ids are unique: exactly one lane owns it
+#pragma unroll
+                    for (int j = 0; j < kRowRegs; ++j)
+                        if (j == cj) v[j] = -INFINITY;
+            }
+            continue;
+        }
+        // rows longer than the register budget: the same reductions over shared memory
+        float bv = -INFINITY;
+        int bi = INT_MAX;
+        for (int i = lane; i < n; i += 32)
+            if (logit_better(row[i], lo + i, bv, bi)) {
+                bv = row[i];
+                bi = lo + i;
+            }
+#pragma unroll
+        for (int o = 16; o > 0; o >>= 1) {
+            const float ov = __shfl_xor_sync(0xffffffffu, bv, o);
+            const int oi = __shfl_xor_sync(0xffffffffu, bi, o);
+            if (logit_better(ov, oi, bv, bi)) {
+                bv = ov;
+                bi = oi;
+            }
+        }
+        float sm = 0.f;
+        if (bv != -INFINITY)
+            for (int i = lane; i < n; i += 32) sm += __expf(row[i] - bv);
+        sm = warp_sum(sm);
+        if (lane == 0) {
+            pp[0] = bv;
+            pp[1] = sm;
+            pp[2] = __int_as_float(bi == INT_MAX ? lo : bi);
+        }
+        for (int k = 0; k < K; ++k) {
+            float kv = -INFINITY;
+            int ki = INT_MAX;
+            for (int i = lane; i < n; i += 32)
+                if (row[i] != -INFINITY && logit_better(row[i], lo + i, kv, ki)) {
+                    kv = row[i];
+                    ki = lo + i;
+                }
+#pragma unroll
+            for (int o = 16; o > 0; o >>= 1) {
+                const float ov = __shfl_xor_sync(0xffffffffu, kv, o);
+                const int oi = __shfl_xor_sync(0xffffffffu, ki, o);
+                if (logit_better(ov, oi, kv, ki)) {
+                    kv = ov;
+                    ki = oi;
                 }
             }
             if (lane == 0) {
-                pp[4 + k] = hi2 == INT_MAX ? -INFINITY : hv;
-                pp[4 + K + k] = __int_as_float(hi2 == INT_MAX ? 0 : hi2);
+                pp[4 + k] = kv;
+                pp[4 + K + k] = __int_as_float(ki == INT_MAX ? 0 : ki);
             }
-            if (hi2 != INT_MAX && ti[0] == hi2) {  // ids are unique: exactly one lane owns it
-#pragma unroll
-                for (int j = 0; j + 1 < kLaneTopK; ++j) {
-                    tv[j] = tv[j + 1];
-                    ti[j] = ti[j + 1];
-                }
-                tv[kLaneTopK - 1] = -INFINITY;
-                ti[kLaneTopK - 1] = INT_MAX;
-            }
+            if (ki != INT_MAX && ki - lo >= 0 && ki - lo < n && lane == ((ki - lo) & 31)) row[ki - lo] = -INFINITY;
+            __syncwarp();
         }
     }
 }

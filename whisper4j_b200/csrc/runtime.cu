@@ -93,9 +93,6 @@ struct w4j_ctx {
     std::vector<char> has_xa;
     // activations / scratch
     float *x = nullptr, *q = nullptr, *attn = nullptr, *h = nullptr, *xa_stage = nullptr;
-    float *attn_part = nullptr;
-    unsigned *attn_ctr = nullptr;
-    int attn_split_max = 1;
     int n_parts = 0;
     float *logit_part = nullptr, *ns_part = nullptr, *ns_value = nullptr;
     float *masked = nullptr;  // M_max x V (sampling)
@@ -229,10 +226,6 @@ extern "C" int w4j_ctx_create(const w4j_dims *dims, int device, int max_streams,
     // activations
     if ((rc = dalloc(c, &c->x, M * d)) || (rc = dalloc(c, &c->q, M * d)) || (rc = dalloc(c, &c->attn, M * d)) ||
         (rc = dalloc(c, &c->h, M * 4 * d)) || (rc = dalloc(c, &c->xa_stage, A * d)))
-        return fail(rc);
-    c->attn_split_max = std::max((int)((C + 63) / 64), (int)((A + 63) / 64));
-    if ((rc = dalloc(c, &c->attn_part, M * H * c->attn_split_max * kAttnRec)) ||
-        (rc = dalloc(c, &c->attn_ctr, M * H)))
         return fail(rc);
     c->n_parts = logits_parts_for(c->V, c->sm_count);
     if ((rc = dalloc(c, &c->logit_part, M * c->n_parts * kPartStride)) || (rc = dalloc(c, &c->ns_part, M * c->n_parts * 2)) ||
@@ -583,8 +576,6 @@ static int run_layers(w4j_ctx *c, const PassArgs &pa, long long &launches) {
         sa.nq = 1;
         sa.groups = pa.M;
         sa.nsplit = self_split;
-        sa.part = c->attn_part;
-        sa.counters = c->attn_ctr;
         sa.out = c->attn;
         sa.active = pa.active;
         sa.err = c->st.err;
@@ -630,8 +621,6 @@ static int run_layers(w4j_ctx *c, const PassArgs &pa, long long &launches) {
         ca.nq = pa.nq;
         ca.groups = pa.groups;
         ca.nsplit = cross_split;
-        ca.part = c->attn_part;
-        ca.counters = c->attn_ctr;
         ca.out = c->attn;
         ca.active = pa.group_active;
         ca.err = c->st.err;

@@ -20,7 +20,6 @@ constexpr int kPartStride = 4 + 2 * kMaxTopK;       // floats per logits partial
 constexpr int kMaxRanges = 4;                       // masked id ranges per sequence
 constexpr int kGemvThreads = 256;
 constexpr int kAttnThreads = 256;
-constexpr int kAttnRec = 68;                       // floats per attention split record: m, l, pad, o[64]
 constexpr int kAttnKeyTile = 128;
 
 enum WType : int { WT_F16 = 1, WT_Q8 = 8 };
@@ -83,8 +82,6 @@ struct AttnArgs {
     int nq = 1;                        // queries per group (cross: beams of one stream)
     int groups = 0;
     int nsplit = 1;
-    float *part = nullptr;             // [groups*nq][n_head][nsplit][kAttnRec]
-    unsigned *counters = nullptr;      // [groups][n_head], zero between uses
     float *out = nullptr;              // [groups*nq][d]
     const int *active = nullptr;       // [groups]
     int *err = nullptr;                // device error word
@@ -256,7 +253,7 @@ inline cudaError_t allow_dynamic_smem(Kern kern) {
 // ---------------------------------------------------------------------------
 cudaError_t launch_gemv(const GemvArgs &a, cudaStream_t s, bool pdl);
 cudaError_t launch_attn(const AttnArgs &a, cudaStream_t s, bool pdl);
-int attn_max_splits(int nq);  // splits whose partials fit the combine's shared-memory staging
+int attn_max_splits(int nq);  // key splits of one attention launch (one thread-block cluster)
 cudaError_t launch_logits(const LogitsArgs &a, int n_parts, cudaStream_t s, bool pdl);
 int logits_parts_for(int V, int sm_count);
 size_t logits_smem_bytes(int M, int V, int d, int n_parts);
