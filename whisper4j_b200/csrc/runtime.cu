@@ -1224,7 +1224,9 @@ extern "C" int w4j_op_linear(w4j_ctx *c, const float *x, int M, int K, const voi
     if (w_type == W4J_GGML_Q8_0 && K % 32) return set_err(W4J_ERR_ARG, "Q8_0 needs K % 32 == 0");
     if ((ln_g == nullptr) != (ln_b == nullptr)) return set_err(W4J_ERR_ARG, "LayerNorm needs both gamma and beta");
     if (epilogue < 0 || epilogue > 2) return set_err(W4J_ERR_ARG, "epilogue must be 0, 1 or 2");
-    if ((size_t)std::min(M, 16) * K * 4 > 160 * 1024) return set_err(W4J_ERR_ARG, "K too large");
+    // one weight row, one activation row and the LayerNorm parameters must fit a block's shared
+    // memory (larger M runs in passes)
+    if ((size_t)K * (2 + 3 * 4) > 200 * 1024) return set_err(W4J_ERR_ARG, "K too large");
     CUDA_TRY(cudaSetDevice(c->device));
     GemvArgs g;
     g.W.N = N;
