@@ -32,6 +32,26 @@ __device__ __forceinline__ void cp_async16(void *smem, const void *gmem) {
     asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" ::"r"(s), "l"(gmem) : "memory");
 }
 __device__ __forceinline__ void cp_async_wait_all() { asm volatile("cp.async.wait_all;" ::: "memory"); }
+// warp-level tensor-core tiles (m16n8k16, f16 inputs, f32 accumulation) and their fragments
+__device__ __forceinline__ void ldsm_x4(uint32_t (&r)[4], const void *p) {
+    asm volatile("ldmatrix.sync.aligned.m8n8.x4.shared.b16 {%0,%1,%2,%3}, [%4];"
+                 : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3])
+                 : "r"(smem_u32(p)));
+}
+__device__ __forceinline__ void ldsm_x4_t(uint32_t (&r)[4], const void *p) {
+    asm volatile("ldmatrix.sync.aligned.m8n8.x4.trans.shared.b16 {%0,%1,%2,%3}, [%4];"
+                 : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3])
+                 : "r"(smem_u32(p)));
+}
+__device__ __forceinline__ void ldsm_x2(uint32_t (&r)[2], const void *p) {
+    asm volatile("ldmatrix.sync.aligned.m8n8.x2.shared.b16 {%0,%1}, [%2];" : "=r"(r[0]), "=r"(r[1]) : "r"(smem_u32(p)));
+}
+__device__ __forceinline__ void mma_16816(float (&c)[4], const uint32_t (&a)[4], const uint32_t (&b)[2]) {
+    asm volatile(
+        "mma.sync.aligned.m16n8k16.row.col.f32.f16.f16.f32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, {%0,%1,%2,%3};"
+        : "+f"(c[0]), "+f"(c[1]), "+f"(c[2]), "+f"(c[3])
+        : "r"(a[0]), "r"(a[1]), "r"(a[2]), "r"(a[3]), "r"(b[0]), "r"(b[1]));
+}
 __device__ __forceinline__ void cluster_sync() {
     asm volatile("barrier.cluster.arrive.release.aligned;\n\tbarrier.cluster.wait.acquire.aligned;" ::: "memory");
 }
@@ -48,9 +68,11 @@ __device__ __forceinline__ float ld_cluster_f32(const float *local, unsigned ran
 template <int NQ>
 __global__ void __launch_bounds__(kAttnThreads) k_attn(AttnArgs a) {
     extern __shared__ __align__(16) __half skv[];  // [tiles][K tile | V tile]; then reused for the reduction
-    __shared__ __align__(16) float sq[NQ][kHeadDim];
-    __shared__ float sp[NQ][kAttnKeyTile];
-    __shared__ float s_m[NQ], s_l[NQ], s_alpha[NQ];
+    constexpr int kQPad = kHeadDim + 8, kPPad = kAttnKeyTile + 8;  // halves per row (16-byte aligned rows)
+    __shared__ __align__(16) __half qh[8][kQPad];        // queries (f16; rows >= NQ zero): MMA B operand
+    __shared__ __align__(16) __half ps[8][kPPad];        // probabilities of the tile (f16): MMA B operand
+    __shared__ float w_max[kWarps][8], w_sum[kWarps][8];
+    __shared__ float s_m[8], s_l[8];
     __shared__ __align__(16) float s_part[NQ][kHeadDim];  // this split's unnormalised output (cluster mode)
 
     const int split = blockIdx.x, head = blockIdx.y, group = blockIdx.z;
@@ -110,110 +132,147 @@ __global__ void __launch_bounds__(kAttnThreads) k_attn(AttnArgs a) {
     pdl_wait();
     for (int ti = 0; ti < nt; ++ti)  // the newest self row (written by the previous kernel), or everything
         stage(ti, j0 + ti * kAttnKeyTile, min(kAttnKeyTile, j1 - j0 - ti * kAttnKeyTile), pre ? 2 : 0);
-    if (tid < NQ * kHeadDim / 4) {  // queries: one 16-byte load per thread
+    if (tid < 8 * kHeadDim / 4) {  // queries as f16, one 16-byte load per thread; rows >= NQ are zero
         const int i = tid / (kHeadDim / 4), c = tid % (kHeadDim / 4);
-        reinterpret_cast<float4 *>(sq[i])[c] =
-            reinterpret_cast<const float4 *>(a.q + (size_t)(group * NQ + i) * a.d + head * kHeadDim)[c];
+        float4 v = make_float4(0.f, 0.f, 0.f, 0.f);
+        if (i < NQ) v = reinterpret_cast<const float4 *>(a.q + (size_t)(group * NQ + i) * a.d + head * kHeadDim)[c];
+        const __half2 h0 = __floats2half2_rn(v.x, v.y), h1 = __floats2half2_rn(v.z, v.w);
+        *reinterpret_cast<uint2 *>(&qh[i][4 * c]) =
+            make_uint2(*reinterpret_cast<const uint32_t *>(&h0), *reinterpret_cast<const uint32_t *>(&h1));
     }
-    if (tid < NQ) {
+    if (tid < 8) {
         s_m[tid] = -INFINITY;
         s_l[tid] = 0.f;
     }
-    // output accumulators: warp w sums the keys j = w (mod kWarps) of every tile for dims
-    // 2*lane, 2*lane+1 of every query; the warp shares are added at the end
-    float ow[NQ][2];
+    // warp w owns keys [16 w, 16 w + 16) of every tile; MMA fragment coordinates
+    const int g = lane >> 2, tq = lane & 3;
+    // O^T accumulators: 4 tiles of 16 dims x 8 queries (c0/c1: dim 16 mt + g, queries 2 tq / 2 tq + 1;
+    // c2/c3: dim 16 mt + g + 8)
+    float of[4][4];
 #pragma unroll
-    for (int i = 0; i < NQ; ++i) ow[i][0] = ow[i][1] = 0.f;
+    for (int mt = 0; mt < 4; ++mt) of[mt][0] = of[mt][1] = of[mt][2] = of[mt][3] = 0.f;
+    // V rows past the keys of a partial tile are zeroed: the P.V product multiplies them by
+    // zero probabilities, which must not meet stale (possibly non-finite) shared memory
+    for (int ti = 0; ti < nt; ++ti) {
+        const int nk = min(kAttnKeyTile, j1 - j0 - ti * kAttnKeyTile);
+        __half *tv = skv + (size_t)ti * kTileHalves + kAttnKeyTile * kRowPad;
+        for (int c = tid; c < (kAttnKeyTile - nk) * 8; c += kAttnThreads)
+            *reinterpret_cast<uint4 *>(&tv[(nk + (c >> 3)) * kRowPad + (c & 7) * 8]) = make_uint4(0u, 0u, 0u, 0u);
+    }
     cp_async_wait_all();
     __syncthreads();
 
     for (int ti = 0; ti < nt; ++ti) {
         const int nk = min(kAttnKeyTile, j1 - j0 - ti * kAttnKeyTile);
         const __half *sk = skv + (size_t)ti * kTileHalves, *sv = sk + kAttnKeyTile * kRowPad;
-        {  // scores: two threads per key, 32 dims each
-            const int key = tid >> 1, hf = tid & 1;
-            float acc[NQ];
+        const int kb = 16 * warp;  // this warp's first key of the tile
+        // scores S^T (16 keys x 8 queries) = K (16 x 64) . Q^T (64 x 8): four k16 steps
+        float sc[4] = {0.f, 0.f, 0.f, 0.f};
+        if (kb < nk) {
 #pragma unroll
-            for (int i = 0; i < NQ; ++i) acc[i] = 0.f;
-            if (key < nk) {
-#pragma unroll
-                for (int c = 0; c < 4; ++c) {
-                    const uint4 u = *reinterpret_cast<const uint4 *>(&sk[key * kRowPad + hf * 32 + c * 8]);
-                    const __half2 *h = reinterpret_cast<const __half2 *>(&u);
-                    float kf[8];
-#pragma unroll
-                    for (int j = 0; j < 4; ++j) {
-                        const float2 f = __half22float2(h[j]);
-                        kf[2 * j] = f.x;
-                        kf[2 * j + 1] = f.y;
-                    }
-#pragma unroll
-                    for (int i = 0; i < NQ; ++i) {
-                        const float4 q0 = *reinterpret_cast<const float4 *>(&sq[i][hf * 32 + c * 8]);
-                        const float4 q1 = *reinterpret_cast<const float4 *>(&sq[i][hf * 32 + c * 8 + 4]);
-                        acc[i] = fmaf(q0.x, kf[0], acc[i]);
-                        acc[i] = fmaf(q0.y, kf[1], acc[i]);
-                        acc[i] = fmaf(q0.z, kf[2], acc[i]);
-                        acc[i] = fmaf(q0.w, kf[3], acc[i]);
-                        acc[i] = fmaf(q1.x, kf[4], acc[i]);
-                        acc[i] = fmaf(q1.y, kf[5], acc[i]);
-                        acc[i] = fmaf(q1.z, kf[6], acc[i]);
-                        acc[i] = fmaf(q1.w, kf[7], acc[i]);
-                    }
-                }
+            for (int kk = 0; kk < 4; ++kk) {
+                uint32_t af[4], bf[2];
+                ldsm_x4(af, &sk[(kb + (lane & 15)) * kRowPad + 16 * kk + (lane >> 4) * 8]);
+                ldsm_x2(bf, &qh[lane & 7][16 * kk + ((lane >> 3) & 1) * 8]);
+                mma_16816(sc, af, bf);
             }
+        }
+        // c0: (key kb+g, query 2tq), c1: (kb+g, 2tq+1), c2: (kb+g+8, 2tq), c3: (kb+g+8, 2tq+1)
+        const int q0 = 2 * tq, q1 = 2 * tq + 1;
+        const bool k0ok = kb + g < nk, k1ok = kb + g + 8 < nk;
+        sc[0] = (k0ok && q0 < NQ) ? sc[0] * scale : -INFINITY;
+        sc[1] = (k0ok && q1 < NQ) ? sc[1] * scale : -INFINITY;
+        sc[2] = (k1ok && q0 < NQ) ? sc[2] * scale : -INFINITY;
+        sc[3] = (k1ok && q1 < NQ) ? sc[3] * scale : -INFINITY;
+        // online softmax over the tile's keys, per query (lanes with the same tq share queries)
+        float mx0 = fmaxf(sc[0], sc[2]), mx1 = fmaxf(sc[1], sc[3]);
 #pragma unroll
-            for (int i = 0; i < NQ; ++i) acc[i] += __shfl_xor_sync(0xffffffffu, acc[i], 1);
-            if (key < nk && hf == 0)
-#pragma unroll
-                for (int i = 0; i < NQ; ++i) sp[i][key] = acc[i] * scale;
+        for (int o = 4; o < 32; o <<= 1) {
+            mx0 = fmaxf(mx0, __shfl_xor_sync(0xffffffffu, mx0, o));
+            mx1 = fmaxf(mx1, __shfl_xor_sync(0xffffffffu, mx1, o));
+        }
+        if (g == 0) {
+            w_max[warp][q0] = mx0;
+            w_max[warp][q1] = mx1;
         }
         __syncthreads();
-        // online softmax bookkeeping: warp i takes query i
-        for (int i = warp; i < NQ; i += kWarps) {
-            float mx = -INFINITY;
-            for (int j = lane; j < nk; j += 32) mx = fmaxf(mx, sp[i][j]);
-            mx = warp_max(mx);
-            const float m_old = s_m[i];
-            const float m_new = fmaxf(m_old, mx);
-            float sum = 0.f;
-            for (int j = lane; j < nk; j += 32) {
-                const float e = __expf(sp[i][j] - m_new);
-                sp[i][j] = e;
-                sum += e;
-            }
-            sum = warp_sum(sum);
-            if (lane == 0) {
-                const float alpha = m_old == -INFINITY ? 0.f : __expf(m_old - m_new);
-                s_alpha[i] = alpha;
-                s_l[i] = s_l[i] * alpha + sum;
-                s_m[i] = m_new;
+        float tm0 = -INFINITY, tm1 = -INFINITY;
+#pragma unroll
+        for (int w = 0; w < kWarps; ++w) {
+            tm0 = fmaxf(tm0, w_max[w][q0]);
+            tm1 = fmaxf(tm1, w_max[w][q1]);
+        }
+        const float mo0 = s_m[q0], mo1 = s_m[q1];
+        const float mn0 = fmaxf(mo0, tm0), mn1 = fmaxf(mo1, tm1);
+        const float p0 = sc[0] == -INFINITY ? 0.f : __expf(sc[0] - mn0);
+        const float p1 = sc[1] == -INFINITY ? 0.f : __expf(sc[1] - mn1);
+        const float p2 = sc[2] == -INFINITY ? 0.f : __expf(sc[2] - mn0);
+        const float p3 = sc[3] == -INFINITY ? 0.f : __expf(sc[3] - mn1);
+        float sm0 = p0 + p2, sm1 = p1 + p3;
+#pragma unroll
+        for (int o = 4; o < 32; o <<= 1) {
+            sm0 += __shfl_xor_sync(0xffffffffu, sm0, o);
+            sm1 += __shfl_xor_sync(0xffffffffu, sm1, o);
+        }
+        if (g == 0) {
+            w_sum[warp][q0] = sm0;
+            w_sum[warp][q1] = sm1;
+        }
+        // P^T of this warp's keys for the P.V step (read back only by this warp)
+        ps[q0][kb + g] = __float2half_rn(p0);
+        ps[q1][kb + g] = __float2half_rn(p1);
+        ps[q0][kb + g + 8] = __float2half_rn(p2);
+        ps[q1][kb + g + 8] = __float2half_rn(p3);
+        const float al0 = mo0 == -INFINITY ? 0.f : __expf(mo0 - mn0);
+        const float al1 = mo1 == -INFINITY ? 0.f : __expf(mo1 - mn1);
+#pragma unroll
+        for (int mt = 0; mt < 4; ++mt) {
+            of[mt][0] *= al0;
+            of[mt][1] *= al1;
+            of[mt][2] *= al0;
+            of[mt][3] *= al1;
+        }
+        __syncwarp();
+        // O^T (16 dims x 8 queries, 4 tiles) += V^T (16 dims x 16 keys) . P^T (16 keys x 8 queries)
+        if (kb < nk) {
+            uint32_t bf[2];
+            ldsm_x2(bf, &ps[lane & 7][kb + ((lane >> 3) & 1) * 8]);
+#pragma unroll
+            for (int mt = 0; mt < 4; ++mt) {
+                uint32_t af[4];
+                ldsm_x4_t(af, &sv[(kb + (lane & 7) + ((lane >> 4) & 1) * 8) * kRowPad + 16 * mt + ((lane >> 3) & 1) * 8]);
+                mma_16816(of[mt], af, bf);
             }
         }
-        __syncthreads();
-        // o = o * alpha + p . V  (this warp's keys, two dims per lane)
+        __syncthreads();  // w_max / w_sum read; s_m read by every thread
+        if (tid < 8) {    // running max and denominator per query
+            float tot = 0.f;
 #pragma unroll
-        for (int i = 0; i < NQ; ++i) {
-            const float al = s_alpha[i];
-            ow[i][0] *= al;
-            ow[i][1] *= al;
-        }
-        for (int j = warp; j < nk; j += kWarps) {
-            const float2 v = __half22float2(*reinterpret_cast<const __half2 *>(&sv[j * kRowPad + 2 * lane]));
+            for (int w = 0; w < kWarps; ++w) tot += w_sum[w][tid];
+            const float mo = s_m[tid];
+            float tmx = -INFINITY;
 #pragma unroll
-            for (int i = 0; i < NQ; ++i) {
-                const float p = sp[i][j];
-                ow[i][0] = fmaf(p, v.x, ow[i][0]);
-                ow[i][1] = fmaf(p, v.y, ow[i][1]);
-            }
+            for (int w = 0; w < kWarps; ++w) tmx = fmaxf(tmx, w_max[w][tid]);
+            const float mn = fmaxf(mo, tmx);
+            s_l[tid] = s_l[tid] * (mo == -INFINITY ? 0.f : __expf(mo - mn)) + tot;
+            s_m[tid] = mn;
         }
         __syncthreads();
     }
     // add the warp shares (through the K/V tiles' shared memory, no longer needed)
     float *red = reinterpret_cast<float *>(skv);  // [kWarps][NQ][64]
 #pragma unroll
-    for (int i = 0; i < NQ; ++i)
-        *reinterpret_cast<float2 *>(&red[((size_t)warp * NQ + i) * kHeadDim + 2 * lane]) = make_float2(ow[i][0], ow[i][1]);
+    for (int mt = 0; mt < 4; ++mt) {
+        const int q0 = 2 * tq, q1 = 2 * tq + 1, d0 = 16 * mt + g;
+        if (q0 < NQ) {
+            red[((size_t)warp * NQ + q0) * kHeadDim + d0] = of[mt][0];
+            red[((size_t)warp * NQ + q0) * kHeadDim + d0 + 8] = of[mt][2];
+        }
+        if (q1 < NQ) {
+            red[((size_t)warp * NQ + q1) * kHeadDim + d0] = of[mt][1];
+            red[((size_t)warp * NQ + q1) * kHeadDim + d0 + 8] = of[mt][3];
+        }
+    }
     __syncthreads();
     constexpr int kPer = (NQ * kHeadDim + kAttnThreads - 1) / kAttnThreads;  // (query, dim) pairs per thread
     float o[kPer];
