@@ -95,7 +95,7 @@ struct LogitsTcLaunch {
     int tiles_total;  // ceil(V / 128)
     int ch;           // max rows of a block (tiles per block * 128)
     int n_stages;
-    unsigned b_off, tile_off, ln_off, bar_off;  // shared-memory layout (bytes)
+    unsigned b_off, tile_off, ln_off, mk_off, bar_off;  // shared-memory layout (bytes)
 };
 
 constexpr int kTileRows = 128, kKB = 64, kStageBytes = kTileRows * kKB * 2;
@@ -117,6 +117,11 @@ __global__ void __launch_bounds__(256, 1) k_logits_tc(LogitsArgs a, const __grid
     unsigned char *bop = smem + L.b_off;  // [KB][NU rows][128 B]
     float *tile = reinterpret_cast<float *>(smem + L.tile_off);
     float *ln_s = reinterpret_cast<float *>(smem + L.ln_off);
+    int2 *mk_rg = reinterpret_cast<int2 *>(smem + L.mk_off);  // 16-byte aligned: the int2 array first
+    int *mk_act = reinterpret_cast<int *>(mk_rg + (size_t)a.M * kMaxRanges);
+    int *mk_nr = mk_act + a.M, *mk_cnt = mk_nr + a.M;
+    int *mk_dyn = mk_cnt + a.M;
+    int *mk_stat = mk_dyn + (size_t)a.M * kDynStage;
     uint64_t *full = reinterpret_cast<uint64_t *>(smem + L.bar_off);
     uint64_t *empty = full + NS;
     uint64_t *accf = empty + NS;  // [2]
@@ -148,6 +153,24 @@ __global__ void __launch_bounds__(256, 1) k_logits_tc(LogitsArgs a, const __grid
         tmem_relinquish();
     }
     for (int i = tid; i < 2 * d; i += blockDim.x) ln_s[i] = i < d ? a.ln_g[i] : a.ln_b[i - d];
+    // liveness and masks of the rows: written by the previous step's select kernel (an earlier
+    // graph launch) or by the mask initialisation that completed before this kernel started
+    if (a.active)
+        for (int i = tid; i < a.M; i += blockDim.x) mk_act[i] = a.active[i];
+    if (a.use_mask) {
+        const MaskArgs &mk = a.mask;
+        for (int i = tid; i < a.M; i += blockDim.x) {
+            mk_nr[i] = mk.n_ranges[i];
+            mk_cnt[i] = mk.dyn_count[i];
+        }
+        for (int i = tid; i < a.M * kMaxRanges; i += blockDim.x) mk_rg[i] = mk.ranges[i];
+        for (int i = tid; i < min(mk.n_static, kStatStage); i += blockDim.x) mk_stat[i] = mk.static_list[i];
+        __syncthreads();
+        for (int i = tid; i < a.M * kDynStage; i += blockDim.x) {
+            const int m = i / kDynStage, j = i - m * kDynStage;
+            if (j < mk_cnt[m]) mk_dyn[i] = mk.dyn_list[(size_t)m * mk.dyn_stride + j];
+        }
+    }
     // rows M..NU of the B operand are zero whatever the activations are
     for (int i = tid; i < (NU - a.M) * (d / 8); i += blockDim.x) {
         const int m = a.M + i / (d / 8), c = i % (d / 8);
@@ -284,7 +307,8 @@ __global__ void __launch_bounds__(256, 1) k_logits_tc(LogitsArgs a, const __grid
             const int m = i / (hi - lo), r = i - m * (hi - lo);
             a.raw_out[(size_t)m * a.V + lo + r] = tile[(size_t)m * L.ch + r];
         }
-    logits_rows_epilogue(a, tile, L.ch, a.M, 0, lo, hi, ok);
+    const MaskStage ms{mk_act, mk_nr, mk_rg, mk_cnt, mk_dyn, mk_stat};
+    logits_rows_epilogue(a, tile, L.ch, a.M, 0, lo, hi, ok, &ms);
     __syncthreads();
     if (!ok && tid == 0)  // let copies in flight land before the block's memory is reused
         for (int i = 0; i < NS; ++i) {
@@ -327,6 +351,12 @@ bool make_tmap_f16_rows(void *map_out, const void *base, int rows, int cols) {
               CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
 }
 
+// Staged masks: ranges (M x kMaxRanges int2), then active, n_ranges, dyn_count (M ints each),
+// dyn (M x kDynStage ints), static list (kStatStage ints); a multiple of 16 bytes.
+static size_t mask_stage_bytes(int M) {
+    return (((size_t)M * (3 + 2 * kMaxRanges + kDynStage) + kStatStage) * 4 + 15) & ~(size_t)15;
+}
+
 static bool plan_tc(int M, int V, int d, int P, int &nu, LogitsTcLaunch &L) {
     if (M < 1 || M > 32 || d % kKB != 0 || d > 1280) return false;
     nu = M <= 16 ? 16 : 32;
@@ -335,7 +365,8 @@ static bool plan_tc(int M, int V, int d, int P, int &nu, LogitsTcLaunch &L) {
     const size_t bbytes = (size_t)nu * d * 2;
     const size_t tbytes = (size_t)M * L.ch * 4;
     const size_t lnbytes = (size_t)2 * d * 4;
-    const size_t fixed = bbytes + tbytes + lnbytes + 256;
+    const size_t mkbytes = mask_stage_bytes(M);
+    const size_t fixed = bbytes + tbytes + lnbytes + mkbytes + 256;
     const size_t budget = 220 * 1024;
     if (fixed + 2 * kStageBytes > budget) return false;
     // 7 stages (112 KB) keep ~16 MB of the embedding in flight over the GPU, enough to cover
@@ -345,7 +376,8 @@ static bool plan_tc(int M, int V, int d, int P, int &nu, LogitsTcLaunch &L) {
     L.b_off = (unsigned)(L.n_stages * kStageBytes);  // 1024-byte aligned (stages are 16 KB)
     L.tile_off = L.b_off + (unsigned)bbytes;        // bbytes is a multiple of 2 KB
     L.ln_off = L.tile_off + (unsigned)((tbytes + 15) & ~(size_t)15);
-    L.bar_off = L.ln_off + (unsigned)lnbytes;
+    L.mk_off = L.ln_off + (unsigned)lnbytes;
+    L.bar_off = L.mk_off + (unsigned)mkbytes;
     return true;
 }
 

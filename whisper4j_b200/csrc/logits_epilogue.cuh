@@ -6,6 +6,19 @@ namespace w4j {
 
 constexpr int kLaneTopK = 9;   // candidates per block: beam + 1 <= 9 (beam <= 8)
 constexpr int kRowRegs = 16;   // row elements per lane held in registers (blocks of <= 512 rows)
+constexpr int kDynStage = 32;  // per-sequence masked ids staged in shared memory (more: read from global)
+constexpr int kStatStage = 128;
+
+// Shared-memory copy of the masks and liveness of the rows (staged before the grid wait by the
+// tensor-core kernel: the select kernel of the previous step wrote them).
+struct MaskStage {
+    const int *active;     // [M] (null: all live)
+    const int *n_ranges;   // [M]
+    const int2 *ranges;    // [M][kMaxRanges]
+    const int *dyn_count;  // [M]
+    const int *dyn;        // [M][kDynStage]
+    const int *stat;       // [min(n_static, kStatStage)]
+};
 
 __device__ __forceinline__ bool logit_better(float v1, int i1, float v2, int i2) {
     return v1 > v2 || (v1 == v2 && i1 < i2);
@@ -16,14 +29,14 @@ __device__ __forceinline__ bool logit_better(float v1, int i1, float v2, int i2)
 // the no-speech probability, the masks (suppress list, n-gram and timestamp rules), then max,
 // first argmax, sum of exp and the block's top-k candidates.  One warp per sequence.
 __device__ __forceinline__ void logits_rows_epilogue(const LogitsArgs &a, float *tile, int ch, int MT, int m0, int lo, int hi,
-                                     bool ok) {
+                                     bool ok, const MaskStage *ms = nullptr) {
     const int P = gridDim.x;
     const int nrows = hi - lo;
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
 for (int mm = warp; mm < MT; mm += blockDim.x / 32) {
         const int m = m0 + mm;
         if (m >= a.M || !ok) continue;
-        if (a.active && !a.active[m]) continue;
+        if (a.active && !(ms ? ms->active[m] : a.active[m])) continue;
         float *row = tile + (size_t)mm * ch;
         const int n = nrows;
         if (a.ns_token >= 0) {  // unmasked statistics of this row (no-speech probability)
@@ -43,8 +56,9 @@ for (int mm = warp; mm < MT; mm += blockDim.x / 32) {
         }
         if (a.use_mask) {
             const MaskArgs &mk = a.mask;
-            for (int r = 0; r < mk.n_ranges[m]; ++r) {
-                const int2 rg = mk.ranges[(size_t)m * kMaxRanges + r];
+            const int nrg = ms ? ms->n_ranges[m] : mk.n_ranges[m];
+            for (int r = 0; r < nrg; ++r) {
+                const int2 rg = ms ? ms->ranges[(size_t)m * kMaxRanges + r] : mk.ranges[(size_t)m * kMaxRanges + r];
                 const int b0 = max(rg.x, lo), b1 = min(rg.y, hi);
                 for (int i = b0 + lane; i < b1; i += 32) row[i - lo] = -INFINITY;
             }
@@ -59,8 +73,17 @@ for (int mm = warp; mm < MT; mm += blockDim.x / 32) {
                         if (tk[j] >= lo && tk[j] < hi) row[tk[j] - lo] = -INFINITY;
                 }
             };
-            mask_list(mk.static_list, mk.n_static);
-            mask_list(mk.dyn_list + (size_t)m * mk.dyn_stride, mk.dyn_count[m]);
+            if (ms) {  // staged heads of the lists, the rest (rare) from global memory
+                const int ns = min(mk.n_static, kStatStage);
+                mask_list(ms->stat, ns);
+                mask_list(mk.static_list + ns, mk.n_static - ns);
+                const int nd = ms->dyn_count[m], nds = min(nd, kDynStage);
+                mask_list(ms->dyn + (size_t)m * kDynStage, nds);
+                mask_list(mk.dyn_list + (size_t)m * mk.dyn_stride + nds, nd - nds);
+            } else {
+                mask_list(mk.static_list, mk.n_static);
+                mask_list(mk.dyn_list + (size_t)m * mk.dyn_stride, mk.dyn_count[m]);
+            }
             __syncwarp();
         }
         if (a.masked_out)
