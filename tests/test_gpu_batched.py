@@ -1,0 +1,94 @@
+"""Batched decoding with 16 or more live sequences, where every projection of the decode step
+runs on the tcgen05 kernel (LayerNorm prologue, token + position embedding of layer 0, Q/K/V
+with the self-cache scatter, residual and GELU epilogues), against the CPU oracle.
+
+WhisperDecoder.decode / decodeBeam (WhisperDecoder.java) per stream; tolerances as in the
+single-stream decoder tests: identical ids except at near ties of the oracle's logits.
+"""
+import numpy as np
+import pytest
+
+from oracle import oracle as O
+from whisper4j_b200 import ggml
+from whisper4j_b200.decoder import WhisperDecoder
+
+from .helpers import LOGIT_ATOL, SMALL, SMALL_OPTS, assert_logits_close, encoder_output, parsed
+from .test_gpu_decoder import check_tokens
+
+pytestmark = pytest.mark.gpu
+
+SO = tuple(sorted(SMALL_OPTS.items()))
+TINY = ggml.ARCHS["tiny.en"]
+N_STREAMS = 20
+
+
+@pytest.fixture(scope="module")
+def wide():
+    gm = parsed(SMALL, 101, "f16", SO)
+    d = WhisperDecoder(gm, max_streams=N_STREAMS, max_beam=2)
+    o = O.OracleModel(gm)
+    xas = [encoder_output(300 + i, SMALL.n_audio_ctx, SMALL.n_text_state) for i in range(N_STREAMS)]
+    for i, xa in enumerate(xas):
+        d.set_encoder_output(xa, slot=i)
+    yield d, o, xas
+    d.close()
+
+
+def _prompts(n):
+    return [[996, 997, 998, 10 + i] for i in range(n)]
+
+
+def test_greedy_20_streams_match_oracle(wide):
+    dec, ora, xas = wide
+    slots = list(range(N_STREAMS))
+    prompts = _prompts(N_STREAMS)
+    res = dec.decode_batch(slots, prompts, 995, 24, suppress_tokens=[995], no_speech_token=3)
+    for s, p, r in zip(slots, prompts, res):
+        w = ora.decode(xas[s], p, 995, 24, suppress=[995], no_speech=3)
+        check_tokens(r.tokens, w["tokens"], ora, xas[s], p)
+        if r.tokens == w["tokens"]:
+            assert r.sum_logprob == pytest.approx(w["sum_logprob"], abs=2e-2 + 1e-3 * abs(w["sum_logprob"]))
+        assert r.no_speech_prob == pytest.approx(w["no_speech_prob"], rel=2e-2, abs=1e-6)
+
+
+def test_greedy_16_streams_with_eot(wide):
+    """Sequences finish at different steps: finished rows leave the projections' epilogues."""
+    dec, ora, xas = wide
+    slots = list(range(16))
+    prompts = _prompts(16)
+    free = ora.decode(xas[0], prompts[0], 995, 16, suppress=[995])
+    eot = free["tokens"][3]
+    res = dec.decode_batch(slots, prompts, eot, 16)
+    for s, p, r in zip(slots, prompts, res):
+        w = ora.decode(xas[s], p, eot, 16)
+        check_tokens(r.tokens, w["tokens"], ora, xas[s], p)
+
+
+def test_beam_2_times_10_streams_match_oracle(wide):
+    dec, ora, xas = wide
+    slots = list(range(10))
+    prompts = _prompts(10)
+    res = dec.decode_beam_batch(slots, prompts, 995, 12, suppress_tokens=[995], beam_size=2)
+    for s, p, r in zip(slots, prompts, res):
+        w = ora.decode_beam(xas[s], p, 995, 12, suppress=[995], beam=2)
+        if r.tokens == w["tokens"]:
+            assert r.sum_logprob == pytest.approx(w["sum_logprob"], abs=2e-2)
+        else:  # a near tie among beam scores may reorder candidates: compare scores instead
+            assert r.sum_logprob == pytest.approx(w["sum_logprob"], abs=5e-2)
+        assert len(r.tokens) == 12
+
+
+@pytest.mark.parametrize("n", [16, 40, 64])
+def test_forward_long_prompt_tiny(n):
+    """Teacher-forced rows: a prompt of n >= 16 tokens is one M = n pass (tiny.en, d = 384)."""
+    gm = parsed(TINY, 23)
+    ora = O.OracleModel(gm)
+    xa = encoder_output(24, TINY.n_audio_ctx, TINY.n_text_state)
+    rng = np.random.default_rng(n)
+    toks = [50257] + [int(t) for t in rng.integers(0, 50000, n - 1)]
+    with WhisperDecoder(gm, max_streams=1, max_beam=1) as dec:
+        dec.set_encoder_output(xa, slot=0)
+        got = dec.forward(toks, kv_cache=dec.new_cache(0))
+    want = ora.forward(toks, xa, ora.new_cache())
+    assert_logits_close(got, want)
+    assert np.abs(got - want).max() < LOGIT_ATOL

@@ -44,7 +44,10 @@ def gelu_table():
         return (0.5 * xs * (1 + np.tanh(np.float32(np.sqrt(2 / np.pi)) * (xs + np.float32(0.044715) * xs ** 3))))
 
 
-@pytest.mark.parametrize("M,K,N", [(1, 384, 1152), (5, 512, 512), (3, 1280, 5120), (8, 2048, 512), (16, 768, 300)])
+# M >= 16 runs on the tcgen05 projection kernel (f16 hi/lo activations, split K over a cluster)
+@pytest.mark.parametrize("M,K,N", [(1, 384, 1152), (5, 512, 512), (3, 1280, 5120), (8, 2048, 512), (16, 768, 300),
+                                   (17, 512, 1536), (32, 1280, 3840), (32, 5120, 1280), (64, 1024, 4096),
+                                   (64, 5120, 1280), (100, 384, 1152), (128, 512, 512)])
 @pytest.mark.parametrize("epi", [0, 1, 2])
 @pytest.mark.parametrize("use_ln", [False, True])
 def test_linear_f16(dec, M, K, N, epi, use_ln):

@@ -1,0 +1,433 @@
+// k_gemm_tc.cu — the decoder projections on the 5th-generation tensor cores (tcgen05 + TMEM +
+// TMA) once streams x beams give M >= 16 rows: y[m][n] = LN?(x[m]) . W[n]^T + b with the
+// epilogues of the GEMV kernel (store, GELU table, residual add, Q/K/V with the self-cache
+// scatter).  Same computation as k_gemv (Linear.forward, nn/Linear.java:23-26, with the
+// LayerNorm of ResidualAttentionBlock.java:48-59 before it), for batched decoding.
+//
+// Grid (split, tile): a block owns 128 rows of W (one UMMA M tile) and a range of K.
+//   * TMA (cp.async.bulk.tensor.2d, 128-byte swizzle) streams its [128 x 64] weight tiles through
+//     a ring of shared-memory stages, the first stages before griddepcontrol.wait.
+//   * The activations (LayerNorm-ed over the full row when the projection has one) of the
+//     block's K range are written as the f16 B operand, K-major with the same swizzle, each f32
+//     value x as two f16 rows: hi = f16(x) and lo = f16(x - hi).  hi + lo carries x to about 22
+//     bits, so with f16 weights and f32 accumulation the product keeps the f32 activations of
+//     the reference instead of rounding them to f16.  Rows hold the NU sequence slots (NU = M
+//     padded to 16, 32, 64 or 128; slots >= M are zero): hi in rows [0, NU), lo in [NU, 2 NU).
+//   * One thread issues tcgen05.mma.kind::f16 (M 128, N 2 NU, K 16) into an f32 accumulator in
+//     tensor memory; four warps read it back with tcgen05.ld and add the hi and lo columns.
+//   * With a split K the split blocks of a tile form a thread-block cluster: each leaves its
+//     partial tile in its own shared memory and, after a cluster barrier, block r adds the
+//     partials of its share of the rows in split order (distributed shared memory), so the
+//     result is deterministic, then applies the epilogue.
+// Every wait on a copy is bounded; a time-out raises the device error word.
+#include "tc_common.cuh"
+#include "w4j_internal.cuh"
+
+namespace w4j {
+
+struct GemmTcLaunch {
+    int KB;        // 64-wide k-blocks in K
+    int ks;        // K splits (cluster size)
+    int nkb_max;   // k-blocks of the largest split
+    int n_stages;  // weight ring stages
+    unsigned b_off, ln_off, bias_off, mi_off, bar_off;  // shared-memory layout (bytes)
+};
+
+__device__ __forceinline__ void gt_cluster_sync() {
+    asm volatile("barrier.cluster.arrive.release.aligned;\n\tbarrier.cluster.wait.acquire.aligned;" ::: "memory");
+}
+__device__ __forceinline__ float gt_ld_cluster(const float *local, unsigned rank) {
+    unsigned remote;
+    asm volatile("mapa.shared::cluster.u32 %0, %1, %2;" : "=r"(remote) : "r"(smem_u32(local)), "r"(rank));
+    float v;
+    asm volatile("ld.shared::cluster.f32 %0, [%1];" : "=f"(v) : "r"(remote) : "memory");
+    return v;
+}
+
+template <int NU>
+__global__ void __launch_bounds__(256, 1) k_gemm_tc(GemvArgs a, const __grid_constant__ CUtensorMap tmap,
+                                                     GemmTcLaunch L) {
+    extern __shared__ __align__(1024) unsigned char smem_raw[];
+    unsigned char *smem = smem_raw + ((1024u - (smem_u32(smem_raw) & 1023u)) & 1023u);
+    const int N = a.W.N, K = a.W.K, M = a.M;
+    const int split = blockIdx.x, ks = L.ks;
+    const int n0 = blockIdx.y * kTileRows;
+    const int kb0 = (split * L.KB) / ks, kb1 = ((split + 1) * L.KB) / ks, nkb = kb1 - kb0;
+    const int NS = L.n_stages;
+    unsigned char *ring = smem;
+    constexpr int NB = 2 * NU;             // B rows: hi, then lo parts of the NU slots
+    unsigned char *bop = smem + L.b_off;  // [nkb][NB rows][128 B]
+    float *ln_s = reinterpret_cast<float *>(smem + L.ln_off);      // gamma, beta of the K range
+    float *bias_s = reinterpret_cast<float *>(smem + L.bias_off);  // [128]
+    int *mi_s = reinterpret_cast<int *>(smem + L.mi_off);          // [4][M] active, slot, pos, token
+    uint64_t *full = reinterpret_cast<uint64_t *>(smem + L.bar_off);
+    uint64_t *empty = full + NS;
+    uint64_t *accf = empty + NS;
+    uint32_t *tslot = reinterpret_cast<uint32_t *>(accf + 1);
+    volatile int *fail = reinterpret_cast<volatile int *>(tslot + 1);
+    volatile int *issued = fail + 1;  // weight tiles whose copy has been started
+    float *part = reinterpret_cast<float *>(ring);  // [128][NU + 1] partial tile (after the MMAs)
+    const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+    constexpr uint32_t kCols = NB;  // 32 .. 256 f32 columns
+    const int kr = nkb * kKB;  // K range of this block: [kb0 * 64, kb0 * 64 + kr)
+
+    // ---- independent of the previous kernel: barriers, TMEM, first weight tiles, parameters ----
+    if (tid == 0) {
+        for (int i = 0; i < NS; ++i) {
+            mbar_init(full + i, 1);
+            mbar_init(empty + i, 1);
+        }
+        mbar_init(accf, 1);
+        *fail = 0;
+        fence_mbar_init();
+        for (int i = 0; i < NS && i < nkb; ++i) {
+            mbar_expect_tx(full + i, kStageBytes);
+            tma_load_2d(ring + (size_t)i * kStageBytes, &tmap, (kb0 + i) * kKB, n0, full + i);
+        }
+        *issued = NS < nkb ? NS : nkb;
+    }
+    if (warp == 1) {
+        tmem_alloc(tslot, kCols);
+        tmem_relinquish();
+    }
+    if (a.in_mode != IN_ACT)
+        for (int i = tid; i < 2 * kr; i += blockDim.x)
+            ln_s[i] = i < kr ? a.ln_g[kb0 * kKB + i] : a.ln_b[kb0 * kKB + i - kr];
+    for (int i = tid; i < kTileRows; i += blockDim.x) bias_s[i] = (a.bias && n0 + i < N) ? a.bias[n0 + i] : 0.f;
+    // liveness, cache slots, positions and tokens: written by the host or an earlier graph launch
+    for (int i = tid; i < M; i += blockDim.x) {
+        mi_s[i] = a.active ? a.active[i] : 1;
+        if (a.out_mode == OUT_QKV) {
+            mi_s[M + i] = a.seq_slot[i];
+            mi_s[2 * M + i] = a.pos[i];
+        }
+        if (a.in_mode == IN_EMBED_LN) {
+            mi_s[2 * M + i] = a.pos[i];
+            mi_s[3 * M + i] = a.tok[i];
+        }
+    }
+    for (int i = tid; i < 2 * (NU - M) * nkb * 8; i += blockDim.x) {  // slots M .. NU are zero
+        const int j = i / (nkb * 8), c = i % (nkb * 8);
+        const int m = j < NU - M ? M + j : NU + M + (j - (NU - M));
+        const int kb = c / 8, cc = c % 8;
+        *reinterpret_cast<uint4 *>(bop + (size_t)kb * NB * 128 + (size_t)m * 128 + ((cc ^ (m & 7)) * 16)) =
+            make_uint4(0, 0, 0, 0);
+    }
+    pdl_trigger();
+    pdl_wait();
+    __syncthreads();
+
+    // ---- B operand: the rows' K range as f16 hi / lo pairs, K-major, 128-byte swizzle ----
+    // 4 consecutive elements k .. k+3 of slot m (k inside the K range) go to their 8-byte half of
+    // the 16-byte chunk of row m (hi) and of row NU + m (lo)
+    auto put4 = [&](int m, int kk, float4 v) {
+        const int kb = kk / kKB, cc = (kk % kKB) / 8, half = (kk % 8) / 4;
+        const __half2 h0 = __floats2half2_rn(v.x, v.y), h1 = __floats2half2_rn(v.z, v.w);
+        const float2 f0 = __half22float2(h0), f1 = __half22float2(h1);
+        const __half2 l0 = __floats2half2_rn(v.x - f0.x, v.y - f0.y), l1 = __floats2half2_rn(v.z - f1.x, v.w - f1.y);
+        unsigned char *row = bop + (size_t)kb * NB * 128 + half * 8;
+        const int ml = NU + m;
+        *reinterpret_cast<uint2 *>(row + (size_t)m * 128 + ((cc ^ (m & 7)) * 16)) =
+            make_uint2(*reinterpret_cast<const uint32_t *>(&h0), *reinterpret_cast<const uint32_t *>(&h1));
+        *reinterpret_cast<uint2 *>(row + (size_t)ml * 128 + ((cc ^ (ml & 7)) * 16)) =
+            make_uint2(*reinterpret_cast<const uint32_t *>(&l0), *reinterpret_cast<const uint32_t *>(&l1));
+    };
+    if (a.in_mode == IN_ACT) {
+        const int r4 = kr / 4;  // float4 per row in the K range
+        const int total = M * r4;
+        for (int i0 = tid; i0 < total; i0 += blockDim.x * 8) {
+            float4 v[8];
+#pragma unroll
+            for (int j = 0; j < 8; ++j) {
+                const int i = i0 + blockDim.x * j;
+                if (i < total) {
+                    const int m = i / r4, c4 = i - m * r4;
+                    v[j] = reinterpret_cast<const float4 *>(a.act + (size_t)m * K + kb0 * kKB)[c4];
+                }
+            }
+#pragma unroll
+            for (int j = 0; j < 8; ++j) {
+                const int i = i0 + blockDim.x * j;
+                if (i < total) {
+                    const int m = i / r4, c4 = i - m * r4;
+                    put4(m, 4 * c4, v[j]);
+                }
+            }
+        }
+    } else {
+        // LayerNorm over the full row (Tensor.java:592-619: two-pass mean / variance, eps 1e-5),
+        // one warp per row with the row in registers; then the K range is written
+        constexpr int kLnF4 = 10;  // K <= 1280
+        const int nf4 = K / 128;
+        for (int m = warp; m < M; m += 8) {
+            float4 v[kLnF4];
+            if (a.in_mode == IN_LN) {
+                const float4 *src = reinterpret_cast<const float4 *>(a.act + (size_t)m * K);
+#pragma unroll
+                for (int j = 0; j < kLnF4; ++j) v[j] = j < nf4 ? src[lane + 32 * j] : make_float4(0.f, 0.f, 0.f, 0.f);
+            } else {  // x = E[tok] + P[pos] (WhisperDecoder.java:66-80), kept in x_out by one block
+                const int tok = mi_s[3 * M + m], pos = mi_s[2 * M + m];
+                const uint2 *e = reinterpret_cast<const uint2 *>(a.E.h + (size_t)tok * K);
+                const float4 *pe = reinterpret_cast<const float4 *>(a.pos_emb + (size_t)pos * K);
+                uint2 eu[kLnF4];
+#pragma unroll
+                for (int j = 0; j < kLnF4; ++j) {
+                    eu[j] = j < nf4 ? e[lane + 32 * j] : make_uint2(0u, 0u);
+                    v[j] = j < nf4 ? pe[lane + 32 * j] : make_float4(0.f, 0.f, 0.f, 0.f);
+                }
+#pragma unroll
+                for (int j = 0; j < kLnF4; ++j) {
+                    const float2 lo = __half22float2(*reinterpret_cast<const __half2 *>(&eu[j].x));
+                    const float2 hi = __half22float2(*reinterpret_cast<const __half2 *>(&eu[j].y));
+                    v[j] = make_float4(lo.x + v[j].x, lo.y + v[j].y, hi.x + v[j].z, hi.y + v[j].w);
+                    if (j < nf4 && blockIdx.x == 0 && blockIdx.y == 0 && a.x_out)
+                        reinterpret_cast<float4 *>(a.x_out)[(size_t)m * (K / 4) + lane + 32 * j] = v[j];
+                }
+            }
+            float sm = 0.f;
+#pragma unroll
+            for (int j = 0; j < kLnF4; ++j)
+                if (j < nf4) sm += (v[j].x + v[j].y) + (v[j].z + v[j].w);
+            const float mean = warp_sum(sm) / (float)K;
+            float v2 = 0.f;
+#pragma unroll
+            for (int j = 0; j < kLnF4; ++j)
+                if (j < nf4) {
+                    const float dx = v[j].x - mean, dy = v[j].y - mean, dz = v[j].z - mean, dw = v[j].w - mean;
+                    v2 += (dx * dx + dy * dy) + (dz * dz + dw * dw);
+                }
+            const float inv_std = 1.0f / sqrtf(warp_sum(v2) / (float)K + 1e-5f);
+#pragma unroll
+            for (int j = 0; j < kLnF4; ++j) {
+                const int k = 4 * (lane + 32 * j), kk = k - kb0 * kKB;
+                if (j < nf4 && kk >= 0 && kk < kr) {
+                    const float4 g = *reinterpret_cast<const float4 *>(ln_s + kk);
+                    const float4 b = *reinterpret_cast<const float4 *>(ln_s + kr + kk);
+                    put4(m, kk, make_float4((v[j].x - mean) * inv_std * g.x + b.x, (v[j].y - mean) * inv_std * g.y + b.y,
+                                            (v[j].z - mean) * inv_std * g.z + b.z, (v[j].w - mean) * inv_std * g.w + b.w));
+                }
+            }
+        }
+    }
+    fence_proxy_async();  // generic-proxy writes of B visible to the tensor core
+    tc_fence_before();
+    __syncthreads();
+    tc_fence_after();
+    const uint32_t taddr = *tslot;
+    const uint32_t idesc = idesc_f16(kTileRows, NB);
+
+    // output (row r of the tile, sequence m) with the GEMV epilogues
+    auto emit = [&](float v, int r, int m) {
+        const int n = n0 + r;
+        if (n >= N || m >= M || !mi_s[m]) return;
+        const float val = v + bias_s[r];
+        switch (a.out_mode) {
+            case OUT_STORE:
+                a.y[(size_t)m * N + n] = val;
+                break;
+            case OUT_GELU:  // Tensor.geluInPlace: table lookup at the f16 rounding of x
+                a.y[(size_t)m * N + n] = a.gelu_lut[__half_as_ushort(__float2half_rn(val))];
+                break;
+            case OUT_RESIDUAL:
+                a.y[(size_t)m * N + n] += val;
+                break;
+            case OUT_QKV: {
+                const int dm = N / 3;
+                const int part_ = n / dm, c = n - part_ * dm;
+                if (part_ == 0) {
+                    a.y[(size_t)m * dm + c] = val;
+                } else {
+                    const int head = c / kHeadDim, dd = c % kHeadDim;
+                    const size_t row = (((size_t)mi_s[M + m] * a.n_layer + a.layer) * a.n_head + head) * (size_t)a.n_ctx +
+                                       (size_t)mi_s[2 * M + m];
+                    __half *dst = part_ == 1 ? a.kcache : a.vcache;
+                    dst[row * kHeadDim + dd] = __float2half_rn(val);
+                }
+                break;
+            }
+        }
+    };
+
+    if (warp == 0 && lane == 0) {
+        // ---- producer: the remaining weight tiles as stages free up ----
+        for (int i = NS; i < nkb && !*fail; ++i) {
+            const int st = i % NS;
+            if (!mbar_wait(empty + st, (unsigned)((i / NS - 1) & 1), a.err)) {
+                *fail = 1;
+                break;
+            }
+            mbar_expect_tx(full + st, kStageBytes);
+            tma_load_2d(ring + (size_t)st * kStageBytes, &tmap, (kb0 + i) * kKB, n0, full + st);
+            *issued = i + 1;
+        }
+    } else if (warp == 1 && lane == 0) {
+        // ---- MMA issuer ----
+        const uint32_t ring_a = smem_u32(ring), b_a = smem_u32(bop);
+        for (int i = 0; i < nkb && !*fail; ++i) {
+            const int st = i % NS;
+            if (!mbar_wait(full + st, (unsigned)((i / NS) & 1), a.err)) {
+                *fail = 1;
+                break;
+            }
+            tc_fence_after();
+#pragma unroll
+            for (int j = 0; j < kKB / 16; ++j) {
+                const uint64_t ad = sw128_desc(ring_a + (uint32_t)st * kStageBytes + j * 32);
+                const uint64_t bd = sw128_desc(b_a + (uint32_t)i * NB * 128 + j * 32);
+                umma_f16(taddr, ad, bd, idesc, (i | j) != 0);
+            }
+            umma_commit(empty + st);  // the stage is free once these MMAs have read it
+        }
+        umma_commit(accf);  // the accumulator is complete (or nothing was issued)
+    }
+    __syncthreads();
+    if (warp >= 4) {
+        // ---- TMEM -> registers: row q * 32 + lane of the tile; slot m = hi column m + lo column NU + m ----
+        const int q = warp - 4, r = q * 32 + lane;
+        const bool ok = !*fail && mbar_wait(accf, 0u, a.err);
+        if (!ok) *fail = 1;
+        tc_fence_after();
+#pragma unroll
+        for (int c0 = 0; c0 < NU; c0 += 16) {
+            float v[16], lo[16];
+            tmem_ld16(taddr + ((uint32_t)(q * 32) << 16) + (uint32_t)c0, v);
+            tmem_ld16(taddr + ((uint32_t)(q * 32) << 16) + (uint32_t)(NU + c0), lo);
+#pragma unroll
+            for (int e = 0; e < 16; ++e) v[e] += lo[e];
+            if (ks == 1) {
+                if (ok)
+#pragma unroll
+                    for (int e = 0; e < 16; ++e) emit(v[e], r, c0 + e);
+            } else if (ok) {  // the ring is free: every copy into it was consumed
+#pragma unroll
+                for (int e = 0; e < 16; ++e) part[(size_t)r * (NU + 1) + c0 + e] = v[e];
+            }
+        }
+        tc_fence_before();
+    }
+    __syncthreads();
+    if (ks > 1) {
+        // every split's partial is in its block's shared memory: block `split` adds rows
+        // [split * 128 / ks, (split + 1) * 128 / ks) over all splits, in split order
+        gt_cluster_sync();
+        const int r0 = (split * kTileRows) / ks, nr = ((split + 1) * kTileRows) / ks - r0;
+        for (int i = tid; i < nr * M && !*fail; i += blockDim.x) {
+            const int m = i / nr, r = r0 + i % nr;  // neighbouring threads: neighbouring outputs
+            float acc = 0.f;
+            for (int q = 0; q < ks; ++q) acc += gt_ld_cluster(&part[(size_t)r * (NU + 1) + m], (unsigned)q);
+            emit(acc, r, m);
+        }
+        gt_cluster_sync();  // no block leaves while its partial may still be read
+    }
+    if (*fail && tid == 0) drain_ring(full, NS, *issued);
+    if (warp == 1) {
+        tc_fence_after();
+        tmem_dealloc(taddr, kCols);
+    }
+}
+
+// ---------------------------------------------------------------------------
+// host side
+// ---------------------------------------------------------------------------
+static int nu_for(int M) { return M <= 16 ? 16 : M <= 32 ? 32 : M <= 64 ? 64 : 128; }
+
+static bool plan_gemm_tc(const GemvArgs &a, int sms, int &nu, GemmTcLaunch &L, int &tiles) {
+    const int M = a.M, N = a.W.N, K = a.W.K;
+    if (M < 16 || M > 128 || a.W.type != WT_F16 || K % kKB != 0 || N < 1) return false;
+    if (a.in_mode != IN_ACT && (K % 128 != 0 || K > 1280)) return false;
+    if (a.in_mode == IN_EMBED_LN && a.E.type != WT_F16) return false;
+    nu = nu_for(M);
+    tiles = (N + kTileRows - 1) / kTileRows;
+    L.KB = K / kKB;
+    int ks = sms / tiles;
+    ks = ks < 1 ? 1 : ks > 8 ? 8 : ks;
+    if (ks > L.KB) ks = L.KB;
+    L.ks = ks;
+    L.nkb_max = (L.KB + ks - 1) / ks;
+    const size_t bbytes = (size_t)L.nkb_max * 2 * nu * 128;  // hi and lo rows
+    const size_t lnbytes = a.in_mode == IN_ACT ? 0 : (size_t)2 * L.nkb_max * kKB * 4;
+    const size_t mibytes = ((size_t)4 * M * 4 + 15) & ~(size_t)15;
+    const size_t partbytes = (size_t)kTileRows * (nu + 1) * 4;
+    const size_t fixed = bbytes + lnbytes + 512 + mibytes + 256;
+    const size_t budget = 220 * 1024;
+    int ns_need = (int)((partbytes + kStageBytes - 1) / kStageBytes);
+    if (ns_need < 2) ns_need = 2;
+    if (fixed + (size_t)ns_need * kStageBytes > budget) return false;
+    int ns = (int)((budget - fixed) / kStageBytes);  // as many stages as fit, up to the k-blocks
+    if (ns > 8) ns = 8;
+    if (ns > L.nkb_max) ns = L.nkb_max;
+    if (ns < ns_need) ns = ns_need;
+    L.n_stages = ns;
+    L.b_off = (unsigned)(ns * kStageBytes);  // 1024-aligned; 2 nu * 128 B per k-block keeps it so
+    L.ln_off = L.b_off + (unsigned)bbytes;
+    L.bias_off = L.ln_off + (unsigned)lnbytes;
+    L.mi_off = L.bias_off + 512;
+    L.bar_off = L.mi_off + (unsigned)mibytes;
+    return true;
+}
+
+// Dynamic shared memory of a launch.  A block holds 2 nu tensor-memory columns of the SM's 512
+// from before griddepcontrol.wait to its exit, and split blocks wait for one another at the
+// cluster barrier, so no more blocks may be resident on an SM than its columns serve: from
+// 128 columns on, the request is raised until 228 KB of shared memory per SM admits no more.
+static size_t gemm_tc_smem(const GemmTcLaunch &L, int nu) {
+    size_t bytes = (size_t)L.bar_off + (2 * L.n_stages + 1) * 8 + 16 + 1024;
+    const int cols = 2 * nu;
+    if (cols >= 128) {
+        const size_t per_sm = 228 * 1024, fit = 512 / cols;
+        const size_t floor_bytes = per_sm / (fit + 1) + 1;
+        if (bytes < floor_bytes) bytes = floor_bytes;
+    }
+    return bytes;
+}
+
+template <int NU>
+static cudaError_t launch_gemm_tc_t(const GemvArgs &a, const CUtensorMap &map, const GemmTcLaunch &L, int tiles,
+                                    cudaStream_t s, bool pdl) {
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = dim3(L.ks, tiles);
+    cfg.blockDim = dim3(256);
+    cfg.dynamicSmemBytes = gemm_tc_smem(L, NU);
+    cfg.stream = s;
+    cudaLaunchAttribute attr[2];
+    int na = 0;
+    if (pdl) {
+        attr[na].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+        attr[na].val.programmaticStreamSerializationAllowed = 1;
+        ++na;
+    }
+    if (L.ks > 1) {
+        attr[na].id = cudaLaunchAttributeClusterDimension;
+        attr[na].val.clusterDim.x = L.ks;
+        attr[na].val.clusterDim.y = 1;
+        attr[na].val.clusterDim.z = 1;
+        ++na;
+    }
+    cfg.attrs = attr;
+    cfg.numAttrs = na;
+    return cudaLaunchKernelEx(&cfg, k_gemm_tc<NU>, a, map, L);
+}
+
+cudaError_t gemm_tc_prepare() {
+    cudaError_t e = allow_dynamic_smem(k_gemm_tc<16>);
+    if (e == cudaSuccess) e = allow_dynamic_smem(k_gemm_tc<32>);
+    if (e == cudaSuccess) e = allow_dynamic_smem(k_gemm_tc<64>);
+    if (e == cudaSuccess) e = allow_dynamic_smem(k_gemm_tc<128>);
+    return e;
+}
+
+// cudaErrorNotSupported when the projection is outside the tensor-core kernel's range.
+cudaError_t launch_gemm_tc(const GemvArgs &a, const void *tmap, int sms, cudaStream_t s, bool pdl) {
+    int nu, tiles;
+    GemmTcLaunch L;
+    if (!tmap || !plan_gemm_tc(a, sms, nu, L, tiles)) return cudaErrorNotSupported;
+    const CUtensorMap &map = *reinterpret_cast<const CUtensorMap *>(tmap);
+    switch (nu) {
+        case 16: return launch_gemm_tc_t<16>(a, map, L, tiles, s, pdl);
+        case 32: return launch_gemm_tc_t<32>(a, map, L, tiles, s, pdl);
+        case 64: return launch_gemm_tc_t<64>(a, map, L, tiles, s, pdl);
+        default: return launch_gemm_tc_t<128>(a, map, L, tiles, s, pdl);
+    }
+}
+
+}  // namespace w4j

@@ -19,77 +19,10 @@
 #include <cudaTypedefs.h>
 
 #include "logits_epilogue.cuh"
+#include "tc_common.cuh"
 #include "w4j_internal.cuh"
 
 namespace w4j {
-
-// ---------------------------------------------------------------------------
-// tcgen05 / TMA helpers
-// ---------------------------------------------------------------------------
-__device__ __forceinline__ void tma_load_2d(void *dst, const CUtensorMap *map, int x, int y, uint64_t *bar) {
-    asm volatile(
-        "cp.async.bulk.tensor.2d.shared::cluster.global.tile.mbarrier::complete_tx::bytes [%0], [%1, {%2, %3}], [%4];" ::
-            "r"(smem_u32(dst)),
-        "l"(map), "r"(x), "r"(y), "r"(smem_u32(bar))
-        : "memory");
-}
-__device__ __forceinline__ void tmem_alloc(uint32_t *slot, uint32_t ncols) {
-    asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(smem_u32(slot)), "r"(ncols)
-                 : "memory");
-}
-__device__ __forceinline__ void tmem_relinquish() {
-    asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;" ::: "memory");
-}
-__device__ __forceinline__ void tmem_dealloc(uint32_t taddr, uint32_t ncols) {
-    asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(taddr), "r"(ncols) : "memory");
-}
-__device__ __forceinline__ void tc_fence_before() { asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory"); }
-__device__ __forceinline__ void tc_fence_after() { asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory"); }
-__device__ __forceinline__ void fence_proxy_async() { asm volatile("fence.proxy.async.shared::cta;" ::: "memory"); }
-__device__ __forceinline__ void umma_f16(uint32_t d_tmem, uint64_t adesc, uint64_t bdesc, uint32_t idesc,
-                                         uint32_t accumulate) {
-    asm volatile(
-        "{\n .reg .pred p;\n setp.ne.b32 p, %4, 0;\n tcgen05.mma.cta_group::1.kind::f16 [%0], %1, %2, %3, p;\n}" ::"r"(
-            d_tmem),
-        "l"(adesc), "l"(bdesc), "r"(idesc), "r"(accumulate)
-        : "memory");
-}
-__device__ __forceinline__ void umma_commit(uint64_t *bar) {
-    asm volatile("tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(smem_u32(bar))
-                 : "memory");
-}
-__device__ __forceinline__ void mbar_arrive(uint64_t *bar) {
-    asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(smem_u32(bar)) : "memory");
-}
-__device__ __forceinline__ void tmem_ld16(uint32_t taddr, float (&v)[16]) {
-    uint32_t r[16];
-    asm volatile(
-        "tcgen05.ld.sync.aligned.32x32b.x16.b32 {%0,%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15}, [%16];"
-        : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]), "=r"(r[7]), "=r"(r[8]),
-          "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]), "=r"(r[13]), "=r"(r[14]), "=r"(r[15])
-        : "r"(taddr)
-        : "memory");
-    asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
-#pragma unroll
-    for (int i = 0; i < 16; ++i) v[i] = __uint_as_float(r[i]);
-}
-
-// Shared-memory matrix descriptor of a K-major operand with the 128-byte swizzle: rows of
-// 128 B (64 f16 along K), 8-row atoms 1024 B apart (stride byte offset), version 1 (sm_100).
-__device__ __forceinline__ uint64_t sw128_desc(uint32_t saddr) {
-    uint64_t d = 0;
-    d |= (uint64_t)((saddr >> 4) & 0x3FFFu);  // start address >> 4
-    d |= (uint64_t)1 << 16;                   // leading byte offset (implied for swizzled K-major)
-    d |= (uint64_t)(1024 >> 4) << 32;         // stride byte offset: next 8-row atom
-    d |= (uint64_t)1 << 46;                   // descriptor version
-    d |= (uint64_t)2 << 61;                   // SWIZZLE_128B
-    return d;
-}
-
-// Instruction descriptor, kind::f16: f32 accumulator, f16 A and B, both K-major, M x N.
-__host__ __device__ constexpr uint32_t idesc_f16(int M, int N) {
-    return (1u << 4) | ((uint32_t)(N >> 3) << 17) | ((uint32_t)(M >> 4) << 24);
-}
 
 struct LogitsTcLaunch {
     int tiles_total;  // ceil(V / 128)
@@ -98,7 +31,6 @@ struct LogitsTcLaunch {
     unsigned b_off, tile_off, ln_off, mk_off, bar_off;  // shared-memory layout (bytes)
 };
 
-constexpr int kTileRows = 128, kKB = 64, kStageBytes = kTileRows * kKB * 2;
 
 template <int NU>
 __global__ void __launch_bounds__(256, 1) k_logits_tc(LogitsArgs a, const __grid_constant__ CUtensorMap tmap,
@@ -128,6 +60,7 @@ __global__ void __launch_bounds__(256, 1) k_logits_tc(LogitsArgs a, const __grid
     uint64_t *acce = accf + 2;    // [2]
     uint32_t *tslot = reinterpret_cast<uint32_t *>(acce + 2);
     volatile int *fail = reinterpret_cast<volatile int *>(tslot + 1);
+    volatile int *issued = fail + 1;  // weight tiles whose copy has been started
     const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
     constexpr uint32_t kCols = NU * 2 <= 32 ? 32 : 64;
 
@@ -147,6 +80,7 @@ __global__ void __launch_bounds__(256, 1) k_logits_tc(LogitsArgs a, const __grid
             mbar_expect_tx(full + i, kStageBytes);
             tma_load_2d(ring + (size_t)i * kStageBytes, &tmap, (i % KB) * kKB, (t0 + i / KB) * kTileRows, full + i);
         }
+        *issued = NS < total ? NS : total;
     }
     if (warp == 1) {
         tmem_alloc(tslot, kCols);
@@ -247,6 +181,7 @@ __global__ void __launch_bounds__(256, 1) k_logits_tc(LogitsArgs a, const __grid
             }
             mbar_expect_tx(full + st, kStageBytes);
             tma_load_2d(ring + (size_t)st * kStageBytes, &tmap, (i % KB) * kKB, (t0 + i / KB) * kTileRows, full + st);
+            *issued = i + 1;
         }
     } else if (warp == 1 && lane == 0) {
         // ---- MMA issuer ----
@@ -310,11 +245,7 @@ __global__ void __launch_bounds__(256, 1) k_logits_tc(LogitsArgs a, const __grid
     const MaskStage ms{mk_act, mk_nr, mk_rg, mk_cnt, mk_dyn, mk_stat};
     logits_rows_epilogue(a, tile, L.ch, a.M, 0, lo, hi, ok, &ms);
     __syncthreads();
-    if (!ok && tid == 0)  // let copies in flight land before the block's memory is reused
-        for (int i = 0; i < NS; ++i) {
-            for (long long it = 0; it < (1ll << 20) && !mbar_test(full + i, 0) && !mbar_test(full + i, 1); ++it) {
-            }
-        }
+    if (!ok && tid == 0) drain_ring(full, NS, *issued);
     if (warp == 1) {
         tc_fence_after();
         tmem_dealloc(taddr, kCols);

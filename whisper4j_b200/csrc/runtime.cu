@@ -65,7 +65,11 @@ struct LayerDev {
     float *bm0 = nullptr, *bm2 = nullptr;
     float *ln1g = nullptr, *ln1b = nullptr, *ln2g = nullptr, *ln2b = nullptr, *ln3g = nullptr, *ln3b = nullptr;
     int qkv_type = 0;
+    // TMA maps of the f16 projections for the tensor-core kernel (M >= 16), by PROJ_*
+    alignas(64) unsigned char tmap[6][128] = {};
+    bool tmap_ok[6] = {};
 };
+enum Proj : int { PROJ_QKV = 0, PROJ_O = 1, PROJ_XQ = 2, PROJ_XO = 3, PROJ_M0 = 4, PROJ_M2 = 5 };
 
 struct GraphKey {
     int mode, S, B, eot, ts_begin, n_sup, max_tokens, ns, n_prompt;
@@ -114,6 +118,7 @@ struct w4j_ctx {
     alignas(64) unsigned char e_tmap[128] = {};  // TMA map of the f16 token embedding
     bool e_tmap_ok = false;
     bool tc_logits = true;
+    bool tc_gemm = true;  // tcgen05 projections once M >= 16
 };
 
 template <typename T>
@@ -200,6 +205,7 @@ extern "C" int w4j_ctx_create(const w4j_dims *dims, int device, int max_streams,
     c->M_max = max_streams * max_beam;
     c->sm_count = prop.multiProcessorCount;
     if (const char *ev = getenv("W4J_NO_TC_LOGITS")) c->tc_logits = ev[0] == '0';
+    if (const char *ev = getenv("W4J_NO_TC_GEMM")) c->tc_gemm = ev[0] == '0';
     c->layers.resize(c->L);
     c->cache_len.assign(max_streams, 0);
     c->has_xa.assign(max_streams, 0);
@@ -213,7 +219,7 @@ extern "C" int w4j_ctx_create(const w4j_dims *dims, int device, int max_streams,
     cudaEventCreate(&c->ev0);
     cudaEventCreate(&c->ev1);
     if ((rc = (int)gemv_prepare()) != 0 || (rc = (int)select_prepare()) != 0 || (rc = (int)logits_tc_prepare()) != 0 ||
-        (rc = (int)attn_prepare()) != 0)
+        (rc = (int)attn_prepare()) != 0 || (rc = (int)gemm_tc_prepare()) != 0)
         return fail(set_err(W4J_ERR_CUDA, "kernel attributes: %s", cudaGetErrorString((cudaError_t)rc)));
     const size_t V = c->V, C = c->C, A = c->A, L = c->L;
     const size_t M = c->M_max;
@@ -471,7 +477,13 @@ static int check_ready(w4j_ctx *c) {
 extern "C" int w4j_finalize(w4j_ctx *c) {
     if (!c) return set_err(W4J_ERR_ARG, "null context");
     std::lock_guard<std::mutex> g(c->mu);
-    return check_ready(c);
+    TRY(check_ready(c));
+    for (LayerDev &ly : c->layers) {
+        const DMat *m[6] = {&ly.qkv, &ly.o, &ly.xq, &ly.xo, &ly.m0, &ly.m2};
+        for (int i = 0; i < 6; ++i)
+            ly.tmap_ok[i] = c->tc_gemm && m[i]->type == WT_F16 && make_tmap_f16_rows(ly.tmap[i], m[i]->h, m[i]->N, m[i]->K);
+    }
+    return W4J_OK;
 }
 
 // ---------------------------------------------------------------------------
@@ -527,6 +539,15 @@ struct PassArgs {
     int self_prefetch;        // older self-cache rows were written by an earlier graph launch
 };
 
+// One projection: the tcgen05 kernel from 16 rows on (f16 weights), else the GEMV.
+static cudaError_t run_proj(w4j_ctx *c, const GemvArgs &g, const LayerDev &ly, Proj p, bool pdl) {
+    if (ly.tmap_ok[p] && g.M >= 16) {
+        const cudaError_t e = launch_gemm_tc(g, ly.tmap[p], c->sm_count, c->stream, pdl);
+        if (e != cudaErrorNotSupported) return e;
+    }
+    return launch_gemv(g, c->stream, pdl);
+}
+
 static int run_layers(w4j_ctx *c, const PassArgs &pa, long long &launches) {
     const bool pdl = true;
     const int d = c->d;
@@ -558,7 +579,7 @@ static int run_layers(w4j_ctx *c, const PassArgs &pa, long long &launches) {
         g.n_ctx = c->C;
         g.active = pa.active;
         g.err = c->st.err;
-        CUDA_TRY(launch_gemv(g, c->stream, pdl));
+        CUDA_TRY(run_proj(c, g, ly, PROJ_QKV, pdl));
 
         AttnArgs sa;
         sa.q = c->q;
@@ -592,7 +613,7 @@ static int run_layers(w4j_ctx *c, const PassArgs &pa, long long &launches) {
         go.y = c->x;
         go.active = pa.active;
         go.err = c->st.err;
-        CUDA_TRY(launch_gemv(go, c->stream, pdl));
+        CUDA_TRY(run_proj(c, go, ly, PROJ_O, pdl));
 
         GemvArgs gq;
         gq.W = ly.xq;
@@ -605,7 +626,7 @@ static int run_layers(w4j_ctx *c, const PassArgs &pa, long long &launches) {
         gq.out_mode = OUT_STORE;
         gq.y = c->q;
         gq.err = c->st.err;
-        CUDA_TRY(launch_gemv(gq, c->stream, pdl));
+        CUDA_TRY(run_proj(c, gq, ly, PROJ_XQ, pdl));
 
         AttnArgs ca;
         ca.q = c->q;
@@ -636,7 +657,7 @@ static int run_layers(w4j_ctx *c, const PassArgs &pa, long long &launches) {
         gxo.y = c->x;
         gxo.active = pa.active;
         gxo.err = c->st.err;
-        CUDA_TRY(launch_gemv(gxo, c->stream, pdl));
+        CUDA_TRY(run_proj(c, gxo, ly, PROJ_XO, pdl));
 
         GemvArgs g1;
         g1.W = ly.m0;
@@ -650,7 +671,7 @@ static int run_layers(w4j_ctx *c, const PassArgs &pa, long long &launches) {
         g1.y = c->h;
         g1.gelu_lut = c->gelu_lut;
         g1.err = c->st.err;
-        CUDA_TRY(launch_gemv(g1, c->stream, pdl));
+        CUDA_TRY(run_proj(c, g1, ly, PROJ_M0, pdl));
 
         GemvArgs g2;
         g2.W = ly.m2;
@@ -662,7 +683,7 @@ static int run_layers(w4j_ctx *c, const PassArgs &pa, long long &launches) {
         g2.y = c->x;
         g2.active = pa.active;
         g2.err = c->st.err;
-        CUDA_TRY(launch_gemv(g2, c->stream, pdl));
+        CUDA_TRY(run_proj(c, g2, ly, PROJ_M2, pdl));
         launches += 8;
     }
     return 0;
@@ -1251,7 +1272,12 @@ extern "C" int w4j_op_linear(w4j_ctx *c, const float *x, int M, int K, const voi
     g.y = y;
     g.gelu_lut = c->gelu_lut;
     cudaStream_t s = stream ? reinterpret_cast<cudaStream_t>(stream) : 0;
-    CUDA_TRY(launch_gemv(g, s, false));
+    cudaError_t e = cudaErrorNotSupported;
+    alignas(64) unsigned char map[128];
+    if (c->tc_gemm && g.W.type == WT_F16 && M >= 16 && make_tmap_f16_rows(map, W, N, K))
+        e = launch_gemm_tc(g, map, c->sm_count, s, false);
+    if (e == cudaErrorNotSupported) e = launch_gemv(g, s, false);
+    CUDA_TRY(e);
     return W4J_OK;
 }
 

@@ -281,6 +281,10 @@ cudaError_t logits_tc_prepare();
 // tcgen05 vocabulary logits (f16 embedding, M <= 32); cudaErrorNotSupported outside its range
 cudaError_t launch_logits_tc(const LogitsArgs &a, const void *tmap, int n_parts, cudaStream_t s, bool pdl);
 bool make_tmap_f16_rows(void *map_out, const void *base, int rows, int cols);  // 128-byte map
+cudaError_t gemm_tc_prepare();
+// tcgen05 projection (f16 weights, 16 <= M <= 128) with the GEMV's input modes and epilogues;
+// `tmap` is make_tmap_f16_rows of a.W; cudaErrorNotSupported outside its range
+cudaError_t launch_gemm_tc(const GemvArgs &a, const void *tmap, int sms, cudaStream_t s, bool pdl);
 cudaError_t select_prepare();
 cudaError_t attn_prepare();
 cudaError_t launch_f32_to_f16(const float *src, __half *dst, size_t n, cudaStream_t s);
