@@ -32,6 +32,9 @@ __device__ __forceinline__ void cp_async16(void *smem, const void *gmem) {
     asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" ::"r"(s), "l"(gmem) : "memory");
 }
 __device__ __forceinline__ void cp_async_wait_all() { asm volatile("cp.async.wait_all;" ::: "memory"); }
+__device__ __forceinline__ void cp_async_commit() { asm volatile("cp.async.commit_group;" ::: "memory"); }
+template <int N>
+__device__ __forceinline__ void cp_async_wait_group() { asm volatile("cp.async.wait_group %0;" ::"n"(N) : "memory"); }
 // warp-level tensor-core tiles (m16n8k16, f16 inputs, f32 accumulation) and their fragments
 __device__ __forceinline__ void ldsm_x4(uint32_t (&r)[4], const void *p) {
     asm volatile("ldmatrix.sync.aligned.m8n8.x4.shared.b16 {%0,%1,%2,%3}, [%4];"
@@ -61,6 +64,129 @@ __device__ __forceinline__ float ld_cluster_f32(const float *local, unsigned ran
     float v;
     asm volatile("ld.shared::cluster.f32 %0, [%1];" : "=f"(v) : "r"(remote) : "memory");
     return v;
+}
+
+// One key tile of the online softmax for NQ queries: scores S^T = K . Q^T and O^T += V^T . P^T on
+// warp-level tensor cores (warp w owns keys [16 w, 16 w + 16) of the tile); s_m / s_l carry the
+// running max and denominator per query, of[4][4] this warp's O^T fragments.
+struct AttnShared {
+    __half (*qh)[kHeadDim + 8];       // queries (f16; rows >= NQ zero): MMA B operand
+    __half (*ps)[kAttnKeyTile + 8];   // probabilities of the tile (f16): MMA B operand
+    float (*w_max)[8], (*w_sum)[8];   // per-warp max / sum per query
+    float *s_m, *s_l;                 // running max / denominator per query
+};
+
+// Barrier of the 256 threads that run one tile: the block (id 0) or a named barrier of one
+// warpgroup pair (ids 1, 2).
+__device__ __forceinline__ void group_sync(int bar) {
+    if (bar == 0) __syncthreads();
+    else asm volatile("bar.sync %0, %1;" ::"r"(bar), "n"(kAttnThreads) : "memory");
+}
+
+// gtid: the thread's index among the kAttnThreads threads running the tile; bar: their barrier.
+template <int NQ>
+__device__ __forceinline__ void attn_tile(const AttnShared &sh, const __half *sk, const __half *sv, int nk,
+                                          float (&of)[4][4], int gtid, int bar) {
+    const int tid = gtid, warp = tid >> 5, lane = tid & 31;
+    const int g = lane >> 2, tq = lane & 3;
+    const float scale = 0.125f;  // (float)(1 / sqrt(64))
+    __half (*qh)[kHeadDim + 8] = sh.qh;
+    __half (*ps)[kAttnKeyTile + 8] = sh.ps;
+    float (*w_max)[8] = sh.w_max, (*w_sum)[8] = sh.w_sum;
+    float *s_m = sh.s_m, *s_l = sh.s_l;
+    const int kb = 16 * warp;  // this warp's first key of the tile
+    // scores S^T (16 keys x 8 queries) = K (16 x 64) . Q^T (64 x 8): four k16 steps
+    float sc[4] = {0.f, 0.f, 0.f, 0.f};
+    if (kb < nk) {
+#pragma unroll
+        for (int kk = 0; kk < 4; ++kk) {
+            uint32_t af[4], bf[2];
+            ldsm_x4(af, &sk[(kb + (lane & 15)) * kRowPad + 16 * kk + (lane >> 4) * 8]);
+            ldsm_x2(bf, &qh[lane & 7][16 * kk + ((lane >> 3) & 1) * 8]);
+            mma_16816(sc, af, bf);
+        }
+    }
+    // c0: (key kb+g, query 2tq), c1: (kb+g, 2tq+1), c2: (kb+g+8, 2tq), c3: (kb+g+8, 2tq+1)
+    const int q0 = 2 * tq, q1 = 2 * tq + 1;
+    const bool k0ok = kb + g < nk, k1ok = kb + g + 8 < nk;
+    sc[0] = (k0ok && q0 < NQ) ? sc[0] * scale : -INFINITY;
+    sc[1] = (k0ok && q1 < NQ) ? sc[1] * scale : -INFINITY;
+    sc[2] = (k1ok && q0 < NQ) ? sc[2] * scale : -INFINITY;
+    sc[3] = (k1ok && q1 < NQ) ? sc[3] * scale : -INFINITY;
+    // online softmax over the tile's keys, per query (lanes with the same tq share queries)
+    float mx0 = fmaxf(sc[0], sc[2]), mx1 = fmaxf(sc[1], sc[3]);
+#pragma unroll
+    for (int o = 4; o < 32; o <<= 1) {
+        mx0 = fmaxf(mx0, __shfl_xor_sync(0xffffffffu, mx0, o));
+        mx1 = fmaxf(mx1, __shfl_xor_sync(0xffffffffu, mx1, o));
+    }
+    if (g == 0) {
+        w_max[warp][q0] = mx0;
+        w_max[warp][q1] = mx1;
+    }
+    group_sync(bar);
+    float tm0 = -INFINITY, tm1 = -INFINITY;
+#pragma unroll
+    for (int w = 0; w < kWarps; ++w) {
+        tm0 = fmaxf(tm0, w_max[w][q0]);
+        tm1 = fmaxf(tm1, w_max[w][q1]);
+    }
+    const float mo0 = s_m[q0], mo1 = s_m[q1];
+    const float mn0 = fmaxf(mo0, tm0), mn1 = fmaxf(mo1, tm1);
+    const float p0 = sc[0] == -INFINITY ? 0.f : __expf(sc[0] - mn0);
+    const float p1 = sc[1] == -INFINITY ? 0.f : __expf(sc[1] - mn1);
+    const float p2 = sc[2] == -INFINITY ? 0.f : __expf(sc[2] - mn0);
+    const float p3 = sc[3] == -INFINITY ? 0.f : __expf(sc[3] - mn1);
+    float sm0 = p0 + p2, sm1 = p1 + p3;
+#pragma unroll
+    for (int o = 4; o < 32; o <<= 1) {
+        sm0 += __shfl_xor_sync(0xffffffffu, sm0, o);
+        sm1 += __shfl_xor_sync(0xffffffffu, sm1, o);
+    }
+    if (g == 0) {
+        w_sum[warp][q0] = sm0;
+        w_sum[warp][q1] = sm1;
+    }
+    // P^T of this warp's keys for the P.V step (read back only by this warp)
+    ps[q0][kb + g] = __float2half_rn(p0);
+    ps[q1][kb + g] = __float2half_rn(p1);
+    ps[q0][kb + g + 8] = __float2half_rn(p2);
+    ps[q1][kb + g + 8] = __float2half_rn(p3);
+    const float al0 = mo0 == -INFINITY ? 0.f : __expf(mo0 - mn0);
+    const float al1 = mo1 == -INFINITY ? 0.f : __expf(mo1 - mn1);
+#pragma unroll
+    for (int mt = 0; mt < 4; ++mt) {
+        of[mt][0] *= al0;
+        of[mt][1] *= al1;
+        of[mt][2] *= al0;
+        of[mt][3] *= al1;
+    }
+    __syncwarp();
+    // O^T (16 dims x 8 queries, 4 tiles) += V^T (16 dims x 16 keys) . P^T (16 keys x 8 queries)
+    if (kb < nk) {
+        uint32_t bf[2];
+        ldsm_x2(bf, &ps[lane & 7][kb + ((lane >> 3) & 1) * 8]);
+#pragma unroll
+        for (int mt = 0; mt < 4; ++mt) {
+            uint32_t af[4];
+            ldsm_x4_t(af, &sv[(kb + (lane & 7) + ((lane >> 4) & 1) * 8) * kRowPad + 16 * mt + ((lane >> 3) & 1) * 8]);
+            mma_16816(of[mt], af, bf);
+        }
+    }
+    group_sync(bar);  // w_max / w_sum read; s_m read by every thread
+    if (tid < 8) {    // running max and denominator per query
+        float tot = 0.f;
+#pragma unroll
+        for (int w = 0; w < kWarps; ++w) tot += w_sum[w][tid];
+        const float mo = s_m[tid];
+        float tmx = -INFINITY;
+#pragma unroll
+        for (int w = 0; w < kWarps; ++w) tmx = fmaxf(tmx, w_max[w][tid]);
+        const float mn = fmaxf(mo, tmx);
+        s_l[tid] = s_l[tid] * (mo == -INFINITY ? 0.f : __expf(mo - mn)) + tot;
+        s_m[tid] = mn;
+    }
+    group_sync(bar);
 }
 
 // Dynamic shared memory: `tiles` K/V tile pairs of the block's key range.
@@ -97,7 +223,6 @@ __global__ void __launch_bounds__(kAttnThreads) k_attn(AttnArgs a) {
     if (ns == 1 && split > 0) return;  // uniform over the cluster: no cluster barrier is reached
     const int j0 = split < ns ? (int)(((long long)split * len) / ns) : len;
     const int j1 = split < ns ? (int)(((long long)(split + 1) * len) / ns) : len;
-    const float scale = 0.125f;  // (float)(1 / sqrt(64))
 
     // stage K and V rows [t0, t0 + nk) into tile pair `ti` (128 B each = 8 x 16 B); which: 0 all,
     // 1 all but the newest self row, 2 only the newest
@@ -162,102 +287,11 @@ __global__ void __launch_bounds__(kAttnThreads) k_attn(AttnArgs a) {
     cp_async_wait_all();
     __syncthreads();
 
+    const AttnShared sh{qh, ps, w_max, w_sum, s_m, s_l};
     for (int ti = 0; ti < nt; ++ti) {
         const int nk = min(kAttnKeyTile, j1 - j0 - ti * kAttnKeyTile);
         const __half *sk = skv + (size_t)ti * kTileHalves, *sv = sk + kAttnKeyTile * kRowPad;
-        const int kb = 16 * warp;  // this warp's first key of the tile
-        // scores S^T (16 keys x 8 queries) = K (16 x 64) . Q^T (64 x 8): four k16 steps
-        float sc[4] = {0.f, 0.f, 0.f, 0.f};
-        if (kb < nk) {
-#pragma unroll
-            for (int kk = 0; kk < 4; ++kk) {
-                uint32_t af[4], bf[2];
-                ldsm_x4(af, &sk[(kb + (lane & 15)) * kRowPad + 16 * kk + (lane >> 4) * 8]);
-                ldsm_x2(bf, &qh[lane & 7][16 * kk + ((lane >> 3) & 1) * 8]);
-                mma_16816(sc, af, bf);
-            }
-        }
-        // c0: (key kb+g, query 2tq), c1: (kb+g, 2tq+1), c2: (kb+g+8, 2tq), c3: (kb+g+8, 2tq+1)
-        const int q0 = 2 * tq, q1 = 2 * tq + 1;
-        const bool k0ok = kb + g < nk, k1ok = kb + g + 8 < nk;
-        sc[0] = (k0ok && q0 < NQ) ? sc[0] * scale : -INFINITY;
-        sc[1] = (k0ok && q1 < NQ) ? sc[1] * scale : -INFINITY;
-        sc[2] = (k1ok && q0 < NQ) ? sc[2] * scale : -INFINITY;
-        sc[3] = (k1ok && q1 < NQ) ? sc[3] * scale : -INFINITY;
-        // online softmax over the tile's keys, per query (lanes with the same tq share queries)
-        float mx0 = fmaxf(sc[0], sc[2]), mx1 = fmaxf(sc[1], sc[3]);
-#pragma unroll
-        for (int o = 4; o < 32; o <<= 1) {
-            mx0 = fmaxf(mx0, __shfl_xor_sync(0xffffffffu, mx0, o));
-            mx1 = fmaxf(mx1, __shfl_xor_sync(0xffffffffu, mx1, o));
-        }
-        if (g == 0) {
-            w_max[warp][q0] = mx0;
-            w_max[warp][q1] = mx1;
-        }
-        __syncthreads();
-        float tm0 = -INFINITY, tm1 = -INFINITY;
-#pragma unroll
-        for (int w = 0; w < kWarps; ++w) {
-            tm0 = fmaxf(tm0, w_max[w][q0]);
-            tm1 = fmaxf(tm1, w_max[w][q1]);
-        }
-        const float mo0 = s_m[q0], mo1 = s_m[q1];
-        const float mn0 = fmaxf(mo0, tm0), mn1 = fmaxf(mo1, tm1);
-        const float p0 = sc[0] == -INFINITY ? 0.f : __expf(sc[0] - mn0);
-        const float p1 = sc[1] == -INFINITY ? 0.f : __expf(sc[1] - mn1);
-        const float p2 = sc[2] == -INFINITY ? 0.f : __expf(sc[2] - mn0);
-        const float p3 = sc[3] == -INFINITY ? 0.f : __expf(sc[3] - mn1);
-        float sm0 = p0 + p2, sm1 = p1 + p3;
-#pragma unroll
-        for (int o = 4; o < 32; o <<= 1) {
-            sm0 += __shfl_xor_sync(0xffffffffu, sm0, o);
-            sm1 += __shfl_xor_sync(0xffffffffu, sm1, o);
-        }
-        if (g == 0) {
-            w_sum[warp][q0] = sm0;
-            w_sum[warp][q1] = sm1;
-        }
-        // P^T of this warp's keys for the P.V step (read back only by this warp)
-        ps[q0][kb + g] = __float2half_rn(p0);
-        ps[q1][kb + g] = __float2half_rn(p1);
-        ps[q0][kb + g + 8] = __float2half_rn(p2);
-        ps[q1][kb + g + 8] = __float2half_rn(p3);
-        const float al0 = mo0 == -INFINITY ? 0.f : __expf(mo0 - mn0);
-        const float al1 = mo1 == -INFINITY ? 0.f : __expf(mo1 - mn1);
-#pragma unroll
-        for (int mt = 0; mt < 4; ++mt) {
-            of[mt][0] *= al0;
-            of[mt][1] *= al1;
-            of[mt][2] *= al0;
-            of[mt][3] *= al1;
-        }
-        __syncwarp();
-        // O^T (16 dims x 8 queries, 4 tiles) += V^T (16 dims x 16 keys) . P^T (16 keys x 8 queries)
-        if (kb < nk) {
-            uint32_t bf[2];
-            ldsm_x2(bf, &ps[lane & 7][kb + ((lane >> 3) & 1) * 8]);
-#pragma unroll
-            for (int mt = 0; mt < 4; ++mt) {
-                uint32_t af[4];
-                ldsm_x4_t(af, &sv[(kb + (lane & 7) + ((lane >> 4) & 1) * 8) * kRowPad + 16 * mt + ((lane >> 3) & 1) * 8]);
-                mma_16816(of[mt], af, bf);
-            }
-        }
-        __syncthreads();  // w_max / w_sum read; s_m read by every thread
-        if (tid < 8) {    // running max and denominator per query
-            float tot = 0.f;
-#pragma unroll
-            for (int w = 0; w < kWarps; ++w) tot += w_sum[w][tid];
-            const float mo = s_m[tid];
-            float tmx = -INFINITY;
-#pragma unroll
-            for (int w = 0; w < kWarps; ++w) tmx = fmaxf(tmx, w_max[w][tid]);
-            const float mn = fmaxf(mo, tmx);
-            s_l[tid] = s_l[tid] * (mo == -INFINITY ? 0.f : __expf(mo - mn)) + tot;
-            s_m[tid] = mn;
-        }
-        __syncthreads();
+        attn_tile<NQ>(sh, sk, sv, nk, of, tid, 0);
     }
     // add the warp shares (through the K/V tiles' shared memory, no longer needed)
     float *red = reinterpret_cast<float *>(skv);  // [kWarps][NQ][64]
@@ -330,6 +364,153 @@ __global__ void __launch_bounds__(kAttnThreads) k_attn(AttnArgs a) {
     cluster_sync();  // no block leaves while its partial may still be read
 }
 
+// ---------------------------------------------------------------------------
+// Streaming cross-attention for many (group, head) pairs (batched greedy / beam decoding).
+// One block per SM walks the pairs round-robin.  Its two warpgroups of 256 threads take the
+// even and the odd 128-key tiles of a pair, each with its own online-softmax state and two tile
+// buffers, so the rows of a warpgroup's next tile stream in (cp.async) while it computes the
+// current one, across pair boundaries, and the first tiles before griddepcontrol.wait.  At the
+// end of a pair the two states are combined in shared memory (even tiles first), so no partial
+// leaves the SM and the result does not depend on timing.  Needs n_audio > 128 (a tile for each
+// warpgroup in every pair: both meet at the block barrier that ends a pair).
+// ---------------------------------------------------------------------------
+constexpr int kStreamThreads = 2 * kAttnThreads;
+
+template <int NQ>
+__global__ void __launch_bounds__(kStreamThreads, 1) k_attn_stream(AttnArgs a) {
+    extern __shared__ __align__(16) __half sbuf[];  // [warpgroup][2 buffers][K tile | V tile]
+    __shared__ __align__(16) __half qh[2][8][kHeadDim + 8];
+    __shared__ __align__(16) __half ps[2][8][kAttnKeyTile + 8];
+    __shared__ float w_max[2][kWarps][8], w_sum[2][kWarps][8];
+    __shared__ float s_m[2][8], s_l[2][8];
+    __shared__ __align__(16) float red[2][kWarps][NQ * kHeadDim];
+    const int tid = threadIdx.x, wg = tid / kAttnThreads, gtid = tid % kAttnThreads;
+    const int gwarp = gtid >> 5, lane = tid & 31, g = lane >> 2, tq = lane & 3;
+    const int H = a.n_head, A = a.n_audio;
+    const int n_pairs = a.groups * H, G = gridDim.x;
+    const int n_tiles = (A + kAttnKeyTile - 1) / kAttnKeyTile;
+    const int my_tiles = (n_tiles - wg + 1) / 2;  // tiles wg, wg + 2, ... of every pair
+    const int my_pairs = blockIdx.x < n_pairs ? (n_pairs - 1 - blockIdx.x) / G + 1 : 0;
+    const int n_items = my_pairs * my_tiles;
+    __half *wbuf = sbuf + (size_t)wg * 2 * kTileHalves;
+
+    // stream liveness and stream of each group: written by the host or an earlier graph launch
+    auto live = [&](int pair) { return !a.active || a.active[pair / H] != 0; };
+    // rows of this warpgroup's item i into buffer i & 1, one cp.async group (empty if the
+    // stream has finished)
+    auto issue = [&](int i) {
+        const int pair = blockIdx.x + (i / my_tiles) * G, t = wg + 2 * (i % my_tiles);
+        if (live(pair)) {
+            const int group = pair / H, head = pair - group * H, j0 = t * kAttnKeyTile;
+            const int nk = min(kAttnKeyTile, A - j0);
+            const size_t off =
+                ((((size_t)a.stream_of_group[group] * a.n_layer + a.layer) * H + head) * (size_t)A + j0) * kHeadDim;
+            const __half *kg = a.kc + off, *vg = a.vc + off;
+            __half *tk = wbuf + (size_t)(i & 1) * kTileHalves, *tv = tk + kAttnKeyTile * kRowPad;
+            for (int c = gtid; c < nk * 8; c += kAttnThreads) {
+                const int r = c >> 3, part = c & 7;
+                cp_async16(&tk[r * kRowPad + part * 8], kg + (size_t)r * kHeadDim + part * 8);
+                cp_async16(&tv[r * kRowPad + part * 8], vg + (size_t)r * kHeadDim + part * 8);
+            }
+        }
+        cp_async_commit();
+    };
+    // this pair's queries (f32 registers; converted into qh when the pair starts)
+    auto load_q = [&](int pair, float4 &v) {
+        v = make_float4(0.f, 0.f, 0.f, 0.f);
+        const int i = gtid / (kHeadDim / 4), c = gtid % (kHeadDim / 4);
+        if (gtid < 8 * kHeadDim / 4 && i < NQ && pair < n_pairs && live(pair)) {
+            const int group = pair / H, head = pair - group * H;
+            v = reinterpret_cast<const float4 *>(a.q + (size_t)(group * NQ + i) * a.d + head * kHeadDim)[c];
+        }
+    };
+
+    if (n_items > 0) issue(0);
+    if (n_items > 1) issue(1);
+    pdl_trigger();
+    pdl_wait();
+    float4 qn;
+    load_q(blockIdx.x, qn);
+    const AttnShared sh{qh[wg], ps[wg], w_max[wg], w_sum[wg], s_m[wg], s_l[wg]};
+    float of[4][4];
+    for (int i = 0; i < n_items; ++i) {
+        const int k = i / my_tiles, j = i - k * my_tiles;
+        const int pair = blockIdx.x + k * G, t = wg + 2 * j;
+        const bool lv = live(pair);
+        const int nk = min(kAttnKeyTile, A - t * kAttnKeyTile);
+        __half *sk = wbuf + (size_t)(i & 1) * kTileHalves, *sv = sk + kAttnKeyTile * kRowPad;
+        if (j == 0) {  // a new pair: queries, running state; the next pair's queries start loading
+            if (gtid < 8 * kHeadDim / 4) {
+                const int qi = gtid / (kHeadDim / 4), c = gtid % (kHeadDim / 4);
+                const __half2 h0 = __floats2half2_rn(qn.x, qn.y), h1 = __floats2half2_rn(qn.z, qn.w);
+                *reinterpret_cast<uint2 *>(&qh[wg][qi][4 * c]) =
+                    make_uint2(*reinterpret_cast<const uint32_t *>(&h0), *reinterpret_cast<const uint32_t *>(&h1));
+            }
+            load_q(pair + G, qn);
+            if (gtid < 8) {
+                s_m[wg][gtid] = -INFINITY;
+                s_l[wg][gtid] = 0.f;
+            }
+#pragma unroll
+            for (int mt = 0; mt < 4; ++mt) of[mt][0] = of[mt][1] = of[mt][2] = of[mt][3] = 0.f;
+        }
+        // V rows past the tile's keys meet zero probabilities: they must not be stale
+        for (int c = gtid; c < (kAttnKeyTile - nk) * 8; c += kAttnThreads)
+            *reinterpret_cast<uint4 *>(&sv[(nk + (c >> 3)) * kRowPad + (c & 7) * 8]) = make_uint4(0u, 0u, 0u, 0u);
+        if (i + 1 < n_items) cp_async_wait_group<1>();  // the next tile may stay in flight
+        else cp_async_wait_group<0>();
+        group_sync(1 + wg);
+        if (lv) attn_tile<NQ>(sh, sk, sv, nk, of, gtid, 1 + wg);  // ends with a barrier: buffer consumed
+        if (i + 2 < n_items) issue(i + 2);
+        if (j == my_tiles - 1) {
+            // end of the pair: each warpgroup's O (sum over its warps), then both states combined
+            if (lv) {
+#pragma unroll
+                for (int mt = 0; mt < 4; ++mt) {
+                    const int q0 = 2 * tq, q1 = 2 * tq + 1, d0 = 16 * mt + g;
+                    if (q0 < NQ) {
+                        red[wg][gwarp][q0 * kHeadDim + d0] = of[mt][0];
+                        red[wg][gwarp][q0 * kHeadDim + d0 + 8] = of[mt][2];
+                    }
+                    if (q1 < NQ) {
+                        red[wg][gwarp][q1 * kHeadDim + d0] = of[mt][1];
+                        red[wg][gwarp][q1 * kHeadDim + d0 + 8] = of[mt][3];
+                    }
+                }
+            }
+            __syncthreads();
+            if (lv) {
+                const int group = pair / H, head = pair - group * H;
+                for (int pidx = tid; pidx < NQ * kHeadDim; pidx += kStreamThreads) {
+                    const int qi = pidx / kHeadDim, dd = pidx % kHeadDim;
+                    float o0 = 0.f, o1 = 0.f;
+#pragma unroll
+                    for (int w = 0; w < kWarps; ++w) {
+                        o0 += red[0][w][pidx];
+                        o1 += red[1][w][pidx];
+                    }
+                    // split combine as in the cluster kernel: weights exp(m_s - M), in split order
+                    const float m0 = s_m[0][qi], m1 = s_m[1][qi];
+                    const float M = fmaxf(m0, m1);
+                    float num = 0.f, den = 0.f;
+                    if (m0 != -INFINITY) {
+                        const float w = __expf(m0 - M);
+                        num = fmaf(w, o0, num);
+                        den = fmaf(w, s_l[0][qi], den);
+                    }
+                    if (m1 != -INFINITY) {
+                        const float w = __expf(m1 - M);
+                        num = fmaf(w, o1, num);
+                        den = fmaf(w, s_l[1][qi], den);
+                    }
+                    a.out[(size_t)(group * NQ + qi) * a.d + head * kHeadDim + dd] = num / den;
+                }
+            }
+            __syncthreads();  // red, s_m, s_l and qh of both warpgroups are free
+        }
+    }
+}
+
 // Key splits of one launch: up to kMaxSplits (one cluster); tiles each block stages.
 int attn_max_splits(int) { return kMaxSplits; }
 static int attn_tiles(const AttnArgs &a) {
@@ -344,7 +525,16 @@ static cudaError_t prep_nq() {
 }
 
 cudaError_t attn_prepare() {
-    cudaError_t e = prep_nq<1>();
+    cudaError_t e = allow_dynamic_smem(k_attn_stream<1>);
+    if (e == cudaSuccess) e = allow_dynamic_smem(k_attn_stream<2>);
+    if (e == cudaSuccess) e = allow_dynamic_smem(k_attn_stream<3>);
+    if (e == cudaSuccess) e = allow_dynamic_smem(k_attn_stream<4>);
+    if (e == cudaSuccess) e = allow_dynamic_smem(k_attn_stream<5>);
+    if (e == cudaSuccess) e = allow_dynamic_smem(k_attn_stream<6>);
+    if (e == cudaSuccess) e = allow_dynamic_smem(k_attn_stream<7>);
+    if (e == cudaSuccess) e = allow_dynamic_smem(k_attn_stream<8>);
+    if (e != cudaSuccess) return e;
+    e = prep_nq<1>();
     if (e == cudaSuccess) e = prep_nq<2>();
     if (e == cudaSuccess) e = prep_nq<3>();
     if (e == cudaSuccess) e = prep_nq<4>();
@@ -353,6 +543,42 @@ cudaError_t attn_prepare() {
     if (e == cudaSuccess) e = prep_nq<7>();
     if (e == cudaSuccess) e = prep_nq<8>();
     return e;
+}
+
+bool attn_stream_pays(const AttnArgs &a, int sms) {
+    // more (split, head, group) blocks than one resident wave of the cluster kernel; both
+    // warpgroups need a tile of every pair
+    return a.cross && a.n_audio > kAttnKeyTile && (long long)a.nsplit * a.n_head * a.groups > 2LL * sms;
+}
+
+static size_t stream_smem() { return 4 * (size_t)kTileHalves * sizeof(__half); }
+
+cudaError_t launch_attn_stream(const AttnArgs &a, int sms, cudaStream_t s, bool pdl) {
+    if (a.groups <= 0) return cudaSuccess;
+    if (!a.cross || a.nq < 1 || a.nq > kMaxNq || a.n_audio <= kAttnKeyTile) return cudaErrorInvalidValue;
+    const long long pairs = (long long)a.groups * a.n_head;
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = dim3((unsigned)(pairs < sms ? pairs : sms));
+    cfg.blockDim = dim3(kStreamThreads);
+    cfg.dynamicSmemBytes = stream_smem();
+    cfg.stream = s;
+    cudaLaunchAttribute attr[1];
+    if (pdl) {
+        attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+        attr[0].val.programmaticStreamSerializationAllowed = 1;
+    }
+    cfg.attrs = attr;
+    cfg.numAttrs = pdl ? 1 : 0;
+    switch (a.nq) {
+        case 1: return cudaLaunchKernelEx(&cfg, k_attn_stream<1>, a);
+        case 2: return cudaLaunchKernelEx(&cfg, k_attn_stream<2>, a);
+        case 3: return cudaLaunchKernelEx(&cfg, k_attn_stream<3>, a);
+        case 4: return cudaLaunchKernelEx(&cfg, k_attn_stream<4>, a);
+        case 5: return cudaLaunchKernelEx(&cfg, k_attn_stream<5>, a);
+        case 6: return cudaLaunchKernelEx(&cfg, k_attn_stream<6>, a);
+        case 7: return cudaLaunchKernelEx(&cfg, k_attn_stream<7>, a);
+        default: return cudaLaunchKernelEx(&cfg, k_attn_stream<8>, a);
+    }
 }
 
 cudaError_t launch_attn(const AttnArgs &a, cudaStream_t s, bool pdl) {

@@ -14,39 +14,51 @@
 //     the reference instead of rounding them to f16.  Rows hold the NU sequence slots (NU = M
 //     padded to 16, 32, 64 or 128; slots >= M are zero): hi in rows [0, NU), lo in [NU, 2 NU).
 //   * One thread issues tcgen05.mma.kind::f16 (M 128, N 2 NU, K 16) into an f32 accumulator in
-//     tensor memory; four warps read it back with tcgen05.ld and add the hi and lo columns.
-//   * With a split K the split blocks of a tile form a thread-block cluster: each leaves its
-//     partial tile in its own shared memory and, after a cluster barrier, block r adds the
-//     partials of its share of the rows in split order (distributed shared memory), so the
-//     result is deterministic, then applies the epilogue.
+//     tensor memory; eight warps read it back with tcgen05.ld and add the hi and lo columns.
+//   * With a split K the split blocks of a tile form a thread-block cluster.  Block q owns rows
+//     [q * 128 / ks, (q + 1) * 128 / ks) of the tile: every block stores its partial of those
+//     rows into the owner's shared memory (distributed shared memory stores), and after one
+//     cluster barrier the owner adds the partials in split order, so the result is
+//     deterministic, then applies the epilogue.
 // Every wait on a copy is bounded; a time-out raises the device error word.
 #include "tc_common.cuh"
 #include "w4j_internal.cuh"
 
 namespace w4j {
 
+constexpr int kGemmThreads = 512, kGemmWarps = kGemmThreads / 32;
+
 struct GemmTcLaunch {
-    int KB;        // 64-wide k-blocks in K
-    int ks;        // K splits (cluster size)
-    int nkb_max;   // k-blocks of the largest split
-    int n_stages;  // weight ring stages
-    unsigned b_off, ln_off, bias_off, mi_off, bar_off;  // shared-memory layout (bytes)
+    int KB;          // 64-wide k-blocks in K
+    int ks;          // K splits (cluster size)
+    int nkb_max;     // k-blocks of the largest split
+    int n_stages;    // weight ring stages
+    int rmax;        // most tile rows a split block owns: ceil(128 / ks)
+    int recv_alias;  // 1: the partials land in the weight ring (free once every block's MMAs are done)
+    unsigned b_off, ln_off, bias_off, mi_off, recv_off, bar_off;  // shared-memory layout (bytes)
 };
 
-__device__ __forceinline__ void gt_cluster_sync() {
-    asm volatile("barrier.cluster.arrive.release.aligned;\n\tbarrier.cluster.wait.acquire.aligned;" ::: "memory");
+__device__ __forceinline__ void cluster_arrive_relaxed() {
+    asm volatile("barrier.cluster.arrive.relaxed.aligned;" ::: "memory");
 }
-__device__ __forceinline__ float gt_ld_cluster(const float *local, unsigned rank) {
+__device__ __forceinline__ void cluster_arrive_release() {
+    asm volatile("barrier.cluster.arrive.release.aligned;" ::: "memory");
+}
+__device__ __forceinline__ void cluster_wait_acquire() {
+    asm volatile("barrier.cluster.wait.acquire.aligned;" ::: "memory");
+}
+__device__ __forceinline__ unsigned cluster_map(const void *local, unsigned rank) {
     unsigned remote;
     asm volatile("mapa.shared::cluster.u32 %0, %1, %2;" : "=r"(remote) : "r"(smem_u32(local)), "r"(rank));
-    float v;
-    asm volatile("ld.shared::cluster.f32 %0, [%1];" : "=f"(v) : "r"(remote) : "memory");
-    return v;
+    return remote;
+}
+__device__ __forceinline__ void st_cluster_f32(unsigned addr, float v) {
+    asm volatile("st.shared::cluster.f32 [%0], %1;" ::"r"(addr), "f"(v) : "memory");
 }
 
 template <int NU>
-__global__ void __launch_bounds__(256, 1) k_gemm_tc(GemvArgs a, const __grid_constant__ CUtensorMap tmap,
-                                                     GemmTcLaunch L) {
+__global__ void __launch_bounds__(kGemmThreads, 1) k_gemm_tc(GemvArgs a, const __grid_constant__ CUtensorMap tmap,
+                                                              GemmTcLaunch L) {
     extern __shared__ __align__(1024) unsigned char smem_raw[];
     unsigned char *smem = smem_raw + ((1024u - (smem_u32(smem_raw) & 1023u)) & 1023u);
     const int N = a.W.N, K = a.W.K, M = a.M;
@@ -60,13 +72,14 @@ __global__ void __launch_bounds__(256, 1) k_gemm_tc(GemvArgs a, const __grid_con
     float *ln_s = reinterpret_cast<float *>(smem + L.ln_off);      // gamma, beta of the K range
     float *bias_s = reinterpret_cast<float *>(smem + L.bias_off);  // [128]
     int *mi_s = reinterpret_cast<int *>(smem + L.mi_off);          // [4][M] active, slot, pos, token
+    // split-K partials of the rows this block owns: [split][M][rmax], written by the cluster
+    float *recv = reinterpret_cast<float *>(smem + (L.recv_alias ? 0u : L.recv_off));
     uint64_t *full = reinterpret_cast<uint64_t *>(smem + L.bar_off);
     uint64_t *empty = full + NS;
     uint64_t *accf = empty + NS;
     uint32_t *tslot = reinterpret_cast<uint32_t *>(accf + 1);
     volatile int *fail = reinterpret_cast<volatile int *>(tslot + 1);
     volatile int *issued = fail + 1;  // weight tiles whose copy has been started
-    float *part = reinterpret_cast<float *>(ring);  // [128][NU + 1] partial tile (after the MMAs)
     const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
     constexpr uint32_t kCols = NB;  // 32 .. 256 f32 columns
     const int kr = nkb * kKB;  // K range of this block: [kb0 * 64, kb0 * 64 + kr)
@@ -113,6 +126,8 @@ __global__ void __launch_bounds__(256, 1) k_gemm_tc(GemvArgs a, const __grid_con
         *reinterpret_cast<uint4 *>(bop + (size_t)kb * NB * 128 + (size_t)m * 128 + ((cc ^ (m & 7)) * 16)) =
             make_uint4(0, 0, 0, 0);
     }
+    // the cluster's blocks must all have started before one stores into another's shared memory
+    if (ks > 1 && !L.recv_alias) cluster_arrive_relaxed();
     pdl_trigger();
     pdl_wait();
     __syncthreads();
@@ -133,21 +148,22 @@ __global__ void __launch_bounds__(256, 1) k_gemm_tc(GemvArgs a, const __grid_con
             make_uint2(*reinterpret_cast<const uint32_t *>(&l0), *reinterpret_cast<const uint32_t *>(&l1));
     };
     if (a.in_mode == IN_ACT) {
+        // the K range of every row, 16 float4 loads in flight per thread
         const int r4 = kr / 4;  // float4 per row in the K range
         const int total = M * r4;
-        for (int i0 = tid; i0 < total; i0 += blockDim.x * 8) {
-            float4 v[8];
+        for (int i0 = tid; i0 < total; i0 += kGemmThreads * 16) {
+            float4 v[16];
 #pragma unroll
-            for (int j = 0; j < 8; ++j) {
-                const int i = i0 + blockDim.x * j;
+            for (int j = 0; j < 16; ++j) {
+                const int i = i0 + kGemmThreads * j;
                 if (i < total) {
                     const int m = i / r4, c4 = i - m * r4;
                     v[j] = reinterpret_cast<const float4 *>(a.act + (size_t)m * K + kb0 * kKB)[c4];
                 }
             }
 #pragma unroll
-            for (int j = 0; j < 8; ++j) {
-                const int i = i0 + blockDim.x * j;
+            for (int j = 0; j < 16; ++j) {
+                const int i = i0 + kGemmThreads * j;
                 if (i < total) {
                     const int m = i / r4, c4 = i - m * r4;
                     put4(m, 4 * c4, v[j]);
@@ -159,31 +175,7 @@ __global__ void __launch_bounds__(256, 1) k_gemm_tc(GemvArgs a, const __grid_con
         // one warp per row with the row in registers; then the K range is written
         constexpr int kLnF4 = 10;  // K <= 1280
         const int nf4 = K / 128;
-        for (int m = warp; m < M; m += 8) {
-            float4 v[kLnF4];
-            if (a.in_mode == IN_LN) {
-                const float4 *src = reinterpret_cast<const float4 *>(a.act + (size_t)m * K);
-#pragma unroll
-                for (int j = 0; j < kLnF4; ++j) v[j] = j < nf4 ? src[lane + 32 * j] : make_float4(0.f, 0.f, 0.f, 0.f);
-            } else {  // x = E[tok] + P[pos] (WhisperDecoder.java:66-80), kept in x_out by one block
-                const int tok = mi_s[3 * M + m], pos = mi_s[2 * M + m];
-                const uint2 *e = reinterpret_cast<const uint2 *>(a.E.h + (size_t)tok * K);
-                const float4 *pe = reinterpret_cast<const float4 *>(a.pos_emb + (size_t)pos * K);
-                uint2 eu[kLnF4];
-#pragma unroll
-                for (int j = 0; j < kLnF4; ++j) {
-                    eu[j] = j < nf4 ? e[lane + 32 * j] : make_uint2(0u, 0u);
-                    v[j] = j < nf4 ? pe[lane + 32 * j] : make_float4(0.f, 0.f, 0.f, 0.f);
-                }
-#pragma unroll
-                for (int j = 0; j < kLnF4; ++j) {
-                    const float2 lo = __half22float2(*reinterpret_cast<const __half2 *>(&eu[j].x));
-                    const float2 hi = __half22float2(*reinterpret_cast<const __half2 *>(&eu[j].y));
-                    v[j] = make_float4(lo.x + v[j].x, lo.y + v[j].y, hi.x + v[j].z, hi.y + v[j].w);
-                    if (j < nf4 && blockIdx.x == 0 && blockIdx.y == 0 && a.x_out)
-                        reinterpret_cast<float4 *>(a.x_out)[(size_t)m * (K / 4) + lane + 32 * j] = v[j];
-                }
-            }
+        auto ln_put = [&](int m, float4 (&v)[kLnF4]) {
             float sm = 0.f;
 #pragma unroll
             for (int j = 0; j < kLnF4; ++j)
@@ -206,6 +198,43 @@ __global__ void __launch_bounds__(256, 1) k_gemm_tc(GemvArgs a, const __grid_con
                     put4(m, kk, make_float4((v[j].x - mean) * inv_std * g.x + b.x, (v[j].y - mean) * inv_std * g.y + b.y,
                                             (v[j].z - mean) * inv_std * g.z + b.z, (v[j].w - mean) * inv_std * g.w + b.w));
                 }
+            }
+        };
+        if (a.in_mode == IN_LN) {
+            // two rows per warp in flight: rows m0 and m0 + 16
+            for (int m0 = warp; m0 < M; m0 += 2 * kGemmWarps) {
+                const int m1 = m0 + kGemmWarps;
+                const float4 *s0 = reinterpret_cast<const float4 *>(a.act + (size_t)m0 * K);
+                const float4 *s1 = reinterpret_cast<const float4 *>(a.act + (size_t)(m1 < M ? m1 : m0) * K);
+                float4 v0[kLnF4], v1[kLnF4];
+#pragma unroll
+                for (int j = 0; j < kLnF4; ++j) v0[j] = j < nf4 ? s0[lane + 32 * j] : make_float4(0.f, 0.f, 0.f, 0.f);
+#pragma unroll
+                for (int j = 0; j < kLnF4; ++j) v1[j] = j < nf4 ? s1[lane + 32 * j] : make_float4(0.f, 0.f, 0.f, 0.f);
+                ln_put(m0, v0);
+                if (m1 < M) ln_put(m1, v1);
+            }
+        } else {  // x = E[tok] + P[pos] (WhisperDecoder.java:66-80), kept in x_out by one block
+            for (int m = warp; m < M; m += kGemmWarps) {
+                const int tok = mi_s[3 * M + m], pos = mi_s[2 * M + m];
+                const uint2 *e = reinterpret_cast<const uint2 *>(a.E.h + (size_t)tok * K);
+                const float4 *pe = reinterpret_cast<const float4 *>(a.pos_emb + (size_t)pos * K);
+                float4 v[kLnF4];
+                uint2 eu[kLnF4];
+#pragma unroll
+                for (int j = 0; j < kLnF4; ++j) {
+                    eu[j] = j < nf4 ? e[lane + 32 * j] : make_uint2(0u, 0u);
+                    v[j] = j < nf4 ? pe[lane + 32 * j] : make_float4(0.f, 0.f, 0.f, 0.f);
+                }
+#pragma unroll
+                for (int j = 0; j < kLnF4; ++j) {
+                    const float2 lo = __half22float2(*reinterpret_cast<const __half2 *>(&eu[j].x));
+                    const float2 hi = __half22float2(*reinterpret_cast<const __half2 *>(&eu[j].y));
+                    v[j] = make_float4(lo.x + v[j].x, lo.y + v[j].y, hi.x + v[j].z, hi.y + v[j].w);
+                    if (j < nf4 && blockIdx.x == 0 && blockIdx.y == 0 && a.x_out)
+                        reinterpret_cast<float4 *>(a.x_out)[(size_t)m * (K / 4) + lane + 32 * j] = v[j];
+                }
+                ln_put(m, v);
             }
         }
     }
@@ -281,44 +310,67 @@ __global__ void __launch_bounds__(256, 1) k_gemm_tc(GemvArgs a, const __grid_con
         umma_commit(accf);  // the accumulator is complete (or nothing was issued)
     }
     __syncthreads();
-    if (warp >= 4) {
-        // ---- TMEM -> registers: row q * 32 + lane of the tile; slot m = hi column m + lo column NU + m ----
-        const int q = warp - 4, r = q * 32 + lane;
-        const bool ok = !*fail && mbar_wait(accf, 0u, a.err);
+    // ---- epilogue warps 8 .. 15: warp w reads TMEM lanes 32 (w % 4) .., column group (w - 8) / 4 ----
+    const bool epi = warp >= 8;
+    const int q4 = warp & 3, cg = (warp - 8) >> 2, r = q4 * 32 + lane;
+    bool ok = true;
+    if (epi) {
+        ok = !*fail && mbar_wait(accf, 0u, a.err);
         if (!ok) *fail = 1;
         tc_fence_after();
-#pragma unroll
-        for (int c0 = 0; c0 < NU; c0 += 16) {
-            float v[16], lo[16];
-            tmem_ld16(taddr + ((uint32_t)(q * 32) << 16) + (uint32_t)c0, v);
-            tmem_ld16(taddr + ((uint32_t)(q * 32) << 16) + (uint32_t)(NU + c0), lo);
-#pragma unroll
-            for (int e = 0; e < 16; ++e) v[e] += lo[e];
-            if (ks == 1) {
+    }
+    if (ks == 1) {
+        if (epi)
+            for (int c0 = 16 * cg; c0 < NU; c0 += 32) {
+                // slot m = hi column m + lo column NU + m
+                float v[16], lo[16];
+                tmem_ld16(taddr + ((uint32_t)(q4 * 32) << 16) + (uint32_t)c0, v);
+                tmem_ld16(taddr + ((uint32_t)(q4 * 32) << 16) + (uint32_t)(NU + c0), lo);
                 if (ok)
 #pragma unroll
-                    for (int e = 0; e < 16; ++e) emit(v[e], r, c0 + e);
-            } else if (ok) {  // the ring is free: every copy into it was consumed
-#pragma unroll
-                for (int e = 0; e < 16; ++e) part[(size_t)r * (NU + 1) + c0 + e] = v[e];
+                    for (int e = 0; e < 16; ++e) emit(v[e] + lo[e], r, c0 + e);
             }
+        if (epi) tc_fence_before();
+    } else {
+        const int R = L.rmax;
+        if (L.recv_alias) {
+            // the partials go into the weight ring: every block of the cluster must be past its
+            // MMAs (its epilogue warps saw the accumulator complete) before any of them stores
+            __syncwarp();
+            cluster_arrive_relaxed();
         }
-        tc_fence_before();
+        __syncwarp();
+        cluster_wait_acquire();
+        if (epi) {
+            // row r belongs to block o: partial -> o's recv[split][m][r - r0(o)]
+            int o = 0;
+            while (o + 1 < ks && ((o + 1) * kTileRows) / ks <= r) ++o;
+            const int rr = r - (o * kTileRows) / ks;
+            const unsigned dst = cluster_map(recv, (unsigned)o) + (unsigned)((split * M * R + rr) * 4);
+            for (int c0 = 16 * cg; c0 < NU; c0 += 32) {
+                float v[16], lo[16];
+                tmem_ld16(taddr + ((uint32_t)(q4 * 32) << 16) + (uint32_t)c0, v);
+                tmem_ld16(taddr + ((uint32_t)(q4 * 32) << 16) + (uint32_t)(NU + c0), lo);
+#pragma unroll
+                for (int e = 0; e < 16; ++e)
+                    if (c0 + e < M) st_cluster_f32(dst + (unsigned)((c0 + e) * R * 4), v[e] + lo[e]);
+            }
+            tc_fence_before();
+        }
+        __syncwarp();
+        cluster_arrive_release();
+        cluster_wait_acquire();
+        // the owned rows [r0, r0 + nr): add the ks partials in split order, then the epilogue
+        const int r0 = (split * kTileRows) / ks, nr = ((split + 1) * kTileRows) / ks - r0;
+        if (!*fail)
+            for (int i = tid; i < nr * M; i += kGemmThreads) {
+                const int m = i / nr, rr = i - m * nr;  // neighbouring threads: neighbouring outputs
+                float acc = 0.f;
+                for (int q = 0; q < ks; ++q) acc += recv[(q * M + m) * R + rr];
+                emit(acc, r0 + rr, m);
+            }
     }
     __syncthreads();
-    if (ks > 1) {
-        // every split's partial is in its block's shared memory: block `split` adds rows
-        // [split * 128 / ks, (split + 1) * 128 / ks) over all splits, in split order
-        gt_cluster_sync();
-        const int r0 = (split * kTileRows) / ks, nr = ((split + 1) * kTileRows) / ks - r0;
-        for (int i = tid; i < nr * M && !*fail; i += blockDim.x) {
-            const int m = i / nr, r = r0 + i % nr;  // neighbouring threads: neighbouring outputs
-            float acc = 0.f;
-            for (int q = 0; q < ks; ++q) acc += gt_ld_cluster(&part[(size_t)r * (NU + 1) + m], (unsigned)q);
-            emit(acc, r, m);
-        }
-        gt_cluster_sync();  // no block leaves while its partial may still be read
-    }
     if (*fail && tid == 0) drain_ring(full, NS, *issued);
     if (warp == 1) {
         tc_fence_after();
@@ -331,6 +383,11 @@ __global__ void __launch_bounds__(256, 1) k_gemm_tc(GemvArgs a, const __grid_con
 // ---------------------------------------------------------------------------
 static int nu_for(int M) { return M <= 16 ? 16 : M <= 32 ? 32 : M <= 64 ? 64 : 128; }
 
+// Clusters of each size that can be resident at once (a cluster's blocks share one GPC, so
+// fewer clusters of 8 fit than 148 / 8); 0 = not queried.  A launch keeps its tiles within one
+// wave of clusters.
+static int g_max_clusters[9];
+
 static bool plan_gemm_tc(const GemvArgs &a, int sms, int &nu, GemmTcLaunch &L, int &tiles) {
     const int M = a.M, N = a.W.N, K = a.W.K;
     if (M < 16 || M > 128 || a.W.type != WT_F16 || K % kKB != 0 || N < 1) return false;
@@ -342,18 +399,23 @@ static bool plan_gemm_tc(const GemvArgs &a, int sms, int &nu, GemmTcLaunch &L, i
     int ks = sms / tiles;
     ks = ks < 1 ? 1 : ks > 8 ? 8 : ks;
     if (ks > L.KB) ks = L.KB;
+    while (ks > 1 && g_max_clusters[ks] > 0 && g_max_clusters[ks] < tiles) --ks;
     L.ks = ks;
     L.nkb_max = (L.KB + ks - 1) / ks;
     const size_t bbytes = (size_t)L.nkb_max * 2 * nu * 128;  // hi and lo rows
     const size_t lnbytes = a.in_mode == IN_ACT ? 0 : (size_t)2 * L.nkb_max * kKB * 4;
     const size_t mibytes = ((size_t)4 * M * 4 + 15) & ~(size_t)15;
-    const size_t partbytes = (size_t)kTileRows * (nu + 1) * 4;
+    L.rmax = (kTileRows + ks - 1) / ks;
+    const size_t recvbytes = ks > 1 ? (((size_t)ks * M * L.rmax * 4 + 15) & ~(size_t)15) : 0;
     const size_t fixed = bbytes + lnbytes + 512 + mibytes + 256;
     const size_t budget = 220 * 1024;
-    int ns_need = (int)((partbytes + kStageBytes - 1) / kStageBytes);
+    // the partials get their own buffer when it fits beside two stages, else they reuse the ring
+    L.recv_alias = fixed + recvbytes + 2 * (size_t)kStageBytes > budget;
+    const size_t own = L.recv_alias ? 0 : recvbytes;
+    int ns_need = L.recv_alias ? (int)((recvbytes + kStageBytes - 1) / kStageBytes) : 2;
     if (ns_need < 2) ns_need = 2;
-    if (fixed + (size_t)ns_need * kStageBytes > budget) return false;
-    int ns = (int)((budget - fixed) / kStageBytes);  // as many stages as fit, up to the k-blocks
+    if (fixed + own + (size_t)ns_need * kStageBytes > budget) return false;
+    int ns = (int)((budget - fixed - own) / kStageBytes);  // as many stages as fit, up to the k-blocks
     if (ns > 8) ns = 8;
     if (ns > L.nkb_max) ns = L.nkb_max;
     if (ns < ns_need) ns = ns_need;
@@ -362,7 +424,8 @@ static bool plan_gemm_tc(const GemvArgs &a, int sms, int &nu, GemmTcLaunch &L, i
     L.ln_off = L.b_off + (unsigned)bbytes;
     L.bias_off = L.ln_off + (unsigned)lnbytes;
     L.mi_off = L.bias_off + 512;
-    L.bar_off = L.mi_off + (unsigned)mibytes;
+    L.recv_off = L.mi_off + (unsigned)mibytes;
+    L.bar_off = L.recv_off + (unsigned)own;
     return true;
 }
 
@@ -386,7 +449,7 @@ static cudaError_t launch_gemm_tc_t(const GemvArgs &a, const CUtensorMap &map, c
                                     cudaStream_t s, bool pdl) {
     cudaLaunchConfig_t cfg = {};
     cfg.gridDim = dim3(L.ks, tiles);
-    cfg.blockDim = dim3(256);
+    cfg.blockDim = dim3(kGemmThreads);
     cfg.dynamicSmemBytes = gemm_tc_smem(L, NU);
     cfg.stream = s;
     cudaLaunchAttribute attr[2];
@@ -413,7 +476,25 @@ cudaError_t gemm_tc_prepare() {
     if (e == cudaSuccess) e = allow_dynamic_smem(k_gemm_tc<32>);
     if (e == cudaSuccess) e = allow_dynamic_smem(k_gemm_tc<64>);
     if (e == cudaSuccess) e = allow_dynamic_smem(k_gemm_tc<128>);
-    return e;
+    if (e != cudaSuccess) return e;
+    // one block per SM (the register file), so the count does not depend on shared memory
+    for (int ks = 2; ks <= 8; ++ks) {
+        cudaLaunchConfig_t cfg = {};
+        cfg.gridDim = dim3(ks);
+        cfg.blockDim = dim3(kGemmThreads);
+        cfg.dynamicSmemBytes = 100 * 1024;
+        cudaLaunchAttribute attr;
+        attr.id = cudaLaunchAttributeClusterDimension;
+        attr.val.clusterDim.x = ks;
+        attr.val.clusterDim.y = 1;
+        attr.val.clusterDim.z = 1;
+        cfg.attrs = &attr;
+        cfg.numAttrs = 1;
+        int n = 0;
+        if (cudaOccupancyMaxActiveClusters(&n, k_gemm_tc<32>, &cfg) == cudaSuccess) g_max_clusters[ks] = n;
+        else cudaGetLastError();
+    }
+    return cudaSuccess;
 }
 
 // cudaErrorNotSupported when the projection is outside the tensor-core kernel's range.

@@ -645,7 +645,8 @@ static int run_layers(w4j_ctx *c, const PassArgs &pa, long long &launches) {
         ca.out = c->attn;
         ca.active = pa.group_active;
         ca.err = c->st.err;
-        CUDA_TRY(launch_attn(ca, c->stream, pdl));
+        if (attn_stream_pays(ca, c->sm_count)) CUDA_TRY(launch_attn_stream(ca, c->sm_count, c->stream, pdl));
+        else CUDA_TRY(launch_attn(ca, c->stream, pdl));
 
         GemvArgs gxo;
         gxo.W = ly.xo;
