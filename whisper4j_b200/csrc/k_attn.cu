@@ -367,37 +367,120 @@ __global__ void __launch_bounds__(kAttnThreads) k_attn(AttnArgs a) {
 // ---------------------------------------------------------------------------
 // Streaming cross-attention for many (group, head) pairs (batched greedy / beam decoding).
 // One block per SM walks the pairs round-robin.  Its two warpgroups of 256 threads take the
-// even and the odd 128-key tiles of a pair, each with its own online-softmax state and two tile
-// buffers, so the rows of a warpgroup's next tile stream in (cp.async) while it computes the
-// current one, across pair boundaries, and the first tiles before griddepcontrol.wait.  At the
-// end of a pair the two states are combined in shared memory (even tiles first), so no partial
-// leaves the SM and the result does not depend on timing.  Needs n_audio > 128 (a tile for each
-// warpgroup in every pair: both meet at the block barrier that ends a pair).
+// even and the odd 128-key tiles of a pair with three tile buffers each: while a warpgroup
+// computes a tile, the rows of its next two tiles stream in (cp.async), across pair boundaries,
+// the first two before griddepcontrol.wait.  Tile rows are 128 B with the 16-byte chunks
+// XOR-swizzled by the row (chunk c of row r at c ^ (r & 7)), so ldmatrix reads are conflict-free
+// without padding.  Every warp keeps its own online-softmax state over its 16
+// keys of each tile, so a tile costs one warpgroup barrier (the rows have landed, the other
+// buffer is free); at the end of a pair the 16 warp states are combined in shared memory in a
+// fixed order, so no partial leaves the SM and the result does not depend on timing.  Needs
+// n_audio > 128 (a tile for each warpgroup in every pair: both meet at the block barrier that
+// ends a pair).
 // ---------------------------------------------------------------------------
 constexpr int kStreamThreads = 2 * kAttnThreads;
+constexpr int kPwPad = 24;  // halves per row of a warp's P^T block (48 B: conflict-free ldmatrix)
+constexpr int kStreamBufs = 3;                           // tile buffers per warpgroup
+constexpr int kStreamTile = 2 * kAttnKeyTile * kHeadDim;  // halves of one K tile + one V tile
+// offset (halves) of 16-byte chunk c of row r in a swizzled 128-byte-row tile
+__device__ __forceinline__ int swz(int r, int c) { return r * kHeadDim + ((c ^ (r & 7)) << 3); }
+
+// One warp's 16 keys [16 w, 16 w + 16) of a 128-key tile, online softmax kept per warp: m / l
+// are the running max / denominator of queries 2 tq and 2 tq + 1, of[4][4] the O^T fragments.
+template <int NQ>
+__device__ __forceinline__ void tile_warp(const __half *sk, const __half *sv, int nk, const __half (*qh)[kHeadDim + 8],
+                                          __half (*pw)[kPwPad], float (&m)[2], float (&l)[2], float (&of)[4][4],
+                                          int gwarp, int lane) {
+    const int g = lane >> 2, tq = lane & 3, kb = 16 * gwarp;
+    const float scale = 0.125f;  // (float)(1 / sqrt(64))
+    float sc[4] = {0.f, 0.f, 0.f, 0.f};
+    if (kb < nk) {
+#pragma unroll
+        for (int kk = 0; kk < 4; ++kk) {
+            uint32_t af[4], bf[2];
+            ldsm_x4(af, &sk[swz(kb + (lane & 15), 2 * kk + (lane >> 4))]);
+            ldsm_x2(bf, &qh[lane & 7][16 * kk + ((lane >> 3) & 1) * 8]);
+            mma_16816(sc, af, bf);
+        }
+    }
+    // c0: (key kb+g, query 2tq), c1: (kb+g, 2tq+1), c2: (kb+g+8, 2tq), c3: (kb+g+8, 2tq+1)
+    const int q0 = 2 * tq, q1 = 2 * tq + 1;
+    const bool k0ok = kb + g < nk, k1ok = kb + g + 8 < nk;
+    sc[0] = (k0ok && q0 < NQ) ? sc[0] * scale : -INFINITY;
+    sc[1] = (k0ok && q1 < NQ) ? sc[1] * scale : -INFINITY;
+    sc[2] = (k1ok && q0 < NQ) ? sc[2] * scale : -INFINITY;
+    sc[3] = (k1ok && q1 < NQ) ? sc[3] * scale : -INFINITY;
+    float mx0 = fmaxf(sc[0], sc[2]), mx1 = fmaxf(sc[1], sc[3]);
+#pragma unroll
+    for (int o = 4; o < 32; o <<= 1) {
+        mx0 = fmaxf(mx0, __shfl_xor_sync(0xffffffffu, mx0, o));
+        mx1 = fmaxf(mx1, __shfl_xor_sync(0xffffffffu, mx1, o));
+    }
+    const float mn0 = fmaxf(m[0], mx0), mn1 = fmaxf(m[1], mx1);
+    const float p0 = sc[0] == -INFINITY ? 0.f : __expf(sc[0] - mn0);
+    const float p1 = sc[1] == -INFINITY ? 0.f : __expf(sc[1] - mn1);
+    const float p2 = sc[2] == -INFINITY ? 0.f : __expf(sc[2] - mn0);
+    const float p3 = sc[3] == -INFINITY ? 0.f : __expf(sc[3] - mn1);
+    float sm0 = p0 + p2, sm1 = p1 + p3;
+#pragma unroll
+    for (int o = 4; o < 32; o <<= 1) {
+        sm0 += __shfl_xor_sync(0xffffffffu, sm0, o);
+        sm1 += __shfl_xor_sync(0xffffffffu, sm1, o);
+    }
+    const float al0 = m[0] == -INFINITY ? 0.f : __expf(m[0] - mn0);
+    const float al1 = m[1] == -INFINITY ? 0.f : __expf(m[1] - mn1);
+    l[0] = l[0] * al0 + sm0;
+    l[1] = l[1] * al1 + sm1;
+    m[0] = mn0;
+    m[1] = mn1;
+#pragma unroll
+    for (int mt = 0; mt < 4; ++mt) {
+        of[mt][0] *= al0;
+        of[mt][1] *= al1;
+        of[mt][2] *= al0;
+        of[mt][3] *= al1;
+    }
+    if (kb < nk) {
+        // O^T (16 dims x 8 queries, 4 tiles) += V^T (16 dims x 16 keys) . P^T (16 keys x 8 queries)
+        pw[q0][g] = __float2half_rn(p0);
+        pw[q1][g] = __float2half_rn(p1);
+        pw[q0][g + 8] = __float2half_rn(p2);
+        pw[q1][g + 8] = __float2half_rn(p3);
+        __syncwarp();
+        uint32_t bf[2];
+        ldsm_x2(bf, &pw[lane & 7][((lane >> 3) & 1) * 8]);
+#pragma unroll
+        for (int mt = 0; mt < 4; ++mt) {
+            uint32_t af[4];
+            ldsm_x4_t(af, &sv[swz(kb + (lane & 7) + ((lane >> 4) & 1) * 8, 2 * mt + ((lane >> 3) & 1))]);
+            mma_16816(of[mt], af, bf);
+        }
+        __syncwarp();  // pw is rewritten by the next tile
+    }
+}
 
 template <int NQ>
 __global__ void __launch_bounds__(kStreamThreads, 1) k_attn_stream(AttnArgs a) {
-    extern __shared__ __align__(16) __half sbuf[];  // [warpgroup][2 buffers][K tile | V tile]
+    extern __shared__ __align__(16) __half sbuf[];  // [warpgroup][kStreamBufs][K tile | V tile]
     __shared__ __align__(16) __half qh[2][8][kHeadDim + 8];
-    __shared__ __align__(16) __half ps[2][8][kAttnKeyTile + 8];
-    __shared__ float w_max[2][kWarps][8], w_sum[2][kWarps][8];
-    __shared__ float s_m[2][8], s_l[2][8];
-    __shared__ __align__(16) float red[2][kWarps][NQ * kHeadDim];
+    __shared__ __align__(16) __half pw[2 * kWarps][8][kPwPad];
+    __shared__ float wm[2 * kWarps][8], wl[2 * kWarps][8];
+    __shared__ __align__(16) float red[2 * kWarps][NQ * kHeadDim];
     const int tid = threadIdx.x, wg = tid / kAttnThreads, gtid = tid % kAttnThreads;
-    const int gwarp = gtid >> 5, lane = tid & 31, g = lane >> 2, tq = lane & 3;
+    const int warp = tid >> 5, gwarp = gtid >> 5, lane = tid & 31, g = lane >> 2, tq = lane & 3;
     const int H = a.n_head, A = a.n_audio;
     const int n_pairs = a.groups * H, G = gridDim.x;
     const int n_tiles = (A + kAttnKeyTile - 1) / kAttnKeyTile;
     const int my_tiles = (n_tiles - wg + 1) / 2;  // tiles wg, wg + 2, ... of every pair
     const int my_pairs = blockIdx.x < n_pairs ? (n_pairs - 1 - blockIdx.x) / G + 1 : 0;
     const int n_items = my_pairs * my_tiles;
-    __half *wbuf = sbuf + (size_t)wg * 2 * kTileHalves;
+    __half *wbuf = sbuf + (size_t)wg * kStreamBufs * kStreamTile;
 
     // stream liveness and stream of each group: written by the host or an earlier graph launch
     auto live = [&](int pair) { return !a.active || a.active[pair / H] != 0; };
-    // rows of this warpgroup's item i into buffer i & 1, one cp.async group (empty if the
-    // stream has finished)
+    // rows of this warpgroup's item i into buffer i % 3 as one cp.async group (empty if the
+    // stream has finished); V rows past a short tile's keys are zeroed (they meet zero
+    // probabilities and must not be stale)
     auto issue = [&](int i) {
         const int pair = blockIdx.x + (i / my_tiles) * G, t = wg + 2 * (i % my_tiles);
         if (live(pair)) {
@@ -406,16 +489,18 @@ __global__ void __launch_bounds__(kStreamThreads, 1) k_attn_stream(AttnArgs a) {
             const size_t off =
                 ((((size_t)a.stream_of_group[group] * a.n_layer + a.layer) * H + head) * (size_t)A + j0) * kHeadDim;
             const __half *kg = a.kc + off, *vg = a.vc + off;
-            __half *tk = wbuf + (size_t)(i & 1) * kTileHalves, *tv = tk + kAttnKeyTile * kRowPad;
+            __half *tk = wbuf + (size_t)(i % kStreamBufs) * kStreamTile, *tv = tk + kAttnKeyTile * kHeadDim;
             for (int c = gtid; c < nk * 8; c += kAttnThreads) {
                 const int r = c >> 3, part = c & 7;
-                cp_async16(&tk[r * kRowPad + part * 8], kg + (size_t)r * kHeadDim + part * 8);
-                cp_async16(&tv[r * kRowPad + part * 8], vg + (size_t)r * kHeadDim + part * 8);
+                cp_async16(&tk[swz(r, part)], kg + (size_t)r * kHeadDim + part * 8);
+                cp_async16(&tv[swz(r, part)], vg + (size_t)r * kHeadDim + part * 8);
             }
+            for (int c = gtid; c < (kAttnKeyTile - nk) * 8; c += kAttnThreads)
+                *reinterpret_cast<uint4 *>(&tv[(nk + (c >> 3)) * kHeadDim + (c & 7) * 8]) = make_uint4(0u, 0u, 0u, 0u);
         }
         cp_async_commit();
     };
-    // this pair's queries (f32 registers; converted into qh when the pair starts)
+    // a pair's queries (f32 registers; converted into qh when the pair starts)
     auto load_q = [&](int pair, float4 &v) {
         v = make_float4(0.f, 0.f, 0.f, 0.f);
         const int i = gtid / (kHeadDim / 4), c = gtid % (kHeadDim / 4);
@@ -431,15 +516,14 @@ __global__ void __launch_bounds__(kStreamThreads, 1) k_attn_stream(AttnArgs a) {
     pdl_wait();
     float4 qn;
     load_q(blockIdx.x, qn);
-    const AttnShared sh{qh[wg], ps[wg], w_max[wg], w_sum[wg], s_m[wg], s_l[wg]};
-    float of[4][4];
+    float m[2], l[2], of[4][4];
     for (int i = 0; i < n_items; ++i) {
         const int k = i / my_tiles, j = i - k * my_tiles;
         const int pair = blockIdx.x + k * G, t = wg + 2 * j;
         const bool lv = live(pair);
         const int nk = min(kAttnKeyTile, A - t * kAttnKeyTile);
-        __half *sk = wbuf + (size_t)(i & 1) * kTileHalves, *sv = sk + kAttnKeyTile * kRowPad;
-        if (j == 0) {  // a new pair: queries, running state; the next pair's queries start loading
+        const __half *sk = wbuf + (size_t)(i % kStreamBufs) * kStreamTile, *sv = sk + kAttnKeyTile * kHeadDim;
+        if (j == 0) {  // a new pair: queries and state; the next pair's queries start loading
             if (gtid < 8 * kHeadDim / 4) {
                 const int qi = gtid / (kHeadDim / 4), c = gtid % (kHeadDim / 4);
                 const __half2 h0 = __floats2half2_rn(qn.x, qn.y), h1 = __floats2half2_rn(qn.z, qn.w);
@@ -447,34 +531,35 @@ __global__ void __launch_bounds__(kStreamThreads, 1) k_attn_stream(AttnArgs a) {
                     make_uint2(*reinterpret_cast<const uint32_t *>(&h0), *reinterpret_cast<const uint32_t *>(&h1));
             }
             load_q(pair + G, qn);
-            if (gtid < 8) {
-                s_m[wg][gtid] = -INFINITY;
-                s_l[wg][gtid] = 0.f;
-            }
+            m[0] = m[1] = -INFINITY;
+            l[0] = l[1] = 0.f;
 #pragma unroll
             for (int mt = 0; mt < 4; ++mt) of[mt][0] = of[mt][1] = of[mt][2] = of[mt][3] = 0.f;
         }
-        // V rows past the tile's keys meet zero probabilities: they must not be stale
-        for (int c = gtid; c < (kAttnKeyTile - nk) * 8; c += kAttnThreads)
-            *reinterpret_cast<uint4 *>(&sv[(nk + (c >> 3)) * kRowPad + (c & 7) * 8]) = make_uint4(0u, 0u, 0u, 0u);
-        if (i + 1 < n_items) cp_async_wait_group<1>();  // the next tile may stay in flight
+        if (i + 1 < n_items) cp_async_wait_group<1>();  // tile i + 1 may stay in flight
         else cp_async_wait_group<0>();
-        group_sync(1 + wg);
-        if (lv) attn_tile<NQ>(sh, sk, sv, nk, of, gtid, 1 + wg);  // ends with a barrier: buffer consumed
+        group_sync(1 + wg);  // tile i has landed (and qh is written); tile i - 1's buffer is free
         if (i + 2 < n_items) issue(i + 2);
+        if (lv) tile_warp<NQ>(sk, sv, nk, qh[wg], pw[warp], m, l, of, gwarp, lane);
         if (j == my_tiles - 1) {
-            // end of the pair: each warpgroup's O (sum over its warps), then both states combined
+            // end of the pair: the 16 warp states, combined in warp order
             if (lv) {
+                if (g == 0) {
+                    wm[warp][2 * tq] = m[0];
+                    wm[warp][2 * tq + 1] = m[1];
+                    wl[warp][2 * tq] = l[0];
+                    wl[warp][2 * tq + 1] = l[1];
+                }
 #pragma unroll
                 for (int mt = 0; mt < 4; ++mt) {
                     const int q0 = 2 * tq, q1 = 2 * tq + 1, d0 = 16 * mt + g;
                     if (q0 < NQ) {
-                        red[wg][gwarp][q0 * kHeadDim + d0] = of[mt][0];
-                        red[wg][gwarp][q0 * kHeadDim + d0 + 8] = of[mt][2];
+                        red[warp][q0 * kHeadDim + d0] = of[mt][0];
+                        red[warp][q0 * kHeadDim + d0 + 8] = of[mt][2];
                     }
                     if (q1 < NQ) {
-                        red[wg][gwarp][q1 * kHeadDim + d0] = of[mt][1];
-                        red[wg][gwarp][q1 * kHeadDim + d0 + 8] = of[mt][3];
+                        red[warp][q1 * kHeadDim + d0] = of[mt][1];
+                        red[warp][q1 * kHeadDim + d0 + 8] = of[mt][3];
                     }
                 }
             }
@@ -483,30 +568,21 @@ __global__ void __launch_bounds__(kStreamThreads, 1) k_attn_stream(AttnArgs a) {
                 const int group = pair / H, head = pair - group * H;
                 for (int pidx = tid; pidx < NQ * kHeadDim; pidx += kStreamThreads) {
                     const int qi = pidx / kHeadDim, dd = pidx % kHeadDim;
-                    float o0 = 0.f, o1 = 0.f;
+                    float M = -INFINITY;
 #pragma unroll
-                    for (int w = 0; w < kWarps; ++w) {
-                        o0 += red[0][w][pidx];
-                        o1 += red[1][w][pidx];
-                    }
-                    // split combine as in the cluster kernel: weights exp(m_s - M), in split order
-                    const float m0 = s_m[0][qi], m1 = s_m[1][qi];
-                    const float M = fmaxf(m0, m1);
+                    for (int w = 0; w < 2 * kWarps; ++w) M = fmaxf(M, wm[w][qi]);
                     float num = 0.f, den = 0.f;
-                    if (m0 != -INFINITY) {
-                        const float w = __expf(m0 - M);
-                        num = fmaf(w, o0, num);
-                        den = fmaf(w, s_l[0][qi], den);
-                    }
-                    if (m1 != -INFINITY) {
-                        const float w = __expf(m1 - M);
-                        num = fmaf(w, o1, num);
-                        den = fmaf(w, s_l[1][qi], den);
-                    }
+#pragma unroll
+                    for (int w = 0; w < 2 * kWarps; ++w)
+                        if (wm[w][qi] != -INFINITY) {
+                            const float wt = __expf(wm[w][qi] - M);
+                            num = fmaf(wt, red[w][pidx], num);
+                            den = fmaf(wt, wl[w][qi], den);
+                        }
                     a.out[(size_t)(group * NQ + qi) * a.d + head * kHeadDim + dd] = num / den;
                 }
             }
-            __syncthreads();  // red, s_m, s_l and qh of both warpgroups are free
+            __syncthreads();  // wm, wl, red and qh of both warpgroups are free
         }
     }
 }
@@ -551,7 +627,7 @@ bool attn_stream_pays(const AttnArgs &a, int sms) {
     return a.cross && a.n_audio > kAttnKeyTile && (long long)a.nsplit * a.n_head * a.groups > 2LL * sms;
 }
 
-static size_t stream_smem() { return 4 * (size_t)kTileHalves * sizeof(__half); }
+static size_t stream_smem() { return 2 * kStreamBufs * (size_t)kStreamTile * sizeof(__half); }
 
 cudaError_t launch_attn_stream(const AttnArgs &a, int sms, cudaStream_t s, bool pdl) {
     if (a.groups <= 0) return cudaSuccess;
