@@ -17,6 +17,7 @@
 // so the result is deterministic and no partial goes through global memory.  Self-attention
 // rows are gathered through the beam table (position -> physical slot), which replaces the
 // reference's per-beam cache copies (WhisperDecoder.java:343-361).
+#include "tc_common.cuh"
 #include "w4j_internal.cuh"
 
 namespace w4j {
@@ -367,21 +368,23 @@ __global__ void __launch_bounds__(kAttnThreads) k_attn(AttnArgs a) {
 // ---------------------------------------------------------------------------
 // Streaming cross-attention for many (group, head) pairs (batched greedy / beam decoding).
 // One block per SM walks the pairs round-robin.  Its two warpgroups of 256 threads take the
-// even and the odd 128-key tiles of a pair with three tile buffers each: while a warpgroup
-// computes a tile, the rows of its next two tiles stream in (cp.async), across pair boundaries,
-// the first two before griddepcontrol.wait.  Tile rows are 128 B with the 16-byte chunks
-// XOR-swizzled by the row (chunk c of row r at c ^ (r & 7)), so ldmatrix reads are conflict-free
-// without padding.  Every warp keeps its own online-softmax state over its 16
-// keys of each tile, so a tile costs one warpgroup barrier (the rows have landed, the other
-// buffer is free); at the end of a pair the 16 warp states are combined in shared memory in a
-// fixed order, so no partial leaves the SM and the result does not depend on timing.  Needs
-// n_audio > 128 (a tile for each warpgroup in every pair: both meet at the block barrier that
-// ends a pair).
+// even and the odd 128-key tiles of a pair.  Each warpgroup streams its tiles through three
+// buffers with TMA (cp.async.bulk.tensor.2d over the cross K and V caches viewed as
+// [rows][64] f16, 128-byte swizzle: chunk c of row r lands at c ^ (r & 7), so ldmatrix reads are
+// conflict-free), completed through an mbarrier per buffer and released through a second one
+// that every warp arrives on; the first three tiles are requested before griddepcontrol.wait,
+// then one thread refills a buffer as soon as all eight warps are done with it, so two tiles
+// are in flight while one is computed, across pair boundaries.  Every warp keeps its own
+// online-softmax state over its 16 keys of each tile; at the end of a pair the 16 warp states
+// are combined in shared memory in a fixed order, so no partial leaves the SM and the result does
+// not depend on timing.  Needs n_audio > 128 (a tile for each warpgroup in every pair: both meet
+// at the block barrier that ends a pair).
 // ---------------------------------------------------------------------------
 constexpr int kStreamThreads = 2 * kAttnThreads;
 constexpr int kPwPad = 24;  // halves per row of a warp's P^T block (48 B: conflict-free ldmatrix)
-constexpr int kStreamBufs = 3;                           // tile buffers per warpgroup
+constexpr int kStreamBufs = 3;                            // tile buffers per warpgroup
 constexpr int kStreamTile = 2 * kAttnKeyTile * kHeadDim;  // halves of one K tile + one V tile
+constexpr unsigned kHalfTileBytes = kAttnKeyTile * kHeadDim * 2;  // one K (or V) tile: 16 KB
 // offset (halves) of 16-byte chunk c of row r in a swizzled 128-byte-row tile
 __device__ __forceinline__ int swz(int r, int c) { return r * kHeadDim + ((c ^ (r & 7)) << 3); }
 
@@ -460,8 +463,12 @@ __device__ __forceinline__ void tile_warp(const __half *sk, const __half *sv, in
 }
 
 template <int NQ>
-__global__ void __launch_bounds__(kStreamThreads, 1) k_attn_stream(AttnArgs a) {
-    extern __shared__ __align__(16) __half sbuf[];  // [warpgroup][kStreamBufs][K tile | V tile]
+__global__ void __launch_bounds__(kStreamThreads, 1)
+    k_attn_stream(AttnArgs a, const __grid_constant__ CUtensorMap kmap, const __grid_constant__ CUtensorMap vmap) {
+    extern __shared__ __align__(1024) unsigned char sraw[];
+    // [warpgroup][kStreamBufs][K tile | V tile], 1024-byte aligned for the 128-byte swizzle
+    __half *sbuf = reinterpret_cast<__half *>(sraw + ((1024u - (smem_u32(sraw) & 1023u)) & 1023u));
+    __shared__ __align__(8) uint64_t full[2][kStreamBufs], empty[2][kStreamBufs];
     __shared__ __align__(16) __half qh[2][8][kHeadDim + 8];
     __shared__ __align__(16) __half pw[2 * kWarps][8][kPwPad];
     __shared__ float wm[2 * kWarps][8], wl[2 * kWarps][8];
@@ -475,30 +482,23 @@ __global__ void __launch_bounds__(kStreamThreads, 1) k_attn_stream(AttnArgs a) {
     const int my_pairs = blockIdx.x < n_pairs ? (n_pairs - 1 - blockIdx.x) / G + 1 : 0;
     const int n_items = my_pairs * my_tiles;
     __half *wbuf = sbuf + (size_t)wg * kStreamBufs * kStreamTile;
+    const bool producer = gwarp == 0 && lane == 0;  // one thread per warpgroup requests its tiles
 
     // stream liveness and stream of each group: written by the host or an earlier graph launch
     auto live = [&](int pair) { return !a.active || a.active[pair / H] != 0; };
-    // rows of this warpgroup's item i into buffer i % 3 as one cp.async group (empty if the
-    // stream has finished); V rows past a short tile's keys are zeroed (they meet zero
-    // probabilities and must not be stale)
+    // item i of this warpgroup -> buffer i % 3 (a finished stream's buffer completes empty)
     auto issue = [&](int i) {
-        const int pair = blockIdx.x + (i / my_tiles) * G, t = wg + 2 * (i % my_tiles);
+        const int pair = blockIdx.x + (i / my_tiles) * G, t = wg + 2 * (i % my_tiles), b = i % kStreamBufs;
         if (live(pair)) {
-            const int group = pair / H, head = pair - group * H, j0 = t * kAttnKeyTile;
-            const int nk = min(kAttnKeyTile, A - j0);
-            const size_t off =
-                ((((size_t)a.stream_of_group[group] * a.n_layer + a.layer) * H + head) * (size_t)A + j0) * kHeadDim;
-            const __half *kg = a.kc + off, *vg = a.vc + off;
-            __half *tk = wbuf + (size_t)(i % kStreamBufs) * kStreamTile, *tv = tk + kAttnKeyTile * kHeadDim;
-            for (int c = gtid; c < nk * 8; c += kAttnThreads) {
-                const int r = c >> 3, part = c & 7;
-                cp_async16(&tk[swz(r, part)], kg + (size_t)r * kHeadDim + part * 8);
-                cp_async16(&tv[swz(r, part)], vg + (size_t)r * kHeadDim + part * 8);
-            }
-            for (int c = gtid; c < (kAttnKeyTile - nk) * 8; c += kAttnThreads)
-                *reinterpret_cast<uint4 *>(&tv[(nk + (c >> 3)) * kHeadDim + (c & 7) * 8]) = make_uint4(0u, 0u, 0u, 0u);
+            const int group = pair / H, head = pair - group * H;
+            const int y = (((a.stream_of_group[group] * a.n_layer + a.layer) * H + head) * A) + t * kAttnKeyTile;
+            __half *tk = wbuf + (size_t)b * kStreamTile;
+            mbar_expect_tx(&full[wg][b], 2 * kHalfTileBytes);
+            tma_load_2d(tk, &kmap, 0, y, &full[wg][b]);
+            tma_load_2d(tk + kAttnKeyTile * kHeadDim, &vmap, 0, y, &full[wg][b]);
+        } else {
+            mbar_arrive(&full[wg][b]);
         }
-        cp_async_commit();
     };
     // a pair's queries (f32 registers; converted into qh when the pair starts)
     auto load_q = [&](int pair, float4 &v) {
@@ -510,19 +510,26 @@ __global__ void __launch_bounds__(kStreamThreads, 1) k_attn_stream(AttnArgs a) {
         }
     };
 
-    if (n_items > 0) issue(0);
-    if (n_items > 1) issue(1);
+    if (tid < 2 * kStreamBufs) {
+        mbar_init(&full[tid / kStreamBufs][tid % kStreamBufs], 1);
+        mbar_init(&empty[tid / kStreamBufs][tid % kStreamBufs], kWarps);
+    }
+    fence_mbar_init();
+    __syncthreads();
+    if (producer)
+        for (int i = 0; i < kStreamBufs && i < n_items; ++i) issue(i);
     pdl_trigger();
     pdl_wait();
     float4 qn;
     load_q(blockIdx.x, qn);
     float m[2], l[2], of[4][4];
+    bool ok = true;
     for (int i = 0; i < n_items; ++i) {
         const int k = i / my_tiles, j = i - k * my_tiles;
-        const int pair = blockIdx.x + k * G, t = wg + 2 * j;
+        const int pair = blockIdx.x + k * G, t = wg + 2 * j, b = i % kStreamBufs;
         const bool lv = live(pair);
         const int nk = min(kAttnKeyTile, A - t * kAttnKeyTile);
-        const __half *sk = wbuf + (size_t)(i % kStreamBufs) * kStreamTile, *sv = sk + kAttnKeyTile * kHeadDim;
+        __half *sk = wbuf + (size_t)b * kStreamTile, *sv = sk + kAttnKeyTile * kHeadDim;
         if (j == 0) {  // a new pair: queries and state; the next pair's queries start loading
             if (gtid < 8 * kHeadDim / 4) {
                 const int qi = gtid / (kHeadDim / 4), c = gtid % (kHeadDim / 4);
@@ -535,12 +542,29 @@ __global__ void __launch_bounds__(kStreamThreads, 1) k_attn_stream(AttnArgs a) {
             l[0] = l[1] = 0.f;
 #pragma unroll
             for (int mt = 0; mt < 4; ++mt) of[mt][0] = of[mt][1] = of[mt][2] = of[mt][3] = 0.f;
+            group_sync(1 + wg);  // qh is read by every warp of the warpgroup
         }
-        if (i + 1 < n_items) cp_async_wait_group<1>();  // tile i + 1 may stay in flight
-        else cp_async_wait_group<0>();
-        group_sync(1 + wg);  // tile i has landed (and qh is written); tile i - 1's buffer is free
-        if (i + 2 < n_items) issue(i + 2);
-        if (lv) tile_warp<NQ>(sk, sv, nk, qh[wg], pw[warp], m, l, of, gwarp, lane);
+        ok = mbar_wait(&full[wg][b], (unsigned)((i / kStreamBufs) & 1), a.err) && ok;
+        if (lv && ok) {
+            // a short last tile: V rows past its keys meet zero probabilities and must be finite;
+            // each warp clears the rows of its own 16 keys (the TMA copy has completed)
+            const int kb = 16 * gwarp;
+            if (nk < kAttnKeyTile && kb < nk && kb + 16 > nk) {
+                for (int c = lane; c < (kb + 16 - nk) * 8; c += 32)
+                    *reinterpret_cast<uint4 *>(&sv[(nk + (c >> 3)) * kHeadDim + (c & 7) * 8]) = make_uint4(0u, 0u, 0u, 0u);
+                __syncwarp();
+            }
+            tile_warp<NQ>(sk, sv, nk, qh[wg], pw[warp], m, l, of, gwarp, lane);
+        }
+        fence_proxy_async();  // this warp's generic accesses to the buffer precede the next copy into it
+        __syncwarp();
+        if (lane == 0) mbar_arrive(&empty[wg][b]);
+        if (producer && i + kStreamBufs < n_items) {
+            // refill buffer b once all eight warps are done with tile i
+            if (mbar_wait(&empty[wg][b], (unsigned)((i / kStreamBufs) & 1), a.err)) issue(i + kStreamBufs);
+            else ok = false;
+        }
+        __syncwarp();  // warp 0 reconverges before the next tile's ldmatrix / mma
         if (j == my_tiles - 1) {
             // end of the pair: the 16 warp states, combined in warp order
             if (lv) {
@@ -585,6 +609,10 @@ __global__ void __launch_bounds__(kStreamThreads, 1) k_attn_stream(AttnArgs a) {
             __syncthreads();  // wm, wl, red and qh of both warpgroups are free
         }
     }
+    // after a wait that ran out: the copies still in flight land before the block exits
+    if (!ok && producer)
+        for (int i = n_items > kStreamBufs ? n_items - kStreamBufs : 0; i < n_items; ++i)
+            mbar_wait(&full[wg][i % kStreamBufs], (unsigned)((i / kStreamBufs) & 1), nullptr);
 }
 
 // Key splits of one launch: up to kMaxSplits (one cluster); tiles each block stages.
@@ -627,12 +655,15 @@ bool attn_stream_pays(const AttnArgs &a, int sms) {
     return a.cross && a.n_audio > kAttnKeyTile && (long long)a.nsplit * a.n_head * a.groups > 2LL * sms;
 }
 
-static size_t stream_smem() { return 2 * kStreamBufs * (size_t)kStreamTile * sizeof(__half); }
+static size_t stream_smem() { return 2 * kStreamBufs * (size_t)kStreamTile * sizeof(__half) + 1024; }
 
-cudaError_t launch_attn_stream(const AttnArgs &a, int sms, cudaStream_t s, bool pdl) {
+cudaError_t launch_attn_stream(const AttnArgs &a, const void *kmap, const void *vmap, int sms, cudaStream_t s, bool pdl) {
     if (a.groups <= 0) return cudaSuccess;
-    if (!a.cross || a.nq < 1 || a.nq > kMaxNq || a.n_audio <= kAttnKeyTile) return cudaErrorInvalidValue;
+    if (!a.cross || a.nq < 1 || a.nq > kMaxNq || a.n_audio <= kAttnKeyTile || !kmap || !vmap)
+        return cudaErrorInvalidValue;
     const long long pairs = (long long)a.groups * a.n_head;
+    const CUtensorMap &km = *reinterpret_cast<const CUtensorMap *>(kmap);
+    const CUtensorMap &vm = *reinterpret_cast<const CUtensorMap *>(vmap);
     cudaLaunchConfig_t cfg = {};
     cfg.gridDim = dim3((unsigned)(pairs < sms ? pairs : sms));
     cfg.blockDim = dim3(kStreamThreads);
@@ -646,14 +677,14 @@ cudaError_t launch_attn_stream(const AttnArgs &a, int sms, cudaStream_t s, bool 
     cfg.attrs = attr;
     cfg.numAttrs = pdl ? 1 : 0;
     switch (a.nq) {
-        case 1: return cudaLaunchKernelEx(&cfg, k_attn_stream<1>, a);
-        case 2: return cudaLaunchKernelEx(&cfg, k_attn_stream<2>, a);
-        case 3: return cudaLaunchKernelEx(&cfg, k_attn_stream<3>, a);
-        case 4: return cudaLaunchKernelEx(&cfg, k_attn_stream<4>, a);
-        case 5: return cudaLaunchKernelEx(&cfg, k_attn_stream<5>, a);
-        case 6: return cudaLaunchKernelEx(&cfg, k_attn_stream<6>, a);
-        case 7: return cudaLaunchKernelEx(&cfg, k_attn_stream<7>, a);
-        default: return cudaLaunchKernelEx(&cfg, k_attn_stream<8>, a);
+        case 1: return cudaLaunchKernelEx(&cfg, k_attn_stream<1>, a, km, vm);
+        case 2: return cudaLaunchKernelEx(&cfg, k_attn_stream<2>, a, km, vm);
+        case 3: return cudaLaunchKernelEx(&cfg, k_attn_stream<3>, a, km, vm);
+        case 4: return cudaLaunchKernelEx(&cfg, k_attn_stream<4>, a, km, vm);
+        case 5: return cudaLaunchKernelEx(&cfg, k_attn_stream<5>, a, km, vm);
+        case 6: return cudaLaunchKernelEx(&cfg, k_attn_stream<6>, a, km, vm);
+        case 7: return cudaLaunchKernelEx(&cfg, k_attn_stream<7>, a, km, vm);
+        default: return cudaLaunchKernelEx(&cfg, k_attn_stream<8>, a, km, vm);
     }
 }
 

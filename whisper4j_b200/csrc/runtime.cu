@@ -116,6 +116,8 @@ struct w4j_ctx {
     long long last_launches = 0;
     cudaEvent_t ev0 = nullptr, ev1 = nullptr;
     alignas(64) unsigned char e_tmap[128] = {};  // TMA map of the f16 token embedding
+    alignas(64) unsigned char xk_tmap[128] = {}, xv_tmap[128] = {};  // cross K / V caches as [rows][64]
+    bool x_tmap_ok = false;
     bool e_tmap_ok = false;
     bool tc_logits = true;
     bool tc_gemm = true;  // tcgen05 projections once M >= 16
@@ -229,6 +231,9 @@ extern "C" int w4j_ctx_create(const w4j_dims *dims, int device, int max_streams,
     if ((rc = dalloc(c, &c->ck, cross)) || (rc = dalloc(c, &c->cv, cross)) || (rc = dalloc(c, &c->sk, self)) ||
         (rc = dalloc(c, &c->sv, self)))
         return fail(rc);
+    c->x_tmap_ok = cross / kHeadDim < (size_t)INT32_MAX &&
+                   make_tmap_f16_rows(c->xk_tmap, c->ck, (int)(cross / kHeadDim), kHeadDim) &&
+                   make_tmap_f16_rows(c->xv_tmap, c->cv, (int)(cross / kHeadDim), kHeadDim);
     // activations
     if ((rc = dalloc(c, &c->x, M * d)) || (rc = dalloc(c, &c->q, M * d)) || (rc = dalloc(c, &c->attn, M * d)) ||
         (rc = dalloc(c, &c->h, M * 4 * d)) || (rc = dalloc(c, &c->xa_stage, A * d)))
@@ -645,7 +650,8 @@ static int run_layers(w4j_ctx *c, const PassArgs &pa, long long &launches) {
         ca.out = c->attn;
         ca.active = pa.group_active;
         ca.err = c->st.err;
-        if (attn_stream_pays(ca, c->sm_count)) CUDA_TRY(launch_attn_stream(ca, c->sm_count, c->stream, pdl));
+        if (c->x_tmap_ok && attn_stream_pays(ca, c->sm_count))
+            CUDA_TRY(launch_attn_stream(ca, c->xk_tmap, c->xv_tmap, c->sm_count, c->stream, pdl));
         else CUDA_TRY(launch_attn(ca, c->stream, pdl));
 
         GemvArgs gxo;

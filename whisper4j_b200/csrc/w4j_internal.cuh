@@ -255,8 +255,9 @@ cudaError_t launch_gemv(const GemvArgs &a, cudaStream_t s, bool pdl);
 cudaError_t launch_attn(const AttnArgs &a, cudaStream_t s, bool pdl);
 int attn_max_splits(int nq);  // key splits of one attention launch (one thread-block cluster)
 bool attn_stream_pays(const AttnArgs &a, int sms);  // the streaming kernel beats the cluster one
-// cross-attention over many (group, head) pairs: one persistent block per SM
-cudaError_t launch_attn_stream(const AttnArgs &a, int sms, cudaStream_t s, bool pdl);
+// cross-attention over many (group, head) pairs: one persistent block per SM; kmap / vmap are
+// make_tmap_f16_rows maps of the cross K / V caches as [rows][64]
+cudaError_t launch_attn_stream(const AttnArgs &a, const void *kmap, const void *vmap, int sms, cudaStream_t s, bool pdl);
 cudaError_t launch_logits(const LogitsArgs &a, int n_parts, cudaStream_t s, bool pdl);
 int logits_parts_for(int V, int sm_count);
 size_t logits_smem_bytes(int M, int V, int d, int n_parts);
