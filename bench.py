@@ -302,8 +302,9 @@ def run_ours(args, cfg, dims, rank, world, local_rank):
                 durs.append(e0.elapsed_time(e1))
         return statistics.median(durs)
 
-    # dominant kernel by time share (profiles/launches_*.md): k_gemv, the six projections of a
-    # decoder layer at this workload's M, K and N (LayerNorm prologue / GELU / residual epilogues)
+    # dominant kernel by time share (profiles/launches_*.md): the projections (k_gemv, or k_gemm_tc
+    # from 16 rows on), the six of a decoder layer at this workload's M, K and N (LayerNorm
+    # prologue / GELU / residual epilogues)
     from whisper4j_b200._lib import GGML_F16, GGML_Q8_0
     proj = [(3 * d, d, 1, 0), (d, d, 0, 2), (d, d, 1, 0), (d, d, 0, 2), (4 * d, d, 1, 1), (d, 4 * d, 0, 2)]
     gdur, galg = [], []
@@ -328,7 +329,9 @@ def run_ours(args, cfg, dims, rank, world, local_rank):
         galg.append(wbytes_ + M * K * 4 + M * N * 4 * (2 if epi == 2 else 1))
     g_ms, g_alg = sum(gdur) / len(gdur), sum(galg) / len(galg)
     g_ach = g_alg / (g_ms * 1e-3) / 1e9
-    roof = {"bound": "hbm", "kernel": "k_gemv: the six projections of one decoder layer (QKV with LN, attn.out + "
+    # from 16 rows on, f16 projections run on the tcgen05 kernel (w4j_op_linear dispatches as the decoder does)
+    kname = "k_gemm_tc (tcgen05, split K over a cluster)" if M >= 16 and cfg["wtype"] == "f16" else "k_gemv"
+    roof = {"bound": "hbm", "kernel": kname + ": the six projections of one decoder layer (QKV with LN, attn.out + "
                                       "residual, cross q with LN, cross out + residual, mlp.0 with LN + GELU, "
                                       "mlp.2 + residual), each replayed alone",
             "achieved": g_ach, "peak": peak, "peak_source": src, "unit": "GB/s", "frac": g_ach / peak,

@@ -35,7 +35,7 @@ struct GemmTcLaunch {
     int n_stages;    // weight ring stages
     int rmax;        // most tile rows a split block owns: ceil(128 / ks)
     int recv_alias;  // 1: the partials land in the weight ring (free once every block's MMAs are done)
-    unsigned b_off, ln_off, bias_off, mi_off, recv_off, bar_off;  // shared-memory layout (bytes)
+    unsigned b_off, ln_off, bias_off, mi_off, stat_off, recv_off, bar_off;  // shared-memory layout (bytes)
 };
 
 __device__ __forceinline__ void cluster_arrive_relaxed() {
@@ -55,6 +55,9 @@ __device__ __forceinline__ unsigned cluster_map(const void *local, unsigned rank
 __device__ __forceinline__ void st_cluster_f32(unsigned addr, float v) {
     asm volatile("st.shared::cluster.f32 [%0], %1;" ::"r"(addr), "f"(v) : "memory");
 }
+__device__ __forceinline__ void st_cluster_f32x2(unsigned addr, float x, float y) {
+    asm volatile("st.shared::cluster.v2.f32 [%0], {%1, %2};" ::"r"(addr), "f"(x), "f"(y) : "memory");
+}
 
 template <int NU>
 __global__ void __launch_bounds__(kGemmThreads, 1) k_gemm_tc(GemvArgs a, const __grid_constant__ CUtensorMap tmap,
@@ -72,6 +75,7 @@ __global__ void __launch_bounds__(kGemmThreads, 1) k_gemm_tc(GemvArgs a, const _
     float *ln_s = reinterpret_cast<float *>(smem + L.ln_off);      // gamma, beta of the K range
     float *bias_s = reinterpret_cast<float *>(smem + L.bias_off);  // [128]
     int *mi_s = reinterpret_cast<int *>(smem + L.mi_off);          // [4][M] active, slot, pos, token
+    float2 *stat_s = reinterpret_cast<float2 *>(smem + L.stat_off); // [M] LayerNorm mean, 1/std (split K)
     // split-K partials of the rows this block owns: [split][M][rmax], written by the cluster
     float *recv = reinterpret_cast<float *>(smem + (L.recv_alias ? 0u : L.recv_off));
     uint64_t *full = reinterpret_cast<uint64_t *>(smem + L.bar_off);
@@ -103,20 +107,36 @@ __global__ void __launch_bounds__(kGemmThreads, 1) k_gemm_tc(GemvArgs a, const _
         tmem_alloc(tslot, kCols);
         tmem_relinquish();
     }
-    if (a.in_mode != IN_ACT)
-        for (int i = tid; i < 2 * kr; i += blockDim.x)
-            ln_s[i] = i < kr ? a.ln_g[kb0 * kKB + i] : a.ln_b[kb0 * kKB + i - kr];
-    for (int i = tid; i < kTileRows; i += blockDim.x) bias_s[i] = (a.bias && n0 + i < N) ? a.bias[n0 + i] : 0.f;
-    // liveness, cache slots, positions and tokens: written by the host or an earlier graph launch
-    for (int i = tid; i < M; i += blockDim.x) {
-        mi_s[i] = a.active ? a.active[i] : 1;
-        if (a.out_mode == OUT_QKV) {
-            mi_s[M + i] = a.seq_slot[i];
-            mi_s[2 * M + i] = a.pos[i];
+    // LayerNorm parameters of the K range (2 kr <= 2560 floats: at most 5 per thread), biases,
+    // liveness, cache slots, positions and tokens (written by the host or an earlier graph
+    // launch): every load of a thread is issued before the first store, so they overlap
+    {
+        const int nln = a.in_mode != IN_ACT ? 2 * kr : 0;
+        float lnv[5];
+#pragma unroll
+        for (int j = 0; j < 5; ++j) {
+            const int i = tid + j * kGemmThreads;
+            lnv[j] = i < nln ? (i < kr ? a.ln_g[kb0 * kKB + i] : a.ln_b[kb0 * kKB + i - kr]) : 0.f;
         }
-        if (a.in_mode == IN_EMBED_LN) {
-            mi_s[2 * M + i] = a.pos[i];
-            mi_s[3 * M + i] = a.tok[i];
+        const float bv = (tid < kTileRows && a.bias && n0 + tid < N) ? a.bias[n0 + tid] : 0.f;
+        int mv0 = 1, mv1 = 0, mv2 = 0, mv3 = 0;
+        if (tid < M) {
+            if (a.active) mv0 = a.active[tid];
+            if (a.out_mode == OUT_QKV) mv1 = a.seq_slot[tid];
+            if (a.out_mode == OUT_QKV || a.in_mode == IN_EMBED_LN) mv2 = a.pos[tid];
+            if (a.in_mode == IN_EMBED_LN) mv3 = a.tok[tid];
+        }
+#pragma unroll
+        for (int j = 0; j < 5; ++j) {
+            const int i = tid + j * kGemmThreads;
+            if (i < nln) ln_s[i] = lnv[j];
+        }
+        if (tid < kTileRows) bias_s[tid] = bv;
+        if (tid < M) {
+            mi_s[tid] = mv0;
+            mi_s[M + tid] = mv1;
+            mi_s[2 * M + tid] = mv2;
+            mi_s[3 * M + tid] = mv3;
         }
     }
     for (int i = tid; i < 2 * (NU - M) * nkb * 8; i += blockDim.x) {  // slots M .. NU are zero
@@ -126,8 +146,10 @@ __global__ void __launch_bounds__(kGemmThreads, 1) k_gemm_tc(GemvArgs a, const _
         *reinterpret_cast<uint4 *>(bop + (size_t)kb * NB * 128 + (size_t)m * 128 + ((cc ^ (m & 7)) * 16)) =
             make_uint4(0, 0, 0, 0);
     }
-    // the cluster's blocks must all have started before one stores into another's shared memory
-    if (ks > 1 && !L.recv_alias) cluster_arrive_relaxed();
+    // the cluster's blocks must all have started before one stores into another's shared memory:
+    // every thread arrives here and waits before its first distributed store
+    if (ks > 1) cluster_arrive_relaxed();
+    bool started = ks == 1;
     pdl_trigger();
     pdl_wait();
     __syncthreads();
@@ -147,7 +169,95 @@ __global__ void __launch_bounds__(kGemmThreads, 1) k_gemm_tc(GemvArgs a, const _
         *reinterpret_cast<uint2 *>(row + (size_t)ml * 128 + ((cc ^ (ml & 7)) * 16)) =
             make_uint2(*reinterpret_cast<const uint32_t *>(&l0), *reinterpret_cast<const uint32_t *>(&l1));
     };
-    if (a.in_mode == IN_ACT) {
+    if (a.in_mode != IN_ACT && ks > 1) {
+        // LayerNorm statistics over the full rows (Tensor.java:592-619: two-pass mean / variance,
+        // eps 1e-5), shared by the split blocks: block `split` computes rows split, split + ks, ...
+        // (one warp per row, the row in registers) and stores (mean, 1/std) into every block of
+        // the cluster; then each block reads only its K range of the rows
+        constexpr int kLnF4 = 10;  // K <= 1280
+        const int nf4 = K / 128;
+        __syncwarp();
+        cluster_wait_acquire();
+        started = true;
+        for (int m = split + ks * warp; m < M; m += ks * kGemmWarps) {
+            float4 v[kLnF4];
+            if (a.in_mode == IN_LN) {
+                const float4 *src = reinterpret_cast<const float4 *>(a.act + (size_t)m * K);
+#pragma unroll
+                for (int j = 0; j < kLnF4; ++j) v[j] = j < nf4 ? src[lane + 32 * j] : make_float4(0.f, 0.f, 0.f, 0.f);
+            } else {  // x = E[tok] + P[pos] (WhisperDecoder.java:66-80); the first tile's owner keeps it
+                const uint2 *e = reinterpret_cast<const uint2 *>(a.E.h + (size_t)mi_s[3 * M + m] * K);
+                const float4 *pe = reinterpret_cast<const float4 *>(a.pos_emb + (size_t)mi_s[2 * M + m] * K);
+                uint2 eu[kLnF4];
+#pragma unroll
+                for (int j = 0; j < kLnF4; ++j) {
+                    eu[j] = j < nf4 ? e[lane + 32 * j] : make_uint2(0u, 0u);
+                    v[j] = j < nf4 ? pe[lane + 32 * j] : make_float4(0.f, 0.f, 0.f, 0.f);
+                }
+#pragma unroll
+                for (int j = 0; j < kLnF4; ++j) {
+                    const float2 lo = __half22float2(*reinterpret_cast<const __half2 *>(&eu[j].x));
+                    const float2 hi = __half22float2(*reinterpret_cast<const __half2 *>(&eu[j].y));
+                    v[j] = make_float4(lo.x + v[j].x, lo.y + v[j].y, hi.x + v[j].z, hi.y + v[j].w);
+                    if (j < nf4 && blockIdx.y == 0 && a.x_out)
+                        reinterpret_cast<float4 *>(a.x_out)[(size_t)m * (K / 4) + lane + 32 * j] = v[j];
+                }
+            }
+            float sm = 0.f;
+#pragma unroll
+            for (int j = 0; j < kLnF4; ++j)
+                if (j < nf4) sm += (v[j].x + v[j].y) + (v[j].z + v[j].w);
+            const float mean = warp_sum(sm) / (float)K;
+            float v2 = 0.f;
+#pragma unroll
+            for (int j = 0; j < kLnF4; ++j)
+                if (j < nf4) {
+                    const float dx = v[j].x - mean, dy = v[j].y - mean, dz = v[j].z - mean, dw = v[j].w - mean;
+                    v2 += (dx * dx + dy * dy) + (dz * dz + dw * dw);
+                }
+            const float inv_std = 1.0f / sqrtf(warp_sum(v2) / (float)K + 1e-5f);
+            if (lane < ks) st_cluster_f32x2(cluster_map(&stat_s[m], (unsigned)lane), mean, inv_std);
+        }
+        __syncwarp();
+        cluster_arrive_release();
+        cluster_wait_acquire();
+        // the K range of every row, normalised: 8 float4 (and for the embedding 8 f16 quads) in flight
+        const int r4 = kr / 4;
+        const int total = M * r4;
+        for (int i0 = tid; i0 < total; i0 += kGemmThreads * 8) {
+            float4 v[8];
+#pragma unroll
+            for (int j = 0; j < 8; ++j) {
+                const int i = i0 + kGemmThreads * j;
+                if (i < total) {
+                    const int m = i / r4, c4 = i - m * r4;
+                    if (a.in_mode == IN_LN) {
+                        v[j] = reinterpret_cast<const float4 *>(a.act + (size_t)m * K + kb0 * kKB)[c4];
+                    } else {
+                        const uint2 eu =
+                            reinterpret_cast<const uint2 *>(a.E.h + (size_t)mi_s[3 * M + m] * K + kb0 * kKB)[c4];
+                        const float4 p =
+                            reinterpret_cast<const float4 *>(a.pos_emb + (size_t)mi_s[2 * M + m] * K + kb0 * kKB)[c4];
+                        const float2 lo = __half22float2(*reinterpret_cast<const __half2 *>(&eu.x));
+                        const float2 hi = __half22float2(*reinterpret_cast<const __half2 *>(&eu.y));
+                        v[j] = make_float4(lo.x + p.x, lo.y + p.y, hi.x + p.z, hi.y + p.w);
+                    }
+                }
+            }
+#pragma unroll
+            for (int j = 0; j < 8; ++j) {
+                const int i = i0 + kGemmThreads * j;
+                if (i < total) {
+                    const int m = i / r4, c4 = i - m * r4, kk = 4 * c4;
+                    const float2 st = stat_s[m];
+                    const float4 g = *reinterpret_cast<const float4 *>(ln_s + kk);
+                    const float4 b = *reinterpret_cast<const float4 *>(ln_s + kr + kk);
+                    put4(m, kk, make_float4((v[j].x - st.x) * st.y * g.x + b.x, (v[j].y - st.x) * st.y * g.y + b.y,
+                                            (v[j].z - st.x) * st.y * g.z + b.z, (v[j].w - st.x) * st.y * g.w + b.w));
+                }
+            }
+        }
+    } else if (a.in_mode == IN_ACT) {
         // the K range of every row, 16 float4 loads in flight per thread
         const int r4 = kr / 4;  // float4 per row in the K range
         const int total = M * r4;
@@ -333,14 +443,18 @@ __global__ void __launch_bounds__(kGemmThreads, 1) k_gemm_tc(GemvArgs a, const _
         if (epi) tc_fence_before();
     } else {
         const int R = L.rmax;
+        if (!started) {  // every block of the cluster has started
+            __syncwarp();
+            cluster_wait_acquire();
+        }
         if (L.recv_alias) {
             // the partials go into the weight ring: every block of the cluster must be past its
             // MMAs (its epilogue warps saw the accumulator complete) before any of them stores
             __syncwarp();
             cluster_arrive_relaxed();
+            __syncwarp();
+            cluster_wait_acquire();
         }
-        __syncwarp();
-        cluster_wait_acquire();
         if (epi) {
             // row r belongs to block o: partial -> o's recv[split][m][r - r0(o)]
             int o = 0;
@@ -407,7 +521,8 @@ static bool plan_gemm_tc(const GemvArgs &a, int sms, int &nu, GemmTcLaunch &L, i
     const size_t mibytes = ((size_t)4 * M * 4 + 15) & ~(size_t)15;
     L.rmax = (kTileRows + ks - 1) / ks;
     const size_t recvbytes = ks > 1 ? (((size_t)ks * M * L.rmax * 4 + 15) & ~(size_t)15) : 0;
-    const size_t fixed = bbytes + lnbytes + 512 + mibytes + 256;
+    const size_t statbytes = (size_t)M * 8;  // 8-byte multiple: keeps recv / barriers aligned
+    const size_t fixed = bbytes + lnbytes + 512 + mibytes + statbytes + 256;
     const size_t budget = 220 * 1024;
     // the partials get their own buffer when it fits beside two stages, else they reuse the ring
     L.recv_alias = fixed + recvbytes + 2 * (size_t)kStageBytes > budget;
@@ -424,7 +539,8 @@ static bool plan_gemm_tc(const GemvArgs &a, int sms, int &nu, GemmTcLaunch &L, i
     L.ln_off = L.b_off + (unsigned)bbytes;
     L.bias_off = L.ln_off + (unsigned)lnbytes;
     L.mi_off = L.bias_off + 512;
-    L.recv_off = L.mi_off + (unsigned)mibytes;
+    L.stat_off = L.mi_off + (unsigned)mibytes;
+    L.recv_off = L.stat_off + (unsigned)statbytes;
     L.bar_off = L.recv_off + (unsigned)own;
     return true;
 }
