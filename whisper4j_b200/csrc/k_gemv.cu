@@ -410,7 +410,6 @@ __global__ void __launch_bounds__(kGemvThreads) k_gemv(GemvArgs a, GemvLaunch L)
             mi_s[3 * M + i] = a.tok[i];
         }
     }
-    pdl_trigger();
     pdl_wait();
 
     bool ok = true;
@@ -433,6 +432,9 @@ __global__ void __launch_bounds__(kGemvThreads) k_gemv(GemvArgs a, GemvLaunch L)
                 for (int mm = 0; mm < MT; ++mm)
                     res_s[mm * L.rows_per_block + r] = m0 + mm < M ? a.y[(size_t)(m0 + mm) * N + r0 + r] : 0.f;
         __syncthreads();
+        // The next kernel may launch (and start its own weight copies) only now: its copies no
+        // longer queue ahead of this block's activation loads, which are on the critical path.
+        if (m0 == 0) pdl_trigger();
         if (m0 == 0) ok = __syncthreads_and(mbar_wait(bar, 0, a.err));  // block-uniform: a barrier follows
         if (ok) {
             constexpr int PM = P2<MT>::v;
