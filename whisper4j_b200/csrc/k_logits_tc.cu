@@ -24,6 +24,10 @@
 
 namespace w4j {
 
+// 16 warps: warp 0 produces, warp 1 issues the MMAs, warps 4-7 move tiles out of TMEM; all
+// sixteen build the B operand (one LayerNorm row per warp at a time) and run the row epilogue.
+constexpr int kLogitsThreads = 512;
+
 struct LogitsTcLaunch {
     int tiles_total;  // ceil(V / 128)
     int ch;           // max rows of a block (tiles per block * 128)
@@ -33,7 +37,7 @@ struct LogitsTcLaunch {
 
 
 template <int NU>
-__global__ void __launch_bounds__(256, 1) k_logits_tc(LogitsArgs a, const __grid_constant__ CUtensorMap tmap,
+__global__ void __launch_bounds__(kLogitsThreads, 1) k_logits_tc(LogitsArgs a, const __grid_constant__ CUtensorMap tmap,
                                                        LogitsTcLaunch L) {
     extern __shared__ __align__(1024) unsigned char smem_raw[];
     // the 128-byte swizzle pattern is anchored on 1024-byte boundaries: align the base
@@ -117,7 +121,7 @@ __global__ void __launch_bounds__(256, 1) k_logits_tc(LogitsArgs a, const __grid
     __syncthreads();  // ln_s is read across warps below
 
     // ---- B operand: LayerNorm(x[m]) as f16, K-major, 128-byte swizzle (rows >= M were zeroed) ----
-    for (int m = warp; m < a.M; m += 8) {
+    for (int m = warp; m < a.M; m += kLogitsThreads / 32) {
         const bool live = true;
         constexpr int kMaxChunks = 1280 / 8 / 32;  // 16-byte chunks per lane for d <= 1280
         float v[kMaxChunks][8];
@@ -210,7 +214,7 @@ __global__ void __launch_bounds__(256, 1) k_logits_tc(LogitsArgs a, const __grid
             }
             umma_commit(accf + b);  // tile lt's accumulator is complete
         }
-    } else if (warp >= 4) {
+    } else if (warp >= 4 && warp < 8) {
         // ---- epilogue: TMEM -> shared logits tile ----
         const int q = warp - 4;  // TMEM lane quarter of this warp
         for (int lt = 0; lt < n_tiles; ++lt) {
@@ -319,7 +323,7 @@ static cudaError_t launch_tc_t(const LogitsArgs &a, const CUtensorMap &map, cons
                                cudaStream_t s, bool pdl) {
     cudaLaunchConfig_t cfg = {};
     cfg.gridDim = dim3(P);
-    cfg.blockDim = dim3(256);
+    cfg.blockDim = dim3(kLogitsThreads);
     cfg.dynamicSmemBytes = tc_smem(L);
     cfg.stream = s;
     cudaLaunchAttribute attr[1];
