@@ -80,6 +80,46 @@ def test_beam_2_times_10_streams_match_oracle(wide):
 
 
 # ---------------------------------------------------------------------------
+# more than 32 live rows: the tcgen05 vocabulary pass runs once per chunk of at most 32 rows
+# ---------------------------------------------------------------------------
+@pytest.fixture(scope="module")
+def wide40():
+    gm = parsed(SMALL, 101, "f16", SO)
+    d = WhisperDecoder(gm, max_streams=40, max_beam=4)
+    o = O.OracleModel(gm)
+    xas = [encoder_output(500 + i, SMALL.n_audio_ctx, SMALL.n_text_state) for i in range(40)]
+    for i, xa in enumerate(xas):
+        d.set_encoder_output(xa, slot=i)
+    yield d, o, xas
+    d.close()
+
+
+def test_greedy_40_streams_match_oracle(wide40):
+    dec, ora, xas = wide40
+    slots = list(range(40))
+    prompts = [[996, 997, 998, 10 + i] for i in range(40)]
+    res = dec.decode_batch(slots, prompts, 995, 16, suppress_tokens=[995], no_speech_token=3)
+    for s, p, r in zip(slots, prompts, res):
+        w = ora.decode(xas[s], p, 995, 16, suppress=[995], no_speech=3)
+        check_tokens(r.tokens, w["tokens"], ora, xas[s], p)
+        if r.tokens == w["tokens"]:
+            assert r.sum_logprob == pytest.approx(w["sum_logprob"], abs=2e-2 + 1e-3 * abs(w["sum_logprob"]))
+        assert r.no_speech_prob == pytest.approx(w["no_speech_prob"], rel=2e-2, abs=1e-6)
+
+
+def test_beam_4_times_10_streams_match_oracle(wide40):
+    dec, ora, xas = wide40
+    slots = list(range(10))
+    prompts = [[996, 997, 998, 10 + i] for i in range(10)]
+    res = dec.decode_beam_batch(slots, prompts, 995, 10, suppress_tokens=[995], beam_size=4)
+    for s, p, r in zip(slots, prompts, res):
+        w = ora.decode_beam(xas[s], p, 995, 10, suppress=[995], beam=4)
+        tol = 2e-2 if r.tokens == w["tokens"] else 5e-2
+        assert r.sum_logprob == pytest.approx(w["sum_logprob"], abs=tol)
+        assert len(r.tokens) == 10
+
+
+# ---------------------------------------------------------------------------
 # tiny.en (6 heads, 1500 encoder rows) with 8 streams: more (group, head, split) work than one
 # wave of the cluster attention kernel, so cross-attention runs on the streaming kernel
 # (persistent blocks, per-split partials in global memory, last-arriver combine)

@@ -711,12 +711,43 @@ static LogitsArgs logits_args(w4j_ctx *c, int M, const int *active) {
     return la;
 }
 
-// The vocabulary pass: tcgen05 kernel when the embedding is f16 and M <= 32, else the SIMT one.
-static cudaError_t run_logits(w4j_ctx *c, const LogitsArgs &la, bool pdl) {
-    if (c->e_tmap_ok) {
-        const cudaError_t e = launch_logits_tc(la, c->e_tmap, c->n_parts, c->stream, pdl);
-        if (e != cudaErrorNotSupported) return e;
+// Rows [m0, m0 + n) of a vocabulary pass: every per-row pointer advanced by m0 rows.
+static LogitsArgs logits_rows(const LogitsArgs &la, int m0, int n, int n_parts) {
+    LogitsArgs r = la;
+    r.M = n;
+    r.x = la.x + (size_t)m0 * la.d;
+    r.part = la.part + (size_t)m0 * n_parts * kPartStride;
+    if (la.raw_out) r.raw_out = la.raw_out + (size_t)m0 * la.V;
+    if (la.masked_out) r.masked_out = la.masked_out + (size_t)m0 * la.V;
+    if (la.ns_part) r.ns_part = la.ns_part + (size_t)m0 * n_parts * 2;
+    if (la.ns_value) r.ns_value = la.ns_value + m0;
+    if (la.active) r.active = la.active + m0;
+    if (la.use_mask) {
+        r.mask.dyn_list = la.mask.dyn_list + (size_t)m0 * la.mask.dyn_stride;
+        r.mask.dyn_count = la.mask.dyn_count + m0;
+        r.mask.ranges = la.mask.ranges + (size_t)m0 * kMaxRanges;
+        r.mask.n_ranges = la.mask.n_ranges + m0;
     }
+    return r;
+}
+
+// The vocabulary pass: the tcgen05 kernel when the embedding is f16 (one launch per 32 rows),
+// else the SIMT one.  Returns the launches enqueued in `launches`.
+static cudaError_t run_logits(w4j_ctx *c, const LogitsArgs &la, bool pdl, long long &launches) {
+    if (c->e_tmap_ok) {
+        const int chunks = (la.M + 31) / 32;
+        cudaError_t e = cudaSuccess;
+        int done = 0;
+        for (int i = 0; i < chunks && e == cudaSuccess; ++i) {
+            const int m0 = (i * la.M) / chunks, m1 = ((i + 1) * la.M) / chunks;
+            e = launch_logits_tc(logits_rows(la, m0, m1 - m0, c->n_parts), c->e_tmap, c->n_parts, c->stream, pdl);
+            if (e == cudaSuccess) ++done;
+        }
+        launches += done;
+        // unsupported shapes are refused by the first chunk; a refusal after a launch is an error
+        if (e != cudaErrorNotSupported || done > 0) return e;
+    }
+    ++launches;
     return launch_logits(la, c->n_parts, c->stream, pdl);
 }
 
@@ -760,7 +791,7 @@ extern "C" int w4j_forward(w4j_ctx *c, int slot, const int32_t *tokens, int n, i
         TRY(run_layers(c, pa, launches));
         LogitsArgs la = logits_args(c, 1, nullptr);
         la.raw_out = c->raw + (size_t)t * c->V;
-        CUDA_TRY(run_logits(c, la, true));
+        CUDA_TRY(run_logits(c, la, true, launches));
     }
     CUDA_TRY(cudaMemcpyAsync(out_logits, c->raw, (size_t)n * c->V * 4, cudaMemcpyDeviceToHost, c->stream));
     CUDA_TRY(cudaStreamSynchronize(c->stream));
@@ -937,8 +968,7 @@ static int run_prompt(w4j_ctx *c, const CallArgs &a, const CallLayout &Ly, int m
             la.ns_part = c->ns_part;
             la.ns_value = c->ns_value;
         }
-        CUDA_TRY(run_logits(c, la, !last));
-        ++launches;
+        CUDA_TRY(run_logits(c, la, !last, launches));
         if (ns_here) {
             CUDA_TRY(launch_nsp(st, c->ns_part, c->n_parts, c->ns_value, c->stream, true));
             ++launches;
@@ -974,10 +1004,10 @@ static int enqueue_step(w4j_ctx *c, const CallArgs &a, const CallLayout &Ly, int
     la.mask = mask_args(c);
     la.topk = mode == MODE_BEAM ? B + 1 : 0;
     if (mode == MODE_SAMPLE) la.masked_out = c->masked;
-    CUDA_TRY(run_logits(c, la, true));
+    CUDA_TRY(run_logits(c, la, true, launches));
     const int sel = mode == MODE_BEAM ? SEL_BEAM : mode == MODE_SAMPLE ? SEL_SAMPLE : SEL_GREEDY;
     CUDA_TRY(launch_select(st, sel, parity, c->logit_part, c->n_parts, c->masked, 0, c->stream, true));
-    launches += 2;
+    launches += 1;
     return 0;
 }
 
@@ -1320,7 +1350,18 @@ extern "C" int w4j_op_logits_argmax(w4j_ctx *c, const float *x, int M, const voi
     cudaStream_t s = stream ? reinterpret_cast<cudaStream_t>(stream) : 0;
     alignas(64) unsigned char map[128];
     cudaError_t e = cudaErrorNotSupported;
-    if (c->tc_logits && make_tmap_f16_rows(map, E, V, c->d)) e = launch_logits_tc(la, map, P, s, false);
+    if (c->tc_logits && make_tmap_f16_rows(map, E, V, c->d)) {
+        // one tcgen05 launch per chunk of at most 32 rows, as in the decode step
+        const int chunks = (M + 31) / 32;
+        int done = 0;
+        e = cudaSuccess;
+        for (int i = 0; i < chunks && e == cudaSuccess; ++i) {
+            const int m0 = (i * M) / chunks, m1 = ((i + 1) * M) / chunks;
+            e = launch_logits_tc(logits_rows(la, m0, m1 - m0, P), map, P, s, false);
+            if (e == cudaSuccess) ++done;
+        }
+        if (e == cudaErrorNotSupported && done > 0) CUDA_TRY(e);
+    }
     if (e == cudaErrorNotSupported) e = launch_logits(la, P, s, false);
     CUDA_TRY(e);
     CUDA_TRY(launch_argmax_merge(c->logit_part, P, M, out_token, out_logprob, s));
