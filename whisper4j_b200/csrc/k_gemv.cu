@@ -86,7 +86,7 @@ __device__ __forceinline__ float row_value(const DMat &m, int row, int k) {
 // token + positional embedding then LayerNorm.  All threads cooperate on the loads with
 // eight independent 16-byte loads in flight each (one L2 round trip for a few KB), then
 // one warp per row normalises in shared memory.
-template <int MT>
+template <int MT, int NT>
 __device__ void load_activations(const GemvArgs &a, int m0, int K, float *act_s, const float *ln_s, int warp,
                                  int lane, const int *tok_s = nullptr, const int *pos_s = nullptr) {
     const int K4 = K / 4;
@@ -98,7 +98,7 @@ __device__ void load_activations(const GemvArgs &a, int m0, int K, float *act_s,
     const bool embed_f16 = a.in_mode == IN_EMBED_LN && a.E.type == WT_F16;
     if ((a.in_mode == IN_LN || embed_f16) && K % 128 == 0 && K <= 128 * kLnF4) {
         const int nf4 = K / 128;
-        for (int mm = warp; mm < MT; mm += kGemvThreads / 32) {
+        for (int mm = warp; mm < MT; mm += (NT / 32)) {
             float4 *dst = reinterpret_cast<float4 *>(act_s + (size_t)mm * K);
             const int m = m0 + mm;
             if (m >= a.M) {
@@ -159,11 +159,11 @@ __device__ void load_activations(const GemvArgs &a, int m0, int K, float *act_s,
     }
     if (a.in_mode == IN_EMBED_LN) {
         const bool f16 = a.E.type == WT_F16;
-        for (int i0 = threadIdx.x; i0 < total; i0 += kGemvThreads * 8) {
+        for (int i0 = threadIdx.x; i0 < total; i0 += NT * 8) {
             float4 e[8], p[8];
 #pragma unroll
             for (int j = 0; j < 8; ++j) {
-                const int i = i0 + kGemvThreads * j;
+                const int i = i0 + NT * j;
                 const int mm = i / K4, k = (i - mm * K4) * 4;
                 const int m = m0 + mm;
                 e[j] = p[j] = make_float4(0.f, 0.f, 0.f, 0.f);
@@ -184,7 +184,7 @@ __device__ void load_activations(const GemvArgs &a, int m0, int K, float *act_s,
             }
 #pragma unroll
             for (int j = 0; j < 8; ++j) {
-                const int i = i0 + kGemvThreads * j;
+                const int i = i0 + NT * j;
                 if (i >= total) continue;
                 const float4 v = make_float4(e[j].x + p[j].x, e[j].y + p[j].y, e[j].z + p[j].z, e[j].w + p[j].w);
                 reinterpret_cast<float4 *>(act_s)[i] = v;
@@ -198,21 +198,21 @@ __device__ void load_activations(const GemvArgs &a, int m0, int K, float *act_s,
         const int live = (a.M - m0 < MT ? a.M - m0 : MT) * K4;
         const float4 *src = reinterpret_cast<const float4 *>(a.act) + (size_t)m0 * K4;
         constexpr int kB = 16;  // 16 x 16 B in flight per thread: 64 KB per block per round trip
-        for (int i0 = threadIdx.x; i0 < total; i0 += kGemvThreads * kB) {
+        for (int i0 = threadIdx.x; i0 < total; i0 += NT * kB) {
             float4 v[kB];
 #pragma unroll
             for (int j = 0; j < kB; ++j) {
-                const int i = i0 + kGemvThreads * j;
+                const int i = i0 + NT * j;
                 v[j] = i < live ? src[i] : make_float4(0.f, 0.f, 0.f, 0.f);
             }
 #pragma unroll
             for (int j = 0; j < kB; ++j)
-                if (i0 + kGemvThreads * j < total) reinterpret_cast<float4 *>(act_s)[i0 + kGemvThreads * j] = v[j];
+                if (i0 + NT * j < total) reinterpret_cast<float4 *>(act_s)[i0 + NT * j] = v[j];
         }
     }
     if (a.in_mode == IN_ACT) return;
     __syncthreads();
-    for (int mm = warp; mm < MT; mm += kGemvThreads / 32) {
+    for (int mm = warp; mm < MT; mm += (NT / 32)) {
         if (m0 + mm >= a.M) continue;
         float *dst = act_s + (size_t)mm * K;
         // Tensor.layerNorm (Tensor.java:592-619): two-pass mean / variance, eps 1e-5,
@@ -233,17 +233,18 @@ __device__ void load_activations(const GemvArgs &a, int m0, int K, float *act_s,
 }
 
 // gamma / beta of the LayerNorm into shared memory (constant: done before the grid wait)
+template <int NT>
 __device__ __forceinline__ void stage_ln(const float *g, const float *b, int K, float *ln_s) {
-    for (int i0 = threadIdx.x; i0 < 2 * K; i0 += kGemvThreads * 8) {
+    for (int i0 = threadIdx.x; i0 < 2 * K; i0 += NT * 8) {
         float v[8];
 #pragma unroll
         for (int j = 0; j < 8; ++j) {
-            const int i = i0 + kGemvThreads * j;
+            const int i = i0 + NT * j;
             v[j] = i < K ? g[i] : i < 2 * K ? b[i - K] : 0.f;
         }
 #pragma unroll
         for (int j = 0; j < 8; ++j)
-            if (i0 + kGemvThreads * j < 2 * K) ln_s[i0 + kGemvThreads * j] = v[j];
+            if (i0 + NT * j < 2 * K) ln_s[i0 + NT * j] = v[j];
     }
 }
 
@@ -359,14 +360,20 @@ __device__ __forceinline__ void drain(uint64_t *bar, unsigned parity) {
 // ---------------------------------------------------------------------------
 // GEMV kernel: block = rows [r0, r0 + rows_per_block) of W, staged whole in shared memory
 // ---------------------------------------------------------------------------
+// Threads of a k_gemv block.  Q8_0 rows carry more arithmetic per weight byte (dequantisation),
+// so sixteen warps split each row group's K; f16 blocks stay at eight warps, which keeps them
+// small enough for blocks of consecutive kernels to be co-resident and prefetch their weights.
+__host__ __device__ constexpr int gemv_threads(int wt) { return wt == WT_Q8 ? 512 : 256; }
+
 struct GemvLaunch {
     int rows_per_block;
     size_t w_bytes, s_bytes;  // staging capacity for weights / Q8 scales (16-byte multiples)
 };
 
 template <int MT, int R, int WT>
-__global__ void __launch_bounds__(kGemvThreads) k_gemv(GemvArgs a, GemvLaunch L) {
+__global__ void __launch_bounds__(gemv_threads(WT)) k_gemv(GemvArgs a, GemvLaunch L) {
     extern __shared__ __align__(128) unsigned char smem[];
+    constexpr int NT = gemv_threads(WT);
     const int N = a.W.N, K = a.W.K;
     const int r0 = blockIdx.x * L.rows_per_block;
     const int nr = min(N, r0 + L.rows_per_block) - r0;
@@ -394,12 +401,12 @@ __global__ void __launch_bounds__(kGemvThreads) k_gemv(GemvArgs a, GemvLaunch L)
         for (unsigned off = 0; off < bytes; off += 65536u) bulk_g2s(w_s + off, src + off, min(65536u, bytes - off), bar);
     }
     if (WT == WT_Q8)
-        for (int i = tid; i < nr * (K / 32); i += kGemvThreads) sc_s[i] = a.W.s[(size_t)r0 * (K / 32) + i];
-    if (a.in_mode != IN_ACT) stage_ln(a.ln_g, a.ln_b, K, ln_s);
+        for (int i = tid; i < nr * (K / 32); i += NT) sc_s[i] = a.W.s[(size_t)r0 * (K / 32) + i];
+    if (a.in_mode != IN_ACT) stage_ln<NT>(a.ln_g, a.ln_b, K, ln_s);
     // Biases are weights; liveness, cache slots, positions and tokens were written by the host
     // or by an earlier graph launch, never by a kernel of this launch's chain: read them now.
-    for (int i = tid; i < nr; i += kGemvThreads) bias_s[i] = a.bias ? a.bias[r0 + i] : 0.f;
-    for (int i = tid; i < M; i += kGemvThreads) {
+    for (int i = tid; i < nr; i += NT) bias_s[i] = a.bias ? a.bias[r0 + i] : 0.f;
+    for (int i = tid; i < M; i += NT) {
         mi_s[i] = a.active ? a.active[i] : 1;
         if (a.out_mode == OUT_QKV) {
             mi_s[M + i] = a.seq_slot[i];
@@ -422,12 +429,12 @@ __global__ void __launch_bounds__(kGemvThreads) k_gemv(GemvArgs a, GemvLaunch L)
 #pragma unroll
             for (int mm = 0; mm < MT; ++mm) resv[mm] = m0 + mm < M ? a.y[(size_t)(m0 + mm) * N + r0 + tid] : 0.f;
         if (m0 == 0) __syncthreads();  // mi_s
-        load_activations<MT>(a, m0, K, act_s, ln_s, warp, lane, mi_s + 3 * M, mi_s + 2 * M);
+        load_activations<MT, NT>(a, m0, K, act_s, ln_s, warp, lane, mi_s + 3 * M, mi_s + 2 * M);
         if (has_res)
 #pragma unroll
             for (int mm = 0; mm < MT; ++mm) res_s[mm * L.rows_per_block + tid] = resv[mm];
-        if (a.out_mode == OUT_RESIDUAL)  // blocks of more than kGemvThreads rows (op-level calls)
-            for (int r = tid + kGemvThreads; r < nr; r += kGemvThreads)
+        if (a.out_mode == OUT_RESIDUAL)  // blocks of more than NT rows (op-level calls)
+            for (int r = tid + NT; r < nr; r += NT)
 #pragma unroll
                 for (int mm = 0; mm < MT; ++mm)
                     res_s[mm * L.rows_per_block + r] = m0 + mm < M ? a.y[(size_t)(m0 + mm) * N + r0 + r] : 0.f;
@@ -472,9 +479,10 @@ __global__ void __launch_bounds__(kGemvThreads) k_gemv(GemvArgs a, GemvLaunch L)
             // G groups of R rows; with fewer groups than warps, KS warps share a group's K
             // chunks and their sums meet in shared memory (added in warp order)
             const int G = (nr + R - 1) / R;
-            const int KS = G >= 5 ? 1 : G >= 3 ? 2 : G == 2 ? 4 : 8;  // G * KS <= 8 warps
+            // G * KS <= warps
+            const int KS = NT == 256 ? (G >= 5 ? 1 : G >= 3 ? 2 : G == 2 ? 4 : 8) : (G >= NT / 32 ? 1 : (NT / 32) / G);
             if (KS == 1) {
-                for (int g = warp; g < G; g += kGemvThreads / 32) {
+                for (int g = warp; g < G; g += NT / 32) {
                     float acc[R * PM];
                     smem_rows<MT, R, WT>(w_s + (size_t)g * R * row_bytes, row_bytes, min(R, nr - g * R),
                                          sc_s + (size_t)g * R * (K / 32), nullptr, K, act_s, acc, lane, lane, 32);
@@ -484,7 +492,7 @@ __global__ void __launch_bounds__(kGemvThreads) k_gemv(GemvArgs a, GemvLaunch L)
                     emit(v, g * R + idx / PM, idx % PM);
                 }
             } else {
-                __shared__ float red_s[kGemvThreads / 32][32];
+                __shared__ float red_s[NT / 32][32];
                 const int g = warp / KS, kp = warp % KS;
                 if (g < G) {
                     float acc[R * PM];
@@ -555,7 +563,7 @@ static cudaError_t launch_gemv_t(const GemvArgs &a, const GemvLaunch &L, int blo
                         ((size_t)L.rows_per_block * (1 + MT) + 4 * (size_t)a.M) * 4;
     cudaLaunchConfig_t cfg = {};
     cfg.gridDim = dim3(blocks);
-    cfg.blockDim = dim3(kGemvThreads);
+    cfg.blockDim = dim3(gemv_threads(WT));
     cfg.dynamicSmemBytes = smem;
     cfg.stream = s;
     cudaLaunchAttribute attr[1];
@@ -571,7 +579,7 @@ static cudaError_t launch_gemv_r(const GemvArgs &a, const GemvLaunch &L, int blo
     // few rows per block: one row per warp keeps all warps busy; many rows: 4 rows share
     // each activation read
     if (L.rows_per_block <= 8) return launch_gemv_t<MT, 1, WT>(a, L, blocks, s, pdl);
-    if constexpr (MT <= 2) {  // > 32 rows: 8 rows per warp keeps every row group within one round
+    if constexpr (MT == 1 || (MT == 2 && WT == WT_F16)) {  // > 32 rows: 8 rows per warp keeps every row group within one round
         if (L.rows_per_block > 32) return launch_gemv_t<MT, 8, WT>(a, L, blocks, s, pdl);
     }
     if constexpr (MT <= 4) return launch_gemv_t<MT, 4, WT>(a, L, blocks, s, pdl);
@@ -654,7 +662,7 @@ __global__ void __launch_bounds__(kGemvThreads) k_logits(LogitsArgs a, LogitsLau
         fence_mbar_init();
         for (int g = 0; g < NS && g < total; ++g) issue(g);
     }
-    stage_ln(a.ln_g, a.ln_b, d, ln_s);
+    stage_ln<kGemvThreads>(a.ln_g, a.ln_b, d, ln_s);
     pdl_trigger();
     pdl_wait();
 
@@ -667,7 +675,7 @@ __global__ void __launch_bounds__(kGemvThreads) k_logits(LogitsArgs a, LogitsLau
         g.act = a.x;
         g.ln_g = a.ln_g;
         g.ln_b = a.ln_b;
-        load_activations<MT>(g, m0, d, act_s, ln_s, warp, lane);
+        load_activations<MT, kGemvThreads>(g, m0, d, act_s, ln_s, warp, lane);
         __syncthreads();
         for (int t = 0; t < n_tiles; ++t) {
             const int gidx = pass * n_tiles + t;
