@@ -65,11 +65,11 @@ struct LayerDev {
     float *bm0 = nullptr, *bm2 = nullptr;
     float *ln1g = nullptr, *ln1b = nullptr, *ln2g = nullptr, *ln2b = nullptr, *ln3g = nullptr, *ln3b = nullptr;
     int qkv_type = 0;
-    // TMA maps of the f16 projections for the tensor-core kernel (M >= 16), by PROJ_*
-    alignas(64) unsigned char tmap[6][128] = {};
-    bool tmap_ok[6] = {};
+    // TMA maps of the f16 projections for the tensor-core kernels (M >= 16; cross K / V prefill), by PROJ_*
+    alignas(64) unsigned char tmap[8][128] = {};
+    bool tmap_ok[8] = {};
 };
-enum Proj : int { PROJ_QKV = 0, PROJ_O = 1, PROJ_XQ = 2, PROJ_XO = 3, PROJ_M0 = 4, PROJ_M2 = 5 };
+enum Proj : int { PROJ_QKV = 0, PROJ_O = 1, PROJ_XQ = 2, PROJ_XO = 3, PROJ_M0 = 4, PROJ_M2 = 5, PROJ_XK = 6, PROJ_XV = 7 };
 
 struct GraphKey {
     int mode, S, B, eot, ts_begin, n_sup, max_tokens, ns, n_prompt;
@@ -221,7 +221,7 @@ extern "C" int w4j_ctx_create(const w4j_dims *dims, int device, int max_streams,
     cudaEventCreate(&c->ev0);
     cudaEventCreate(&c->ev1);
     if ((rc = (int)gemv_prepare()) != 0 || (rc = (int)select_prepare()) != 0 || (rc = (int)logits_tc_prepare()) != 0 ||
-        (rc = (int)attn_prepare()) != 0 || (rc = (int)gemm_tc_prepare()) != 0)
+        (rc = (int)attn_prepare()) != 0 || (rc = (int)gemm_tc_prepare()) != 0 || (rc = (int)xkv_tc_prepare()) != 0)
         return fail(set_err(W4J_ERR_CUDA, "kernel attributes: %s", cudaGetErrorString((cudaError_t)rc)));
     const size_t V = c->V, C = c->C, A = c->A, L = c->L;
     const size_t M = c->M_max;
@@ -484,8 +484,8 @@ extern "C" int w4j_finalize(w4j_ctx *c) {
     std::lock_guard<std::mutex> g(c->mu);
     TRY(check_ready(c));
     for (LayerDev &ly : c->layers) {
-        const DMat *m[6] = {&ly.qkv, &ly.o, &ly.xq, &ly.xo, &ly.m0, &ly.m2};
-        for (int i = 0; i < 6; ++i)
+        const DMat *m[8] = {&ly.qkv, &ly.o, &ly.xq, &ly.xo, &ly.m0, &ly.m2, &ly.xk, &ly.xv};
+        for (int i = 0; i < 8; ++i)
             ly.tmap_ok[i] = c->tc_gemm && m[i]->type == WT_F16 && make_tmap_f16_rows(ly.tmap[i], m[i]->h, m[i]->N, m[i]->K);
     }
     return W4J_OK;
@@ -498,8 +498,15 @@ static int prefill(w4j_ctx *c, int slot, const float *xa_dev) {
     for (int l = 0; l < c->L; ++l) {
         LayerDev &ly = c->layers[l];
         const size_t off = ((size_t)slot * c->L + l) * (size_t)c->H * c->A * kHeadDim;
-        CUDA_TRY(launch_cross_kv(xa_dev, c->A, c->d, ly.xk, ly.xv, ly.bxk, ly.bxv, c->ck + off, c->cv + off, c->H,
-                                 c->stream));
+        // tensor cores for f16 weights, else the SIMT GEMM
+        cudaError_t e = cudaErrorNotSupported;
+        if (ly.tmap_ok[PROJ_XK] && ly.tmap_ok[PROJ_XV])
+            e = launch_cross_kv_tc(xa_dev, c->A, c->d, ly.tmap[PROJ_XK], ly.tmap[PROJ_XV], ly.bxk, ly.bxv,
+                                   c->ck + off, c->cv + off, c->st.err, c->stream);
+        if (e == cudaErrorNotSupported)
+            e = launch_cross_kv(xa_dev, c->A, c->d, ly.xk, ly.xv, ly.bxk, ly.bxv, c->ck + off, c->cv + off, c->H,
+                                c->stream);
+        CUDA_TRY(e);
     }
     CUDA_TRY(cudaStreamSynchronize(c->stream));
     c->has_xa[slot] = 1;

@@ -286,6 +286,11 @@ cudaError_t logits_tc_prepare();
 cudaError_t launch_logits_tc(const LogitsArgs &a, const void *tmap, int n_parts, cudaStream_t s, bool pdl);
 bool make_tmap_f16_rows(void *map_out, const void *base, int rows, int cols);  // 128-byte map
 cudaError_t gemm_tc_prepare();
+cudaError_t xkv_tc_prepare();
+// tcgen05 cross K/V projection of one stream and layer (f16 Wk / Wv, d a multiple of 128); kmap /
+// vmap are make_tmap_f16_rows maps of Wk and Wv; cudaErrorNotSupported outside its range
+cudaError_t launch_cross_kv_tc(const float *xa, int A, int d, const void *kmap, const void *vmap, const float *bk,
+                               const float *bv, __half *kout, __half *vout, int *err, cudaStream_t s);
 // tcgen05 projection (f16 weights, 16 <= M <= 128) with the GEMV's input modes and epilogues;
 // `tmap` is make_tmap_f16_rows of a.W; cudaErrorNotSupported outside its range
 cudaError_t launch_gemm_tc(const GemvArgs &a, const void *tmap, int sms, cudaStream_t s, bool pdl);
