@@ -7,12 +7,12 @@
 // Block (n tile, a tile): 128 rows of [Wk; Wv] (the UMMA M) x 128 encoder rows.
 //   * One thread streams the weight tiles [128 x 64] f16 with TMA (128-byte swizzle) through a
 //     ring of stages.
-//   * Four warps read the encoder rows' f32 values for the same 64-wide k-block and write them
+//   * Eight warps read the encoder rows' f32 values for the same 64-wide k-block and write them
 //     into the stage's B operand as f16 hi / lo pairs (hi = f16(x), lo = f16(x - hi): about 22
 //     bits of x, so the product keeps the reference's f32 activations): rows [0, 128) hi,
 //     [128, 256) lo, K-major with the same swizzle.
 //   * One thread issues tcgen05.mma.kind::f16 (M 128, N 256, K 16) into a TMEM accumulator; each
-//     stage is released by tcgen05.commit.  The four converter warps then read the accumulator
+//     stage is released by tcgen05.commit.  Four of the converter warps then read the accumulator
 //     (tcgen05.ld), add the hi and lo columns and the bias, and store f16 rows of the cache.
 // Every wait is bounded; a time-out raises the device error word.
 #include "tc_common.cuh"
@@ -20,11 +20,11 @@
 
 namespace w4j {
 
-constexpr int kXkvThreads = 256;
+constexpr int kXkvThreads = 384;
 constexpr int kXkvStages = 4;
 constexpr int kXRows = 128;                            // encoder rows per block
 constexpr unsigned kXStageB = 2u * kXRows * 128u;      // B stage: 256 rows x 64 f16 = 32 KB
-constexpr int kConvWarps = 4;                          // warps 4..7 convert, then drain TMEM
+constexpr int kConvWarps = 8;                          // warps 4..11 convert; warps 4..7 then drain TMEM
 
 __global__ void __launch_bounds__(kXkvThreads, 1)
     k_xkv_tc(const float *xa, int A, int d, const __grid_constant__ CUtensorMap kmap,
@@ -97,9 +97,9 @@ __global__ void __launch_bounds__(kXkvThreads, 1)
             umma_commit(empty + st);  // the stage is free once these MMAs have read it
         }
         umma_commit(accf);
-    } else if (warp >= 8 - kConvWarps) {
+    } else if (warp >= 4) {
         // ---- encoder rows -> B operand (f16 hi / lo, K-major, 128-byte swizzle) ----
-        const int ct = tid - (8 - kConvWarps) * 32;  // 0 .. 127
+        const int ct = tid - 4 * 32;  // 0 .. kConvWarps * 32 - 1
         for (int i = 0; i < KB; ++i) {
             const int st = i % kXkvStages;
             if (i >= kXkvStages && !mbar_wait(empty + st, (unsigned)((i / kXkvStages - 1) & 1), err)) {
@@ -107,17 +107,18 @@ __global__ void __launch_bounds__(kXkvThreads, 1)
                 break;
             }
             unsigned char *bs = ring_b + (size_t)st * kXStageB;
-            // 128 rows x 16 float4 of the k-block: 16 per thread, all loads in flight
-            float4 v[16];
+            // 128 rows x 16 float4 of the k-block: 8 per thread, all loads in flight
+            constexpr int kPer = 2048 / (kConvWarps * 32);
+            float4 v[kPer];
 #pragma unroll
-            for (int u = 0; u < 16; ++u) {
-                const int idx = ct + 128 * u, r = idx >> 4, c4 = idx & 15;
+            for (int u = 0; u < kPer; ++u) {
+                const int idx = ct + kConvWarps * 32 * u, r = idx >> 4, c4 = idx & 15;
                 v[u] = a0 + r < A ? reinterpret_cast<const float4 *>(xa + (size_t)(a0 + r) * d + i * kKB)[c4]
                                   : make_float4(0.f, 0.f, 0.f, 0.f);
             }
 #pragma unroll
-            for (int u = 0; u < 16; ++u) {
-                const int idx = ct + 128 * u, r = idx >> 4, c4 = idx & 15;
+            for (int u = 0; u < kPer; ++u) {
+                const int idx = ct + kConvWarps * 32 * u, r = idx >> 4, c4 = idx & 15;
                 const int cc = c4 >> 1, half = c4 & 1, rl = r + kXRows;
                 const __half2 h0 = __floats2half2_rn(v[u].x, v[u].y), h1 = __floats2half2_rn(v[u].z, v[u].w);
                 const float2 f0 = __half22float2(h0), f1 = __half22float2(h1);
@@ -134,7 +135,7 @@ __global__ void __launch_bounds__(kXkvThreads, 1)
         }
     }
     __syncthreads();
-    if (warp >= 8 - kConvWarps) {
+    if (warp >= 4 && warp < 8) {
         // ---- TMEM -> cache: tile row r (warp w reads TMEM lanes 32 (w % 4) ..), encoder rows a0 .. ----
         const int q = warp & 3, r = q * 32 + lane;
         const bool ok = !*fail && mbar_wait(accf, 0u, err);
