@@ -7,8 +7,11 @@
 // Grid (split, tile): a block owns 128 rows of W (one UMMA M tile) and a range of K.
 //   * TMA (cp.async.bulk.tensor.2d, 128-byte swizzle) streams its [128 x 64] weight tiles through
 //     a ring of shared-memory stages, the first stages before griddepcontrol.wait.
-//   * The activations (LayerNorm-ed over the full row when the projection has one) of the
-//     block's K range are written as the f16 B operand, K-major with the same swizzle, each f32
+//   * With a LayerNorm prologue and a split K, block q of the tile's cluster computes the
+//     two-pass statistics of rows q, q + ks, ... over the full row and stores (mean, 1/std)
+//     into every block of the cluster, so each block then reads only its K range of the rows.
+//   * The activations (LayerNorm-ed when the projection has one) of the block's K range are
+//     written as the f16 B operand, K-major with the same swizzle, each f32
 //     value x as two f16 rows: hi = f16(x) and lo = f16(x - hi).  hi + lo carries x to about 22
 //     bits, so with f16 weights and f32 accumulation the product keeps the f32 activations of
 //     the reference instead of rounding them to f16.  Rows hold the NU sequence slots (NU = M
