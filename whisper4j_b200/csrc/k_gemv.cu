@@ -76,11 +76,6 @@ struct P2 {
     static constexpr int v = MT <= 1 ? 1 : MT <= 2 ? 2 : MT <= 4 ? 4 : MT <= 8 ? 8 : 16;
 };
 
-__device__ __forceinline__ float row_value(const DMat &m, int row, int k) {
-    if (m.type == WT_F16) return __half2float(m.h[(size_t)row * m.K + k]);
-    const float s = __half2float(m.s[(size_t)row * (m.K / 32) + k / 32]);
-    return (float)m.q[(size_t)row * m.K + k] * s;
-}
 
 // Fill act_s[mm][k] (mm < MT) for rows m0.. of the pass: plain copy, LayerNorm of x, or
 // token + positional embedding then LayerNorm.  All threads cooperate on the loads with

@@ -164,10 +164,6 @@ struct DecodeState {
 __device__ __forceinline__ void pdl_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
 __device__ __forceinline__ void pdl_trigger() { asm volatile("griddepcontrol.launch_dependents;" ::: "memory"); }
 
-// Bulk prefetch of a contiguous global range into L2 (no shared-memory destination).
-__device__ __forceinline__ void prefetch_l2(const void *p, unsigned bytes) {
-    asm volatile("cp.async.bulk.prefetch.L2.global [%0], %1;" ::"l"(p), "r"(bytes) : "memory");
-}
 
 // ---- TMA bulk copies into shared memory, completed through an mbarrier ----
 __device__ __forceinline__ unsigned smem_u32(const void *p) { return (unsigned)__cvta_generic_to_shared(p); }
@@ -205,13 +201,6 @@ __device__ __forceinline__ bool mbar_wait(uint64_t *b, unsigned parity, int *err
     return false;
 }
 
-__device__ __forceinline__ uint4 ld_nc_v4(const void *p) {
-    uint4 r;
-    asm volatile("ld.global.nc.L1::no_allocate.v4.u32 {%0,%1,%2,%3}, [%4];"
-                 : "=r"(r.x), "=r"(r.y), "=r"(r.z), "=r"(r.w)
-                 : "l"(p));
-    return r;
-}
 
 __device__ __forceinline__ float warp_sum(float v) {
 #pragma unroll
