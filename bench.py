@@ -3,9 +3,11 @@
 
 One bench step = one full decode call over this rank's streams (prompt + forced
 max_tokens tokens per stream), i.e. the work WhisperDecoder.decode / decodeBeam does
-for one 30 s chunk.  The default workload is the configuration the headline metric is
-quoted on (base.en, beam 5, 224 forced tokens, one stream per GPU); more streams or
-GPUs are weak scaling (streams are independent: no collective on the data path).
+for its 30 s chunks.  The default workload is the largest single-GPU configuration of the
+benchmark list: large-v3-turbo, 256 independent streams, greedy, 224 forced tokens, the
+streams sharded over the GPUs of the run (strong scaling: 256 / N streams per GPU; streams
+are independent, so there is no collective on the data path).  Batch-1 latency of the same
+model is reported beside it.
 
   python bench.py [--gpus N] [--steps K] [--warmup W] [--config NAME] [--impl ours|reference]
 
@@ -16,7 +18,6 @@ host cores instead.
 from __future__ import annotations
 
 import argparse
-import ctypes
 import json
 import os
 import statistics
@@ -32,8 +33,12 @@ sys.path.insert(0, ROOT)
 
 from whisper4j_b200 import ggml  # noqa: E402
 
-# name -> workload (the BASELINE configurations; streams are per GPU, weak scaling)
+# name -> workload (the benchmark configurations).  "streams" is per GPU (weak scaling);
+# "streams_total" is the job's total, sharded over the GPUs (strong scaling).
 CONFIGS = {
+    "turbo-greedy-256": dict(arch="large-v3-turbo", wtype="f16", beam=1, max_tokens=224, streams_total=256,
+                             note="configs[3]: large-v3-turbo, 256 streams sharded over the GPUs, greedy, "
+                                  "224 forced tokens"),
     "base.en-beam5": dict(arch="base.en", wtype="f16", beam=5, max_tokens=224, streams=1,
                           note="configs[1]: base.en, beam 5, 224 forced tokens, 1 stream per GPU"),
     "tiny.en-greedy": dict(arch="tiny.en", wtype="f16", beam=1, max_tokens=64, streams=1,
@@ -47,7 +52,7 @@ CONFIGS = {
     "large-v3-q8-beam5": dict(arch="large-v3", wtype="q8_0", beam=5, max_tokens=444, streams=1,
                               note="configs[4] per stream: large-v3 Q8_0, beam 5, 448-position context"),
 }
-DEFAULT_CONFIG = "base.en-beam5"
+DEFAULT_CONFIG = "turbo-greedy-256"
 MODEL_SEED = 1234
 
 
@@ -68,11 +73,6 @@ def encoder_output(seed, n_audio_ctx, d):
     x = rng.standard_normal((n_audio_ctx, d), dtype=np.float32)
     x = (x - x.mean(axis=1, keepdims=True)) / x.std(axis=1, keepdims=True)
     return x.astype(np.float32)
-
-
-# DRAM bytes per k_gemv launch (read + write, mean over the six projections of a layer) from the
-# ncu capture summarised in profiles/k_gemv_base.en-beam5.md; other workloads were not captured.
-GEMV_TRAFFIC = {"base.en-beam5": (2.265 + 2.218 + 1.666 + 0.614 + 0.609 + 0.615) / 6 * 1e6}
 
 
 def step_bytes(dims, wtype, streams, beam, max_tokens, n_prompt):
@@ -143,24 +143,50 @@ class ClockSampler:
 # ---------------------------------------------------------------------------
 # CPU baseline: the oracle (restatement of the reference's scalar Java decoder)
 # ---------------------------------------------------------------------------
-def cpu_decode_sample(gm, dims, cfg, n_streams, sample_steps, seed0=0):
-    """Decode `sample_steps` steps of `n_streams` streams, one oracle thread per stream (the reference's
-    decoder is single-threaded per call and thread-safe across calls).  Returns tokens, seconds, threads."""
+def cpu_model():
+    try:
+        with open("/proc/cpuinfo") as f:
+            for line in f:
+                if line.startswith("model name"):
+                    return line.split(":", 1)[1].strip()
+    except OSError:
+        pass
+    return "unknown"
+
+
+def shard(cfg, rank, world):
+    """Global stream ids of this rank, the job's total and the scaling kind.  A strong-scaling
+    workload deals its streams round-robin over the ranks (stream i -> rank i mod world, as
+    whisper4j_b200.shard does); a weak-scaling one gives every rank the same count."""
+    if "streams_total" in cfg:
+        total = cfg["streams_total"]
+        return [i for i in range(total) if i % world == rank], total, "strong"
+    per = cfg["streams"]
+    return [rank * per + i for i in range(per)], per * world, "weak"
+
+
+def cpu_decode_sample(gm, dims, cfg, stream_ids, sample_steps):
+    """Decode `sample_steps` steps of each stream, one oracle thread per stream at a time (the
+    reference's decoder is single-threaded per call and thread-safe across calls), with as many
+    threads as the host has cores.  Returns tokens, seconds (slowest thread's token-loop time),
+    threads, wall seconds."""
     from oracle import oracle as O
+    O.set_threads(1)
     model = O.OracleModel(gm)
     prompt, eot = prompt_for(dims), eot_for(dims)
-    threads = max(1, min(n_streams, os.cpu_count() or 1))
-    results = [None] * n_streams
-    xas = [encoder_output(seed0 + s, dims.n_audio_ctx, dims.n_text_state) for s in range(n_streams)]
+    n = len(stream_ids)
+    threads = max(1, min(n, os.cpu_count() or 1))
+    results = [0.0] * n
 
     def work(idx):
-        for s in range(idx, n_streams, threads):
+        for k in range(idx, n, threads):
+            xa = encoder_output(stream_ids[k], dims.n_audio_ctx, dims.n_text_state)
             if cfg["beam"] > 1:
-                r = model.decode_beam(xas[s], prompt, eot, cfg["max_tokens"], suppress=[eot], beam=cfg["beam"],
+                r = model.decode_beam(xa, prompt, eot, cfg["max_tokens"], suppress=[eot], beam=cfg["beam"],
                                       max_steps=sample_steps)
             else:
-                r = model.decode(xas[s], prompt, eot, cfg["max_tokens"], suppress=[eot], max_steps=sample_steps)
-            results[s] = r["loop_seconds"]
+                r = model.decode(xa, prompt, eot, cfg["max_tokens"], suppress=[eot], max_steps=sample_steps)
+            results[k] = r["loop_seconds"]
 
     ts = [threading.Thread(target=work, args=(i,)) for i in range(threads)]
     t0 = time.perf_counter()
@@ -170,38 +196,72 @@ def cpu_decode_sample(gm, dims, cfg, n_streams, sample_steps, seed0=0):
         t.join()
     wall = time.perf_counter() - t0
     # per-thread loop seconds run concurrently: the slowest thread bounds the sample
-    per_thread = [sum(results[s] for s in range(i, n_streams, threads)) for i in range(threads)]
-    tokens = n_streams * (sample_steps - 1)
+    per_thread = [sum(results[k] for k in range(i, n, threads)) for i in range(threads)]
+    tokens = n * (sample_steps - 1) * cfg["beam"]
     return tokens, max(per_thread), threads, wall
 
 
 def run_reference(args, cfg, dims, rank, world):
+    """The reference arm: the oracle port of the reference's CPU decoder (the Java reference needs a
+    JDK, which this image lacks) on the host cores, one stream per thread, every core busy.  Each
+    bench step decodes a bounded sample of the workload's streams (as many as there are cores)
+    for a few token steps; tokens/s counts the token loop after the prompt, as the GPU arm does."""
     if rank != 0:
         return 0
     gm = ggml.parse(ggml.synthetic_model_bytes(dims, MODEL_SEED, cfg["wtype"]))
-    n_streams = cfg["streams"] * world
-    sample = int(os.environ.get("W4J_REF_SAMPLE_STEPS", "0")) or max(3, min(24, int(24 / cfg["beam"]) + 2))
+    _, total, scaling = shard(cfg, 0, world)
+    n_sample = max(1, min(total, os.cpu_count() or 1))
+    sample = int(os.environ.get("W4J_REF_SAMPLE_STEPS", "0")) or max(3, min(12, int(12 / cfg["beam"]) + 2))
     times, toks = [], 0
     threads = 1
     for i in range(args.warmup + args.steps):
-        t, sec, threads, _ = cpu_decode_sample(gm, dims, cfg, n_streams, sample, seed0=100 * i)
+        ids = [(i * n_sample + k) % total for k in range(n_sample)]
+        t, sec, threads, _ = cpu_decode_sample(gm, dims, cfg, ids, sample)
         if i >= args.warmup:
             times.append(sec)
             toks += t
     value = toks / sum(times)
     out = {"metric": "decoder tokens/s", "value": value, "unit": "tokens/s", "impl": "reference", "n_gpus": world,
            "steps": args.steps, "warmup": args.warmup, "ms_per_step": 1e3 * sum(times) / args.steps,
-           "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "f32", "data": "synthetic",
+           "higher_is_better": True, "scaling": scaling, "vs_baseline": None, "dtype": "f32", "data": "synthetic",
            "config": {"workload": args.config, "note": cfg["note"], "model_arch": cfg["arch"],
-                      "weights": cfg["wtype"], "streams": n_streams, "beam": cfg["beam"],
+                      "weights": cfg["wtype"], "streams_total": total, "beam": cfg["beam"],
                       "max_tokens": cfg["max_tokens"]},
            "cpu_baseline": {"value": value, "unit": "tokens/s", "cores": threads, "kind": "port",
-                            "sample": f"{sample - 1} token steps after the prompt of each of {n_streams} stream(s) "
-                                      f"per bench step (prompt and cross K/V projection excluded); oracle/w4j_oracle.c, "
-                                      f"the scalar f32 restatement of WhisperDecoder, one thread per stream"},
+                            "cpu_model": cpu_model(),
+                            "sample": f"per bench step {n_sample} of the {total} streams, {sample - 1} token steps "
+                                      f"each after the prompt (prompt and cross K/V projection excluded), one "
+                                      f"stream per thread on {threads} threads; oracle/w4j_oracle.c, the scalar f32 "
+                                      f"restatement of WhisperDecoder"},
            "e2e": {"value": value, "unit": "tokens/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
     print(json.dumps(out), flush=True)
     return 0
+
+
+# kernel classes of w4j_set_kernel_timing
+KCLASSES = {1: "projections", 2: "self-attention", 3: "cross-attention", 4: "vocabulary logits", 5: "token selection"}
+KNAMES = {1: "k_gemv / k_gemm_tc", 2: "k_attn (self)", 3: "k_attn_stream / k_attn (cross)",
+          4: "k_logits_tc / k_logits", 5: "k_select_*"}
+
+
+def class_bytes(cls, dims, wtype, S, B, T, n_prompt):
+    """Algorithmic HBM bytes per launch of a kernel class at this workload (mean over the
+    graph-replayed steps 1 .. T-1, whose self-attention spans n_prompt + 1 .. n_prompt + T - 1 keys)."""
+    d, L, V, A = dims.n_text_state, dims.n_text_layer, dims.n_vocab, dims.n_audio_ctx
+    M = S * B
+    wb = 2.0 if wtype == "f16" else 34.0 / 32.0
+    if cls == 1:  # the six projections of a layer: weights + activations in + out (+ residual read)
+        proj = [(3 * d, d, 1), (d, d, 2), (d, d, 1), (d, d, 2), (4 * d, d, 1), (d, 4 * d, 2)]
+        return sum(N * K * wb + M * K * 4.0 + M * N * 4.0 * f for N, K, f in proj) / 6
+    if cls == 2:  # every sequence's self K/V rows + q in + out
+        kv = n_prompt + T / 2.0
+        return M * 2.0 * kv * d * 2.0 + 2.0 * M * d * 4.0
+    if cls == 3:  # every stream's cross K/V of one layer (shared by its beams) + q in + out
+        return S * 2.0 * A * d * 2.0 + 2.0 * M * d * 4.0
+    if cls == 4:  # the embedding per launch (one launch per chunk of <= 32 rows) + the rows
+        chunks = (M + 31) // 32
+        return V * d * 2.0 + M * d * 4.0 / chunks
+    return M * 148 * 144.0  # selection: the per-block partial records
 
 
 # ---------------------------------------------------------------------------
@@ -211,27 +271,27 @@ def run_ours(args, cfg, dims, rank, world, local_rank):
     import torch
     import torch.distributed as dist
 
-    from whisper4j_b200._lib import check, lib
     from whisper4j_b200.decoder import WhisperDecoder
 
     torch.cuda.set_device(local_rank)
     dev = torch.device("cuda", local_rank)
-    S, B, T = cfg["streams"], cfg["beam"], cfg["max_tokens"]
+    ids, total, scaling = shard(cfg, rank, world)
+    S, B, T = len(ids), cfg["beam"], cfg["max_tokens"]
     gm = ggml.parse(ggml.synthetic_model_bytes(dims, MODEL_SEED, cfg["wtype"]))
     prompt, eot = prompt_for(dims), eot_for(dims)
-    dec = WhisperDecoder(gm, device=local_rank, max_streams=S, max_beam=B)
-    xas = [encoder_output(1000 * rank + s, dims.n_audio_ctx, dims.n_text_state) for s in range(S)]
-    pinned = [torch.from_numpy(x).pin_memory() for x in xas]
+    dec = WhisperDecoder(gm, device=local_rank, max_streams=max(S, 1), max_beam=B)
+    pinned = [torch.from_numpy(encoder_output(g, dims.n_audio_ctx, dims.n_text_state)).pin_memory() for g in ids]
     for s in range(S):
         dec.set_encoder_output(pinned[s].numpy(), slot=s)
     slots = list(range(S))
     prompts = [prompt] * S
     flush = torch.empty(64 * 1024 * 1024, dtype=torch.float32, device=dev)  # 256 MB > 126 MB L2
 
-    def one_step():
+    def one_step(sl=None):
+        sl = slots if sl is None else sl
         if B > 1:
-            return dec.decode_beam_batch(slots, prompts, eot, T, suppress_tokens=[eot], beam_size=B)
-        return dec.decode_batch(slots, prompts, eot, T, suppress_tokens=[eot])
+            return dec.decode_beam_batch(sl, [prompt] * len(sl), eot, T, suppress_tokens=[eot], beam_size=B)
+        return dec.decode_batch(sl, [prompt] * len(sl), eot, T, suppress_tokens=[eot])
 
     def barrier():
         if world > 1:
@@ -258,11 +318,12 @@ def run_ours(args, cfg, dims, rank, world, local_rank):
     barrier()
     wall = time.perf_counter() - t0
     clocks = sampler.stop(local_rank) if sampler else None
-    tokens = sum(len(r.tokens) for r in res) * args.steps
+    tokens = sum(len(r.tokens) for r in res) * B * args.steps
     assert all(len(r.tokens) == T for r in res), "forced-length decode produced a short sequence"
-    # ---- end to end through the C ABI with host buffers ----
+    # ---- end to end through the public API: host encoder outputs in, host results out ----
+    e2e_steps = max(1, args.steps // 2)
     e2e_s = 0.0
-    for _ in range(max(1, args.steps // 2)):
+    for _ in range(e2e_steps):
         flush.fill_(1.0)
         torch.cuda.synchronize()
         t1 = time.perf_counter()
@@ -270,12 +331,7 @@ def run_ours(args, cfg, dims, rank, world, local_rank):
             dec.set_encoder_output(pinned[s].numpy(), slot=s)
         one_step()
         e2e_s += time.perf_counter() - t1
-    e2e_steps = max(1, args.steps // 2)
-    # ---- kernels replayed alone with CUDA events (cold L2), on the stream they are launched on ----
-    M = S * B
-    d, V = dims.n_text_state, dims.n_vocab
-    st = torch.cuda.current_stream()
-    vp = lambda t: ctypes.c_void_p(t.data_ptr())  # noqa: E731
+    # ---- in-chain time of each kernel class (one profiling decode per class, outside the timed region) ----
     peaks = {}
     try:
         with open(os.path.join(ROOT, "MEASURED_PEAKS.json")) as f:
@@ -283,79 +339,49 @@ def run_ours(args, cfg, dims, rank, world, local_rank):
     except Exception:
         pass
     peak = peaks.get("hbm_gbs")
-    src = "measured" if peak else "fallback"
+    src = "measured (MEASURED_PEAKS.json hbm_gbs)" if peak else "fallback"
     peak = peak or 6650.0
-
-    def time_alone(launch, reps=20):
-        # a device-side sleep ahead of the first event keeps the stream busy while the host
-        # submits the event pair and the launch, so the events bracket device time only
-        durs = []
-        for i in range(args.warmup + reps):
+    chain = {}
+    for cls in KCLASSES:
+        dec.kernel_timing(cls)
+        flush.fill_(1.0)
+        torch.cuda.synchronize()
+        one_step()
+        cms, cn = dec.kernel_times()
+        chain[cls] = (cms, cn)
+    dec.kernel_timing(0)
+    tot_chain = sum(v[0] for v in chain.values()) or 1.0
+    dom = max(chain, key=lambda k: chain[k][0])
+    dms, dn = chain[dom]
+    alg = class_bytes(dom, dims, cfg["wtype"], S, B, T, len(prompt))
+    per_launch_ms = dms / max(dn, 1)
+    ach = alg / (per_launch_ms * 1e-3) / 1e9
+    roof = {"bound": "hbm", "kernel": f"{KNAMES[dom]} ({KCLASSES[dom]})", "achieved": ach, "peak": peak,
+            "peak_source": src, "unit": "GB/s", "frac": ach / peak, "traffic": None,
+            "algorithmic_bytes_per_launch": alg, "launch_ms": per_launch_ms, "launches": dn,
+            "timing": "in chain: CUDA events recorded inside the step graphs around every launch of the class, "
+                      "over one full decode of the workload",
+            "class_share_in_chain": {KCLASSES[k]: v[0] / tot_chain for k, v in chain.items()},
+            "class_ms_per_decode": {KCLASSES[k]: v[0] for k, v in chain.items()},
+            "class_launches_per_decode": {KCLASSES[k]: v[1] for k, v in chain.items()}}
+    # ---- batch-1 latency of the same model (one stream of this context) ----
+    b1 = None
+    if B == 1:
+        for _ in range(3):
+            one_step([0])
+        b1_ms = []
+        for _ in range(5):
             flush.fill_(1.0)
-            torch.cuda._sleep(200000)
-            e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-            e0.record(st)
-            launch()
-            e1.record(st)
-            e1.synchronize()
-            if i >= args.warmup:
-                durs.append(e0.elapsed_time(e1))
-        return statistics.median(durs)
-
-    # dominant kernel by time share (profiles/launches_*.md): the projections (k_gemv, or k_gemm_tc
-    # from 16 rows on), the six of a decoder layer at this workload's M, K and N (LayerNorm
-    # prologue / GELU / residual epilogues)
-    from whisper4j_b200._lib import GGML_F16, GGML_Q8_0
-    proj = [(3 * d, d, 1, 0), (d, d, 0, 2), (d, d, 1, 0), (d, d, 0, 2), (4 * d, d, 1, 1), (d, 4 * d, 0, 2)]
-    gdur, galg = [], []
-    for N, K, ln, epi in proj:
-        W = (torch.randn(N, K, device=dev) * 0.02).half()
-        wt = GGML_F16
-        if cfg["wtype"] == "q8_0":
-            raw = torch.empty(N * K // 32 * 34, dtype=torch.uint8, device=dev)
-            raw.view(-1, 34)[:, 2:] = torch.randint(-127, 128, (N * K // 32, 32), device=dev).to(torch.int8).view(torch.uint8)
-            raw.view(-1, 34)[:, :2] = torch.full((N * K // 32, 1), 0.01, device=dev).half().view(torch.uint8)
-            W = torch.empty(N * K + N * K // 16, dtype=torch.uint8, device=dev)
-            check(lib().w4j_q8_0_repack(vp(raw), N, K, vp(W), ctypes.c_void_p(st.cuda_stream)))
-            wt = GGML_Q8_0
-        x = torch.randn(M, K, device=dev)
-        y = torch.zeros(M, N, device=dev)
-        bias = torch.zeros(N, device=dev)
-        g, bt = torch.ones(K, device=dev), torch.zeros(K, device=dev)
-        gdur.append(time_alone(lambda: check(lib().w4j_op_linear(
-            dec._ctx, vp(x), M, K, vp(W), wt, N, vp(bias), vp(g) if ln else None, vp(bt) if ln else None, epi, vp(y),
-            ctypes.c_void_p(st.cuda_stream)))))
-        wbytes_ = N * K * 2 if cfg["wtype"] == "f16" else N * K * 34 // 32
-        galg.append(wbytes_ + M * K * 4 + M * N * 4 * (2 if epi == 2 else 1))
-    g_ms, g_alg = sum(gdur) / len(gdur), sum(galg) / len(galg)
-    g_ach = g_alg / (g_ms * 1e-3) / 1e9
-    # from 16 rows on, f16 projections run on the tcgen05 kernel (w4j_op_linear dispatches as the decoder does)
-    kname = "k_gemm_tc (tcgen05, split K over a cluster)" if M >= 16 and cfg["wtype"] == "f16" else "k_gemv"
-    roof = {"bound": "hbm", "kernel": kname + ": the six projections of one decoder layer (QKV with LN, attn.out + "
-                                      "residual, cross q with LN, cross out + residual, mlp.0 with LN + GELU, "
-                                      "mlp.2 + residual), each replayed alone",
-            "achieved": g_ach, "peak": peak, "peak_source": src, "unit": "GB/s", "frac": g_ach / peak,
-            "traffic": GEMV_TRAFFIC.get(args.config) if not args.max_tokens else None,
-            "algorithmic_bytes_per_launch": g_alg, "launch_ms": g_ms,
-            "launch_ms_each": gdur, "timing": "cold L2, alone, CUDA events around one launch queued behind a device sleep"}
-    roof_logits = None
-    if cfg["wtype"] == "f16":
-        E = torch.from_numpy(np.frombuffer(gm.tensors["decoder.token_embedding.weight"].data, np.float16).copy()
-                             ).to(dev).view(V, d)
-        x = torch.randn(M, d, device=dev)
-        g = torch.ones(d, device=dev)
-        bta = torch.zeros(d, device=dev)
-        tok = torch.zeros(M, dtype=torch.int32, device=dev)
-        lp = torch.zeros(M, dtype=torch.float64, device=dev)
-        kern_ms = time_alone(lambda: check(lib().w4j_op_logits_argmax(
-            dec._ctx, vp(x), M, vp(E), V, vp(g), vp(bta), vp(tok), vp(lp), ctypes.c_void_p(st.cuda_stream))))
-        alg = V * d * 2.0 + M * d * 4.0
-        achieved = alg / (kern_ms * 1e-3) / 1e9
-        roof_logits = {"bound": "hbm", "kernel": "k_logits_tc (vocabulary logits + processors + partial reductions) "
-                                                 "followed by the argmax merge", "achieved": achieved, "peak": peak,
-                       "peak_source": src, "unit": "GB/s", "frac": achieved / peak, "traffic": None,
-                       "algorithmic_bytes_per_launch": alg, "launch_ms": kern_ms,
-                       "timing": "cold L2, alone, CUDA events around one launch queued behind a device sleep"}
+            torch.cuda.synchronize()
+            one_step([0])
+            b1_ms.append(dec.last_timing()[0])
+        b1_step = statistics.median(b1_ms) / T
+        b1_bytes, b1_w = step_bytes(dims, cfg["wtype"], 1, 1, T, len(prompt))
+        b1 = {"us_per_token_step": b1_step * 1e3, "tokens_per_s": 1e3 / b1_step,
+              "bytes_per_token_step": b1_bytes,
+              "step_frac": b1_bytes / (b1_step * 1e-3) / 1e9 / peak,
+              "weight_frac": b1_w / (b1_step * 1e-3) / 1e9 / peak,
+              "timing": "median of 5 decodes of one stream (224 forced tokens), device time, L2 flushed"}
     # ---- gather over ranks ----
     vals = torch.tensor([dev_ms, wall, e2e_s, float(tokens)], dtype=torch.float64, device=dev)
     if world > 1:
@@ -368,17 +394,19 @@ def run_ours(args, cfg, dims, rank, world, local_rank):
     else:
         tokens_all = float(tokens)
     if rank != 0:
+        dec.close()
         return 0
     value = tokens_all / (dev_ms * 1e-3)
     per_token_step_ms = dev_ms / args.steps / T
     bstep, wbytes = step_bytes(dims, cfg["wtype"], S, B, T, len(prompt))
     out = {
         "metric": "decoder tokens/s", "value": value, "unit": "tokens/s", "n_gpus": world, "steps": args.steps,
-        "warmup": args.warmup, "ms_per_step": dev_ms / args.steps, "higher_is_better": True, "scaling": "weak",
+        "warmup": args.warmup, "ms_per_step": dev_ms / args.steps, "higher_is_better": True, "scaling": scaling,
         "vs_baseline": None, "dtype": "f16" if cfg["wtype"] == "f16" else "q8_0", "data": "synthetic",
         "config": {"workload": args.config, "note": cfg["note"], "model_arch": cfg["arch"], "weights": cfg["wtype"],
-                   "streams_per_gpu": S, "beam": B, "max_tokens": T, "prompt_tokens": len(prompt),
-                   "l2": "flushed between steps (256 MB write)", "parallelism": f"{world} independent shard(s)",
+                   "streams_total": total, "streams_per_gpu": S, "beam": B, "max_tokens": T,
+                   "prompt_tokens": len(prompt), "l2": "flushed between steps (256 MB write)",
+                   "parallelism": f"{world} independent shard(s), no collective on the data path",
                    "encoder_output": "seeded standardised rows (encoder out of scope)"},
         "us_per_token_step": per_token_step_ms * 1e3,
         "step_roofline": {"bytes_per_token_step": bstep, "weight_bytes": wbytes,
@@ -387,19 +415,21 @@ def run_ours(args, cfg, dims, rank, world, local_rank):
                           "weight_frac": wbytes / (per_token_step_ms * 1e-3) / 1e9 / peak},
         "wall_s_timed": wall,
         "e2e": {"value": tokens_all / args.steps * e2e_steps / e2e_s, "unit": "tokens/s",
-                "h2d_bytes_per_step": S * dims.n_audio_ctx * d * 4 + S * len(prompt) * 4,
+                "h2d_bytes_per_step": S * dims.n_audio_ctx * dims.n_text_state * 4 + S * len(prompt) * 4,
                 "d2h_bytes_per_step": S * (T * 4 + 4 + 8 + 4 + 4 + 4),
-                "includes": "w4j_set_encoder_output (host xa -> device, cross K/V projection) + decode + results"},
+                "includes": "w4j_set_encoder_output per stream (pinned host xa -> device, cross K/V projection) "
+                            "+ decode + results to host, wall clock"},
         "gpu_launches": launches,
         "clocks": clocks,
+        "roofline": roof,
     }
-    out["roofline"] = roof
-    if roof_logits:
-        out["roofline_logits"] = roof_logits
+    if b1:
+        out["batch1"] = b1
     if world == 1 and not args.no_cpu_baseline:
-        sample = int(os.environ.get("W4J_CPU_SAMPLE_STEPS", "0")) or max(4, min(64, int(40 / B) + 2))
-        ctoks, csec, cthreads, _ = cpu_decode_sample(gm, dims, cfg, 1, sample)
+        sample = int(os.environ.get("W4J_CPU_SAMPLE_STEPS", "0")) or max(4, min(24, int(24 / B) + 2))
+        ctoks, csec, cthreads, _ = cpu_decode_sample(gm, dims, cfg, [0], sample)
         out["cpu_baseline"] = {"value": ctoks / csec, "unit": "tokens/s", "cores": cthreads, "kind": "port",
+                               "cpu_model": cpu_model(),
                                "sample": f"{sample - 1} token steps of one stream after the prompt (prompt and "
                                          f"cross K/V projection excluded), oracle/w4j_oracle.c scalar f32 "
                                          f"restatement of WhisperDecoder, 1 thread"}
@@ -426,6 +456,10 @@ def main():
         cfg["max_tokens"] = args.max_tokens
     dims = ggml.ARCHS[cfg["arch"]]
     world = int(os.environ.get("WORLD_SIZE", "1"))
+    if world != args.gpus:
+        print(json.dumps({"error": f"--gpus {args.gpus} but WORLD_SIZE is {world}: launch N ranks with torchrun "
+                                   f"for --gpus N"}), flush=True)
+        return 2
     rank = int(os.environ.get("RANK", "0"))
     local_rank = int(os.environ.get("LOCAL_RANK", "0"))
     if args.impl == "reference":

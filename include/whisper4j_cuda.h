@@ -153,6 +153,23 @@ int w4j_needs_fallback(float compression_ratio, float avg_logprob, float no_spee
  */
 int w4j_last_timing(w4j_ctx *ctx, double *loop_ms, int *steps, long long *kernel_launches);
 
+/*
+ * In-chain kernel timing (measurement; no counterpart in the reference).  With a kernel class
+ * set, the step graphs of later decode calls are captured with CUDA event records around every
+ * launch of that class, and each step is waited for, so w4j_kernel_timing returns the summed
+ * device milliseconds and the number of those launches over the graph-replayed steps of the last
+ * decode call.  The events cost each timed launch its overlap with the launch before it, so use
+ * this for a separate profiling call, not for the timed throughput.  Classes: 0 off,
+ * 1 projections, 2 self-attention, 3 cross-attention, 4 vocabulary logits, 5 token selection.
+ */
+#define W4J_KC_PROJ 1
+#define W4J_KC_SELF_ATTN 2
+#define W4J_KC_CROSS_ATTN 3
+#define W4J_KC_LOGITS 4
+#define W4J_KC_SELECT 5
+int w4j_set_kernel_timing(w4j_ctx *ctx, int kernel_class);
+int w4j_kernel_timing(w4j_ctx *ctx, double *ms, long long *launches);
+
 /* ---------------------------------------------------------------------------
  * Op-level entry points on device buffers (plain pointers on the context's
  * device, stream 0 of the calling thread unless `stream` is given).  They run
@@ -178,7 +195,10 @@ int w4j_q8_0_repack(const void *src_device, int N, int K, void *dst_device, void
  * of the chosen id, for M rows (WhisperDecoder.java:102-103 then argmax :566-574
  * and logSoftmax :614-626).  x: M x d f32, E: V x d f16, ln: d f32 each;
  * outputs token ids (M) and log-probabilities (M, double).  Scratch memory for
- * the per-block partial results is taken from the context.
+ * the per-block partial results is taken from the context (1 <= M <= max(max_streams *
+ * max_beam, n_text_ctx)).  If a bounded wait inside the kernels ran out, every out_token of
+ * that call is -1 and every out_logprob NaN (the context's error word for this op is cleared
+ * for the next call).  Asynchronous on `stream`.
  */
 int w4j_op_logits_argmax(w4j_ctx *ctx, const float *x, int M, const void *E, int V, const float *ln_g,
                          const float *ln_b, int32_t *out_token, double *out_logprob, void *stream);
@@ -214,6 +234,15 @@ int w4j_op_logits_argmax(w4j_ctx *ctx, const float *x, int M, const void *E, int
  * If a bounded wait inside the kernels ran out, every out_token of that call is -1 and every
  * out_logprob NaN.  Asynchronous on `stream` (NULL = legacy default stream).
  */
+/*
+ * Test hook (no counterpart in the reference): the next n_launches tcgen05 vocabulary passes of
+ * w4j_op_logits_argmax / w4j_op_logits_argmax_noalloc issue none of their weight copies, so
+ * every bounded wait inside them runs out (about a second) and the call reports it through its
+ * error word (token -1, NaN log-probability).  Lets a test exercise that path without faulting
+ * the GPU.  0 turns it off.
+ */
+int w4j_test_withhold_logits_copies(int n_launches);
+
 #define W4J_NOALLOC_MAX_ROWS 16
 #define W4J_NOALLOC_MAX_PARTS 160
 int w4j_op_logits_argmax_noalloc(int device, const float *x, int M, int d, const void *E, int V,

@@ -55,6 +55,9 @@ def lib():
             L.orc_forward.argtypes = [P, P, I, P, I, P, P]
             L.orc_decode.argtypes = [P, P, I, P, I, I, I, P, I, I, F, I, ctypes.c_uint64, P, P, P, P, P, I]
             L.orc_decode_beam.argtypes = [P, P, I, P, I, I, I, P, I, I, I, I, P, P, P, P, P, I]
+            L.orc_set_threads.argtypes = [I]
+            L.orc_set_beam_trace.argtypes = [P, ctypes.c_long]
+            L.orc_beam_trace_count.restype = ctypes.c_long
             L.orc_apply_repetition_penalty.argtypes = [P, P, I, I]
             L.orc_apply_timestamp_rules.argtypes = [P, P, I, I, I, I, I]
             L.orc_dot.restype = F
@@ -91,6 +94,11 @@ class OracleError(RuntimeError):
 def _check(rc):
     if rc < 0:
         raise OracleError(lib().orc_last_error().decode())
+
+
+def set_threads(n: int) -> None:
+    """Threads of the oracle's own loops (1 = the reference's single-threaded decoder)."""
+    lib().orc_set_threads(int(n))
 
 
 # ---- tensor KATs ------------------------------------------------------------
@@ -206,18 +214,32 @@ class OracleModel:
                     no_speech_prob=ns.value, loop_seconds=lib().orc_last_loop_seconds())
 
     def decode_beam(self, xa, prompt, eot, max_tokens, suppress=(), no_speech=-1, ts_begin=-1, beam=5,
-                    max_steps=0):
+                    max_steps=0, trace=False):
+        """WhisperDecoder.decodeBeam.  trace=True adds ``trace``: every ranked candidate of every step
+        as rows (step, parent beam, token, score, outcome) — outcome is the new beam index when
+        kept, -2 when the candidate finished a sequence, -1 when dropped or not reached."""
         xa, pr, sp = _f32(xa), _i32(prompt), _i32(list(suppress) or [0])
         toks = np.zeros(max(max_tokens, 1) + 1, np.int32)
         n = ctypes.c_int()
         s = ctypes.c_double()
         a = ctypes.c_float()
         ns = ctypes.c_float()
-        _check(lib().orc_decode_beam(self._m, _p(xa), xa.shape[0], _p(pr), pr.size, eot, max_tokens, _p(sp),
-                                     len(suppress), no_speech, ts_begin, beam, _p(toks), ctypes.byref(n),
-                                     ctypes.byref(s), ctypes.byref(a), ctypes.byref(ns), max_steps))
-        return dict(tokens=toks[:n.value].tolist(), sum_logprob=s.value, avg_logprob=a.value,
-                    no_speech_prob=ns.value, loop_seconds=lib().orc_last_loop_seconds())
+        tbuf = np.zeros(((max_tokens + 1) * beam * (beam + 1) + beam, 5), np.float64) if trace else None
+        if trace:
+            lib().orc_set_beam_trace(_p(tbuf), tbuf.shape[0])
+        try:
+            _check(lib().orc_decode_beam(self._m, _p(xa), xa.shape[0], _p(pr), pr.size, eot, max_tokens, _p(sp),
+                                         len(suppress), no_speech, ts_begin, beam, _p(toks), ctypes.byref(n),
+                                         ctypes.byref(s), ctypes.byref(a), ctypes.byref(ns), max_steps))
+        finally:
+            count = lib().orc_beam_trace_count() if trace else 0
+            if trace:
+                lib().orc_set_beam_trace(None, 0)
+        out = dict(tokens=toks[:n.value].tolist(), sum_logprob=s.value, avg_logprob=a.value,
+                   no_speech_prob=ns.value, loop_seconds=lib().orc_last_loop_seconds())
+        if trace:
+            out["trace"] = tbuf[:count].copy()
+        return out
 
 
 class OracleCache:

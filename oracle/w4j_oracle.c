@@ -37,6 +37,8 @@
 #include <stdlib.h>
 #include <string.h>
 
+#include <pthread.h>
+
 #include "w4j_oracle.h"
 
 /* ------------------------------------------------------------------------ */
@@ -54,6 +56,52 @@ static double now_seconds(void) {
 }
 
 double orc_last_loop_seconds(void) { return g_loop_seconds; }
+
+/* Threads of the oracle's own loops (tests only; 1 = the reference's single-threaded decoder).
+ * Work is split over independent output elements (rows, column blocks, heads, vocabulary ids),
+ * so every sum keeps the order of the loop it restates and results do not depend on it. */
+static int g_threads = 1;
+void orc_set_threads(int n) { g_threads = n < 1 ? 1 : n > 256 ? 256 : n; }
+
+/* fn(ctx, i) for i in [0, n), split into g_threads contiguous ranges */
+typedef void (*par_fn)(void *ctx, int i);
+typedef struct {
+    par_fn fn;
+    void *ctx;
+    int i0, i1, slot;
+} par_range;
+static __thread int g_worker = 0; /* index of the par_for range this thread runs (scratch buffers) */
+static void *par_worker(void *p) {
+    par_range *r = (par_range *)p;
+    const int saved = g_worker;
+    g_worker = r->slot;
+    for (int i = r->i0; i < r->i1; i++) r->fn(r->ctx, i);
+    g_worker = saved;
+    return NULL;
+}
+static void par_for(int n, par_fn fn, void *ctx) {
+    const int T = g_threads < n ? g_threads : n;
+    if (T <= 1) {
+        for (int i = 0; i < n; i++) fn(ctx, i);
+        return;
+    }
+    pthread_t th[256];
+    par_range rg[256];
+    int ok[256];
+    for (int t = 0; t < T; t++) {
+        rg[t].fn = fn;
+        rg[t].ctx = ctx;
+        rg[t].i0 = (int)((long long)n * t / T);
+        rg[t].i1 = (int)((long long)n * (t + 1) / T);
+        rg[t].slot = t;
+        ok[t] = t > 0 && pthread_create(&th[t], NULL, par_worker, &rg[t]) == 0;
+    }
+    par_worker(&rg[0]);
+    for (int t = 1; t < T; t++) {
+        if (ok[t]) pthread_join(th[t], NULL);
+        else par_worker(&rg[t]); /* a thread that could not start: its range runs here */
+    }
+}
 
 static int fail(const char *msg, const char *detail) {
     snprintf(g_err, sizeof g_err, "%s%s%s", msg, detail ? ": " : "", detail ? detail : "");
@@ -280,18 +328,45 @@ float orc_dot(const float *a, const float *b, int n) {
 /* y(M,N) = x(M,K) . wt(K,N) [+ bias]; Tensor.java:383-398 (M=1) and :460-489 (M>1):
  * both accumulate out[i][j] over k ascending from 0.  Bias added after
  * (Linear.java:25 -> Tensor.java:251-263). */
+static void linear_cols(const float *xi, int K, const float *wt, const float *bias, int N, float *yi, int j0, int j1) {
+    for (int j = j0; j < j1; j++) yi[j] = 0.0f;
+    for (int k = 0; k < K; k++) {
+        const float xk = xi[k];
+        const float *wk = wt + (size_t)k * N;
+        for (int j = j0; j < j1; j++) yi[j] = yi[j] + xk * wk[j];
+    }
+    if (bias)
+        for (int j = j0; j < j1; j++) yi[j] = yi[j] + bias[j];
+}
+
+typedef struct {
+    const float *x, *wt, *bias;
+    int K, N, row;
+    float *y;
+} linear_job;
+static void linear_row_job(void *p, int i) {
+    const linear_job *j = (const linear_job *)p;
+    linear_cols(j->x + (size_t)i * j->K, j->K, j->wt, j->bias, j->N, j->y + (size_t)i * j->N, 0, j->N);
+}
+static void linear_block_job(void *p, int b) {
+    const linear_job *j = (const linear_job *)p;
+    const int j0 = b * 256, j1 = j0 + 256 < j->N ? j0 + 256 : j->N;
+    linear_cols(j->x + (size_t)j->row * j->K, j->K, j->wt, j->bias, j->N, j->y + (size_t)j->row * j->N, j0, j1);
+}
+
 static void linear(const float *x, int M, int K, const float *wt, const float *bias, int N, float *y) {
+    linear_job job = {x, wt, bias, K, N, 0, y};
+    if (g_threads > 1 && M >= 2 * g_threads) {
+        par_for(M, linear_row_job, &job);
+        return;
+    }
     for (int i = 0; i < M; i++) {
-        float *yi = y + (size_t)i * N;
-        for (int j = 0; j < N; j++) yi[j] = 0.0f;
-        const float *xi = x + (size_t)i * K;
-        for (int k = 0; k < K; k++) {
-            const float xk = xi[k];
-            const float *wk = wt + (size_t)k * N;
-            for (int j = 0; j < N; j++) yi[j] = yi[j] + xk * wk[j];
+        if (g_threads > 1 && N >= 512) {
+            job.row = i;
+            par_for((N + 255) / 256, linear_block_job, &job);
+        } else {
+            linear_cols(x + (size_t)i * K, K, wt, bias, N, y + (size_t)i * N, 0, N);
         }
-        if (bias)
-            for (int j = 0; j < N; j++) yi[j] = yi[j] + bias[j];
     }
 }
 
@@ -344,6 +419,39 @@ static void attention_head(const float *q, const float *k, const float *v, int k
         const float *vr = v + (size_t)j * row_stride;
         for (int dd = 0; dd < 64; dd++) out[dd] = out[dd] + sj * vr[dd];
     }
+}
+
+/* one (row, head) of an attention loop; mask_c >= 0: the multi-token causal mask with n_ctx mask_c */
+typedef struct {
+    const float *q, *K, *V;
+    float *out;
+    int d, H, kv_len, mask_c;
+    float scale;
+    float *scores;
+    int scores_len;
+} attn_job;
+static void attn_self_job(void *p, int th) {
+    const attn_job *j = (const attn_job *)p;
+    const int t = th / j->H, hh = th % j->H;
+    int masked_from = j->kv_len, masked_to = j->kv_len;
+    if (j->mask_c >= 0 && t < j->mask_c) {
+        masked_from = t + 1;
+        masked_to = j->kv_len < j->mask_c ? j->kv_len : j->mask_c;
+    }
+    float *sc = j->scores + (size_t)j->scores_len * (size_t)g_worker; /* this range's score buffer */
+    attention_head(j->q + (size_t)t * j->d + hh * 64, j->K + hh * 64, j->V + hh * 64, j->kv_len, j->d, masked_from,
+                   masked_to, j->scale, sc, j->out + (size_t)t * j->d + hh * 64);
+}
+
+typedef struct {
+    const float *x, *E;
+    int d, V;
+    float *out;
+} logits_job;
+static void logits_block_job(void *p, int b) {
+    const logits_job *j = (const logits_job *)p;
+    const int j1 = (b + 1) * 1024 < j->V ? (b + 1) * 1024 : j->V;
+    for (int v = b * 1024; v < j1; v++) j->out[v] = orc_dot(j->x, j->E + (size_t)v * j->d, j->d) * 1.0f;
 }
 
 /* KATs for the reference's tensor unit tests (TensorTest.java). */
@@ -485,7 +593,7 @@ int orc_forward(const orc_model *m, const int *tokens, int n, const float *xa, i
     float *knew = (float *)malloc((size_t)n * d * sizeof(float));
     float *vnew = (float *)malloc((size_t)n * d * sizeof(float));
     int scores_len = kv_len > n_audio_ctx ? kv_len : n_audio_ctx;
-    float *scores = (float *)malloc((size_t)scores_len * sizeof(float));
+    float *scores = (float *)malloc((size_t)scores_len * g_threads * sizeof(float));
     float *selfk = NULL, *selfv = NULL; /* no-cache path: own K/V */
     float *xk_tmp = NULL, *xv_tmp = NULL;
     if (cache) cache_reserve(cache, kv_len);
@@ -515,19 +623,13 @@ int orc_forward(const orc_model *m, const int *tokens, int n, const float *xa, i
             K = selfk;
             Vv = selfv;
         }
-        for (int t = 0; t < n; t++)
-            for (int hh = 0; hh < H; hh++) {
-                /* mask (WhisperDecoder.java:43-49, Tensor.java:622-640) applies only when
-                 * qLen > 1, relative to this call's first row, and only to the first
-                 * min(kvLen, C) key columns. */
-                int masked_from = kv_len, masked_to = kv_len;
-                if (n > 1 && t < C) {
-                    masked_from = t + 1;
-                    masked_to = kv_len < C ? kv_len : C;
-                }
-                attention_head(q + (size_t)t * d + hh * 64, K + hh * 64, Vv + hh * 64, kv_len, d, masked_from,
-                               masked_to, scale, scores, merged + (size_t)t * d + hh * 64);
-            }
+        {
+            /* mask (WhisperDecoder.java:43-49, Tensor.java:622-640) applies only when
+             * qLen > 1, relative to this call's first row, and only to the first
+             * min(kvLen, C) key columns. */
+            attn_job job = {q, K, Vv, merged, d, H, kv_len, n > 1 ? C : -1, scale, scores, scores_len};
+            par_for(n * H, attn_self_job, &job);
+        }
         linear(merged, n, d, Ly->o_wt, Ly->o_b, d, tmp);
         for (long i = 0; i < (long)n * d; i++) x[i] = tmp[i] + x[i]; /* attnOut.addInPlace(x) */
 
@@ -557,10 +659,10 @@ int orc_forward(const orc_model *m, const int *tokens, int n, const float *xa, i
             XK = kk;
             XV = vv;
         }
-        for (int t = 0; t < n; t++)
-            for (int hh = 0; hh < H; hh++)
-                attention_head(q + (size_t)t * d + hh * 64, XK + hh * 64, XV + hh * 64, n_audio_ctx, d, n_audio_ctx,
-                               n_audio_ctx, scale, scores, merged + (size_t)t * d + hh * 64);
+        {
+            attn_job job = {q, XK, XV, merged, d, H, n_audio_ctx, -1, scale, scores, scores_len};
+            par_for(n * H, attn_self_job, &job);
+        }
         linear(merged, n, d, Ly->xo_wt, Ly->xo_b, d, tmp);
         for (long i = 0; i < (long)n * d; i++) x[i] = x[i] + tmp[i];
 
@@ -577,9 +679,10 @@ int orc_forward(const orc_model *m, const int *tokens, int n, const float *xa, i
     }
 
     layer_norm(x, n, d, m->ln_w, m->ln_b, 1e-5f, ln);
-    for (int t = 0; t < n; t++)
-        for (int j = 0; j < V; j++)
-            logits[(size_t)t * V + j] = orc_dot(ln + (size_t)t * d, m->tok_emb + (size_t)j * d, d) * 1.0f;
+    for (int t = 0; t < n; t++) {
+        logits_job job = {ln + (size_t)t * d, m->tok_emb, d, V, logits + (size_t)t * V};
+        par_for((V + 1023) / 1024, logits_block_job, &job);
+    }
 
     free(x); free(ln); free(q); free(merged); free(tmp); free(h); free(knew); free(vnew); free(scores);
     free(xk_tmp); free(xv_tmp);
@@ -807,6 +910,31 @@ static int dcompare(double a, double b) {
     return bs - as;
 }
 
+/* Optional trace of the beam search for parity tests: every ranked candidate of every step as
+ * (step, parent beam, token, score, outcome), outcome = new beam index (kept), -2 (finished) or
+ * -1 (dropped or not reached).  Step 0 records the initial top-beam expansion (parent -1). */
+static __thread double *g_trace = NULL;
+static __thread long g_trace_cap = 0, g_trace_n = 0;
+
+void orc_set_beam_trace(double *buf, long cap_entries) {
+    g_trace = buf;
+    g_trace_cap = buf ? cap_entries : 0;
+    g_trace_n = 0;
+}
+
+long orc_beam_trace_count(void) { return g_trace_n; }
+
+static void trace_put(int step, int parent, int token, double score, int outcome) {
+    if (!g_trace || g_trace_n >= g_trace_cap) return;
+    double *e = g_trace + g_trace_n * 5;
+    e[0] = step;
+    e[1] = parent;
+    e[2] = token;
+    e[3] = score;
+    e[4] = outcome;
+    g_trace_n++;
+}
+
 int orc_decode_beam(const orc_model *m, const float *xa, int n_audio_ctx, const int *prompt, int n_prompt, int eot,
                     int max_tokens, const int *suppress, int n_suppress, int no_speech, int ts_begin, int beam,
                     int *out_tokens, int *out_len, double *out_sum_logprob, float *out_avg_logprob,
@@ -860,6 +988,7 @@ int orc_decode_beam(const orc_model *m, const float *xa, int n_audio_ctx, const 
         btok[(size_t)b * max_tokens] = top[b];
         blen[b] = 1;
         blp[b] = (double)lp[top[b]];
+        trace_put(0, -1, top[b], blp[b], b);
         if (b > 0) {
             cache_share_cross(caches[b], owner);
             cache_copy_self(caches[b], caches[0]);
@@ -900,10 +1029,12 @@ int orc_decode_beam(const orc_model *m, const float *xa, int n_audio_ctx, const 
             }
             cands[j + 1] = c;
         }
-        int saved = 0;
+        int saved = 0, walked = 0;
         for (int i = 0; i < nc; i++) {
             int sb = cands[i].beam, token = cands[i].token;
+            walked = i + 1;
             if (token == eot) {
+                trace_put(step, sb, token, cands[i].score, -2);
                 if (fin_n == fin_cap) break; /* unreachable: loop breaks at beam finished */
                 fin_tok[fin_n] = (int *)malloc((size_t)blen[sb] * sizeof(int) + 1);
                 memcpy(fin_tok[fin_n], btok + (size_t)sb * max_tokens, (size_t)blen[sb] * sizeof(int));
@@ -913,6 +1044,7 @@ int orc_decode_beam(const orc_model *m, const float *xa, int n_audio_ctx, const 
                 if (fin_n >= beam) break;
                 continue;
             }
+            trace_put(step, sb, token, cands[i].score, saved < beam ? saved : -1);
             if (saved >= beam) continue;
             memcpy(nbtok + (size_t)saved * max_tokens, btok + (size_t)sb * max_tokens, (size_t)blen[sb] * sizeof(int));
             nbtok[(size_t)saved * max_tokens + blen[sb]] = token;
@@ -921,6 +1053,7 @@ int orc_decode_beam(const orc_model *m, const float *xa, int n_audio_ctx, const 
             src[saved] = sb;
             saved++;
         }
+        for (int i = walked; i < nc; i++) trace_put(step, cands[i].beam, cands[i].token, cands[i].score, -1);
         if (saved == 0 || fin_n >= beam) break;
         /* :343-361 rearrange caches */
         for (int b = 0; b < saved; b++) {

@@ -25,6 +25,10 @@ const char *orc_last_error(void);
  * projection excluded), on the calling thread. */
 double orc_last_loop_seconds(void);
 
+/* Threads of the oracle's own loops (default 1, the reference's single-threaded decoder);
+ * results do not depend on it. */
+void orc_set_threads(int n);
+
 orc_model *orc_model_new(const orc_dims *d);
 void orc_model_free(orc_model *m);
 /* name: canonical GGML tensor name; data: f32 values in the file's row-major
@@ -53,6 +57,12 @@ int orc_decode_beam(const orc_model *m, const float *xa, int n_audio_ctx, const 
                     int max_tokens, const int *suppress, int n_suppress, int no_speech, int ts_begin, int beam,
                     int *out_tokens, int *out_len, double *out_sum_logprob, float *out_avg_logprob,
                     float *out_no_speech_prob, int max_steps);
+
+/* Beam-search trace (parity tests): while set, orc_decode_beam on this thread appends 5 doubles
+ * per ranked candidate: step, parent beam, token, score, outcome (kept beam index, -2 finished,
+ * -1 dropped or not reached).  buf = NULL stops tracing. */
+void orc_set_beam_trace(double *buf, long cap_entries);
+long orc_beam_trace_count(void);
 
 /* processors exposed for unit tests */
 void orc_apply_repetition_penalty(float *logits, const int *gen, int count, int n);

@@ -1,8 +1,8 @@
 #!/usr/bin/env python3
 """Generate golden decode-step vectors from the reference's own Python restatement.
 
-Run in a container where the reference tree is mounted (its path is given with
---reference, default /root/reference).  It imports the reference's
+Run where a checkout of the reference is available; its path is given with
+--reference.  It imports the reference's
 ``tools/validate_decode_steps.py`` (``load_ggml`` and ``decoder_step``, the
 numpy restatement that the reference's ValidateAgainstReferenceTest pins the
 Java decoder against), feeds it a seeded synthetic GGML model written by
@@ -46,7 +46,7 @@ def encoder_output(seed: int, n_audio_ctx: int, d: int) -> np.ndarray:
 
 def main():
     ap = argparse.ArgumentParser()
-    ap.add_argument("--reference", default="/root/reference")
+    ap.add_argument("--reference", required=True, help="checkout of sparrowlogic/whisper4j (its tools/ directory)")
     ap.add_argument("--out", default=HERE)
     args = ap.parse_args()
     sys.path.insert(0, os.path.join(args.reference, "tools"))

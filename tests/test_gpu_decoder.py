@@ -11,8 +11,8 @@ from oracle import oracle as O
 from whisper4j_b200 import ggml
 from whisper4j_b200.decoder import WhisperDecoder
 
-from .helpers import (LOGIT_ATOL, SMALL, SMALL_OPTS, assert_logits_close, encoder_output, first_divergence,
-                      load_golden, parsed)
+from .helpers import (LOGIT_ATOL, SMALL, SMALL_OPTS, assert_logits_close, check_beam, encoder_output,
+                      first_divergence, load_golden, parsed)
 
 pytestmark = pytest.mark.gpu
 
@@ -85,6 +85,51 @@ def test_forward_without_cache_leaves_cache_alone(small):
     ora.forward([5, 6], xas[1], o_cache)
     assert_logits_close(c, ora.forward([8], xas[1], o_cache))
     assert_logits_close(a, ora.forward([5, 6], xas[1], None))
+
+
+def test_forward_past_n_text_ctx_matches_oracle(small):
+    """WhisperDecoder.java:72: offset = min(cache length, n_ctx - seqLen) while the cache keeps
+    growing, so positions past n_text_ctx reuse the last positional row."""
+    dec, ora, xas = small
+    cache_d, cache_o = dec.new_cache(2), ora.new_cache()
+    prompt = [996, 997, 998, 999]
+    assert_logits_close(dec.forward(prompt, kv_cache=cache_d), ora.forward(prompt, xas[2], cache_o))
+    rng = np.random.default_rng(3)
+    for i in range(SMALL.n_text_ctx + 8):
+        t = [int(rng.integers(0, SMALL.n_vocab))]
+        assert_logits_close(dec.forward(t, kv_cache=cache_d), ora.forward(t, xas[2], cache_o),
+                            what=f"position {len(prompt) + i}")
+    assert len(cache_o) == len(prompt) + SMALL.n_text_ctx + 8
+
+
+def test_forward_multi_token_on_filled_cache(small):
+    """MultiHeadAttention.java:84-88 with Tensor.java:622-640: a multi-token call applies the
+    (n_ctx x n_ctx) causal mask from key column 0 even when the cache already holds rows, so query t
+    attends keys [0, t] and [n_ctx, kv_len) — not its own new rows.  Also a call that crosses
+    n_text_ctx (clamped offset) and one of n_text_ctx tokens."""
+    dec, ora, xas = small
+    rng = np.random.default_rng(9)
+    cache_d, cache_o = dec.new_cache(3), ora.new_cache()
+    for n in (4, 3, 1, 20, 30, 10, 2):
+        t = [int(v) for v in rng.integers(0, SMALL.n_vocab, n)]
+        assert_logits_close(dec.forward(t, kv_cache=cache_d), ora.forward(t, xas[3], cache_o),
+                            what=f"{n} tokens after {len(cache_o) - n}")
+    full = [int(v) for v in rng.integers(0, SMALL.n_vocab, SMALL.n_text_ctx)]
+    cache_d, cache_o = dec.new_cache(3), ora.new_cache()
+    assert_logits_close(dec.forward(full, kv_cache=cache_d), ora.forward(full, xas[3], cache_o))
+    assert_logits_close(dec.forward(full[:40], kv_cache=cache_d), ora.forward(full[:40], xas[3], cache_o))
+    assert_logits_close(dec.forward(full[:40], kv_cache=None, slot=3), ora.forward(full[:40], xas[3], None))
+    with pytest.raises(ValueError):
+        dec.forward([1] * (SMALL.n_text_ctx + 1), kv_cache=cache_d)
+
+
+def test_beam_past_n_text_ctx_matches_oracle(small):
+    dec, ora, xas = small
+    prompt, eot, n = [996, 997], 995, SMALL.n_text_ctx + 6
+    r = dec.decode_beam(None, prompt, eot, n, suppress_tokens=[eot], beam_size=3)
+    w = ora.decode_beam(xas[0], prompt, eot, n, suppress=[eot], beam=3, trace=True)
+    assert len(r.tokens) == n
+    check_beam(r.tokens, w, ora, xas[0], prompt, [eot], eot, 3, n)
 
 
 @pytest.mark.parametrize("case", ["small_rand", "tiny_en"])
@@ -177,8 +222,15 @@ def test_greedy_max_tokens_edge_cases(small):
     # prompt + generated fills the whole 64-position context
     rf = dec.decode(None, [996, 997], 995, SMALL.n_text_ctx - 1, suppress_tokens=[995])
     assert len(rf.tokens) == SMALL.n_text_ctx - 1
+    # past n_text_ctx the reference reuses the last positional row while its cache keeps growing
+    # (WhisperDecoder.java:72): same as the oracle
+    n = SMALL.n_text_ctx + 12
+    rp = dec.decode(None, [996, 997], 995, n, suppress_tokens=[995])
+    wp = ora.decode(xas[0], [996, 997], 995, n, suppress=[995])
+    assert len(rp.tokens) == n
+    check_tokens(rp.tokens, wp["tokens"], ora, xas[0], [996, 997])
     with pytest.raises(ValueError):
-        dec.decode(None, [996, 997], 995, SMALL.n_text_ctx)
+        dec.decode(None, [996] * (SMALL.n_text_ctx + 1), 995, 4)  # a prompt longer than the positional table
 
 
 def test_tiny_greedy_64_tokens(tiny):
@@ -199,11 +251,9 @@ def test_beam_forced_length_matches_oracle(small, beam):
     dec, ora, xas = small
     prompt, eot = [996, 997, 998, 999], 995
     r = dec.decode_beam_batch([1], [prompt], eot, 16, suppress_tokens=[eot], no_speech_token=3, beam_size=beam)[0]
-    w = ora.decode_beam(xas[1], prompt, eot, 16, suppress=[eot], no_speech=3, beam=beam)
-    if r.tokens == w["tokens"]:
+    w = ora.decode_beam(xas[1], prompt, eot, 16, suppress=[eot], no_speech=3, beam=beam, trace=True)
+    if check_beam(r.tokens, w, ora, xas[1], prompt, [eot], eot, beam, 16) == "equal":
         assert r.sum_logprob == pytest.approx(w["sum_logprob"], abs=2e-2)
-    else:  # a near tie among beam scores may reorder candidates: compare scores instead
-        assert r.sum_logprob == pytest.approx(w["sum_logprob"], abs=5e-2)
     assert len(r.tokens) == 16
     assert r.no_speech_prob == pytest.approx(w["no_speech_prob"], rel=2e-2, abs=1e-6)
 
@@ -214,9 +264,9 @@ def test_beam_with_finished_sequences(small):
     free = ora.decode_beam(xas[2], prompt, 995, 12, suppress=[995], beam=3)
     eot = free["tokens"][4]  # an id the beams actually reach, so sequences finish early
     r = dec.decode_beam_batch([2], [prompt], eot, 12, beam_size=3)[0]
-    w = ora.decode_beam(xas[2], prompt, eot, 12, beam=3)
-    assert r.tokens == w["tokens"]
-    assert r.sum_logprob == pytest.approx(w["sum_logprob"], abs=2e-2)
+    w = ora.decode_beam(xas[2], prompt, eot, 12, beam=3, trace=True)
+    if check_beam(r.tokens, w, ora, xas[2], prompt, [], eot, 3, 12) == "equal":
+        assert r.sum_logprob == pytest.approx(w["sum_logprob"], abs=2e-2)
 
 
 def test_beam_batch_equals_single(small):
@@ -232,8 +282,9 @@ def test_tiny_beam(tiny):
     dec, ora, xa = tiny
     prompt, eot = [50257, 50258, 50259, 50362], 50256
     r = dec.decode_beam(None, prompt, eot, 12, suppress_tokens=[eot], beam_size=3)
-    w = ora.decode_beam(xa, prompt, eot, 12, suppress=[eot], beam=3)
-    assert r.sum_logprob == pytest.approx(w["sum_logprob"], abs=5e-2)
+    w = ora.decode_beam(xa, prompt, eot, 12, suppress=[eot], beam=3, trace=True)
+    if check_beam(r.tokens, w, ora, xa, prompt, [eot], eot, 3, 12) == "equal":
+        assert r.sum_logprob == pytest.approx(w["sum_logprob"], abs=2e-2)
     assert len(r.tokens) == 12
 
 
@@ -253,8 +304,9 @@ def test_q8_0_model_matches_oracle():
         w = ora.decode(xa, prompt, 995, 20, suppress=[995])
         check_tokens(r.tokens, w["tokens"], ora, xa, prompt)
         rb = dec.decode_beam(None, prompt, 995, 8, suppress_tokens=[995], beam_size=2)
-        wb = ora.decode_beam(xa, prompt, 995, 8, suppress=[995], beam=2)
-        assert rb.sum_logprob == pytest.approx(wb["sum_logprob"], abs=5e-2)
+        wb = ora.decode_beam(xa, prompt, 995, 8, suppress=[995], beam=2, trace=True)
+        if check_beam(rb.tokens, wb, ora, xa, prompt, [995], 995, 2, 8) == "equal":
+            assert rb.sum_logprob == pytest.approx(wb["sum_logprob"], abs=2e-2)
 
 
 # ---------------------------------------------------------------------------
@@ -272,12 +324,82 @@ def test_sampling_is_seeded_and_valid(small):
     assert np.isfinite(a.avg_logprob)
 
 
-def test_decode_with_fallback_runs_policy(small):
-    dec, _, _ = small
+@pytest.mark.parametrize("allowed,n,seed", [(None, 24, 3), (8, 100, 11)])
+def test_decode_with_fallback_matches_policy(small, allowed, n, seed):
+    """w4j_decode_with_fallback against a restatement of WhisperDecoder.java:119-149 driven by the same
+    device decodes (each temperature decoded alone with the same seed; sampling is seeded, so the
+    attempts are reproducible).  Random-init log-probabilities are far below -1, so every result
+    needs a fallback: with the full vocabulary the temperature-0 result compresses below 2.4 and the
+    policy stops there (it must also match the oracle); with 8 allowed ids over 100 forced tokens the
+    greedy ids compress above 2.4 and the policy goes on to the sampled attempts."""
+    from .helpers import fallback_policy_ref
+    dec, ora, xas = small
     prompt = [996, 997, 998, 999]
-    r = dec.decode_with_fallback(None, prompt, 995, 24, suppress_tokens=[995])
-    assert r.temperature in (0.0, 0.2, 0.4, 0.6, 0.8, 1.0)
-    assert len(r.tokens) == 24
+    sup = [995] if allowed is None else [t for t in range(SMALL.n_vocab) if not 100 <= t < 100 + allowed]
+    r = dec.decode_with_fallback(None, prompt, 995, n, suppress_tokens=sup, seed=seed)
+    want, want_t, attempts = fallback_policy_ref(
+        lambda t: dec.decode(None, prompt, 995, n, suppress_tokens=sup, temperature=t, seed=seed))
+    assert r.temperature == want_t and r.tokens == want.tokens
+    assert r.avg_logprob == pytest.approx(want.avg_logprob, abs=1e-6)
+    if allowed is None:
+        assert attempts == 1 and r.temperature == 0.0
+        w = ora.decode(xas[0], prompt, 995, n, suppress=sup)
+        check_tokens(r.tokens, w["tokens"], ora, xas[0], prompt)
+    assert len(r.tokens) == n
+
+
+def test_cancel_from_another_thread(small):
+    """w4j_cancel (TranscriptionHandle cancellation, WhisperModel.java:620-633) from a second host thread
+    stops a long decode at a step boundary with W4J_ERR_CANCELLED; the context stays usable."""
+    import threading
+    import time
+
+    from whisper4j_b200._lib import CancelledError
+    dec, ora, xas = small
+    prompt = [996, 997, 998, 999]
+    done = threading.Event()
+
+    def canceller():
+        while not done.is_set():
+            dec.cancel()
+            time.sleep(0.0005)
+
+    th = threading.Thread(target=canceller)
+    th.start()
+    try:
+        with pytest.raises(CancelledError):
+            dec.decode(None, prompt, 995, 4000, suppress_tokens=[995])
+    finally:
+        done.set()
+        th.join()
+    r = dec.decode(None, prompt, 995, 16, suppress_tokens=[995])
+    w = ora.decode(xas[0], prompt, 995, 16, suppress=[995])
+    check_tokens(r.tokens, w["tokens"], ora, xas[0], prompt)
+
+
+def test_host_injected_failures(small):
+    """Failures made on the host, none on the GPU: a context whose caches cannot be allocated
+    (W4J_ERR_OOM -> MemoryError), a truncated GGML payload (IllegalArgumentException -> ValueError);
+    the existing context keeps working afterwards."""
+    from whisper4j_b200._lib import Dims, check, lib
+    import ctypes
+    dec, ora, xas = small
+    gm = parsed(SMALL, 101, "f16", SO)
+    big = ggml.ModelDimensions(80, 1500, 1280, 20, 1, 51866, 448, 1280, 20, 4)
+    cd = Dims(*[getattr(big, f) for f in ("n_mels", "n_audio_ctx", "n_audio_state", "n_audio_head", "n_audio_layer",
+                                           "n_vocab", "n_text_ctx", "n_text_state", "n_text_head", "n_text_layer")])
+    h = ctypes.c_void_p()
+    with pytest.raises(MemoryError):  # 1e5 streams x 31 MB of cross K/V: far beyond any GPU
+        check(lib().w4j_ctx_create(ctypes.byref(cd), 0, 100000, 1, ctypes.byref(h)))
+    assert not h.value
+    t = gm.tensors["decoder.blocks.0.mlp.0.weight"]
+    buf = np.frombuffer(t.data, np.uint8)[:-2]  # two bytes short
+    ne = (ctypes.c_int64 * len(t.ne))(*t.ne)
+    with pytest.raises(ValueError, match="payload size"):
+        check(lib().w4j_upload_tensor(dec._ctx, t.name.encode(), t.ttype, ne, len(t.ne),
+                                      buf.ctypes.data_as(ctypes.c_void_p), buf.size))
+    r = dec.decode(None, [996, 997, 998, 999], 995, 8, suppress_tokens=[995])
+    assert len(r.tokens) == 8
 
 
 # ---------------------------------------------------------------------------

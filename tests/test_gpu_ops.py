@@ -47,10 +47,12 @@ def gelu_table():
 # M >= 16 runs on the tcgen05 projection kernel (f16 hi/lo activations, split K over a cluster)
 @pytest.mark.parametrize("M,K,N", [(1, 384, 1152), (5, 512, 512), (3, 1280, 5120), (8, 2048, 512), (16, 768, 300),
                                    (17, 512, 1536), (32, 1280, 3840), (32, 5120, 1280), (64, 1024, 4096),
-                                   (64, 5120, 1280), (100, 384, 1152), (128, 512, 512)])
+                                   (64, 5120, 1280), (100, 384, 1152), (128, 512, 512), (129, 1280, 3840),
+                                   (256, 1280, 5120), (256, 5120, 1280), (200, 768, 768)])
 @pytest.mark.parametrize("epi", [0, 1, 2])
 @pytest.mark.parametrize("use_ln", [False, True])
 def test_linear_f16(dec, M, K, N, epi, use_ln):
+    """Past 128 rows the tcgen05 kernel walks 128-row chunks of the activations (grid z)."""
     rng = np.random.default_rng(M * 7 + K + N + epi)
     x = rng.standard_normal((M, K)).astype(np.float32)
     W = (rng.standard_normal((N, K)) * 0.05).astype(np.float16)
@@ -74,9 +76,14 @@ def test_linear_f16(dec, M, K, N, epi, use_ln):
     np.testing.assert_allclose(got, ref, atol=2e-4 * np.sqrt(K) + 1e-3 * (epi == 1), rtol=1e-4)
 
 
-@pytest.mark.parametrize("M,K,N", [(1, 512, 512), (5, 384, 1536), (2, 1280, 700)])
-def test_linear_q8_0(dec, M, K, N):
-    rng = np.random.default_rng(K + N)
+# M >= 16 with N a multiple of 128 runs on the tcgen05 kernel: int8 tiles by TMA, dequantised in
+# shared memory into f16 hi / lo tiles (exact q * scale), two MMAs per k-step
+@pytest.mark.parametrize("M,K,N", [(1, 512, 512), (5, 384, 1536), (2, 1280, 700), (16, 512, 512), (40, 1280, 3840),
+                                   (40, 5120, 1280), (40, 1280, 5120), (129, 1280, 1280), (256, 1280, 3840),
+                                   (24, 1280, 700)])
+@pytest.mark.parametrize("use_ln,epi", [(False, 0), (True, 1), (False, 2)])
+def test_linear_q8_0(dec, M, K, N, use_ln, epi):
+    rng = np.random.default_rng(K + N + M)
     x = rng.standard_normal((M, K)).astype(np.float32)
     W = (rng.standard_normal((N, K)) * 0.05).astype(np.float32)
     blocks = np.frombuffer(ggml.quantize_q8_0(W), np.uint8)
@@ -84,12 +91,22 @@ def test_linear_q8_0(dec, M, K, N):
     tsrc = torch.tensor(blocks, device="cuda")
     tdst = torch.zeros(N * K + N * K // 16, dtype=torch.uint8, device="cuda")
     check(lib().w4j_q8_0_repack(vp(tsrc), N, K, vp(tdst), None))
-    tx = torch.tensor(x, device="cuda")
-    ty = torch.zeros((M, N), device="cuda")
-    check(lib().w4j_op_linear(dec._ctx, vp(tx), M, K, vp(tdst), GGML_Q8_0, N, None, None, None, 0, vp(ty), None))
+    b = (rng.standard_normal(N) * 0.1).astype(np.float32)
+    g = (1 + 0.1 * rng.standard_normal(K)).astype(np.float32)
+    beta = (0.1 * rng.standard_normal(K)).astype(np.float32)
+    y0 = rng.standard_normal((M, N)).astype(np.float32)
+    tx, tb = torch.tensor(x, device="cuda"), torch.tensor(b, device="cuda")
+    tg, tbeta, ty = torch.tensor(g, device="cuda"), torch.tensor(beta, device="cuda"), torch.tensor(y0, device="cuda")
+    check(lib().w4j_op_linear(dec._ctx, vp(tx), M, K, vp(tdst), GGML_Q8_0, N, vp(tb), vp(tg) if use_ln else None,
+                              vp(tbeta) if use_ln else None, epi, vp(ty), None))
     torch.cuda.synchronize()
-    ref = x.astype(np.float64) @ Wq.astype(np.float64).T
-    np.testing.assert_allclose(ty.cpu().numpy(), ref, atol=2e-4 * np.sqrt(K), rtol=1e-4)
+    xin = ln_ref(x.astype(np.float64), g, beta) if use_ln else x.astype(np.float64)
+    ref = xin @ Wq.astype(np.float64).T + b
+    if epi == 1:
+        ref = gelu_table()[ref.astype(np.float32).astype(np.float16).view(np.uint16)]
+    elif epi == 2:
+        ref = y0 + ref
+    np.testing.assert_allclose(ty.cpu().numpy(), ref, atol=2e-4 * np.sqrt(K) + 1e-3 * (epi == 1), rtol=1e-4)
 
 
 def test_linear_rejects_bad_shapes(dec):

@@ -98,3 +98,44 @@ def test_no_device_memory_taken():
         check(_call(dev, _vp(x), M, d, _vp(E), V, _vp(g), _vp(b), _vp(tok), _vp(lp)))
     torch.cuda.synchronize()
     assert torch.cuda.mem_get_info()[0] == free0
+
+
+@pytest.mark.gpu
+def test_wait_timeout_reports_through_error_word(vocab_ctx):
+    """A bounded wait inside the vocabulary pass that runs out (the test hook withholds the kernel's
+    weight copies, so no GPU fault is involved) is reported through the error word: every id -1,
+    every log-probability NaN.  The next call is normal again, which shows the word was cleared.
+    The context op reports the same way through its own error word."""
+    import torch
+
+    d, M = 384, 4
+    x, E, g, b = _inputs(torch, M, d, 5)
+    dev = torch.cuda.current_device()
+    tok = torch.zeros(M, dtype=torch.int32, device="cuda")
+    lp = torch.zeros(M, dtype=torch.float64, device="cuda")
+    tok_b, lp_b = tok.clone(), lp.clone()
+    check(lib().w4j_test_withhold_logits_copies(1))
+    try:
+        check(_call(dev, _vp(x), M, d, _vp(E), V, _vp(g), _vp(b), _vp(tok), _vp(lp)))
+        torch.cuda.synchronize()
+    finally:
+        check(lib().w4j_test_withhold_logits_copies(0))
+    assert tok.tolist() == [-1] * M and bool(torch.isnan(lp).all())
+    check(_call(dev, _vp(x), M, d, _vp(E), V, _vp(g), _vp(b), _vp(tok), _vp(lp)))
+    check(lib().w4j_op_logits_argmax(vocab_ctx._ctx, _vp(x), M, _vp(E), V, _vp(g), _vp(b), _vp(tok_b), _vp(lp_b),
+                                     None))
+    torch.cuda.synchronize()
+    assert (tok >= 0).all() and tok.tolist() == tok_b.tolist()
+    # the context op
+    check(lib().w4j_test_withhold_logits_copies(1))
+    try:
+        check(lib().w4j_op_logits_argmax(vocab_ctx._ctx, _vp(x), M, _vp(E), V, _vp(g), _vp(b), _vp(tok_b),
+                                         _vp(lp_b), None))
+        torch.cuda.synchronize()
+    finally:
+        check(lib().w4j_test_withhold_logits_copies(0))
+    assert tok_b.tolist() == [-1] * M and bool(torch.isnan(lp_b).all())
+    check(lib().w4j_op_logits_argmax(vocab_ctx._ctx, _vp(x), M, _vp(E), V, _vp(g), _vp(b), _vp(tok_b), _vp(lp_b),
+                                     None))
+    torch.cuda.synchronize()
+    assert tok_b.tolist() == tok.tolist()

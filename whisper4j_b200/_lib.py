@@ -71,10 +71,13 @@ SIGNATURES = {
     "w4j_compression_ratio": (_F, [_P, _I]),
     "w4j_needs_fallback": (_I, [_F, _F, _F]),
     "w4j_last_timing": (_I, [_P, ctypes.POINTER(_D), ctypes.POINTER(_I), ctypes.POINTER(ctypes.c_longlong)]),
+    "w4j_set_kernel_timing": (_I, [_P, _I]),
+    "w4j_kernel_timing": (_I, [_P, ctypes.POINTER(_D), ctypes.POINTER(ctypes.c_longlong)]),
     "w4j_op_linear": (_I, [_P, _P, _I, _I, _P, _I, _I, _P, _P, _P, _I, _P, _P]),
     "w4j_q8_0_repack": (_I, [_P, _I, _I, _P, _P]),
     "w4j_op_logits_argmax": (_I, [_P, _P, _I, _P, _I, _P, _P, _P, _P, _P]),
     "w4j_op_logits_argmax_noalloc": (_I, [_I, _P, _I, _I, _P, _I, _P, _P, _P, _P, _P]),
+    "w4j_test_withhold_logits_copies": (_I, [_I]),
 }
 
 _lib = None

@@ -85,9 +85,10 @@ __device__ __forceinline__ void group_sync(int bar) {
 }
 
 // gtid: the thread's index among the kAttnThreads threads running the tile; bar: their barrier.
+// kpos0: position of the tile's first key; keys with mk.x <= position < mk.y are masked.
 template <int NQ>
 __device__ __forceinline__ void attn_tile(const AttnShared &sh, const __half *sk, const __half *sv, int nk,
-                                          float (&of)[4][4], int gtid, int bar) {
+                                          float (&of)[4][4], int gtid, int bar, int kpos0, int2 mk) {
     const int tid = gtid, warp = tid >> 5, lane = tid & 31;
     const int g = lane >> 2, tq = lane & 3;
     const float scale = 0.125f;  // (float)(1 / sqrt(64))
@@ -109,7 +110,9 @@ __device__ __forceinline__ void attn_tile(const AttnShared &sh, const __half *sk
     }
     // c0: (key kb+g, query 2tq), c1: (kb+g, 2tq+1), c2: (kb+g+8, 2tq), c3: (kb+g+8, 2tq+1)
     const int q0 = 2 * tq, q1 = 2 * tq + 1;
-    const bool k0ok = kb + g < nk, k1ok = kb + g + 8 < nk;
+    const int kp0 = kpos0 + kb + g, kp1 = kp0 + 8;
+    const bool k0ok = kb + g < nk && !(kp0 >= mk.x && kp0 < mk.y);
+    const bool k1ok = kb + g + 8 < nk && !(kp1 >= mk.x && kp1 < mk.y);
     sc[0] = (k0ok && q0 < NQ) ? sc[0] * scale : -INFINITY;
     sc[1] = (k0ok && q1 < NQ) ? sc[1] * scale : -INFINITY;
     sc[2] = (k1ok && q0 < NQ) ? sc[2] * scale : -INFINITY;
@@ -216,7 +219,9 @@ __global__ void __launch_bounds__(kAttnThreads) k_attn(AttnArgs a) {
         kbase = a.kc + off;
         vbase = a.vc + off;
     }
-    const int len = a.cross ? a.n_audio : a.pos[group] + 1;
+    const int len = a.cross ? a.n_audio : a.kv_len ? a.kv_len[group] : a.pos[group] + 1;
+    // a multi-token pass masks keys [lo, hi) of this query (the causal mask from key column 0)
+    const int2 mk = (!a.cross && a.mask) ? a.mask[group] : make_int2(0, 0);
     const int newest = a.cross ? -1 : len - 1;  // the row the previous kernel (QKV) writes
     // splits in use: one key tile each while the context is short (the grid is sized for the
     // longest context); with a single one, the other blocks have nothing to do
@@ -292,7 +297,7 @@ __global__ void __launch_bounds__(kAttnThreads) k_attn(AttnArgs a) {
     for (int ti = 0; ti < nt; ++ti) {
         const int nk = min(kAttnKeyTile, j1 - j0 - ti * kAttnKeyTile);
         const __half *sk = skv + (size_t)ti * kTileHalves, *sv = sk + kAttnKeyTile * kRowPad;
-        attn_tile<NQ>(sh, sk, sv, nk, of, tid, 0);
+        attn_tile<NQ>(sh, sk, sv, nk, of, tid, 0, j0 + ti * kAttnKeyTile, mk);
     }
     // add the warp shares (through the K/V tiles' shared memory, no longer needed)
     float *red = reinterpret_cast<float *>(skv);  // [kWarps][NQ][64]

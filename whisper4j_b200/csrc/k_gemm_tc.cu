@@ -30,14 +30,24 @@
 namespace w4j {
 
 constexpr int kGemmThreads = 512, kGemmWarps = kGemmThreads / 32;
+// Q8_0 weights: a raw stage holds the [128 x 64] int8 tile (TMA) and its 128 x 2 f16 scales (bulk
+// copy from the tiled scale layout); eight converter warps dequantise it into an A stage of two
+// swizzled f16 tiles, hi = f16(q * s) and lo = f16(q * s - hi), so the product keeps the
+// reference's exact f32 weight q * s (GgmlLoader.java:292-300)
+constexpr unsigned kRawBytes = kTileRows * kKB;                  // int8 tile: 8 KB
+constexpr unsigned kRawStage = kRawBytes + kTileRows * 2 * 2;    // + its scales: 8704 B
+constexpr unsigned kAStage = 2 * kStageBytes;                    // hi and lo f16 tiles: 32 KB
+constexpr int kConvWarps = 8;                                    // warps 8 .. 15
 
 struct GemmTcLaunch {
+    int mchunk;      // sequence rows per block (grid z walks the chunks of M > 128 rows)
     int KB;          // 64-wide k-blocks in K
     int ks;          // K splits (cluster size)
     int nkb_max;     // k-blocks of the largest split
     int n_stages;    // weight ring stages
     int rmax;        // most tile rows a split block owns: ceil(128 / ks)
     int recv_alias;  // 1: the partials land in the weight ring (free once every block's MMAs are done)
+    unsigned ring_off;  // weight ring (Q8_0: raw stages after the two dequantised A stages at 0)
     unsigned b_off, ln_off, bias_off, mi_off, stat_off, recv_off, bar_off;  // shared-memory layout (bytes)
 };
 
@@ -62,9 +72,36 @@ __device__ __forceinline__ void st_cluster_f32x2(unsigned addr, float x, float y
     asm volatile("st.shared::cluster.v2.f32 [%0], {%1, %2};" ::"r"(addr), "f"(x), "f"(y) : "memory");
 }
 
-template <int NU>
-__global__ void __launch_bounds__(kGemmThreads, 1) k_gemm_tc(GemvArgs a, const __grid_constant__ CUtensorMap tmap,
-                                                              GemmTcLaunch L) {
+// Rows [m0, m0 + n) of a projection: every per-sequence pointer advanced by m0 rows.
+__device__ __forceinline__ GemvArgs rows_of(const GemvArgs &g, int m0, int n) {
+    GemvArgs a = g;
+    const int K = g.W.K, N = g.W.N;
+    a.M = n;
+    if (a.act) a.act += (size_t)m0 * K;
+    if (a.tok) a.tok += m0;
+    if (a.pos) a.pos += m0;
+    if (a.pe_pos) a.pe_pos += m0;
+    if (a.seq_slot) a.seq_slot += m0;
+    if (a.active) a.active += m0;
+    if (a.x_out) a.x_out += (size_t)m0 * K;
+    a.y += (size_t)m0 * (a.out_mode == OUT_QKV ? N / 3 : N);
+    return a;
+}
+
+// BT: the B operand comes from a staged f16 hi / lo activation buffer (k_act_hilo) through TMA, one
+// [256 rows x 64] tile per ring stage beside the weight tile, instead of being built in shared memory
+// for the block's whole K range (more than 128 rows: NU = 128, f16 weights)
+template <int NU, int WT, bool BT>
+__global__ void __launch_bounds__(kGemmThreads, 1) k_gemm_tc(GemvArgs a_all, const __grid_constant__ CUtensorMap tmap,
+                                                              const __grid_constant__ CUtensorMap bmap, GemmTcLaunch L) {
+    static_assert(!BT || (NU == 128 && WT == WT_F16), "staged B: 128-row chunks of f16 projections");
+    constexpr bool kQ8 = WT == WT_Q8;
+    constexpr unsigned kBTile = 2u * NU * 128u;  // one k-block of B: hi and lo rows of 128 bytes
+    constexpr unsigned SB = kQ8 ? kRawStage : BT ? (unsigned)kStageBytes + kBTile : (unsigned)kStageBytes;
+    // grid z: chunks of at most 128 sequence rows; every chunk's blocks stream the same weight
+    // tiles at about the same time, so the chunks after the first mostly read them from L2
+    const int mc0 = blockIdx.z * L.mchunk;
+    const GemvArgs a = rows_of(a_all, mc0, min(L.mchunk, a_all.M - mc0));
     extern __shared__ __align__(1024) unsigned char smem_raw[];
     unsigned char *smem = smem_raw + ((1024u - (smem_u32(smem_raw) & 1023u)) & 1023u);
     const int N = a.W.N, K = a.W.K, M = a.M;
@@ -72,18 +109,21 @@ __global__ void __launch_bounds__(kGemmThreads, 1) k_gemm_tc(GemvArgs a, const _
     const int n0 = blockIdx.y * kTileRows;
     const int kb0 = (split * L.KB) / ks, kb1 = ((split + 1) * L.KB) / ks, nkb = kb1 - kb0;
     const int NS = L.n_stages;
-    unsigned char *ring = smem;
+    unsigned char *ring = smem + L.ring_off;
+    unsigned char *aring = smem;  // Q8_0: two dequantised A stages
     constexpr int NB = 2 * NU;             // B rows: hi, then lo parts of the NU slots
     unsigned char *bop = smem + L.b_off;  // [nkb][NB rows][128 B]
     float *ln_s = reinterpret_cast<float *>(smem + L.ln_off);      // gamma, beta of the K range
     float *bias_s = reinterpret_cast<float *>(smem + L.bias_off);  // [128]
-    int *mi_s = reinterpret_cast<int *>(smem + L.mi_off);          // [4][M] active, slot, pos, token
+    int *mi_s = reinterpret_cast<int *>(smem + L.mi_off);          // [5][M] active, slot, row, token, pe row
     float2 *stat_s = reinterpret_cast<float2 *>(smem + L.stat_off); // [M] LayerNorm mean, 1/std (split K)
     // split-K partials of the rows this block owns: [split][M][rmax], written by the cluster
     float *recv = reinterpret_cast<float *>(smem + (L.recv_alias ? 0u : L.recv_off));
     uint64_t *full = reinterpret_cast<uint64_t *>(smem + L.bar_off);
     uint64_t *empty = full + NS;
-    uint64_t *accf = empty + NS;
+    uint64_t *afull = empty + NS;  // Q8_0: A stage converted (one arrival per converter warp)
+    uint64_t *aempty = afull + 2;  // Q8_0: A stage read by the MMAs (commit)
+    uint64_t *accf = aempty + 2;
     uint32_t *tslot = reinterpret_cast<uint32_t *>(accf + 1);
     volatile int *fail = reinterpret_cast<volatile int *>(tslot + 1);
     volatile int *issued = fail + 1;  // weight tiles whose copy has been started
@@ -92,19 +132,40 @@ __global__ void __launch_bounds__(kGemmThreads, 1) k_gemm_tc(GemvArgs a, const _
     const int kr = nkb * kKB;  // K range of this block: [kb0 * 64, kb0 * 64 + kr)
 
     // ---- independent of the previous kernel: barriers, TMEM, first weight tiles, parameters ----
+    // copy of weight k-block i of this block's range into ring stage i % NS
+    auto issue = [&](int i) {
+        const int st = i % NS;
+        unsigned char *dst = ring + (size_t)st * SB;
+        if (kQ8) {
+            mbar_expect_tx(full + st, kRawStage);
+            tma_load_2d(dst, &tmap, (kb0 + i) * kKB, n0, full + st);
+            bulk_g2s(dst + kRawBytes, a.W.st + ((size_t)blockIdx.y * L.KB + kb0 + i) * (kTileRows * 2),
+                     kRawStage - kRawBytes, full + st);
+        } else if (BT) {
+            mbar_expect_tx(full + st, kStageBytes + kBTile);
+            tma_load_2d(dst, &tmap, (kb0 + i) * kKB, n0, full + st);
+            tma_load_2d(dst + kStageBytes, &bmap, (kb0 + i) * kKB, (int)blockIdx.z * 2 * NU, full + st);
+        } else {
+            mbar_expect_tx(full + st, kStageBytes);
+            tma_load_2d(dst, &tmap, (kb0 + i) * kKB, n0, full + st);
+        }
+    };
     if (tid == 0) {
         for (int i = 0; i < NS; ++i) {
             mbar_init(full + i, 1);
-            mbar_init(empty + i, 1);
+            mbar_init(empty + i, kQ8 ? kConvWarps : 1);  // Q8_0: released by the converters
+        }
+        for (int i = 0; i < 2; ++i) {
+            mbar_init(afull + i, kConvWarps);
+            mbar_init(aempty + i, 1);
         }
         mbar_init(accf, 1);
         *fail = 0;
         fence_mbar_init();
-        for (int i = 0; i < NS && i < nkb; ++i) {
-            mbar_expect_tx(full + i, kStageBytes);
-            tma_load_2d(ring + (size_t)i * kStageBytes, &tmap, (kb0 + i) * kKB, n0, full + i);
-        }
-        *issued = NS < nkb ? NS : nkb;
+        // staged B tiles are written by the previous kernel: those stages start after the wait
+        if (!BT)
+            for (int i = 0; i < NS && i < nkb; ++i) issue(i);
+        *issued = BT ? 0 : (NS < nkb ? NS : nkb);
     }
     if (warp == 1) {
         tmem_alloc(tslot, kCols);
@@ -114,7 +175,7 @@ __global__ void __launch_bounds__(kGemmThreads, 1) k_gemm_tc(GemvArgs a, const _
     // liveness, cache slots, positions and tokens (written by the host or an earlier graph
     // launch): every load of a thread is issued before the first store, so they overlap
     {
-        const int nln = a.in_mode != IN_ACT ? 2 * kr : 0;
+        const int nln = (a.in_mode != IN_ACT && !BT) ? 2 * kr : 0;
         float lnv[5];
 #pragma unroll
         for (int j = 0; j < 5; ++j) {
@@ -122,12 +183,15 @@ __global__ void __launch_bounds__(kGemmThreads, 1) k_gemm_tc(GemvArgs a, const _
             lnv[j] = i < nln ? (i < kr ? a.ln_g[kb0 * kKB + i] : a.ln_b[kb0 * kKB + i - kr]) : 0.f;
         }
         const float bv = (tid < kTileRows && a.bias && n0 + tid < N) ? a.bias[n0 + tid] : 0.f;
-        int mv0 = 1, mv1 = 0, mv2 = 0, mv3 = 0;
+        int mv0 = 1, mv1 = 0, mv2 = 0, mv3 = 0, mv4 = 0;
         if (tid < M) {
             if (a.active) mv0 = a.active[tid];
             if (a.out_mode == OUT_QKV) mv1 = a.seq_slot[tid];
-            if (a.out_mode == OUT_QKV || a.in_mode == IN_EMBED_LN) mv2 = a.pos[tid];
-            if (a.in_mode == IN_EMBED_LN) mv3 = a.tok[tid];
+            if (a.out_mode == OUT_QKV) mv2 = a.pos[tid];
+            if (a.in_mode == IN_EMBED_LN) {
+                mv3 = a.tok[tid];
+                mv4 = pe_row(a, tid);
+            }
         }
 #pragma unroll
         for (int j = 0; j < 5; ++j) {
@@ -140,9 +204,10 @@ __global__ void __launch_bounds__(kGemmThreads, 1) k_gemm_tc(GemvArgs a, const _
             mi_s[M + tid] = mv1;
             mi_s[2 * M + tid] = mv2;
             mi_s[3 * M + tid] = mv3;
+            mi_s[4 * M + tid] = mv4;
         }
     }
-    for (int i = tid; i < 2 * (NU - M) * nkb * 8; i += blockDim.x) {  // slots M .. NU are zero
+    for (int i = tid; !BT && i < 2 * (NU - M) * nkb * 8; i += blockDim.x) {  // slots M .. NU are zero
         const int j = i / (nkb * 8), c = i % (nkb * 8);
         const int m = j < NU - M ? M + j : NU + M + (j - (NU - M));
         const int kb = c / 8, cc = c % 8;
@@ -155,8 +220,13 @@ __global__ void __launch_bounds__(kGemmThreads, 1) k_gemm_tc(GemvArgs a, const _
     bool started = ks == 1;
     pdl_trigger();
     pdl_wait();
+    if (BT && tid == 0) {
+        for (int i = 0; i < NS && i < nkb; ++i) issue(i);
+        *issued = NS < nkb ? NS : nkb;
+    }
     __syncthreads();
 
+    if constexpr (!BT) {
     // ---- B operand: the rows' K range as f16 hi / lo pairs, K-major, 128-byte swizzle ----
     // 4 consecutive elements k .. k+3 of slot m (k inside the K range) go to their 8-byte half of
     // the 16-byte chunk of row m (hi) and of row NU + m (lo)
@@ -190,7 +260,7 @@ __global__ void __launch_bounds__(kGemmThreads, 1) k_gemm_tc(GemvArgs a, const _
                 for (int j = 0; j < kLnF4; ++j) v[j] = j < nf4 ? src[lane + 32 * j] : make_float4(0.f, 0.f, 0.f, 0.f);
             } else {  // x = E[tok] + P[pos] (WhisperDecoder.java:66-80); the first tile's owner keeps it
                 const uint2 *e = reinterpret_cast<const uint2 *>(a.E.h + (size_t)mi_s[3 * M + m] * K);
-                const float4 *pe = reinterpret_cast<const float4 *>(a.pos_emb + (size_t)mi_s[2 * M + m] * K);
+                const float4 *pe = reinterpret_cast<const float4 *>(a.pos_emb + (size_t)mi_s[4 * M + m] * K);
                 uint2 eu[kLnF4];
 #pragma unroll
                 for (int j = 0; j < kLnF4; ++j) {
@@ -240,7 +310,7 @@ __global__ void __launch_bounds__(kGemmThreads, 1) k_gemm_tc(GemvArgs a, const _
                         const uint2 eu =
                             reinterpret_cast<const uint2 *>(a.E.h + (size_t)mi_s[3 * M + m] * K + kb0 * kKB)[c4];
                         const float4 p =
-                            reinterpret_cast<const float4 *>(a.pos_emb + (size_t)mi_s[2 * M + m] * K + kb0 * kKB)[c4];
+                            reinterpret_cast<const float4 *>(a.pos_emb + (size_t)mi_s[4 * M + m] * K + kb0 * kKB)[c4];
                         const float2 lo = __half22float2(*reinterpret_cast<const __half2 *>(&eu.x));
                         const float2 hi = __half22float2(*reinterpret_cast<const __half2 *>(&eu.y));
                         v[j] = make_float4(lo.x + p.x, lo.y + p.y, hi.x + p.z, hi.y + p.w);
@@ -329,7 +399,7 @@ __global__ void __launch_bounds__(kGemmThreads, 1) k_gemm_tc(GemvArgs a, const _
             }
         } else {  // x = E[tok] + P[pos] (WhisperDecoder.java:66-80), kept in x_out by one block
             for (int m = warp; m < M; m += kGemmWarps) {
-                const int tok = mi_s[3 * M + m], pos = mi_s[2 * M + m];
+                const int tok = mi_s[3 * M + m], pos = mi_s[4 * M + m];
                 const uint2 *e = reinterpret_cast<const uint2 *>(a.E.h + (size_t)tok * K);
                 const float4 *pe = reinterpret_cast<const float4 *>(a.pos_emb + (size_t)pos * K);
                 float4 v[kLnF4];
@@ -350,6 +420,7 @@ __global__ void __launch_bounds__(kGemmThreads, 1) k_gemm_tc(GemvArgs a, const _
                 ln_put(m, v);
             }
         }
+    }
     }
     fence_proxy_async();  // generic-proxy writes of B visible to the tensor core
     tc_fence_before();
@@ -398,29 +469,84 @@ __global__ void __launch_bounds__(kGemmThreads, 1) k_gemm_tc(GemvArgs a, const _
                 *fail = 1;
                 break;
             }
-            mbar_expect_tx(full + st, kStageBytes);
-            tma_load_2d(ring + (size_t)st * kStageBytes, &tmap, (kb0 + i) * kKB, n0, full + st);
+            issue(i);
             *issued = i + 1;
         }
     } else if (warp == 1 && lane == 0) {
         // ---- MMA issuer ----
-        const uint32_t ring_a = smem_u32(ring), b_a = smem_u32(bop);
+        const uint32_t ring_a = smem_u32(ring), aring_a = smem_u32(aring), b_a = smem_u32(bop);
         for (int i = 0; i < nkb && !*fail; ++i) {
             const int st = i % NS;
-            if (!mbar_wait(full + st, (unsigned)((i / NS) & 1), a.err)) {
+            if (!mbar_wait(kQ8 ? afull + (i & 1) : full + st, (unsigned)((kQ8 ? i >> 1 : i / NS) & 1), a.err)) {
                 *fail = 1;
                 break;
             }
             tc_fence_after();
+            if (kQ8) {
+                // W = hi + lo: both dequantised tiles against the same B columns, one accumulator
+                const uint32_t ahi = aring_a + (uint32_t)(i & 1) * kAStage, alo = ahi + kStageBytes;
 #pragma unroll
-            for (int j = 0; j < kKB / 16; ++j) {
-                const uint64_t ad = sw128_desc(ring_a + (uint32_t)st * kStageBytes + j * 32);
-                const uint64_t bd = sw128_desc(b_a + (uint32_t)i * NB * 128 + j * 32);
-                umma_f16(taddr, ad, bd, idesc, (i | j) != 0);
+                for (int j = 0; j < kKB / 16; ++j) {
+                    const uint64_t bd = sw128_desc(b_a + (uint32_t)i * NB * 128 + j * 32);
+                    umma_f16(taddr, sw128_desc(ahi + j * 32), bd, idesc, (i | j) != 0);
+                    umma_f16(taddr, sw128_desc(alo + j * 32), bd, idesc, 1u);
+                }
+                umma_commit(aempty + (i & 1));  // the A stage is free once these MMAs have read it
+            } else {
+#pragma unroll
+                for (int j = 0; j < kKB / 16; ++j) {
+                    const uint32_t sa = ring_a + (uint32_t)st * SB;
+                    const uint64_t ad = sw128_desc(sa + j * 32);
+                    const uint64_t bd = BT ? sw128_desc(sa + kStageBytes + j * 32)
+                                           : sw128_desc(b_a + (uint32_t)i * NB * 128 + j * 32);
+                    umma_f16(taddr, ad, bd, idesc, (i | j) != 0);
+                }
+                umma_commit(empty + st);  // the stage is free once these MMAs have read it
             }
-            umma_commit(empty + st);  // the stage is free once these MMAs have read it
         }
         umma_commit(accf);  // the accumulator is complete (or nothing was issued)
+    } else if (kQ8 && warp >= 16 - kConvWarps) {
+        // ---- Q8_0 converters: raw stage i -> A stage i % 2 (thread: row r, scale group h) ----
+        const int ct = tid - (16 - kConvWarps) * 32, r = ct >> 1, h = ct & 1;
+        for (int i = 0; i < nkb && !*fail; ++i) {
+            const int st = i % NS;
+            if (!mbar_wait(full + st, (unsigned)((i / NS) & 1), a.err) ||
+                (i >= 2 && !mbar_wait(aempty + (i & 1), (unsigned)(((i >> 1) - 1) & 1), a.err))) {
+                *fail = 1;
+                break;
+            }
+            const unsigned char *raw = ring + (size_t)st * SB;
+            const uint4 q0 = *reinterpret_cast<const uint4 *>(raw + r * kKB + h * 32);
+            const uint4 q1 = *reinterpret_cast<const uint4 *>(raw + r * kKB + h * 32 + 16);
+            const float sc = __half2float(reinterpret_cast<const __half *>(raw + kRawBytes)[r * 2 + h]);
+            unsigned char *ahi = aring + (size_t)(i & 1) * kAStage, *alo = ahi + kStageBytes;
+            const uint32_t qw[8] = {q0.x, q0.y, q0.z, q0.w, q1.x, q1.y, q1.z, q1.w};
+#pragma unroll
+            for (int c = 0; c < 4; ++c) {  // 8 weights per 16-byte chunk: chunk 4 h + c of row r
+                uint32_t hv[4], lv[4];
+#pragma unroll
+                for (int p = 0; p < 4; ++p) {
+                    const uint32_t wd = qw[2 * c + (p >> 1)];
+                    const int b0 = (p & 1) * 16;
+                    const float w0 = (float)(int8_t)((wd >> b0) & 0xffu) * sc;
+                    const float w1 = (float)(int8_t)((wd >> (b0 + 8)) & 0xffu) * sc;
+                    const __half2 hh = __floats2half2_rn(w0, w1);
+                    const float2 hf = __half22float2(hh);
+                    const __half2 ll = __floats2half2_rn(w0 - hf.x, w1 - hf.y);
+                    hv[p] = *reinterpret_cast<const uint32_t *>(&hh);
+                    lv[p] = *reinterpret_cast<const uint32_t *>(&ll);
+                }
+                const int off = r * 128 + (((4 * h + c) ^ (r & 7)) * 16);
+                *reinterpret_cast<uint4 *>(ahi + off) = make_uint4(hv[0], hv[1], hv[2], hv[3]);
+                *reinterpret_cast<uint4 *>(alo + off) = make_uint4(lv[0], lv[1], lv[2], lv[3]);
+            }
+            fence_proxy_async();  // A visible to the tensor core; raw reads done before the refill
+            __syncwarp();
+            if (lane == 0) {
+                mbar_arrive(empty + st);
+                mbar_arrive(afull + (i & 1));
+            }
+        }
     }
     __syncthreads();
     // ---- epilogue warps 8 .. 15: warp w reads TMEM lanes 32 (w % 4) .., column group (w - 8) / 4 ----
@@ -505,40 +631,55 @@ static int nu_for(int M) { return M <= 16 ? 16 : M <= 32 ? 32 : M <= 64 ? 64 : 1
 // wave of clusters.
 static int g_max_clusters[9];
 
-static bool plan_gemm_tc(const GemvArgs &a, int sms, int &nu, GemmTcLaunch &L, int &tiles) {
-    const int M = a.M, N = a.W.N, K = a.W.K;
-    if (M < 16 || M > 128 || a.W.type != WT_F16 || K % kKB != 0 || N < 1) return false;
-    if (a.in_mode != IN_ACT && (K % 128 != 0 || K > 1280)) return false;
-    if (a.in_mode == IN_EMBED_LN && a.E.type != WT_F16) return false;
+static bool plan_gemm_tc(const GemvArgs &a, int sms, int &nu, GemmTcLaunch &L, int &tiles, int &chunks, bool &bt) {
+    const int N = a.W.N, K = a.W.K;
+    const bool q8 = a.W.type == WT_Q8;
+    if (a.M < 16 || K % kKB != 0 || N < 1) return false;
+    if (!(a.W.type == WT_F16 || (q8 && a.W.st && N % kTileRows == 0))) return false;
+    // more than 128 rows (f16): the activations come staged as f16 hi / lo rows (k_act_hilo)
+    bt = !q8 && a.M > 128;
+    if (q8 && a.M > 128) return false;
+    if (!bt && a.in_mode != IN_ACT && (K % 128 != 0 || K > 1280)) return false;
+    if (!bt && a.in_mode == IN_EMBED_LN && a.E.type != WT_F16) return false;
+    chunks = (a.M + 127) / 128;
+    L.mchunk = (a.M + chunks - 1) / chunks;
+    const int M = L.mchunk;  // rows of one block
     nu = nu_for(M);
     tiles = (N + kTileRows - 1) / kTileRows;
     L.KB = K / kKB;
-    int ks = sms / tiles;
+    int ks = sms / (tiles * chunks);
     ks = ks < 1 ? 1 : ks > 8 ? 8 : ks;
     if (ks > L.KB) ks = L.KB;
-    while (ks > 1 && g_max_clusters[ks] > 0 && g_max_clusters[ks] < tiles) --ks;
+    while (ks > 1 && g_max_clusters[ks] > 0 && g_max_clusters[ks] < tiles * chunks) --ks;
     L.ks = ks;
     L.nkb_max = (L.KB + ks - 1) / ks;
-    const size_t bbytes = (size_t)L.nkb_max * 2 * nu * 128;  // hi and lo rows
-    const size_t lnbytes = a.in_mode == IN_ACT ? 0 : (size_t)2 * L.nkb_max * kKB * 4;
-    const size_t mibytes = ((size_t)4 * M * 4 + 15) & ~(size_t)15;
+    const size_t bbytes = bt ? 0 : (size_t)L.nkb_max * 2 * nu * 128;  // hi and lo rows
+    const size_t lnbytes = (a.in_mode == IN_ACT || bt) ? 0 : (size_t)2 * L.nkb_max * kKB * 4;
+    const size_t mibytes = ((size_t)5 * M * 4 + 15) & ~(size_t)15;
     L.rmax = (kTileRows + ks - 1) / ks;
     const size_t recvbytes = ks > 1 ? (((size_t)ks * M * L.rmax * 4 + 15) & ~(size_t)15) : 0;
     const size_t statbytes = (size_t)M * 8;  // 8-byte multiple: keeps recv / barriers aligned
-    const size_t fixed = bbytes + lnbytes + 512 + mibytes + statbytes + 256;
+    const size_t fixed = bbytes + lnbytes + 512 + mibytes + statbytes + 256 + (q8 ? 1024 : 0);
     const size_t budget = 220 * 1024;
+    // weight ring: f16 tiles straight from TMA; Q8_0 raw int8 + scale stages after the two
+    // dequantised A stages (the A stages come first, 1024-aligned for the swizzle)
+    const size_t sb = q8 ? kRawStage : bt ? (size_t)kStageBytes + 2 * 128 * 128 : (size_t)kStageBytes;
+    const size_t front = q8 ? 2 * (size_t)kAStage : 0;
     // the partials get their own buffer when it fits beside two stages, else they reuse the ring
-    L.recv_alias = fixed + recvbytes + 2 * (size_t)kStageBytes > budget;
+    L.recv_alias = fixed + front + recvbytes + 2 * sb > budget;
     const size_t own = L.recv_alias ? 0 : recvbytes;
-    int ns_need = L.recv_alias ? (int)((recvbytes + kStageBytes - 1) / kStageBytes) : 2;
+    int ns_need = 2;
+    if (L.recv_alias && recvbytes > front) ns_need = (int)((recvbytes - front + sb - 1) / sb);
     if (ns_need < 2) ns_need = 2;
-    if (fixed + own + (size_t)ns_need * kStageBytes > budget) return false;
-    int ns = (int)((budget - fixed - own) / kStageBytes);  // as many stages as fit, up to the k-blocks
-    if (ns > 8) ns = 8;
+    if (fixed + front + own + (size_t)ns_need * sb > budget) return false;
+    int ns = (int)((budget - fixed - front - own) / sb);  // as many stages as fit, up to the k-blocks
+    if (ns > (q8 ? 12 : 8)) ns = q8 ? 12 : 8;
     if (ns > L.nkb_max) ns = L.nkb_max;
     if (ns < ns_need) ns = ns_need;
     L.n_stages = ns;
-    L.b_off = (unsigned)(ns * kStageBytes);  // 1024-aligned; 2 nu * 128 B per k-block keeps it so
+    L.ring_off = (unsigned)front;
+    // B after the ring, 1024-aligned (2 nu * 128 B per k-block keeps the k-blocks so)
+    L.b_off = (unsigned)((front + ns * sb + 1023) & ~(size_t)1023);
     L.ln_off = L.b_off + (unsigned)bbytes;
     L.bias_off = L.ln_off + (unsigned)lnbytes;
     L.mi_off = L.bias_off + 512;
@@ -553,7 +694,7 @@ static bool plan_gemm_tc(const GemvArgs &a, int sms, int &nu, GemmTcLaunch &L, i
 // cluster barrier, so no more blocks may be resident on an SM than its columns serve: from
 // 128 columns on, the request is raised until 228 KB of shared memory per SM admits no more.
 static size_t gemm_tc_smem(const GemmTcLaunch &L, int nu) {
-    size_t bytes = (size_t)L.bar_off + (2 * L.n_stages + 1) * 8 + 16 + 1024;
+    size_t bytes = (size_t)L.bar_off + (2 * L.n_stages + 5) * 8 + 16 + 1024;
     const int cols = 2 * nu;
     if (cols >= 128) {
         const size_t per_sm = 228 * 1024, fit = 512 / cols;
@@ -563,11 +704,11 @@ static size_t gemm_tc_smem(const GemmTcLaunch &L, int nu) {
     return bytes;
 }
 
-template <int NU>
-static cudaError_t launch_gemm_tc_t(const GemvArgs &a, const CUtensorMap &map, const GemmTcLaunch &L, int tiles,
-                                    cudaStream_t s, bool pdl) {
+template <int NU, int WT, bool BT>
+static cudaError_t launch_gemm_tc_t(const GemvArgs &a, const CUtensorMap &map, const CUtensorMap &bmap,
+                                    const GemmTcLaunch &L, int tiles, int chunks, cudaStream_t s, bool pdl) {
     cudaLaunchConfig_t cfg = {};
-    cfg.gridDim = dim3(L.ks, tiles);
+    cfg.gridDim = dim3(L.ks, tiles, chunks);
     cfg.blockDim = dim3(kGemmThreads);
     cfg.dynamicSmemBytes = gemm_tc_smem(L, NU);
     cfg.stream = s;
@@ -587,14 +728,22 @@ static cudaError_t launch_gemm_tc_t(const GemvArgs &a, const CUtensorMap &map, c
     }
     cfg.attrs = attr;
     cfg.numAttrs = na;
-    return cudaLaunchKernelEx(&cfg, k_gemm_tc<NU>, a, map, L);
+    return cudaLaunchKernelEx(&cfg, k_gemm_tc<NU, WT, BT>, a, map, bmap, L);
+}
+
+template <int WT>
+static cudaError_t prep_wt() {
+    cudaError_t e = allow_dynamic_smem(k_gemm_tc<16, WT, false>);
+    if (e == cudaSuccess) e = allow_dynamic_smem(k_gemm_tc<32, WT, false>);
+    if (e == cudaSuccess) e = allow_dynamic_smem(k_gemm_tc<64, WT, false>);
+    if (e == cudaSuccess) e = allow_dynamic_smem(k_gemm_tc<128, WT, false>);
+    return e;
 }
 
 cudaError_t gemm_tc_prepare() {
-    cudaError_t e = allow_dynamic_smem(k_gemm_tc<16>);
-    if (e == cudaSuccess) e = allow_dynamic_smem(k_gemm_tc<32>);
-    if (e == cudaSuccess) e = allow_dynamic_smem(k_gemm_tc<64>);
-    if (e == cudaSuccess) e = allow_dynamic_smem(k_gemm_tc<128>);
+    cudaError_t e = prep_wt<WT_F16>();
+    if (e == cudaSuccess) e = prep_wt<WT_Q8>();
+    if (e == cudaSuccess) e = allow_dynamic_smem(k_gemm_tc<128, WT_F16, true>);
     if (e != cudaSuccess) return e;
     // one block per SM (the register file), so the count does not depend on shared memory
     for (int ks = 2; ks <= 8; ++ks) {
@@ -610,24 +759,144 @@ cudaError_t gemm_tc_prepare() {
         cfg.attrs = &attr;
         cfg.numAttrs = 1;
         int n = 0;
-        if (cudaOccupancyMaxActiveClusters(&n, k_gemm_tc<32>, &cfg) == cudaSuccess) g_max_clusters[ks] = n;
+        if (cudaOccupancyMaxActiveClusters(&n, k_gemm_tc<32, WT_F16, false>, &cfg) == cudaSuccess) g_max_clusters[ks] = n;
         else cudaGetLastError();
     }
     return cudaSuccess;
 }
 
 // cudaErrorNotSupported when the projection is outside the tensor-core kernel's range.
-cudaError_t launch_gemm_tc(const GemvArgs &a, const void *tmap, int sms, cudaStream_t s, bool pdl) {
-    int nu, tiles;
+bool gemm_tc_staged(const GemvArgs &a) { return a.W.type == WT_F16 && a.M > 128; }
+
+bool gemm_tc_supported(const GemvArgs &a, int sms) {
+    int nu, tiles, chunks;
+    bool bt;
     GemmTcLaunch L;
-    if (!tmap || !plan_gemm_tc(a, sms, nu, L, tiles)) return cudaErrorNotSupported;
+    return plan_gemm_tc(a, sms, nu, L, tiles, chunks, bt);
+}
+
+cudaError_t launch_gemm_tc(const GemvArgs &a, const void *tmap, const void *bmap, int sms, cudaStream_t s, bool pdl) {
+    int nu, tiles, chunks;
+    bool bt = false;
+    GemmTcLaunch L;
+    if (!tmap || !plan_gemm_tc(a, sms, nu, L, tiles, chunks, bt) || (bt && !bmap)) return cudaErrorNotSupported;
     const CUtensorMap &map = *reinterpret_cast<const CUtensorMap *>(tmap);
+    const CUtensorMap &bm = bt ? *reinterpret_cast<const CUtensorMap *>(bmap) : map;
+    if (bt) return launch_gemm_tc_t<128, WT_F16, true>(a, map, bm, L, tiles, chunks, s, pdl);
+    if (a.W.type == WT_Q8) switch (nu) {
+            case 16: return launch_gemm_tc_t<16, WT_Q8, false>(a, map, bm, L, tiles, chunks, s, pdl);
+            case 32: return launch_gemm_tc_t<32, WT_Q8, false>(a, map, bm, L, tiles, chunks, s, pdl);
+            case 64: return launch_gemm_tc_t<64, WT_Q8, false>(a, map, bm, L, tiles, chunks, s, pdl);
+            default: return launch_gemm_tc_t<128, WT_Q8, false>(a, map, bm, L, tiles, chunks, s, pdl);
+        }
     switch (nu) {
-        case 16: return launch_gemm_tc_t<16>(a, map, L, tiles, s, pdl);
-        case 32: return launch_gemm_tc_t<32>(a, map, L, tiles, s, pdl);
-        case 64: return launch_gemm_tc_t<64>(a, map, L, tiles, s, pdl);
-        default: return launch_gemm_tc_t<128>(a, map, L, tiles, s, pdl);
+        case 16: return launch_gemm_tc_t<16, WT_F16, false>(a, map, bm, L, tiles, chunks, s, pdl);
+        case 32: return launch_gemm_tc_t<32, WT_F16, false>(a, map, bm, L, tiles, chunks, s, pdl);
+        case 64: return launch_gemm_tc_t<64, WT_F16, false>(a, map, bm, L, tiles, chunks, s, pdl);
+        default: return launch_gemm_tc_t<128, WT_F16, false>(a, map, bm, L, tiles, chunks, s, pdl);
     }
+}
+
+// ---------------------------------------------------------------------------
+// k_act_hilo: the activations of a projection with more than 128 rows, once, as the UMMA B
+// operand's f16 hi / lo rows: out[(z * 256 + r) * K + k] = hi, out[(z * 256 + 128 + r) * K + k] = lo
+// for sequence m = z * mchunk + r (rows past the chunk's sequences zero), after the input mode
+// (plain, LayerNorm of x, or token + positional embedding then LayerNorm, kept in x_out).
+// One warp per (chunk, row); LayerNorm as Tensor.java:592-619 (two-pass, eps 1e-5).
+// ---------------------------------------------------------------------------
+__global__ void __launch_bounds__(256) k_act_hilo(GemvArgs a, int mchunk, int chunks, __half *out) {
+    const int K = a.W.K;
+    const int gw = (int)((blockIdx.x * blockDim.x + threadIdx.x) >> 5), lane = threadIdx.x & 31;
+    pdl_trigger();
+    pdl_wait();
+    if (gw >= chunks * 128) return;
+    const int z = gw >> 7, r = gw & 127, m = z * mchunk + r;
+    __half *hi = out + ((size_t)z * 256 + r) * K, *lo = hi + (size_t)128 * K;
+    const bool live = r < mchunk && m < a.M;
+    auto put = [&](int k, float4 v) {
+        const __half2 h0 = __floats2half2_rn(v.x, v.y), h1 = __floats2half2_rn(v.z, v.w);
+        const float2 f0 = __half22float2(h0), f1 = __half22float2(h1);
+        const __half2 l0 = __floats2half2_rn(v.x - f0.x, v.y - f0.y), l1 = __floats2half2_rn(v.z - f1.x, v.w - f1.y);
+        *reinterpret_cast<uint2 *>(hi + k) =
+            make_uint2(*reinterpret_cast<const uint32_t *>(&h0), *reinterpret_cast<const uint32_t *>(&h1));
+        *reinterpret_cast<uint2 *>(lo + k) =
+            make_uint2(*reinterpret_cast<const uint32_t *>(&l0), *reinterpret_cast<const uint32_t *>(&l1));
+    };
+    if (!live) {
+        for (int k = 4 * lane; k < K; k += 128) put(k, make_float4(0.f, 0.f, 0.f, 0.f));
+        return;
+    }
+    if (a.in_mode == IN_ACT) {
+        const float4 *src = reinterpret_cast<const float4 *>(a.act + (size_t)m * K);
+        for (int c = lane; c < K / 4; c += 32) put(4 * c, src[c]);
+        return;
+    }
+    // LayerNorm inputs: K <= 1280, a multiple of 128 (the row in registers)
+    constexpr int kLnF4 = 10;
+    const int nf4 = K / 128;
+    float4 v[kLnF4];
+    if (a.in_mode == IN_LN) {
+        const float4 *src = reinterpret_cast<const float4 *>(a.act + (size_t)m * K);
+#pragma unroll
+        for (int j = 0; j < kLnF4; ++j) v[j] = j < nf4 ? src[lane + 32 * j] : make_float4(0.f, 0.f, 0.f, 0.f);
+    } else {  // x = E[tok] + P[pos] (WhisperDecoder.java:66-80), kept in x_out
+        const uint2 *e = reinterpret_cast<const uint2 *>(a.E.h + (size_t)a.tok[m] * K);
+        const float4 *pe = reinterpret_cast<const float4 *>(a.pos_emb + (size_t)pe_row(a, m) * K);
+#pragma unroll
+        for (int j = 0; j < kLnF4; ++j) {
+            if (j < nf4) {
+                const uint2 eu = e[lane + 32 * j];
+                const float4 p = pe[lane + 32 * j];
+                const float2 l2 = __half22float2(*reinterpret_cast<const __half2 *>(&eu.x));
+                const float2 h2 = __half22float2(*reinterpret_cast<const __half2 *>(&eu.y));
+                v[j] = make_float4(l2.x + p.x, l2.y + p.y, h2.x + p.z, h2.y + p.w);
+                if (a.x_out) reinterpret_cast<float4 *>(a.x_out)[(size_t)m * (K / 4) + lane + 32 * j] = v[j];
+            } else {
+                v[j] = make_float4(0.f, 0.f, 0.f, 0.f);
+            }
+        }
+    }
+    float sm = 0.f;
+#pragma unroll
+    for (int j = 0; j < kLnF4; ++j)
+        if (j < nf4) sm += (v[j].x + v[j].y) + (v[j].z + v[j].w);
+    const float mean = warp_sum(sm) / (float)K;
+    float v2 = 0.f;
+#pragma unroll
+    for (int j = 0; j < kLnF4; ++j)
+        if (j < nf4) {
+            const float dx = v[j].x - mean, dy = v[j].y - mean, dz = v[j].z - mean, dw = v[j].w - mean;
+            v2 += (dx * dx + dy * dy) + (dz * dz + dw * dw);
+        }
+    const float inv_std = 1.0f / sqrtf(warp_sum(v2) / (float)K + 1e-5f);
+#pragma unroll
+    for (int j = 0; j < kLnF4; ++j)
+        if (j < nf4) {
+            const int k = 4 * (lane + 32 * j);
+            const float4 g = *reinterpret_cast<const float4 *>(a.ln_g + k);
+            const float4 b = *reinterpret_cast<const float4 *>(a.ln_b + k);
+            put(k, make_float4((v[j].x - mean) * inv_std * g.x + b.x, (v[j].y - mean) * inv_std * g.y + b.y,
+                               (v[j].z - mean) * inv_std * g.z + b.z, (v[j].w - mean) * inv_std * g.w + b.w));
+        }
+}
+
+// Rows of the staged activation buffer for M sequences: chunks * 256.
+int act_hilo_rows(int M) { return ((M + 127) / 128) * 256; }
+
+cudaError_t launch_act_hilo(const GemvArgs &a, __half *out, cudaStream_t s, bool pdl) {
+    const int K = a.W.K;
+    if (K % 4 != 0 || (a.in_mode != IN_ACT && (K % 128 != 0 || K > 1280))) return cudaErrorNotSupported;
+    const int chunks = (a.M + 127) / 128, mchunk = (a.M + chunks - 1) / chunks;
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = dim3((unsigned)(chunks * 128 * 32 + 255) / 256);
+    cfg.blockDim = dim3(256);
+    cfg.stream = s;
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[0].val.programmaticStreamSerializationAllowed = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = pdl ? 1 : 0;
+    return cudaLaunchKernelEx(&cfg, k_act_hilo, a, mchunk, chunks, out);
 }
 
 }  // namespace w4j

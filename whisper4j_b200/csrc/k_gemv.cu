@@ -106,7 +106,7 @@ __device__ void load_activations(const GemvArgs &a, int m0, int K, float *act_s,
 #pragma unroll
                 for (int j = 0; j < kLnF4; ++j) v[j] = j < nf4 ? src[lane + 32 * j] : make_float4(0.f, 0.f, 0.f, 0.f);
             } else {  // x = E[tok] + P[pos] (WhisperDecoder.java:66-80), kept in x_out by block 0
-                const int tok = tok_s ? tok_s[m] : a.tok[m], pos = pos_s ? pos_s[m] : a.pos[m];
+                const int tok = tok_s ? tok_s[m] : a.tok[m], pos = pos_s ? pos_s[m] : pe_row(a, m);
                 const uint2 *e = reinterpret_cast<const uint2 *>(a.E.h + (size_t)tok * K);
                 const float4 *pe = reinterpret_cast<const float4 *>(a.pos_emb + (size_t)pos * K);
                 uint2 eu[kLnF4];
@@ -163,7 +163,7 @@ __device__ void load_activations(const GemvArgs &a, int m0, int K, float *act_s,
                 const int m = m0 + mm;
                 e[j] = p[j] = make_float4(0.f, 0.f, 0.f, 0.f);
                 if (i < total && m < a.M) {
-                    const int tok = tok_s ? tok_s[m] : a.tok[m], pos = pos_s ? pos_s[m] : a.pos[m];
+                    const int tok = tok_s ? tok_s[m] : a.tok[m], pos = pos_s ? pos_s[m] : pe_row(a, m);
                     p[j] = *reinterpret_cast<const float4 *>(a.pos_emb + (size_t)pos * K + k);
                     if (f16) {
                         const uint2 u = *reinterpret_cast<const uint2 *>(a.E.h + (size_t)tok * K + k);
@@ -380,8 +380,8 @@ __global__ void __launch_bounds__(gemv_threads(WT)) k_gemv(GemvArgs a, GemvLaunc
     // epilogue operands: bias of the block's rows, per-sequence liveness / cache slot / position /
     // token, and (residual epilogue) the residual values of the pass
     float *bias_s = reinterpret_cast<float *>(bar + 2);                        // [rows_per_block]
-    int *mi_s = reinterpret_cast<int *>(bias_s + L.rows_per_block);           // [4][M]
-    float *res_s = reinterpret_cast<float *>(mi_s + 4 * (size_t)a.M);         // [MT][rows_per_block]
+    int *mi_s = reinterpret_cast<int *>(bias_s + L.rows_per_block);           // [5][M]
+    float *res_s = reinterpret_cast<float *>(mi_s + 5 * (size_t)a.M);         // [MT][rows_per_block]
     const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
     const int row_bytes = WT == WT_F16 ? K * 2 : K;
     const int M = a.M;
@@ -408,8 +408,8 @@ __global__ void __launch_bounds__(gemv_threads(WT)) k_gemv(GemvArgs a, GemvLaunc
             mi_s[2 * M + i] = a.pos[i];
         }
         if (a.in_mode == IN_EMBED_LN) {
-            mi_s[2 * M + i] = a.pos[i];
             mi_s[3 * M + i] = a.tok[i];
+            mi_s[4 * M + i] = pe_row(a, i);
         }
     }
     pdl_wait();
@@ -424,7 +424,7 @@ __global__ void __launch_bounds__(gemv_threads(WT)) k_gemv(GemvArgs a, GemvLaunc
 #pragma unroll
             for (int mm = 0; mm < MT; ++mm) resv[mm] = m0 + mm < M ? a.y[(size_t)(m0 + mm) * N + r0 + tid] : 0.f;
         if (m0 == 0) __syncthreads();  // mi_s
-        load_activations<MT, NT>(a, m0, K, act_s, ln_s, warp, lane, mi_s + 3 * M, mi_s + 2 * M);
+        load_activations<MT, NT>(a, m0, K, act_s, ln_s, warp, lane, mi_s + 3 * M, mi_s + 4 * M);
         if (has_res)
 #pragma unroll
             for (int mm = 0; mm < MT; ++mm) res_s[mm * L.rows_per_block + tid] = resv[mm];
@@ -539,8 +539,8 @@ static void plan_gemv(int M, int N, int K, int type, int sms, int &mt, GemvLaunc
     L.rows_per_block = rpb;
     L.w_bytes = align16((size_t)rpb * row_bytes);
     L.s_bytes = align16((size_t)rpb * srow);
-    // epilogue staging: bias, 4 ints per sequence, up to 8 residual rows
-    const size_t epi = ((size_t)rpb * 9 + 4 * (size_t)M) * 4;
+    // epilogue staging: bias, 5 ints per sequence, up to 8 residual rows
+    const size_t epi = ((size_t)rpb * 9 + 5 * (size_t)M) * 4;
     const size_t left = kSmemBudget - L.w_bytes - L.s_bytes - 64 - 2 * (size_t)K * 4 - epi;
     int cap = (int)(left / ((size_t)K * 4));
     mt = M < 8 ? M : 8;
@@ -555,7 +555,7 @@ static void plan_gemv(int M, int N, int K, int type, int sms, int &mt, GemvLaunc
 template <int MT, int R, int WT>
 static cudaError_t launch_gemv_t(const GemvArgs &a, const GemvLaunch &L, int blocks, cudaStream_t s, bool pdl) {
     const size_t smem = L.w_bytes + L.s_bytes + ((size_t)MT + (a.in_mode != IN_ACT ? 2 : 0)) * a.W.K * sizeof(float) + 16 +
-                        ((size_t)L.rows_per_block * (1 + MT) + 4 * (size_t)a.M) * 4;
+                        ((size_t)L.rows_per_block * (1 + MT) + 5 * (size_t)a.M) * 4;
     cudaLaunchConfig_t cfg = {};
     cfg.gridDim = dim3(blocks);
     cfg.blockDim = dim3(gemv_threads(WT));

@@ -80,11 +80,12 @@ __global__ void __launch_bounds__(kLogitsThreads, 1) k_logits_tc(LogitsArgs a, c
         mbar_init(acce + 1, 4);
         *fail = 0;
         fence_mbar_init();
-        for (int i = 0; i < NS && i < total; ++i) {
+        const int first = a.withhold ? 0 : (NS < total ? NS : total);
+        for (int i = 0; i < first; ++i) {
             mbar_expect_tx(full + i, kStageBytes);
             tma_load_2d(ring + (size_t)i * kStageBytes, &tmap, (i % KB) * kKB, (t0 + i / KB) * kTileRows, full + i);
         }
-        *issued = NS < total ? NS : total;
+        *issued = first;
     }
     if (warp == 1) {
         tmem_alloc(tslot, kCols);
@@ -177,7 +178,7 @@ __global__ void __launch_bounds__(kLogitsThreads, 1) k_logits_tc(LogitsArgs a, c
 
     if (warp == 0 && lane == 0) {
         // ---- producer: stream the remaining tiles as stages free up ----
-        for (int i = NS; i < total && !*fail; ++i) {
+        for (int i = NS; i < total && !*fail && !a.withhold; ++i) {
             const int st = i % NS, use = i / NS;
             if (!mbar_wait(empty + st, (unsigned)((use - 1) & 1), a.err)) {
                 *fail = 1;
@@ -274,15 +275,34 @@ static PFN_cuTensorMapEncodeTiled_v12000 encode_fn() {
 // Tensor map of a row-major f16 matrix [rows][cols] read in [128 rows x 64 cols] boxes with
 // the 128-byte swizzle the UMMA K-major operand expects.
 bool make_tmap_f16_rows(void *map_out, const void *base, int rows, int cols) {
+    return make_tmap_f16_box(map_out, base, rows, cols, kTileRows);
+}
+
+bool make_tmap_f16_box(void *map_out, const void *base, int rows, int cols, int box_rows) {
+    auto fn = encode_fn();
+    if (!fn || cols % kKB != 0 || ((uintptr_t)base & 15) || box_rows < 1 || box_rows > 256) return false;
+    CUtensorMap *m = reinterpret_cast<CUtensorMap *>(map_out);
+    const cuuint64_t dims[2] = {(cuuint64_t)cols, (cuuint64_t)rows};
+    const cuuint64_t strides[1] = {(cuuint64_t)cols * 2};
+    const cuuint32_t box[2] = {(cuuint32_t)kKB, (cuuint32_t)box_rows};
+    const cuuint32_t estr[2] = {1, 1};
+    return fn(m, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 2, const_cast<void *>(base), dims, strides, box, estr,
+              CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+              CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
+}
+
+// Tensor map of a row-major int8 matrix [rows][cols] read in [128 rows x 64 cols] boxes, unswizzled
+// (the Q8_0 converters read it with 16-byte loads).
+bool make_tmap_i8_rows(void *map_out, const void *base, int rows, int cols) {
     auto fn = encode_fn();
     if (!fn || cols % kKB != 0 || ((uintptr_t)base & 15)) return false;
     CUtensorMap *m = reinterpret_cast<CUtensorMap *>(map_out);
     const cuuint64_t dims[2] = {(cuuint64_t)cols, (cuuint64_t)rows};
-    const cuuint64_t strides[1] = {(cuuint64_t)cols * 2};
+    const cuuint64_t strides[1] = {(cuuint64_t)cols};
     const cuuint32_t box[2] = {(cuuint32_t)kKB, (cuuint32_t)kTileRows};
     const cuuint32_t estr[2] = {1, 1};
-    return fn(m, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 2, const_cast<void *>(base), dims, strides, box, estr,
-              CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+    return fn(m, CU_TENSOR_MAP_DATA_TYPE_UINT8, 2, const_cast<void *>(base), dims, strides, box, estr,
+              CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_NONE, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
               CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
 }
 

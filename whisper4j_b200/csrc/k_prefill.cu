@@ -117,3 +117,24 @@ cudaError_t launch_f32_to_f16(const float *src, __half *dst, size_t n, cudaStrea
 }
 
 }  // namespace w4j
+
+namespace w4j {
+// st[((t * KB + kb) * 128 + r) * 2 + h] = s[(t * 128 + r) * (K / 32) + kb * 2 + h]: the two scales of row
+// r in 64-wide k-block kb of 128-row tile t, contiguous per (tile, k-block) for one bulk copy
+__global__ void k_q8_tile_scales(const __half *s, int N, int K, __half *st) {
+    const size_t n = (size_t)N * (K / 32);
+    const int KB = K / 64;
+    for (size_t i = blockIdx.x * (size_t)blockDim.x + threadIdx.x; i < n; i += (size_t)gridDim.x * blockDim.x) {
+        const int h = (int)(i & 1), r = (int)((i >> 1) & 127);
+        const size_t tk = i >> 8;
+        const int kb = (int)(tk % KB), t = (int)(tk / KB);
+        st[i] = s[((size_t)t * 128 + r) * (K / 32) + (size_t)kb * 2 + h];
+    }
+}
+
+cudaError_t launch_q8_tile_scales(const __half *s, int N, int K, __half *st, cudaStream_t stream) {
+    if (N % 128 || K % 64) return cudaErrorInvalidValue;
+    k_q8_tile_scales<<<256, 256, 0, stream>>>(s, N, K, st);
+    return cudaGetLastError();
+}
+}  // namespace w4j

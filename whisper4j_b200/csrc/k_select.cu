@@ -839,6 +839,21 @@ __global__ void k_argmax_merge_status(const float *part, int P, int M, int32_t *
     }
 }
 
+// After a merge of M rows: if the device error word is set (a bounded wait of the vocabulary
+// pass ran out), every row reports token -1 and a NaN log-probability, and the word is cleared.
+__global__ void k_err_apply(int M, int32_t *tok, double *lp, int *err) {
+    __shared__ int e;
+    if (threadIdx.x == 0) e = *err;
+    __syncthreads();
+    if (!e) return;
+    for (int m = threadIdx.x; m < M; m += blockDim.x) {
+        tok[m] = -1;
+        lp[m] = __longlong_as_double(0x7ff8000000000000ll);
+    }
+    __syncthreads();
+    if (threadIdx.x == 0) *err = 0;
+}
+
 // ---------------------------------------------------------------------------
 static cudaLaunchConfig_t cfg_for(dim3 grid, dim3 block, cudaStream_t s, bool pdl, cudaLaunchAttribute *attr) {
     cudaLaunchConfig_t cfg = {};
@@ -861,6 +876,8 @@ static size_t select_smem(const DecodeState &st, int mode, int P) {
     const size_t fp = (size_t)4 << rec_l2(B + 1);
     return ((size_t)B * (((size_t)P * fp + st.hs + 3) & ~(size_t)3) + (size_t)B * (st.hs + st.n_ctx)) * 4;
 }
+
+size_t select_smem_bytes(const DecodeState &st, int mode, int P) { return select_smem(st, mode, P); }
 
 cudaError_t select_prepare() {
     cudaError_t e = allow_dynamic_smem(k_select_greedy);
@@ -912,6 +929,11 @@ cudaError_t launch_finalize(const DecodeState &st, int beam_mode, int parity, cu
 
 cudaError_t launch_argmax_merge(const float *part, int n_parts, int M, int32_t *tok, double *lp, cudaStream_t s) {
     k_argmax_merge<<<M, kSelThreads, (size_t)n_parts * 4 * 4, s>>>(part, n_parts, tok, lp);
+    return cudaGetLastError();
+}
+
+cudaError_t launch_err_apply(int M, int32_t *tok, double *lp, int *err, cudaStream_t s) {
+    k_err_apply<<<1, 256, 0, s>>>(M, tok, lp, err);
     return cudaGetLastError();
 }
 

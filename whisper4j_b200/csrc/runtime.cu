@@ -72,7 +72,7 @@ struct LayerDev {
 enum Proj : int { PROJ_QKV = 0, PROJ_O = 1, PROJ_XQ = 2, PROJ_XO = 3, PROJ_M0 = 4, PROJ_M2 = 5, PROJ_XK = 6, PROJ_XV = 7 };
 
 struct GraphKey {
-    int mode, S, B, eot, ts_begin, n_sup, max_tokens, ns, n_prompt;
+    int mode, S, B, eot, ts_begin, n_sup, max_tokens, ns, n_prompt, time_class;
     float temperature;
     unsigned long long seed;
     bool operator<(const GraphKey &o) const { return memcmp(this, &o, sizeof *this) < 0; }
@@ -85,6 +85,8 @@ struct w4j_ctx {
     int V = 0, C = 0, A = 0, d = 0, H = 0, L = 0;
     w4j_dims dims{};
     int max_streams = 0, max_beam = 0, n_slots = 0, M_max = 0;
+    int cap = 0;   // self-cache rows per slot: n_text_ctx, grown on demand (the reference's cache is unbounded)
+    int Mbuf = 0;  // activation rows: max(M_max, n_text_ctx) (a multi-token forward is one pass of its tokens)
     int sm_count = 148;
     std::vector<LayerDev> layers;
     DMat E;
@@ -101,6 +103,16 @@ struct w4j_ctx {
     float *logit_part = nullptr, *ns_part = nullptr, *ns_value = nullptr;
     float *masked = nullptr;  // M_max x V (sampling)
     float *raw = nullptr;     // n_text_ctx x V (forward)
+    int *op_err = nullptr;    // error word of the op-level vocabulary pass (w4j_op_logits_argmax)
+    __half *op_st = nullptr;  // tiled Q8_0 scales of the op-level linear (w4j_op_linear)
+    size_t op_st_n = 0;
+    // activations of projections with more than 128 rows, staged as f16 hi / lo B-operand rows
+    // ([act_hilo_rows(Mbuf)][K] for K = d and 4d), with a tensor map for each K
+    __half *hilo = nullptr;
+    alignas(64) unsigned char hilo_map_d[128] = {}, hilo_map_4d[128] = {};
+    bool hilo_ok = false;
+    __half *op_hilo = nullptr;  // the same for w4j_op_linear, grown on demand
+    size_t op_hilo_n = 0;
     // decode state
     DecodeState st;
     int *d_int_area = nullptr;     // per-call small int arrays (see layout in prepare_call)
@@ -110,6 +122,7 @@ struct w4j_ctx {
     int *h_done = nullptr;
     // graphs
     std::map<GraphKey, cudaGraphExec_t> graphs;
+    std::map<GraphKey, long long> graph_launches;  // kernels in each cached step graph
     std::atomic<int> cancel{0};
     double last_ms = 0;
     int last_steps = 0;
@@ -121,7 +134,34 @@ struct w4j_ctx {
     bool e_tmap_ok = false;
     bool tc_logits = true;
     bool tc_gemm = true;  // tcgen05 projections once M >= 16
+    // in-chain kernel timing (w4j_set_kernel_timing): step graphs captured with external event
+    // records around every launch of one kernel class; read back after each step
+    int time_class = 0;
+    bool timing_capture = false;
+    int tev_used = 0, tev_pairs = 0;
+    std::vector<cudaEvent_t> tev;
+    double class_ms = 0;
+    long long class_launches = 0;
 };
+
+// Kernel classes of w4j_set_kernel_timing.
+enum KClass : int { KC_PROJ = 1, KC_SELF_ATTN = 2, KC_CROSS_ATTN = 3, KC_LOGITS = 4, KC_SELECT = 5 };
+
+// Around one launch of class `cls` while a timed step graph is being captured: an external event
+// record before (begin) and after (!begin) it.
+static cudaError_t tmark(w4j_ctx *c, int cls, bool begin) {
+    if (!c->timing_capture || c->time_class != cls) return cudaSuccess;
+    if ((size_t)c->tev_used >= c->tev.size()) {
+        cudaEvent_t e;
+        const cudaError_t r = cudaEventCreate(&e);
+        if (r != cudaSuccess) return r;
+        c->tev.push_back(e);
+    }
+    const cudaError_t r = cudaEventRecordWithFlags(c->tev[c->tev_used], c->stream, cudaEventRecordExternal);
+    ++c->tev_used;
+    if (!begin) c->tev_pairs = c->tev_used / 2;
+    return r;
+}
 
 template <typename T>
 static int dalloc(w4j_ctx *c, T **p, size_t n) {
@@ -134,9 +174,18 @@ static int dalloc(w4j_ctx *c, T **p, size_t n) {
     return 0;
 }
 
+static void dfree(w4j_ctx *c, void *p) {
+    if (!p) return;
+    auto it = std::find(c->allocs.begin(), c->allocs.end(), p);
+    if (it != c->allocs.end()) c->allocs.erase(it);
+    cudaFree(p);
+}
+
 static void free_all(w4j_ctx *c) {
     for (auto &kv : c->graphs) cudaGraphExecDestroy(kv.second);
     c->graphs.clear();
+    for (cudaEvent_t e : c->tev) cudaEventDestroy(e);
+    c->tev.clear();
     for (void *p : c->allocs) cudaFree(p);
     c->allocs.clear();
     if (c->h_int_area) cudaFreeHost(c->h_int_area);
@@ -167,6 +216,74 @@ static void build_gelu_lut(std::vector<float> &t) {
 // longest context.
 static int choose_split(int len, int nq) {
     return std::max(1, std::min((len + kAttnKeyTile - 1) / kAttnKeyTile, attn_max_splits(nq)));
+}
+
+// The self-cache capacity (rows per slot) and everything sized by it: the self K / V caches
+// (keep_rows: the rows of the old caches are copied into the new ones), the beam tables, the
+// token histories and mask lists, the finished lists and the output tokens.  The reference's
+// cache grows without bound once a sequence passes n_text_ctx (WhisperDecoder.java:72 clamps only
+// the positional offset); here it grows on demand up to kMaxSelfRows.  Graphs captured with the
+// old arrays are dropped.
+constexpr int kMaxSelfRows = 4096;
+
+static int size_self(w4j_ctx *c, int cap, bool keep_rows) {
+    DecodeState &st = c->st;
+    const size_t M = c->M_max, S = c->max_streams, L = c->L, d = c->d;
+    const int hs = cap + 1, dyn_stride = 2 * (cap + 1) + 8;
+    __half *sk = nullptr, *sv = nullptr;
+    int *t0 = nullptr, *t1 = nullptr, *h0 = nullptr, *h1 = nullptr, *dl = nullptr, *ft = nullptr, *ot = nullptr;
+    auto undo = [&](int rc) {
+        for (void *p : {(void *)sk, (void *)sv, (void *)t0, (void *)t1, (void *)h0, (void *)h1, (void *)dl, (void *)ft,
+                        (void *)ot})
+            dfree(c, p);
+        return rc;
+    };
+    int rc;
+    if ((rc = dalloc(c, &sk, (size_t)c->n_slots * L * cap * d)) || (rc = dalloc(c, &sv, (size_t)c->n_slots * L * cap * d)) ||
+        (rc = dalloc(c, &t0, M * cap)) || (rc = dalloc(c, &t1, M * cap)) || (rc = dalloc(c, &h0, M * hs)) ||
+        (rc = dalloc(c, &h1, M * hs)) || (rc = dalloc(c, &dl, M * dyn_stride)) || (rc = dalloc(c, &ft, M * hs)) ||
+        (rc = dalloc(c, &ot, S * hs)))
+        return undo(rc);
+    if (keep_rows && c->sk) {
+        // [slot][layer][head][rows][64]: one run of old-capacity rows per (slot, layer, head)
+        const size_t runs = (size_t)c->n_slots * L * c->H, old_b = (size_t)c->cap * kHeadDim * 2,
+                     new_b = (size_t)cap * kHeadDim * 2;
+        cudaError_t e = cudaMemcpy2DAsync(sk, new_b, c->sk, old_b, old_b, runs, cudaMemcpyDeviceToDevice, c->stream);
+        if (e == cudaSuccess)
+            e = cudaMemcpy2DAsync(sv, new_b, c->sv, old_b, old_b, runs, cudaMemcpyDeviceToDevice, c->stream);
+        if (e == cudaSuccess) e = cudaStreamSynchronize(c->stream);
+        if (e != cudaSuccess) return undo(set_err(W4J_ERR_CUDA, "self-cache growth: %s", cudaGetErrorString(e)));
+    }
+    for (auto &kv : c->graphs) cudaGraphExecDestroy(kv.second);
+    c->graphs.clear();
+    c->graph_launches.clear();
+    for (void *p : {(void *)c->sk, (void *)c->sv, (void *)st.table[0], (void *)st.table[1], (void *)st.hist[0],
+                    (void *)st.hist[1], (void *)st.dyn_list, (void *)st.fin_tok, (void *)st.out_tok})
+        dfree(c, p);
+    c->sk = sk;
+    c->sv = sv;
+    st.table[0] = t0;
+    st.table[1] = t1;
+    st.hist[0] = h0;
+    st.hist[1] = h1;
+    st.dyn_list = dl;
+    st.fin_tok = ft;
+    st.out_tok = ot;
+    st.n_ctx = cap;
+    st.hs = hs;
+    st.dyn_stride = dyn_stride;
+    c->cap = cap;
+    return 0;
+}
+
+// Make room for `rows` self-cache rows per slot (keeping the cached rows).
+static int grow_self(w4j_ctx *c, int rows) {
+    if (rows <= c->cap) return 0;
+    if (rows > kMaxSelfRows)
+        return set_err(W4J_ERR_ARG, "%d self-attention positions exceed this library's limit of %d", rows, kMaxSelfRows);
+    int cap = std::max(rows, c->cap + c->cap / 2);
+    cap = std::min(kMaxSelfRows, (cap + 63) / 64 * 64);
+    return size_self(c, cap, true);
 }
 
 extern "C" const char *w4j_last_error(void) { return g_err.c_str(); }
@@ -205,6 +322,8 @@ extern "C" int w4j_ctx_create(const w4j_dims *dims, int device, int max_streams,
     c->max_beam = max_beam;
     c->n_slots = max_streams * max_beam + 1;  // + one private slot for forward without a cache
     c->M_max = max_streams * max_beam;
+    c->cap = dims->n_text_ctx;
+    c->Mbuf = std::max(c->M_max, dims->n_text_ctx);
     c->sm_count = prop.multiProcessorCount;
     if (const char *ev = getenv("W4J_NO_TC_LOGITS")) c->tc_logits = ev[0] == '0';
     if (const char *ev = getenv("W4J_NO_TC_GEMM")) c->tc_gemm = ev[0] == '0';
@@ -224,23 +343,27 @@ extern "C" int w4j_ctx_create(const w4j_dims *dims, int device, int max_streams,
         (rc = (int)attn_prepare()) != 0 || (rc = (int)gemm_tc_prepare()) != 0 || (rc = (int)xkv_tc_prepare()) != 0)
         return fail(set_err(W4J_ERR_CUDA, "kernel attributes: %s", cudaGetErrorString((cudaError_t)rc)));
     const size_t V = c->V, C = c->C, A = c->A, L = c->L;
-    const size_t M = c->M_max;
+    const size_t M = c->M_max, MB = c->Mbuf;
     // caches
     const size_t cross = (size_t)max_streams * L * A * d;
-    const size_t self = (size_t)c->n_slots * L * C * d;
-    if ((rc = dalloc(c, &c->ck, cross)) || (rc = dalloc(c, &c->cv, cross)) || (rc = dalloc(c, &c->sk, self)) ||
-        (rc = dalloc(c, &c->sv, self)))
-        return fail(rc);
+    if ((rc = dalloc(c, &c->ck, cross)) || (rc = dalloc(c, &c->cv, cross))) return fail(rc);
     c->x_tmap_ok = cross / kHeadDim < (size_t)INT32_MAX &&
                    make_tmap_f16_rows(c->xk_tmap, c->ck, (int)(cross / kHeadDim), kHeadDim) &&
                    make_tmap_f16_rows(c->xv_tmap, c->cv, (int)(cross / kHeadDim), kHeadDim);
     // activations
-    if ((rc = dalloc(c, &c->x, M * d)) || (rc = dalloc(c, &c->q, M * d)) || (rc = dalloc(c, &c->attn, M * d)) ||
-        (rc = dalloc(c, &c->h, M * 4 * d)) || (rc = dalloc(c, &c->xa_stage, A * d)))
+    if ((rc = dalloc(c, &c->x, MB * d)) || (rc = dalloc(c, &c->q, MB * d)) || (rc = dalloc(c, &c->attn, MB * d)) ||
+        (rc = dalloc(c, &c->h, MB * 4 * d)) || (rc = dalloc(c, &c->xa_stage, A * d)))
         return fail(rc);
+    {
+        const int rows = act_hilo_rows(c->Mbuf);
+        if ((rc = dalloc(c, &c->hilo, (size_t)rows * 4 * d))) return fail(rc);
+        c->hilo_ok = make_tmap_f16_box(c->hilo_map_d, c->hilo, rows, d, 256) &&
+                     make_tmap_f16_box(c->hilo_map_4d, c->hilo, rows, 4 * d, 256);
+    }
     c->n_parts = logits_parts_for(c->V, c->sm_count);
-    if ((rc = dalloc(c, &c->logit_part, M * c->n_parts * kPartStride)) || (rc = dalloc(c, &c->ns_part, M * c->n_parts * 2)) ||
-        (rc = dalloc(c, &c->ns_value, M)) || (rc = dalloc(c, &c->masked, M * V)) || (rc = dalloc(c, &c->raw, C * V)))
+    if ((rc = dalloc(c, &c->logit_part, MB * c->n_parts * kPartStride)) ||
+        (rc = dalloc(c, &c->ns_part, MB * c->n_parts * 2)) || (rc = dalloc(c, &c->ns_value, MB)) ||
+        (rc = dalloc(c, &c->masked, M * V)) || (rc = dalloc(c, &c->raw, C * V)) || (rc = dalloc(c, &c->op_err, 1)))
         return fail(rc);
     // GELU table
     {
@@ -250,28 +373,24 @@ extern "C" int w4j_ctx_create(const w4j_dims *dims, int device, int max_streams,
         if (cudaMemcpy(c->gelu_lut, lut.data(), 65536 * 4, cudaMemcpyHostToDevice) != cudaSuccess)
             return fail(set_err(W4J_ERR_CUDA, "gelu table upload"));
     }
-    // decode state
+    // decode state (the arrays sized by the self-cache capacity are allocated by size_self)
     DecodeState &st = c->st;
-    st.n_ctx = (int)C;
     st.V = (int)V;
-    st.hs = (int)C + 1;
-    st.dyn_stride = 2 * ((int)C + 1) + 8;
     if ((rc = dalloc(c, &st.tok_in, M)) || (rc = dalloc(c, &st.seq_slot, M)) || (rc = dalloc(c, &st.seq_pos, M)) ||
-        (rc = dalloc(c, &st.active, M)) || (rc = dalloc(c, &st.table[0], M * C)) || (rc = dalloc(c, &st.table[1], M * C)) ||
-        (rc = dalloc(c, &st.hist[0], M * st.hs)) || (rc = dalloc(c, &st.hist[1], M * st.hs)) ||
-        (rc = dalloc(c, &st.hist_len[0], M)) || (rc = dalloc(c, &st.hist_len[1], M)) || (rc = dalloc(c, &st.lp[0], M)) ||
-        (rc = dalloc(c, &st.lp[1], M)) || (rc = dalloc(c, &st.dyn_list, M * st.dyn_stride)) ||
-        (rc = dalloc(c, &st.dyn_count, M)) || (rc = dalloc(c, &st.ranges, M * kMaxRanges)) ||
-        (rc = dalloc(c, &st.n_ranges, M)) || (rc = dalloc(c, &st.done, (size_t)max_streams)) ||
-        (rc = dalloc(c, &st.beam_par, (size_t)max_streams)) || (rc = dalloc(c, &st.nsp, (size_t)max_streams)) ||
-        (rc = dalloc(c, &st.fin_n, (size_t)max_streams)) || (rc = dalloc(c, &st.fin_tok, M * st.hs)) ||
+        (rc = dalloc(c, &st.active, M)) || (rc = dalloc(c, &st.hist_len[0], M)) || (rc = dalloc(c, &st.hist_len[1], M)) ||
+        (rc = dalloc(c, &st.lp[0], M)) || (rc = dalloc(c, &st.lp[1], M)) || (rc = dalloc(c, &st.dyn_count, M)) ||
+        (rc = dalloc(c, &st.ranges, M * kMaxRanges)) || (rc = dalloc(c, &st.n_ranges, M)) ||
+        (rc = dalloc(c, &st.done, (size_t)max_streams)) || (rc = dalloc(c, &st.beam_par, (size_t)max_streams)) ||
+        (rc = dalloc(c, &st.nsp, (size_t)max_streams)) || (rc = dalloc(c, &st.fin_n, (size_t)max_streams)) ||
         (rc = dalloc(c, &st.fin_len, M)) || (rc = dalloc(c, &st.fin_lp, M)) ||
-        (rc = dalloc(c, &st.out_tok, (size_t)max_streams * st.hs)) || (rc = dalloc(c, &st.out_len, (size_t)max_streams)) ||
-        (rc = dalloc(c, &st.out_sum, (size_t)max_streams)) || (rc = dalloc(c, &st.err, 1)))
+        (rc = dalloc(c, &st.out_len, (size_t)max_streams)) || (rc = dalloc(c, &st.out_sum, (size_t)max_streams)) ||
+        (rc = dalloc(c, &st.err, 1)))
         return fail(rc);
-    // per-call int arrays: prompt tokens [C][S], prompt positions [C][S], stream base [S],
-    // cross stream [S], suppress list [V], forward tokens [C], forward positions [C], misc [16]
-    c->int_area_n = 2 * C * (size_t)max_streams + 2 * (size_t)max_streams + V + 2 * C + 16;
+    if ((rc = size_self(c, c->cap, false))) return fail(rc);
+    // per-call int arrays: a decode call's prompt tokens [C][S], prompt positions [C][S], stream
+    // base [S], cross stream [S] and suppress list [V]; or a forward call's nine per-token
+    // arrays [9][C] (forward_layout)
+    c->int_area_n = std::max(2 * C * (size_t)max_streams + 2 * (size_t)max_streams + V, 9 * C) + 16;
     if ((rc = dalloc(c, &c->d_int_area, c->int_area_n)) || (rc = dalloc(c, &c->d_done_snapshot, (size_t)max_streams)))
         return fail(rc);
     if (cudaMallocHost(&c->h_int_area, c->int_area_n * sizeof(int)) != cudaSuccess ||
@@ -483,11 +602,27 @@ extern "C" int w4j_finalize(w4j_ctx *c) {
     if (!c) return set_err(W4J_ERR_ARG, "null context");
     std::lock_guard<std::mutex> g(c->mu);
     TRY(check_ready(c));
+    CUDA_TRY(cudaSetDevice(c->device));
     for (LayerDev &ly : c->layers) {
-        const DMat *m[8] = {&ly.qkv, &ly.o, &ly.xq, &ly.xo, &ly.m0, &ly.m2, &ly.xk, &ly.xv};
-        for (int i = 0; i < 8; ++i)
-            ly.tmap_ok[i] = c->tc_gemm && m[i]->type == WT_F16 && make_tmap_f16_rows(ly.tmap[i], m[i]->h, m[i]->N, m[i]->K);
+        DMat *m[8] = {&ly.qkv, &ly.o, &ly.xq, &ly.xo, &ly.m0, &ly.m2, &ly.xk, &ly.xv};
+        for (int i = 0; i < 8; ++i) {
+            ly.tmap_ok[i] = false;
+            if (!c->tc_gemm) continue;
+            if (m[i]->type == WT_F16) {
+                ly.tmap_ok[i] = make_tmap_f16_rows(ly.tmap[i], m[i]->h, m[i]->N, m[i]->K);
+            } else if (m[i]->type == WT_Q8 && m[i]->N % 128 == 0 && m[i]->K % 64 == 0 && i < 6) {
+                // the tensor-core projections read Q8_0 scales per (128-row tile, 64-wide k-block)
+                if (!m[i]->st) {
+                    __half *st = nullptr;
+                    TRY(dalloc(c, &st, (size_t)m[i]->N * (m[i]->K / 32)));
+                    CUDA_TRY(launch_q8_tile_scales(m[i]->s, m[i]->N, m[i]->K, st, 0));
+                    m[i]->st = st;
+                }
+                ly.tmap_ok[i] = make_tmap_i8_rows(ly.tmap[i], m[i]->q, m[i]->N, m[i]->K);
+            }
+        }
     }
+    CUDA_TRY(cudaDeviceSynchronize());
     return W4J_OK;
 }
 
@@ -500,7 +635,7 @@ static int prefill(w4j_ctx *c, int slot, const float *xa_dev) {
         const size_t off = ((size_t)slot * c->L + l) * (size_t)c->H * c->A * kHeadDim;
         // tensor cores for f16 weights, else the SIMT GEMM
         cudaError_t e = cudaErrorNotSupported;
-        if (ly.tmap_ok[PROJ_XK] && ly.tmap_ok[PROJ_XV])
+        if (ly.tmap_ok[PROJ_XK] && ly.tmap_ok[PROJ_XV] && ly.xk.type == WT_F16 && ly.xv.type == WT_F16)
             e = launch_cross_kv_tc(xa_dev, c->A, c->d, ly.tmap[PROJ_XK], ly.tmap[PROJ_XV], ly.bxk, ly.bxv,
                                    c->ck + off, c->cv + off, c->st.err, c->stream);
         if (e == cudaErrorNotSupported)
@@ -549,21 +684,41 @@ struct PassArgs {
     const int *cross_stream;  // [groups]
     const int *group_active;  // [groups] or null
     int self_prefetch;        // older self-cache rows were written by an earlier graph launch
+    const int *pe_pos;        // [M] positional-embedding rows, or null: min(pos, n_text_ctx - 1)
+    const int *kv_len;        // [M] self-attention keys, or null: pos + 1
+    const int2 *mask;         // [M] masked self-attention keys [lo, hi), or null
 };
 
 // One projection: the tcgen05 kernel from 16 rows on (f16 weights), else the GEMV.
-static cudaError_t run_proj(w4j_ctx *c, const GemvArgs &g, const LayerDev &ly, Proj p, bool pdl) {
-    if (ly.tmap_ok[p] && g.M >= 16) {
-        const cudaError_t e = launch_gemm_tc(g, ly.tmap[p], c->sm_count, c->stream, pdl);
-        if (e != cudaErrorNotSupported) return e;
+// One projection: the tcgen05 kernel from 16 rows on (past 128 rows of f16 weights after staging the
+// activations as f16 hi / lo rows), else the GEMV.
+static cudaError_t run_proj(w4j_ctx *c, const GemvArgs &g, const LayerDev &ly, Proj p, bool pdl, long long &launches) {
+    cudaError_t e = tmark(c, KC_PROJ, true);
+    if (e != cudaSuccess) return e;
+    e = cudaErrorNotSupported;
+    if (ly.tmap_ok[p] && g.M >= 16 && gemm_tc_supported(g, c->sm_count)) {
+        const void *bmap = nullptr;
+        if (gemm_tc_staged(g)) {
+            if (c->hilo_ok && (g.W.K == c->d || g.W.K == 4 * c->d)) {
+                e = launch_act_hilo(g, c->hilo, c->stream, pdl);
+                if (e != cudaSuccess) return e;
+                ++launches;
+                bmap = g.W.K == c->d ? c->hilo_map_d : c->hilo_map_4d;
+                e = launch_gemm_tc(g, ly.tmap[p], bmap, c->sm_count, c->stream, pdl);
+            }
+        } else {
+            e = launch_gemm_tc(g, ly.tmap[p], nullptr, c->sm_count, c->stream, pdl);
+        }
     }
-    return launch_gemv(g, c->stream, pdl);
+    if (e == cudaErrorNotSupported) e = launch_gemv(g, c->stream, pdl);
+    ++launches;
+    return e != cudaSuccess ? e : tmark(c, KC_PROJ, false);
 }
 
 static int run_layers(w4j_ctx *c, const PassArgs &pa, long long &launches) {
     const bool pdl = true;
     const int d = c->d;
-    const int self_split = choose_split(c->C, 1);
+    const int self_split = choose_split(c->cap, 1);
     const int cross_split = choose_split(c->A, pa.nq);
     for (int l = 0; l < c->L; ++l) {
         LayerDev &ly = c->layers[l];
@@ -579,6 +734,8 @@ static int run_layers(w4j_ctx *c, const PassArgs &pa, long long &launches) {
         g.pos_emb = c->pos_emb;
         g.tok = pa.tok;
         g.pos = pa.pos;
+        g.pe_pos = pa.pe_pos;
+        g.pe_rows = c->C;
         g.x_out = c->x;
         g.out_mode = OUT_QKV;
         g.y = c->q;
@@ -588,10 +745,10 @@ static int run_layers(w4j_ctx *c, const PassArgs &pa, long long &launches) {
         g.layer = l;
         g.n_layer = c->L;
         g.n_head = c->H;
-        g.n_ctx = c->C;
+        g.n_ctx = c->cap;
         g.active = pa.active;
         g.err = c->st.err;
-        CUDA_TRY(run_proj(c, g, ly, PROJ_QKV, pdl));
+        CUDA_TRY(run_proj(c, g, ly, PROJ_QKV, pdl, launches));
 
         AttnArgs sa;
         sa.q = c->q;
@@ -602,10 +759,12 @@ static int run_layers(w4j_ctx *c, const PassArgs &pa, long long &launches) {
         sa.cross = 0;
         sa.kc = c->sk;
         sa.vc = c->sv;
-        sa.n_ctx = c->C;
+        sa.n_ctx = c->cap;
         sa.seq_slot = pa.seq_slot;
         sa.table = pa.table;
         sa.pos = pa.pos;
+        sa.kv_len = pa.kv_len;
+        sa.mask = pa.mask;
         sa.nq = 1;
         sa.groups = pa.M;
         sa.nsplit = self_split;
@@ -613,7 +772,9 @@ static int run_layers(w4j_ctx *c, const PassArgs &pa, long long &launches) {
         sa.active = pa.active;
         sa.err = c->st.err;
         sa.self_prefetch = pa.self_prefetch;
+        CUDA_TRY(tmark(c, KC_SELF_ATTN, true));
         CUDA_TRY(launch_attn(sa, c->stream, pdl));
+        CUDA_TRY(tmark(c, KC_SELF_ATTN, false));
 
         GemvArgs go;
         go.W = ly.o;
@@ -625,7 +786,7 @@ static int run_layers(w4j_ctx *c, const PassArgs &pa, long long &launches) {
         go.y = c->x;
         go.active = pa.active;
         go.err = c->st.err;
-        CUDA_TRY(run_proj(c, go, ly, PROJ_O, pdl));
+        CUDA_TRY(run_proj(c, go, ly, PROJ_O, pdl, launches));
 
         GemvArgs gq;
         gq.W = ly.xq;
@@ -638,7 +799,7 @@ static int run_layers(w4j_ctx *c, const PassArgs &pa, long long &launches) {
         gq.out_mode = OUT_STORE;
         gq.y = c->q;
         gq.err = c->st.err;
-        CUDA_TRY(run_proj(c, gq, ly, PROJ_XQ, pdl));
+        CUDA_TRY(run_proj(c, gq, ly, PROJ_XQ, pdl, launches));
 
         AttnArgs ca;
         ca.q = c->q;
@@ -657,9 +818,11 @@ static int run_layers(w4j_ctx *c, const PassArgs &pa, long long &launches) {
         ca.out = c->attn;
         ca.active = pa.group_active;
         ca.err = c->st.err;
+        CUDA_TRY(tmark(c, KC_CROSS_ATTN, true));
         if (c->x_tmap_ok && attn_stream_pays(ca, c->sm_count))
             CUDA_TRY(launch_attn_stream(ca, c->xk_tmap, c->xv_tmap, c->sm_count, c->stream, pdl));
         else CUDA_TRY(launch_attn(ca, c->stream, pdl));
+        CUDA_TRY(tmark(c, KC_CROSS_ATTN, false));
 
         GemvArgs gxo;
         gxo.W = ly.xo;
@@ -671,7 +834,7 @@ static int run_layers(w4j_ctx *c, const PassArgs &pa, long long &launches) {
         gxo.y = c->x;
         gxo.active = pa.active;
         gxo.err = c->st.err;
-        CUDA_TRY(run_proj(c, gxo, ly, PROJ_XO, pdl));
+        CUDA_TRY(run_proj(c, gxo, ly, PROJ_XO, pdl, launches));
 
         GemvArgs g1;
         g1.W = ly.m0;
@@ -685,7 +848,7 @@ static int run_layers(w4j_ctx *c, const PassArgs &pa, long long &launches) {
         g1.y = c->h;
         g1.gelu_lut = c->gelu_lut;
         g1.err = c->st.err;
-        CUDA_TRY(run_proj(c, g1, ly, PROJ_M0, pdl));
+        CUDA_TRY(run_proj(c, g1, ly, PROJ_M0, pdl, launches));
 
         GemvArgs g2;
         g2.W = ly.m2;
@@ -697,8 +860,8 @@ static int run_layers(w4j_ctx *c, const PassArgs &pa, long long &launches) {
         g2.y = c->x;
         g2.active = pa.active;
         g2.err = c->st.err;
-        CUDA_TRY(run_proj(c, g2, ly, PROJ_M2, pdl));
-        launches += 8;
+        CUDA_TRY(run_proj(c, g2, ly, PROJ_M2, pdl, launches));
+        launches += 2;  // the two attentions
     }
     return 0;
 }
@@ -740,7 +903,13 @@ static LogitsArgs logits_rows(const LogitsArgs &la, int m0, int n, int n_parts) 
 
 // The vocabulary pass: the tcgen05 kernel when the embedding is f16 (one launch per 32 rows),
 // else the SIMT one.  Returns the launches enqueued in `launches`.
+static cudaError_t run_logits_untimed(w4j_ctx *c, const LogitsArgs &la, bool pdl, long long &launches);
 static cudaError_t run_logits(w4j_ctx *c, const LogitsArgs &la, bool pdl, long long &launches) {
+    cudaError_t e = tmark(c, KC_LOGITS, true);
+    if (e == cudaSuccess) e = run_logits_untimed(c, la, pdl, launches);
+    return e != cudaSuccess ? e : tmark(c, KC_LOGITS, false);
+}
+static cudaError_t run_logits_untimed(w4j_ctx *c, const LogitsArgs &la, bool pdl, long long &launches) {
     if (c->e_tmap_ok) {
         const int chunks = (la.M + 31) / 32;
         cudaError_t e = cudaSuccess;
@@ -769,39 +938,57 @@ extern "C" int w4j_forward(w4j_ctx *c, int slot, const int32_t *tokens, int n, i
     if (slot < 0 || slot >= c->max_streams) return set_err(W4J_ERR_ARG, "slot %d out of range", slot);
     if (!c->has_xa[slot]) return set_err(W4J_ERR_STATE, "no encoder output set for slot %d", slot);
     if (n <= 0) return set_err(W4J_ERR_ARG, "empty token list");
+    // WhisperDecoder.java:72: offset = min(cache length, n_ctx - seqLen); a sequence longer than
+    // the positional table has no valid offset (the reference fails reading the table)
+    if (n > c->C) return set_err(W4J_ERR_ARG, "%d tokens exceed n_text_ctx %d", n, c->C);
     for (int i = 0; i < n; ++i)
         if (tokens[i] < 0 || tokens[i] >= c->V) return set_err(W4J_ERR_ARG, "token id %d out of range", tokens[i]);
     const int start = use_cache ? c->cache_len[slot] : 0;
-    if (start + n > c->C)
-        return set_err(W4J_ERR_ARG, "sequence of %d tokens exceeds n_text_ctx %d", start + n, c->C);
+    const int offset = std::min(start, c->C - n);
+    TRY(grow_self(c, start + n));  // the cache keeps growing past n_text_ctx, as the reference's does
     const int phys = use_cache ? slot * c->max_beam : c->n_slots - 1;
-    // int area layout for forward: tok[C], pos[C], slot[1], stream[1]
+    // one pass over the n tokens as n rows (forward_layout: [9][C] ints): every layer appends all
+    // their K / V rows before its attention, which for n > 1 applies the reference's causal mask
+    // from key column 0 (MultiHeadAttention.java:84-88, Tensor.java:622-640): query t attends keys
+    // [0, t] and [n_ctx, kv_len); with an empty cache that is the usual causal mask
+    const int C = c->C, kv = start + n;
     int *hi = c->h_int_area;
     int *di = c->d_int_area;
-    for (int i = 0; i < n; ++i) {
-        hi[i] = tokens[i];
-        hi[c->C + i] = start + i;
-    }
-    hi[2 * c->C] = phys;
-    hi[2 * c->C + 1] = slot;
-    CUDA_TRY(cudaMemcpyAsync(di, hi, (2 * (size_t)c->C + 2) * 4, cudaMemcpyHostToDevice, c->stream));
-    long long launches = 0;
     for (int t = 0; t < n; ++t) {
-        PassArgs pa{};
-        pa.M = 1;
-        pa.tok = di + t;
-        pa.pos = di + c->C + t;
-        pa.seq_slot = di + 2 * c->C;
-        pa.groups = 1;
-        pa.nq = 1;
-        pa.cross_stream = di + 2 * c->C + 1;
-        TRY(run_layers(c, pa, launches));
-        LogitsArgs la = logits_args(c, 1, nullptr);
-        la.raw_out = c->raw + (size_t)t * c->V;
-        CUDA_TRY(run_logits(c, la, true, launches));
+        hi[t] = tokens[t];
+        hi[C + t] = start + t;
+        hi[2 * C + t] = offset + t;
+        hi[3 * C + t] = phys;
+        hi[4 * C + t] = slot;
+        hi[5 * C + t] = kv;
+        hi[6 * C + 2 * t] = n > 1 ? t + 1 : 0;
+        hi[6 * C + 2 * t + 1] = n > 1 ? std::min(kv, C) : 0;
     }
+    CUDA_TRY(cudaMemcpyAsync(di, hi, 8 * (size_t)C * 4, cudaMemcpyHostToDevice, c->stream));
+    long long launches = 0;
+    PassArgs pa{};
+    pa.M = n;
+    pa.tok = di;
+    pa.pos = di + C;
+    pa.pe_pos = di + 2 * C;
+    pa.seq_slot = di + 3 * C;
+    pa.cross_stream = di + 4 * C;
+    pa.kv_len = di + 5 * C;
+    pa.mask = reinterpret_cast<const int2 *>(di + 6 * C);
+    pa.groups = n;
+    pa.nq = 1;
+    TRY(run_layers(c, pa, launches));
+    LogitsArgs la = logits_args(c, n, nullptr);
+    la.raw_out = c->raw;
+    CUDA_TRY(run_logits(c, la, true, launches));
     CUDA_TRY(cudaMemcpyAsync(out_logits, c->raw, (size_t)n * c->V * 4, cudaMemcpyDeviceToHost, c->stream));
     CUDA_TRY(cudaStreamSynchronize(c->stream));
+    int errw = 0;
+    CUDA_TRY(cudaMemcpy(&errw, c->st.err, 4, cudaMemcpyDeviceToHost));
+    if (errw) {
+        cudaMemset(c->st.err, 0, 4);
+        return set_err(W4J_ERR_CUDA, "a bounded device wait ran out (copy never completed)");
+    }
     if (use_cache) c->cache_len[slot] = start + n;
     return W4J_OK;
 }
@@ -860,9 +1047,11 @@ static int validate_call(w4j_ctx *c, const CallArgs &a) {
     if (a.eot < 0 || a.eot >= c->V) return set_err(W4J_ERR_ARG, "eot token %d out of range", a.eot);
     if (a.max_tokens < 0) return set_err(W4J_ERR_ARG, "max_tokens must be >= 0");
     if (a.beam > 1 && a.max_tokens < 1) return set_err(W4J_ERR_ARG, "beam search needs max_tokens >= 1");
-    if (a.n_prompt + std::max(a.max_tokens, 1) - 1 > c->C)
-        return set_err(W4J_ERR_ARG, "prompt (%d) + max_tokens (%d) exceeds the %d-position self-attention cache",
-                       a.n_prompt, a.max_tokens, c->C);
+    // positions past n_text_ctx reuse its last positional row (WhisperDecoder.java:72) while the
+    // self cache keeps growing; the capacity is made at the start of the call (grow_self)
+    if ((long long)a.n_prompt + std::max(a.max_tokens, 1) - 1 > kMaxSelfRows)
+        return set_err(W4J_ERR_ARG, "prompt (%d) + max_tokens (%d) exceeds this library's limit of %d positions",
+                       a.n_prompt, a.max_tokens, kMaxSelfRows);
     if (a.n_sup < 0 || (a.n_sup > 0 && !a.suppress)) return set_err(W4J_ERR_ARG, "suppress list");
     if (a.n_sup > c->V) return set_err(W4J_ERR_ARG, "suppress list longer than the vocabulary");
     if (a.temperature < 0.f || !(a.temperature == a.temperature)) return set_err(W4J_ERR_ARG, "temperature");
@@ -1013,7 +1202,9 @@ static int enqueue_step(w4j_ctx *c, const CallArgs &a, const CallLayout &Ly, int
     if (mode == MODE_SAMPLE) la.masked_out = c->masked;
     CUDA_TRY(run_logits(c, la, true, launches));
     const int sel = mode == MODE_BEAM ? SEL_BEAM : mode == MODE_SAMPLE ? SEL_SAMPLE : SEL_GREEDY;
+    CUDA_TRY(tmark(c, KC_SELECT, true));
     CUDA_TRY(launch_select(st, sel, parity, c->logit_part, c->n_parts, c->masked, 0, c->stream, true));
+    CUDA_TRY(tmark(c, KC_SELECT, false));
     launches += 1;
     return 0;
 }
@@ -1033,20 +1224,25 @@ static int get_step_graph(w4j_ctx *c, const CallArgs &a, const CallLayout &Ly, i
     k.n_prompt = a.n_prompt;
     k.temperature = a.temperature;
     k.seed = a.seed;
+    k.time_class = c->time_class;
     long long launches = 0;
     auto it = c->graphs.find(k);
     if (it != c->graphs.end()) {
         *out = it->second;
-        per_step = (long long)c->L * 8 + 2;
+        per_step = c->graph_launches[k];
         return 0;
     }
     if (c->graphs.size() >= 16) {
         for (auto &kv : c->graphs) cudaGraphExecDestroy(kv.second);
         c->graphs.clear();
+        c->graph_launches.clear();
     }
     cudaGraph_t graph = nullptr;
     CUDA_TRY(cudaStreamBeginCapture(c->stream, cudaStreamCaptureModeThreadLocal));
+    c->timing_capture = c->time_class != 0;
+    c->tev_used = 0;
     int rc = enqueue_step(c, a, Ly, mode, parity, launches);
+    c->timing_capture = false;
     cudaError_t e = cudaStreamEndCapture(c->stream, &graph);
     if (rc < 0) {
         if (graph) cudaGraphDestroy(graph);
@@ -1058,6 +1254,7 @@ static int get_step_graph(w4j_ctx *c, const CallArgs &a, const CallLayout &Ly, i
     cudaGraphDestroy(graph);
     if (e != cudaSuccess) return set_err(W4J_ERR_CUDA, "graph instantiate: %s", cudaGetErrorString(e));
     c->graphs[k] = exec;
+    c->graph_launches[k] = launches;
     *out = exec;
     per_step = launches;
     return 0;
@@ -1100,6 +1297,8 @@ static int decode_impl(w4j_ctx *c, const CallArgs &a, w4j_result *r) {
     c->last_ms = 0;
     c->last_steps = 0;
     c->last_launches = 0;
+    c->class_ms = 0;
+    c->class_launches = 0;
     if (a.max_tokens == 0) {  // the reference's loop body never runs: empty result
         for (int s = 0; s < a.S; ++s) {
             if (r->lens) r->lens[s] = 0;
@@ -1109,6 +1308,16 @@ static int decode_impl(w4j_ctx *c, const CallArgs &a, w4j_result *r) {
             if (r->no_speech_prob) r->no_speech_prob[s] = 0;
         }
         return W4J_OK;
+    }
+    TRY(grow_self(c, a.n_prompt + a.max_tokens - 1));
+    {
+        // the select kernels stage each sequence's history and beam table in shared memory
+        DecodeState probe = c->st;
+        probe.beam = a.beam;
+        const int sel = mode == MODE_BEAM ? SEL_BEAM : SEL_GREEDY;
+        if (select_smem_bytes(probe, sel, c->n_parts) > 227 * 1024)
+            return set_err(W4J_ERR_ARG, "beam %d with %d positions needs more shared memory than a block has",
+                           a.beam, a.n_prompt + a.max_tokens - 1);
     }
     const CallLayout Ly = call_layout(c, a.S, a.n_prompt, a.n_sup);
     TRY(prepare_call(c, a, Ly));
@@ -1131,6 +1340,15 @@ static int decode_impl(w4j_ctx *c, const CallArgs &a, w4j_result *r) {
         CUDA_TRY(cudaGraphLaunch(g, c->stream));
         launches += per;
         ++steps;
+        if (c->time_class) {  // in-chain durations of this step's launches of the timed class
+            CUDA_TRY(cudaStreamSynchronize(c->stream));
+            for (int i = 0; i < c->tev_pairs; ++i) {
+                float ms = 0.f;
+                CUDA_TRY(cudaEventElapsedTime(&ms, c->tev[2 * i], c->tev[2 * i + 1]));
+                c->class_ms += ms;
+            }
+            c->class_launches += c->tev_pairs;
+        }
         // every 16 steps look at a done-flag snapshot taken 16 steps earlier (no stall)
         if ((step & 15) == 0) {
             if (snapshot_pending && cudaEventQuery(c->ev1) == cudaSuccess) {
@@ -1270,6 +1488,21 @@ extern "C" int w4j_cancel(w4j_ctx *c) {
     return W4J_OK;
 }
 
+extern "C" int w4j_set_kernel_timing(w4j_ctx *c, int kernel_class) {
+    if (!c) return set_err(W4J_ERR_ARG, "null context");
+    if (kernel_class < 0 || kernel_class > KC_SELECT) return set_err(W4J_ERR_ARG, "kernel class %d", kernel_class);
+    std::lock_guard<std::mutex> g(c->mu);
+    c->time_class = kernel_class;
+    return W4J_OK;
+}
+
+extern "C" int w4j_kernel_timing(w4j_ctx *c, double *ms, long long *launches) {
+    if (!c) return set_err(W4J_ERR_ARG, "null context");
+    if (ms) *ms = c->class_ms;
+    if (launches) *launches = c->class_launches;
+    return W4J_OK;
+}
+
 extern "C" int w4j_last_timing(w4j_ctx *c, double *ms, int *steps, long long *launches) {
     if (!c) return set_err(W4J_ERR_ARG, "null context");
     if (ms) *ms = c->last_ms;
@@ -1292,6 +1525,7 @@ extern "C" int w4j_op_linear(w4j_ctx *c, const float *x, int M, int K, const voi
     // one weight row, one activation row and the LayerNorm parameters must fit a block's shared
     // memory (larger M runs in passes)
     if ((size_t)K * (2 + 3 * 4) > 200 * 1024) return set_err(W4J_ERR_ARG, "K too large");
+    std::lock_guard<std::mutex> lk(c->mu);  // the op scratch belongs to the context
     CUDA_TRY(cudaSetDevice(c->device));
     GemvArgs g;
     g.W.N = N;
@@ -1318,8 +1552,45 @@ extern "C" int w4j_op_linear(w4j_ctx *c, const float *x, int M, int K, const voi
     cudaStream_t s = stream ? reinterpret_cast<cudaStream_t>(stream) : 0;
     cudaError_t e = cudaErrorNotSupported;
     alignas(64) unsigned char map[128];
-    if (c->tc_gemm && g.W.type == WT_F16 && M >= 16 && make_tmap_f16_rows(map, W, N, K))
-        e = launch_gemm_tc(g, map, c->sm_count, s, false);
+    if (c->tc_gemm && M >= 16) {
+        if (g.W.type == WT_F16 && gemm_tc_supported(g, c->sm_count) && make_tmap_f16_rows(map, W, N, K)) {
+            if (gemm_tc_staged(g)) {
+                // the staged activations in the context's op scratch (grown on demand)
+                const size_t need = (size_t)act_hilo_rows(M) * K;
+                if (need > c->op_hilo_n) {
+                    CUDA_TRY(cudaStreamSynchronize(s));
+                    dfree(c, c->op_hilo);
+                    c->op_hilo = nullptr;
+                    c->op_hilo_n = 0;
+                    TRY(dalloc(c, &c->op_hilo, need));
+                    c->op_hilo_n = need;
+                }
+                alignas(64) unsigned char bmap[128];
+                if (make_tmap_f16_box(bmap, c->op_hilo, act_hilo_rows(M), K, 256)) {
+                    e = launch_act_hilo(g, c->op_hilo, s, false);
+                    if (e == cudaSuccess) e = launch_gemm_tc(g, map, bmap, c->sm_count, s, false);
+                }
+            } else {
+                e = launch_gemm_tc(g, map, nullptr, c->sm_count, s, false);
+            }
+        } else if (g.W.type == WT_Q8 && N % 128 == 0 && K % 64 == 0 && make_tmap_i8_rows(map, W, N, K)) {
+            // tiled scales in the context's op scratch (grown on demand, stream-ordered reuse)
+            const size_t need = (size_t)N * (K / 32);
+            if (need > c->op_st_n) {
+                CUDA_TRY(cudaStreamSynchronize(s));
+                dfree(c, c->op_st);
+                c->op_st = nullptr;
+                c->op_st_n = 0;
+                TRY(dalloc(c, &c->op_st, need));
+                c->op_st_n = need;
+            }
+            g.W.st = c->op_st;
+            if (gemm_tc_supported(g, c->sm_count)) {
+                CUDA_TRY(launch_q8_tile_scales(g.W.s, N, K, c->op_st, s));
+                e = launch_gemm_tc(g, map, nullptr, c->sm_count, s, false);
+            }
+        }
+    }
     if (e == cudaErrorNotSupported) e = launch_gemv(g, s, false);
     CUDA_TRY(e);
     return W4J_OK;
@@ -1333,11 +1604,27 @@ extern "C" int w4j_q8_0_repack(const void *src, int N, int K, void *dst, void *s
     return W4J_OK;
 }
 
+// Test hook (w4j_test_withhold_logits_copies): op-level vocabulary passes that still withhold.
+static std::atomic<int> g_withhold_logits{0};
+
+static int take_withhold() {
+    int n = g_withhold_logits.load();
+    while (n > 0 && !g_withhold_logits.compare_exchange_weak(n, n - 1)) {
+    }
+    return n > 0;
+}
+
+extern "C" int w4j_test_withhold_logits_copies(int n_launches) {
+    if (n_launches < 0) return set_err(W4J_ERR_ARG, "n_launches must be >= 0");
+    g_withhold_logits.store(n_launches);
+    return W4J_OK;
+}
+
 extern "C" int w4j_op_logits_argmax(w4j_ctx *c, const float *x, int M, const void *E, int V, const float *ln_g,
                                     const float *ln_b, int32_t *out_token, double *out_logprob, void *stream) {
     if (!c || !x || !E || !ln_g || !ln_b || !out_token || !out_logprob)
         return set_err(W4J_ERR_ARG, "w4j_op_logits_argmax: null argument");
-    if (M < 1 || M > c->M_max) return set_err(W4J_ERR_ARG, "M %d out of [1, %d]", M, c->M_max);
+    if (M < 1 || M > c->Mbuf) return set_err(W4J_ERR_ARG, "M %d out of [1, %d]", M, c->Mbuf);
     if (V < 1 || V > c->V) return set_err(W4J_ERR_ARG, "V %d out of [1, %d]", V, c->V);
     CUDA_TRY(cudaSetDevice(c->device));
     std::lock_guard<std::mutex> g(c->mu);
@@ -1353,6 +1640,8 @@ extern "C" int w4j_op_logits_argmax(w4j_ctx *c, const float *x, int M, const voi
     la.V = V;
     la.d = c->d;
     la.part = c->logit_part;
+    la.err = c->op_err;
+    la.withhold = take_withhold();
     const int P = logits_parts_for(V, c->sm_count);
     cudaStream_t s = stream ? reinterpret_cast<cudaStream_t>(stream) : 0;
     alignas(64) unsigned char map[128];
@@ -1372,6 +1661,7 @@ extern "C" int w4j_op_logits_argmax(w4j_ctx *c, const float *x, int M, const voi
     if (e == cudaErrorNotSupported) e = launch_logits(la, P, s, false);
     CUDA_TRY(e);
     CUDA_TRY(launch_argmax_merge(c->logit_part, P, M, out_token, out_logprob, s));
+    CUDA_TRY(launch_err_apply(M, out_token, out_logprob, c->op_err, s));
     return W4J_OK;
 }
 
@@ -1392,6 +1682,7 @@ struct NoAllocDevice {
     float *part = nullptr;
     int *err = nullptr;
     int sms = 0;
+    bool tc = true;  // tcgen05 vocabulary pass (off with W4J_NO_TC_LOGITS=1, as for a context)
 };
 NoAllocDevice g_noalloc_dev[kNoAllocMaxDevices];
 
@@ -1403,6 +1694,7 @@ void noalloc_setup(int device, NoAllocDevice &nd) {
                  what + ": " + cudaGetErrorString(e);
     };
     cudaError_t e;
+    if (const char *ev = getenv("W4J_NO_TC_LOGITS")) nd.tc = ev[0] == '0';
     if ((e = gemv_prepare()) != cudaSuccess) return fail(e, "kernel attributes");
     if ((e = logits_tc_prepare()) != cudaSuccess) return fail(e, "kernel attributes");
     if ((e = cudaDeviceGetAttribute(&nd.sms, cudaDevAttrMultiProcessorCount, device)) != cudaSuccess)
@@ -1456,10 +1748,11 @@ extern "C" int w4j_op_logits_argmax_noalloc(int device, const float *x, int M, i
     la.d = d;
     la.part = nd.part;
     la.err = nd.err;
+    la.withhold = take_withhold();
     cudaStream_t s = stream ? reinterpret_cast<cudaStream_t>(stream) : 0;
     alignas(64) unsigned char map[128];
     cudaError_t e = cudaErrorNotSupported;
-    if (make_tmap_f16_rows(map, E, V, d)) e = launch_logits_tc(la, map, P, s, false);
+    if (nd.tc && make_tmap_f16_rows(map, E, V, d)) e = launch_logits_tc(la, map, P, s, false);
     if (e == cudaErrorNotSupported) e = launch_logits(la, P, s, false);
     CUDA_TRY(e);
     CUDA_TRY(launch_argmax_merge_status(nd.part, P, M, out_token, out_logprob, nd.err, s));

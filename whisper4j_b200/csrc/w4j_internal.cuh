@@ -30,6 +30,7 @@ struct DMat {
     const __half *h = nullptr;   // WT_F16: [N][K]
     const int8_t *q = nullptr;   // WT_Q8: [N][K]
     const __half *s = nullptr;   // WT_Q8: [N][K/32]
+    const __half *st = nullptr;  // WT_Q8 for the tensor-core projections: scales [N/128][K/64][128][2]
 };
 
 // ---------------------------------------------------------------------------
@@ -49,7 +50,11 @@ struct GemvArgs {
     DMat E;
     const float *pos_emb = nullptr;    // [n_text_ctx][d]
     const int *tok = nullptr;          // [M]
-    const int *pos = nullptr;          // [M] positions (also the self-cache row written by OUT_QKV)
+    const int *pos = nullptr;          // [M] self-cache row written by OUT_QKV (the sequence position)
+    // positional-embedding row of each sequence: pe_pos[m] when given, else min(pos[m], pe_rows - 1)
+    // (WhisperDecoder.java:72 clamps the offset so the table is never read past n_text_ctx - 1)
+    const int *pe_pos = nullptr;       // [M] or null
+    int pe_rows = 0;                   // rows of the positional table (n_text_ctx)
     float *x_out = nullptr;            // [M][d]
     // outputs
     int out_mode = OUT_STORE;
@@ -77,6 +82,10 @@ struct AttnArgs {
     const int *seq_slot = nullptr;     // self: [groups] own slot
     const int *table = nullptr;        // self: [groups][n_ctx] slot per position (null: own slot)
     const int *pos = nullptr;          // self: [groups] position of the newest row (kv len = pos+1)
+    const int *kv_len = nullptr;       // self: [groups] keys to attend (overrides pos + 1) or null
+    // self: [groups] (lo, hi): keys lo <= j < hi are masked (-inf), the reference's causal mask
+    // applied from key column 0 on a multi-token pass (Tensor.java:622-640); null = no mask
+    const int2 *mask = nullptr;
     const int *stream_of_group = nullptr;  // cross: [groups] stream index into the cross cache
     int self_prefetch = 0;             // self rows before the newest may be staged before the wait
     int nq = 1;                        // queries per group (cross: beams of one stream)
@@ -116,6 +125,7 @@ struct LogitsArgs {
     float *ns_value = nullptr;         // [M]
     const int *active = nullptr;       // [M]
     int *err = nullptr;                // device error word
+    int withhold = 0;                  // test hook: issue no weight copies, so the bounded waits run out
 };
 
 // ---------------------------------------------------------------------------
@@ -202,6 +212,13 @@ __device__ __forceinline__ bool mbar_wait(uint64_t *b, unsigned parity, int *err
 }
 
 
+// Positional-embedding row of sequence m of a projection with the embedding prologue.
+__device__ __forceinline__ int pe_row(const GemvArgs &a, int m) {
+    if (a.pe_pos) return a.pe_pos[m];
+    const int p = a.pos[m];
+    return a.pe_rows > 0 && p > a.pe_rows - 1 ? a.pe_rows - 1 : p;
+}
+
 __device__ __forceinline__ float warp_sum(float v) {
 #pragma unroll
     for (int o = 16; o > 0; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
@@ -255,11 +272,15 @@ size_t logits_smem_bytes(int M, int V, int d, int n_parts);
 enum SelectMode : int { SEL_GREEDY = 0, SEL_SAMPLE = 1, SEL_BEAM_INIT = 2, SEL_BEAM = 3 };
 cudaError_t launch_select(const DecodeState &st, int mode, int parity, const float *part, int n_parts,
                           float *masked_logits, int step, cudaStream_t s, bool pdl);
+// dynamic shared memory a select launch of `mode` needs (history and beam-table staging)
+size_t select_smem_bytes(const DecodeState &st, int mode, int P);
 cudaError_t launch_nsp(const DecodeState &st, const float *ns_part, int n_parts, const float *ns_value,
                        cudaStream_t s, bool pdl);
 cudaError_t launch_init_masks(const DecodeState &st, int beam_mode, cudaStream_t s);
 cudaError_t launch_finalize(const DecodeState &st, int beam_mode, int parity, cudaStream_t s);
 cudaError_t launch_argmax_merge(const float *part, int n_parts, int M, int32_t *tok, double *lp, cudaStream_t s);
+// after a merge: outputs of all M rows become -1 / NaN if `err` is set, and `err` is cleared
+cudaError_t launch_err_apply(int M, int32_t *tok, double *lp, int *err, cudaStream_t s);
 // single-block merge that also reports and clears the device error word `err`
 cudaError_t launch_argmax_merge_status(const float *part, int n_parts, int M, int32_t *tok, double *lp, int *err,
                                        cudaStream_t s);
@@ -274,15 +295,27 @@ cudaError_t logits_tc_prepare();
 // tcgen05 vocabulary logits (f16 embedding, M <= 32); cudaErrorNotSupported outside its range
 cudaError_t launch_logits_tc(const LogitsArgs &a, const void *tmap, int n_parts, cudaStream_t s, bool pdl);
 bool make_tmap_f16_rows(void *map_out, const void *base, int rows, int cols);  // 128-byte map
+bool make_tmap_i8_rows(void *map_out, const void *base, int rows, int cols);   // [128 x 64] int8 boxes
+// Q8_0 scales [N][K/32] -> the tile layout [N/128][K/64][128][2] of the tensor-core projections
+cudaError_t launch_q8_tile_scales(const __half *s, int N, int K, __half *st, cudaStream_t stream);
 cudaError_t gemm_tc_prepare();
 cudaError_t xkv_tc_prepare();
 // tcgen05 cross K/V projection of one stream and layer (f16 Wk / Wv, d a multiple of 128); kmap /
 // vmap are make_tmap_f16_rows maps of Wk and Wv; cudaErrorNotSupported outside its range
 cudaError_t launch_cross_kv_tc(const float *xa, int A, int d, const void *kmap, const void *vmap, const float *bk,
                                const float *bv, __half *kout, __half *vout, int *err, cudaStream_t s);
-// tcgen05 projection (f16 weights, 16 <= M <= 128) with the GEMV's input modes and epilogues;
-// `tmap` is make_tmap_f16_rows of a.W; cudaErrorNotSupported outside its range
-cudaError_t launch_gemm_tc(const GemvArgs &a, const void *tmap, int sms, cudaStream_t s, bool pdl);
+// tcgen05 projection (M >= 16; f16 weights, or Q8_0 with tiled scales and N a multiple of 128) with
+// the GEMV's input modes and epilogues; `tmap` is make_tmap_f16_rows of a.W.h (f16) or
+// make_tmap_i8_rows of a.W.q (Q8_0); cudaErrorNotSupported outside its range
+// More than 128 rows (f16): `bmap` is make_tmap_f16_rows(…, rows 256) of the activations staged by
+// launch_act_hilo beforehand ([act_hilo_rows(M)][K] f16), read as [256 x 64] boxes.
+cudaError_t launch_gemm_tc(const GemvArgs &a, const void *tmap, const void *bmap, int sms, cudaStream_t s, bool pdl);
+bool gemm_tc_staged(const GemvArgs &a);  // the projection reads staged activations (launch_act_hilo first)
+bool gemm_tc_supported(const GemvArgs &a, int sms);  // the tensor-core kernel takes this projection
+int act_hilo_rows(int M);
+cudaError_t launch_act_hilo(const GemvArgs &a, __half *out, cudaStream_t s, bool pdl);
+// tensor map of a row-major f16 matrix read in [box_rows x 64 cols] boxes, 128-byte swizzle
+bool make_tmap_f16_box(void *map_out, const void *base, int rows, int cols, int box_rows);
 cudaError_t select_prepare();
 cudaError_t attn_prepare();
 cudaError_t launch_f32_to_f16(const float *src, __half *dst, size_t n, cudaStream_t s);

@@ -228,6 +228,18 @@ class WhisperDecoder:
     def cancel(self):
         check(lib().w4j_cancel(self._ctx))
 
+    def kernel_timing(self, kernel_class: int):
+        """In-chain device time of one kernel class over the next decode call: set the class (1 projections,
+        2 self-attention, 3 cross-attention, 4 logits, 5 selection; 0 off), decode, then read
+        ``kernel_times()``."""
+        check(lib().w4j_set_kernel_timing(self._ctx, int(kernel_class)))
+
+    def kernel_times(self):
+        ms = ctypes.c_double()
+        n = ctypes.c_longlong()
+        check(lib().w4j_kernel_timing(self._ctx, ctypes.byref(ms), ctypes.byref(n)))
+        return ms.value, n.value
+
     def last_timing(self):
         ms = ctypes.c_double()
         steps = ctypes.c_int()
