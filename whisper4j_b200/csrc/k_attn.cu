@@ -17,6 +17,7 @@
 // so the result is deterministic and no partial goes through global memory.  Self-attention
 // rows are gathered through the beam table (position -> physical slot), which replaces the
 // reference's per-beam cache copies (WhisperDecoder.java:343-361).
+#include "attn_tile.cuh"
 #include "tc_common.cuh"
 #include "w4j_internal.cuh"
 
@@ -36,26 +37,6 @@ __device__ __forceinline__ void cp_async_wait_all() { asm volatile("cp.async.wai
 __device__ __forceinline__ void cp_async_commit() { asm volatile("cp.async.commit_group;" ::: "memory"); }
 template <int N>
 __device__ __forceinline__ void cp_async_wait_group() { asm volatile("cp.async.wait_group %0;" ::"n"(N) : "memory"); }
-// warp-level tensor-core tiles (m16n8k16, f16 inputs, f32 accumulation) and their fragments
-__device__ __forceinline__ void ldsm_x4(uint32_t (&r)[4], const void *p) {
-    asm volatile("ldmatrix.sync.aligned.m8n8.x4.shared.b16 {%0,%1,%2,%3}, [%4];"
-                 : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3])
-                 : "r"(smem_u32(p)));
-}
-__device__ __forceinline__ void ldsm_x4_t(uint32_t (&r)[4], const void *p) {
-    asm volatile("ldmatrix.sync.aligned.m8n8.x4.trans.shared.b16 {%0,%1,%2,%3}, [%4];"
-                 : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3])
-                 : "r"(smem_u32(p)));
-}
-__device__ __forceinline__ void ldsm_x2(uint32_t (&r)[2], const void *p) {
-    asm volatile("ldmatrix.sync.aligned.m8n8.x2.shared.b16 {%0,%1}, [%2];" : "=r"(r[0]), "=r"(r[1]) : "r"(smem_u32(p)));
-}
-__device__ __forceinline__ void mma_16816(float (&c)[4], const uint32_t (&a)[4], const uint32_t (&b)[2]) {
-    asm volatile(
-        "mma.sync.aligned.m16n8k16.row.col.f32.f16.f16.f32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, {%0,%1,%2,%3};"
-        : "+f"(c[0]), "+f"(c[1]), "+f"(c[2]), "+f"(c[3])
-        : "r"(a[0]), "r"(a[1]), "r"(a[2]), "r"(a[3]), "r"(b[0]), "r"(b[1]));
-}
 __device__ __forceinline__ void cluster_sync() {
     asm volatile("barrier.cluster.arrive.release.aligned;\n\tbarrier.cluster.wait.acquire.aligned;" ::: "memory");
 }
@@ -385,88 +366,6 @@ __global__ void __launch_bounds__(kAttnThreads) k_attn(AttnArgs a) {
 // not depend on timing.  Needs n_audio > 128 (a tile for each warpgroup in every pair: both meet
 // at the block barrier that ends a pair).
 // ---------------------------------------------------------------------------
-constexpr int kStreamThreads = 2 * kAttnThreads;
-constexpr int kPwPad = 24;  // halves per row of a warp's P^T block (48 B: conflict-free ldmatrix)
-constexpr int kStreamBufs = 3;                            // tile buffers per warpgroup
-constexpr int kStreamTile = 2 * kAttnKeyTile * kHeadDim;  // halves of one K tile + one V tile
-constexpr unsigned kHalfTileBytes = kAttnKeyTile * kHeadDim * 2;  // one K (or V) tile: 16 KB
-// offset (halves) of 16-byte chunk c of row r in a swizzled 128-byte-row tile
-__device__ __forceinline__ int swz(int r, int c) { return r * kHeadDim + ((c ^ (r & 7)) << 3); }
-
-// One warp's 16 keys [16 w, 16 w + 16) of a 128-key tile, online softmax kept per warp: m / l
-// are the running max / denominator of queries 2 tq and 2 tq + 1, of[4][4] the O^T fragments.
-template <int NQ>
-__device__ __forceinline__ void tile_warp(const __half *sk, const __half *sv, int nk, const __half (*qh)[kHeadDim + 8],
-                                          __half (*pw)[kPwPad], float (&m)[2], float (&l)[2], float (&of)[4][4],
-                                          int gwarp, int lane) {
-    const int g = lane >> 2, tq = lane & 3, kb = 16 * gwarp;
-    const float scale = 0.125f;  // (float)(1 / sqrt(64))
-    float sc[4] = {0.f, 0.f, 0.f, 0.f};
-    if (kb < nk) {
-#pragma unroll
-        for (int kk = 0; kk < 4; ++kk) {
-            uint32_t af[4], bf[2];
-            ldsm_x4(af, &sk[swz(kb + (lane & 15), 2 * kk + (lane >> 4))]);
-            ldsm_x2(bf, &qh[lane & 7][16 * kk + ((lane >> 3) & 1) * 8]);
-            mma_16816(sc, af, bf);
-        }
-    }
-    // c0: (key kb+g, query 2tq), c1: (kb+g, 2tq+1), c2: (kb+g+8, 2tq), c3: (kb+g+8, 2tq+1)
-    const int q0 = 2 * tq, q1 = 2 * tq + 1;
-    const bool k0ok = kb + g < nk, k1ok = kb + g + 8 < nk;
-    sc[0] = (k0ok && q0 < NQ) ? sc[0] * scale : -INFINITY;
-    sc[1] = (k0ok && q1 < NQ) ? sc[1] * scale : -INFINITY;
-    sc[2] = (k1ok && q0 < NQ) ? sc[2] * scale : -INFINITY;
-    sc[3] = (k1ok && q1 < NQ) ? sc[3] * scale : -INFINITY;
-    float mx0 = fmaxf(sc[0], sc[2]), mx1 = fmaxf(sc[1], sc[3]);
-#pragma unroll
-    for (int o = 4; o < 32; o <<= 1) {
-        mx0 = fmaxf(mx0, __shfl_xor_sync(0xffffffffu, mx0, o));
-        mx1 = fmaxf(mx1, __shfl_xor_sync(0xffffffffu, mx1, o));
-    }
-    const float mn0 = fmaxf(m[0], mx0), mn1 = fmaxf(m[1], mx1);
-    const float p0 = sc[0] == -INFINITY ? 0.f : __expf(sc[0] - mn0);
-    const float p1 = sc[1] == -INFINITY ? 0.f : __expf(sc[1] - mn1);
-    const float p2 = sc[2] == -INFINITY ? 0.f : __expf(sc[2] - mn0);
-    const float p3 = sc[3] == -INFINITY ? 0.f : __expf(sc[3] - mn1);
-    float sm0 = p0 + p2, sm1 = p1 + p3;
-#pragma unroll
-    for (int o = 4; o < 32; o <<= 1) {
-        sm0 += __shfl_xor_sync(0xffffffffu, sm0, o);
-        sm1 += __shfl_xor_sync(0xffffffffu, sm1, o);
-    }
-    const float al0 = m[0] == -INFINITY ? 0.f : __expf(m[0] - mn0);
-    const float al1 = m[1] == -INFINITY ? 0.f : __expf(m[1] - mn1);
-    l[0] = l[0] * al0 + sm0;
-    l[1] = l[1] * al1 + sm1;
-    m[0] = mn0;
-    m[1] = mn1;
-#pragma unroll
-    for (int mt = 0; mt < 4; ++mt) {
-        of[mt][0] *= al0;
-        of[mt][1] *= al1;
-        of[mt][2] *= al0;
-        of[mt][3] *= al1;
-    }
-    if (kb < nk) {
-        // O^T (16 dims x 8 queries, 4 tiles) += V^T (16 dims x 16 keys) . P^T (16 keys x 8 queries)
-        pw[q0][g] = __float2half_rn(p0);
-        pw[q1][g] = __float2half_rn(p1);
-        pw[q0][g + 8] = __float2half_rn(p2);
-        pw[q1][g + 8] = __float2half_rn(p3);
-        __syncwarp();
-        uint32_t bf[2];
-        ldsm_x2(bf, &pw[lane & 7][((lane >> 3) & 1) * 8]);
-#pragma unroll
-        for (int mt = 0; mt < 4; ++mt) {
-            uint32_t af[4];
-            ldsm_x4_t(af, &sv[swz(kb + (lane & 7) + ((lane >> 4) & 1) * 8, 2 * mt + ((lane >> 3) & 1))]);
-            mma_16816(of[mt], af, bf);
-        }
-        __syncwarp();  // pw is rewritten by the next tile
-    }
-}
-
 template <int NQ>
 __global__ void __launch_bounds__(kStreamThreads, 1)
     k_attn_stream(AttnArgs a, const __grid_constant__ CUtensorMap kmap, const __grid_constant__ CUtensorMap vmap) {
@@ -620,6 +519,228 @@ __global__ void __launch_bounds__(kStreamThreads, 1)
             mbar_wait(&full[wg][i % kStreamBufs], (unsigned)((i / kStreamBufs) & 1), nullptr);
 }
 
+// ---------------------------------------------------------------------------
+// Streaming self-attention for many sequences without beam tables (batched greedy steps): each
+// warpgroup owns whole (sequence, head) pairs — pairs wg + 2 b, wg + 2 b + 2 G, ... of block b —
+// and streams their 128-key tiles of the self cache (viewed as [rows][64] f16: one contiguous
+// run of n_ctx rows per (slot, layer, head)) through three buffers with TMA, one thread of the
+// warpgroup requesting the next tile as soon as all eight warps released a buffer.  The pairs
+// of a step all have the same length, so the round-robin split is balanced.  The newest row of
+// every sequence is written by the kernel before, so the copies start after the grid wait.
+// Warp states (16 keys of each tile) are combined per pair in a fixed order, as in the
+// cross-attention kernel.  Needs no mask and no explicit key counts (the decode step's case).
+// ---------------------------------------------------------------------------
+// CROSS: the same over the encoder K / V (n_audio keys per pair, NQ queries: the beams of a stream);
+// those rows are constant during the decode, so the first copies start before the grid wait.
+template <int NQ, bool CROSS>
+__global__ void __launch_bounds__(kStreamThreads, 1)
+    k_attn_pairs(AttnArgs a, const __grid_constant__ CUtensorMap kmap, const __grid_constant__ CUtensorMap vmap) {
+    extern __shared__ __align__(1024) unsigned char sraw[];
+    __half *sbuf = reinterpret_cast<__half *>(sraw + ((1024u - (smem_u32(sraw) & 1023u)) & 1023u));
+    __shared__ __align__(8) uint64_t full[2][kStreamBufs], empty[2][kStreamBufs];
+    __shared__ __align__(16) __half qh[2][8][kHeadDim + 8];
+    __shared__ __align__(16) __half pw[2 * kWarps][8][kPwPad];
+    __shared__ float wm[2 * kWarps][8], wl[2 * kWarps][8];
+    __shared__ __align__(16) float red[2 * kWarps][NQ * kHeadDim];
+    const int tid = threadIdx.x, wg = tid / kAttnThreads, gtid = tid % kAttnThreads;
+    const int warp = tid >> 5, gwarp = gtid >> 5, lane = tid & 31, g = lane >> 2, tq = lane & 3;
+    const int H = a.n_head, n_pairs = a.groups * H;
+    const int stride = 2 * (int)gridDim.x, first = 2 * (int)blockIdx.x + wg;
+    __half *wbuf = sbuf + (size_t)wg * kStreamBufs * kStreamTile;
+    const bool producer = gwarp == 0 && lane == 0;
+    // keys of a pair's group: the encoder rows, or the sequence's positions 0 .. pos
+    auto len_of = [&](int grp) { return CROSS ? a.n_audio : a.pos[grp] + 1; };
+    auto tiles_of = [&](int pair) {
+        const int grp = pair / H;
+        return (a.active && !a.active[grp]) ? 0 : (len_of(grp) + kAttnKeyTile - 1) / kAttnKeyTile;
+    };
+    if (tid < 2 * kStreamBufs) {
+        mbar_init(&full[tid / kStreamBufs][tid % kStreamBufs], 1);
+        mbar_init(&empty[tid / kStreamBufs][tid % kStreamBufs], kWarps);
+    }
+    fence_mbar_init();
+    __syncthreads();
+    if (!CROSS) {
+        pdl_trigger();
+        pdl_wait();
+    }
+    // producer cursor: the next (pair, tile) to request, in the consumers' order
+    int ppair = first, ptile = 0, pn = ppair < n_pairs ? tiles_of(ppair) : 0;
+    auto skip_empty = [&]() {
+        while (ppair < n_pairs && ptile >= pn) {
+            ppair += stride;
+            ptile = 0;
+            pn = ppair < n_pairs ? tiles_of(ppair) : 0;
+        }
+    };
+    int issued = 0;
+    auto issue = [&]() {  // request the cursor's tile into buffer issued % 3
+        const int grp = ppair / H, head = ppair - grp * H, b = issued % kStreamBufs;
+        const int y = CROSS ? ((a.stream_of_group[grp] * a.n_layer + a.layer) * H + head) * a.n_audio + ptile * kAttnKeyTile
+                            : ((a.seq_slot[grp] * a.n_layer + a.layer) * H + head) * a.n_ctx + ptile * kAttnKeyTile;
+        __half *tk = wbuf + (size_t)b * kStreamTile;
+        mbar_expect_tx(&full[wg][b], 2 * kHalfTileBytes);
+        tma_load_2d(tk, &kmap, 0, y, &full[wg][b]);
+        tma_load_2d(tk + kAttnKeyTile * kHeadDim, &vmap, 0, y, &full[wg][b]);
+        ++issued;
+        ++ptile;
+        skip_empty();
+    };
+    if (producer) {
+        skip_empty();
+        for (int i = 0; i < kStreamBufs && ppair < n_pairs; ++i) issue();
+    }
+    if (CROSS) {  // the queries come from the kernel before
+        pdl_trigger();
+        pdl_wait();
+    }
+    float m[2], l[2], of[4][4];
+    bool ok = true;
+    int item = 0;
+    for (int pair = first; pair < n_pairs; pair += stride) {
+        const int nt = tiles_of(pair);
+        if (nt == 0) continue;
+        const int grp = pair / H, head = pair - grp * H, len = len_of(grp);
+        if (gtid < 8 * kHeadDim / 4) {  // this pair's queries as f16; rows >= NQ zero
+            const int qi = gtid / (kHeadDim / 4), c = gtid % (kHeadDim / 4);
+            float4 v = make_float4(0.f, 0.f, 0.f, 0.f);
+            if (qi < NQ) v = reinterpret_cast<const float4 *>(a.q + (size_t)(grp * NQ + qi) * a.d + head * kHeadDim)[c];
+            const __half2 h0 = __floats2half2_rn(v.x, v.y), h1 = __floats2half2_rn(v.z, v.w);
+            *reinterpret_cast<uint2 *>(&qh[wg][qi][4 * c]) =
+                make_uint2(*reinterpret_cast<const uint32_t *>(&h0), *reinterpret_cast<const uint32_t *>(&h1));
+        }
+        m[0] = m[1] = -INFINITY;
+        l[0] = l[1] = 0.f;
+#pragma unroll
+        for (int mt = 0; mt < 4; ++mt) of[mt][0] = of[mt][1] = of[mt][2] = of[mt][3] = 0.f;
+        group_sync(1 + wg);  // qh is read by every warp of the warpgroup
+        for (int j = 0; j < nt; ++j, ++item) {
+            const int b = item % kStreamBufs;
+            const int nk = min(kAttnKeyTile, len - j * kAttnKeyTile);
+            __half *sk = wbuf + (size_t)b * kStreamTile, *sv = sk + kAttnKeyTile * kHeadDim;
+            ok = mbar_wait(&full[wg][b], (unsigned)((item / kStreamBufs) & 1), a.err) && ok;
+            if (ok) {
+                // rows past the keys meet zero probabilities in P.V and must be finite: each warp
+                // clears the V rows of its own 16 keys past nk (the copy has completed)
+                const int kb = 16 * gwarp;
+                if (nk < kAttnKeyTile && kb < nk && kb + 16 > nk) {
+                    for (int c = lane; c < (kb + 16 - nk) * 8; c += 32)
+                        *reinterpret_cast<uint4 *>(&sv[(nk + (c >> 3)) * kHeadDim + (c & 7) * 8]) = make_uint4(0u, 0u, 0u, 0u);
+                    __syncwarp();
+                }
+                tile_warp<NQ>(sk, sv, nk, qh[wg], pw[warp], m, l, of, gwarp, lane);
+            }
+            fence_proxy_async();  // this warp's generic accesses to the buffer precede the next copy into it
+            __syncwarp();
+            if (lane == 0) mbar_arrive(&empty[wg][b]);
+            if (producer && ppair < n_pairs) {
+                if (mbar_wait(&empty[wg][b], (unsigned)((item / kStreamBufs) & 1), a.err)) issue();
+                else {
+                    ok = false;
+                    ppair = n_pairs;  // request nothing more
+                }
+            }
+            __syncwarp();
+        }
+        // the pair's eight warp states, combined in warp order
+        if (g == 0) {
+            wm[warp][2 * tq] = m[0];
+            wm[warp][2 * tq + 1] = m[1];
+            wl[warp][2 * tq] = l[0];
+            wl[warp][2 * tq + 1] = l[1];
+        }
+#pragma unroll
+        for (int mt = 0; mt < 4; ++mt) {
+            const int q0 = 2 * tq, q1 = 2 * tq + 1, d0 = 16 * mt + g;
+            if (q0 < NQ) {
+                red[warp][q0 * kHeadDim + d0] = of[mt][0];
+                red[warp][q0 * kHeadDim + d0 + 8] = of[mt][2];
+            }
+            if (q1 < NQ) {
+                red[warp][q1 * kHeadDim + d0] = of[mt][1];
+                red[warp][q1 * kHeadDim + d0 + 8] = of[mt][3];
+            }
+        }
+        group_sync(1 + wg);
+        for (int pidx = gtid; pidx < NQ * kHeadDim; pidx += kAttnThreads) {
+            const int qi = pidx / kHeadDim, dd = pidx % kHeadDim;
+            float M = -INFINITY;
+#pragma unroll
+            for (int w = 0; w < kWarps; ++w) M = fmaxf(M, wm[wg * kWarps + w][qi]);
+            float num = 0.f, den = 0.f;
+#pragma unroll
+            for (int w = 0; w < kWarps; ++w)
+                if (wm[wg * kWarps + w][qi] != -INFINITY) {
+                    const float wt = __expf(wm[wg * kWarps + w][qi] - M);
+                    num = fmaf(wt, red[wg * kWarps + w][pidx], num);
+                    den = fmaf(wt, wl[wg * kWarps + w][qi], den);
+                }
+            if (ok) a.out[(size_t)(grp * NQ + qi) * a.d + head * kHeadDim + dd] = num / den;
+        }
+        group_sync(1 + wg);  // wm, wl, red and qh of this warpgroup are free
+    }
+    // after a wait that ran out: the copies still in flight land before the block exits
+    if (!ok && producer)
+        for (int i = issued > kStreamBufs ? issued - kStreamBufs : 0; i < issued; ++i)
+            mbar_wait(&full[wg][i % kStreamBufs], (unsigned)((i / kStreamBufs) & 1), nullptr);
+}
+
+bool attn_self_stream_pays(const AttnArgs &a, int sms) {
+    return !a.cross && !a.table && !a.mask && !a.kv_len && a.nq == 1 && (long long)a.groups * a.n_head > 2LL * sms;
+}
+
+// Cross-attention with a warpgroup per pair pays once every warpgroup has several pairs (the
+// pair-end block barrier of k_attn_stream then costs more than the last round's imbalance).
+bool attn_pairs_pays(const AttnArgs &a, int sms) {
+    // (up to 5 queries per pair: the warp sums of 8 would not fit beside the six tile buffers)
+    return a.cross && a.nq <= 5 && a.n_audio > kAttnKeyTile && (long long)a.groups * a.n_head >= 8LL * sms;
+}
+
+cudaError_t launch_attn_pairs(const AttnArgs &a, const void *kmap, const void *vmap, int sms, cudaStream_t s, bool pdl) {
+    if (a.groups <= 0) return cudaSuccess;
+    if (!a.cross || a.nq < 1 || a.nq > 5 || !kmap || !vmap) return cudaErrorInvalidValue;
+    const long long pairs = (long long)a.groups * a.n_head;
+    const long long want = (pairs + 1) / 2;
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = dim3((unsigned)(want < sms ? want : sms));
+    cfg.blockDim = dim3(kStreamThreads);
+    cfg.dynamicSmemBytes = 2 * kStreamBufs * (size_t)kStreamTile * sizeof(__half) + 1024;
+    cfg.stream = s;
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[0].val.programmaticStreamSerializationAllowed = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = pdl ? 1 : 0;
+    const CUtensorMap &km = *reinterpret_cast<const CUtensorMap *>(kmap), &vm = *reinterpret_cast<const CUtensorMap *>(vmap);
+    switch (a.nq) {
+        case 1: return cudaLaunchKernelEx(&cfg, k_attn_pairs<1, true>, a, km, vm);
+        case 2: return cudaLaunchKernelEx(&cfg, k_attn_pairs<2, true>, a, km, vm);
+        case 3: return cudaLaunchKernelEx(&cfg, k_attn_pairs<3, true>, a, km, vm);
+        case 4: return cudaLaunchKernelEx(&cfg, k_attn_pairs<4, true>, a, km, vm);
+        default: return cudaLaunchKernelEx(&cfg, k_attn_pairs<5, true>, a, km, vm);
+    }
+}
+
+cudaError_t launch_attn_self_stream(const AttnArgs &a, const void *kmap, const void *vmap, int sms, cudaStream_t s,
+                                    bool pdl) {
+    if (a.groups <= 0) return cudaSuccess;
+    if (a.cross || a.table || a.mask || a.kv_len || a.nq != 1 || !kmap || !vmap) return cudaErrorInvalidValue;
+    const long long pairs = (long long)a.groups * a.n_head;
+    const long long want = (pairs + 1) / 2;
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = dim3((unsigned)(want < sms ? want : sms));
+    cfg.blockDim = dim3(kStreamThreads);
+    cfg.dynamicSmemBytes = 2 * kStreamBufs * (size_t)kStreamTile * sizeof(__half) + 1024;
+    cfg.stream = s;
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[0].val.programmaticStreamSerializationAllowed = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = pdl ? 1 : 0;
+    return cudaLaunchKernelEx(&cfg, k_attn_pairs<1, false>, a, *reinterpret_cast<const CUtensorMap *>(kmap),
+                              *reinterpret_cast<const CUtensorMap *>(vmap));
+}
+
 // Key splits of one launch: up to kMaxSplits (one cluster); tiles each block stages.
 int attn_max_splits(int) { return kMaxSplits; }
 static int attn_tiles(const AttnArgs &a) {
@@ -634,7 +755,13 @@ static cudaError_t prep_nq() {
 }
 
 cudaError_t attn_prepare() {
-    cudaError_t e = allow_dynamic_smem(k_attn_stream<1>);
+    cudaError_t e = allow_dynamic_smem(k_attn_pairs<1, false>);
+    if (e == cudaSuccess) e = allow_dynamic_smem(k_attn_pairs<1, true>);
+    if (e == cudaSuccess) e = allow_dynamic_smem(k_attn_pairs<2, true>);
+    if (e == cudaSuccess) e = allow_dynamic_smem(k_attn_pairs<3, true>);
+    if (e == cudaSuccess) e = allow_dynamic_smem(k_attn_pairs<4, true>);
+    if (e == cudaSuccess) e = allow_dynamic_smem(k_attn_pairs<5, true>);
+    if (e == cudaSuccess) e = allow_dynamic_smem(k_attn_stream<1>);
     if (e == cudaSuccess) e = allow_dynamic_smem(k_attn_stream<2>);
     if (e == cudaSuccess) e = allow_dynamic_smem(k_attn_stream<3>);
     if (e == cudaSuccess) e = allow_dynamic_smem(k_attn_stream<4>);
@@ -657,7 +784,8 @@ cudaError_t attn_prepare() {
 bool attn_stream_pays(const AttnArgs &a, int sms) {
     // more (split, head, group) blocks than one resident wave of the cluster kernel; both
     // warpgroups need a tile of every pair
-    return a.cross && a.n_audio > kAttnKeyTile && (long long)a.nsplit * a.n_head * a.groups > 2LL * sms;
+    // (up to 5 queries: the warp sums of more would not fit beside the six tile buffers)
+    return a.cross && a.nq <= 5 && a.n_audio > kAttnKeyTile && (long long)a.nsplit * a.n_head * a.groups > 2LL * sms;
 }
 
 static size_t stream_smem() { return 2 * kStreamBufs * (size_t)kStreamTile * sizeof(__half) + 1024; }

@@ -416,6 +416,10 @@ __global__ void __launch_bounds__(kSelThreads) k_select_greedy(DecodeState st, i
     if (!s_done) stage_ints(st.hist[0] + (size_t)m * st.hs, len, hbuf);
     pdl_trigger();
     pdl_wait();
+    if (st.gbar && blockIdx.x == 0) {  // the next step kernel's barriers
+        if (threadIdx.x == 0) *st.gbar = 0;
+        for (int j = threadIdx.x; j < st.n_gflag; j += blockDim.x) st.gflag[32 * j] = 0;
+    }
     if (s_done) return;
     if (mode == SEL_GREEDY) {
         if (threadIdx.x < 32) {
@@ -465,6 +469,10 @@ __global__ void __launch_bounds__(kSelThreads) k_select_beam_init(DecodeState st
     __shared__ int ti[kMaxTopK];
     pdl_trigger();
     pdl_wait();
+    if (st.gbar && blockIdx.x == 0) {  // the next step kernel's barriers
+        if (threadIdx.x == 0) *st.gbar = 0;
+        for (int j = threadIdx.x; j < st.n_gflag; j += blockDim.x) st.gflag[32 * j] = 0;
+    }
     const int s = blockIdx.x;
     const int B = st.beam;
     const float *pp = part + (size_t)s * P * kPartStride;
@@ -575,6 +583,10 @@ __global__ void __launch_bounds__(kSelThreads) k_select_beam(DecodeState st, int
     }
     pdl_trigger();
     pdl_wait();
+    if (st.gbar && blockIdx.x == 0) {  // the next step kernel's barriers
+        if (threadIdx.x == 0) *st.gbar = 0;
+        for (int j = threadIdx.x; j < st.n_gflag; j += blockDim.x) st.gflag[32 * j] = 0;
+    }
     if (s_done) return;
     __syncthreads();  // staged histories
     // one warp per beam: its partials, their merge and top-(beam + 1); finished beams skip

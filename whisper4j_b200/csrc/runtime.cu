@@ -23,6 +23,7 @@
 #include <vector>
 
 #include "../../include/whisper4j_cuda.h"
+#include "k_step.cuh"
 #include "w4j_internal.cuh"
 
 using namespace w4j;
@@ -42,12 +43,17 @@ static int set_err(int code, const char *fmt, ...) {
     return code;
 }
 
+// A failed call leaves its error as the thread's last CUDA error (cudaGetLastError); it is consumed
+// here, so a later launch check does not report an earlier, already handled failure (a refused
+// allocation, for instance).
 #define CUDA_TRY(expr)                                                                             \
     do {                                                                                           \
         cudaError_t e_ = (expr);                                                                   \
-        if (e_ != cudaSuccess)                                                                     \
+        if (e_ != cudaSuccess) {                                                                   \
+            cudaGetLastError();                                                                    \
             return set_err(e_ == cudaErrorMemoryAllocation ? W4J_ERR_OOM : W4J_ERR_CUDA, "%s: %s (%s:%d)", \
                            #expr, cudaGetErrorString(e_), __FILE__, __LINE__);                     \
+        }                                                                                          \
     } while (0)
 
 #define TRY(expr)            \
@@ -130,10 +136,27 @@ struct w4j_ctx {
     cudaEvent_t ev0 = nullptr, ev1 = nullptr;
     alignas(64) unsigned char e_tmap[128] = {};  // TMA map of the f16 token embedding
     alignas(64) unsigned char xk_tmap[128] = {}, xv_tmap[128] = {};  // cross K / V caches as [rows][64]
+    alignas(64) unsigned char sk_tmap[128] = {}, sv_tmap[128] = {};  // self K / V caches as [rows][64]
+    bool s_tmap_ok = false;
     bool x_tmap_ok = false;
     bool e_tmap_ok = false;
     bool tc_logits = true;
     bool tc_gemm = true;  // tcgen05 projections once M >= 16
+    // the persistent step kernel (k_step) for up to 8 sequences: plans per (streams, beams)
+    struct StepPlanDev {
+        bool ok = false;
+        StepArgs base;  // plan pointers and model fields; per-call fields are set at capture
+    };
+    bool use_step = false;  // W4J_STEP_KERNEL=1: one persistent kernel per step of <= 8 sequences
+    bool step_coop = true;  // launch it with the cooperative attribute (dropped if capture refuses it)
+    bool verbose = false;   // W4J_VERBOSE=1: say on stderr why a faster path was not taken
+    unsigned step_inflight = 48u << 10;  // W4J_STEP_INFLIGHT_KB: copy bytes in flight per block of the step kernel
+    bool attn_pairs = true;  // W4J_NO_ATTN_PAIRS=1: cross-attention of many streams on k_attn_stream
+    std::map<std::pair<int, int>, StepPlanDev> step_plans;
+    unsigned *gbar = nullptr;  // grid barrier counter of the step kernel
+    unsigned *gflag = nullptr; // its per-block release flags (32 words apart)
+    int *xcnt = nullptr;       // finished cross-attention splits per (stream, head)
+    float *xpart = nullptr;    // cross-attention partial results of the step kernel
     // in-chain kernel timing (w4j_set_kernel_timing): step graphs captured with external event
     // records around every launch of one kernel class; read back after each step
     int time_class = 0;
@@ -145,7 +168,7 @@ struct w4j_ctx {
 };
 
 // Kernel classes of w4j_set_kernel_timing.
-enum KClass : int { KC_PROJ = 1, KC_SELF_ATTN = 2, KC_CROSS_ATTN = 3, KC_LOGITS = 4, KC_SELECT = 5 };
+enum KClass : int { KC_PROJ = 1, KC_SELF_ATTN = 2, KC_CROSS_ATTN = 3, KC_LOGITS = 4, KC_SELECT = 5, KC_STEP = 6 };
 
 // Around one launch of class `cls` while a timed step graph is being captured: an external event
 // record before (begin) and after (!begin) it.
@@ -273,6 +296,9 @@ static int size_self(w4j_ctx *c, int cap, bool keep_rows) {
     st.hs = hs;
     st.dyn_stride = dyn_stride;
     c->cap = cap;
+    const size_t srows = (size_t)c->n_slots * L * c->H * cap;
+    c->s_tmap_ok = srows < (size_t)INT32_MAX && make_tmap_f16_rows(c->sk_tmap, c->sk, (int)srows, kHeadDim) &&
+                   make_tmap_f16_rows(c->sv_tmap, c->sv, (int)srows, kHeadDim);
     return 0;
 }
 
@@ -327,6 +353,13 @@ extern "C" int w4j_ctx_create(const w4j_dims *dims, int device, int max_streams,
     c->sm_count = prop.multiProcessorCount;
     if (const char *ev = getenv("W4J_NO_TC_LOGITS")) c->tc_logits = ev[0] == '0';
     if (const char *ev = getenv("W4J_NO_TC_GEMM")) c->tc_gemm = ev[0] == '0';
+    if (const char *ev = getenv("W4J_STEP_KERNEL")) c->use_step = ev[0] == '1';
+    if (const char *ev = getenv("W4J_NO_ATTN_PAIRS")) c->attn_pairs = ev[0] == '0';
+    if (const char *ev = getenv("W4J_STEP_INFLIGHT_KB")) {
+        const long kb = strtol(ev, nullptr, 10);
+        if (kb >= 16 && kb <= 128) c->step_inflight = (unsigned)kb << 10;
+    }
+    if (const char *ev = getenv("W4J_VERBOSE")) c->verbose = ev[0] == '1';
     c->layers.resize(c->L);
     c->cache_len.assign(max_streams, 0);
     c->has_xa.assign(max_streams, 0);
@@ -340,7 +373,8 @@ extern "C" int w4j_ctx_create(const w4j_dims *dims, int device, int max_streams,
     cudaEventCreate(&c->ev0);
     cudaEventCreate(&c->ev1);
     if ((rc = (int)gemv_prepare()) != 0 || (rc = (int)select_prepare()) != 0 || (rc = (int)logits_tc_prepare()) != 0 ||
-        (rc = (int)attn_prepare()) != 0 || (rc = (int)gemm_tc_prepare()) != 0 || (rc = (int)xkv_tc_prepare()) != 0)
+        (rc = (int)attn_prepare()) != 0 || (rc = (int)gemm_tc_prepare()) != 0 || (rc = (int)xkv_tc_prepare()) != 0 ||
+        (rc = (int)step_prepare()) != 0)
         return fail(set_err(W4J_ERR_CUDA, "kernel attributes: %s", cudaGetErrorString((cudaError_t)rc)));
     const size_t V = c->V, C = c->C, A = c->A, L = c->L;
     const size_t M = c->M_max, MB = c->Mbuf;
@@ -384,8 +418,14 @@ extern "C" int w4j_ctx_create(const w4j_dims *dims, int device, int max_streams,
         (rc = dalloc(c, &st.nsp, (size_t)max_streams)) || (rc = dalloc(c, &st.fin_n, (size_t)max_streams)) ||
         (rc = dalloc(c, &st.fin_len, M)) || (rc = dalloc(c, &st.fin_lp, M)) ||
         (rc = dalloc(c, &st.out_len, (size_t)max_streams)) || (rc = dalloc(c, &st.out_sum, (size_t)max_streams)) ||
-        (rc = dalloc(c, &st.err, 1)))
+        (rc = dalloc(c, &st.err, 1)) || (rc = dalloc(c, &c->gbar, 1)) ||
+        (rc = dalloc(c, &c->gflag, (size_t)32 * c->sm_count)) ||
+        (rc = dalloc(c, &c->xcnt, (size_t)max_streams * H)) ||
+        (rc = dalloc(c, &c->xpart, (size_t)c->sm_count * 8 * (kHeadDim + 2))))
         return fail(rc);
+    st.gbar = c->gbar;
+    st.gflag = c->gflag;
+    st.n_gflag = c->sm_count;
     if ((rc = size_self(c, c->cap, false))) return fail(rc);
     // per-call int arrays: a decode call's prompt tokens [C][S], prompt positions [C][S], stream
     // base [S], cross stream [S] and suppress list [V]; or a forward call's nine per-token
@@ -394,8 +434,10 @@ extern "C" int w4j_ctx_create(const w4j_dims *dims, int device, int max_streams,
     if ((rc = dalloc(c, &c->d_int_area, c->int_area_n)) || (rc = dalloc(c, &c->d_done_snapshot, (size_t)max_streams)))
         return fail(rc);
     if (cudaMallocHost(&c->h_int_area, c->int_area_n * sizeof(int)) != cudaSuccess ||
-        cudaMallocHost(&c->h_done, (size_t)max_streams * sizeof(int)) != cudaSuccess)
+        cudaMallocHost(&c->h_done, (size_t)max_streams * sizeof(int)) != cudaSuccess) {
+        cudaGetLastError();
         return fail(set_err(W4J_ERR_OOM, "pinned host buffers"));
+    }
     // fused self-attention bias (key bias defaults to zero)
     for (int l = 0; l < c->L; ++l) {
         LayerDev &ly = c->layers[l];
@@ -502,7 +544,10 @@ static int upload_mat(w4j_ctx *c, DMat &m, int rows_total, int row0, int N, int 
     }
     if (e == cudaSuccess) e = cudaDeviceSynchronize();
     cudaFree(stage);
-    if (e != cudaSuccess) return set_err(W4J_ERR_CUDA, "matrix upload: %s", cudaGetErrorString(e));
+    if (e != cudaSuccess) {
+        cudaGetLastError();
+        return set_err(W4J_ERR_CUDA, "matrix upload: %s", cudaGetErrorString(e));
+    }
     return 0;
 }
 
@@ -773,7 +818,9 @@ static int run_layers(w4j_ctx *c, const PassArgs &pa, long long &launches) {
         sa.err = c->st.err;
         sa.self_prefetch = pa.self_prefetch;
         CUDA_TRY(tmark(c, KC_SELF_ATTN, true));
-        CUDA_TRY(launch_attn(sa, c->stream, pdl));
+        if (c->s_tmap_ok && attn_self_stream_pays(sa, c->sm_count))
+            CUDA_TRY(launch_attn_self_stream(sa, c->sk_tmap, c->sv_tmap, c->sm_count, c->stream, pdl));
+        else CUDA_TRY(launch_attn(sa, c->stream, pdl));
         CUDA_TRY(tmark(c, KC_SELF_ATTN, false));
 
         GemvArgs go;
@@ -819,7 +866,9 @@ static int run_layers(w4j_ctx *c, const PassArgs &pa, long long &launches) {
         ca.active = pa.group_active;
         ca.err = c->st.err;
         CUDA_TRY(tmark(c, KC_CROSS_ATTN, true));
-        if (c->x_tmap_ok && attn_stream_pays(ca, c->sm_count))
+        if (c->x_tmap_ok && c->attn_pairs && attn_pairs_pays(ca, c->sm_count))
+            CUDA_TRY(launch_attn_pairs(ca, c->xk_tmap, c->xv_tmap, c->sm_count, c->stream, pdl));
+        else if (c->x_tmap_ok && attn_stream_pays(ca, c->sm_count))
             CUDA_TRY(launch_attn_stream(ca, c->xk_tmap, c->xv_tmap, c->sm_count, c->stream, pdl));
         else CUDA_TRY(launch_attn(ca, c->stream, pdl));
         CUDA_TRY(tmark(c, KC_CROSS_ATTN, false));
@@ -1102,6 +1151,9 @@ static int prepare_call(w4j_ctx *c, const CallArgs &a, const CallLayout &Ly) {
     CUDA_TRY(cudaMemsetAsync(st.fin_n, 0, a.S * 4, c->stream));
     CUDA_TRY(cudaMemsetAsync(st.nsp, 0, a.S * 4, c->stream));
     CUDA_TRY(cudaMemsetAsync(st.err, 0, 4, c->stream));
+    CUDA_TRY(cudaMemsetAsync(c->xcnt, 0, (size_t)c->max_streams * c->H * 4, c->stream));
+    CUDA_TRY(cudaMemsetAsync(c->gbar, 0, 4, c->stream));
+    CUDA_TRY(cudaMemsetAsync(c->gflag, 0, (size_t)32 * c->sm_count * 4, c->stream));
     st.n_streams = a.S;
     st.beam = B;
     st.max_tokens = a.max_tokens;
@@ -1178,6 +1230,136 @@ static int run_prompt(w4j_ctx *c, const CallArgs &a, const CallLayout &Ly, int m
     return 0;
 }
 
+// The step kernel's plan for S streams of B beams (built once per shape; ok = false when the
+// shape or the weights do not fit it, and the chained kernels run instead).
+static const w4j_ctx::StepPlanDev *get_step_plan(w4j_ctx *c, int S, int B) {
+    auto key = std::make_pair(S, B);
+    auto it = c->step_plans.find(key);
+    if (it != c->step_plans.end()) return &it->second;
+    w4j_ctx::StepPlanDev &pd = c->step_plans[key];
+    const int M = S * B, d = c->d, G = c->n_parts;
+    if (!c->use_step || M > 8 || !c->x_tmap_ok || c->E.type != WT_F16 || G > c->sm_count) return &pd;
+    StepPlanIn in;
+    in.G = G;
+    in.M = M;
+    in.S = S;
+    in.B = B;
+    in.H = c->H;
+    in.A = c->A;
+    in.V = c->V;
+    in.d = d;
+    auto gemv = [&](int in_mode, int out_mode, int l, int K, int N, const float *bias, const float *g, const float *bb,
+                    const float *act, float *y, const DMat &W) {
+        StepPhase ph{};
+        ph.kind = SK_GEMV;
+        ph.in_mode = in_mode;
+        ph.out_mode = out_mode;
+        ph.layer = l;
+        ph.K = K;
+        ph.N = N;
+        ph.bias = bias;
+        ph.ln_g = g;
+        ph.ln_b = bb;
+        ph.act = act;
+        ph.y = y;
+        in.phases.push_back(ph);
+        in.W.push_back(W.h);
+        return W.type == WT_F16;
+    };
+    auto attn = [&](int kind, int l) {
+        StepPhase ph{};
+        ph.kind = kind;
+        ph.layer = l;
+        in.phases.push_back(ph);
+        in.W.push_back(nullptr);
+    };
+    bool f16 = true;
+    for (int l = 0; l < c->L; ++l) {
+        const LayerDev &ly = c->layers[l];
+        f16 &= gemv(l == 0 ? SI_EMBED_LN : SI_LN, SO_QKV, l, d, 3 * d, ly.bqkv, ly.ln1g, ly.ln1b, c->x, c->q, ly.qkv);
+        attn(SK_SELF, l);
+        f16 &= gemv(SI_ACT, SO_RESIDUAL, l, d, d, ly.bo, nullptr, nullptr, c->attn, c->x, ly.o);
+        f16 &= gemv(SI_LN, SO_STORE, l, d, d, ly.bxq, ly.ln2g, ly.ln2b, c->x, c->q, ly.xq);
+        attn(SK_CROSS, l);
+        f16 &= gemv(SI_ACT, SO_RESIDUAL, l, d, d, ly.bxo, nullptr, nullptr, c->attn, c->x, ly.xo);
+        f16 &= gemv(SI_LN, SO_GELU, l, d, 4 * d, ly.bm0, ly.ln3g, ly.ln3b, c->x, c->h, ly.m0);
+        f16 &= gemv(SI_ACT, SO_RESIDUAL, l, 4 * d, d, ly.bm2, nullptr, nullptr, c->h, c->x, ly.m2);
+    }
+    {
+        StepPhase ph{};
+        ph.kind = SK_LOGITS;
+        ph.in_mode = SI_LN;
+        ph.K = d;
+        ph.N = c->V;
+        ph.ln_g = c->lng;
+        ph.ln_b = c->lnb;
+        ph.act = c->x;
+        in.phases.push_back(ph);
+        in.W.push_back(c->E.h);
+    }
+    if (!f16) return &pd;
+    StepPlanOut out;
+    std::string why;
+    if (!step_plan_build(in, out, why)) {
+        if (c->verbose) fprintf(stderr, "w4j: step kernel plan refused for %d x %d: %s\n", S, B, why.c_str());
+        return &pd;
+    }
+    for (size_t p = 0; p < in.phases.size(); ++p) {
+        in.phases[p].box_rows = out.box_rows[p];
+        in.phases[p].w = in.W[p];
+    }
+    StepPhase *dph = nullptr;
+    StepChunk *dch = nullptr;
+    StepPiece *dpc = nullptr;
+    int *dnc = nullptr, *dpp = nullptr;
+    if (dalloc(c, &dph, in.phases.size()) || dalloc(c, &dch, out.chunks.size()) || dalloc(c, &dpc, out.pieces.size()) ||
+        dalloc(c, &dnc, out.n_chunks.size()) || dalloc(c, &dpp, out.phase_piece.size()))
+        return &pd;
+    if (cudaMemcpy(dph, in.phases.data(), in.phases.size() * sizeof(StepPhase), cudaMemcpyHostToDevice) != cudaSuccess ||
+        cudaMemcpy(dch, out.chunks.data(), out.chunks.size() * sizeof(StepChunk), cudaMemcpyHostToDevice) != cudaSuccess ||
+        cudaMemcpy(dpc, out.pieces.data(), out.pieces.size() * sizeof(StepPiece), cudaMemcpyHostToDevice) != cudaSuccess ||
+        cudaMemcpy(dnc, out.n_chunks.data(), out.n_chunks.size() * 4, cudaMemcpyHostToDevice) != cudaSuccess ||
+        cudaMemcpy(dpp, out.phase_piece.data(), out.phase_piece.size() * 4, cudaMemcpyHostToDevice) != cudaSuccess) {
+        cudaGetLastError();
+        return &pd;
+    }
+    StepArgs &a = pd.base;
+    a = StepArgs{};
+    a.phases = dph;
+    a.n_phases = (int)in.phases.size();
+    a.chunks = dch;
+    a.n_chunks = dnc;
+    a.pieces = dpc;
+    a.phase_piece = dpp;
+    a.max_chunks = out.max_chunks;
+    a.max_pieces = out.max_pieces;
+    a.d = d;
+    a.H = c->H;
+    a.L = c->L;
+    a.V = c->V;
+    a.C = c->C;
+    a.A = c->A;
+    a.splits = out.splits;
+    a.E = c->E.h;
+    a.pos_emb = c->pos_emb;
+    a.lng = c->lng;
+    a.lnb = c->lnb;
+    a.gelu_lut = c->gelu_lut;
+    a.M = M;
+    a.S = S;
+    a.B = B;
+    a.x = c->x;
+    a.q = c->q;
+    a.attn_o = c->attn;
+    a.xpart = c->xpart;
+    a.xcnt = c->xcnt;
+    a.gbar = c->gbar;
+    a.gflag = c->gflag;
+    a.inflight = c->step_inflight;
+    pd.ok = true;
+    return &pd;
+}
+
 // One decode step after the prompt (captured into a graph).
 static int enqueue_step(w4j_ctx *c, const CallArgs &a, const CallLayout &Ly, int mode, int parity, long long &launches) {
     DecodeState &st = c->st;
@@ -1194,13 +1376,34 @@ static int enqueue_step(w4j_ctx *c, const CallArgs &a, const CallLayout &Ly, int
     pa.cross_stream = c->d_int_area + Ly.cross;
     pa.group_active = B == 1 ? st.active : nullptr;
     pa.self_prefetch = 1;  // each step is its own graph launch: older rows are complete
-    TRY(run_layers(c, pa, launches));
     LogitsArgs la = logits_args(c, M, st.active);
     la.use_mask = 1;
     la.mask = mask_args(c);
     la.topk = mode == MODE_BEAM ? B + 1 : 0;
     if (mode == MODE_SAMPLE) la.masked_out = c->masked;
-    CUDA_TRY(run_logits(c, la, true, launches));
+    const w4j_ctx::StepPlanDev *sp = c->use_step ? get_step_plan(c, S, B) : nullptr;
+    if (sp && sp->ok) {
+        // the whole step in one persistent launch (k_step.cu), then the selection
+        StepArgs sa = sp->base;
+        sa.n_ctx = c->cap;
+        sa.sk = c->sk;
+        sa.sv = c->sv;
+        sa.tok = st.tok_in;
+        sa.pos = st.seq_pos;
+        sa.slot = st.seq_slot;
+        sa.table = pa.table;
+        sa.active = st.active;
+        sa.cross_stream = pa.cross_stream;
+        sa.lg = la;
+        sa.err = st.err;
+        CUDA_TRY(tmark(c, KC_STEP, true));
+        CUDA_TRY(launch_step(sa, c->n_parts, c->xk_tmap, c->xv_tmap, c->step_coop, c->stream));
+        CUDA_TRY(tmark(c, KC_STEP, false));
+        ++launches;
+    } else {
+        TRY(run_layers(c, pa, launches));
+        CUDA_TRY(run_logits(c, la, true, launches));
+    }
     const int sel = mode == MODE_BEAM ? SEL_BEAM : mode == MODE_SAMPLE ? SEL_SAMPLE : SEL_GREEDY;
     CUDA_TRY(tmark(c, KC_SELECT, true));
     CUDA_TRY(launch_select(st, sel, parity, c->logit_part, c->n_parts, c->masked, 0, c->stream, true));
@@ -1238,21 +1441,36 @@ static int get_step_graph(w4j_ctx *c, const CallArgs &a, const CallLayout &Ly, i
         c->graph_launches.clear();
     }
     cudaGraph_t graph = nullptr;
+    // the step kernel's plan allocates and uploads: build it before the capture begins
+    if (c->use_step && a.S * a.beam <= 8) get_step_plan(c, a.S, a.beam);
     CUDA_TRY(cudaStreamBeginCapture(c->stream, cudaStreamCaptureModeThreadLocal));
     c->timing_capture = c->time_class != 0;
     c->tev_used = 0;
     int rc = enqueue_step(c, a, Ly, mode, parity, launches);
     c->timing_capture = false;
     cudaError_t e = cudaStreamEndCapture(c->stream, &graph);
-    if (rc < 0) {
-        if (graph) cudaGraphDestroy(graph);
-        return rc;
-    }
-    if (e != cudaSuccess) return set_err(W4J_ERR_CUDA, "graph capture: %s", cudaGetErrorString(e));
     cudaGraphExec_t exec = nullptr;
-    e = cudaGraphInstantiate(&exec, graph, 0);
-    cudaGraphDestroy(graph);
-    if (e != cudaSuccess) return set_err(W4J_ERR_CUDA, "graph instantiate: %s", cudaGetErrorString(e));
+    if (rc >= 0 && e == cudaSuccess) {
+        e = cudaGraphInstantiate(&exec, graph, 0);
+        if (e != cudaSuccess) exec = nullptr;
+    }
+    if (graph) cudaGraphDestroy(graph);
+    if ((rc < 0 || e != cudaSuccess) && c->use_step) {
+        // a capture that refuses the step kernel: without the cooperative attribute, then the
+        // chained kernels
+        cudaGetLastError();
+        if (c->verbose)
+            fprintf(stderr, "w4j: step graph capture failed (%s; %s), %s\n", cudaGetErrorString(e), g_err.c_str(),
+                    c->step_coop ? "retrying without the cooperative attribute" : "using the chained kernels");
+        if (c->step_coop) c->step_coop = false;
+        else c->use_step = false;
+        return get_step_graph(c, a, Ly, mode, parity, out, per_step);
+    }
+    if (rc < 0) return rc;
+    if (e != cudaSuccess) {
+        cudaGetLastError();
+        return set_err(W4J_ERR_CUDA, "graph capture: %s", cudaGetErrorString(e));
+    }
     c->graphs[k] = exec;
     c->graph_launches[k] = launches;
     *out = exec;
@@ -1490,7 +1708,7 @@ extern "C" int w4j_cancel(w4j_ctx *c) {
 
 extern "C" int w4j_set_kernel_timing(w4j_ctx *c, int kernel_class) {
     if (!c) return set_err(W4J_ERR_ARG, "null context");
-    if (kernel_class < 0 || kernel_class > KC_SELECT) return set_err(W4J_ERR_ARG, "kernel class %d", kernel_class);
+    if (kernel_class < 0 || kernel_class > KC_STEP) return set_err(W4J_ERR_ARG, "kernel class %d", kernel_class);
     std::lock_guard<std::mutex> g(c->mu);
     c->time_class = kernel_class;
     return W4J_OK;

@@ -166,6 +166,9 @@ struct DecodeState {
     int *out_len = nullptr;            // [S]
     double *out_sum = nullptr;         // [S]
     int *err = nullptr;                // device error word (bounds failures), 0 = ok
+    unsigned *gbar = nullptr;          // grid barrier counter of the step kernel (reset by selection)
+    unsigned *gflag = nullptr;         // its per-block flags, 32 words apart (reset by selection)
+    int n_gflag = 0;
 };
 
 // ---------------------------------------------------------------------------
@@ -190,6 +193,20 @@ __device__ __forceinline__ void bulk_g2s(void *dst, const void *src, unsigned by
                      smem_u32(dst)),
                  "l"(src), "r"(bytes), "r"(smem_u32(b))
                  : "memory");
+}
+// L2 policy for data read once per step (weights, encoder K / V): evicted before anything else, so
+// the small per-step working set (activations, norms, biases, caches) stays resident in L2
+__device__ __forceinline__ uint64_t l2_evict_first() {
+    uint64_t pol;
+    asm volatile("createpolicy.fractional.L2::evict_first.b64 %0, 1.0;" : "=l"(pol));
+    return pol;
+}
+__device__ __forceinline__ void bulk_g2s_hint(void *dst, const void *src, unsigned bytes, uint64_t *b, uint64_t pol) {
+    asm volatile(
+        "cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes.L2::cache_hint [%0], [%1], %2, [%3], %4;" ::"r"(
+            smem_u32(dst)),
+        "l"(src), "r"(bytes), "r"(smem_u32(b)), "l"(pol)
+        : "memory");
 }
 __device__ __forceinline__ bool mbar_test(uint64_t *b, unsigned parity) {
     unsigned ok;
@@ -264,6 +281,14 @@ bool attn_stream_pays(const AttnArgs &a, int sms);  // the streaming kernel beat
 // cross-attention over many (group, head) pairs: one persistent block per SM; kmap / vmap are
 // make_tmap_f16_rows maps of the cross K / V caches as [rows][64]
 cudaError_t launch_attn_stream(const AttnArgs &a, const void *kmap, const void *vmap, int sms, cudaStream_t s, bool pdl);
+// self-attention of many sequences without beam tables, masks or explicit key counts: a persistent
+// warpgroup per (sequence, head) pair; kmap / vmap are make_tmap_f16_rows maps of the self K / V caches
+bool attn_self_stream_pays(const AttnArgs &a, int sms);
+cudaError_t launch_attn_self_stream(const AttnArgs &a, const void *kmap, const void *vmap, int sms, cudaStream_t s,
+                                    bool pdl);
+// cross-attention of many (stream, head) pairs with a warpgroup per pair (maps: the cross caches)
+bool attn_pairs_pays(const AttnArgs &a, int sms);
+cudaError_t launch_attn_pairs(const AttnArgs &a, const void *kmap, const void *vmap, int sms, cudaStream_t s, bool pdl);
 cudaError_t launch_logits(const LogitsArgs &a, int n_parts, cudaStream_t s, bool pdl);
 int logits_parts_for(int V, int sm_count);
 size_t logits_smem_bytes(int M, int V, int d, int n_parts);
