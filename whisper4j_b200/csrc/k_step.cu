@@ -61,8 +61,16 @@ struct StepSmem {
     __half (*pw)[8][kRowPadPw];
     float (*wm)[8], (*wl)[8];
     float *acc;        // GEMV partial sums across activation segments [rows][kStepMaxM]
-    int *flags;        // [0] next chunk to issue, [1] chunks released, [2] dead (a wait ran out), [3] last
+    int *flags;        // [0] issued, [1] released, [2] dead (a wait ran out), [3] last split, [4] landed,
+                       // [5] bytes in flight, [8 + i % 16] bytes of chunk i
+    float *xs;         // [64 rows][8] the block's rows b d / G .. of the residual stream x, every sequence
+    int *sq;           // per sequence m: [m] token, [8 + m] position, [16 + m] cache slot, [24 + m] live;
+                       // per stream s: [32 + s] cross-cache slot
+    int *nph;          // the next phase's descriptor (StepPhase words)
+    const StepChunk *ch;  // the block's copies
 };
+constexpr int kPhaseWords = (int)(sizeof(StepPhase) / 4);
+static_assert(sizeof(StepPhase) % 4 == 0 && kPhaseWords <= kStepThreads, "phase descriptor words");
 
 // Block-uniform wait for chunk i.  After any wait ran out the block is dead: it waits for nothing
 // more and issues no copies (it still takes part in the grid barriers).
@@ -74,6 +82,7 @@ __device__ __forceinline__ bool step_wait_chunk(const StepArgs &a, const StepSme
     bool r = true;
     if (threadIdx.x == 0) {
         r = false;
+        step_service(a, sm, kmap, vmap);  // refill the ring (released space) before anything else
         for (long long it = 0; !sm.flags[2] && it < (1ll << 22); ++it) {
             if (mbar_test(sm.bars + (i % kStepBars), (unsigned)((i / kStepBars) & 1))) {
                 r = true;
@@ -98,8 +107,8 @@ __device__ __forceinline__ bool step_wait_chunk(const StepArgs &a, const StepSme
 // flags: [0] issued, [1] released, [2] dead, [4] landed, [5] bytes in flight, [8 + i % 16] bytes of chunk i
 __device__ void step_service(const StepArgs &a, const StepSmem &sm, const CUtensorMap *kmap, const CUtensorMap *vmap) {
     if (sm.flags[2]) return;
-    const int b = blockIdx.x, n = a.n_chunks[b];
-    const StepChunk *ch = a.chunks + (size_t)b * a.max_chunks;
+    const int n = a.n_chunks[blockIdx.x];
+    const StepChunk *ch = sm.ch;
     int i = sm.flags[0], landed = sm.flags[4], infl = sm.flags[5];
     while (landed < i && mbar_test(sm.bars + (landed % kStepBars), (unsigned)((landed / kStepBars) & 1))) {
         infl -= sm.flags[8 + landed % kStepBars];
@@ -113,11 +122,10 @@ __device__ void step_service(const StepArgs &a, const StepSmem &sm, const CUtens
         uint64_t *bar = sm.bars + (i % kStepBars);
         mbar_expect_tx(bar, c.bytes);
         unsigned char *dst = sm.ring + c.off;
-        if (c.kind == 0) {  // weight rows [j0, ..): contiguous in the row-major matrix, one bulk copy
-            const StepPhase &ph = a.phases[c.p];
-            bulk_g2s_hint(dst, ph.w + (size_t)c.j0 * ph.K, c.bytes, bar, pol);
+        if (c.kind == 0) {  // weight rows: contiguous in the row-major matrix, one bulk copy
+            bulk_g2s_hint(dst, reinterpret_cast<const void *>(c.src), c.bytes, bar, pol);
         } else {
-            const int y = ((a.cross_stream[c.s] * a.L + c.layer) * a.H + c.h) * a.A + c.j0;
+            const int y = sm.sq[32 + c.s] * a.L * a.H * a.A + (int)c.src;
             for (int t = 0; t < c.nbox; ++t) {
                 tma_load_2d_hint(dst + (size_t)t * kBox, kmap, 0, y + t * kAttnKeyTile, bar, pol);
                 tma_load_2d_hint(dst + (size_t)(c.nbox + t) * kBox, vmap, 0, y + t * kAttnKeyTile, bar, pol);
@@ -139,7 +147,21 @@ __device__ void step_service(const StepArgs &a, const StepSmem &sm, const CUtens
 __device__ void step_barrier(const StepArgs &a, const StepSmem &sm, unsigned k, const CUtensorMap *kmap,
                              const CUtensorMap *vmap) {
     __syncthreads();
-    if (threadIdx.x == 0) {
+    if (threadIdx.x == 0 && a.bar_mode == 1) {
+        // every block polls the counter itself (no release stores; one more reader per address)
+        red_release_add(a.gbar, 1u);  // the block's writes (ordered by the block barrier) before its arrival
+        const unsigned target = k * gridDim.x;
+        long long it = 0;
+        while (!sm.flags[2] && ld_acquire_u32(a.gbar) < target) {
+            if (++it > (1ll << 22)) {
+                atomicExch(a.err, 3);
+                sm.flags[2] = 1;
+                break;
+            }
+            step_service(a, sm, kmap, vmap);
+            if (it > 4) __nanosleep(64);
+        }
+    } else if (threadIdx.x == 0) {
         __threadfence();
         const unsigned old = atomicAdd(a.gbar, 1u);
         if (old == k * gridDim.x - 1) {  // the last to arrive releases everyone: one fence, then plain stores
@@ -163,15 +185,12 @@ __device__ void step_barrier(const StepArgs &a, const StepSmem &sm, unsigned k, 
     __syncthreads();
 }
 
-// Release chunk i (every thread is done with it) and refill the ring.
-__device__ void step_release(const StepArgs &a, const StepSmem &sm, int i, const CUtensorMap *kmap,
-                             const CUtensorMap *vmap) {
+// Release chunk i (every thread is done with it).  The ring is refilled by the next wait (for a
+// chunk or at a grid barrier), off the phase's critical path.
+__device__ void step_release(const StepSmem &sm, int i) {
     fence_proxy_async();  // generic accesses to the ring precede the copies that reuse it
     __syncthreads();
-    if (threadIdx.x == 0) {
-        sm.flags[1] = i + 1;
-        step_service(a, sm, kmap, vmap);
-    }
+    if (threadIdx.x == 0) sm.flags[1] = i + 1;
 }
 
 // Stage the activation rows of a phase (columns [k0, k0 + kn)) into sm.act, rows `ast` floats apart,
@@ -198,10 +217,10 @@ __device__ void step_stage(const StepArgs &a, const StepSmem &sm, const StepPhas
         }
         return;
     }
-    // LayerNorm inputs (K = d <= 1280, one segment): rows and gamma / beta into shared memory
+    // LayerNorm inputs (K = d <= 1280, one segment): rows into shared memory; gamma / beta are on
+    // their way there since before the phase's barrier (step_ln_prefetch)
     float *lnp = reinterpret_cast<float *>(sm.kt);  // [gamma | beta], 2 K floats
-    const int lq = 2 * (K / 4);
-    for (int i0 = tid; i0 < total + lq; i0 += kStepThreads * U) {
+    for (int i0 = tid; i0 < total; i0 += kStepThreads * U) {
         float4 v[U];
 #pragma unroll
         for (int u = 0; u < U; ++u) {
@@ -211,16 +230,13 @@ __device__ void step_stage(const StepArgs &a, const StepSmem &sm, const StepPhas
                 if (ph.in_mode == SI_LN) {
                     v[u] = __ldcg(reinterpret_cast<const float4 *>(ph.act + (size_t)m * K) + c);
                 } else {  // x = E[tok] + P[pos] (WhisperDecoder.java:66-80); the offset clamped as at :72
-                    const int p = a.pos[m], pe = p > a.C - 1 ? a.C - 1 : p;
-                    const uint2 e = __ldg(reinterpret_cast<const uint2 *>(a.E + (size_t)a.tok[m] * K) + c);
+                    const int p = sm.sq[8 + m], pe = p > a.C - 1 ? a.C - 1 : p;
+                    const uint2 e = __ldg(reinterpret_cast<const uint2 *>(a.E + (size_t)sm.sq[m] * K) + c);
                     const float4 pp = __ldg(reinterpret_cast<const float4 *>(a.pos_emb + (size_t)pe * K) + c);
                     const float2 lo = __half22float2(*reinterpret_cast<const __half2 *>(&e.x));
                     const float2 hi = __half22float2(*reinterpret_cast<const __half2 *>(&e.y));
                     v[u] = make_float4(lo.x + pp.x, lo.y + pp.y, hi.x + pp.z, hi.y + pp.w);
                 }
-            } else if (i < total + lq) {
-                const int j = i - total;
-                v[u] = __ldg(reinterpret_cast<const float4 *>(j < K / 4 ? ph.ln_g : ph.ln_b) + (j % (K / 4)));
             }
         }
 #pragma unroll
@@ -231,12 +247,16 @@ __device__ void step_stage(const StepArgs &a, const StepSmem &sm, const StepPhas
                 *reinterpret_cast<float4 *>(sm.act + (size_t)m * ast + 4 * c) = v[u];
                 // block 0 keeps the embedded rows as the residual stream
                 if (ph.in_mode == SI_EMBED_LN && blockIdx.x == 0) __stcg(reinterpret_cast<float4 *>(a.x + (size_t)m * K) + c, v[u]);
-            } else if (i < total + lq) {
-                *reinterpret_cast<float4 *>(lnp + 4 * (i - total)) = v[u];
             }
         }
     }
+    cp_async_wait_all();
     __syncthreads();
+    if (ph.in_mode == SI_EMBED_LN) {  // the block's rows of the residual stream start as the embedding
+        const int x0 = (int)((long long)blockIdx.x * K / gridDim.x), x1 = (int)((long long)(blockIdx.x + 1) * K / gridDim.x);
+        for (int i = tid; i < (x1 - x0) * a.M; i += kStepThreads)
+            sm.xs[(i / a.M) * kStepMaxM + i % a.M] = sm.act[(size_t)(i % a.M) * ast + x0 + i / a.M];
+    }
     // Every row in eight fixed column parts (part w: columns 32 w + lane + 256 i), part w summed by
     // warp w and the parts added in order: the same sums for any number of sequences.
     float *r1 = lnp + 2 * K, *r2 = r1 + kStepMaxM * kStepWarps;  // [M][8] partial sums
@@ -322,50 +342,60 @@ __device__ void step_dots(const StepArgs &a, const StepSmem &sm, const __half *w
     }
 }
 
-// Epilogues of the block's output rows [rbase, rend) for every live sequence: thread t takes pairs
-// (row, sequence) t, t + 256, ...; bias and residual values are loaded before anything is stored.
-__device__ void step_emit_all(const StepArgs &a, const StepSmem &sm, const StepPhase &ph, int rbase, int rend) {
+// gamma / beta of a LayerNorm phase into shared memory (sm.kt), issued before the phase's barrier
+__device__ __forceinline__ void step_ln_prefetch(const StepSmem &sm, const StepPhase &ph) {
+    if (ph.in_mode != SI_LN && ph.in_mode != SI_EMBED_LN) return;
+    float *lnp = reinterpret_cast<float *>(sm.kt);
+    const int q = ph.K / 4;
+    for (int i = threadIdx.x; i < 2 * q; i += kStepThreads)
+        cp_async16(lnp + 4 * i, reinterpret_cast<const float4 *>(i < q ? ph.ln_g : ph.ln_b) + i % q);
+    cp_async_commit();
+}
+
+// Bias values of the epilogue pairs of thread t (pairs t and t + 256: row rbase + pair / M, sequence
+// pair % M), loaded before the phase's grid barrier so that they arrive while the block waits.
+constexpr int kEmitU = 2;  // <= 64 rows x 8 sequences / 256 threads
+__device__ __forceinline__ void step_bias_prefetch(const StepPhase &ph, int M, int rbase, int rend, float (&bv)[kEmitU]) {
+#pragma unroll
+    for (int u = 0; u < kEmitU; ++u) {
+        const int i = threadIdx.x + u * kStepThreads;
+        bv[u] = ph.kind == SK_GEMV && ph.bias && i < (rend - rbase) * M ? __ldg(ph.bias + rbase + i / M) : 0.f;
+    }
+}
+
+// Epilogues of the block's output rows [rbase, rend) for every live sequence.  The residual rows
+// are the block's own (sm.xs: a residual phase's rows are b d / G .. like every other one's).
+__device__ void step_emit_all(const StepArgs &a, const StepSmem &sm, const StepPhase &ph, int rbase, int rend,
+                              const float (&bv)[kEmitU]) {
     const int M = a.M, np = (rend - rbase) * M;
-    constexpr int U = 2;  // <= 64 rows x 8 sequences / 256 threads
-    for (int i0 = threadIdx.x; i0 < np; i0 += kStepThreads * U) {
-        float bv[U], rv[U];
 #pragma unroll
-        for (int u = 0; u < U; ++u) {
-            const int i = i0 + u * kStepThreads;
-            bv[u] = 0.f;
-            rv[u] = 0.f;
-            if (i < np) {
-                const int n = rbase + i / M, m = i % M;
-                if (ph.bias) bv[u] = __ldg(ph.bias + n);
-                if (ph.out_mode == SO_RESIDUAL) rv[u] = __ldcg(ph.y + (size_t)m * ph.N + n);
+    for (int u = 0; u < kEmitU; ++u) {
+        const int i = threadIdx.x + u * kStepThreads;
+        if (i >= np) continue;
+        const int n = rbase + i / M, m = i % M;
+        if (!sm.sq[24 + m]) continue;
+        const float val = sm.acc[(n - rbase) * kStepMaxM + m] + bv[u];
+        switch (ph.out_mode) {
+            case SO_STORE:
+                __stcg(ph.y + (size_t)m * ph.N + n, val);
+                break;
+            case SO_GELU:  // Tensor.geluInPlace: table lookup at the f16 rounding of x
+                __stcg(ph.y + (size_t)m * ph.N + n, __ldg(a.gelu_lut + __half_as_ushort(__float2half_rn(val))));
+                break;
+            case SO_RESIDUAL: {
+                float &xr = sm.xs[(n - rbase) * kStepMaxM + m];
+                xr += val;
+                __stcg(ph.y + (size_t)m * ph.N + n, xr);
+                break;
             }
-        }
-#pragma unroll
-        for (int u = 0; u < U; ++u) {
-            const int i = i0 + u * kStepThreads;
-            if (i >= np) continue;
-            const int n = rbase + i / M, m = i % M;
-            if (a.active && !a.active[m]) continue;
-            const float val = sm.acc[(n - rbase) * kStepMaxM + m] + bv[u];
-            switch (ph.out_mode) {
-                case SO_STORE:
-                    __stcg(ph.y + (size_t)m * ph.N + n, val);
-                    break;
-                case SO_GELU:  // Tensor.geluInPlace: table lookup at the f16 rounding of x
-                    __stcg(ph.y + (size_t)m * ph.N + n, __ldg(a.gelu_lut + __half_as_ushort(__float2half_rn(val))));
-                    break;
-                case SO_RESIDUAL:
-                    __stcg(ph.y + (size_t)m * ph.N + n, rv[u] + val);
-                    break;
-                default: {  // SO_QKV: q rows, then K / V rows into the self cache at this step's position
-                    const int d = a.d, part = n / d, c = n - part * d;
-                    if (part == 0) {
-                        __stcg(ph.y + (size_t)m * d + c, val);
-                    } else {
-                        const int head = c / kHeadDim, dd = c % kHeadDim;
-                        const size_t row = (((size_t)a.slot[m] * a.L + ph.layer) * a.H + head) * (size_t)a.n_ctx + a.pos[m];
-                        (part == 1 ? a.sk : a.sv)[row * kHeadDim + dd] = __float2half_rn(val);
-                    }
+            default: {  // SO_QKV: q rows, then K / V rows into the self cache at this step's position
+                const int d = a.d, part = n / d, c = n - part * d;
+                if (part == 0) {
+                    __stcg(ph.y + (size_t)m * d + c, val);
+                } else {
+                    const int head = c / kHeadDim, dd = c % kHeadDim;
+                    const size_t row = (((size_t)sm.sq[16 + m] * a.L + ph.layer) * a.H + head) * (size_t)a.n_ctx + sm.sq[8 + m];
+                    (part == 1 ? a.sk : a.sv)[row * kHeadDim + dd] = __float2half_rn(val);
                 }
             }
         }
@@ -429,13 +459,28 @@ __global__ void __launch_bounds__(kStepThreads, 1)
     float *fl = reinterpret_cast<float *>(misc + kStepBars * 8 + 8 * (kHeadDim + 8) * 2 + kStepWarps * 8 * kRowPadPw * 2);
     sm.wm = reinterpret_cast<float(*)[8]>(fl);
     sm.wl = reinterpret_cast<float(*)[8]>(fl + 64);
-    sm.acc = fl + 128 + 2 * kStepMaxM;  // [64 rows][8]
-    sm.flags = reinterpret_cast<int *>(sm.acc + 64 * kStepMaxM);
+    sm.acc = fl + 128;                               // [64 rows][8]
+    sm.xs = sm.acc + 64 * kStepMaxM;                 // [64 rows][8]
+    sm.flags = reinterpret_cast<int *>(sm.xs + 64 * kStepMaxM);  // [32]
+    sm.sq = sm.flags + 32;                           // [40]
+    sm.nph = sm.sq + 40;                             // [kPhaseWords]
+    StepChunk *chl = reinterpret_cast<StepChunk *>(sm.nph + ((kPhaseWords + 1) & ~1));
+    sm.ch = chl;
     const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
     const int b = blockIdx.x;
     const StepPiece *pcs = a.pieces + (size_t)b * a.max_pieces;
-    const int *pp = a.phase_piece + (size_t)b * (a.n_phases + 1);
+    const int4 *pinfo = a.pinfo + (size_t)b * (a.n_phases + 1);
 
+    // the block's copy list and the streams' cross-cache slots (fixed for the call): shared memory,
+    // so that issuing a copy reads nothing from global memory
+    {
+        const unsigned long long *src = reinterpret_cast<const unsigned long long *>(a.chunks + (size_t)b * a.max_chunks);
+        unsigned long long *dst = reinterpret_cast<unsigned long long *>(chl);
+        for (int i = tid; i < a.n_chunks[b] * 3; i += kStepThreads) dst[i] = __ldg(src + i);
+        if (tid < a.S) sm.sq[32 + tid] = a.cross_stream[tid];
+        if (tid < kPhaseWords) sm.nph[tid] = __ldg(reinterpret_cast<const int *>(a.phases) + tid);
+    }
+    __syncthreads();
     if (tid == 0) {
         for (int i = 0; i < kStepBars; ++i) mbar_init(sm.bars + i, 1);
         fence_mbar_init();
@@ -443,19 +488,35 @@ __global__ void __launch_bounds__(kStepThreads, 1)
         // weights and encoder K / V do not depend on the previous kernel: start streaming now
         step_service(a, sm, &kmap, &vmap);
     }
-    __syncthreads();
     pdl_wait();  // tokens, positions, tables and liveness come from the previous step's selection
+    if (tid < a.M) {
+        sm.sq[tid] = a.tok[tid];
+        sm.sq[8 + tid] = a.pos[tid];
+        sm.sq[16 + tid] = a.slot[tid];
+        sm.sq[24 + tid] = a.active ? a.active[tid] : 1;
+    }
+    __syncthreads();
 
     bool ok = true;
+    int4 pi = pinfo[0], pn = pinfo[1];
     for (int p = 0; p < a.n_phases; ++p) {
+        const StepPhase ph = *reinterpret_cast<const StepPhase *>(sm.nph);  // phase p (written before a block barrier)
+        const int q0 = pi.x, q1 = pn.x, rbase = pi.y, rend = pi.z;
+        float bv[kEmitU];
+        step_bias_prefetch(ph, a.M, rbase, rend, bv);  // in flight across the barrier
+        step_ln_prefetch(sm, ph);
         if (p > 0) step_barrier(a, sm, (unsigned)p, &kmap, &vmap);
-        const StepPhase ph = a.phases[p];
-        const int q0 = pp[p], q1 = pp[p + 1];
+        // the next phase's descriptor, in flight during this one
+        int nph_word = 0;
+        int4 pnn = make_int4(0, 0, 0, 0);
+        if (p + 1 < a.n_phases) {
+            if (tid < kPhaseWords) nph_word = __ldg(reinterpret_cast<const int *>(a.phases + p + 1) + tid);
+            pnn = pinfo[p + 2];
+        }
         if (ph.kind == SK_GEMV) {
             // the whole activation rows fit in sm.act for M K <= 8 x 1280 (mlp.2 of one or two
             // sequences too): one stage; otherwise segments of 1280 columns over resident pieces
             const int K = ph.K, nseg = a.M * K <= kStepMaxM * kStepSeg ? 1 : (K + kStepSeg - 1) / kStepSeg;
-            const int rbase = q0 < q1 ? pcs[q0].r0 : 0, rend = q0 < q1 ? pcs[q1 - 1].r1 : 0;
             for (int i = tid; i < (rend - rbase) * kStepMaxM; i += kStepThreads) sm.acc[i] = 0.f;
             if (nseg == 1) {
                 step_stage(a, sm, ph, 0, K, K);
@@ -463,12 +524,12 @@ __global__ void __launch_bounds__(kStepThreads, 1)
                 for (int qi = q0; qi < q1; ++qi) {
                     const StepPiece pc = pcs[qi];
                     ok = step_wait_chunk(a, sm, pc.chunk, &kmap, &vmap) && ok;
-                    if (ok) step_dots(a, sm, reinterpret_cast<const __half *>(sm.ring + a.chunks[(size_t)b * a.max_chunks + pc.chunk].off),
-                                      K, pc.r0, pc.r1, rbase, 0, K, K);
-                    step_release(a, sm, pc.chunk, &kmap, &vmap);
+                    if (ok) step_dots(a, sm, reinterpret_cast<const __half *>(sm.ring + sm.ch[pc.chunk].off), K, pc.r0, pc.r1,
+                                      rbase, 0, K, K);
+                    step_release(sm, pc.chunk);
                 }
             } else {
-                // K > 1280 (mlp.2): every piece of the phase is resident; activations by segment
+                // every piece of the phase is resident; activations by segment
                 for (int qi = q0; qi < q1; ++qi) ok = step_wait_chunk(a, sm, pcs[qi].chunk, &kmap, &vmap) && ok;
                 ok = ok && !sm.flags[2];
                 for (int sg = 0; sg < nseg; ++sg) {
@@ -478,20 +539,20 @@ __global__ void __launch_bounds__(kStepThreads, 1)
                     __syncthreads();
                     for (int qi = q0; qi < q1 && ok; ++qi) {
                         const StepPiece pc = pcs[qi];
-                        step_dots(a, sm, reinterpret_cast<const __half *>(sm.ring + a.chunks[(size_t)b * a.max_chunks + pc.chunk].off),
-                                  K, pc.r0, pc.r1, rbase, k0, kn, kStepSeg);
+                        step_dots(a, sm, reinterpret_cast<const __half *>(sm.ring + sm.ch[pc.chunk].off), K, pc.r0, pc.r1,
+                                  rbase, k0, kn, kStepSeg);
                     }
                 }
-                for (int qi = q0; qi < q1; ++qi) step_release(a, sm, pcs[qi].chunk, &kmap, &vmap);
+                for (int qi = q0; qi < q1; ++qi) step_release(sm, pcs[qi].chunk);
             }
             __syncthreads();  // acc complete
-            if (ok) step_emit_all(a, sm, ph, rbase, rend);
+            if (ok) step_emit_all(a, sm, ph, rbase, rend, bv);
         } else if (ph.kind == SK_SELF) {
             // one (sequence, head) pair: keys gathered through the beam table, tiles of 128
             for (int qi = q0; qi < q1; ++qi) {
                 const int item = pcs[qi].r0, m = item / a.H, head = item - m * a.H;
-                if (a.active && !a.active[m]) continue;  // uniform over the block
-                const int len = a.pos[m] + 1;
+                if (!sm.sq[24 + m]) continue;  // uniform over the block
+                const int len = sm.sq[8 + m] + 1;
                 step_load_q(sm, a.q + (size_t)m * a.d, a.d, head, 1);
                 float mm[2] = {-INFINITY, -INFINITY}, ll[2] = {0.f, 0.f}, of[4][4];
 #pragma unroll
@@ -509,7 +570,7 @@ __global__ void __launch_bounds__(kStepThreads, 1)
                         vv[u] = make_uint4(0u, 0u, 0u, 0u);
                         if (r < nk) {
                             const int p = t0 + r;
-                            const int sl = a.table ? a.table[(size_t)m * a.n_ctx + p] : a.slot[m];
+                            const int sl = a.table ? a.table[(size_t)m * a.n_ctx + p] : sm.sq[16 + m];
                             const size_t off = ((((size_t)sl * a.L + ph.layer) * a.H + head) * (size_t)a.n_ctx + p) * kHeadDim + ch * 8;
                             kv[u] = __ldcg(reinterpret_cast<const uint4 *>(a.sk + off));
                             vv[u] = __ldcg(reinterpret_cast<const uint4 *>(a.sv + off));
@@ -547,7 +608,7 @@ __global__ void __launch_bounds__(kStepThreads, 1)
                 const int pair = pc.item / a.splits, s = pair / a.H, head = pair - s * a.H;
                 const int B = a.B;
                 ok = step_wait_chunk(a, sm, pc.chunk, &kmap, &vmap) && ok;
-                const StepChunk cc = a.chunks[(size_t)b * a.max_chunks + pc.chunk];
+                const StepChunk cc = sm.ch[pc.chunk];
                 step_load_q(sm, a.q + (size_t)s * B * a.d, a.d, head, B);
                 __syncthreads();
                 float mm[2] = {-INFINITY, -INFINITY}, ll[2] = {0.f, 0.f}, of[4][4];
@@ -586,7 +647,7 @@ __global__ void __launch_bounds__(kStepThreads, 1)
                         __stcg(xp + qq * (kHeadDim + 2) + 1, den);
                     }
                 }
-                step_release(a, sm, pc.chunk, &kmap, &vmap);
+                step_release(sm, pc.chunk);
                 // the block finishing a pair's last split combines the splits in split order
                 __threadfence();
                 __syncthreads();
@@ -622,13 +683,13 @@ __global__ void __launch_bounds__(kStepThreads, 1)
         } else {
             // vocabulary: logits of this block's embedding rows for every sequence, then the row epilogue
             pdl_trigger();  // the selection kernel may start its prologue
-            const int lo = q0 < q1 ? pcs[q0].r0 : 0, hi = q0 < q1 ? pcs[q1 - 1].r1 : 0, chs = hi - lo;
+            const int lo = rbase, hi = rend, chs = hi - lo;
             step_stage(a, sm, ph, 0, ph.K, kStepSeg);
             __syncthreads();
             for (int qi = q0; qi < q1; ++qi) {
                 const StepPiece pc = pcs[qi];
                 ok = step_wait_chunk(a, sm, pc.chunk, &kmap, &vmap) && ok;
-                const __half *w = reinterpret_cast<const __half *>(sm.ring + a.chunks[(size_t)b * a.max_chunks + pc.chunk].off);
+                const __half *w = reinterpret_cast<const __half *>(sm.ring + sm.ch[pc.chunk].off);
                 for (int r = pc.r0 + warp; r < pc.r1 && ok; r += kStepWarps) {
                     float acc[kStepMaxM];
 #pragma unroll
@@ -667,12 +728,17 @@ __global__ void __launch_bounds__(kStepThreads, 1)
                         if (lane == 0) sm.tile[(size_t)m * chs + (r - lo)] = v;
                     }
                 }
-                step_release(a, sm, pc.chunk, &kmap, &vmap);
+                step_release(sm, pc.chunk);
             }
             __syncthreads();
             LogitsArgs la = a.lg;
             logits_rows_epilogue(la, sm.tile, chs, a.M, 0, lo, hi, ok && !sm.flags[2], nullptr);
         }
+        // phase p + 1's descriptor: read at the loop's top, after this block barrier
+        if (tid < kPhaseWords) sm.nph[tid] = nph_word;
+        pi = pn;
+        pn = pnn;
+        __syncthreads();
     }
     // after a wait that ran out: the copies in flight land before the block exits
     __syncthreads();
@@ -702,16 +768,18 @@ bool step_plan_build(const StepPlanIn &in, StepPlanOut &out, std::string &why) {
     out.chunks.clear();
     out.pieces.clear();
     out.box_rows.assign(P, 0);
-    for (int p = 0; p < P; ++p) {  // weight rows per piece: a block's rows in pieces of <= 48 KB
+    // weight rows per piece: a GEMV block's rows in pieces of <= 48 KB; the vocabulary rows, a stream of
+    // a few hundred rows per block, in pieces of one row per warp, so that several are in flight at once
+    for (int p = 0; p < P; ++p) {
         const StepPhase &ph = in.phases[p];
         if (ph.kind != SK_GEMV && ph.kind != SK_LOGITS) continue;
         if (ph.K % 64 != 0) return why = "K", false;
         const int rpb = (ph.N + G - 1) / G;
         const int np = std::max(1, (int)(((size_t)rpb * ph.K * 2 + kStepPiece - 1) / kStepPiece));
-        out.box_rows[p] = (rpb + np - 1) / np;
+        out.box_rows[p] = ph.kind == SK_LOGITS ? std::min(rpb, kStepWarps) : (rpb + np - 1) / np;
     }
     out.n_chunks.assign(G, 0);
-    out.phase_piece.assign((size_t)G * (P + 1), 0);
+    out.pinfo.assign((size_t)G * (P + 1), make_int4(0, 0, 0, 0));
     std::vector<std::vector<StepChunk>> ch(G);
     std::vector<std::vector<StepPiece>> pc(G);
     for (int b = 0; b < G; ++b) {
@@ -720,18 +788,19 @@ bool step_plan_build(const StepPlanIn &in, StepPlanOut &out, std::string &why) {
         std::vector<int> all_resident;  // chunk ranges that must be resident together
         for (int p = 0; p < P; ++p) {
             const StepPhase &ph = in.phases[p];
-            out.phase_piece[(size_t)b * (P + 1) + p] = (int)Q.size();
+            out.pinfo[(size_t)b * (P + 1) + p].x = (int)Q.size();
             if (ph.kind == SK_GEMV || ph.kind == SK_LOGITS) {
                 const int N = ph.N, K = ph.K;
                 const int r0 = (int)((long long)b * N / G), r1 = (int)((long long)(b + 1) * N / G);
                 if (ph.kind == SK_GEMV && r1 - r0 > 64) return why = "rows per block", false;
+                out.pinfo[(size_t)b * (P + 1) + p].y = r0;
+                out.pinfo[(size_t)b * (P + 1) + p].z = r1;
                 const int rpp = out.box_rows[p];
                 const int first = (int)C.size();
                 for (int r = r0; r < r1; r += rpp) {
                     const int re = std::min(r1, r + rpp);
                     StepChunk c{};
-                    c.p = p;
-                    c.j0 = r;
+                    c.src = (unsigned long long)(uintptr_t)(in.W[p] + (size_t)r * K);
                     c.bytes = (unsigned)(re - r) * K * 2u;  // rows [r, re): contiguous, a multiple of 128 bytes
                     c.kind = 0;
                     Q.push_back(StepPiece{(int)C.size(), r, re, 0});
@@ -749,18 +818,16 @@ bool step_plan_build(const StepPlanIn &in, StepPlanOut &out, std::string &why) {
                     const int j0 = (int)((long long)j * in.A / out.splits), j1 = (int)((long long)(j + 1) * in.A / out.splits);
                     StepChunk c{};
                     c.kind = 1;
-                    c.s = pair / in.H;
-                    c.h = pair % in.H;
-                    c.layer = ph.layer;
-                    c.j0 = j0;
-                    c.nbox = (j1 - j0 + kAttnKeyTile - 1) / kAttnKeyTile;
+                    c.s = (unsigned char)(pair / in.H);
+                    c.src = ((unsigned long long)ph.layer * in.H + pair % in.H) * in.A + j0;
+                    c.nbox = (unsigned char)((j1 - j0 + kAttnKeyTile - 1) / kAttnKeyTile);
                     c.bytes = 2u * c.nbox * kBox;
                     Q.push_back(StepPiece{(int)C.size(), j0, j1, it});
                     C.push_back(c);
                 }
             }
         }
-        out.phase_piece[(size_t)b * (P + 1) + P] = (int)Q.size();
+        out.pinfo[(size_t)b * (P + 1) + P].x = (int)Q.size();
         // ring places (sequential, wrapping) and the releases each copy waits for
         unsigned pos = 0;
         for (size_t i = 0; i < C.size(); ++i) {
@@ -788,6 +855,7 @@ bool step_plan_build(const StepPlanIn &in, StepPlanOut &out, std::string &why) {
         out.max_pieces = std::max(out.max_pieces, (int)Q.size());
     }
     out.max_chunks = std::max(out.max_chunks, 1);
+    if (step_smem(out.max_chunks) > (size_t)kMaxDynSmem) return why = "copy list larger than shared memory", false;
     out.max_pieces = std::max(out.max_pieces, 1);
     out.chunks.assign((size_t)G * out.max_chunks, StepChunk{});
     out.pieces.assign((size_t)G * out.max_pieces, StepPiece{});
@@ -798,9 +866,11 @@ bool step_plan_build(const StepPlanIn &in, StepPlanOut &out, std::string &why) {
     return true;
 }
 
-static size_t step_smem() {
-    return (size_t)kStepRing + 2 * kBox + (size_t)kStepMaxM * kStepSeg * 4 + kStepBars * 8 + 8 * (kHeadDim + 8) * 2 +
-           (size_t)kStepWarps * 8 * kRowPadPw * 2 + (128 + 2 * kStepMaxM + 64 * kStepMaxM) * 4 + 32 * 4 + 1024;
+size_t step_smem(int max_chunks) {
+    const size_t misc = (size_t)kStepBars * 8 + 8 * (kHeadDim + 8) * 2 + (size_t)kStepWarps * 8 * kRowPadPw * 2 +
+                        (128 + 2 * 64 * kStepMaxM + 32 + 40 + ((kPhaseWords + 1) & ~1)) * 4 +
+                        (size_t)max_chunks * sizeof(StepChunk);
+    return (size_t)kStepRing + 2 * kBox + (size_t)kStepMaxM * kStepSeg * 4 + misc + 1024;
 }
 
 cudaError_t step_prepare() { return allow_dynamic_smem(k_step); }
@@ -809,7 +879,7 @@ cudaError_t launch_step(const StepArgs &a, int G, const void *kmap, const void *
     cudaLaunchConfig_t cfg = {};
     cfg.gridDim = dim3(G);
     cfg.blockDim = dim3(kStepThreads);
-    cfg.dynamicSmemBytes = step_smem();
+    cfg.dynamicSmemBytes = step_smem(a.max_chunks);
     cfg.stream = s;
     cudaLaunchAttribute attr[1];
     // every block resident at once (grid barriers): the cooperative attribute guarantees it; without

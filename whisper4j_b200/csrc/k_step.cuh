@@ -17,21 +17,25 @@ constexpr int kStepSeg = 1280;               // activation columns staged at a t
 constexpr unsigned kStepPiece = 48 * 1024;   // bytes of one weight piece (at most)
 constexpr unsigned kBox = kAttnKeyTile * kHeadDim * 2;  // one [128 x 64] f16 key tile: 16 KB
 constexpr int kRowPadPw = 24;  // halves per row of a warp's P^T block (kPwPad of attn_tile.cuh)
+constexpr int kMaxDynSmem = 227 * 1024;  // opt-in shared memory of one block on sm_100
 
 enum StepKind : int { SK_GEMV = 0, SK_SELF = 1, SK_CROSS = 2, SK_LOGITS = 3 };
 enum StepIn : int { SI_ACT = 0, SI_LN = 1, SI_EMBED_LN = 2 };
 enum StepOut : int { SO_QKV = 0, SO_STORE = 1, SO_GELU = 2, SO_RESIDUAL = 3 };
 
-// consumption-ordered copies of one block
+// consumption-ordered copies of one block (the kernel keeps its block's list in shared memory)
 struct StepChunk {
-    int p;            // kind 0: phase whose weight rows [j0, j0 + bytes / (2 K)) the chunk copies (one bulk copy)
-    unsigned bytes;   // bytes the chunk's mbarrier expects
-    unsigned off;     // ring offset (1024-aligned)
-    int kind;         // 0 weight rows, 1 encoder K / V boxes
-    int s, h, layer, j0, nbox;  // kind 1: stream index, head, layer, first key, boxes per K and V;
-                                // kind 0: j0 first weight row
-    int wait_rel;     // chunks consumed before this one may be issued
+    unsigned long long src;  // kind 0: global address of the weight rows (one bulk copy); kind 1: key row of
+                             // the first box without the stream term, (layer * H + head) * A + first key
+    unsigned bytes;          // bytes the chunk's mbarrier expects
+    int wait_rel;            // chunks consumed before this one may be issued
+    unsigned off;            // ring offset (1024-aligned)
+    unsigned char kind;      // 0 weight rows, 1 encoder K / V boxes
+    unsigned char s;         // kind 1: stream index
+    unsigned char nbox;      // kind 1: boxes per K and per V
+    unsigned char pad;
 };
+static_assert(sizeof(StepChunk) == 24, "StepChunk is copied to shared memory as three 8-byte words");
 
 struct StepPiece {
     int chunk;  // ring chunk (-1: none)
@@ -55,7 +59,7 @@ struct StepArgs {
     const StepChunk *chunks;      // [G][max_chunks]
     const int *n_chunks;          // [G]
     const StepPiece *pieces;      // [G][max_pieces]
-    const int *phase_piece;       // [G][n_phases + 1]
+    const int4 *pinfo;            // [G][n_phases + 1]: first piece, first and end row of the block's slice
     int max_chunks, max_pieces;
     // model
     int d, H, L, V, C, A, n_ctx, splits;
@@ -71,6 +75,7 @@ struct StepArgs {
     unsigned *gflag;              // per block, 128 bytes apart: the last barrier it may pass (reset likewise)
     LogitsArgs lg;                // vocabulary phase (x, part, masks, top-k; E, V, d)
     unsigned inflight;            // bytes of copies a block keeps in flight (at least one copy)
+    int bar_mode;                 // grid barrier: 0 last arriver releases per-block flags, 1 all poll the counter
     int *err;
 };
 
@@ -88,11 +93,12 @@ struct StepPlanOut {
     std::vector<StepChunk> chunks;   // [G][max_chunks]
     std::vector<StepPiece> pieces;   // [G][max_pieces]
     std::vector<int> n_chunks;       // [G]
-    std::vector<int> phase_piece;    // [G][phases + 1]
+    std::vector<int4> pinfo;         // [G][phases + 1]
 };
 
 // false (with the reason) when the step does not fit the kernel (too many streams, rows, ...)
 bool step_plan_build(const StepPlanIn &in, StepPlanOut &out, std::string &why);
+size_t step_smem(int max_chunks);
 cudaError_t step_prepare();
 // G blocks (one per SM, all resident); kmap / vmap: make_tmap_f16_rows maps of the cross K / V caches
 cudaError_t launch_step(const StepArgs &a, int G, const void *kmap, const void *vmap, bool coop, cudaStream_t s);

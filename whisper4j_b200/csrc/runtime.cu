@@ -150,7 +150,8 @@ struct w4j_ctx {
     bool use_step = false;  // W4J_STEP_KERNEL=1: one persistent kernel per step of <= 8 sequences
     bool step_coop = true;  // launch it with the cooperative attribute (dropped if capture refuses it)
     bool verbose = false;   // W4J_VERBOSE=1: say on stderr why a faster path was not taken
-    unsigned step_inflight = 48u << 10;  // W4J_STEP_INFLIGHT_KB: copy bytes in flight per block of the step kernel
+    unsigned step_inflight = 128u << 10;  // W4J_STEP_INFLIGHT_KB: copy bytes in flight per block of the step kernel
+    int step_bar_mode = 0;               // W4J_STEP_BAR: the step kernel's grid barrier (0 flags, 1 counter)
     bool attn_pairs = true;  // W4J_NO_ATTN_PAIRS=1: cross-attention of many streams on k_attn_stream
     std::map<std::pair<int, int>, StepPlanDev> step_plans;
     unsigned *gbar = nullptr;  // grid barrier counter of the step kernel
@@ -355,6 +356,7 @@ extern "C" int w4j_ctx_create(const w4j_dims *dims, int device, int max_streams,
     if (const char *ev = getenv("W4J_NO_TC_GEMM")) c->tc_gemm = ev[0] == '0';
     if (const char *ev = getenv("W4J_STEP_KERNEL")) c->use_step = ev[0] == '1';
     if (const char *ev = getenv("W4J_NO_ATTN_PAIRS")) c->attn_pairs = ev[0] == '0';
+    if (const char *ev = getenv("W4J_STEP_BAR")) c->step_bar_mode = ev[0] == '1';
     if (const char *ev = getenv("W4J_STEP_INFLIGHT_KB")) {
         const long kb = strtol(ev, nullptr, 10);
         if (kb >= 16 && kb <= 128) c->step_inflight = (unsigned)kb << 10;
@@ -1311,15 +1313,16 @@ static const w4j_ctx::StepPlanDev *get_step_plan(w4j_ctx *c, int S, int B) {
     StepPhase *dph = nullptr;
     StepChunk *dch = nullptr;
     StepPiece *dpc = nullptr;
-    int *dnc = nullptr, *dpp = nullptr;
+    int *dnc = nullptr;
+    int4 *dpp = nullptr;
     if (dalloc(c, &dph, in.phases.size()) || dalloc(c, &dch, out.chunks.size()) || dalloc(c, &dpc, out.pieces.size()) ||
-        dalloc(c, &dnc, out.n_chunks.size()) || dalloc(c, &dpp, out.phase_piece.size()))
+        dalloc(c, &dnc, out.n_chunks.size()) || dalloc(c, &dpp, out.pinfo.size()))
         return &pd;
     if (cudaMemcpy(dph, in.phases.data(), in.phases.size() * sizeof(StepPhase), cudaMemcpyHostToDevice) != cudaSuccess ||
         cudaMemcpy(dch, out.chunks.data(), out.chunks.size() * sizeof(StepChunk), cudaMemcpyHostToDevice) != cudaSuccess ||
         cudaMemcpy(dpc, out.pieces.data(), out.pieces.size() * sizeof(StepPiece), cudaMemcpyHostToDevice) != cudaSuccess ||
         cudaMemcpy(dnc, out.n_chunks.data(), out.n_chunks.size() * 4, cudaMemcpyHostToDevice) != cudaSuccess ||
-        cudaMemcpy(dpp, out.phase_piece.data(), out.phase_piece.size() * 4, cudaMemcpyHostToDevice) != cudaSuccess) {
+        cudaMemcpy(dpp, out.pinfo.data(), out.pinfo.size() * sizeof(int4), cudaMemcpyHostToDevice) != cudaSuccess) {
         cudaGetLastError();
         return &pd;
     }
@@ -1330,7 +1333,7 @@ static const w4j_ctx::StepPlanDev *get_step_plan(w4j_ctx *c, int S, int B) {
     a.chunks = dch;
     a.n_chunks = dnc;
     a.pieces = dpc;
-    a.phase_piece = dpp;
+    a.pinfo = dpp;
     a.max_chunks = out.max_chunks;
     a.max_pieces = out.max_pieces;
     a.d = d;
@@ -1356,6 +1359,7 @@ static const w4j_ctx::StepPlanDev *get_step_plan(w4j_ctx *c, int S, int B) {
     a.gbar = c->gbar;
     a.gflag = c->gflag;
     a.inflight = c->step_inflight;
+    a.bar_mode = c->step_bar_mode;
     pd.ok = true;
     return &pd;
 }
