@@ -49,6 +49,8 @@ CONFIGS = {
                             note="north star: large-v3-turbo batch 1, greedy, 224 forced tokens"),
     "turbo-greedy-32": dict(arch="large-v3-turbo", wtype="f16", beam=1, max_tokens=224, streams=32,
                             note="configs[3] at 8 GPUs: 256 streams = 32 per GPU, greedy, 224 tokens"),
+    "turbo-greedy-64": dict(arch="large-v3-turbo", wtype="f16", beam=1, max_tokens=224, streams=64,
+                            note="configs[3] at 4 GPUs: 256 streams = 64 per GPU, greedy, 224 tokens"),
     "large-v3-q8-beam5": dict(arch="large-v3", wtype="q8_0", beam=5, max_tokens=444, streams=1,
                               note="configs[4] per stream: large-v3 Q8_0, beam 5, 448-position context"),
 }
@@ -240,7 +242,7 @@ def run_reference(args, cfg, dims, rank, world):
 
 # kernel classes of w4j_set_kernel_timing
 KCLASSES = {1: "projections", 2: "self-attention", 3: "cross-attention", 4: "vocabulary logits", 5: "token selection"}
-KNAMES = {1: "k_gemv / k_gemm_tc", 2: "k_attn (self)", 3: "k_attn_stream / k_attn (cross)",
+KNAMES = {1: "k_gemv / k_gemm_tc", 2: "k_attn / k_attn_pairs (self)", 3: "k_attn_pairs / k_attn_stream / k_attn (cross)",
           4: "k_logits_tc / k_logits", 5: "k_select_*"}
 
 
