@@ -32,6 +32,11 @@ class _Dims(ctypes.Structure):
                 ("n_vocab", "n_audio_ctx", "n_text_ctx", "n_text_state", "n_text_head", "n_text_layer")]
 
 
+class _EncDims(ctypes.Structure):
+    _fields_ = [(n, ctypes.c_int) for n in
+                ("n_mels", "n_audio_ctx", "n_audio_state", "n_audio_head", "n_audio_layer")]
+
+
 def lib():
     global _lib
     with _lock:
@@ -71,6 +76,12 @@ def lib():
             L.orc_f16_to_f32.argtypes = [ctypes.c_uint16]
             L.orc_f32_to_f16.restype = ctypes.c_uint16
             L.orc_f32_to_f16.argtypes = [F]
+            L.orc_encoder_new.restype = P
+            L.orc_encoder_new.argtypes = [ctypes.POINTER(_EncDims)]
+            L.orc_encoder_free.argtypes = [P]
+            L.orc_encoder_set_tensor.argtypes = [P, ctypes.c_char_p, P, ctypes.c_long]
+            L.orc_encoder_check.argtypes = [P]
+            L.orc_encoder_forward.argtypes = [P, P, P]
             _lib = L
     return _lib
 
@@ -269,3 +280,44 @@ def apply_timestamp_rules(logits, generated, ts_begin, eot, is_first):
     g = _i32(list(generated) or [0])
     lib().orc_apply_timestamp_rules(_p(lg), _p(g), len(generated), ts_begin, eot, lg.size, int(is_first))
     return lg
+
+
+class OracleEncoder:
+    """The oracle's audio encoder (WhisperEncoder.forward), loaded from a parsed GGML model with
+    encoder tensors."""
+
+    def __init__(self, gmodel):
+        from whisper4j_b200 import ggml
+
+        dm = gmodel.dims
+        self.dims = dm
+        d = _EncDims(dm.n_mels, dm.n_audio_ctx, dm.n_audio_state, dm.n_audio_head, dm.n_audio_layer)
+        self._e = lib().orc_encoder_new(ctypes.byref(d))
+        if not self._e:
+            raise OracleError(lib().orc_last_error().decode())
+        for name, t in gmodel.tensors.items():
+            if name.startswith("encoder."):
+                arr = _f32(ggml.dequantize(t)).reshape(-1)
+                _check(lib().orc_encoder_set_tensor(self._e, name.encode(), _p(arr), arr.size))
+        _check(lib().orc_encoder_check(self._e))
+
+    def forward(self, mel) -> np.ndarray:
+        """mel: (n_mels, 2 n_audio_ctx) -> encoder output xa (n_audio_ctx, n_audio_state)."""
+        dm = self.dims
+        m = _f32(mel)
+        if m.shape != (dm.n_mels, 2 * dm.n_audio_ctx):
+            raise ValueError(f"mel must be ({dm.n_mels}, {2 * dm.n_audio_ctx}), got {m.shape}")
+        out = np.empty((dm.n_audio_ctx, dm.n_audio_state), np.float32)
+        _check(lib().orc_encoder_forward(self._e, _p(m), _p(out)))
+        return out
+
+    def close(self):
+        if self._e:
+            lib().orc_encoder_free(self._e)
+            self._e = None
+
+    def __del__(self):
+        try:
+            self.close()
+        except Exception:
+            pass

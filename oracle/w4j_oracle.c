@@ -1112,3 +1112,182 @@ done:
     free(logits); free(last); free(lp); free(top); free(cands);
     return rc;
 }
+
+/* ------------------------------------------------------------------------ */
+/* audio encoder (WhisperEncoder.java:42-76; Conv1d.java:38-80)             */
+/* ------------------------------------------------------------------------ */
+
+typedef struct {
+    float *attn_ln_w, *attn_ln_b;
+    float *q_wt, *q_b, *k_wt, *v_wt, *v_b, *o_wt, *o_b; /* transposed (in, out); the key has no bias */
+    float *mlp_ln_w, *mlp_ln_b;
+    float *m0_wt, *m0_b, *m2_wt, *m2_b;
+} orc_enc_layer;
+
+struct orc_encoder {
+    orc_enc_dims d;
+    float *conv1_wt, *conv1_b; /* conv weights as (in * k, out): Conv1d's (out, in * k) weightMatrix transposed */
+    float *conv2_wt, *conv2_b;
+    float *pos;                /* (n_audio_ctx, d) */
+    float *ln_w, *ln_b;        /* ln_post */
+    orc_enc_layer *layers;
+    float gelu_table[65536];
+};
+
+orc_encoder *orc_encoder_new(const orc_enc_dims *d) {
+    if (!d || d->n_mels <= 0 || d->n_audio_ctx <= 0 || d->n_audio_state <= 0 || d->n_audio_head <= 0 ||
+        d->n_audio_state % d->n_audio_head != 0 || d->n_audio_state / d->n_audio_head != 64 || d->n_audio_layer <= 0) {
+        fail("orc_encoder_new", "invalid dimensions");
+        return NULL;
+    }
+    orc_encoder *e = (orc_encoder *)calloc(1, sizeof *e);
+    if (!e) return NULL;
+    e->d = *d;
+    e->layers = (orc_enc_layer *)calloc((size_t)d->n_audio_layer, sizeof(orc_enc_layer));
+    build_gelu_table(e->gelu_table);
+    return e;
+}
+
+void orc_encoder_free(orc_encoder *e) {
+    if (!e) return;
+    for (int i = 0; i < e->d.n_audio_layer; i++) {
+        float **p = (float **)&e->layers[i];
+        for (size_t j = 0; j < sizeof(orc_enc_layer) / sizeof(float *); j++) free(p[j]);
+    }
+    free(e->layers);
+    free(e->conv1_wt); free(e->conv1_b); free(e->conv2_wt); free(e->conv2_b);
+    free(e->pos); free(e->ln_w); free(e->ln_b);
+    free(e);
+}
+
+int orc_encoder_set_tensor(orc_encoder *e, const char *name, const float *data, long n) {
+    const int d = e->d.n_audio_state, nm = e->d.n_mels;
+    if (strncmp(name, "encoder.", 8) != 0) return 1;
+    const char *s = name + 8;
+#define EXPECT(cnt)                                                                      \
+    do {                                                                                 \
+        if (n != (long)(cnt)) return fail("orc_encoder_set_tensor: wrong element count", name); \
+    } while (0)
+    struct { const char *nm; float **dst; int rows, cols; } top[] = {
+        {"conv1.weight", &e->conv1_wt, d, nm * 3}, {"conv1.bias", &e->conv1_b, 0, d},
+        {"conv2.weight", &e->conv2_wt, d, d * 3}, {"conv2.bias", &e->conv2_b, 0, d},
+        {"positional_embedding", &e->pos, 0, e->d.n_audio_ctx * d},
+        {"ln_post.weight", &e->ln_w, 0, d}, {"ln_post.bias", &e->ln_b, 0, d},
+    };
+    float **dst = NULL;
+    int rows = 0, cols = 0;
+    for (size_t i = 0; i < sizeof top / sizeof top[0] && !dst; i++)
+        if (!strcmp(s, top[i].nm)) dst = top[i].dst, rows = top[i].rows, cols = top[i].cols;
+    if (!dst) {
+        int li = -1, off = 0;
+        if (sscanf(s, "blocks.%d.%n", &li, &off) != 1 || li < 0 || li >= e->d.n_audio_layer)
+            return fail("orc_encoder_set_tensor: unknown tensor", name);
+        orc_enc_layer *L = &e->layers[li];
+        struct { const char *nm; float **dst; int rows, cols; } tab[] = {
+            {"attn_ln.weight", &L->attn_ln_w, 0, d}, {"attn_ln.bias", &L->attn_ln_b, 0, d},
+            {"attn.query.weight", &L->q_wt, d, d}, {"attn.query.bias", &L->q_b, 0, d},
+            {"attn.key.weight", &L->k_wt, d, d},
+            {"attn.value.weight", &L->v_wt, d, d}, {"attn.value.bias", &L->v_b, 0, d},
+            {"attn.out.weight", &L->o_wt, d, d}, {"attn.out.bias", &L->o_b, 0, d},
+            {"mlp_ln.weight", &L->mlp_ln_w, 0, d}, {"mlp_ln.bias", &L->mlp_ln_b, 0, d},
+            {"mlp.0.weight", &L->m0_wt, 4 * d, d}, {"mlp.0.bias", &L->m0_b, 0, 4 * d},
+            {"mlp.2.weight", &L->m2_wt, d, 4 * d}, {"mlp.2.bias", &L->m2_b, 0, d},
+        };
+        for (size_t i = 0; i < sizeof tab / sizeof tab[0] && !dst; i++)
+            if (!strcmp(s + off, tab[i].nm)) dst = tab[i].dst, rows = tab[i].rows, cols = tab[i].cols;
+        if (!dst) return fail("orc_encoder_set_tensor: unknown tensor", name);
+    }
+    free(*dst);
+    if (rows == 0) {
+        EXPECT(cols);
+        *dst = dup_f32(data, n);
+    } else {
+        EXPECT((long)rows * cols);
+        *dst = dup_transposed(data, rows, cols);
+    }
+    return *dst ? 0 : fail("orc_encoder_set_tensor: out of memory", name);
+#undef EXPECT
+}
+
+int orc_encoder_check(const orc_encoder *e) {
+    if (!e->conv1_wt || !e->conv1_b || !e->conv2_wt || !e->conv2_b) return fail("weight not found", "encoder.conv");
+    if (!e->pos) return fail("weight not found", "encoder.positional_embedding");
+    if (!e->ln_w || !e->ln_b) return fail("weight not found", "encoder.ln_post");
+    for (int i = 0; i < e->d.n_audio_layer; i++) {
+        const orc_enc_layer *L = &e->layers[i];
+        if (!L->attn_ln_w || !L->attn_ln_b || !L->q_wt || !L->q_b || !L->k_wt || !L->v_wt || !L->v_b || !L->o_wt ||
+            !L->o_b || !L->mlp_ln_w || !L->mlp_ln_b || !L->m0_wt || !L->m0_b || !L->m2_wt || !L->m2_b)
+            return fail("weight not found", "encoder.blocks");
+    }
+    return 0;
+}
+
+/* Conv1d.forward (:38-47): im2col (:49-64) as rows colT[t][ic * k + kk] = in(ic, t * stride - pad + kk)
+ * (zero outside), then the (out, in * k) weight matrix times col, summed over ic * k + kk ascending
+ * (Tensor.java:460-489), then the bias (:66-80).  in(ic, i) = src[ic * in_ld + i] for a channel-major
+ * source (the mel input), src[i * in_ld + ic] for a time-major one (conv1's output).  y: (out_len, out). */
+static void conv1d_k3(const float *src, int in_ch, int in_len, int in_ld, int time_major, int stride, int out_ch,
+                      const float *wt, const float *bias, float *y) {
+    const int pad = 1, k = 3, out_len = (in_len + 2 * pad - k) / stride + 1, R = in_ch * k;
+    float *col = (float *)malloc((size_t)out_len * R * sizeof(float));
+    for (int t = 0; t < out_len; t++)
+        for (int ic = 0; ic < in_ch; ic++)
+            for (int kk = 0; kk < k; kk++) {
+                const int i = t * stride - pad + kk;
+                float v = 0.0f;
+                if (i >= 0 && i < in_len) v = time_major ? src[(size_t)i * in_ld + ic] : src[(size_t)ic * in_ld + i];
+                col[(size_t)t * R + ic * k + kk] = v;
+            }
+    linear(col, out_len, R, wt, bias, out_ch, y);
+    free(col);
+}
+
+int orc_encoder_forward(const orc_encoder *e, const float *mel, float *out) {
+    if (!e || !mel || !out) return fail("orc_encoder_forward", "null argument");
+    if (orc_encoder_check(e)) return -1;
+    const int d = e->d.n_audio_state, T = e->d.n_audio_ctx, H = e->d.n_audio_head, nm = e->d.n_mels;
+    const int T1 = 2 * T; /* mel frames; conv2 (stride 2) halves them */
+    float *y1 = (float *)malloc((size_t)T1 * d * sizeof(float));
+    float *x = (float *)malloc((size_t)T * d * sizeof(float));
+    float *h = (float *)malloc((size_t)T * d * sizeof(float));
+    float *q = (float *)malloc((size_t)T * d * sizeof(float));
+    float *kk = (float *)malloc((size_t)T * d * sizeof(float));
+    float *v = (float *)malloc((size_t)T * d * sizeof(float));
+    float *att = (float *)malloc((size_t)T * d * sizeof(float));
+    float *m = (float *)malloc((size_t)T * 4 * d * sizeof(float));
+    const int nthr = g_threads > 1 ? g_threads : 1;
+    float *scores = (float *)malloc((size_t)T * nthr * sizeof(float));
+    int rc = 0;
+    if (!y1 || !x || !h || !q || !kk || !v || !att || !m || !scores) {
+        rc = fail("orc_encoder_forward", "out of memory");
+        goto done;
+    }
+    /* conv1 + GELU, conv2 + GELU (WhisperEncoder.java:47-54), transpose, + positional embedding (:56-58) */
+    conv1d_k3(mel, nm, T1, T1, 0, 1, d, e->conv1_wt, e->conv1_b, y1);
+    gelu_inplace(e->gelu_table, y1, (long)T1 * d);
+    conv1d_k3(y1, d, T1, d, 1, 2, d, e->conv2_wt, e->conv2_b, x);
+    gelu_inplace(e->gelu_table, x, (long)T * d);
+    for (long i = 0; i < (long)T * d; i++) x[i] = x[i] + e->pos[i];
+    /* blocks (:60-70): ResidualAttentionBlock.forwardWithAttn without cross-attention, mask or cache */
+    for (int l = 0; l < e->d.n_audio_layer; l++) {
+        const orc_enc_layer *L = &e->layers[l];
+        layer_norm(x, T, d, L->attn_ln_w, L->attn_ln_b, 1e-5f, h);
+        linear(h, T, d, L->q_wt, L->q_b, d, q);
+        linear(h, T, d, L->k_wt, NULL, d, kk);
+        linear(h, T, d, L->v_wt, L->v_b, d, v);
+        attn_job aj = {q, kk, v, att, d, H, T, -1, (float)(1.0 / sqrt(64.0)), scores, T};
+        if (g_threads > 1) par_for(T * H, attn_self_job, &aj);
+        else for (int th = 0; th < T * H; th++) attn_self_job(&aj, th);
+        linear(att, T, d, L->o_wt, L->o_b, d, h);
+        for (long i = 0; i < (long)T * d; i++) x[i] = h[i] + x[i];  /* attnOut[0].addInPlace(x) */
+        layer_norm(x, T, d, L->mlp_ln_w, L->mlp_ln_b, 1e-5f, h);
+        linear(h, T, d, L->m0_wt, L->m0_b, 4 * d, m);
+        gelu_inplace(e->gelu_table, m, (long)T * 4 * d);
+        linear(m, T, 4 * d, L->m2_wt, L->m2_b, d, q);
+        for (long i = 0; i < (long)T * d; i++) x[i] = x[i] + q[i];  /* result.addInPlace(mlpOut) */
+    }
+    layer_norm(x, T, d, e->ln_w, e->ln_b, 1e-5f, out); /* ln_post (:72) */
+done:
+    free(y1); free(x); free(h); free(q); free(kk); free(v); free(att); free(m); free(scores);
+    return rc;
+}

@@ -78,6 +78,22 @@ void orc_gelu(const orc_model *m, float *x, long n);
 float orc_f16_to_f32(uint16_t h);
 uint16_t orc_f32_to_f16(float f);
 
+/* ---- audio encoder (WhisperEncoder.java:42-76, Conv1d.java:38-80) ---- */
+typedef struct {
+    int n_mels, n_audio_ctx, n_audio_state, n_audio_head, n_audio_layer;
+} orc_enc_dims;
+typedef struct orc_encoder orc_encoder;
+
+orc_encoder *orc_encoder_new(const orc_enc_dims *d);
+void orc_encoder_free(orc_encoder *e);
+/* name: canonical GGML tensor name, data: f32 values in row-major order (GGML `ne` reversed).
+ * Returns 0 when stored, 1 when the tensor is not an encoder tensor, -1 on a bad name or size. */
+int orc_encoder_set_tensor(orc_encoder *e, const char *name, const float *data, long n);
+int orc_encoder_check(const orc_encoder *e);
+/* mel: (n_mels, 2 n_audio_ctx) row-major, as the reference's (1, n_mels, n_ctx) input;
+ * out: (n_audio_ctx, n_audio_state), the encoder output xa.  Returns 0 or -1. */
+int orc_encoder_forward(const orc_encoder *e, const float *mel, float *out);
+
 #ifdef __cplusplus
 }
 #endif

@@ -1,0 +1,65 @@
+"""The oracle's audio encoder (oracle/w4j_oracle.c, restating WhisperEncoder.forward and Conv1d)
+pinned to golden vectors from the reference's own numpy restatement
+(tools/generate_reference_values.py, via tests/golden/make_golden_encoder.py).
+
+The numpy restatement uses the exact tanh GELU; the Java encoder (and the oracle) use the
+f16-indexed GELU table, a relative difference of up to about 2^-11 per activation.  The encoder
+output is LayerNorm-ed (unit scale), so the rows are compared at max-abs 3e-2, the drift bound the
+reference's own cross-validation allows for its decoder (ValidateAgainstReferenceTest.java:145-161).
+"""
+import dataclasses
+import json
+import os
+
+import numpy as np
+import pytest
+
+from oracle import oracle as O
+from whisper4j_b200 import ggml
+
+from .golden.make_golden_encoder import CASES, mel_input
+
+GOLDEN = os.path.join(os.path.dirname(__file__), "golden")
+ATOL = 3e-2
+
+
+def golden(name):
+    with open(os.path.join(GOLDEN, f"encoder_{name}.json")) as f:
+        return json.load(f)
+
+
+def encoder_model(name):
+    dims, mseed, _, opts, _ = CASES[name]
+    return ggml.parse(ggml.synthetic_model_bytes(dims, mseed, include_encoder=True, **opts))
+
+
+@pytest.fixture(scope="module", autouse=True)
+def threads():
+    O.set_threads(min(16, os.cpu_count() or 1))
+    yield
+    O.set_threads(1)
+
+
+@pytest.mark.parametrize("name", ["enc_small", "enc_tiny"])
+def test_oracle_encoder_matches_reference_restatement(name):
+    g = golden(name)
+    dims, _, xseed, _, _ = CASES[name]
+    assert g["dims"] == list(dataclasses.astuple(dims))
+    enc = O.OracleEncoder(encoder_model(name))
+    out = enc.forward(mel_input(xseed, dims.n_mels, 2 * dims.n_audio_ctx))
+    assert out.shape == tuple(g["stages"]["encoder_output"]["shape"])
+    assert np.isfinite(out).all()
+    rows = sorted(int(r) for r in g["rows"])
+    want = np.array([g["rows"][str(r)] for r in rows], np.float32)
+    got = out[rows]
+    assert np.abs(got - want).max() < ATOL
+    # the whole output's first values and sums, as the reference's stage records keep them
+    st = g["stages"]["encoder_output"]
+    np.testing.assert_allclose(out.ravel()[:8], st["first8"], atol=ATOL)
+    assert abs(float(np.abs(out).sum()) - st["abs_sum"]) < 1e-2 * st["abs_sum"]
+
+
+def test_oracle_encoder_rejects_bad_input():
+    enc = O.OracleEncoder(encoder_model("enc_small"))
+    with pytest.raises(ValueError):
+        enc.forward(np.zeros((80, 10), np.float32))
