@@ -84,6 +84,17 @@ int w4j_set_encoder_output(w4j_ctx *ctx, int slot, const float *xa, int n_audio_
 int w4j_set_encoder_output_device(w4j_ctx *ctx, int slot, const float *xa_device, int n_audio_ctx);
 
 /*
+ * Run the audio encoder on the device (replaces WhisperEncoder.forward, W4J/nn/WhisperEncoder.java:42-76,
+ * with Conv1d.forward, W4J/nn/Conv1d.java:38-80): mel is the log-mel spectrogram, n_mels x n_frames f32
+ * row-major host memory (the reference's (1, n_mels, n_ctx) tensor), n_frames = 2 * n_audio_ctx.  The
+ * encoder weights ("encoder.*") come through w4j_upload_tensor like the decoder's, F16 or F32
+ * matrices.  xa_out (host, n_audio_ctx x n_audio_state f32) receives the encoder output when not
+ * NULL; slot >= 0 also sets that stream's encoder output on the device (as
+ * w4j_set_encoder_output_device, no host round trip), which needs a finalized decoder.
+ */
+int w4j_encoder_forward(w4j_ctx *ctx, const float *mel, int n_frames, float *xa_out, int slot);
+
+/*
  * WhisperDecoder.forward(tokens, xa, kvCache) (W4J/nn/WhisperDecoder.java:59-104)
  * for stream `slot`.  use_cache=1 appends the tokens to the slot's self-attention
  * cache (the kvCache map); use_cache=0 runs with an empty private cache and leaves

@@ -4,8 +4,9 @@ pinned to golden vectors from the reference's own numpy restatement
 
 The numpy restatement uses the exact tanh GELU; the Java encoder (and the oracle) use the
 f16-indexed GELU table, a relative difference of up to about 2^-11 per activation.  The encoder
-output is LayerNorm-ed (unit scale), so the rows are compared at max-abs 3e-2, the drift bound the
-reference's own cross-validation allows for its decoder (ValidateAgainstReferenceTest.java:145-161).
+output is LayerNorm-ed (unit scale); the rows are compared at max-abs 5e-3 (observed 7e-4), well
+inside the 3e-2 drift bound the reference's own cross-validation allows for its decoder
+(ValidateAgainstReferenceTest.java:145-161).
 """
 import dataclasses
 import json
@@ -20,7 +21,7 @@ from whisper4j_b200 import ggml
 from .golden.make_golden_encoder import CASES, mel_input
 
 GOLDEN = os.path.join(os.path.dirname(__file__), "golden")
-ATOL = 3e-2
+ATOL = 5e-3  # observed 7e-4 (the GELU table against tanh)
 
 
 def golden(name):

@@ -77,6 +77,28 @@ struct LayerDev {
 };
 enum Proj : int { PROJ_QKV = 0, PROJ_O = 1, PROJ_XQ = 2, PROJ_XO = 3, PROJ_M0 = 4, PROJ_M2 = 5, PROJ_XK = 6, PROJ_XV = 7 };
 
+// The audio encoder on the same device as the decoder (WhisperEncoder.java:27-39): its weights come
+// through w4j_upload_tensor ("encoder.*", raw GGML payloads like the decoder's), its work buffers
+// are allocated at the first w4j_encoder_forward.
+struct EncLayer {
+    DMat qkv, o, m0, m2;  // q, k, v fused into [3 d][d] (the key has no bias: zeros)
+    float *bqkv = nullptr, *bo = nullptr, *bm0 = nullptr, *bm2 = nullptr;
+    float *ln1g = nullptr, *ln1b = nullptr, *ln2g = nullptr, *ln2b = nullptr;
+    alignas(64) unsigned char tmap[4][128] = {};  // qkv, o, m0, m2
+};
+struct EncDev {
+    DMat c1, c2;  // conv weights as [d][in * 3] f16 (Conv1d's weightMatrix); conv1's columns padded to k1
+    float *b1 = nullptr, *b2 = nullptr, *pos = nullptr, *lng = nullptr, *lnb = nullptr;
+    std::vector<EncLayer> layers;
+    alignas(64) unsigned char c1map[128] = {}, c2map[128] = {};
+    int k1 = 0;
+    bool maps_ok = false, q8_skipped = false;
+    std::set<std::string> uploaded;
+    float *mel = nullptr, *col = nullptr, *y1 = nullptr, *x = nullptr, *qkv = nullptr, *att = nullptr, *hid = nullptr,
+          *xa = nullptr;
+    __half *qkvh = nullptr, *hilo = nullptr;
+};
+
 struct GraphKey {
     int mode, S, B, eot, ts_begin, n_sup, max_tokens, ns, n_prompt, time_class;
     float temperature;
@@ -90,6 +112,7 @@ struct w4j_ctx {
     std::mutex mu;
     int V = 0, C = 0, A = 0, d = 0, H = 0, L = 0;
     w4j_dims dims{};
+    EncDev enc;
     int max_streams = 0, max_beam = 0, n_slots = 0, M_max = 0;
     int cap = 0;   // self-cache rows per slot: n_text_ctx, grown on demand (the reference's cache is unbounded)
     int Mbuf = 0;  // activation rows: max(M_max, n_text_ctx) (a multi-token forward is one pass of its tokens)
@@ -553,19 +576,106 @@ static int upload_mat(w4j_ctx *c, DMat &m, int rows_total, int row0, int N, int 
     return 0;
 }
 
+// An "encoder.*" tensor (WhisperEncoder.java:27-39, :86-105): matrices stored f16 ([N][K] rows, the
+// convolutions as Conv1d's (out, in * 3) weightMatrix), vectors f32.  Q8_0 encoder matrices are
+// skipped (return 1): the encoder's row counts (1500 and 3000) run on the tensor cores with f16 weights.
+static int upload_encoder_tensor(w4j_ctx *c, const std::string &nm, int type, int64_t nel, const void *data,
+                                 size_t nbytes) {
+    const w4j_dims &dm = c->dims;
+    const int d = dm.n_audio_state, T = dm.n_audio_ctx, nmel = dm.n_mels;
+    if (d <= 0 || d % 64 || dm.n_audio_head <= 0 || d != dm.n_audio_head * kHeadDim || dm.n_audio_layer <= 0 ||
+        nmel <= 0 || T <= 0)
+        return set_err(W4J_ERR_ARG, "encoder dims: n_audio_state must be 64 x n_audio_head");
+    EncDev &e = c->enc;
+    if (e.layers.empty()) {
+        e.layers.resize(dm.n_audio_layer);
+        for (EncLayer &ly : e.layers) TRY(dalloc(c, &ly.bqkv, 3 * (size_t)d));
+        e.k1 = (nmel * 3 + 63) / 64 * 64;
+    }
+    if (type == W4J_GGML_Q8_0 && nel > d) {  // skipped (the decoder still loads); w4j_encoder_forward says why
+        e.q8_skipped = true;
+        return 1;
+    }
+    const std::string s = nm.substr(8);
+    auto vec = [&](float **dst, int64_t n, size_t off = 0) -> int {
+        if (nel != n) return set_err(W4J_ERR_ARG, "%s: expected %lld elements", nm.c_str(), (long long)n);
+        return upload_vec(c, dst, (size_t)n, data, nbytes, type, off);
+    };
+    if (s == "conv1.weight") {  // (d, n_mels, 3): rows of n_mels * 3, padded with zeros to k1 columns
+        if (nel != (int64_t)d * nmel * 3) return set_err(W4J_ERR_ARG, "%s: expected (%d, %d, 3)", nm.c_str(), d, nmel);
+        std::vector<float> f;
+        TRY(host_f32(data, nbytes, type, (size_t)nel, f));
+        std::vector<__half> h((size_t)d * e.k1, __float2half(0.f));
+        for (int o = 0; o < d; ++o)
+            for (int r = 0; r < nmel * 3; ++r) h[(size_t)o * e.k1 + r] = __float2half_rn(f[(size_t)o * nmel * 3 + r]);
+        TRY(upload_mat(c, e.c1, d, 0, d, e.k1, h.data(), h.size() * 2, W4J_GGML_F16));
+    } else if (s == "conv2.weight") {
+        if (nel != (int64_t)d * d * 3) return set_err(W4J_ERR_ARG, "%s: expected (%d, %d, 3)", nm.c_str(), d, d);
+        TRY(upload_mat(c, e.c2, d, 0, d, 3 * d, data, nbytes, type));
+    } else if (s == "conv1.bias") {
+        TRY(vec(&e.b1, d));
+    } else if (s == "conv2.bias") {
+        TRY(vec(&e.b2, d));
+    } else if (s == "positional_embedding") {
+        TRY(vec(&e.pos, (int64_t)T * d));
+    } else if (s == "ln_post.weight") {
+        TRY(vec(&e.lng, d));
+    } else if (s == "ln_post.bias") {
+        TRY(vec(&e.lnb, d));
+    } else {
+        int li = -1, off = 0;
+        if (sscanf(s.c_str(), "blocks.%d.%n", &li, &off) != 1 || li < 0 || li >= dm.n_audio_layer)
+            return set_err(W4J_ERR_ARG, "unknown encoder tensor %s", nm.c_str());
+        EncLayer &ly = e.layers[li];
+        const std::string t = s.substr(off);
+        struct MatRole { const char *nm; DMat *m; int rows_total, row0, N, K; };
+        const MatRole mats[] = {
+            {"attn.query.weight", &ly.qkv, 3 * d, 0, d, d}, {"attn.key.weight", &ly.qkv, 3 * d, d, d, d},
+            {"attn.value.weight", &ly.qkv, 3 * d, 2 * d, d, d}, {"attn.out.weight", &ly.o, d, 0, d, d},
+            {"mlp.0.weight", &ly.m0, 4 * d, 0, 4 * d, d}, {"mlp.2.weight", &ly.m2, d, 0, d, 4 * d},
+        };
+        bool found = false;
+        for (const MatRole &r : mats) {
+            if (t != r.nm) continue;
+            if (nel != (int64_t)r.N * r.K) return set_err(W4J_ERR_ARG, "%s: expected (%d, %d)", nm.c_str(), r.N, r.K);
+            TRY(upload_mat(c, *r.m, r.rows_total, r.row0, r.N, r.K, data, nbytes, type));
+            found = true;
+        }
+        struct VecRole { const char *nm; float **dst; int n; size_t off; };
+        const VecRole vecs[] = {
+            {"attn.query.bias", &ly.bqkv, d, 0},      {"attn.key.bias", &ly.bqkv, d, (size_t)d},
+            {"attn.value.bias", &ly.bqkv, d, 2 * (size_t)d}, {"attn.out.bias", &ly.bo, d, 0},
+            {"mlp.0.bias", &ly.bm0, 4 * d, 0},        {"mlp.2.bias", &ly.bm2, d, 0},
+            {"attn_ln.weight", &ly.ln1g, d, 0},       {"attn_ln.bias", &ly.ln1b, d, 0},
+            {"mlp_ln.weight", &ly.ln2g, d, 0},        {"mlp_ln.bias", &ly.ln2b, d, 0},
+        };
+        for (const VecRole &r : vecs) {
+            if (found || t != r.nm) continue;
+            TRY(vec(r.dst, r.n, r.off));
+            found = true;
+        }
+        if (!found) return set_err(W4J_ERR_ARG, "unknown encoder tensor %s", nm.c_str());
+    }
+    e.uploaded.insert(nm);
+    e.maps_ok = false;
+    return W4J_OK;
+}
+
 extern "C" int w4j_upload_tensor(w4j_ctx *c, const char *name, int type, const int64_t *ne, int n_dims,
                                  const void *data, size_t nbytes) {
     if (!c || !name || !ne || !data) return set_err(W4J_ERR_ARG, "w4j_upload_tensor: null argument");
     std::lock_guard<std::mutex> g(c->mu);
     CUDA_TRY(cudaSetDevice(c->device));
     const std::string nm(name);
-    if (nm.rfind("decoder.", 0) != 0) return 1;  // encoder tensors are not on this path
+    const bool enc = nm.rfind("encoder.", 0) == 0;
+    if (!enc && nm.rfind("decoder.", 0) != 0) return 1;  // neither encoder nor decoder: not on this path
     if (n_dims < 1 || n_dims > 4) return set_err(W4J_ERR_ARG, "%s: n_dims %d", name, n_dims);
     int64_t nel = 1;
     for (int i = 0; i < n_dims; ++i) {
         if (ne[i] <= 0) return set_err(W4J_ERR_ARG, "%s: bad shape", name);
         nel *= ne[i];
     }
+    if (enc) return upload_encoder_tensor(c, nm, type, nel, data, nbytes);
     const int d = c->d;
     auto shape_is = [&](int64_t in, int64_t out) { return ne[0] == in && nel == in * out; };
     std::string s = nm.substr(8);
@@ -715,6 +825,131 @@ extern "C" int w4j_set_encoder_output_device(w4j_ctx *c, int slot, const float *
     if (slot < 0 || slot >= c->max_streams) return set_err(W4J_ERR_ARG, "slot %d out of range", slot);
     if (n_audio_ctx != c->A) return set_err(W4J_ERR_ARG, "encoder output has %d frames, model expects %d", n_audio_ctx, c->A);
     return prefill(c, slot, xa);
+}
+
+// ---------------------------------------------------------------------------
+// audio encoder (WhisperEncoder.forward, WhisperEncoder.java:42-76)
+// ---------------------------------------------------------------------------
+static std::vector<std::string> encoder_names(int L) {
+    std::vector<std::string> r = {"encoder.conv1.weight", "encoder.conv1.bias", "encoder.conv2.weight",
+                                  "encoder.conv2.bias", "encoder.positional_embedding", "encoder.ln_post.weight",
+                                  "encoder.ln_post.bias"};
+    const char *per[] = {"attn.query.weight", "attn.query.bias", "attn.key.weight", "attn.value.weight",
+                         "attn.value.bias", "attn.out.weight", "attn.out.bias", "attn_ln.weight", "attn_ln.bias",
+                         "mlp.0.weight", "mlp.0.bias", "mlp.2.weight", "mlp.2.bias", "mlp_ln.weight", "mlp_ln.bias"};
+    for (int l = 0; l < L; ++l)
+        for (const char *q : per) r.push_back("encoder.blocks." + std::to_string(l) + "." + q);
+    return r;
+}
+
+// y = act . W^T + bias (+ epilogue) on the tcgen05 GEMM; above 128 rows (every real model: 1500 and
+// 3000) the activations are first staged as f16 hi / lo rows (LayerNorm applied when ln_g is given).
+static int enc_gemm(w4j_ctx *c, const DMat &W, const void *wmap, int M, const float *act, const float *bias,
+                    const float *ln_g, const float *ln_b, int out_mode, float *y) {
+    GemvArgs g;
+    g.W = W;
+    g.bias = bias;
+    g.M = M;
+    g.in_mode = ln_g ? IN_LN : IN_ACT;
+    g.act = act;
+    g.ln_g = ln_g;
+    g.ln_b = ln_b;
+    g.out_mode = out_mode;
+    g.y = y;
+    g.gelu_lut = c->gelu_lut;
+    if (!gemm_tc_supported(g, c->sm_count))
+        return set_err(W4J_ERR_ARG, "encoder projection %d x %d x %d outside the tensor-core GEMM", M, W.N, W.K);
+    if (!gemm_tc_staged(g)) {  // up to 128 rows (short test models): the B operand built in shared memory
+        CUDA_TRY(launch_gemm_tc(g, wmap, nullptr, c->sm_count, c->stream, false));
+        return 0;
+    }
+    alignas(64) unsigned char bmap[128];
+    if (!make_tmap_f16_box(bmap, c->enc.hilo, act_hilo_rows(M), W.K, 256))
+        return set_err(W4J_ERR_CUDA, "encoder: activation tensor map");
+    CUDA_TRY(launch_act_hilo(g, c->enc.hilo, c->stream, false));
+    CUDA_TRY(launch_gemm_tc(g, wmap, bmap, c->sm_count, c->stream, false));
+    return 0;
+}
+
+static int enc_prepare(w4j_ctx *c) {
+    EncDev &e = c->enc;
+    const w4j_dims &dm = c->dims;
+    for (const std::string &n : encoder_names(dm.n_audio_layer))
+        if (!e.uploaded.count(n))
+            return set_err(W4J_ERR_STATE, "encoder weight not uploaded: %s%s", n.c_str(),
+                           e.q8_skipped ? " (Q8_0 encoder matrices are not taken by the device encoder)" : "");
+    const int d = dm.n_audio_state, T = dm.n_audio_ctx;
+    if (!e.maps_ok) {
+        bool ok = make_tmap_f16_rows(e.c1map, e.c1.h, d, e.k1) && make_tmap_f16_rows(e.c2map, e.c2.h, d, 3 * d);
+        for (EncLayer &ly : e.layers)
+            ok = ok && make_tmap_f16_rows(ly.tmap[0], ly.qkv.h, 3 * d, d) && make_tmap_f16_rows(ly.tmap[1], ly.o.h, d, d) &&
+                 make_tmap_f16_rows(ly.tmap[2], ly.m0.h, 4 * d, d) && make_tmap_f16_rows(ly.tmap[3], ly.m2.h, d, 4 * d);
+        if (!ok) return set_err(W4J_ERR_CUDA, "encoder: weight tensor maps");
+        e.maps_ok = true;
+    }
+    if (!e.mel) {
+        const size_t T1 = 2 * (size_t)T;
+        TRY(dalloc(c, &e.mel, (size_t)dm.n_mels * T1));
+        TRY(dalloc(c, &e.col, std::max(T1 * e.k1, (size_t)T * 3 * d)));
+        TRY(dalloc(c, &e.y1, T1 * d));
+        TRY(dalloc(c, &e.x, (size_t)T * d));
+        TRY(dalloc(c, &e.qkv, (size_t)T * 3 * d));
+        TRY(dalloc(c, &e.att, (size_t)T * d));
+        TRY(dalloc(c, &e.hid, (size_t)T * 4 * d));
+        TRY(dalloc(c, &e.xa, (size_t)T * d));
+        TRY(dalloc(c, &e.qkvh, (size_t)T * 3 * d));
+        TRY(dalloc(c, &e.hilo, (size_t)act_hilo_rows((int)T1) * std::max(e.k1, 4 * d)));
+    }
+    return 0;
+}
+
+// The encoder over one mel spectrogram (n_mels x 2 n_audio_ctx, device), output in c->enc.xa.
+static int enc_run(w4j_ctx *c) {
+    EncDev &e = c->enc;
+    const w4j_dims &dm = c->dims;
+    const int d = dm.n_audio_state, T = dm.n_audio_ctx, T1 = 2 * T, H = dm.n_audio_head;
+    cudaStream_t st = c->stream;
+    // conv1 + GELU (:46-47), conv2 + GELU (:50-51), + positional embedding (:56-58)
+    CUDA_TRY(launch_enc_im2col(e.mel, dm.n_mels, T1, false, 1, T1, e.k1, e.col, st));
+    TRY(enc_gemm(c, e.c1, e.c1map, T1, e.col, e.b1, nullptr, nullptr, OUT_GELU, e.y1));
+    CUDA_TRY(launch_enc_im2col(e.y1, d, T1, true, 2, T, 3 * d, e.col, st));
+    TRY(enc_gemm(c, e.c2, e.c2map, T, e.col, e.b2, nullptr, nullptr, OUT_GELU, e.x));
+    CUDA_TRY(launch_enc_add(e.x, e.pos, (long long)T * d, st));
+    // blocks (:60-70): x += attn(attn_ln(x)); x += mlp(mlp_ln(x))
+    for (EncLayer &ly : e.layers) {
+        TRY(enc_gemm(c, ly.qkv, ly.tmap[0], T, e.x, ly.bqkv, ly.ln1g, ly.ln1b, OUT_STORE, e.qkv));
+        CUDA_TRY(launch_enc_qkv_f16(e.qkv, T, H, e.qkvh, st));
+        CUDA_TRY(launch_enc_attn(e.qkvh, T, H, e.att, st));
+        TRY(enc_gemm(c, ly.o, ly.tmap[1], T, e.att, ly.bo, nullptr, nullptr, OUT_RESIDUAL, e.x));
+        TRY(enc_gemm(c, ly.m0, ly.tmap[2], T, e.x, ly.bm0, ly.ln2g, ly.ln2b, OUT_GELU, e.hid));
+        TRY(enc_gemm(c, ly.m2, ly.tmap[3], T, e.hid, ly.bm2, nullptr, nullptr, OUT_RESIDUAL, e.x));
+    }
+    CUDA_TRY(launch_enc_ln(e.x, T, d, e.lng, e.lnb, e.xa, st));  // ln_post (:72)
+    return 0;
+}
+
+extern "C" int w4j_encoder_forward(w4j_ctx *c, const float *mel, int n_frames, float *xa_out, int slot) {
+    if (!c || !mel) return set_err(W4J_ERR_ARG, "w4j_encoder_forward: null argument");
+    std::lock_guard<std::mutex> g(c->mu);
+    CUDA_TRY(cudaSetDevice(c->device));
+    const w4j_dims &dm = c->dims;
+    if (n_frames != 2 * dm.n_audio_ctx)
+        return set_err(W4J_ERR_ARG, "mel has %d frames, the encoder takes %d", n_frames, 2 * dm.n_audio_ctx);
+    if (slot >= 0) {
+        TRY(check_ready(c));
+        if (slot >= c->max_streams) return set_err(W4J_ERR_ARG, "slot %d out of range", slot);
+        if (dm.n_audio_state != c->d) return set_err(W4J_ERR_ARG, "n_audio_state differs from n_text_state");
+    }
+    TRY(enc_prepare(c));
+    const size_t mel_bytes = (size_t)dm.n_mels * n_frames * 4;
+    CUDA_TRY(cudaMemcpyAsync(c->enc.mel, mel, mel_bytes, cudaMemcpyHostToDevice, c->stream));
+    TRY(enc_run(c));
+    if (xa_out)
+        CUDA_TRY(cudaMemcpyAsync(xa_out, c->enc.xa, (size_t)dm.n_audio_ctx * dm.n_audio_state * 4, cudaMemcpyDeviceToHost,
+                                 c->stream));
+    CUDA_TRY(cudaStreamSynchronize(c->stream));
+    if (slot >= 0) TRY(prefill(c, slot, c->enc.xa));
+    return W4J_OK;
 }
 
 // ---------------------------------------------------------------------------

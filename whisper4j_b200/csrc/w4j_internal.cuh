@@ -348,7 +348,14 @@ bool gemm_tc_staged(const GemvArgs &a);  // the projection reads staged activati
 bool gemm_tc_supported(const GemvArgs &a, int sms);  // the tensor-core kernel takes this projection
 int act_hilo_rows(int M);
 cudaError_t launch_act_hilo(const GemvArgs &a, __half *out, cudaStream_t s, bool pdl);
-// tensor map of a row-major f16 matrix read in [box_rows x 64 cols] boxes, 128-byte swizzle
+
+// audio encoder (k_encoder.cu)
+cudaError_t launch_enc_im2col(const float *src, int in_ch, int in_len, bool time_major, int stride, int out_len, int kp,
+                              float *out, cudaStream_t s);
+cudaError_t launch_enc_add(float *x, const float *p, long long n, cudaStream_t s);
+cudaError_t launch_enc_ln(const float *x, int rows, int n, const float *g, const float *b, float *y, cudaStream_t s);
+cudaError_t launch_enc_qkv_f16(const float *qkv, int T, int H, __half *out, cudaStream_t s);
+cudaError_t launch_enc_attn(const __half *qkvh, int T, int H, float *out, cudaStream_t s);// tensor map of a row-major f16 matrix read in [box_rows x 64 cols] boxes, 128-byte swizzle
 bool make_tmap_f16_box(void *map_out, const void *base, int rows, int cols, int box_rows);
 cudaError_t select_prepare();
 cudaError_t attn_prepare();

@@ -79,7 +79,7 @@ class WhisperDecoder:
         self._ctx = h
         try:
             for name, t in model.tensors.items():
-                if not name.startswith("decoder."):
+                if not name.startswith(("decoder.", "encoder.")):
                     continue
                 ne = (ctypes.c_int64 * len(t.ne))(*t.ne)
                 buf = np.frombuffer(t.data, dtype=np.uint8)
@@ -118,6 +118,24 @@ class WhisperDecoder:
             a = np.ascontiguousarray(np.asarray(xa, dtype=np.float32).reshape(-1, self.dims.n_text_state))
             check(lib().w4j_set_encoder_output(self._ctx, slot, _ptr(a), a.shape[0]))
         self._xa_ids[slot] = id(xa)
+
+    def encode(self, mel, slot: int | None = None, return_output: bool = True):
+        """WhisperEncoder.forward on the device: mel (n_mels x 2 n_audio_ctx, as the reference's
+        (1, n_mels, n_ctx) input) -> encoder output xa (n_audio_ctx x n_audio_state), with the model's
+        "encoder.*" weights on this decoder's device.  With ``slot`` the output also becomes that
+        stream's encoder output (cross K/V projected on the device, no host round trip)."""
+        dm = self.dims
+        m = np.ascontiguousarray(np.asarray(mel, dtype=np.float32))
+        if m.ndim == 3 and m.shape[0] == 1:
+            m = m[0]
+        if m.ndim != 2 or m.shape[0] != dm.n_mels:
+            raise ValueError(f"mel must be ({dm.n_mels}, {2 * dm.n_audio_ctx}), got {m.shape}")
+        out = np.empty((dm.n_audio_ctx, dm.n_audio_state), np.float32) if return_output else None
+        check(lib().w4j_encoder_forward(self._ctx, _ptr(m), m.shape[1], _ptr(out) if out is not None else None,
+                                        -1 if slot is None else slot))
+        if slot is not None:
+            self._xa_ids[slot] = ("encoder", id(mel))
+        return out
 
     def _slot_for(self, xa, slot):
         if xa is None:
