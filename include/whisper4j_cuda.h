@@ -64,8 +64,10 @@ int w4j_ctx_destroy(w4j_ctx *ctx);
  * Upload one decoder tensor straight from the GGML file's bytes (the hook next
  * to GgmlLoader.dequantize, W4J/model/GgmlLoader.java:185-202).  `ne` is the
  * GGML shape (fastest dimension first), `data` the raw payload: F32, F16 or
- * Q8_0 (34-byte blocks).  Encoder tensors are accepted and ignored (return 1).
- * Unknown decoder tensor names, wrong shapes and unsupported types are errors.
+ * Q8_0 (34-byte blocks).  Encoder tensors ("encoder.*") are kept on the same
+ * device for w4j_encoder_forward (F16 / F32 matrices; a Q8_0 encoder matrix is
+ * skipped with return 1).  Other names return 1.  Unknown decoder or encoder
+ * tensor names, wrong shapes and unsupported types are errors.
  */
 int w4j_upload_tensor(w4j_ctx *ctx, const char *name, int ggml_type, const int64_t *ne, int n_dims,
                       const void *data, size_t nbytes);
@@ -93,6 +95,20 @@ int w4j_set_encoder_output_device(w4j_ctx *ctx, int slot, const float *xa_device
  * w4j_set_encoder_output_device, no host round trip), which needs a finalized decoder.
  */
 int w4j_encoder_forward(w4j_ctx *ctx, const float *mel, int n_frames, float *xa_out, int slot);
+
+/*
+ * The log-mel front end on the device (replaces FeatureExtractor.extract + padOrTrim,
+ * W4J/audio/FeatureExtractor.java:68-160, with the model's filters as the
+ * FeatureExtractor(nMels, melFilterData, nFftBins) constructor takes them, :44-55).
+ * w4j_upload_mel_filters: the GGML file's mel filters, n_mels x n_bins f32 (n_fft = 2 (n_bins - 1)).
+ * w4j_log_mel: 16 kHz mono samples -> n_mels x (2 n_audio_ctx) log-mel (host, when mel_out is not NULL).
+ * w4j_encode_audio: the same spectrogram straight into the encoder (w4j_encoder_forward's outputs:
+ * xa_out on the host, and / or stream `slot`'s cross K/V on the device) — one chunk of
+ * WhisperModel.transcribe's feature + encoder stage (W4J/WhisperModel.java:361-366).
+ */
+int w4j_upload_mel_filters(w4j_ctx *ctx, const float *filters, int n_mels, int n_bins);
+int w4j_log_mel(w4j_ctx *ctx, const float *audio, int n_samples, float *mel_out);
+int w4j_encode_audio(w4j_ctx *ctx, const float *audio, int n_samples, float *xa_out, int slot);
 
 /*
  * WhisperDecoder.forward(tokens, xa, kvCache) (W4J/nn/WhisperDecoder.java:59-104)

@@ -82,6 +82,7 @@ def lib():
             L.orc_encoder_set_tensor.argtypes = [P, ctypes.c_char_p, P, ctypes.c_long]
             L.orc_encoder_check.argtypes = [P]
             L.orc_encoder_forward.argtypes = [P, P, P]
+            L.orc_log_mel.argtypes = [P, I, P, I, I, I, I, P]
             _lib = L
     return _lib
 
@@ -321,3 +322,14 @@ class OracleEncoder:
             self.close()
         except Exception:
             pass
+
+
+def log_mel(audio, filters, out_frames: int, hop: int = 160) -> np.ndarray:
+    """FeatureExtractor.extract + padOrTrim: (n_mels, out_frames) log-mel of 16 kHz samples with the
+    model's filters (n_mels, n_bins)."""
+    a = _f32(audio).reshape(-1)
+    f = _f32(filters)
+    n_mels, n_bins = f.shape
+    out = np.empty((n_mels, out_frames), np.float32)
+    _check(lib().orc_log_mel(_p(a) if a.size else None, a.size, _p(f), n_mels, n_bins, hop, out_frames, _p(out)))
+    return out

@@ -1291,3 +1291,136 @@ done:
     free(y1); free(x); free(h); free(q); free(kk); free(v); free(att); free(m); free(scores);
     return rc;
 }
+
+/* ------------------------------------------------------------------------ */
+/* log-mel front end (FeatureExtractor.java:68-160 extract + padOrTrim,     */
+/* :248-320 Bluestein / radix-2 FFT, :322-328 Hann window)                  */
+/* ------------------------------------------------------------------------ */
+
+/* :282-320 radix-2 FFT, twiddles by recurrence in float (as the Java loop does) */
+static void fft_radix2(float *re, float *im, int n) {
+    for (int i = 1, j = 0; i < n; i++) {
+        int bit = n >> 1;
+        while (j & bit) {
+            j ^= bit;
+            bit >>= 1;
+        }
+        j ^= bit;
+        if (i < j) {
+            float t = re[i]; re[i] = re[j]; re[j] = t;
+            t = im[i]; im[i] = im[j]; im[j] = t;
+        }
+    }
+    for (int len = 2; len <= n; len <<= 1) {
+        const double angle = -2.0 * M_PI / len;
+        const float wre = (float)cos(angle), wim = (float)sin(angle);
+        for (int i = 0; i < n; i += len) {
+            float cre = 1.0f, cim = 0.0f;
+            for (int j = 0; j < len / 2; j++) {
+                const int a = i + j, b = i + j + len / 2;
+                const float ure = re[a], uim = im[a];
+                const float vre = re[b] * cre - im[b] * cim;
+                const float vim = re[b] * cim + im[b] * cre;
+                re[a] = ure + vre;
+                im[a] = uim + vim;
+                re[b] = ure - vre;
+                im[b] = uim - vim;
+                const float ncre = cre * wre - cim * wim;
+                cim = cre * wim + cim * wre;
+                cre = ncre;
+            }
+        }
+    }
+}
+
+/* :200-280 Bluestein for a non-power-of-two n (Whisper's n_fft = 400) */
+static void fft_bluestein(float *re, float *im, int n) {
+    int m = 1;
+    while (m < 2 * n - 1) m <<= 1;
+    float *cre = (float *)calloc((size_t)n, sizeof(float)), *cim = (float *)calloc((size_t)n, sizeof(float));
+    float *are = (float *)calloc((size_t)m, sizeof(float)), *aim = (float *)calloc((size_t)m, sizeof(float));
+    float *bre = (float *)calloc((size_t)m, sizeof(float)), *bim = (float *)calloc((size_t)m, sizeof(float));
+    for (int k = 0; k < n; k++) {
+        const double angle = -M_PI * (double)(((long long)k * k) % (2LL * n)) / n;
+        cre[k] = (float)cos(angle);
+        cim[k] = (float)sin(angle);
+    }
+    for (int k = 0; k < n; k++) {
+        are[k] = re[k] * cre[k] + im[k] * cim[k];
+        aim[k] = im[k] * cre[k] - re[k] * cim[k];
+    }
+    bre[0] = cre[0];
+    bim[0] = cim[0];
+    for (int k = 1; k < n; k++) {
+        bre[k] = bre[m - k] = cre[k];
+        bim[k] = bim[m - k] = cim[k];
+    }
+    fft_radix2(are, aim, m);
+    fft_radix2(bre, bim, m);
+    for (int k = 0; k < m; k++) {
+        const float tr = are[k] * bre[k] - aim[k] * bim[k];
+        const float ti = are[k] * bim[k] + aim[k] * bre[k];
+        are[k] = tr;
+        aim[k] = ti;
+    }
+    for (int k = 0; k < m; k++) aim[k] = -aim[k];
+    fft_radix2(are, aim, m);
+    const float inv_m = 1.0f / m;
+    for (int k = 0; k < m; k++) {
+        are[k] *= inv_m;
+        aim[k] *= -inv_m;
+    }
+    for (int k = 0; k < n; k++) {
+        re[k] = are[k] * cre[k] + aim[k] * cim[k];
+        im[k] = aim[k] * cre[k] - are[k] * cim[k];
+    }
+    free(cre); free(cim); free(are); free(aim); free(bre); free(bim);
+}
+
+int orc_log_mel(const float *audio, int n_samples, const float *filters, int n_mels, int n_bins, int hop,
+                int out_frames, float *out) {
+    const int n_fft = (n_bins - 1) * 2, pad = n_fft / 2;
+    if ((!audio && n_samples > 0) || !filters || !out || n_samples < 0 || n_mels <= 0 || n_bins < 2 || hop <= 0 ||
+        out_frames <= 0)
+        return fail("orc_log_mel", "bad argument");
+    const int len = n_samples < n_fft ? n_fft : n_samples; /* :75-79 short inputs padded to n_fft */
+    const int plen = len + 2 * pad;
+    float *padded = (float *)calloc((size_t)plen, sizeof(float));
+    if (n_samples > 0) memcpy(padded + pad, audio, (size_t)n_samples * sizeof(float));
+    float *window = (float *)malloc((size_t)n_fft * sizeof(float));
+    for (int i = 0; i < n_fft; i++) window[i] = 0.5f * (1.0f - (float)cos(2.0 * M_PI * i / n_fft));
+    const int frames = 1 + (plen - n_fft) / hop;
+    float *mag = (float *)malloc((size_t)n_bins * frames * sizeof(float));
+    float *re = (float *)malloc((size_t)n_fft * sizeof(float)), *im = (float *)malloc((size_t)n_fft * sizeof(float));
+    for (int t = 0; t < frames; t++) {
+        for (int i = 0; i < n_fft; i++) {
+            re[i] = padded[(size_t)t * hop + i] * window[i];
+            im[i] = 0.0f;
+        }
+        if ((n_fft & (n_fft - 1)) == 0) fft_radix2(re, im, n_fft);
+        else fft_bluestein(re, im, n_fft);
+        for (int f = 0; f < n_bins; f++) mag[(size_t)f * frames + t] = re[f] * re[f] + im[f] * im[f];
+    }
+    float *spec = (float *)malloc((size_t)n_mels * frames * sizeof(float));
+    float gmax = -INFINITY;
+    for (int mm = 0; mm < n_mels; mm++)
+        for (int t = 0; t < frames; t++) {
+            float sum = 0.0f;
+            for (int f = 0; f < n_bins; f++) sum += filters[(size_t)mm * n_bins + f] * mag[(size_t)f * frames + t];
+            const float v = (float)log10(fmax((double)sum, 1e-10));
+            spec[(size_t)mm * frames + t] = v;
+            if (v > gmax) gmax = v;
+        }
+    const float floor_v = gmax - 8.0f;
+    float vmin = INFINITY;
+    for (long i = 0; i < (long)n_mels * frames; i++) {
+        spec[i] = ((spec[i] > floor_v ? spec[i] : floor_v) + 4.0f) / 4.0f;
+        if (spec[i] < vmin) vmin = spec[i];
+    }
+    /* padOrTrim (:130-160): the first out_frames frames, or padded with the spectrogram's minimum */
+    for (int mm = 0; mm < n_mels; mm++)
+        for (int t = 0; t < out_frames; t++)
+            out[(size_t)mm * out_frames + t] = t < frames ? spec[(size_t)mm * frames + t] : vmin;
+    free(padded); free(window); free(mag); free(re); free(im); free(spec);
+    return 0;
+}

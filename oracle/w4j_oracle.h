@@ -94,6 +94,12 @@ int orc_encoder_check(const orc_encoder *e);
  * out: (n_audio_ctx, n_audio_state), the encoder output xa.  Returns 0 or -1. */
 int orc_encoder_forward(const orc_encoder *e, const float *mel, float *out);
 
+/* FeatureExtractor.extract + padOrTrim (FeatureExtractor.java:68-160): log-mel spectrogram of 16 kHz
+ * mono samples with the model's filters (n_mels x n_bins, n_fft = 2 (n_bins - 1)), hop samples per
+ * frame, out: n_mels x out_frames (first frames, or padded with the spectrogram's minimum). */
+int orc_log_mel(const float *audio, int n_samples, const float *filters, int n_mels, int n_bins, int hop,
+                int out_frames, float *out);
+
 #ifdef __cplusplus
 }
 #endif

@@ -62,6 +62,9 @@ SIGNATURES = {
     "w4j_set_encoder_output": (_I, [_P, _I, _P, _I]),
     "w4j_set_encoder_output_device": (_I, [_P, _I, _P, _I]),
     "w4j_encoder_forward": (_I, [_P, _P, _I, _P, _I]),
+    "w4j_upload_mel_filters": (_I, [_P, _P, _I, _I]),
+    "w4j_log_mel": (_I, [_P, _P, _I, _P]),
+    "w4j_encode_audio": (_I, [_P, _P, _I, _P, _I]),
     "w4j_forward": (_I, [_P, _I, _P, _I, _I, _P]),
     "w4j_reset_cache": (_I, [_P, _I]),
     "w4j_decode": (_I, [_P, _P, _I, _P, _I, _I, _I, _P, _I, _I, _F, _I, _U64, ctypes.POINTER(Result)]),

@@ -97,6 +97,10 @@ struct EncDev {
     float *mel = nullptr, *col = nullptr, *y1 = nullptr, *x = nullptr, *qkv = nullptr, *att = nullptr, *hid = nullptr,
           *xa = nullptr;
     __half *qkvh = nullptr, *hilo = nullptr;
+    // log-mel front end: the model's filters, the transform tables, the audio and its spectrogram
+    float *filt = nullptr, *tabs = nullptr, *audio = nullptr, *spec = nullptr, *fmx = nullptr, *fmn = nullptr;
+    int filt_bins = 0;
+    size_t audio_cap = 0, frames_cap = 0;
 };
 
 struct GraphKey {
@@ -887,9 +891,9 @@ static int enc_prepare(w4j_ctx *c) {
         if (!ok) return set_err(W4J_ERR_CUDA, "encoder: weight tensor maps");
         e.maps_ok = true;
     }
-    if (!e.mel) {
+    if (!e.mel) TRY(dalloc(c, &e.mel, (size_t)dm.n_mels * 2 * T));
+    if (!e.col) {
         const size_t T1 = 2 * (size_t)T;
-        TRY(dalloc(c, &e.mel, (size_t)dm.n_mels * T1));
         TRY(dalloc(c, &e.col, std::max(T1 * e.k1, (size_t)T * 3 * d)));
         TRY(dalloc(c, &e.y1, T1 * d));
         TRY(dalloc(c, &e.x, (size_t)T * d));
@@ -928,21 +932,76 @@ static int enc_run(w4j_ctx *c) {
     return 0;
 }
 
-extern "C" int w4j_encoder_forward(w4j_ctx *c, const float *mel, int n_frames, float *xa_out, int slot) {
-    if (!c || !mel) return set_err(W4J_ERR_ARG, "w4j_encoder_forward: null argument");
+// log-mel of host audio into c->enc.mel (n_mels x 2 n_audio_ctx), FeatureExtractor.extract + padOrTrim
+static int logmel_run(w4j_ctx *c, const float *audio, int n_samples) {
+    EncDev &e = c->enc;
+    const w4j_dims &dm = c->dims;
+    if (!e.filt) return set_err(W4J_ERR_STATE, "mel filters not uploaded (w4j_upload_mel_filters)");
+    if (n_samples < 0) return set_err(W4J_ERR_ARG, "n_samples %d", n_samples);
+    const int n_fft = 2 * (e.filt_bins - 1), hop = 160;
+    const int frames = logmel_frames(n_samples, n_fft, hop);
+    if (!e.mel) TRY(dalloc(c, &e.mel, (size_t)dm.n_mels * 2 * dm.n_audio_ctx));
+    if ((size_t)std::max(n_samples, 1) > e.audio_cap) {
+        CUDA_TRY(cudaStreamSynchronize(c->stream));
+        dfree(c, e.audio);
+        e.audio = nullptr;
+        TRY(dalloc(c, &e.audio, (size_t)std::max(n_samples, 1)));
+        e.audio_cap = (size_t)std::max(n_samples, 1);
+    }
+    if ((size_t)frames > e.frames_cap) {
+        CUDA_TRY(cudaStreamSynchronize(c->stream));
+        dfree(c, e.spec);
+        dfree(c, e.fmx);
+        dfree(c, e.fmn);
+        e.spec = e.fmx = e.fmn = nullptr;
+        TRY(dalloc(c, &e.spec, (size_t)dm.n_mels * frames));
+        TRY(dalloc(c, &e.fmx, (size_t)frames));
+        TRY(dalloc(c, &e.fmn, (size_t)frames));
+        e.frames_cap = (size_t)frames;
+    }
+    if (n_samples > 0)
+        CUDA_TRY(cudaMemcpyAsync(e.audio, audio, (size_t)n_samples * 4, cudaMemcpyHostToDevice, c->stream));
+    CUDA_TRY(launch_logmel(e.audio, n_samples, n_fft, hop, e.tabs, e.filt, dm.n_mels, e.filt_bins, 2 * dm.n_audio_ctx,
+                           e.spec, e.fmx, e.fmn, e.mel, c->stream));
+    return 0;
+}
+
+extern "C" int w4j_upload_mel_filters(w4j_ctx *c, const float *filters, int n_mels, int n_bins) {
+    if (!c || !filters) return set_err(W4J_ERR_ARG, "w4j_upload_mel_filters: null argument");
     std::lock_guard<std::mutex> g(c->mu);
     CUDA_TRY(cudaSetDevice(c->device));
-    const w4j_dims &dm = c->dims;
-    if (n_frames != 2 * dm.n_audio_ctx)
-        return set_err(W4J_ERR_ARG, "mel has %d frames, the encoder takes %d", n_frames, 2 * dm.n_audio_ctx);
-    if (slot >= 0) {
-        TRY(check_ready(c));
-        if (slot >= c->max_streams) return set_err(W4J_ERR_ARG, "slot %d out of range", slot);
-        if (dm.n_audio_state != c->d) return set_err(W4J_ERR_ARG, "n_audio_state differs from n_text_state");
+    if (n_mels != c->dims.n_mels) return set_err(W4J_ERR_ARG, "%d mel filters, the model has %d", n_mels, c->dims.n_mels);
+    if (n_bins < 2 || 2 * (n_bins - 1) > 512) return set_err(W4J_ERR_ARG, "n_bins %d (n_fft = 2 (n_bins - 1) <= 512)", n_bins);
+    EncDev &e = c->enc;
+    if (e.filt && e.filt_bins != n_bins) return set_err(W4J_ERR_STATE, "mel filters already uploaded with %d bins", e.filt_bins);
+    std::vector<float> tabs;
+    logmel_tables(2 * (n_bins - 1), tabs);
+    if (!e.filt) {
+        TRY(dalloc(c, &e.filt, (size_t)n_mels * n_bins));
+        TRY(dalloc(c, &e.tabs, tabs.size()));
     }
-    TRY(enc_prepare(c));
-    const size_t mel_bytes = (size_t)dm.n_mels * n_frames * 4;
-    CUDA_TRY(cudaMemcpyAsync(c->enc.mel, mel, mel_bytes, cudaMemcpyHostToDevice, c->stream));
+    e.filt_bins = n_bins;
+    CUDA_TRY(cudaMemcpy(e.filt, filters, (size_t)n_mels * n_bins * 4, cudaMemcpyHostToDevice));
+    CUDA_TRY(cudaMemcpy(e.tabs, tabs.data(), tabs.size() * 4, cudaMemcpyHostToDevice));
+    return W4J_OK;
+}
+
+extern "C" int w4j_log_mel(w4j_ctx *c, const float *audio, int n_samples, float *mel_out) {
+    if (!c || (!audio && n_samples > 0)) return set_err(W4J_ERR_ARG, "w4j_log_mel: null argument");
+    std::lock_guard<std::mutex> g(c->mu);
+    CUDA_TRY(cudaSetDevice(c->device));
+    TRY(logmel_run(c, audio, n_samples));
+    const w4j_dims &dm = c->dims;
+    if (mel_out)
+        CUDA_TRY(cudaMemcpyAsync(mel_out, c->enc.mel, (size_t)dm.n_mels * 2 * dm.n_audio_ctx * 4, cudaMemcpyDeviceToHost,
+                                 c->stream));
+    CUDA_TRY(cudaStreamSynchronize(c->stream));
+    return W4J_OK;
+}
+
+// encoder over c->enc.mel, then the output to the host and / or a decode slot
+static int enc_finish(w4j_ctx *c, float *xa_out, int slot) {
+    const w4j_dims &dm = c->dims;
     TRY(enc_run(c));
     if (xa_out)
         CUDA_TRY(cudaMemcpyAsync(xa_out, c->enc.xa, (size_t)dm.n_audio_ctx * dm.n_audio_state * 4, cudaMemcpyDeviceToHost,
@@ -950,6 +1009,38 @@ extern "C" int w4j_encoder_forward(w4j_ctx *c, const float *mel, int n_frames, f
     CUDA_TRY(cudaStreamSynchronize(c->stream));
     if (slot >= 0) TRY(prefill(c, slot, c->enc.xa));
     return W4J_OK;
+}
+
+static int enc_check_slot(w4j_ctx *c, int slot) {
+    if (slot < 0) return 0;
+    TRY(check_ready(c));
+    if (slot >= c->max_streams) return set_err(W4J_ERR_ARG, "slot %d out of range", slot);
+    if (c->dims.n_audio_state != c->d) return set_err(W4J_ERR_ARG, "n_audio_state differs from n_text_state");
+    return 0;
+}
+
+extern "C" int w4j_encode_audio(w4j_ctx *c, const float *audio, int n_samples, float *xa_out, int slot) {
+    if (!c || (!audio && n_samples > 0)) return set_err(W4J_ERR_ARG, "w4j_encode_audio: null argument");
+    std::lock_guard<std::mutex> g(c->mu);
+    CUDA_TRY(cudaSetDevice(c->device));
+    TRY(enc_check_slot(c, slot));
+    TRY(enc_prepare(c));
+    TRY(logmel_run(c, audio, n_samples));
+    return enc_finish(c, xa_out, slot);
+}
+
+extern "C" int w4j_encoder_forward(w4j_ctx *c, const float *mel, int n_frames, float *xa_out, int slot) {
+    if (!c || !mel) return set_err(W4J_ERR_ARG, "w4j_encoder_forward: null argument");
+    std::lock_guard<std::mutex> g(c->mu);
+    CUDA_TRY(cudaSetDevice(c->device));
+    const w4j_dims &dm = c->dims;
+    if (n_frames != 2 * dm.n_audio_ctx)
+        return set_err(W4J_ERR_ARG, "mel has %d frames, the encoder takes %d", n_frames, 2 * dm.n_audio_ctx);
+    TRY(enc_check_slot(c, slot));
+    TRY(enc_prepare(c));
+    const size_t mel_bytes = (size_t)dm.n_mels * n_frames * 4;
+    CUDA_TRY(cudaMemcpyAsync(c->enc.mel, mel, mel_bytes, cudaMemcpyHostToDevice, c->stream));
+    return enc_finish(c, xa_out, slot);
 }
 
 // ---------------------------------------------------------------------------

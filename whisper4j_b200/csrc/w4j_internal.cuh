@@ -8,6 +8,7 @@
 //   self  K / V   f16 [seq slot][layer][head][n_text_ctx][64]
 //   activations   f32 [M][d] residual stream x, q, attention output, [M][4d] MLP hidden
 #pragma once
+#include <vector>
 #include <cuda_fp16.h>
 #include <cuda_runtime.h>
 #include <stdint.h>
@@ -355,7 +356,13 @@ cudaError_t launch_enc_im2col(const float *src, int in_ch, int in_len, bool time
 cudaError_t launch_enc_add(float *x, const float *p, long long n, cudaStream_t s);
 cudaError_t launch_enc_ln(const float *x, int rows, int n, const float *g, const float *b, float *y, cudaStream_t s);
 cudaError_t launch_enc_qkv_f16(const float *qkv, int T, int H, __half *out, cudaStream_t s);
-cudaError_t launch_enc_attn(const __half *qkvh, int T, int H, float *out, cudaStream_t s);// tensor map of a row-major f16 matrix read in [box_rows x 64 cols] boxes, 128-byte swizzle
+cudaError_t launch_enc_attn(const __half *qkvh, int T, int H, float *out, cudaStream_t s);
+// log-mel front end (k_logmel.cu)
+void logmel_tables(int n_fft, std::vector<float> &tabs);
+int logmel_frames(int n_samples, int n_fft, int hop);
+cudaError_t launch_logmel(const float *audio, int n_samples, int n, int hop, const float *tabs, const float *filt,
+                          int n_mels, int n_bins, int out_frames, float *spec, float *fmx, float *fmn, float *out,
+                          cudaStream_t s);// tensor map of a row-major f16 matrix read in [box_rows x 64 cols] boxes, 128-byte swizzle
 bool make_tmap_f16_box(void *map_out, const void *base, int rows, int cols, int box_rows);
 cudaError_t select_prepare();
 cudaError_t attn_prepare();

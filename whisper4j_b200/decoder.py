@@ -85,6 +85,10 @@ class WhisperDecoder:
                 buf = np.frombuffer(t.data, dtype=np.uint8)
                 check(lib().w4j_upload_tensor(self._ctx, name.encode(), t.ttype, ne, len(t.ne), _ptr(buf), buf.size))
             check(lib().w4j_finalize(self._ctx))
+            mf = getattr(model, "mel_filters", None)
+            if mf is not None and mf.ndim == 2 and mf.shape[0] == dm.n_mels and 2 <= mf.shape[1] <= 257 and mf.any():
+                f = np.ascontiguousarray(mf, dtype=np.float32)
+                check(lib().w4j_upload_mel_filters(self._ctx, _ptr(f), f.shape[0], f.shape[1]))
         except Exception:
             self.close()
             raise
@@ -135,6 +139,26 @@ class WhisperDecoder:
                                         -1 if slot is None else slot))
         if slot is not None:
             self._xa_ids[slot] = ("encoder", id(mel))
+        return out
+
+    def log_mel(self, audio) -> np.ndarray:
+        """FeatureExtractor.extract + padOrTrim on the device: 16 kHz mono samples -> the
+        (n_mels, 2 n_audio_ctx) log-mel spectrogram, with the model file's mel filters."""
+        a = np.ascontiguousarray(np.asarray(audio, dtype=np.float32).reshape(-1))
+        out = np.empty((self.dims.n_mels, 2 * self.dims.n_audio_ctx), np.float32)
+        check(lib().w4j_log_mel(self._ctx, _ptr(a) if a.size else None, a.size, _ptr(out)))
+        return out
+
+    def encode_audio(self, audio, slot: int | None = None, return_output: bool = True):
+        """One chunk's front end on the device: log-mel, encoder, and with ``slot`` that stream's
+        cross K/V (WhisperModel.transcribe's feature + encoder stage)."""
+        a = np.ascontiguousarray(np.asarray(audio, dtype=np.float32).reshape(-1))
+        dm = self.dims
+        out = np.empty((dm.n_audio_ctx, dm.n_audio_state), np.float32) if return_output else None
+        check(lib().w4j_encode_audio(self._ctx, _ptr(a) if a.size else None, a.size,
+                                     _ptr(out) if out is not None else None, -1 if slot is None else slot))
+        if slot is not None:
+            self._xa_ids[slot] = ("audio", id(audio))
         return out
 
     def _slot_for(self, xa, slot):
