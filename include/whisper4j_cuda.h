@@ -111,6 +111,47 @@ int w4j_log_mel(w4j_ctx *ctx, const float *audio, int n_samples, float *mel_out)
 int w4j_encode_audio(w4j_ctx *ctx, const float *audio, int n_samples, float *xa_out, int slot);
 
 /*
+ * The chunked transcription loop (replaces WhisperModel.transcribeChunked, W4J/WhisperModel.java:334-427,
+ * with parseTimestampSegments / findLastTimestampPos / buildPromptWithContext, :430-530): the whole
+ * recording (16 kHz mono f32, host) is copied to the device once; per 30 s window at the seek
+ * position the library runs the log-mel, the encoder, the cross K/V projection into stream 0 and
+ * decodeWithFallback, retries without the previous-text context when it made the average
+ * log-probability drop below -1, skips no-speech windows, cuts the tokens into timestamped
+ * segments and advances the seek from the last timestamp.  Token ids only: the host's tokenizer
+ * turns them into text.  A segment is kept when it has at least one text token (the reference keeps
+ * it when the decoded text is not blank; the host drops segments whose text is blank).
+ */
+typedef struct w4j_transcribe_opts {
+    const int32_t *sot;          /* tokenizer.sotSequence() (the prompt before the no-timestamps token) */
+    int32_t n_sot;
+    int32_t eot, no_speech;      /* token ids (tokenizer.eot(), tokenizer.noSpeech()) */
+    int32_t no_timestamps;       /* appended to the prompt when ts_begin < 0 (buildPrompt, :573-582) */
+    int32_t sot_prev;            /* the previous-text marker of buildPromptWithContext (:522-524) */
+    int32_t ts_begin;            /* tokenizer.timestampBegin() with timestamps, -1 without */
+    const int32_t *suppress;     /* buildSuppressTokens() */
+    int32_t n_suppress;
+    int32_t beam_size;           /* 1: greedy */
+    int32_t condition_on_previous;
+    uint64_t seed;               /* temperature-fallback sampling */
+} w4j_transcribe_opts;
+
+typedef struct w4j_segment {
+    float start, end;            /* seconds */
+    int32_t token_begin, n_tokens;  /* the segment's tokens: w4j_transcript.tokens[token_begin ..] */
+} w4j_segment;
+
+typedef struct w4j_transcript {
+    int32_t *tokens;             /* caller's buffer: every segment's tokens, in order */
+    int32_t tokens_cap;
+    w4j_segment *segments;       /* caller's buffer */
+    int32_t segments_cap;
+    int32_t n_tokens, n_segments, n_windows;  /* out: used entries, 30 s windows decoded */
+} w4j_transcript;
+
+int w4j_transcribe(w4j_ctx *ctx, const float *audio, int n_samples, const w4j_transcribe_opts *opts,
+                   w4j_transcript *out);
+
+/*
  * WhisperDecoder.forward(tokens, xa, kvCache) (W4J/nn/WhisperDecoder.java:59-104)
  * for stream `slot`.  use_cache=1 appends the tokens to the slot's self-attention
  * cache (the kvCache map); use_cache=0 runs with an empty private cache and leaves

@@ -333,3 +333,98 @@ def log_mel(audio, filters, out_frames: int, hop: int = 160) -> np.ndarray:
     out = np.empty((n_mels, out_frames), np.float32)
     _check(lib().orc_log_mel(_p(a) if a.size else None, a.size, _p(f), n_mels, n_bins, hop, out_frames, _p(out)))
     return out
+
+
+# ---------------------------------------------------------------------------
+# the chunked transcription loop (WhisperModel.transcribeChunked, WhisperModel.java:334-427)
+# ---------------------------------------------------------------------------
+def f32(x) -> float:
+    return float(np.float32(x))
+
+
+def timestamp_segments(tokens, ts_begin, offset, precision):
+    """parseTimestampSegments (WhisperModel.java:430-490): [(start, end, text_tokens)], segments with
+    at least one text token."""
+    offset, precision = np.float32(offset), np.float32(precision)
+    ts = [i for i, t in enumerate(tokens) if t >= ts_begin]
+    out = []
+    if len(ts) < 2:
+        text = [t for t in tokens if t < ts_begin]
+        if text:
+            end = offset + np.float32(30.0) if not ts else offset + np.float32(tokens[ts[0]] - ts_begin) * precision
+            out.append((f32(offset), f32(end), text))
+        return out
+    last = 0
+    for i in range(len(ts) - 1):
+        if ts[i + 1] != ts[i] + 1:
+            continue
+        sl = tokens[last:ts[i + 1]]
+        start, end = offset, offset + np.float32(30.0)
+        for t in sl:
+            if t >= ts_begin:
+                start = offset + np.float32(t - ts_begin) * precision
+                break
+        for t in reversed(sl):
+            if t >= ts_begin:
+                end = offset + np.float32(t - ts_begin) * precision
+                break
+        text = [t for t in sl if t < ts_begin]
+        if text:
+            out.append((f32(start), f32(end), text))
+        last = ts[i + 1]
+    return out
+
+
+def prompt_with_context(base, prev, sot_prev, n_text_ctx, condition):
+    """buildPromptWithContext (WhisperModel.java:507-530)."""
+    if not condition or not prev:
+        return list(base)
+    max_prev = (n_text_ctx // 2 - 1) - len(base) - 1
+    if max_prev <= 0:
+        return list(base)
+    n = min(len(prev), max_prev)
+    return [sot_prev] + list(prev[len(prev) - n:]) + list(base)
+
+
+def transcribe_chunked(n_samples, n_audio_ctx, n_text_ctx, sot, no_timestamps, sot_prev, ts_begin,
+                       condition_on_previous, window, decode):
+    """The loop of WhisperModel.transcribeChunked over injected stages: window(a0, n_valid) prepares
+    the 30 s window at sample a0 (front end + encoder), decode(prompt, max_tokens) -> (tokens,
+    avg_logprob, no_speech_prob) runs decodeWithFallback on it.  Returns [(start, end, tokens)]."""
+    n_frames = 2 * n_audio_ctx
+    stride, hop = n_frames // n_audio_ctx, 160
+    chunk = n_frames * hop
+    precision = np.float32(stride) * np.float32(160.0) / np.float32(16000.0)
+    total = int(np.float32(n_samples) / np.float32(160.0))
+    duration = np.float32(n_samples) / np.float32(16000.0)
+    with_ts = ts_begin > 0
+    base = list(sot) + ([] if with_ts else [no_timestamps])
+    prev, segs, seek = [], [], 0
+    while seek < total:
+        offset = np.float32(seek) * np.float32(160.0) / np.float32(16000.0)
+        seg_size = min(n_frames, total - seek)
+        a0 = seek * hop
+        window(a0, max(min(n_samples - a0, chunk), 0))
+        max_tokens = n_text_ctx // 2
+        if seg_size < n_frames:
+            max_tokens = max(8, max_tokens * seg_size // n_frames)
+        tokens, avg, nsp = decode(prompt_with_context(base, prev, sot_prev, n_text_ctx, condition_on_previous),
+                                  max_tokens)
+        if condition_on_previous and prev and avg < -1.0:
+            tokens, avg, nsp = decode(base, max_tokens)
+            prev = []
+        if nsp > 0.6 and avg < -1.0:
+            seek += seg_size
+            continue
+        if with_ts:
+            segs += timestamp_segments(tokens, ts_begin, offset, precision)
+            last = next((t - ts_begin for t in reversed(tokens) if t >= ts_begin), -1)
+            seek += max(last * stride, stride) if last > 0 else seg_size
+        else:
+            if tokens:
+                segs.append((f32(offset), f32(min(offset + np.float32(seg_size) * np.float32(160.0) / np.float32(16000.0),
+                                                   duration)), list(tokens)))
+            seek += seg_size
+        if condition_on_previous:
+            prev = list(tokens)
+    return segs

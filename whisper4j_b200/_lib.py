@@ -44,6 +44,24 @@ class Dims(ctypes.Structure):
         "n_vocab", "n_text_ctx", "n_text_state", "n_text_head", "n_text_layer")]
 
 
+class TranscribeOpts(ctypes.Structure):
+    _fields_ = [("sot", ctypes.POINTER(ctypes.c_int32)), ("n_sot", ctypes.c_int32), ("eot", ctypes.c_int32),
+                ("no_speech", ctypes.c_int32), ("no_timestamps", ctypes.c_int32), ("sot_prev", ctypes.c_int32),
+                ("ts_begin", ctypes.c_int32), ("suppress", ctypes.POINTER(ctypes.c_int32)), ("n_suppress", ctypes.c_int32),
+                ("beam_size", ctypes.c_int32), ("condition_on_previous", ctypes.c_int32), ("seed", ctypes.c_uint64)]
+
+
+class Segment(ctypes.Structure):
+    _fields_ = [("start", ctypes.c_float), ("end", ctypes.c_float), ("token_begin", ctypes.c_int32),
+                ("n_tokens", ctypes.c_int32)]
+
+
+class Transcript(ctypes.Structure):
+    _fields_ = [("tokens", ctypes.POINTER(ctypes.c_int32)), ("tokens_cap", ctypes.c_int32),
+                ("segments", ctypes.POINTER(Segment)), ("segments_cap", ctypes.c_int32),
+                ("n_tokens", ctypes.c_int32), ("n_segments", ctypes.c_int32), ("n_windows", ctypes.c_int32)]
+
+
 class Result(ctypes.Structure):
     _fields_ = [("tokens", ctypes.POINTER(ctypes.c_int32)), ("lens", ctypes.POINTER(ctypes.c_int32)),
                 ("sum_logprob", ctypes.POINTER(ctypes.c_double)), ("avg_logprob", ctypes.POINTER(ctypes.c_float)),
@@ -65,6 +83,7 @@ SIGNATURES = {
     "w4j_upload_mel_filters": (_I, [_P, _P, _I, _I]),
     "w4j_log_mel": (_I, [_P, _P, _I, _P]),
     "w4j_encode_audio": (_I, [_P, _P, _I, _P, _I]),
+    "w4j_transcribe": (_I, [_P, _P, _I, _P, _P]),
     "w4j_forward": (_I, [_P, _I, _P, _I, _I, _P]),
     "w4j_reset_cache": (_I, [_P, _I]),
     "w4j_decode": (_I, [_P, _P, _I, _P, _I, _I, _I, _P, _I, _I, _F, _I, _U64, ctypes.POINTER(Result)]),

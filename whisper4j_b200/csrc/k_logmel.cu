@@ -226,24 +226,25 @@ __global__ void __launch_bounds__(256) k_logmel_norm(const float *spec, int n_me
     }
 }
 
-cudaError_t launch_logmel(const float *audio, int n_samples, int n, int hop, const float *tabs, const float *filt,
-                          int n_mels, int n_bins, int out_frames, float *spec, float *fmx, float *fmn, float *out,
-                          cudaStream_t s) {
-    if (n < 2 || 2 * n - 1 > kMelFftN || n_bins != n / 2 + 1 || n_mels > 512) return cudaErrorInvalidValue;
+int logmel_frames(int n_samples, int n, int hop) {
     const int len = n_samples < n ? n : n_samples;
-    const int frames = 1 + (len + 2 * (n / 2) - n) / hop;
-    k_logmel_frames<<<frames, 512, 0, s>>>(audio, n_samples, n, hop, frames, tabs, filt, n_mels, n_bins, spec, fmx, fmn);
+    return 1 + (len + 2 * (n / 2) - n) / hop;
+}
+
+// n_total samples (the spectrogram's length), of which the first n_valid are read from audio and the
+// rest are zero (a chunk shorter than 30 s, as WhisperModel zero-fills its chunk array, :355-358)
+cudaError_t launch_logmel(const float *audio, int n_valid, int n_total, int n, int hop, const float *tabs,
+                          const float *filt, int n_mels, int n_bins, int out_frames, float *spec, float *fmx, float *fmn,
+                          float *out, cudaStream_t s) {
+    if (n < 2 || 2 * n - 1 > kMelFftN || n_bins != n / 2 + 1 || n_mels > 512 || n_valid > n_total) return cudaErrorInvalidValue;
+    const int frames = logmel_frames(n_total, n, hop);
+    k_logmel_frames<<<frames, 512, 0, s>>>(audio, n_valid, n, hop, frames, tabs, filt, n_mels, n_bins, spec, fmx, fmn);
     cudaError_t e = cudaGetLastError();
     if (e != cudaSuccess) return e;
     const long long total = (long long)n_mels * out_frames;
     const int blocks = (int)std::min<long long>((total + 255) / 256, 148LL * 8);
     k_logmel_norm<<<blocks, 256, 0, s>>>(spec, n_mels, frames, fmx, fmn, out_frames, out);
     return cudaGetLastError();
-}
-
-int logmel_frames(int n_samples, int n, int hop) {
-    const int len = n_samples < n ? n : n_samples;
-    return 1 + (len + 2 * (n / 2) - n) / hop;
 }
 
 }  // namespace w4j

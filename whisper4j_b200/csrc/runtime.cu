@@ -932,38 +932,54 @@ static int enc_run(w4j_ctx *c) {
     return 0;
 }
 
-// log-mel of host audio into c->enc.mel (n_mels x 2 n_audio_ctx), FeatureExtractor.extract + padOrTrim
-static int logmel_run(w4j_ctx *c, const float *audio, int n_samples) {
+// room for n samples of device audio (c->enc.audio)
+static int audio_reserve(w4j_ctx *c, int n) {
+    EncDev &e = c->enc;
+    if ((size_t)std::max(n, 1) <= e.audio_cap) return 0;
+    CUDA_TRY(cudaStreamSynchronize(c->stream));
+    dfree(c, e.audio);
+    e.audio = nullptr;
+    e.audio_cap = 0;
+    TRY(dalloc(c, &e.audio, (size_t)std::max(n, 1)));
+    e.audio_cap = (size_t)std::max(n, 1);
+    return 0;
+}
+
+// log-mel of n_total samples (the first n_valid from device audio, the rest zero) into c->enc.mel
+// (n_mels x 2 n_audio_ctx): FeatureExtractor.extract + padOrTrim
+static int logmel_device(w4j_ctx *c, const float *dev_audio, int n_valid, int n_total) {
     EncDev &e = c->enc;
     const w4j_dims &dm = c->dims;
     if (!e.filt) return set_err(W4J_ERR_STATE, "mel filters not uploaded (w4j_upload_mel_filters)");
-    if (n_samples < 0) return set_err(W4J_ERR_ARG, "n_samples %d", n_samples);
     const int n_fft = 2 * (e.filt_bins - 1), hop = 160;
-    const int frames = logmel_frames(n_samples, n_fft, hop);
+    const int frames = logmel_frames(n_total, n_fft, hop);
     if (!e.mel) TRY(dalloc(c, &e.mel, (size_t)dm.n_mels * 2 * dm.n_audio_ctx));
-    if ((size_t)std::max(n_samples, 1) > e.audio_cap) {
-        CUDA_TRY(cudaStreamSynchronize(c->stream));
-        dfree(c, e.audio);
-        e.audio = nullptr;
-        TRY(dalloc(c, &e.audio, (size_t)std::max(n_samples, 1)));
-        e.audio_cap = (size_t)std::max(n_samples, 1);
-    }
     if ((size_t)frames > e.frames_cap) {
         CUDA_TRY(cudaStreamSynchronize(c->stream));
         dfree(c, e.spec);
         dfree(c, e.fmx);
         dfree(c, e.fmn);
         e.spec = e.fmx = e.fmn = nullptr;
+        e.frames_cap = 0;
         TRY(dalloc(c, &e.spec, (size_t)dm.n_mels * frames));
         TRY(dalloc(c, &e.fmx, (size_t)frames));
         TRY(dalloc(c, &e.fmn, (size_t)frames));
         e.frames_cap = (size_t)frames;
     }
+    CUDA_TRY(launch_logmel(dev_audio, n_valid, n_total, n_fft, hop, e.tabs, e.filt, dm.n_mels, e.filt_bins,
+                           2 * dm.n_audio_ctx, e.spec, e.fmx, e.fmn, e.mel, c->stream));
+    return 0;
+}
+
+// log-mel of host audio into c->enc.mel
+static int logmel_run(w4j_ctx *c, const float *audio, int n_samples) {
+    EncDev &e = c->enc;
+    if (!e.filt) return set_err(W4J_ERR_STATE, "mel filters not uploaded (w4j_upload_mel_filters)");
+    if (n_samples < 0) return set_err(W4J_ERR_ARG, "n_samples %d", n_samples);
+    TRY(audio_reserve(c, n_samples));
     if (n_samples > 0)
         CUDA_TRY(cudaMemcpyAsync(e.audio, audio, (size_t)n_samples * 4, cudaMemcpyHostToDevice, c->stream));
-    CUDA_TRY(launch_logmel(e.audio, n_samples, n_fft, hop, e.tabs, e.filt, dm.n_mels, e.filt_bins, 2 * dm.n_audio_ctx,
-                           e.spec, e.fmx, e.fmn, e.mel, c->stream));
-    return 0;
+    return logmel_device(c, e.audio, n_samples, n_samples);
 }
 
 extern "C" int w4j_upload_mel_filters(w4j_ctx *c, const float *filters, int n_mels, int n_bins) {
@@ -2305,4 +2321,161 @@ extern "C" int w4j_op_logits_argmax_noalloc(int device, const float *x, int M, i
     CUDA_TRY(e);
     CUDA_TRY(launch_argmax_merge_status(nd.part, P, M, out_token, out_logprob, nd.err, s));
     return W4J_OK;
+}
+
+// ---------------------------------------------------------------------------
+// chunked transcription (WhisperModel.transcribeChunked, WhisperModel.java:334-427)
+// ---------------------------------------------------------------------------
+namespace {
+struct TsOut {
+    w4j_transcript *t;
+    int add(float start, float end, const std::vector<int32_t> &toks) {
+        if (t->n_segments >= t->segments_cap || t->n_tokens + (int)toks.size() > t->tokens_cap)
+            return set_err(W4J_ERR_ARG, "transcript buffers too small (%d segments, %d tokens)", t->segments_cap,
+                           t->tokens_cap);
+        w4j_segment &s = t->segments[t->n_segments++];
+        s.start = start;
+        s.end = end;
+        s.token_begin = t->n_tokens;
+        s.n_tokens = (int32_t)toks.size();
+        for (int32_t v : toks) t->tokens[t->n_tokens++] = v;
+        return 0;
+    }
+};
+
+std::vector<int32_t> text_tokens(const int32_t *tok, int n, int ts_begin) {  // filterTextTokens (:503-505)
+    std::vector<int32_t> r;
+    for (int i = 0; i < n; ++i)
+        if (tok[i] < ts_begin) r.push_back(tok[i]);
+    return r;
+}
+
+// parseTimestampSegments (:430-490)
+int timestamp_segments(const int32_t *tok, int n, int ts_begin, float offset, float precision, TsOut &out) {
+    std::vector<int> ts;
+    for (int i = 0; i < n; ++i)
+        if (tok[i] >= ts_begin) ts.push_back(i);
+    if (ts.size() < 2) {
+        const std::vector<int32_t> text = text_tokens(tok, n, ts_begin);
+        if (!text.empty()) {
+            const float end = ts.empty() ? offset + 30.0f : offset + (float)(tok[ts[0]] - ts_begin) * precision;
+            TRY(out.add(offset, end, text));
+        }
+        return 0;
+    }
+    int last = 0;
+    for (size_t i = 0; i + 1 < ts.size(); ++i) {
+        if (ts[i + 1] != ts[i] + 1) continue;
+        const int slice_end = ts[i + 1];
+        float start = offset, end = offset + 30.0f;
+        for (int j = last; j < slice_end; ++j)
+            if (tok[j] >= ts_begin) {
+                start = offset + (float)(tok[j] - ts_begin) * precision;
+                break;
+            }
+        for (int j = slice_end - 1; j >= last; --j)
+            if (tok[j] >= ts_begin) {
+                end = offset + (float)(tok[j] - ts_begin) * precision;
+                break;
+            }
+        const std::vector<int32_t> text = text_tokens(tok + last, slice_end - last, ts_begin);
+        if (!text.empty()) TRY(out.add(start, end, text));
+        last = slice_end;
+    }
+    return 0;
+}
+}  // namespace
+
+extern "C" int w4j_transcribe(w4j_ctx *c, const float *audio, int n_samples, const w4j_transcribe_opts *o,
+                              w4j_transcript *out) {
+    if (!c || !o || !out || (!audio && n_samples > 0) || !o->sot || o->n_sot < 1 || !out->tokens || !out->segments)
+        return set_err(W4J_ERR_ARG, "w4j_transcribe: null argument");
+    if (n_samples < 0) return set_err(W4J_ERR_ARG, "n_samples %d", n_samples);
+    out->n_tokens = out->n_segments = out->n_windows = 0;
+    const w4j_dims &dm = c->dims;
+    const int n_frames = 2 * dm.n_audio_ctx, stride = n_frames / dm.n_audio_ctx, hop = 160;
+    const int chunk = n_frames * hop;
+    const float precision = (float)stride * 160.0f / 16000.0f;
+    const int total_frames = (int)((float)n_samples / 160.0f);
+    const float duration = (float)n_samples / 16000.0f;
+    const bool with_ts = o->ts_begin > 0;
+    {  // the recording on the device once
+        std::lock_guard<std::mutex> g(c->mu);
+        CUDA_TRY(cudaSetDevice(c->device));
+        TRY(check_ready(c));
+        if (dm.n_audio_state != c->d) return set_err(W4J_ERR_ARG, "n_audio_state differs from n_text_state");
+        TRY(enc_prepare(c));
+        TRY(audio_reserve(c, n_samples));
+        if (n_samples > 0)
+            CUDA_TRY(cudaMemcpyAsync(c->enc.audio, audio, (size_t)n_samples * 4, cudaMemcpyHostToDevice, c->stream));
+    }
+    std::vector<int32_t> base(o->sot, o->sot + o->n_sot);  // buildPrompt (:573-582)
+    if (!with_ts) base.push_back(o->no_timestamps);
+    std::vector<int32_t> prev;
+    const int max_tok_full = dm.n_text_ctx / 2;
+    std::vector<int32_t> tok((size_t)max_tok_full);
+    TsOut so{out};
+    int seek = 0;
+    c->cancel.store(0);
+    while (seek < total_frames) {
+        if (c->cancel.load()) break;
+        const float offset = (float)seek * 160.0f / 16000.0f;
+        const int seg_size = std::min(n_frames, total_frames - seek);
+        const int a0 = seek * hop, n_valid = std::min(n_samples - a0, chunk);
+        {  // log-mel of the zero-filled 30 s window, encoder, cross K/V of stream 0 (:352-366)
+            std::lock_guard<std::mutex> g(c->mu);
+            CUDA_TRY(cudaSetDevice(c->device));
+            TRY(logmel_device(c, c->enc.audio + a0, std::max(n_valid, 0), chunk));
+            TRY(enc_finish(c, nullptr, 0));
+        }
+        ++out->n_windows;
+        // buildPromptWithContext (:507-530)
+        std::vector<int32_t> prompt = base;
+        if (o->condition_on_previous && !prev.empty()) {
+            const int max_prev = (dm.n_text_ctx / 2 - 1) - (int)base.size() - 1;
+            if (max_prev > 0) {
+                const int n = std::min((int)prev.size(), max_prev);
+                prompt.assign(1, o->sot_prev);
+                prompt.insert(prompt.end(), prev.end() - n, prev.end());
+                prompt.insert(prompt.end(), base.begin(), base.end());
+            }
+        }
+        int max_tokens = max_tok_full;
+        if (seg_size < n_frames) max_tokens = std::max(8, max_tokens * seg_size / n_frames);
+        int32_t len = 0;
+        double sum = 0;
+        float avg = 0, cr = 0, nsp = 0, temp = 0;
+        auto run = [&](const std::vector<int32_t> &p) -> int {
+            const int32_t slot = 0;
+            w4j_result r{tok.data(), &len, &sum, &avg, &cr, &nsp};
+            return w4j_decode_with_fallback(c, &slot, 1, p.data(), (int)p.size(), o->eot, max_tokens, o->suppress,
+                                            o->n_suppress, o->no_speech, o->ts_begin, std::max(1, o->beam_size), o->seed,
+                                            &r, &temp);
+        };
+        TRY(run(prompt));
+        if (o->condition_on_previous && !prev.empty() && avg < -1.0f) {  // :383-391
+            TRY(run(base));
+            prev.clear();
+        }
+        if (nsp > 0.6f && avg < -1.0f) {  // no speech (:396-399)
+            seek += seg_size;
+            continue;
+        }
+        if (with_ts) {  // :402-413
+            TRY(timestamp_segments(tok.data(), len, o->ts_begin, offset, precision, so));
+            int last_ts = -1;
+            for (int i = len - 1; i >= 0; --i)
+                if (tok[i] >= o->ts_begin) {
+                    last_ts = tok[i] - o->ts_begin;
+                    break;
+                }
+            seek += last_ts > 0 ? std::max(last_ts * stride, stride) : seg_size;
+        } else {  // one segment per window (:414-421)
+            if (len > 0) TRY(so.add(offset, std::min(offset + (float)seg_size * 160.0f / 16000.0f, duration),
+                                    std::vector<int32_t>(tok.begin(), tok.begin() + len)));
+            seek += seg_size;
+        }
+        if (o->condition_on_previous) prev.assign(tok.begin(), tok.begin() + len);  // :424-426
+    }
+    return c->cancel.load() ? set_err(W4J_ERR_CANCELLED, "cancelled") : W4J_OK;
 }

@@ -360,9 +360,9 @@ cudaError_t launch_enc_attn(const __half *qkvh, int T, int H, float *out, cudaSt
 // log-mel front end (k_logmel.cu)
 void logmel_tables(int n_fft, std::vector<float> &tabs);
 int logmel_frames(int n_samples, int n_fft, int hop);
-cudaError_t launch_logmel(const float *audio, int n_samples, int n, int hop, const float *tabs, const float *filt,
-                          int n_mels, int n_bins, int out_frames, float *spec, float *fmx, float *fmn, float *out,
-                          cudaStream_t s);// tensor map of a row-major f16 matrix read in [box_rows x 64 cols] boxes, 128-byte swizzle
+cudaError_t launch_logmel(const float *audio, int n_valid, int n_total, int n, int hop, const float *tabs,
+                          const float *filt, int n_mels, int n_bins, int out_frames, float *spec, float *fmx, float *fmn,
+                          float *out, cudaStream_t s);// tensor map of a row-major f16 matrix read in [box_rows x 64 cols] boxes, 128-byte swizzle
 bool make_tmap_f16_box(void *map_out, const void *base, int rows, int cols, int box_rows);
 cudaError_t select_prepare();
 cudaError_t attn_prepare();

@@ -23,7 +23,7 @@ from typing import NamedTuple, Sequence
 import numpy as np
 
 from . import ggml
-from ._lib import Dims, Result, check, lib
+from ._lib import Dims, Result, Segment, TranscribeOpts, Transcript, check, lib
 
 
 class DecodeResult(NamedTuple):
@@ -160,6 +160,29 @@ class WhisperDecoder:
         if slot is not None:
             self._xa_ids[slot] = ("audio", id(audio))
         return out
+
+    def transcribe(self, audio, sot, eot, no_speech, no_timestamps, sot_prev, ts_begin=-1, suppress_tokens=(),
+                   beam_size=1, condition_on_previous=True, seed=0):
+        """WhisperModel.transcribeChunked on the device (stream 0 is the working stream): 30 s windows
+        from the seek position through log-mel, encoder and decodeWithFallback, cut into segments.
+        Returns (segments, windows) with segments [(start_s, end_s, token_ids)]."""
+        a = np.ascontiguousarray(np.asarray(audio, dtype=np.float32).reshape(-1))
+        sot_a = np.ascontiguousarray(sot, dtype=np.int32)
+        sup = np.ascontiguousarray(list(suppress_tokens) or [0], dtype=np.int32)
+        i32p = ctypes.POINTER(ctypes.c_int32)
+        o = TranscribeOpts(sot_a.ctypes.data_as(i32p), sot_a.size, eot, no_speech, no_timestamps, sot_prev, ts_begin,
+                           sup.ctypes.data_as(i32p), len(suppress_tokens), beam_size, int(condition_on_previous), seed)
+        # the seek advances at least 2 frames (20 ms) per window: every window's tokens fit this bound
+        windows = a.size // 320 + 2
+        cap_tok = windows * (self.dims.n_text_ctx // 2) + 16
+        toks = np.zeros(cap_tok, np.int32)
+        segs = (Segment * cap_tok)()
+        t = Transcript(toks.ctypes.data_as(i32p), cap_tok, segs, cap_tok, 0, 0, 0)
+        check(lib().w4j_transcribe(self._ctx, _ptr(a) if a.size else None, a.size, ctypes.byref(o), ctypes.byref(t)))
+        out = [(segs[i].start, segs[i].end, toks[segs[i].token_begin:segs[i].token_begin + segs[i].n_tokens].tolist())
+               for i in range(t.n_segments)]
+        self._xa_ids.pop(0, None)
+        return out, t.n_windows
 
     def _slot_for(self, xa, slot):
         if xa is None:
