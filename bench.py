@@ -49,6 +49,8 @@ CONFIGS = {
                             note="north star: large-v3-turbo batch 1, greedy, 224 forced tokens"),
     "turbo-greedy-32": dict(arch="large-v3-turbo", wtype="f16", beam=1, max_tokens=224, streams=32,
                             note="configs[3] at 8 GPUs: 256 streams = 32 per GPU, greedy, 224 tokens"),
+    "turbo-greedy-128": dict(arch="large-v3-turbo", wtype="f16", beam=1, max_tokens=224, streams=128,
+                             note="configs[3] at 2 GPUs: 256 streams = 128 per GPU, greedy, 224 tokens"),
     "turbo-greedy-64": dict(arch="large-v3-turbo", wtype="f16", beam=1, max_tokens=224, streams=64,
                             note="configs[3] at 4 GPUs: 256 streams = 64 per GPU, greedy, 224 tokens"),
     "large-v3-q8-beam5": dict(arch="large-v3", wtype="q8_0", beam=5, max_tokens=444, streams=1,

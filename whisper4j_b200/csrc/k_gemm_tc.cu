@@ -637,7 +637,7 @@ static bool plan_gemm_tc(const GemvArgs &a, int sms, int &nu, GemmTcLaunch &L, i
     if (a.M < 16 || K % kKB != 0 || N < 1) return false;
     if (!(a.W.type == WT_F16 || (q8 && a.W.st && N % kTileRows == 0))) return false;
     // more than 128 rows (f16): the activations come staged as f16 hi / lo rows (k_act_hilo)
-    bt = !q8 && a.M > 128;
+    bt = gemm_tc_staged(a);
     if (q8 && a.M > 128) return false;
     if (!bt && a.in_mode != IN_ACT && (K % 128 != 0 || K > 1280)) return false;
     if (!bt && a.in_mode == IN_EMBED_LN && a.E.type != WT_F16) return false;
@@ -765,8 +765,19 @@ cudaError_t gemm_tc_prepare() {
     return cudaSuccess;
 }
 
+// f16 projections of at least this many rows take their activations staged as f16 hi / lo rows
+// (k_act_hilo) instead of building the B operand in every block (W4J_STAGED_MIN_ROWS overrides)
+static int staged_min_rows() {
+    static const int v = [] {
+        const char *e = getenv("W4J_STAGED_MIN_ROWS");
+        const int r = e ? atoi(e) : 65;
+        return r < 16 ? 16 : r;
+    }();
+    return v;
+}
+
 // cudaErrorNotSupported when the projection is outside the tensor-core kernel's range.
-bool gemm_tc_staged(const GemvArgs &a) { return a.W.type == WT_F16 && a.M > 128; }
+bool gemm_tc_staged(const GemvArgs &a) { return a.W.type == WT_F16 && (a.M > 128 || a.M >= staged_min_rows()); }
 
 bool gemm_tc_supported(const GemvArgs &a, int sms) {
     int nu, tiles, chunks;
