@@ -534,6 +534,8 @@ __global__ void __launch_bounds__(kStreamThreads, 1)
     __shared__ __align__(16) __half pw[2 * kWarps][8][kPwPad];
     __shared__ float wm[2 * kWarps][8], wl[2 * kWarps][8];
     __shared__ __align__(16) float red[2 * kWarps][NQ * kHeadDim];
+    constexpr int kLocal = 64;  // pairs of one warpgroup whose key counts are kept in shared memory
+    __shared__ short plen[2][kLocal];
     const int tid = threadIdx.x, wg = tid / kAttnThreads, gtid = tid % kAttnThreads;
     const int warp = tid >> 5, gwarp = gtid >> 5, lane = tid & 31, g = lane >> 2, tq = lane & 3;
     const int H = a.n_head, n_pairs = a.groups * H;
@@ -542,9 +544,20 @@ __global__ void __launch_bounds__(kStreamThreads, 1)
     const bool producer = gwarp == 0 && lane == 0;
     // keys of a pair's group: the encoder rows, or the sequence's positions 0 .. pos
     auto len_of = [&](int grp) { return CROSS ? a.n_audio : a.pos[grp] + 1; };
-    auto tiles_of = [&](int pair) {
+    auto len_global = [&](int pair) {
         const int grp = pair / H;
-        return (a.active && !a.active[grp]) ? 0 : (len_of(grp) + kAttnKeyTile - 1) / kAttnKeyTile;
+        return (a.active && !a.active[grp]) ? 0 : len_of(grp);
+    };
+    // the warpgroup's pairs first, first + stride, ...: their key counts (0 for finished sequences) read
+    // once into shared memory, so that neither the producer nor a pair's start waits on a global load
+    const bool local = (n_pairs - first + stride - 1) / stride <= kLocal;
+    auto keys_of = [&](int pair) { return local ? (int)plen[wg][(pair - first) / stride] : len_global(pair); };
+    auto tiles_of = [&](int pair) { return (keys_of(pair) + kAttnKeyTile - 1) / kAttnKeyTile; };
+    auto fill_local = [&]() {
+        if (local)
+            for (int i = gtid; first + i * stride < n_pairs; i += kAttnThreads)
+                plen[wg][i] = (short)len_global(first + i * stride);
+        group_sync(1 + wg);
     };
     if (tid < 2 * kStreamBufs) {
         mbar_init(&full[tid / kStreamBufs][tid % kStreamBufs], 1);
@@ -556,6 +569,7 @@ __global__ void __launch_bounds__(kStreamThreads, 1)
         pdl_trigger();
         pdl_wait();
     }
+    fill_local();
     // producer cursor: the next (pair, tile) to request, in the consumers' order
     int ppair = first, ptile = 0, pn = ppair < n_pairs ? tiles_of(ppair) : 0;
     auto skip_empty = [&]() {
@@ -589,14 +603,32 @@ __global__ void __launch_bounds__(kStreamThreads, 1)
     float m[2], l[2], of[4][4];
     bool ok = true;
     int item = 0;
+    // the queries of the warpgroup's next pair are loaded while the current one is computed
+    const int qi_l = gtid / (kHeadDim / 4), qc_l = gtid % (kHeadDim / 4);
+    auto q_load = [&](int pair) {
+        float4 v = make_float4(0.f, 0.f, 0.f, 0.f);
+        if (gtid < 8 * kHeadDim / 4 && qi_l < NQ && pair < n_pairs) {
+            const int grp = pair / H, head = pair - grp * H;
+            v = reinterpret_cast<const float4 *>(a.q + (size_t)(grp * NQ + qi_l) * a.d + head * kHeadDim)[qc_l];
+        }
+        return v;
+    };
+    auto next_live = [&](int pair) {
+        while (pair < n_pairs && tiles_of(pair) == 0) pair += stride;
+        return pair;
+    };
+    int qpair = next_live(first);
+    float4 qnext = q_load(qpair);
     for (int pair = first; pair < n_pairs; pair += stride) {
         const int nt = tiles_of(pair);
         if (nt == 0) continue;
-        const int grp = pair / H, head = pair - grp * H, len = len_of(grp);
+        const int grp = pair / H, head = pair - grp * H, len = keys_of(pair);
+        const float4 qcur = qpair == pair ? qnext : q_load(pair);
+        qpair = next_live(pair + stride);
+        qnext = q_load(qpair);
         if (gtid < 8 * kHeadDim / 4) {  // this pair's queries as f16; rows >= NQ zero
-            const int qi = gtid / (kHeadDim / 4), c = gtid % (kHeadDim / 4);
-            float4 v = make_float4(0.f, 0.f, 0.f, 0.f);
-            if (qi < NQ) v = reinterpret_cast<const float4 *>(a.q + (size_t)(grp * NQ + qi) * a.d + head * kHeadDim)[c];
+            const int qi = qi_l, c = qc_l;
+            const float4 v = qcur;
             const __half2 h0 = __floats2half2_rn(v.x, v.y), h1 = __floats2half2_rn(v.z, v.w);
             *reinterpret_cast<uint2 *>(&qh[wg][qi][4 * c]) =
                 make_uint2(*reinterpret_cast<const uint32_t *>(&h0), *reinterpret_cast<const uint32_t *>(&h1));
