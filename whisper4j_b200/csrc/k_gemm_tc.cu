@@ -94,7 +94,7 @@ __device__ __forceinline__ GemvArgs rows_of(const GemvArgs &g, int m0, int n) {
 template <int NU, int WT, bool BT>
 __global__ void __launch_bounds__(kGemmThreads, 1) k_gemm_tc(GemvArgs a_all, const __grid_constant__ CUtensorMap tmap,
                                                               const __grid_constant__ CUtensorMap bmap, GemmTcLaunch L) {
-    static_assert(!BT || (NU == 128 && WT == WT_F16), "staged B: 128-row chunks of f16 projections");
+    static_assert(!BT || WT == WT_F16, "staged B: f16 projections");
     constexpr bool kQ8 = WT == WT_Q8;
     constexpr unsigned kBTile = 2u * NU * 128u;  // one k-block of B: hi and lo rows of 128 bytes
     constexpr unsigned SB = kQ8 ? kRawStage : BT ? (unsigned)kStageBytes + kBTile : (unsigned)kStageBytes;
@@ -663,7 +663,7 @@ static bool plan_gemm_tc(const GemvArgs &a, int sms, int &nu, GemmTcLaunch &L, i
     const size_t budget = 220 * 1024;
     // weight ring: f16 tiles straight from TMA; Q8_0 raw int8 + scale stages after the two
     // dequantised A stages (the A stages come first, 1024-aligned for the swizzle)
-    const size_t sb = q8 ? kRawStage : bt ? (size_t)kStageBytes + 2 * 128 * 128 : (size_t)kStageBytes;
+    const size_t sb = q8 ? kRawStage : bt ? (size_t)kStageBytes + 2 * (size_t)nu * 128 : (size_t)kStageBytes;
     const size_t front = q8 ? 2 * (size_t)kAStage : 0;
     // the partials get their own buffer when it fits beside two stages, else they reuse the ring
     L.recv_alias = fixed + front + recvbytes + 2 * sb > budget;
@@ -743,6 +743,9 @@ static cudaError_t prep_wt() {
 cudaError_t gemm_tc_prepare() {
     cudaError_t e = prep_wt<WT_F16>();
     if (e == cudaSuccess) e = prep_wt<WT_Q8>();
+    if (e == cudaSuccess) e = allow_dynamic_smem(k_gemm_tc<16, WT_F16, true>);
+    if (e == cudaSuccess) e = allow_dynamic_smem(k_gemm_tc<32, WT_F16, true>);
+    if (e == cudaSuccess) e = allow_dynamic_smem(k_gemm_tc<64, WT_F16, true>);
     if (e == cudaSuccess) e = allow_dynamic_smem(k_gemm_tc<128, WT_F16, true>);
     if (e != cudaSuccess) return e;
     // one block per SM (the register file), so the count does not depend on shared memory
@@ -766,7 +769,9 @@ cudaError_t gemm_tc_prepare() {
 }
 
 // f16 projections of at least this many rows take their activations staged as f16 hi / lo rows
-// (k_act_hilo) instead of building the B operand in every block (W4J_STAGED_MIN_ROWS overrides)
+// (k_act_hilo) instead of building the B operand in every block (W4J_STAGED_MIN_ROWS overrides).
+// Measured at 224-token turbo decodes: staged from 65 rows is 2.1x faster at 128 rows per GPU and
+// equal at 64; below that the extra launch costs more than the in-block build (32 rows: -10 %).
 static int staged_min_rows() {
     static const int v = [] {
         const char *e = getenv("W4J_STAGED_MIN_ROWS");
@@ -793,7 +798,12 @@ cudaError_t launch_gemm_tc(const GemvArgs &a, const void *tmap, const void *bmap
     if (!tmap || !plan_gemm_tc(a, sms, nu, L, tiles, chunks, bt) || (bt && !bmap)) return cudaErrorNotSupported;
     const CUtensorMap &map = *reinterpret_cast<const CUtensorMap *>(tmap);
     const CUtensorMap &bm = bt ? *reinterpret_cast<const CUtensorMap *>(bmap) : map;
-    if (bt) return launch_gemm_tc_t<128, WT_F16, true>(a, map, bm, L, tiles, chunks, s, pdl);
+    if (bt) switch (nu) {  // staged B tiles of 2 nu rows (hi, lo)
+            case 16: return launch_gemm_tc_t<16, WT_F16, true>(a, map, bm, L, tiles, chunks, s, pdl);
+            case 32: return launch_gemm_tc_t<32, WT_F16, true>(a, map, bm, L, tiles, chunks, s, pdl);
+            case 64: return launch_gemm_tc_t<64, WT_F16, true>(a, map, bm, L, tiles, chunks, s, pdl);
+            default: return launch_gemm_tc_t<128, WT_F16, true>(a, map, bm, L, tiles, chunks, s, pdl);
+        }
     if (a.W.type == WT_Q8) switch (nu) {
             case 16: return launch_gemm_tc_t<16, WT_Q8, false>(a, map, bm, L, tiles, chunks, s, pdl);
             case 32: return launch_gemm_tc_t<32, WT_Q8, false>(a, map, bm, L, tiles, chunks, s, pdl);
@@ -809,20 +819,20 @@ cudaError_t launch_gemm_tc(const GemvArgs &a, const void *tmap, const void *bmap
 }
 
 // ---------------------------------------------------------------------------
-// k_act_hilo: the activations of a projection with more than 128 rows, once, as the UMMA B
-// operand's f16 hi / lo rows: out[(z * 256 + r) * K + k] = hi, out[(z * 256 + 128 + r) * K + k] = lo
-// for sequence m = z * mchunk + r (rows past the chunk's sequences zero), after the input mode
+// k_act_hilo: the activations of a staged projection, once, as the UMMA B operand's f16 hi / lo
+// rows: out[(z * 2 nu + r) * K + k] = hi, out[(z * 2 nu + nu + r) * K + k] = lo for sequence
+// m = z * mchunk + r (rows past the chunk's sequences zero; nu = the GEMM's row tile), after the input mode
 // (plain, LayerNorm of x, or token + positional embedding then LayerNorm, kept in x_out).
 // One warp per (chunk, row); LayerNorm as Tensor.java:592-619 (two-pass, eps 1e-5).
 // ---------------------------------------------------------------------------
-__global__ void __launch_bounds__(256) k_act_hilo(GemvArgs a, int mchunk, int chunks, __half *out) {
+__global__ void __launch_bounds__(256) k_act_hilo(GemvArgs a, int mchunk, int chunks, int nu, __half *out) {
     const int K = a.W.K;
     const int gw = (int)((blockIdx.x * blockDim.x + threadIdx.x) >> 5), lane = threadIdx.x & 31;
     pdl_trigger();
     pdl_wait();
-    if (gw >= chunks * 128) return;
-    const int z = gw >> 7, r = gw & 127, m = z * mchunk + r;
-    __half *hi = out + ((size_t)z * 256 + r) * K, *lo = hi + (size_t)128 * K;
+    if (gw >= chunks * nu) return;
+    const int z = gw / nu, r = gw - z * nu, m = z * mchunk + r;
+    __half *hi = out + ((size_t)z * 2 * nu + r) * K, *lo = hi + (size_t)nu * K;
     const bool live = r < mchunk && m < a.M;
     auto put = [&](int k, float4 v) {
         const __half2 h0 = __floats2half2_rn(v.x, v.y), h1 = __floats2half2_rn(v.z, v.w);
@@ -891,15 +901,20 @@ __global__ void __launch_bounds__(256) k_act_hilo(GemvArgs a, int mchunk, int ch
         }
 }
 
-// Rows of the staged activation buffer for M sequences: chunks * 256.
+// Rows of the staged activation buffer for M sequences (at most chunks * 256), and the rows of one
+// staged B tile (2 nu: the tensor map's box height)
 int act_hilo_rows(int M) { return ((M + 127) / 128) * 256; }
+int act_hilo_box_rows(int M) {
+    const int chunks = (M + 127) / 128, mchunk = (M + chunks - 1) / chunks;
+    return 2 * nu_for(mchunk);
+}
 
 cudaError_t launch_act_hilo(const GemvArgs &a, __half *out, cudaStream_t s, bool pdl) {
     const int K = a.W.K;
     if (K % 4 != 0 || (a.in_mode != IN_ACT && (K % 128 != 0 || K > 1280))) return cudaErrorNotSupported;
-    const int chunks = (a.M + 127) / 128, mchunk = (a.M + chunks - 1) / chunks;
+    const int chunks = (a.M + 127) / 128, mchunk = (a.M + chunks - 1) / chunks, nu = nu_for(mchunk);
     cudaLaunchConfig_t cfg = {};
-    cfg.gridDim = dim3((unsigned)(chunks * 128 * 32 + 255) / 256);
+    cfg.gridDim = dim3((unsigned)(chunks * nu * 32 + 255) / 256);
     cfg.blockDim = dim3(256);
     cfg.stream = s;
     cudaLaunchAttribute attr[1];
@@ -907,7 +922,7 @@ cudaError_t launch_act_hilo(const GemvArgs &a, __half *out, cudaStream_t s, bool
     attr[0].val.programmaticStreamSerializationAllowed = 1;
     cfg.attrs = attr;
     cfg.numAttrs = pdl ? 1 : 0;
-    return cudaLaunchKernelEx(&cfg, k_act_hilo, a, mchunk, chunks, out);
+    return cudaLaunchKernelEx(&cfg, k_act_hilo, a, mchunk, chunks, nu, out);
 }
 
 }  // namespace w4j

@@ -139,10 +139,9 @@ struct w4j_ctx {
     int *op_err = nullptr;    // error word of the op-level vocabulary pass (w4j_op_logits_argmax)
     __half *op_st = nullptr;  // tiled Q8_0 scales of the op-level linear (w4j_op_linear)
     size_t op_st_n = 0;
-    // activations of projections with more than 128 rows, staged as f16 hi / lo B-operand rows
-    // ([act_hilo_rows(Mbuf)][K] for K = d and 4d), with a tensor map for each K
+    // activations of the staged projections (f16, 16 rows and more) as f16 hi / lo B-operand rows
+    // ([act_hilo_rows(Mbuf)][K] for K = d and 4d); their tensor maps are made per launch
     __half *hilo = nullptr;
-    alignas(64) unsigned char hilo_map_d[128] = {}, hilo_map_4d[128] = {};
     bool hilo_ok = false;
     __half *op_hilo = nullptr;  // the same for w4j_op_linear, grown on demand
     size_t op_hilo_n = 0;
@@ -420,8 +419,7 @@ extern "C" int w4j_ctx_create(const w4j_dims *dims, int device, int max_streams,
     {
         const int rows = act_hilo_rows(c->Mbuf);
         if ((rc = dalloc(c, &c->hilo, (size_t)rows * 4 * d))) return fail(rc);
-        c->hilo_ok = make_tmap_f16_box(c->hilo_map_d, c->hilo, rows, d, 256) &&
-                     make_tmap_f16_box(c->hilo_map_4d, c->hilo, rows, 4 * d, 256);
+        c->hilo_ok = c->hilo != nullptr;  // its tensor maps are made per launch (box height by row count)
     }
     c->n_parts = logits_parts_for(c->V, c->sm_count);
     if ((rc = dalloc(c, &c->logit_part, MB * c->n_parts * kPartStride)) ||
@@ -868,7 +866,7 @@ static int enc_gemm(w4j_ctx *c, const DMat &W, const void *wmap, int M, const fl
         return 0;
     }
     alignas(64) unsigned char bmap[128];
-    if (!make_tmap_f16_box(bmap, c->enc.hilo, act_hilo_rows(M), W.K, 256))
+    if (!make_tmap_f16_box(bmap, c->enc.hilo, act_hilo_rows(M), W.K, act_hilo_box_rows(M)))
         return set_err(W4J_ERR_CUDA, "encoder: activation tensor map");
     CUDA_TRY(launch_act_hilo(g, c->enc.hilo, c->stream, false));
     CUDA_TRY(launch_gemm_tc(g, wmap, bmap, c->sm_count, c->stream, false));
@@ -1088,11 +1086,13 @@ static cudaError_t run_proj(w4j_ctx *c, const GemvArgs &g, const LayerDev &ly, P
     if (ly.tmap_ok[p] && g.M >= 16 && gemm_tc_supported(g, c->sm_count)) {
         const void *bmap = nullptr;
         if (gemm_tc_staged(g)) {
-            if (c->hilo_ok && (g.W.K == c->d || g.W.K == 4 * c->d)) {
+            alignas(64) unsigned char bm[128];
+            if (c->hilo_ok && (g.W.K == c->d || g.W.K == 4 * c->d) &&
+                make_tmap_f16_box(bm, c->hilo, act_hilo_rows(c->Mbuf), g.W.K, act_hilo_box_rows(g.M))) {
                 e = launch_act_hilo(g, c->hilo, c->stream, pdl);
                 if (e != cudaSuccess) return e;
                 ++launches;
-                bmap = g.W.K == c->d ? c->hilo_map_d : c->hilo_map_4d;
+                bmap = bm;
                 e = launch_gemm_tc(g, ly.tmap[p], bmap, c->sm_count, c->stream, pdl);
             }
         } else {
@@ -2130,7 +2130,7 @@ extern "C" int w4j_op_linear(w4j_ctx *c, const float *x, int M, int K, const voi
                     c->op_hilo_n = need;
                 }
                 alignas(64) unsigned char bmap[128];
-                if (make_tmap_f16_box(bmap, c->op_hilo, act_hilo_rows(M), K, 256)) {
+                if (make_tmap_f16_box(bmap, c->op_hilo, act_hilo_rows(M), K, act_hilo_box_rows(M))) {
                     e = launch_act_hilo(g, c->op_hilo, s, false);
                     if (e == cudaSuccess) e = launch_gemm_tc(g, map, bmap, c->sm_count, s, false);
                 }

@@ -343,11 +343,12 @@ cudaError_t launch_cross_kv_tc(const float *xa, int A, int d, const void *kmap, 
 // the GEMV's input modes and epilogues; `tmap` is make_tmap_f16_rows of a.W.h (f16) or
 // make_tmap_i8_rows of a.W.q (Q8_0); cudaErrorNotSupported outside its range
 // More than 128 rows (f16): `bmap` is make_tmap_f16_rows(…, rows 256) of the activations staged by
-// launch_act_hilo beforehand ([act_hilo_rows(M)][K] f16), read as [256 x 64] boxes.
+// launch_act_hilo beforehand ([act_hilo_rows(M)][K] f16), read as [act_hilo_box_rows(M) x 64] boxes.
 cudaError_t launch_gemm_tc(const GemvArgs &a, const void *tmap, const void *bmap, int sms, cudaStream_t s, bool pdl);
 bool gemm_tc_staged(const GemvArgs &a);  // the projection reads staged activations (launch_act_hilo first)
 bool gemm_tc_supported(const GemvArgs &a, int sms);  // the tensor-core kernel takes this projection
 int act_hilo_rows(int M);
+int act_hilo_box_rows(int M);  // rows of one staged B tile (the tensor map box height)
 cudaError_t launch_act_hilo(const GemvArgs &a, __half *out, cudaStream_t s, bool pdl);
 
 // audio encoder (k_encoder.cu)
