@@ -488,6 +488,21 @@ def front_end_timing(cfg, local_rank, tc_peak):
             t0 = time.perf_counter()
             dec.log_mel(audio)
             mel_ms.append(1e3 * (time.perf_counter() - t0))
+        # the whole chunked loop (w4j_transcribe) on 120 s of audio, greedy, timestamps on
+        long_audio = seeded_audio(8, seconds=120.0)
+        sot = prompt_for(dims)[:3]
+        eot = eot_for(dims)
+        # previous-text marker, no-speech, no-timestamps and the first timestamp of this vocabulary
+        sot_prev, no_speech, no_ts, ts_begin = {51866: (50362, 50363, 50364, 50365),
+                                                 51865: (50361, 50362, 50363, 50364)}.get(
+            dims.n_vocab, (50360, 50361, 50362, 50363))
+        dec.transcribe(long_audio[:480000], sot, eot, no_speech, no_ts, sot_prev, ts_begin=ts_begin,
+                       suppress_tokens=[eot])
+        torch.cuda.synchronize()
+        t0 = time.perf_counter()
+        segs, windows = dec.transcribe(long_audio, sot, eot, no_speech, no_ts, sot_prev, ts_begin=ts_begin,
+                                       suppress_tokens=[eot])
+        tr_s = time.perf_counter() - t0
     w = statistics.median(ms)
     fl = encoder_flops(dims)
     return {"model": cfg["arch"], "window_s": 30, "ms_per_window": w, "log_mel_ms": statistics.median(mel_ms),
@@ -495,7 +510,11 @@ def front_end_timing(cfg, local_rank, tc_peak):
             "frac_of_bf16_peak": fl / (w * 1e-3) / 1e12 / tc_peak if tc_peak else None,
             "includes": "w4j_encode_audio wall clock: 30 s of host audio to the device, log-mel, encoder, the "
                         "stream's cross K/V projection; log_mel_ms: w4j_log_mel with the spectrogram back to the host",
-            "data": "seeded sinusoid audio, seeded synthetic weights"}
+            "data": "seeded sinusoid audio, seeded synthetic weights",
+            "transcribe": {"audio_s": 120.0, "wall_s": tr_s, "realtime_factor": 120.0 / tr_s, "windows": windows,
+                           "segments": len(segs),
+                           "includes": "w4j_transcribe: audio upload, per 30 s window log-mel, encoder, cross K/V, "
+                                       "decode with temperature fallback, segments and seek, token ids to the host"}}
 
 
 def main():
