@@ -765,6 +765,135 @@ cudaError_t launch_attn_self_stream(const AttnArgs &a, const void *kmap, const v
                               *reinterpret_cast<const CUtensorMap *>(vmap));
 }
 
+// ---------------------------------------------------------------------------
+// k_attn_self_warps: self-attention of many sequences (one query each, keys 0 .. pos) with one
+// warp per (sequence, head) pair and no step that involves more than one warp: each warp streams its
+// pair's keys in 32-key tiles through its own two-buffer TMA ring (128-byte swizzle, the layout
+// tile_warp reads), runs tile_warp over both 16-key halves of a tile, and writes its output row.
+// Twelve warps per SM, each with a tile in flight while it computes the other, replace the
+// warpgroup-wide combine of k_attn_pairs, whose per-pair barriers dominated at ~120 keys per pair.
+// ---------------------------------------------------------------------------
+constexpr int kSwWarps = 12, kSwKeys = 32, kSwBufs = 2;
+constexpr unsigned kSwHalf = kSwKeys * kHeadDim * 2;  // K (or V) of one tile: 4 KB
+
+__global__ void __launch_bounds__(kSwWarps * 32, 1)
+    k_attn_self_warps(AttnArgs a, const __grid_constant__ CUtensorMap kmap, const __grid_constant__ CUtensorMap vmap) {
+    extern __shared__ __align__(1024) unsigned char sraw[];
+    unsigned char *base = sraw + ((1024u - (smem_u32(sraw) & 1023u)) & 1023u);
+    __shared__ __align__(8) uint64_t full[kSwWarps][kSwBufs];
+    __shared__ __align__(16) __half qh[kSwWarps][8][kHeadDim + 8];
+    __shared__ __align__(16) __half pw[kSwWarps][8][kPwPad];
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31, g = lane >> 2, tq = lane & 3;
+    const int H = a.n_head, n_pairs = a.groups * H;
+    const int stride = kSwWarps * (int)gridDim.x, first = (int)blockIdx.x * kSwWarps + warp;
+    unsigned char *wb = base + (size_t)warp * kSwBufs * 2 * kSwHalf;
+    if (lane < kSwBufs) mbar_init(&full[warp][lane], 1);
+    fence_mbar_init();
+    __syncwarp();
+    pdl_trigger();
+    pdl_wait();  // positions, slots, queries and this step's K / V rows come from the kernels before
+    auto keys_of = [&](int pair) {
+        const int grp = pair / H;
+        return (a.active && !a.active[grp]) ? 0 : a.pos[grp] + 1;
+    };
+    // lane 0's cursor: the next (pair, tile) to request, in the order the warp consumes them
+    int ppair = first, ptile = 0, pn = ppair < n_pairs ? (keys_of(ppair) + kSwKeys - 1) / kSwKeys : 0;
+    int issued = 0;
+    auto skip = [&]() {
+        while (ppair < n_pairs && ptile >= pn) {
+            ppair += stride;
+            ptile = 0;
+            pn = ppair < n_pairs ? (keys_of(ppair) + kSwKeys - 1) / kSwKeys : 0;
+        }
+    };
+    auto issue = [&]() {
+        const int grp = ppair / H, head = ppair - grp * H, b = issued % kSwBufs;
+        const int y = ((a.seq_slot[grp] * a.n_layer + a.layer) * H + head) * a.n_ctx + ptile * kSwKeys;
+        unsigned char *dst = wb + (size_t)b * 2 * kSwHalf;
+        mbar_expect_tx(&full[warp][b], 2 * kSwHalf);
+        tma_load_2d(dst, &kmap, 0, y, &full[warp][b]);
+        tma_load_2d(dst + kSwHalf, &vmap, 0, y, &full[warp][b]);
+        ++issued;
+        ++ptile;
+        skip();
+    };
+    if (lane == 0) {
+        skip();
+        for (int i = 0; i < kSwBufs && ppair < n_pairs; ++i) issue();
+    }
+    bool ok = true;
+    int item = 0;
+    for (int pair = first; pair < n_pairs; pair += stride) {
+        const int len = keys_of(pair);
+        if (len == 0) continue;
+        const int grp = pair / H, head = pair - grp * H;
+        for (int i = lane; i < 8 * kHeadDim / 4; i += 32) {  // the query as row 0 of the B tile, rows 1-7 zero
+            const int qi = i / (kHeadDim / 4), c = i % (kHeadDim / 4);
+            float4 v = make_float4(0.f, 0.f, 0.f, 0.f);
+            if (qi == 0) v = reinterpret_cast<const float4 *>(a.q + (size_t)grp * a.d + head * kHeadDim)[c];
+            const __half2 h0 = __floats2half2_rn(v.x, v.y), h1 = __floats2half2_rn(v.z, v.w);
+            *reinterpret_cast<uint2 *>(&qh[warp][qi][4 * c]) =
+                make_uint2(*reinterpret_cast<const uint32_t *>(&h0), *reinterpret_cast<const uint32_t *>(&h1));
+        }
+        __syncwarp();
+        float m[2] = {-INFINITY, -INFINITY}, l[2] = {0.f, 0.f}, of[4][4];
+#pragma unroll
+        for (int mt = 0; mt < 4; ++mt) of[mt][0] = of[mt][1] = of[mt][2] = of[mt][3] = 0.f;
+        const int nt = (len + kSwKeys - 1) / kSwKeys;
+        for (int t = 0; t < nt; ++t, ++item) {
+            const int b = item % kSwBufs, nk = min(kSwKeys, len - t * kSwKeys);
+            __half *sk = reinterpret_cast<__half *>(wb + (size_t)b * 2 * kSwHalf), *sv = sk + kSwKeys * kHeadDim;
+            ok = ok && mbar_wait(&full[warp][b], (unsigned)((item / kSwBufs) & 1), a.err);
+            if (ok) {
+                // V rows past the keys meet zero probabilities in P.V and must be finite (whole rows:
+                // the swizzle only permutes chunks within a row)
+                for (int c = lane; c < (kSwKeys - nk) * 8; c += 32)
+                    *reinterpret_cast<uint4 *>(&sv[(nk + (c >> 3)) * kHeadDim + (c & 7) * 8]) = make_uint4(0u, 0u, 0u, 0u);
+                __syncwarp();
+                tile_warp<1>(sk, sv, nk, qh[warp], pw[warp], m, l, of, 0, lane);
+                tile_warp<1>(sk, sv, nk, qh[warp], pw[warp], m, l, of, 1, lane);
+            }
+            fence_proxy_async();  // the warp's generic accesses to the buffer precede the next copy into it
+            __syncwarp();
+            if (lane == 0 && ok && ppair < n_pairs) issue();
+        }
+        if (ok && tq == 0) {  // query 0's O: dims 16 mt + g and 16 mt + g + 8 on the lanes with tq = 0
+            const float inv = 1.0f / l[0];
+            float *o = a.out + (size_t)grp * a.d + head * kHeadDim;
+#pragma unroll
+            for (int mt = 0; mt < 4; ++mt) {
+                o[16 * mt + g] = of[mt][0] * inv;
+                o[16 * mt + g + 8] = of[mt][2] * inv;
+            }
+        }
+        __syncwarp();  // qh and pw are rewritten by the next pair
+    }
+    // after a wait that ran out: the copies still in flight land before the warp exits
+    if (!ok && lane == 0)
+        for (int i = issued > kSwBufs ? issued - kSwBufs : 0; i < issued; ++i)
+            mbar_wait(&full[warp][i % kSwBufs], (unsigned)((i / kSwBufs) & 1), nullptr);
+}
+
+cudaError_t launch_attn_self_warps(const AttnArgs &a, const void *kmap32, const void *vmap32, int sms, cudaStream_t s,
+                                   bool pdl) {
+    if (a.groups <= 0) return cudaSuccess;
+    if (a.cross || a.table || a.mask || a.kv_len || a.nq != 1 || !kmap32 || !vmap32) return cudaErrorInvalidValue;
+    const long long pairs = (long long)a.groups * a.n_head;
+    const long long want = (pairs + kSwWarps - 1) / kSwWarps;
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = dim3((unsigned)(want < sms ? want : sms));
+    cfg.blockDim = dim3(kSwWarps * 32);
+    cfg.dynamicSmemBytes = (size_t)kSwWarps * kSwBufs * 2 * kSwHalf + 1024;
+    cfg.stream = s;
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[0].val.programmaticStreamSerializationAllowed = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = pdl ? 1 : 0;
+    return cudaLaunchKernelEx(&cfg, k_attn_self_warps, a, *reinterpret_cast<const CUtensorMap *>(kmap32),
+                              *reinterpret_cast<const CUtensorMap *>(vmap32));
+}
+
 // Key splits of one launch: up to kMaxSplits (one cluster); tiles each block stages.
 int attn_max_splits(int) { return kMaxSplits; }
 static int attn_tiles(const AttnArgs &a) {
@@ -780,6 +909,7 @@ static cudaError_t prep_nq() {
 
 cudaError_t attn_prepare() {
     cudaError_t e = allow_dynamic_smem(k_attn_pairs<1, false>);
+    if (e == cudaSuccess) e = allow_dynamic_smem(k_attn_self_warps);
     if (e == cudaSuccess) e = allow_dynamic_smem(k_attn_pairs<1, true>);
     if (e == cudaSuccess) e = allow_dynamic_smem(k_attn_pairs<2, true>);
     if (e == cudaSuccess) e = allow_dynamic_smem(k_attn_pairs<3, true>);

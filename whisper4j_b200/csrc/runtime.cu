@@ -163,6 +163,8 @@ struct w4j_ctx {
     alignas(64) unsigned char e_tmap[128] = {};  // TMA map of the f16 token embedding
     alignas(64) unsigned char xk_tmap[128] = {}, xv_tmap[128] = {};  // cross K / V caches as [rows][64]
     alignas(64) unsigned char sk_tmap[128] = {}, sv_tmap[128] = {};  // self K / V caches as [rows][64]
+    alignas(64) unsigned char sk_tmap32[128] = {}, sv_tmap32[128] = {};  // the same, 32-row boxes
+    bool self_warps = true;  // W4J_SELF_PAIRS=1: many-sequence self-attention on k_attn_pairs instead
     bool s_tmap_ok = false;
     bool x_tmap_ok = false;
     bool e_tmap_ok = false;
@@ -325,7 +327,9 @@ static int size_self(w4j_ctx *c, int cap, bool keep_rows) {
     c->cap = cap;
     const size_t srows = (size_t)c->n_slots * L * c->H * cap;
     c->s_tmap_ok = srows < (size_t)INT32_MAX && make_tmap_f16_rows(c->sk_tmap, c->sk, (int)srows, kHeadDim) &&
-                   make_tmap_f16_rows(c->sv_tmap, c->sv, (int)srows, kHeadDim);
+                   make_tmap_f16_rows(c->sv_tmap, c->sv, (int)srows, kHeadDim) &&
+                   make_tmap_f16_box(c->sk_tmap32, c->sk, (int)srows, kHeadDim, 32) &&
+                   make_tmap_f16_box(c->sv_tmap32, c->sv, (int)srows, kHeadDim, 32);
     return 0;
 }
 
@@ -383,6 +387,7 @@ extern "C" int w4j_ctx_create(const w4j_dims *dims, int device, int max_streams,
     if (const char *ev = getenv("W4J_STEP_KERNEL")) c->use_step = ev[0] == '1';
     if (const char *ev = getenv("W4J_NO_ATTN_PAIRS")) c->attn_pairs = ev[0] == '0';
     if (const char *ev = getenv("W4J_STEP_BAR")) c->step_bar_mode = ev[0] == '1';
+    if (const char *ev = getenv("W4J_SELF_PAIRS")) c->self_warps = ev[0] != '1';
     if (const char *ev = getenv("W4J_STEP_INFLIGHT_KB")) {
         const long kb = strtol(ev, nullptr, 10);
         if (kb >= 16 && kb <= 128) c->step_inflight = (unsigned)kb << 10;
@@ -1163,7 +1168,8 @@ static int run_layers(w4j_ctx *c, const PassArgs &pa, long long &launches) {
         sa.self_prefetch = pa.self_prefetch;
         CUDA_TRY(tmark(c, KC_SELF_ATTN, true));
         if (c->s_tmap_ok && attn_self_stream_pays(sa, c->sm_count))
-            CUDA_TRY(launch_attn_self_stream(sa, c->sk_tmap, c->sv_tmap, c->sm_count, c->stream, pdl));
+            CUDA_TRY(c->self_warps ? launch_attn_self_warps(sa, c->sk_tmap32, c->sv_tmap32, c->sm_count, c->stream, pdl)
+                                   : launch_attn_self_stream(sa, c->sk_tmap, c->sv_tmap, c->sm_count, c->stream, pdl));
         else CUDA_TRY(launch_attn(sa, c->stream, pdl));
         CUDA_TRY(tmark(c, KC_SELF_ATTN, false));
 

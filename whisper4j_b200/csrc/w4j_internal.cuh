@@ -296,6 +296,9 @@ cudaError_t launch_attn_stream(const AttnArgs &a, const void *kmap, const void *
 bool attn_self_stream_pays(const AttnArgs &a, int sms);
 cudaError_t launch_attn_self_stream(const AttnArgs &a, const void *kmap, const void *vmap, int sms, cudaStream_t s,
                                     bool pdl);
+// the same, one warp per pair in 32-key tiles (maps with 32-row boxes)
+cudaError_t launch_attn_self_warps(const AttnArgs &a, const void *kmap32, const void *vmap32, int sms, cudaStream_t s,
+                                   bool pdl);
 // cross-attention of many (stream, head) pairs with a warpgroup per pair (maps: the cross caches)
 bool attn_pairs_pays(const AttnArgs &a, int sms);
 cudaError_t launch_attn_pairs(const AttnArgs &a, const void *kmap, const void *vmap, int sms, cudaStream_t s, bool pdl);
