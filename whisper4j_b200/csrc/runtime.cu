@@ -160,6 +160,12 @@ struct w4j_ctx {
     int last_steps = 0;
     long long last_launches = 0;
     cudaEvent_t ev0 = nullptr, ev1 = nullptr;
+    // host encoder outputs: two staging buffers, copied on their own stream, so that one stream's
+    // upload overlaps the previous stream's cross K/V projection
+    cudaStream_t copy_stream = nullptr;
+    cudaEvent_t xa_copied[2] = {nullptr, nullptr}, xa_used[2] = {nullptr, nullptr};
+    float *xa_stage2 = nullptr;
+    int xa_flip = 0;
     alignas(64) unsigned char e_tmap[128] = {};  // TMA map of the f16 token embedding
     alignas(64) unsigned char xk_tmap[128] = {}, xv_tmap[128] = {};  // cross K / V caches as [rows][64]
     alignas(64) unsigned char sk_tmap[128] = {}, sv_tmap[128] = {};  // self K / V caches as [rows][64]
@@ -244,6 +250,11 @@ static void free_all(w4j_ctx *c) {
     if (c->h_done) cudaFreeHost(c->h_done);
     if (c->ev0) cudaEventDestroy(c->ev0);
     if (c->ev1) cudaEventDestroy(c->ev1);
+    for (int i = 0; i < 2; ++i) {
+        if (c->xa_copied[i]) cudaEventDestroy(c->xa_copied[i]);
+        if (c->xa_used[i]) cudaEventDestroy(c->xa_used[i]);
+    }
+    if (c->copy_stream) cudaStreamDestroy(c->copy_stream);
     if (c->stream) cudaStreamDestroy(c->stream);
 }
 
@@ -405,6 +416,12 @@ extern "C" int w4j_ctx_create(const w4j_dims *dims, int device, int max_streams,
     if (cudaStreamCreateWithFlags(&c->stream, cudaStreamNonBlocking) != cudaSuccess) return fail(set_err(W4J_ERR_CUDA, "stream"));
     cudaEventCreate(&c->ev0);
     cudaEventCreate(&c->ev1);
+    if (cudaStreamCreateWithFlags(&c->copy_stream, cudaStreamNonBlocking) != cudaSuccess)
+        return fail(set_err(W4J_ERR_CUDA, "copy stream"));
+    for (int i = 0; i < 2; ++i)
+        if (cudaEventCreateWithFlags(&c->xa_copied[i], cudaEventDisableTiming) != cudaSuccess ||
+            cudaEventCreateWithFlags(&c->xa_used[i], cudaEventDisableTiming) != cudaSuccess)
+            return fail(set_err(W4J_ERR_CUDA, "events"));
     if ((rc = (int)gemv_prepare()) != 0 || (rc = (int)select_prepare()) != 0 || (rc = (int)logits_tc_prepare()) != 0 ||
         (rc = (int)attn_prepare()) != 0 || (rc = (int)gemm_tc_prepare()) != 0 || (rc = (int)xkv_tc_prepare()) != 0 ||
         (rc = (int)step_prepare()) != 0)
@@ -419,7 +436,8 @@ extern "C" int w4j_ctx_create(const w4j_dims *dims, int device, int max_streams,
                    make_tmap_f16_rows(c->xv_tmap, c->cv, (int)(cross / kHeadDim), kHeadDim);
     // activations
     if ((rc = dalloc(c, &c->x, MB * d)) || (rc = dalloc(c, &c->q, MB * d)) || (rc = dalloc(c, &c->attn, MB * d)) ||
-        (rc = dalloc(c, &c->h, MB * 4 * d)) || (rc = dalloc(c, &c->xa_stage, A * d)))
+        (rc = dalloc(c, &c->h, MB * 4 * d)) || (rc = dalloc(c, &c->xa_stage, A * d)) ||
+        (rc = dalloc(c, &c->xa_stage2, A * d)))
         return fail(rc);
     {
         const int rows = act_hilo_rows(c->Mbuf);
@@ -793,7 +811,7 @@ extern "C" int w4j_finalize(w4j_ctx *c) {
 // ---------------------------------------------------------------------------
 // cross K/V prefill
 // ---------------------------------------------------------------------------
-static int prefill(w4j_ctx *c, int slot, const float *xa_dev) {
+static int prefill(w4j_ctx *c, int slot, const float *xa_dev, bool sync = true) {
     for (int l = 0; l < c->L; ++l) {
         LayerDev &ly = c->layers[l];
         const size_t off = ((size_t)slot * c->L + l) * (size_t)c->H * c->A * kHeadDim;
@@ -807,7 +825,7 @@ static int prefill(w4j_ctx *c, int slot, const float *xa_dev) {
                                 c->stream);
         CUDA_TRY(e);
     }
-    CUDA_TRY(cudaStreamSynchronize(c->stream));
+    if (sync) CUDA_TRY(cudaStreamSynchronize(c->stream));
     c->has_xa[slot] = 1;
     c->cache_len[slot] = 0;
     return 0;
@@ -820,8 +838,21 @@ extern "C" int w4j_set_encoder_output(w4j_ctx *c, int slot, const float *xa, int
     TRY(check_ready(c));
     if (slot < 0 || slot >= c->max_streams) return set_err(W4J_ERR_ARG, "slot %d out of range", slot);
     if (n_audio_ctx != c->A) return set_err(W4J_ERR_ARG, "encoder output has %d frames, model expects %d", n_audio_ctx, c->A);
-    CUDA_TRY(cudaMemcpyAsync(c->xa_stage, xa, (size_t)c->A * c->d * 4, cudaMemcpyHostToDevice, c->stream));
-    return prefill(c, slot, c->xa_stage);
+    // the copy into the staging buffer the call before last used (its projection has read it: the
+    // copy stream waits for that), the host buffer free again when this call returns; the
+    // projection itself runs behind the next call's copy (the decode after it is ordered on the
+    // same stream)
+    const int b = c->xa_flip;
+    c->xa_flip ^= 1;
+    float *stage = b ? c->xa_stage2 : c->xa_stage;
+    CUDA_TRY(cudaStreamWaitEvent(c->copy_stream, c->xa_used[b], 0));
+    CUDA_TRY(cudaMemcpyAsync(stage, xa, (size_t)c->A * c->d * 4, cudaMemcpyHostToDevice, c->copy_stream));
+    CUDA_TRY(cudaEventRecord(c->xa_copied[b], c->copy_stream));
+    CUDA_TRY(cudaEventSynchronize(c->xa_copied[b]));
+    CUDA_TRY(cudaStreamWaitEvent(c->stream, c->xa_copied[b], 0));
+    TRY(prefill(c, slot, stage, false));
+    CUDA_TRY(cudaEventRecord(c->xa_used[b], c->stream));
+    return W4J_OK;
 }
 
 extern "C" int w4j_set_encoder_output_device(w4j_ctx *c, int slot, const float *xa, int n_audio_ctx) {
