@@ -158,3 +158,44 @@ def test_tiny_beam_2_times_8_streams_match_oracle(tiny8):
         if check_beam(r.tokens, w, ora, xas[s], p, [50256], 50256, 2, 8) == "equal":
             assert r.sum_logprob == pytest.approx(w["sum_logprob"], abs=2e-2)
         assert len(r.tokens) == 8
+
+
+# 129 .. 256 live rows: the vocabulary pass is one launch over two 128-row chunks of staged rows
+# (k_logits_big), one record per (row, 128-row embedding tile) merged by the select kernel.
+N_BIG = 136
+
+
+@pytest.fixture(scope="module")
+def wide136():
+    gm = parsed(SMALL, 103, "f16", SO)
+    xas = [encoder_output(700 + i, SMALL.n_audio_ctx, SMALL.n_text_state) for i in range(N_BIG)]
+    yield gm, O.OracleModel(gm), xas
+
+
+def _decode_all(gm, xas, env, monkeypatch):
+    for k, v in env.items():
+        monkeypatch.setenv(k, v)
+    with WhisperDecoder(gm, max_streams=N_BIG, max_beam=1) as d:
+        for i, xa in enumerate(xas):
+            d.set_encoder_output(xa, slot=i)
+        prompts = [[996, 997, 998, 10 + i % 900] for i in range(N_BIG)]
+        return prompts, d.decode_batch(list(range(N_BIG)), prompts, 995, 12, suppress_tokens=[995], no_speech_token=3)
+
+
+def test_greedy_136_streams_one_launch_vocabulary(wide136, monkeypatch):
+    gm, ora, xas = wide136
+    prompts, res = _decode_all(gm, xas, {}, monkeypatch)
+    for s in range(0, N_BIG, 9):  # a sample of the streams against the oracle
+        w = ora.decode(xas[s], prompts[s], 995, 12, suppress=[995], no_speech=3)
+        check_tokens(res[s].tokens, w["tokens"], ora, xas[s], prompts[s])
+        if res[s].tokens == w["tokens"]:
+            assert res[s].sum_logprob == pytest.approx(w["sum_logprob"], abs=2e-2 + 1e-3 * abs(w["sum_logprob"]))
+        assert res[s].no_speech_prob == pytest.approx(w["no_speech_prob"], rel=2e-2, abs=1e-6)
+    # the same decode with 32-row vocabulary launches (one record per block): same decisions
+    _, ref = _decode_all(gm, xas, {"W4J_LOGITS_CHUNKED": "1"}, monkeypatch)
+    same = [a.tokens == b.tokens for a, b in zip(res, ref)]
+    assert sum(same) >= 0.95 * N_BIG
+    for a, b, eq in zip(res, ref, same):
+        if eq:
+            assert a.sum_logprob == pytest.approx(b.sum_logprob, abs=1e-3)
+            assert a.no_speech_prob == pytest.approx(b.no_speech_prob, rel=1e-3, abs=1e-7)

@@ -823,15 +823,26 @@ cudaError_t launch_gemm_tc(const GemvArgs &a, const void *tmap, const void *bmap
 // rows: out[(z * 2 nu + r) * K + k] = hi, out[(z * 2 nu + nu + r) * K + k] = lo for sequence
 // m = z * mchunk + r (rows past the chunk's sequences zero; nu = the GEMM's row tile), after the input mode
 // (plain, LayerNorm of x, or token + positional embedding then LayerNorm, kept in x_out).
-// One warp per (chunk, row); LayerNorm as Tensor.java:592-619 (two-pass, eps 1e-5).
+// One warp per (chunk, row, segment of K): a LayerNorm row is one segment (Tensor.java:592-619,
+// two-pass, eps 1e-5); a plain row of more than 1280 values is cut into `parts` segments of at most
+// 1280, a multiple of 128, so every lane has all its loads of a segment in flight at once.
 // ---------------------------------------------------------------------------
-__global__ void __launch_bounds__(256) k_act_hilo(GemvArgs a, int mchunk, int chunks, int nu, __half *out) {
+static int act_hilo_parts(const GemvArgs &a) {
+    const int K = a.W.K;
+    if (a.in_mode != IN_ACT || K % 128 != 0 || K <= 1280) return 1;
+    int p = (K + 1279) / 1280;
+    while (K % (p * 128) != 0) ++p;
+    return p;
+}
+
+__global__ void __launch_bounds__(256) k_act_hilo(GemvArgs a, int mchunk, int chunks, int nu, int parts, __half *out) {
     const int K = a.W.K;
     const int gw = (int)((blockIdx.x * blockDim.x + threadIdx.x) >> 5), lane = threadIdx.x & 31;
     pdl_trigger();
     pdl_wait();
-    if (gw >= chunks * nu) return;
-    const int z = gw / nu, r = gw - z * nu, m = z * mchunk + r;
+    if (gw >= chunks * nu * parts) return;
+    const int row = gw / parts, part = gw - row * parts;
+    const int z = row / nu, r = row - z * nu, m = z * mchunk + r;
     __half *hi = out + ((size_t)z * 2 * nu + r) * K, *lo = hi + (size_t)nu * K;
     const bool live = r < mchunk && m < a.M;
     auto put = [&](int k, float4 v) {
@@ -843,17 +854,28 @@ __global__ void __launch_bounds__(256) k_act_hilo(GemvArgs a, int mchunk, int ch
         *reinterpret_cast<uint2 *>(lo + k) =
             make_uint2(*reinterpret_cast<const uint32_t *>(&l0), *reinterpret_cast<const uint32_t *>(&l1));
     };
+    const int seg = K / parts, k0 = part * seg;
     if (!live) {
-        for (int k = 4 * lane; k < K; k += 128) put(k, make_float4(0.f, 0.f, 0.f, 0.f));
+        for (int k = k0 + 4 * lane; k < k0 + seg; k += 128) put(k, make_float4(0.f, 0.f, 0.f, 0.f));
         return;
     }
+    constexpr int kLnF4 = 10;
     if (a.in_mode == IN_ACT) {
-        const float4 *src = reinterpret_cast<const float4 *>(a.act + (size_t)m * K);
-        for (int c = lane; c < K / 4; c += 32) put(4 * c, src[c]);
+        const float4 *src = reinterpret_cast<const float4 *>(a.act + (size_t)m * K + k0);
+        if (seg % 128 == 0 && seg <= 128 * kLnF4) {  // every load of the lane issued before any store
+            const int nf = seg / 128;
+            float4 v[kLnF4];
+#pragma unroll
+            for (int j = 0; j < kLnF4; ++j) v[j] = j < nf ? src[lane + 32 * j] : make_float4(0.f, 0.f, 0.f, 0.f);
+#pragma unroll
+            for (int j = 0; j < kLnF4; ++j)
+                if (j < nf) put(k0 + 4 * (lane + 32 * j), v[j]);
+        } else {
+            for (int c = lane; c < seg / 4; c += 32) put(k0 + 4 * c, src[c]);
+        }
         return;
     }
     // LayerNorm inputs: K <= 1280, a multiple of 128 (the row in registers)
-    constexpr int kLnF4 = 10;
     const int nf4 = K / 128;
     float4 v[kLnF4];
     if (a.in_mode == IN_LN) {
@@ -913,8 +935,9 @@ cudaError_t launch_act_hilo(const GemvArgs &a, __half *out, cudaStream_t s, bool
     const int K = a.W.K;
     if (K % 4 != 0 || (a.in_mode != IN_ACT && (K % 128 != 0 || K > 1280))) return cudaErrorNotSupported;
     const int chunks = (a.M + 127) / 128, mchunk = (a.M + chunks - 1) / chunks, nu = nu_for(mchunk);
+    const int parts = act_hilo_parts(a);
     cudaLaunchConfig_t cfg = {};
-    cfg.gridDim = dim3((unsigned)(chunks * nu * 32 + 255) / 256);
+    cfg.gridDim = dim3((unsigned)(chunks * nu * parts * 32 + 255) / 256);
     cfg.blockDim = dim3(256);
     cfg.stream = s;
     cudaLaunchAttribute attr[1];
@@ -922,7 +945,7 @@ cudaError_t launch_act_hilo(const GemvArgs &a, __half *out, cudaStream_t s, bool
     attr[0].val.programmaticStreamSerializationAllowed = 1;
     cfg.attrs = attr;
     cfg.numAttrs = pdl ? 1 : 0;
-    return cudaLaunchKernelEx(&cfg, k_act_hilo, a, mchunk, chunks, nu, out);
+    return cudaLaunchKernelEx(&cfg, k_act_hilo, a, mchunk, chunks, nu, parts, out);
 }
 
 }  // namespace w4j

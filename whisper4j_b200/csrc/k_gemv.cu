@@ -394,6 +394,7 @@ __global__ void __launch_bounds__(gemv_threads(WT)) k_gemv(GemvArgs a, GemvLaunc
         const unsigned char *src = WT == WT_F16 ? reinterpret_cast<const unsigned char *>(a.W.h + (size_t)r0 * K)
                                                 : reinterpret_cast<const unsigned char *>(a.W.q + (size_t)r0 * K);
         for (unsigned off = 0; off < bytes; off += 65536u) bulk_g2s(w_s + off, src + off, min(65536u, bytes - off), bar);
+        l2_ahead(a.pf, blockIdx.x, gridDim.x);
     }
     if (WT == WT_Q8)
         for (int i = tid; i < nr * (K / 32); i += NT) sc_s[i] = a.W.s[(size_t)r0 * (K / 32) + i];

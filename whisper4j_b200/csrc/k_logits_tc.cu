@@ -28,6 +28,18 @@ namespace w4j {
 // sixteen build the B operand (one LayerNorm row per warp at a time) and run the row epilogue.
 constexpr int kLogitsThreads = 512;
 
+struct LogitsBigLaunch {
+    int tiles_total;  // ceil(V / 128): embedding tiles, also the records per row
+    int chunks;       // chunks of rows (grid-independent: every block walks them all)
+    int mchunk;       // rows per chunk
+    int n_stages;
+    unsigned tile_off, mk_off, bar_off;  // shared-memory layout (bytes)
+};
+
+__device__ __forceinline__ void named_bar_sync(int id, int threads) {
+    asm volatile("bar.sync %0, %1;" ::"r"(id), "r"(threads) : "memory");
+}
+
 struct LogitsTcLaunch {
     int tiles_total;  // ceil(V / 128)
     int ch;           // max rows of a block (tiles per block * 128)
@@ -258,6 +270,200 @@ __global__ void __launch_bounds__(kLogitsThreads, 1) k_logits_tc(LogitsArgs a, c
 }
 
 // ---------------------------------------------------------------------------
+// k_logits_big: the same vocabulary pass for 33 .. 256 rows in one launch, reading the embedding
+// once.  The rows come LayerNorm-ed and rounded to f16 from the staged activation buffer (k_act_hilo's
+// hi rows, K = d: the f16(LN(x)) that k_logits_tc builds in shared memory) and stream beside the
+// embedding: a stage is a [128 x 64] embedding tile and the [NU x 64] tile of the rows.  Work items
+// are (embedding tile, chunk of <= 128 rows) pairs, tile-major, so the second chunk of a tile finds
+// the tile's bytes in L2.  Each item's logits go through the same row epilogue, one record per
+// (row, embedding tile): P = ceil(V / 128) records per row for the greedy / sampling select.
+// Warps: 0 produces, 1 issues the MMAs, 4-7 move accumulators out of TMEM, 2-15 run the epilogue.
+// ---------------------------------------------------------------------------
+template <int NU>
+__global__ void __launch_bounds__(kLogitsThreads, 1)
+    k_logits_big(LogitsArgs a, const __grid_constant__ CUtensorMap tmap, const __grid_constant__ CUtensorMap bmap,
+                 LogitsBigLaunch L) {
+    extern __shared__ __align__(1024) unsigned char smem_raw[];
+    unsigned char *smem = smem_raw + ((1024u - (smem_u32(smem_raw) & 1023u)) & 1023u);
+    constexpr unsigned kB = NU * 128, kSt = kStageBytes + kB;  // stage: embedding tile, then row tile
+    constexpr uint32_t kCols = 2 * NU;                         // two accumulators
+    constexpr int kEpiWarp0 = 2, kEpiWarps = kLogitsThreads / 32 - kEpiWarp0;
+    const int P = gridDim.x;
+    const int t0 = (int)(((long long)blockIdx.x * L.tiles_total) / P);
+    const int t1 = (int)(((long long)(blockIdx.x + 1) * L.tiles_total) / P);
+    const int d = a.d, KB = d / kKB, NS = L.n_stages, CH = L.chunks;
+    const int items = (t1 - t0) * CH, total = items * KB;
+    unsigned char *ring = smem;
+    float *tile = reinterpret_cast<float *>(smem + L.tile_off);  // [NU][128]
+    int2 *mk_rg = reinterpret_cast<int2 *>(smem + L.mk_off);
+    int *mk_act = reinterpret_cast<int *>(mk_rg + (size_t)a.M * kMaxRanges);
+    int *mk_nr = mk_act + a.M, *mk_cnt = mk_nr + a.M;
+    int *mk_dyn = mk_cnt + a.M;
+    int *mk_stat = mk_dyn + (size_t)a.M * kDynStage;
+    uint64_t *full = reinterpret_cast<uint64_t *>(smem + L.bar_off);
+    uint64_t *empty = full + NS;
+    uint64_t *accf = empty + NS;  // [2]
+    uint64_t *acce = accf + 2;    // [2]
+    uint32_t *tslot = reinterpret_cast<uint32_t *>(acce + 2);
+    volatile int *fail = reinterpret_cast<volatile int *>(tslot + 1);
+    volatile int *issued = fail + 1;
+    const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+    auto a_coords = [&](int i, int &x, int &y) {  // stage i: item i / KB (tile-major), k-block i % KB
+        x = (i % KB) * kKB;
+        y = (t0 + (i / KB) / CH) * kTileRows;
+    };
+    auto b_coords = [&](int i, int &x, int &y) {
+        x = (i % KB) * kKB;
+        y = ((i / KB) % CH) * 2 * NU;  // the chunk's hi rows in the staged buffer
+    };
+
+    // ---- independent of the previous kernel: barriers, TMEM, the first embedding tiles, masks ----
+    const int first = a.withhold ? 0 : (NS < total ? NS : total);
+    if (tid == 0) {
+        for (int i = 0; i < NS; ++i) {
+            mbar_init(full + i, 1);
+            mbar_init(empty + i, 1);
+        }
+        mbar_init(accf + 0, 1);
+        mbar_init(accf + 1, 1);
+        mbar_init(acce + 0, 1);
+        mbar_init(acce + 1, 1);
+        *fail = 0;
+        fence_mbar_init();
+        for (int i = 0; i < first; ++i) {
+            int x, y;
+            a_coords(i, x, y);
+            mbar_expect_tx(full + i, kSt);  // the row tile follows after the wait
+            tma_load_2d(ring + (size_t)i * kSt, &tmap, x, y, full + i);
+        }
+        *issued = first;
+    }
+    if (warp == 1) {
+        tmem_alloc(tslot, kCols);
+        tmem_relinquish();
+    }
+    if (a.active)
+        for (int i = tid; i < a.M; i += blockDim.x) mk_act[i] = a.active[i];
+    if (a.use_mask) {
+        const MaskArgs &mk = a.mask;
+        for (int i = tid; i < a.M; i += blockDim.x) {
+            mk_nr[i] = mk.n_ranges[i];
+            mk_cnt[i] = mk.dyn_count[i];
+        }
+        for (int i = tid; i < a.M * kMaxRanges; i += blockDim.x) mk_rg[i] = mk.ranges[i];
+        for (int i = tid; i < min(mk.n_static, kStatStage); i += blockDim.x) mk_stat[i] = mk.static_list[i];
+        __syncthreads();
+        for (int i = tid; i < a.M * kDynStage; i += blockDim.x) {
+            const int m = i / kDynStage, j = i - m * kDynStage;
+            if (j < mk_cnt[m]) mk_dyn[i] = mk.dyn_list[(size_t)m * mk.dyn_stride + j];
+        }
+    }
+    pdl_trigger();
+    pdl_wait();
+    tc_fence_before();
+    __syncthreads();
+    tc_fence_after();
+    const uint32_t taddr = *tslot;
+
+    if (warp == 0 && lane == 0) {
+        // ---- producer: the row tiles of the first stages, then whole stages as they free up ----
+        for (int i = 0; i < first; ++i) {
+            int x, y;
+            b_coords(i, x, y);
+            tma_load_2d(ring + (size_t)i * kSt + kStageBytes, &bmap, x, y, full + i);
+        }
+        for (int i = NS; i < total && !*fail && !a.withhold; ++i) {
+            const int st = i % NS, use = i / NS;
+            if (!mbar_wait(empty + st, (unsigned)((use - 1) & 1), a.err)) {
+                *fail = 1;
+                break;
+            }
+            int x, y;
+            mbar_expect_tx(full + st, kSt);
+            a_coords(i, x, y);
+            tma_load_2d(ring + (size_t)st * kSt, &tmap, x, y, full + st);
+            b_coords(i, x, y);
+            tma_load_2d(ring + (size_t)st * kSt + kStageBytes, &bmap, x, y, full + st);
+            *issued = i + 1;
+        }
+    } else if (warp == 1 && lane == 0) {
+        // ---- MMA issuer: item it accumulates into buffer it & 1 ----
+        const uint32_t ring_a = smem_u32(ring);
+        const uint32_t idesc = idesc_f16(kTileRows, NU);
+        for (int it = 0; it < items && !*fail; ++it) {
+            const int b = it & 1;
+            if (it >= 2 && !mbar_wait(acce + b, (unsigned)(((it - 2) >> 1) & 1), a.err)) {
+                *fail = 1;
+                break;
+            }
+            tc_fence_after();
+            for (int kb = 0; kb < KB; ++kb) {
+                const int i = it * KB + kb, st = i % NS;
+                if (!mbar_wait(full + st, (unsigned)((i / NS) & 1), a.err)) {
+                    *fail = 1;
+                    break;
+                }
+                tc_fence_after();
+#pragma unroll
+                for (int j = 0; j < kKB / 16; ++j) {
+                    const uint64_t ad = sw128_desc(ring_a + (uint32_t)st * kSt + j * 32);
+                    const uint64_t bd = sw128_desc(ring_a + (uint32_t)st * kSt + kStageBytes + j * 32);
+                    umma_f16(taddr + (uint32_t)(b * NU), ad, bd, idesc, (kb | j) != 0);
+                }
+                umma_commit(empty + st);
+            }
+            if (*fail) break;
+            umma_commit(accf + b);
+        }
+    } else if (warp >= kEpiWarp0) {
+        // ---- epilogue: TMEM -> [rows][128] logits tile -> row epilogue, one item at a time.  Every
+        // epilogue thread passes the same three barriers per item, failed or not. ----
+        const MaskStage ms{mk_act, mk_nr, mk_rg, mk_cnt, mk_dyn, mk_stat};
+        const int etid = tid - kEpiWarp0 * 32, ecount = kEpiWarps * 32;
+        for (int it = 0; it < items; ++it) {
+            const int b = it & 1, lt = it / CH, z = it % CH;
+            if (!*fail && !mbar_wait(accf + b, (unsigned)((it >> 1) & 1), a.err)) *fail = 1;
+            tc_fence_after();
+            named_bar_sync(1, ecount);
+            const bool go = !*fail;
+            const int lo = (t0 + lt) * kTileRows, hi = min(a.V, lo + kTileRows), n = hi - lo;
+            const int m0 = z * L.mchunk, mt = min(L.mchunk, a.M - m0);
+            if (go && warp >= 4 && warp < 8) {
+                const int q = warp - 4, row = q * 32 + lane;
+#pragma unroll
+                for (int c0 = 0; c0 < NU; c0 += 16) {
+                    float v[16];
+                    tmem_ld16(taddr + ((uint32_t)(q * 32) << 16) + (uint32_t)(b * NU + c0), v);
+                    if (row < n)
+#pragma unroll
+                        for (int e = 0; e < 16; ++e)
+                            if (c0 + e < mt) tile[(size_t)(c0 + e) * kTileRows + row] = v[e];
+                }
+            }
+            tc_fence_before();
+            named_bar_sync(1, ecount);
+            if (etid == 0) mbar_arrive(acce + b);  // the accumulator may be overwritten
+            if (go && a.raw_out)
+                for (int i = etid; i < mt * n; i += ecount) {
+                    const int mm = i / n, r = i - mm * n;
+                    a.raw_out[(size_t)(m0 + mm) * a.V + lo + r] = tile[(size_t)mm * kTileRows + r];
+                }
+            if (a.raw_out) named_bar_sync(1, ecount);
+            if (go)
+                logits_rows_epilogue(a, tile, kTileRows, mt, m0, lo, hi, true, &ms, L.tiles_total, t0 + lt, kEpiWarp0,
+                                     kEpiWarps);
+            named_bar_sync(1, ecount);
+        }
+    }
+    __syncthreads();
+    if (*fail && tid == 0) drain_ring(full, NS, *issued);
+    if (warp == 1) {
+        tc_fence_after();
+        tmem_dealloc(taddr, kCols);
+    }
+}
+
+// ---------------------------------------------------------------------------
 // host side
 // ---------------------------------------------------------------------------
 static PFN_cuTensorMapEncodeTiled_v12000 encode_fn() {
@@ -357,7 +563,62 @@ static cudaError_t launch_tc_t(const LogitsArgs &a, const CUtensorMap &map, cons
 cudaError_t logits_tc_prepare() {
     cudaError_t e = allow_dynamic_smem(k_logits_tc<16>);
     if (e == cudaSuccess) e = allow_dynamic_smem(k_logits_tc<32>);
+    if (e == cudaSuccess) e = allow_dynamic_smem(k_logits_big<64>);
+    if (e == cudaSuccess) e = allow_dynamic_smem(k_logits_big<128>);
     return e;
+}
+
+// The one-launch pass over M rows (33 .. 256, greedy / sampling: no per-block top-k) in chunks
+// of the staged activation buffer's layout: ceil(M / 128) chunks of mchunk rows, NU = 64 or 128.
+static bool plan_big(int M, int V, int d, int topk, int &nu, LogitsBigLaunch &L) {
+    if (M <= 32 || M > kLogitsBigMaxRows || topk != 0 || d % 128 != 0 || d > 1280) return false;
+    L.chunks = (M + 127) / 128;
+    L.mchunk = (M + L.chunks - 1) / L.chunks;
+    nu = L.mchunk <= 64 ? 64 : 128;
+    L.tiles_total = (V + kTileRows - 1) / kTileRows;
+    const size_t st = (size_t)kStageBytes + (size_t)nu * 128;
+    const size_t tbytes = (size_t)nu * kTileRows * 4;
+    const size_t mkbytes = mask_stage_bytes(M);
+    const size_t fixed = tbytes + mkbytes + 256;
+    const size_t budget = 220 * 1024;
+    if (fixed + 2 * st > budget) return false;
+    int ns = (int)((budget - fixed) / st);
+    L.n_stages = ns > 6 ? 6 : ns;
+    L.tile_off = (unsigned)(L.n_stages * st);  // 1024-byte multiple
+    L.mk_off = L.tile_off + (unsigned)tbytes;
+    L.bar_off = L.mk_off + (unsigned)mkbytes;
+    return true;
+}
+
+int logits_big_box_rows(int M) {
+    const int chunks = (M + 127) / 128, mchunk = (M + chunks - 1) / chunks;
+    return mchunk <= 64 ? 64 : 128;
+}
+
+int logits_big_parts(int M, int V, int d, int topk) {
+    int nu;
+    LogitsBigLaunch L;
+    return plan_big(M, V, d, topk, nu, L) ? L.tiles_total : 0;
+}
+
+cudaError_t launch_logits_big(const LogitsArgs &a, const void *tmap, const void *bmap, int blocks, cudaStream_t s, bool pdl) {
+    int nu;
+    LogitsBigLaunch L;
+    if (!tmap || !bmap || a.E.type != WT_F16 || !plan_big(a.M, a.V, a.d, a.topk, nu, L)) return cudaErrorNotSupported;
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = dim3(blocks);
+    cfg.blockDim = dim3(kLogitsThreads);
+    cfg.dynamicSmemBytes = (size_t)L.bar_off + (2 * L.n_stages + 4) * 8 + 16 + 1024;
+    cfg.stream = s;
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[0].val.programmaticStreamSerializationAllowed = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = pdl ? 1 : 0;
+    const CUtensorMap &map = *reinterpret_cast<const CUtensorMap *>(tmap);
+    const CUtensorMap &bm = *reinterpret_cast<const CUtensorMap *>(bmap);
+    if (nu == 64) return cudaLaunchKernelEx(&cfg, k_logits_big<64>, a, map, bm, L);
+    return cudaLaunchKernelEx(&cfg, k_logits_big<128>, a, map, bm, L);
 }
 
 // Returns cudaErrorNotSupported when the shape is outside the tensor-core kernel's range.

@@ -908,7 +908,9 @@ cudaError_t launch_select(const DecodeState &st, int mode, int parity, const flo
     cudaLaunchAttribute attr[1];
     cudaLaunchConfig_t cfg = cfg_for(dim3(st.n_streams), dim3(kSelThreads), s, pdl, attr);
     cfg.dynamicSmemBytes = select_smem(st, mode, n_parts);
-    if (cfg.dynamicSmemBytes > 227 * 1024 || n_parts > 256 || st.beam > kMaxBeam) return cudaErrorInvalidValue;
+    // the beam merge keeps at most 256 records' heads in registers (merge_topk); greedy takes any count
+    const bool beam = mode == SEL_BEAM_INIT || mode == SEL_BEAM;
+    if (cfg.dynamicSmemBytes > 227 * 1024 || (beam && n_parts > 256) || st.beam > kMaxBeam) return cudaErrorInvalidValue;
     switch (mode) {
         case SEL_GREEDY:
         case SEL_SAMPLE:

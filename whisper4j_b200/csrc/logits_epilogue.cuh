@@ -27,13 +27,21 @@ __device__ __forceinline__ bool logit_better(float v1, int i1, float v2, int i2)
 // Logit processors and block reductions over the logits of rows [lo, hi) held in shared
 // memory (tile[mm][row - lo], stride ch) for sequences m0 .. m0+MT: unmasked statistics for
 // the no-speech probability, the masks (suppress list, n-gram and timestamp rules), then max,
-// first argmax, sum of exp and the block's top-k candidates.  One warp per sequence.
+// first argmax, sum of exp and the block's top-k candidates.  One warp per sequence: warps
+// w0 .. w0 + nw of the block (nw = 0: all).  The records of row m are part[m][P][..] (P = 0: one
+// per block, this block's at blockIdx.x; else record `slot`).
 __device__ __forceinline__ void logits_rows_epilogue(const LogitsArgs &a, float *tile, int ch, int MT, int m0, int lo, int hi,
-                                     bool ok, const MaskStage *ms = nullptr) {
-    const int P = gridDim.x;
+                                     bool ok, const MaskStage *ms = nullptr, int P = 0, int slot = 0, int w0 = 0,
+                                     int nw = 0) {
+    if (P == 0) {
+        P = gridDim.x;
+        slot = blockIdx.x;
+    }
+    if (nw == 0) nw = blockDim.x / 32;
     const int nrows = hi - lo;
-    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-for (int mm = warp; mm < MT; mm += blockDim.x / 32) {
+    const int warp = (threadIdx.x >> 5) - w0, lane = threadIdx.x & 31;
+    if (warp < 0) return;
+for (int mm = warp; mm < MT; mm += nw) {
         const int m = m0 + mm;
         if (m >= a.M || !ok) continue;
         if (a.active && !(ms ? ms->active[m] : a.active[m])) continue;
@@ -47,7 +55,7 @@ for (int mm = warp; mm < MT; mm += blockDim.x / 32) {
             for (int i = lane; i < n; i += 32) sm += (mx == -INFINITY) ? 0.f : __expf(row[i] - mx);
             sm = warp_sum(sm);
             if (lane == 0) {
-                float *np = a.ns_part + ((size_t)m * P + blockIdx.x) * 2;
+                float *np = a.ns_part + ((size_t)m * P + slot) * 2;
                 np[0] = mx;
                 np[1] = sm;
             }
@@ -89,7 +97,7 @@ for (int mm = warp; mm < MT; mm += blockDim.x / 32) {
         if (a.masked_out)
             for (int i = lane; i < n; i += 32) a.masked_out[(size_t)m * a.V + lo + i] = row[i];
         const int K = a.topk;
-        float *pp = a.part + ((size_t)m * P + blockIdx.x) * kPartStride;
+        float *pp = a.part + ((size_t)m * P + slot) * kPartStride;
         if (n <= 32 * kRowRegs) {
             // the row in registers (lane + 32 j: ids ascending in j), then every reduction there
             float v[kRowRegs];

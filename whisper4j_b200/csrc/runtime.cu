@@ -171,6 +171,8 @@ struct w4j_ctx {
     alignas(64) unsigned char sk_tmap[128] = {}, sv_tmap[128] = {};  // self K / V caches as [rows][64]
     alignas(64) unsigned char sk_tmap32[128] = {}, sv_tmap32[128] = {};  // the same, 32-row boxes
     bool self_warps = true;  // W4J_SELF_PAIRS=1: many-sequence self-attention on k_attn_pairs instead
+    bool big_logits = true;  // W4J_LOGITS_CHUNKED=1: 33 .. 256 rows in 32-row launches instead of one
+    int l2_ahead = 0;        // W4J_L2_AHEAD=n: a GEMV projection pulls the weights n projections on into L2 (0: off)
     bool s_tmap_ok = false;
     bool x_tmap_ok = false;
     bool e_tmap_ok = false;
@@ -399,6 +401,8 @@ extern "C" int w4j_ctx_create(const w4j_dims *dims, int device, int max_streams,
     if (const char *ev = getenv("W4J_NO_ATTN_PAIRS")) c->attn_pairs = ev[0] == '0';
     if (const char *ev = getenv("W4J_STEP_BAR")) c->step_bar_mode = ev[0] == '1';
     if (const char *ev = getenv("W4J_SELF_PAIRS")) c->self_warps = ev[0] != '1';
+    if (const char *ev = getenv("W4J_LOGITS_CHUNKED")) c->big_logits = ev[0] != '1';
+    if (const char *ev = getenv("W4J_L2_AHEAD")) c->l2_ahead = (int)strtol(ev, nullptr, 10);
     if (const char *ev = getenv("W4J_STEP_INFLIGHT_KB")) {
         const long kb = strtol(ev, nullptr, 10);
         if (kb >= 16 && kb <= 128) c->step_inflight = (unsigned)kb << 10;
@@ -445,8 +449,10 @@ extern "C" int w4j_ctx_create(const w4j_dims *dims, int device, int max_streams,
         c->hilo_ok = c->hilo != nullptr;  // its tensor maps are made per launch (box height by row count)
     }
     c->n_parts = logits_parts_for(c->V, c->sm_count);
-    if ((rc = dalloc(c, &c->logit_part, MB * c->n_parts * kPartStride)) ||
-        (rc = dalloc(c, &c->ns_part, MB * c->n_parts * 2)) || (rc = dalloc(c, &c->ns_value, MB)) ||
+    // records per row: one per block, or one per 128-row embedding tile (the one-launch pass)
+    const size_t parts_max = std::max(c->n_parts, (c->V + 127) / 128);
+    if ((rc = dalloc(c, &c->logit_part, MB * parts_max * kPartStride)) ||
+        (rc = dalloc(c, &c->ns_part, MB * parts_max * 2)) || (rc = dalloc(c, &c->ns_value, MB)) ||
         (rc = dalloc(c, &c->masked, M * V)) || (rc = dalloc(c, &c->raw, C * V)) || (rc = dalloc(c, &c->op_err, 1)))
         return fail(rc);
     // GELU table
@@ -1112,7 +1118,6 @@ struct PassArgs {
     const int2 *mask;         // [M] masked self-attention keys [lo, hi), or null
 };
 
-// One projection: the tcgen05 kernel from 16 rows on (f16 weights), else the GEMV.
 // One projection: the tcgen05 kernel from 16 rows on (past 128 rows of f16 weights after staging the
 // activations as f16 hi / lo rows), else the GEMV.
 static cudaError_t run_proj(w4j_ctx *c, const GemvArgs &g, const LayerDev &ly, Proj p, bool pdl, long long &launches) {
@@ -1138,6 +1143,40 @@ static cudaError_t run_proj(w4j_ctx *c, const GemvArgs &g, const LayerDev &ly, P
     if (e == cudaErrorNotSupported) e = launch_gemv(g, c->stream, pdl);
     ++launches;
     return e != cudaSuccess ? e : tmark(c, KC_PROJ, false);
+}
+
+static const DMat &proj_mat(const LayerDev &ly, int p) {
+    switch (p) {
+        case PROJ_QKV: return ly.qkv;
+        case PROJ_O: return ly.o;
+        case PROJ_XQ: return ly.xq;
+        case PROJ_XO: return ly.xo;
+        case PROJ_M0: return ly.m0;
+        default: return ly.m2;
+    }
+}
+
+// What projection p of layer l pulls into L2 for later kernels of the step: the weights of the
+// projection c->l2_ahead places further along the chain (wrapping to the next step's first
+// layer), and with the cross query's weights, for a pass over one stream, that layer's cross K / V.
+static L2Ahead l2_ahead_for(const w4j_ctx *c, const PassArgs &pa, int l, int p) {
+    L2Ahead f;
+    if (c->l2_ahead <= 0 || pa.M >= 16) return f;
+    const int n = 6 * c->L, t = (6 * l + p + c->l2_ahead) % n;
+    const int tl = t / 6, tp = t % 6;
+    const DMat &m = proj_mat(c->layers[tl], tp);
+    f.w = m.type == WT_F16 ? reinterpret_cast<const unsigned char *>(m.h) : reinterpret_cast<const unsigned char *>(m.q);
+    f.w_bytes = (size_t)m.N * m.K * (m.type == WT_F16 ? 2 : 1);
+    if (tp == PROJ_XQ && pa.groups == 1 && c->ck && c->cv) {
+        const size_t layer_elems = (size_t)c->H * c->A * kHeadDim;
+        f.k = reinterpret_cast<const unsigned char *>(c->ck + (size_t)tl * layer_elems);
+        f.v = reinterpret_cast<const unsigned char *>(c->cv + (size_t)tl * layer_elems);
+        f.kv_bytes = layer_elems * 2;
+        f.kv_stride = (size_t)c->L * layer_elems * 2;
+        f.stream = pa.cross_stream;
+        f.n_streams = c->max_streams;
+    }
+    return f;
 }
 
 static int run_layers(w4j_ctx *c, const PassArgs &pa, long long &launches) {
@@ -1173,6 +1212,7 @@ static int run_layers(w4j_ctx *c, const PassArgs &pa, long long &launches) {
         g.n_ctx = c->cap;
         g.active = pa.active;
         g.err = c->st.err;
+        g.pf = l2_ahead_for(c, pa, l, PROJ_QKV);
         CUDA_TRY(run_proj(c, g, ly, PROJ_QKV, pdl, launches));
 
         AttnArgs sa;
@@ -1214,6 +1254,7 @@ static int run_layers(w4j_ctx *c, const PassArgs &pa, long long &launches) {
         go.y = c->x;
         go.active = pa.active;
         go.err = c->st.err;
+        go.pf = l2_ahead_for(c, pa, l, PROJ_O);
         CUDA_TRY(run_proj(c, go, ly, PROJ_O, pdl, launches));
 
         GemvArgs gq;
@@ -1227,6 +1268,7 @@ static int run_layers(w4j_ctx *c, const PassArgs &pa, long long &launches) {
         gq.out_mode = OUT_STORE;
         gq.y = c->q;
         gq.err = c->st.err;
+        gq.pf = l2_ahead_for(c, pa, l, PROJ_XQ);
         CUDA_TRY(run_proj(c, gq, ly, PROJ_XQ, pdl, launches));
 
         AttnArgs ca;
@@ -1264,6 +1306,7 @@ static int run_layers(w4j_ctx *c, const PassArgs &pa, long long &launches) {
         gxo.y = c->x;
         gxo.active = pa.active;
         gxo.err = c->st.err;
+        gxo.pf = l2_ahead_for(c, pa, l, PROJ_XO);
         CUDA_TRY(run_proj(c, gxo, ly, PROJ_XO, pdl, launches));
 
         GemvArgs g1;
@@ -1278,6 +1321,7 @@ static int run_layers(w4j_ctx *c, const PassArgs &pa, long long &launches) {
         g1.y = c->h;
         g1.gelu_lut = c->gelu_lut;
         g1.err = c->st.err;
+        g1.pf = l2_ahead_for(c, pa, l, PROJ_M0);
         CUDA_TRY(run_proj(c, g1, ly, PROJ_M0, pdl, launches));
 
         GemvArgs g2;
@@ -1290,6 +1334,7 @@ static int run_layers(w4j_ctx *c, const PassArgs &pa, long long &launches) {
         g2.y = c->x;
         g2.active = pa.active;
         g2.err = c->st.err;
+        g2.pf = l2_ahead_for(c, pa, l, PROJ_M2);
         CUDA_TRY(run_proj(c, g2, ly, PROJ_M2, pdl, launches));
         launches += 2;  // the two attentions
     }
@@ -1331,8 +1376,21 @@ static LogitsArgs logits_rows(const LogitsArgs &la, int m0, int n, int n_parts) 
     return r;
 }
 
-// The vocabulary pass: the tcgen05 kernel when the embedding is f16 (one launch per 32 rows),
-// else the SIMT one.  Returns the launches enqueued in `launches`.
+// The vocabulary pass over la.M rows takes the one-launch tcgen05 kernel (33 .. 256 rows, no beam
+// top-k, the rows staged as f16 through the activation buffer) when the embedding is f16.
+static bool logits_big(const w4j_ctx *c, const LogitsArgs &la) {
+    return c->e_tmap_ok && c->hilo_ok && c->big_logits && la.M <= c->Mbuf &&
+           logits_big_parts(la.M, la.V, la.d, la.topk) > 0;
+}
+
+// Records per row that the vocabulary pass for la writes (what the select kernels merge).
+static int logit_parts(const w4j_ctx *c, const LogitsArgs &la) {
+    return logits_big(c, la) ? logits_big_parts(la.M, la.V, la.d, la.topk) : c->n_parts;
+}
+
+// The vocabulary pass: the one-launch tcgen05 kernel for 33 .. 256 rows (after staging the rows), the
+// 32-row tcgen05 kernel (one launch per 32 rows) otherwise when the embedding is f16, else the SIMT
+// one.  Returns the launches enqueued in `launches`.
 static cudaError_t run_logits_untimed(w4j_ctx *c, const LogitsArgs &la, bool pdl, long long &launches);
 static cudaError_t run_logits(w4j_ctx *c, const LogitsArgs &la, bool pdl, long long &launches) {
     cudaError_t e = tmark(c, KC_LOGITS, true);
@@ -1340,6 +1398,26 @@ static cudaError_t run_logits(w4j_ctx *c, const LogitsArgs &la, bool pdl, long l
     return e != cudaSuccess ? e : tmark(c, KC_LOGITS, false);
 }
 static cudaError_t run_logits_untimed(w4j_ctx *c, const LogitsArgs &la, bool pdl, long long &launches) {
+    if (logits_big(c, la)) {
+        // the final LayerNorm of the rows, as f16 hi (and lo) rows of the staged buffer
+        GemvArgs g;
+        g.W.type = WT_F16;
+        g.W.N = la.V;
+        g.W.K = la.d;
+        g.M = la.M;
+        g.in_mode = IN_LN;
+        g.act = la.x;
+        g.ln_g = la.ln_g;
+        g.ln_b = la.ln_b;
+        alignas(64) unsigned char bm[128];
+        if (!make_tmap_f16_box(bm, c->hilo, act_hilo_rows(c->Mbuf), la.d, logits_big_box_rows(la.M)))
+            return cudaErrorInvalidValue;
+        cudaError_t e = launch_act_hilo(g, c->hilo, c->stream, pdl);
+        if (e != cudaSuccess) return e;
+        e = launch_logits_big(la, c->e_tmap, bm, c->n_parts, c->stream, pdl);
+        launches += 2;
+        return e;
+    }
     if (c->e_tmap_ok) {
         const int chunks = (la.M + 31) / 32;
         cudaError_t e = cudaSuccess;
@@ -1598,13 +1676,14 @@ static int run_prompt(w4j_ctx *c, const CallArgs &a, const CallLayout &Ly, int m
             la.ns_value = c->ns_value;
         }
         CUDA_TRY(run_logits(c, la, !last, launches));
+        const int P = logit_parts(c, la);
         if (ns_here) {
-            CUDA_TRY(launch_nsp(st, c->ns_part, c->n_parts, c->ns_value, c->stream, true));
+            CUDA_TRY(launch_nsp(st, c->ns_part, P, c->ns_value, c->stream, true));
             ++launches;
         }
         if (last) {
             const int sel = mode == MODE_BEAM ? SEL_BEAM_INIT : mode == MODE_SAMPLE ? SEL_SAMPLE : SEL_GREEDY;
-            CUDA_TRY(launch_select(st, sel, 0, c->logit_part, c->n_parts, c->masked, 0, c->stream, true));
+            CUDA_TRY(launch_select(st, sel, 0, c->logit_part, P, c->masked, 0, c->stream, true));
             ++launches;
         }
     }
@@ -1789,7 +1868,8 @@ static int enqueue_step(w4j_ctx *c, const CallArgs &a, const CallLayout &Ly, int
     }
     const int sel = mode == MODE_BEAM ? SEL_BEAM : mode == MODE_SAMPLE ? SEL_SAMPLE : SEL_GREEDY;
     CUDA_TRY(tmark(c, KC_SELECT, true));
-    CUDA_TRY(launch_select(st, sel, parity, c->logit_part, c->n_parts, c->masked, 0, c->stream, true));
+    CUDA_TRY(launch_select(st, sel, parity, c->logit_part, sp && sp->ok ? c->n_parts : logit_parts(c, la), c->masked, 0,
+                           c->stream, true));
     CUDA_TRY(tmark(c, KC_SELECT, false));
     launches += 1;
     return 0;

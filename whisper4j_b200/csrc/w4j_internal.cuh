@@ -40,8 +40,21 @@ struct DMat {
 enum InMode : int { IN_ACT = 0, IN_LN = 1, IN_EMBED_LN = 2 };
 enum OutMode : int { OUT_STORE = 0, OUT_GELU = 1, OUT_RESIDUAL = 2, OUT_QKV = 3 };
 
+// Bytes a later kernel of the step will read, pulled into L2 while this one runs: a weight
+// matrix and, for one stream, a layer's cross K / V (stream index read on the device; the host
+// writes it before the step, no kernel of the step does).
+struct L2Ahead {
+    const unsigned char *w = nullptr;
+    size_t w_bytes = 0;
+    const unsigned char *k = nullptr, *v = nullptr;  // the layer's cross K / V of stream 0
+    size_t kv_bytes = 0, kv_stride = 0;              // bytes of one stream's layer, stride between streams
+    const int *stream = nullptr;                     // [1] the stream whose cross K / V are read
+    int n_streams = 0;
+};
+
 struct GemvArgs {
     DMat W;
+    L2Ahead pf;                        // prefetched into L2 before the wait on the previous kernel
     const float *bias = nullptr;       // [N] or null
     int M = 0;
     int in_mode = IN_ACT;
@@ -218,6 +231,25 @@ __device__ __forceinline__ void bulk_g2s_hint(void *dst, const void *src, unsign
         "l"(src), "r"(bytes), "r"(smem_u32(b)), "l"(pol)
         : "memory");
 }
+// Block b of nb pulls its share of [p, p + bytes) into L2 (whole 16-byte units, 64 KB requests).
+__device__ __forceinline__ void l2_prefetch_share(const unsigned char *p, size_t bytes, int b, int nb) {
+    const size_t units = bytes >> 4, per = (units + nb - 1) / nb;
+    const size_t u0 = (size_t)b * per, u1 = u0 + per < units ? u0 + per : units;
+    for (size_t u = u0; u < u1; u += 4096) {
+        const unsigned sz = (unsigned)((u1 - u < 4096 ? u1 - u : 4096) << 4);
+        asm volatile("cp.async.bulk.prefetch.L2.global [%0], %1;" ::"l"(p + (u << 4)), "r"(sz) : "memory");
+    }
+}
+__device__ __forceinline__ void l2_ahead(const L2Ahead &f, int b, int nb) {
+    if (f.w) l2_prefetch_share(f.w, f.w_bytes, b, nb);
+    if (f.k && f.stream) {
+        const int s = *f.stream;
+        if (s < 0 || s >= f.n_streams) return;
+        const size_t o = (size_t)s * f.kv_stride;
+        l2_prefetch_share(f.k + o, f.kv_bytes, b, nb);
+        l2_prefetch_share(f.v + o, f.kv_bytes, b, nb);
+    }
+}
 __device__ __forceinline__ bool mbar_test(uint64_t *b, unsigned parity) {
     unsigned ok;
     asm volatile(
@@ -332,6 +364,13 @@ cudaError_t gemv_prepare();
 cudaError_t logits_tc_prepare();
 // tcgen05 vocabulary logits (f16 embedding, M <= 32); cudaErrorNotSupported outside its range
 cudaError_t launch_logits_tc(const LogitsArgs &a, const void *tmap, int n_parts, cudaStream_t s, bool pdl);
+// one-launch tcgen05 vocabulary pass over 33 .. kLogitsBigMaxRows rows without the beam top-k, the
+// rows read as f16 LayerNorm-ed activations staged by launch_act_hilo (bmap: their hi rows, K = d, boxes
+// of the chunk's NU rows): records per row of that pass (0 when it does not take the shape)
+constexpr int kLogitsBigMaxRows = 256;
+int logits_big_parts(int M, int V, int d, int topk);
+int logits_big_box_rows(int M);
+cudaError_t launch_logits_big(const LogitsArgs &a, const void *tmap, const void *bmap, int blocks, cudaStream_t s, bool pdl);
 bool make_tmap_f16_rows(void *map_out, const void *base, int rows, int cols);  // 128-byte map
 bool make_tmap_i8_rows(void *map_out, const void *base, int rows, int cols);   // [128 x 64] int8 boxes
 // Q8_0 scales [N][K/32] -> the tile layout [N/128][K/64][128][2] of the tensor-core projections
