@@ -162,10 +162,17 @@ __global__ void __launch_bounds__(kGemmThreads, 1) k_gemm_tc(GemvArgs a_all, con
         mbar_init(accf, 1);
         *fail = 0;
         fence_mbar_init();
-        // staged B tiles are written by the previous kernel: those stages start after the wait
-        if (!BT)
-            for (int i = 0; i < NS && i < nkb; ++i) issue(i);
-        *issued = BT ? 0 : (NS < nkb ? NS : nkb);
+        // the first stages' weight tiles now; staged B tiles are written by the previous kernel, so
+        // their copies into the same stages follow the wait (each stage's barrier expects both)
+        for (int i = 0; i < NS && i < nkb; ++i) {
+            if (BT) {
+                mbar_expect_tx(full + i, kStageBytes + kBTile);
+                tma_load_2d(ring + (size_t)i * SB, &tmap, (kb0 + i) * kKB, n0, full + i);
+            } else {
+                issue(i);
+            }
+        }
+        *issued = NS < nkb ? NS : nkb;
     }
     if (warp == 1) {
         tmem_alloc(tslot, kCols);
@@ -220,10 +227,9 @@ __global__ void __launch_bounds__(kGemmThreads, 1) k_gemm_tc(GemvArgs a_all, con
     bool started = ks == 1;
     pdl_trigger();
     pdl_wait();
-    if (BT && tid == 0) {
-        for (int i = 0; i < NS && i < nkb; ++i) issue(i);
-        *issued = NS < nkb ? NS : nkb;
-    }
+    if (BT && tid == 0)
+        for (int i = 0; i < NS && i < nkb; ++i)
+            tma_load_2d(ring + (size_t)i * SB + kStageBytes, &bmap, (kb0 + i) * kKB, (int)blockIdx.z * 2 * NU, full + i);
     __syncthreads();
 
     if constexpr (!BT) {
@@ -839,6 +845,16 @@ __global__ void __launch_bounds__(256) k_act_hilo(GemvArgs a, int mchunk, int ch
     const int K = a.W.K;
     const int gw = (int)((blockIdx.x * blockDim.x + threadIdx.x) >> 5), lane = threadIdx.x & 31;
     pdl_trigger();
+    // the LayerNorm parameters are weights: in registers before the wait
+    constexpr int kLnF4 = 10;
+    float4 gv[kLnF4], bv[kLnF4];
+    if (a.in_mode != IN_ACT)
+#pragma unroll
+        for (int j = 0; j < kLnF4; ++j) {
+            const bool in = j < K / 128 && K <= 128 * kLnF4;
+            gv[j] = in ? reinterpret_cast<const float4 *>(a.ln_g)[lane + 32 * j] : make_float4(0.f, 0.f, 0.f, 0.f);
+            bv[j] = in ? reinterpret_cast<const float4 *>(a.ln_b)[lane + 32 * j] : make_float4(0.f, 0.f, 0.f, 0.f);
+        }
     pdl_wait();
     if (gw >= chunks * nu * parts) return;
     const int row = gw / parts, part = gw - row * parts;
@@ -859,7 +875,6 @@ __global__ void __launch_bounds__(256) k_act_hilo(GemvArgs a, int mchunk, int ch
         for (int k = k0 + 4 * lane; k < k0 + seg; k += 128) put(k, make_float4(0.f, 0.f, 0.f, 0.f));
         return;
     }
-    constexpr int kLnF4 = 10;
     if (a.in_mode == IN_ACT) {
         const float4 *src = reinterpret_cast<const float4 *>(a.act + (size_t)m * K + k0);
         if (seg % 128 == 0 && seg <= 128 * kLnF4) {  // every load of the lane issued before any store
@@ -916,8 +931,7 @@ __global__ void __launch_bounds__(256) k_act_hilo(GemvArgs a, int mchunk, int ch
     for (int j = 0; j < kLnF4; ++j)
         if (j < nf4) {
             const int k = 4 * (lane + 32 * j);
-            const float4 g = *reinterpret_cast<const float4 *>(a.ln_g + k);
-            const float4 b = *reinterpret_cast<const float4 *>(a.ln_b + k);
+            const float4 g = gv[j], b = bv[j];
             put(k, make_float4((v[j].x - mean) * inv_std * g.x + b.x, (v[j].y - mean) * inv_std * g.y + b.y,
                                (v[j].z - mean) * inv_std * g.z + b.z, (v[j].w - mean) * inv_std * g.w + b.w));
         }
