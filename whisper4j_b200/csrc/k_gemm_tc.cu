@@ -466,6 +466,30 @@ __global__ void __launch_bounds__(kGemmThreads, 1) k_gemm_tc(GemvArgs a_all, con
             }
         }
     };
+    // The residual and GELU epilogues for 16 outputs at once (m < 0: none): their global loads are
+    // all issued before the first store, one L2 round trip for the batch instead of one per output.
+    const bool batched = a.out_mode == OUT_GELU || a.out_mode == OUT_RESIDUAL;
+    auto emit16 = [&](const float (&v)[16], const int (&rr)[16], const int (&mm)[16]) {
+        float val[16], g[16];
+        bool live[16];
+#pragma unroll
+        for (int e = 0; e < 16; ++e) {
+            const int n = n0 + rr[e], m = mm[e];
+            live[e] = m >= 0 && n < N && m < M && mi_s[m];
+            val[e] = live[e] ? v[e] + bias_s[rr[e]] : 0.f;
+        }
+        if (a.out_mode == OUT_GELU) {
+#pragma unroll
+            for (int e = 0; e < 16; ++e)
+                g[e] = live[e] ? __ldg(a.gelu_lut + __half_as_ushort(__float2half_rn(val[e]))) : 0.f;
+        } else {
+#pragma unroll
+            for (int e = 0; e < 16; ++e) g[e] = live[e] ? a.y[(size_t)mm[e] * N + n0 + rr[e]] : 0.f;
+        }
+#pragma unroll
+        for (int e = 0; e < 16; ++e)
+            if (live[e]) a.y[(size_t)mm[e] * N + n0 + rr[e]] = a.out_mode == OUT_GELU ? g[e] : g[e] + val[e];
+    };
 
     if (warp == 0 && lane == 0) {
         // ---- producer: the remaining weight tiles as stages free up ----
@@ -571,9 +595,19 @@ __global__ void __launch_bounds__(kGemmThreads, 1) k_gemm_tc(GemvArgs a_all, con
                 float v[16], lo[16];
                 tmem_ld16(taddr + ((uint32_t)(q4 * 32) << 16) + (uint32_t)c0, v);
                 tmem_ld16(taddr + ((uint32_t)(q4 * 32) << 16) + (uint32_t)(NU + c0), lo);
-                if (ok)
+                if (ok && batched) {
+                    int rr[16], mm[16];
+#pragma unroll
+                    for (int e = 0; e < 16; ++e) {
+                        v[e] += lo[e];
+                        rr[e] = r;
+                        mm[e] = c0 + e;
+                    }
+                    emit16(v, rr, mm);
+                } else if (ok) {
 #pragma unroll
                     for (int e = 0; e < 16; ++e) emit(v[e] + lo[e], r, c0 + e);
+                }
             }
         if (epi) tc_fence_before();
     } else {
@@ -606,12 +640,31 @@ __global__ void __launch_bounds__(kGemmThreads, 1) k_gemm_tc(GemvArgs a_all, con
             }
             tc_fence_before();
         }
+        // the owned rows [r0, r0 + nr): their residual values load while the partials arrive
+        const int r0 = (split * kTileRows) / ks, nr = ((split + 1) * kTileRows) / ks - r0, n_out = nr * M;
+        constexpr int kResPer = 8;
+        const bool res_pre = a.out_mode == OUT_RESIDUAL && n_out <= kResPer * kGemmThreads;
+        float resv[kResPer];
+#pragma unroll
+        for (int j = 0; j < kResPer; ++j) {
+            const int i = tid + j * kGemmThreads, m = i / nr, n = n0 + r0 + (i - m * nr);
+            resv[j] = res_pre && !*fail && i < n_out && n < N ? a.y[(size_t)m * N + n] : 0.f;
+        }
         __syncwarp();
         cluster_arrive_release();
         cluster_wait_acquire();
-        // the owned rows [r0, r0 + nr): add the ks partials in split order, then the epilogue
-        const int r0 = (split * kTileRows) / ks, nr = ((split + 1) * kTileRows) / ks - r0;
-        if (!*fail)
+        // add the ks partials in split order, then the epilogue
+        if (!*fail && res_pre) {
+#pragma unroll
+            for (int j = 0; j < kResPer; ++j) {
+                const int i = tid + j * kGemmThreads;
+                if (i >= n_out) break;
+                const int m = i / nr, rr = i - m * nr, n = n0 + r0 + rr;
+                float acc = 0.f;
+                for (int q = 0; q < ks; ++q) acc += recv[(q * M + m) * R + rr];
+                if (n < N && mi_s[m]) a.y[(size_t)m * N + n] = resv[j] + (acc + bias_s[r0 + rr]);
+            }
+        } else if (!*fail)
             for (int i = tid; i < nr * M; i += kGemmThreads) {
                 const int m = i / nr, rr = i - m * nr;  // neighbouring threads: neighbouring outputs
                 float acc = 0.f;
