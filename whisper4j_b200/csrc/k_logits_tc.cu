@@ -450,7 +450,7 @@ __global__ void __launch_bounds__(kLogitsThreads, 1)
                 }
             if (a.raw_out) named_bar_sync(1, ecount);
             if (go)
-                logits_rows_epilogue(a, tile, kTileRows, mt, m0, lo, hi, true, &ms, L.tiles_total, t0 + lt, kEpiWarp0,
+                logits_rows_epilogue<kTileRows / 32>(a, tile, kTileRows, mt, m0, lo, hi, true, &ms, L.tiles_total, t0 + lt, kEpiWarp0,
                                      kEpiWarps);
             named_bar_sync(1, ecount);
         }

@@ -30,6 +30,8 @@ __device__ __forceinline__ bool logit_better(float v1, int i1, float v2, int i2)
 // first argmax, sum of exp and the block's top-k candidates.  One warp per sequence: warps
 // w0 .. w0 + nw of the block (nw = 0: all).  The records of row m are part[m][P][..] (P = 0: one
 // per block, this block's at blockIdx.x; else record `slot`).
+// RR: row elements per lane held in registers (rows of up to 32 RR ids take the register path).
+template <int RR = kRowRegs>
 __device__ __forceinline__ void logits_rows_epilogue(const LogitsArgs &a, float *tile, int ch, int MT, int m0, int lo, int hi,
                                      bool ok, const MaskStage *ms = nullptr, int P = 0, int slot = 0, int w0 = 0,
                                      int nw = 0) {
@@ -98,15 +100,15 @@ for (int mm = warp; mm < MT; mm += nw) {
             for (int i = lane; i < n; i += 32) a.masked_out[(size_t)m * a.V + lo + i] = row[i];
         const int K = a.topk;
         float *pp = a.part + ((size_t)m * P + slot) * kPartStride;
-        if (n <= 32 * kRowRegs) {
+        if (n <= 32 * RR) {
             // the row in registers (lane + 32 j: ids ascending in j), then every reduction there
-            float v[kRowRegs];
+            float v[RR];
 #pragma unroll
-            for (int j = 0; j < kRowRegs; ++j) v[j] = lane + 32 * j < n ? row[lane + 32 * j] : -INFINITY;
+            for (int j = 0; j < RR; ++j) v[j] = lane + 32 * j < n ? row[lane + 32 * j] : -INFINITY;
             float bv = -INFINITY;
             int bj = -1;
 #pragma unroll
-            for (int j = 0; j < kRowRegs; ++j)
+            for (int j = 0; j < RR; ++j)
                 if (v[j] > bv) {  // strict: the first index of the lane's maximum
                     bv = v[j];
                     bj = j;
@@ -125,7 +127,7 @@ for (int mm = warp; mm < MT; mm += nw) {
             float sm = 0.f;
             if (wv != -INFINITY)
 #pragma unroll
-                for (int j = 0; j < kRowRegs; ++j) sm += __expf(v[j] - wv);  // exp(-inf) = 0
+                for (int j = 0; j < RR; ++j) sm += __expf(v[j] - wv);  // exp(-inf) = 0
             sm = warp_sum(sm);
             if (lane == 0) {
                 pp[0] = wv;
@@ -138,7 +140,7 @@ for (int mm = warp; mm < MT; mm += nw) {
                 float cv = -INFINITY;
                 int cj = -1;
 #pragma unroll
-                for (int j = 0; j < kRowRegs; ++j)
+                for (int j = 0; j < RR; ++j)
                     if (v[j] > cv) {
                         cv = v[j];
                         cj = j;
@@ -161,7 +163,7 @@ for (int mm = warp; mm < MT; mm += nw) {
                 }
                 if (hi2 != INT_MAX && ci == hi2)  // ids are unique: exactly one lane owns it
 #pragma unroll
-                    for (int j = 0; j < kRowRegs; ++j)
+                    for (int j = 0; j < RR; ++j)
                         if (j == cj) v[j] = -INFINITY;
             }
             continue;
