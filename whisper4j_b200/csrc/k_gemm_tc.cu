@@ -640,37 +640,60 @@ __global__ void __launch_bounds__(kGemmThreads, 1) k_gemm_tc(GemvArgs a_all, con
             }
             tc_fence_before();
         }
-        // the owned rows [r0, r0 + nr): their residual values load while the partials arrive
-        const int r0 = (split * kTileRows) / ks, nr = ((split + 1) * kTileRows) / ks - r0, n_out = nr * M;
+        // the owned rows [r0, r0 + nr): thread t adds up output row rr = t mod nr for the sequences
+        // m = t / nr + j * per (neighbouring threads: neighbouring outputs), so the row's index
+        // arithmetic and bias are done once; residual values load while the partials arrive
+        const int r0 = (split * kTileRows) / ks, nr = ((split + 1) * kTileRows) / ks - r0;
+        const int per = kGemmThreads / nr, rr = tid % nr, mt0 = tid / nr, n = n0 + r0 + rr;
+        const bool own = tid < per * nr && n < N;
         constexpr int kResPer = 8;
-        const bool res_pre = a.out_mode == OUT_RESIDUAL && n_out <= kResPer * kGemmThreads;
+        const bool res_pre = a.out_mode == OUT_RESIDUAL && (M + per - 1) / per <= kResPer;
         float resv[kResPer];
 #pragma unroll
         for (int j = 0; j < kResPer; ++j) {
-            const int i = tid + j * kGemmThreads, m = i / nr, n = n0 + r0 + (i - m * nr);
-            resv[j] = res_pre && !*fail && i < n_out && n < N ? a.y[(size_t)m * N + n] : 0.f;
+            const int m = mt0 + j * per;
+            resv[j] = res_pre && own && !*fail && m < M ? a.y[(size_t)m * N + n] : 0.f;
         }
         __syncwarp();
         cluster_arrive_release();
         cluster_wait_acquire();
         // add the ks partials in split order, then the epilogue
-        if (!*fail && res_pre) {
+        if (!*fail && own) {
+            const float b = bias_s[r0 + rr];
+            if (res_pre) {
 #pragma unroll
-            for (int j = 0; j < kResPer; ++j) {
-                const int i = tid + j * kGemmThreads;
-                if (i >= n_out) break;
-                const int m = i / nr, rr = i - m * nr, n = n0 + r0 + rr;
-                float acc = 0.f;
-                for (int q = 0; q < ks; ++q) acc += recv[(q * M + m) * R + rr];
-                if (n < N && mi_s[m]) a.y[(size_t)m * N + n] = resv[j] + (acc + bias_s[r0 + rr]);
+                for (int j = 0; j < kResPer; ++j) {
+                    const int m = mt0 + j * per;
+                    if (m >= M) break;
+                    float acc = 0.f;
+                    for (int q = 0; q < ks; ++q) acc += recv[(q * M + m) * R + rr];
+                    if (mi_s[m]) a.y[(size_t)m * N + n] = resv[j] + (acc + b);
+                }
+            } else if (a.out_mode == OUT_QKV) {
+                const int dm = N / 3, part_ = n / dm, c = n - part_ * dm;
+                const int head = c / kHeadDim, dd = c % kHeadDim;
+                __half *dst = part_ == 1 ? a.kcache : a.vcache;
+                for (int m = mt0; m < M; m += per) {
+                    float acc = 0.f;
+                    for (int q = 0; q < ks; ++q) acc += recv[(q * M + m) * R + rr];
+                    if (!mi_s[m]) continue;
+                    const float val = acc + b;
+                    if (part_ == 0) {
+                        a.y[(size_t)m * dm + c] = val;
+                    } else {
+                        const size_t row = (((size_t)mi_s[M + m] * a.n_layer + a.layer) * a.n_head + head) * (size_t)a.n_ctx +
+                                           (size_t)mi_s[2 * M + m];
+                        dst[row * kHeadDim + dd] = __float2half_rn(val);
+                    }
+                }
+            } else {
+                for (int m = mt0; m < M; m += per) {
+                    float acc = 0.f;
+                    for (int q = 0; q < ks; ++q) acc += recv[(q * M + m) * R + rr];
+                    emit(acc, r0 + rr, m);
+                }
             }
-        } else if (!*fail)
-            for (int i = tid; i < nr * M; i += kGemmThreads) {
-                const int m = i / nr, rr = i - m * nr;  // neighbouring threads: neighbouring outputs
-                float acc = 0.f;
-                for (int q = 0; q < ks; ++q) acc += recv[(q * M + m) * R + rr];
-                emit(acc, r0 + rr, m);
-            }
+        }
     }
     __syncthreads();
     if (*fail && tid == 0) drain_ring(full, NS, *issued);
