@@ -579,9 +579,10 @@ __global__ void __launch_bounds__(kGemmThreads, 1) k_gemm_tc(GemvArgs a_all, con
         }
     }
     __syncthreads();
-    // ---- epilogue warps 8 .. 15: warp w reads TMEM lanes 32 (w % 4) .., column group (w - 8) / 4 ----
-    const bool epi = warp >= 8;
-    const int q4 = warp & 3, cg = (warp - 8) >> 2, r = q4 * 32 + lane;
+    // ---- epilogue, all sixteen warps (their roles above are done): warp w reads TMEM lanes
+    // 32 (w % 4) .. and the 16-column groups cg, cg + 4, ... of its column set cg = w / 4 ----
+    const bool epi = true;
+    const int q4 = warp & 3, cg = warp >> 2, r = q4 * 32 + lane;
     bool ok = true;
     if (epi) {
         ok = !*fail && mbar_wait(accf, 0u, a.err);
@@ -590,7 +591,7 @@ __global__ void __launch_bounds__(kGemmThreads, 1) k_gemm_tc(GemvArgs a_all, con
     }
     if (ks == 1) {
         if (epi)
-            for (int c0 = 16 * cg; c0 < NU; c0 += 32) {
+            for (int c0 = 16 * cg; c0 < NU; c0 += 64) {
                 // slot m = hi column m + lo column NU + m
                 float v[16], lo[16];
                 tmem_ld16(taddr + ((uint32_t)(q4 * 32) << 16) + (uint32_t)c0, v);
@@ -630,7 +631,7 @@ __global__ void __launch_bounds__(kGemmThreads, 1) k_gemm_tc(GemvArgs a_all, con
             while (o + 1 < ks && ((o + 1) * kTileRows) / ks <= r) ++o;
             const int rr = r - (o * kTileRows) / ks;
             const unsigned dst = cluster_map(recv, (unsigned)o) + (unsigned)((split * M * R + rr) * 4);
-            for (int c0 = 16 * cg; c0 < NU; c0 += 32) {
+            for (int c0 = 16 * cg; c0 < NU; c0 += 64) {
                 float v[16], lo[16];
                 tmem_ld16(taddr + ((uint32_t)(q4 * 32) << 16) + (uint32_t)c0, v);
                 tmem_ld16(taddr + ((uint32_t)(q4 * 32) << 16) + (uint32_t)(NU + c0), lo);
