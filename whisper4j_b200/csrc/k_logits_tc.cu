@@ -275,8 +275,9 @@ __global__ void __launch_bounds__(kLogitsThreads, 1) k_logits_tc(LogitsArgs a, c
 // hi rows, K = d: the f16(LN(x)) that k_logits_tc builds in shared memory) and stream beside the
 // embedding: a stage is a [128 x 64] embedding tile and the [NU x 64] tile of the rows.  Work items
 // are (embedding tile, chunk of <= 128 rows) pairs, tile-major, so the second chunk of a tile finds
-// the tile's bytes in L2.  Each item's logits go through the same row epilogue, one record per
-// (row, embedding tile): P = ceil(V / 128) records per row for the greedy / sampling select.
+// the tile's bytes in L2.  Each item's logits go through the row epilogue's processors and
+// reductions (logits_row_thread: one thread per row, in id order), one record per (row, embedding
+// tile): P = ceil(V / 128) records per row for the greedy / sampling select.
 // Warps: 0 produces, 1 issues the MMAs, 4-7 move accumulators out of TMEM, 2-15 run the epilogue.
 // ---------------------------------------------------------------------------
 template <int NU>
@@ -294,7 +295,10 @@ __global__ void __launch_bounds__(kLogitsThreads, 1)
     const int d = a.d, KB = d / kKB, NS = L.n_stages, CH = L.chunks;
     const int items = (t1 - t0) * CH, total = items * KB;
     unsigned char *ring = smem;
-    float *tile = reinterpret_cast<float *>(smem + L.tile_off);  // [NU][128]
+    // logits of the item, column-major: tile[id * kTS + row], the odd stride keeps both the
+    // accumulator copy (a thread per id) and the row scans (a thread per row) free of bank conflicts
+    constexpr int kTS = NU + 1;
+    float *tile = reinterpret_cast<float *>(smem + L.tile_off);
     int2 *mk_rg = reinterpret_cast<int2 *>(smem + L.mk_off);
     int *mk_act = reinterpret_cast<int *>(mk_rg + (size_t)a.M * kMaxRanges);
     int *mk_nr = mk_act + a.M, *mk_cnt = mk_nr + a.M;
@@ -416,8 +420,9 @@ __global__ void __launch_bounds__(kLogitsThreads, 1)
             umma_commit(accf + b);
         }
     } else if (warp >= kEpiWarp0) {
-        // ---- epilogue: TMEM -> [rows][128] logits tile -> row epilogue, one item at a time.  Every
-        // epilogue thread passes the same three barriers per item, failed or not. ----
+        // ---- epilogue: TMEM -> column-major logits tile -> the row epilogue with one thread per
+        // row, one item at a time.  Every epilogue thread passes the same barriers per item, failed
+        // or not. ----
         const MaskStage ms{mk_act, mk_nr, mk_rg, mk_cnt, mk_dyn, mk_stat};
         const int etid = tid - kEpiWarp0 * 32, ecount = kEpiWarps * 32;
         for (int it = 0; it < items; ++it) {
@@ -437,7 +442,7 @@ __global__ void __launch_bounds__(kLogitsThreads, 1)
                     if (row < n)
 #pragma unroll
                         for (int e = 0; e < 16; ++e)
-                            if (c0 + e < mt) tile[(size_t)(c0 + e) * kTileRows + row] = v[e];
+                            if (c0 + e < mt) tile[(size_t)row * kTS + c0 + e] = v[e];
                 }
             }
             tc_fence_before();
@@ -446,12 +451,12 @@ __global__ void __launch_bounds__(kLogitsThreads, 1)
             if (go && a.raw_out)
                 for (int i = etid; i < mt * n; i += ecount) {
                     const int mm = i / n, r = i - mm * n;
-                    a.raw_out[(size_t)(m0 + mm) * a.V + lo + r] = tile[(size_t)mm * kTileRows + r];
+                    a.raw_out[(size_t)(m0 + mm) * a.V + lo + r] = tile[(size_t)r * kTS + mm];
                 }
             if (a.raw_out) named_bar_sync(1, ecount);
             if (go)
-                logits_rows_epilogue<kTileRows / 32>(a, tile, kTileRows, mt, m0, lo, hi, true, &ms, L.tiles_total, t0 + lt, kEpiWarp0,
-                                     kEpiWarps);
+                for (int mm = etid; mm < mt; mm += ecount)
+                    logits_row_thread(a, tile, kTS, mm, m0, lo, hi, &ms, L.tiles_total, t0 + lt);
             named_bar_sync(1, ecount);
         }
     }
@@ -577,7 +582,7 @@ static bool plan_big(int M, int V, int d, int topk, int &nu, LogitsBigLaunch &L)
     nu = L.mchunk <= 64 ? 64 : 128;
     L.tiles_total = (V + kTileRows - 1) / kTileRows;
     const size_t st = (size_t)kStageBytes + (size_t)nu * 128;
-    const size_t tbytes = (size_t)nu * kTileRows * 4;
+    const size_t tbytes = (((size_t)(nu + 1) * kTileRows * 4) + 15) & ~(size_t)15;
     const size_t mkbytes = mask_stage_bytes(M);
     const size_t fixed = tbytes + mkbytes + 256;
     const size_t budget = 220 * 1024;

@@ -221,4 +221,64 @@ for (int mm = warp; mm < MT; mm += nw) {
     }
 }
 
+// The same processors and record for one row of at most 128 ids, run by ONE thread over a
+// column-major tile (tile[i * stride + mm] = the logit of id lo + i for row m = m0 + mm): the row's
+// masks, then max and first argmax in one scan and the sum of exp in a second, in id order, with no
+// warp reductions.  No top-k (greedy and sampling passes).  The records are part[m][P][..] at `slot`.
+__device__ __forceinline__ void logits_row_thread(const LogitsArgs &a, float *tile, int stride, int mm, int m0, int lo,
+                                                  int hi, const MaskStage *ms, int P, int slot) {
+    const int m = m0 + mm, n = hi - lo;
+    if (m >= a.M || (a.active && !ms->active[m])) return;
+    float *col = tile + mm;  // id lo + i at col[i * stride]
+    if (a.ns_token >= 0) {  // unmasked statistics (no-speech probability)
+        float mx = -INFINITY;
+        for (int i = 0; i < n; ++i) mx = fmaxf(mx, col[i * stride]);
+        float sm = 0.f;
+        if (mx != -INFINITY)
+            for (int i = 0; i < n; ++i) sm += __expf(col[i * stride] - mx);
+        float *np = a.ns_part + ((size_t)m * P + slot) * 2;
+        np[0] = mx;
+        np[1] = sm;
+        if (a.ns_token >= lo && a.ns_token < hi) a.ns_value[m] = col[(a.ns_token - lo) * stride];
+    }
+    if (a.use_mask) {
+        const MaskArgs &mk = a.mask;
+        const int nrg = ms->n_ranges[m];
+        for (int r = 0; r < nrg; ++r) {
+            const int2 rg = ms->ranges[(size_t)m * kMaxRanges + r];
+            for (int i = max(rg.x, lo); i < min(rg.y, hi); ++i) col[(i - lo) * stride] = -INFINITY;
+        }
+        auto mask_list = [&](const int *list, int n_list) {
+            for (int j = 0; j < n_list; ++j) {
+                const int t = list[j];
+                if (t >= lo && t < hi) col[(t - lo) * stride] = -INFINITY;
+            }
+        };
+        const int ns = min(mk.n_static, kStatStage);
+        mask_list(ms->stat, ns);
+        mask_list(mk.static_list + ns, mk.n_static - ns);
+        const int nd = ms->dyn_count[m], nds = min(nd, kDynStage);
+        mask_list(ms->dyn + (size_t)m * kDynStage, nds);
+        mask_list(mk.dyn_list + (size_t)m * mk.dyn_stride + nds, nd - nds);
+    }
+    if (a.masked_out)
+        for (int i = 0; i < n; ++i) a.masked_out[(size_t)m * a.V + lo + i] = col[i * stride];
+    float bv = -INFINITY;
+    int bi = -1;
+    for (int i = 0; i < n; ++i) {
+        const float v = col[i * stride];
+        if (v > bv) {  // strict: the first index of the maximum
+            bv = v;
+            bi = i;
+        }
+    }
+    float sm = 0.f;
+    if (bv != -INFINITY)
+        for (int i = 0; i < n; ++i) sm += __expf(col[i * stride] - bv);  // exp(-inf) = 0
+    float *pp = a.part + ((size_t)m * P + slot) * kPartStride;
+    pp[0] = bv;
+    pp[1] = sm;
+    pp[2] = __int_as_float(bi < 0 ? lo : lo + bi);
+}
+
 }  // namespace w4j
