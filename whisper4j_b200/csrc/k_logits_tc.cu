@@ -278,7 +278,8 @@ __global__ void __launch_bounds__(kLogitsThreads, 1) k_logits_tc(LogitsArgs a, c
 // the tile's bytes in L2.  Each item's logits go through the row epilogue's processors and
 // reductions (logits_row_thread: one thread per row, in id order), one record per (row, embedding
 // tile): P = ceil(V / 128) records per row for the greedy / sampling select.
-// Warps: 0 produces, 1 issues the MMAs, 4-7 move accumulators out of TMEM, 2-15 run the epilogue.
+// Warps: 0 produces, 1 issues the MMAs, 4-7 move accumulators out of TMEM, 2-15 take part in the
+// epilogue (threads 64 .. 64 + rows scan the rows).
 // ---------------------------------------------------------------------------
 template <int NU>
 __global__ void __launch_bounds__(kLogitsThreads, 1)
